@@ -326,3 +326,38 @@ def synthetic_kv(n, nkv, hs, seed=0, outlier_frac=0.02, outlier_gain=8.0):
         k[:, h, ch] *= outlier_gain
         v[:, h, ch] *= outlier_gain
     return f32_to_bf16(k), f32_to_bf16(v)
+
+
+def read_range(cache, layout, block_row, start, end):
+    """(K, V) fp64 of positions [start, end) of one sequence (see read_sequence)."""
+    hs, nkv = layout.head_size, layout.nkv
+    pos = np.arange(start, end)
+    blk = np.asarray(block_row, dtype=np.int64)[pos // layout.block_size]
+    s = pos % layout.block_size
+    base = blk[:, None] * layout.block_stride + np.arange(nkv)[None, :] * layout.head_stride + \
+        s[:, None] * layout.slot_stride
+
+    def gather(off, nbytes):
+        return cache[base[..., None] + off + np.arange(nbytes)]
+
+    kb = hs // 2 if layout.fmt == "int4" else hs
+    kraw = gather(layout.k_off, kb)
+    kw = gather(layout.ks_off, 4).copy().view(np.uint32)[..., 0]
+    vraw = gather(layout.v_off, hs // 2)
+    vw = gather(layout.vs_off, 4).copy().view(np.uint32)[..., 0]
+    K = dequant_int4(kraw, kw) if layout.fmt == "int4" else dequant_int8(kraw.view(np.int8), kw.view(np.float32))
+    return K, dequant_int4(vraw, vw)
+
+
+def attention_from_cache(q_rot, cache, layout, block_row, n, softmax_scale, chunk=16384):
+    """attention_rht_domain over the cached context of one sequence, streamed in chunks of keys and folded by
+    log-sum-exp (memory bounded for long contexts). Returns (out, natural-log lse)."""
+    hs = layout.head_size
+    outs, lses = [], []
+    for start in range(0, max(n, 1), chunk):
+        end = min(n, start + chunk)
+        K, V = read_range(cache, layout, block_row, start, end)
+        o, l = attention_rht_domain(q_rot, K, V, n - start, softmax_scale, hs)
+        outs.append(o)
+        lses.append(l)
+    return merge_partials(np.stack(outs), np.stack(lses))

@@ -1,0 +1,213 @@
+"""B200 ops behind the plugin's patch points: cache write, split-KV decode, RHT and partial merge.
+
+These are the functions the stock vLLM int4 module (`vllm.v1.attention.ops.int4_per_token_head`, vLLM >= 0.31)
+exposes and the plugin patches (vllm_quantpack/attention/int4_kv.py:39, 212-216, 294-333;
+vllm_quantpack/attention/k8v4_kv.py:152-163), with the same names, arguments and tensor views, each one a thin
+launch of a CUDA kernel of libquantpack_b200.so on the current stream. There is no CPU path: on a machine without
+the library or a GPU every op raises.
+"""
+import threading
+
+import torch
+
+from .. import _lib
+from . import rht
+
+_DTYPES = {torch.bfloat16: 0, torch.float16: 1}
+FMT_INT4, FMT_K8V4 = 0, 1
+MAX_Q_DECODE_ROWS = 32      # query rows (tokens x query heads per KV head) one decode CTA holds
+
+
+def _stream(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _dtype_code(t, what):
+    code = _DTYPES.get(t.dtype)
+    if code is None:
+        raise TypeError(f"{what}: dtype {t.dtype} (bf16 or fp16 expected)")
+    return code
+
+
+class CacheLayout:
+    """Byte layout of a paged int4 / k8v4 cache, derived from the four views vLLM passes.
+
+    int4 views (tests/test_int4_kv.py:95-103): key / value (blocks, block size, KV heads, hs/2 + 4) uint8 over cells
+    [K | K scale | V | V scale]; k8v4 views (vllm_quantpack/attention/k8v4_kv.py:41-65): key (..., hs) int8, value
+    (..., hs/2) uint8. Scale views are fp32 (blocks, block size, KV heads) over the same storage."""
+
+    def __init__(self, k_cache, v_cache, k_scale_cache, v_scale_cache, head_size):
+        if k_cache.dtype == torch.int8:
+            self.fmt, kb = FMT_K8V4, head_size
+        elif k_cache.dtype == torch.uint8:
+            self.fmt, kb = FMT_INT4, head_size // 2
+        else:
+            raise TypeError(f"key cache dtype {k_cache.dtype}: uint8 (int4) or int8 (k8v4) expected")
+        if k_cache.dim() != 4 or v_cache.dim() != 4:
+            raise ValueError("cache views must be (blocks, block size, KV heads, bytes)")
+        self.nblocks, self.block_size, self.nkv = k_cache.shape[0], k_cache.shape[1], k_cache.shape[2]
+        self.head_size = head_size
+        base = k_cache.data_ptr()
+        self.base = base
+        self.block_stride, self.slot_stride, self.head_stride = (int(s) for s in k_cache.stride()[:3])
+        self.k_off = 0
+        self.ks_off = k_scale_cache.data_ptr() - base
+        self.v_off = v_cache.data_ptr() - base
+        self.vs_off = v_scale_cache.data_ptr() - base
+        self.cell = kb + 8 + head_size // 2
+        if (tuple(v_cache.stride()[:3]) != (self.block_stride, self.slot_stride, self.head_stride)
+                or tuple(v_cache.shape[:3]) != tuple(k_cache.shape[:3])):
+            raise ValueError("key and value cache views disagree on blocks / slots / heads")
+        for sc in (k_scale_cache, v_scale_cache):
+            if sc.dtype != torch.float32 or tuple(sc.shape) != (self.nblocks, self.block_size, self.nkv):
+                raise ValueError("scale views must be fp32 (blocks, block size, KV heads)")
+            if tuple(4 * s for s in sc.stride()) != (self.block_stride, self.slot_stride, self.head_stride):
+                raise ValueError("scale views must share the cache's strides")
+        if self.ks_off != kb or self.v_off != kb + 4 or self.vs_off != kb + 4 + head_size // 2:
+            raise ValueError(f"cell fields at K 0, K scale {self.ks_off}, V {self.v_off}, V scale {self.vs_off}: "
+                             f"expected 0, {kb}, {kb + 4}, {kb + 4 + head_size // 2}")
+
+    def args(self):
+        return (self.base, self.block_size, self.block_stride, self.head_stride, self.slot_stride, self.k_off,
+                self.ks_off, self.v_off, self.vs_off)
+
+    @property
+    def hnd(self):
+        return self.slot_stride == self.cell
+
+
+# ------------------------------------------------------------------------------------------------------ RHT
+
+
+def single_rht(x, inverse=False):
+    """Randomized Hadamard transform over the last axis of fp32 `x` (unnormalised; see rht.py). Returns fp32."""
+    if x.dtype != torch.float32:
+        raise TypeError("single_rht takes fp32 (as the callers pass x.float())")
+    hs = x.shape[-1]
+    xc = x.contiguous()
+    y = torch.empty_like(xc)
+    rows = xc.numel() // hs if hs else 0
+    _lib.call("qp_single_rht", xc.data_ptr(), y.data_ptr(), rows, hs, int(bool(inverse)),
+              rht.device_sign_bits(hs, x.device).data_ptr(), _stream(x.device))
+    return y
+
+
+# ------------------------------------------------------------------------------------------------------ cache write
+
+
+def reshape_and_cache_int4(key, value, key_cache, value_cache, slot_mapping, *, k_scale_cache, v_scale_cache,
+                           rotate=True):
+    """Rotate, quantize and write key / value (tokens, KV heads, hs) into the cache; slots < 0 are skipped.
+    A uint8 key view is the int4 cache, an int8 one k8v4 (vllm_quantpack/attention/k8v4_kv.py:36-38, 152-157).
+    rotate=False takes key / value as already in the RHT domain (the `_store_k8v4` kernel contract)."""
+    hs = key.shape[-1]
+    if value.shape[-1] != hs:
+        raise ValueError(f"key head size {hs} != value head size {value.shape[-1]}")
+    if key.stride(-1) != 1 or value.stride(-1) != 1:
+        raise ValueError("key / value rows must be contiguous")
+    lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
+    if slot_mapping.dtype != torch.int64:
+        slot_mapping = slot_mapping.to(torch.int64)
+    slot_mapping = slot_mapping.contiguous()
+    dt = _dtype_code(key, "reshape_and_cache_int4")
+    if value.dtype != key.dtype:
+        raise TypeError("key and value dtypes differ")
+    name = "qp_reshape_and_cache_int4" if lay.fmt == FMT_INT4 else "qp_reshape_and_cache_k8v4"
+    _lib.call(name, key.data_ptr(), value.data_ptr(), dt, key.shape[0], key.shape[1], hs, key.stride(0),
+              key.stride(1), value.stride(0), value.stride(1), slot_mapping.data_ptr(), *lay.args(),
+              rht.device_sign_bits(hs, key.device).data_ptr(), int(bool(rotate)), _stream(key.device))
+
+
+# ------------------------------------------------------------------------------------------------------ decode
+
+_ws_lock = threading.Lock()
+_workspaces = {}
+
+
+def workspace(device, nbytes):
+    """A per-device scratch buffer for the split-KV partials, grown geometrically and kept for the process. Growing
+    it inside a CUDA-graph capture allocates from the graph's pool: warm up with the largest batch first."""
+    key = str(torch.device(device))
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            size = max(nbytes, 2 * (ws.numel() if ws is not None else 0), 1 << 20)
+            ws = torch.empty(size, dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+    return ws
+
+
+def sm_count(device):
+    return torch.cuda.get_device_properties(device).multi_processor_count
+
+
+def decode_num_splits(num_seqs, num_kv_heads, max_seqlen_k, sms):
+    return _lib.load().qp_decode_num_splits(num_seqs, num_kv_heads, max_seqlen_k, sms)
+
+
+def paged_decode(q, key_cache, value_cache, out, *, cu_seqlens_q, max_seqlen_q, seqused_k, max_seqlen_k,
+                 softmax_scale, block_table, k_scale_cache, v_scale_cache, num_splits=None, q_rotated=False,
+                 out_fp32_lse=None, ws=None, partials_only=False):
+    """Split-KV decode of up to 32 query rows per KV head (4 MTP tokens x 6 heads) over the paged cache.
+
+    q / out (tokens, query heads, hs). When `out_fp32_lse` is a tensor (tokens, query heads) fp32, `out` must be fp32
+    and receives the RHT-domain output with its base-2 log-sum-exp in `out_fp32_lse` (the partial a sequence-parallel
+    rank exchanges); otherwise `out` gets the model-domain output in q's dtype. partials_only=True launches the split
+    kernel alone and leaves its partials in the workspace (returned)."""
+    hs = q.shape[-1]
+    nq = q.shape[1]
+    lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
+    nkv = lay.nkv
+    num_seqs = cu_seqlens_q.shape[0] - 1
+    if num_splits is None:
+        num_splits = decode_num_splits(num_seqs, nkv, int(max_seqlen_k), sm_count(q.device))
+    wbytes = _lib.load().qp_decode_workspace_bytes(q.shape[0], nq, hs, int(num_splits))
+    if ws is None:
+        ws = workspace(q.device, wbytes)
+    for name, t in (("cu_seqlens_q", cu_seqlens_q), ("seqused_k", seqused_k), ("block_table", block_table)):
+        if t.dtype != torch.int32:
+            raise TypeError(f"{name} must be int32")
+    if cu_seqlens_q.stride(0) != 1 or seqused_k.stride(0) != 1 or block_table.stride(-1) != 1:
+        raise ValueError("cu_seqlens_q, seqused_k and block_table rows must be contiguous")
+    if q.stride(-1) != 1 or out.stride(-1) != 1:
+        raise ValueError("q / out rows must be contiguous")
+    dt = _dtype_code(q, "paged_decode")
+    if partials_only:
+        mode, lse_ptr = 2, None
+    elif out_fp32_lse is not None:
+        if out.dtype != torch.float32 or out_fp32_lse.dtype != torch.float32:
+            raise TypeError("out and lse must be fp32 for the RHT-domain output")
+        if not out_fp32_lse.is_contiguous():
+            raise ValueError("lse must be contiguous (tokens, query heads)")
+        mode, lse_ptr = 1, out_fp32_lse.data_ptr()
+    else:
+        if out.dtype != q.dtype:
+            raise TypeError("out dtype must match q")
+        mode, lse_ptr = 0, None
+    _lib.call("qp_paged_decode", lay.fmt, dt, q.data_ptr(), q.stride(0), q.stride(1), out.data_ptr(), out.stride(0),
+              out.stride(1), q.shape[0], num_seqs, cu_seqlens_q.data_ptr(), seqused_k.data_ptr(), int(max_seqlen_q),
+              block_table.data_ptr(), block_table.stride(0), *lay.args(), nq, nkv, hs, float(softmax_scale),
+              rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)), mode, lse_ptr, int(num_splits),
+              ws.data_ptr(), ws.numel() * ws.element_size(), _stream(q.device))
+    return ws if partials_only else out
+
+
+def merge_attn_partials(part_o, part_lse, out, lse_out=None):
+    """Fold P partials part_o (P, tokens, heads, hs) fp32 / part_lse (P, tokens, heads) base-2 into `out`: in the
+    model domain (inverse RHT / head, out's dtype) or, with `lse_out`, fp32 in the RHT domain plus the folded lse."""
+    P, T, H, hs = part_o.shape
+    if part_o.dtype != torch.float32 or part_lse.dtype != torch.float32:
+        raise TypeError("partials must be fp32")
+    if part_o.stride(-1) != 1:
+        raise ValueError("partial rows must be contiguous")
+    if lse_out is not None:
+        if out.dtype != torch.float32 or not lse_out.is_contiguous():
+            raise TypeError("out must be fp32 and lse_out contiguous")
+        mode, dt, lptr, sbits = 1, 0, lse_out.data_ptr(), None
+    else:
+        mode, dt, lptr = 0, _dtype_code(out, "merge_attn_partials"), None
+        sbits = rht.device_sign_bits(hs, out.device).data_ptr()
+    _lib.call("qp_merge_attn_partials", dt, hs, T, H, P, part_o.data_ptr(), part_o.stride(1), part_o.stride(2),
+              part_o.stride(0), part_lse.data_ptr(), part_lse.stride(1), part_lse.stride(2), part_lse.stride(0), mode,
+              out.data_ptr(), out.stride(0), out.stride(1), lptr, sbits, _stream(out.device))
+    return out

@@ -1,0 +1,917 @@
+// K1: split-KV paged decode over an int4_per_token_head / k8v4_per_token_head cache, up to 32 query rows
+//     (qlen x query heads per KV head) per KV head, 64-token tiles; and K2: log-sum-exp merge of the segments with
+//     the inverse RHT fused in.
+//
+// Reference behaviour (what this computes, not how): the split-KV 3D path of vLLM's int4 kernel as the plugin
+// configures it (vllm_quantpack/attention/int4_kv.py:98-122: 64-token tiles, every query token of a step in one
+// program, segments sized to the SM count) and vLLM's reduce_segments (vllm/v1/attention/ops/
+// triton_unified_attention.py:645-732 in vLLM 0.22). Scores S = (Q.u - Q_sum zp) k_scale scale, P_v = P v_scale,
+// out += P_v16 u - sum(P_v16 zp) with the same rounded P_v16 in both terms (int4_kv.py:80-94).
+//
+// B200 design:
+// - one CTA (4 warps) per (split, KV head, sequence); the segment's cells stream through a 4-stage shared-memory
+//   ring filled by 1-D bulk copies (TMA engine) of whole 16-token runs, completing on mbarriers;
+// - Q is rotated (RHT) and scaled once per CTA into fp16 with a per-row power of two, its channels permuted so that
+//   the nibble extraction below needs no shuffles; odd (high-nibble) channels carry a factor 1/16;
+// - QK: mma.sync m16n8k16 with the keys as M (16 tokens per warp) and the query rows as N (8 per n-tile). Key
+//   nibbles become fp16 by the exponent-bias trick ((w & 0x000F000F) | 0x64006400 = 1024 + u): one lop3 per two
+//   values, the bias removed once per score (Q.1024 is a per-row constant);
+// - softmax in log2 units with the row max exchanged through shared memory, the V scale folded into P (P_v16 in fp16
+//   with a running power-of-two range), the V zero point folded out as a per-row sum of P_v16 zp;
+// - PV: mma.sync with the head dimension as M (64 channels per warp) and the query rows as N; the value nibbles of
+//   two tokens are interleaved by prmt so each register holds one channel of two tokens;
+// - each split writes its normalised partial O (fp32, RHT domain) and its log2-sum-exp; K2 folds the splits and
+//   applies the inverse RHT / head, launched with programmatic dependent launch so its launch overlaps K1.
+#include <math.h>
+
+#include "qp_api_internal.h"
+#include "qp_common.cuh"
+
+namespace qp {
+
+constexpr int DEC_TILE = 64;
+constexpr int DEC_STAGES = 4;
+constexpr int DEC_THREADS = 128;
+constexpr int DEC_HS = 256;
+constexpr int DEC_MAX_ROWS = 32;
+constexpr int Q_STRIDE = DEC_HS * 2 + 16;  // bytes per Q row in shared memory (conflict-free ldmatrix)
+constexpr float LOG2E = 1.4426950408889634f;
+
+struct DecodeParams {
+  const void* q;
+  int64_t q_st, q_sh;  // element strides of q (token, head)
+  const int32_t* cu_seqlens_q;
+  const int32_t* seqused_k;
+  const int32_t* block_table;
+  int64_t bt_stride;
+  const uint8_t* cache;
+  int block_size;
+  int64_t block_stride, head_stride;  // bytes; cells of one (block, head) are contiguous (slot stride == cell)
+  int ks_off, v_off, vs_off;
+  int nq, nkv, group;  // query heads, KV heads, query heads per KV head
+  float qk_scale;      // softmax_scale / head_size * log2(e)
+  const uint32_t* sign_bits;
+  int q_rotated;  // q already in the RHT domain
+  int num_splits;
+  float* part_o;    // [tokens][nq][splits][HS]
+  float* part_lse;  // [tokens][nq][splits], log2 units
+};
+
+template <int FMT>
+struct Cell {
+  static constexpr int BYTES = FMT == FMT_INT4 ? DEC_HS + 8 : DEC_HS * 3 / 2 + 8;
+};
+
+template <int NT>
+struct PLayout {
+  // P^T in shared memory: [64 tokens][8 NT rows] fp16, row stride chosen for conflict-free ldmatrix.trans
+  static constexpr int STRIDE = NT == 1 ? 16 : (NT == 2 ? 48 : (NT == 3 ? 48 : 80));
+};
+
+template <int FMT, int NT>
+struct DecSmem {
+  static constexpr int CELL = Cell<FMT>::BYTES;
+  static constexpr int STAGE_BYTES = DEC_TILE * CELL;
+  static constexpr int OFF_STAGES = 0;
+  static constexpr int OFF_Q = OFF_STAGES + DEC_STAGES * STAGE_BYTES;
+  static constexpr int OFF_P = OFF_Q + DEC_MAX_ROWS * Q_STRIDE;
+  static constexpr int OFF_RED = OFF_P + DEC_TILE * PLayout<NT>::STRIDE;  // [4][32] f32
+  static constexpr int OFF_VS = OFF_RED + 4 * DEC_MAX_ROWS * 4;           // [4] f32
+  static constexpr int OFF_ROWP = OFF_VS + 16;                            // qscale, cq, qsum: [3][32]
+  static constexpr int OFF_BAR = (OFF_ROWP + 3 * DEC_MAX_ROWS * 4 + 7) / 8 * 8;
+  static constexpr int BYTES = OFF_BAR + DEC_STAGES * 8;
+};
+
+// k index (0..255) of the QK MMA that carries channel c (see the fragment mapping in decode_kernel).
+template <int FMT>
+__device__ __forceinline__ int qk_k_of_channel(int c) {
+  if constexpr (FMT == FMT_INT4) {
+    // word W = 8 t + j of the key row feeds k-steps 2j (h = 0) and 2j + 1 (h = 1) of lane quad t; inside the word,
+    // nibble r = (2h + f) + 4e is element e of register f.
+    const int W = c >> 3, r = c & 7;
+    const int t = W >> 3, j = W & 7;
+    const int h = (r & 3) >> 1, f = r & 1, e = r >> 2;
+    return 16 * (2 * j + h) + 2 * t + e + 8 * f;
+  } else {
+    // word W of the int8 key row: k-step s = W & 7 (W < 32) or 8 + (W & 7) (W >= 32) of lane quad t = (W >> 3) & 3;
+    // byte 2f + e is element e of register f.
+    const int W = c >> 2;
+    const int f = (c >> 1) & 1, e = c & 1;
+    const int t = (W >> 3) & 3;
+    const int s = (W < 32 ? 0 : 8) + (W & 7);
+    return 16 * s + 2 * t + e + 8 * f;
+  }
+}
+
+// Row of P^T (the PV MMA's k index inside the tile) that holds tile-local token tau: lane quad t of k-step kk reads
+// tokens 16 kk + 4 t + {0, 1, 2, 3} as k = 2 t, 2 t + 1, 2 t + 8, 2 t + 9.
+__device__ __forceinline__ int pv_k_of_token(int tau) {
+  const int kk = tau >> 4, u = tau & 15;
+  const int t = u >> 2, f = (u >> 1) & 1, e = u & 1;
+  return 16 * kk + 2 * t + e + 8 * f;
+}
+
+// fp16 pair -> exact nibble values: low-nibble form (1024 + u) minus 1024; high-nibble form (1024 + 16 u) / 16 - 64.
+__device__ __forceinline__ uint32_t nib_lo(uint32_t x) {
+  return hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), 0x64006400u);
+}
+__device__ __forceinline__ uint32_t nib_hi(uint32_t x) {
+  return hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u /* 1/16 */, 0xD400D400u /* -64 */);
+}
+
+template <int FMT, int DT, int NT>
+__global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodeParams p) {
+  using SM = DecSmem<FMT, NT>;
+  constexpr int CELL = SM::CELL;
+  constexpr int PSTRIDE = PLayout<NT>::STRIDE;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* stages = smem + SM::OFF_STAGES;
+  uint8_t* qsm = smem + SM::OFF_Q;
+  uint8_t* psm = smem + SM::OFF_P;
+  float* red = reinterpret_cast<float*>(smem + SM::OFF_RED);
+  float* red_vs = reinterpret_cast<float*>(smem + SM::OFF_VS);
+  float* row_qscale = reinterpret_cast<float*>(smem + SM::OFF_ROWP);
+  float* row_cq = row_qscale + DEC_MAX_ROWS;
+  float* row_qsum = row_cq + DEC_MAX_ROWS;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::OFF_BAR);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+
+  // Let the merge kernel (launched with programmatic stream serialization) start its launch now; it waits for this
+  // grid's completion before reading anything.
+  asm volatile("griddepcontrol.launch_dependents;");
+
+  const int q0 = p.cu_seqlens_q[seq];
+  const int qlen = p.cu_seqlens_q[seq + 1] - q0;
+  const int n = p.seqused_k[seq];
+  const int rows = qlen * p.group;
+  if (qlen <= 0) return;
+
+  const int n_tiles = (n + DEC_TILE - 1) / DEC_TILE;
+  const int tps = (n_tiles + p.num_splits - 1) / p.num_splits;
+  const int tile0 = split * tps;
+  const int ntl = max(0, min(tile0 + tps, n_tiles) - tile0);
+
+  if (ntl == 0) {  // empty segment: lse = -inf
+    for (int r = tid; r < rows; r += DEC_THREADS) {
+      const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
+      p.part_lse[(static_cast<int64_t>(tok) * p.nq + qh) * p.num_splits + split] = -INFINITY;
+    }
+    return;
+  }
+
+  const int32_t* btab = p.block_table + static_cast<int64_t>(seq) * p.bt_stride;
+  const uint8_t* head_base = p.cache + static_cast<int64_t>(kvh) * p.head_stride;
+
+  // --- producer: one thread issues the bulk copies of a tile (whole 16-token runs; block_size % 16 == 0, so a run
+  // never crosses a block, and the last run of a sequence stays inside the block that holds its last token) -----
+  auto issue_tile = [&](int i) {
+    const int stage = i % DEC_STAGES;
+    const int tok_begin = (tile0 + i) * DEC_TILE;
+    const int tok_end = min(tok_begin + DEC_TILE, n);
+    const int groups = (tok_end - tok_begin + 15) >> 4;
+    mbar_arrive_expect_tx(&bars[stage], static_cast<uint32_t>(groups * 16 * CELL));
+    uint8_t* dst = stages + stage * SM::STAGE_BYTES;
+    for (int gi = 0; gi < groups;) {
+      const int tok = tok_begin + gi * 16;
+      const int blk = btab[tok / p.block_size];
+      const int in_blk = tok % p.block_size;
+      const int run = min(groups - gi, (p.block_size - in_blk) >> 4);
+      const uint8_t* src = head_base + static_cast<int64_t>(blk) * p.block_stride + static_cast<int64_t>(in_blk) * CELL;
+      bulk_g2s(dst + gi * 16 * CELL, src, static_cast<uint32_t>(run * 16 * CELL), &bars[stage]);
+      gi += run;
+    }
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int issued = 0;  // tiles whose copies thread 0 has issued
+  if (tid == 0) {
+    issued = min(ntl, DEC_STAGES);
+    for (int i = 0; i < issued; ++i) issue_tile(i);
+  }
+
+  // --- Q: rotate, scale to fp16 with a per-row power of two, permute channels ------------------------------
+  {
+    using EL = Elem<DT>;
+    for (int r = warp; r < DEC_MAX_ROWS; r += 4) {
+      __half* qrow = reinterpret_cast<__half*>(qsm + r * Q_STRIDE);
+      if (r >= rows) {
+        for (int c = lane; c < DEC_HS; c += 32) qrow[c] = __float2half_rn(0.f);
+        if (lane == 0) {
+          row_qscale[r] = 0.f;
+          row_cq[r] = 0.f;
+          row_qsum[r] = 0.f;
+        }
+        continue;
+      }
+      const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
+      const typename EL::T* src = reinterpret_cast<const typename EL::T*>(p.q) + tok * p.q_st + qh * p.q_sh + lane * 8;
+      float x[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = EL::to_f(src[i]);
+      if (!p.q_rotated) {
+        apply_signs<8>(x, p.sign_bits, lane);
+        warp_wht<8>(x, lane);
+      }
+      float am = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(x[i]));
+      am = warp_max(am);
+      int ex = 0;
+      if (am > 0.f) {
+        frexpf(am, &ex);  // am < 2^ex
+        ex = 14 - ex;     // am * 2^ex in [2^13, 2^14)
+      }
+      float cq = 0.f, qs = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = lane * 8 + i;
+        const __half h = __float2half_rn(ldexpf(x[i], ex));
+        const float hv = __half2float(h);
+        qs += hv;
+        if constexpr (FMT == FMT_INT4) {
+          const bool odd = c & 1;
+          cq += odd ? 64.f * hv : 1024.f * hv;
+          qrow[qk_k_of_channel<FMT>(c)] = odd ? __float2half_rn(hv * 0.0625f) : h;
+        } else {
+          cq += 1152.f * hv;
+          qrow[qk_k_of_channel<FMT>(c)] = h;
+        }
+      }
+      cq = warp_sum(cq);
+      qs = warp_sum(qs);
+      if (lane == 0) {
+        row_qscale[r] = ldexpf(p.qk_scale, -ex);
+        row_cq[r] = cq;
+        row_qsum[r] = qs;
+      }
+    }
+  }
+  __syncthreads();
+
+  // --- per-thread state ------------------------------------------------------------------------------------
+  float o[4][NT][4];
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) o[mt][nt][c] = 0.f;
+  float m_run[NT][2], l_part[NT][2], c_part[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      m_run[nt][e] = -INFINITY;
+      l_part[nt][e] = 0.f;
+      c_part[nt][e] = 0.f;
+    }
+  int e_run = -1000;                     // running power-of-two range of P_v (value scales)
+  const int causal_from = n - qlen + 1;  // keys >= this are hidden from some query token
+  const uint32_t qsm_base = smem_u32(qsm);
+  const uint32_t psm_base = smem_u32(psm);
+  bool failed = false;
+  int fail_tile = ntl;
+
+  for (int i = 0; i < ntl; ++i) {
+    const int stage = i % DEC_STAGES;
+    // A thread whose wait runs out keeps going on whatever the stage holds (nothing reaches global memory before
+    // the epilogue); the CTA leaves together at barrier (A), so no thread skips a __syncthreads.
+    failed |= !mbar_wait_bounded(&bars[stage], (i / DEC_STAGES) & 1);
+    const uint8_t* tile = stages + stage * SM::STAGE_BYTES;
+    const int tok_base = (tile0 + i) * DEC_TILE;
+
+    // ---------------- QK: warp handles tokens 16 warp + [0, 16) ----------------
+    float sacc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sacc[nt][c] = 0.f;
+    const uint8_t* rowg = tile + (16 * warp + g) * CELL;
+    const uint8_t* rowg8 = rowg + 8 * CELL;
+    if constexpr (FMT == FMT_INT4) {
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const uint2 wa = *reinterpret_cast<const uint2*>(rowg + 4 * (8 * t + 2 * jj));
+        const uint2 wb = *reinterpret_cast<const uint2*>(rowg8 + 4 * (8 * t + 2 * jj));
+#pragma unroll
+        for (int hw = 0; hw < 2; ++hw) {
+          const int j = 2 * jj + hw;
+          const uint32_t xa = hw ? wa.y : wa.x, xb = hw ? wb.y : wb.x;
+          const uint32_t xa8 = xa >> 8, xb8 = xb >> 8;
+          uint32_t A0[4], A1[4];  // k-steps 2j (h = 0) and 2j + 1 (h = 1)
+          A0[0] = lop3_and_or(xa, 0x000F000Fu, 0x64006400u);
+          A0[1] = lop3_and_or(xb, 0x000F000Fu, 0x64006400u);
+          A0[2] = lop3_and_or(xa, 0x00F000F0u, 0x64006400u);
+          A0[3] = lop3_and_or(xb, 0x00F000F0u, 0x64006400u);
+          A1[0] = lop3_and_or(xa8, 0x000F000Fu, 0x64006400u);
+          A1[1] = lop3_and_or(xb8, 0x000F000Fu, 0x64006400u);
+          A1[2] = lop3_and_or(xa8, 0x00F000F0u, 0x64006400u);
+          A1[3] = lop3_and_or(xb8, 0x00F000F0u, 0x64006400u);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4(b0, b1, b2, b3, qsm_base + (8 * nt + (lane & 7)) * Q_STRIDE + (32 * j + 8 * (lane >> 3)) * 2);
+            mma_f16_16816(sacc[nt], A0, b0, b1);
+            mma_f16_16816(sacc[nt], A1, b2, b3);
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int wbase = half * 32 + 8 * t + 2 * jj;  // words wbase, wbase + 1 = k-steps s0, s0 + 1
+          const int s0 = half * 8 + 2 * jj;
+          const uint2 wa = *reinterpret_cast<const uint2*>(rowg + 4 * wbase);
+          const uint2 wb = *reinterpret_cast<const uint2*>(rowg8 + 4 * wbase);
+          uint32_t A[2][4];
+#pragma unroll
+          for (int hw = 0; hw < 2; ++hw) {
+            const uint32_t xa = (hw ? wa.y : wa.x) ^ 0x80808080u, xb = (hw ? wb.y : wb.x) ^ 0x80808080u;
+            A[hw][0] = prmt(xa, 0x64646464u, 0x4140u);  // {1024 + 128 + c0, 1024 + 128 + c1}
+            A[hw][1] = prmt(xb, 0x64646464u, 0x4140u);
+            A[hw][2] = prmt(xa, 0x64646464u, 0x4342u);  // {.. + c2, .. + c3}
+            A[hw][3] = prmt(xb, 0x64646464u, 0x4342u);
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4(b0, b1, b2, b3, qsm_base + (8 * nt + (lane & 7)) * Q_STRIDE + (16 * s0 + 8 * (lane >> 3)) * 2);
+            mma_f16_16816(sacc[nt], A[0], b0, b1);
+            mma_f16_16816(sacc[nt], A[1], b2, b3);
+          }
+        }
+      }
+    }
+
+    // ---------------- scores (log2 units), masks, tile row max ----------------
+    const int tau_a = 16 * warp + g, tau_b = tau_a + 8;
+    const int tok_a = tok_base + tau_a, tok_b = tok_base + tau_b;
+    float ks_a, ks_b, kz_a = 0.f, kz_b = 0.f;
+    {
+      const uint32_t wa = *reinterpret_cast<const uint32_t*>(tile + tau_a * CELL + p.ks_off);
+      const uint32_t wb = *reinterpret_cast<const uint32_t*>(tile + tau_b * CELL + p.ks_off);
+      if constexpr (FMT == FMT_INT4) {
+        ks_a = __uint_as_float(wa & 0xFFFFFFF0u);
+        ks_b = __uint_as_float(wb & 0xFFFFFFF0u);
+        kz_a = static_cast<float>(wa & 0xFu);
+        kz_b = static_cast<float>(wb & 0xFu);
+      } else {
+        ks_a = __uint_as_float(wa);
+        ks_b = __uint_as_float(wb);
+      }
+    }
+    const bool need_mask = tok_base + DEC_TILE > causal_from;
+    float sc[NT][4];
+    float tmax[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int r = 8 * nt + 2 * t + e;
+        const float qsc = row_qscale[r], cq = row_cq[r], qsum = row_qsum[r];
+        float s0 = (sacc[nt][e] - fmaf(kz_a, qsum, cq)) * (ks_a * qsc);
+        float s1 = (sacc[nt][2 + e] - fmaf(kz_b, qsum, cq)) * (ks_b * qsc);
+        if (need_mask) {
+          const int lim = n - qlen + r / p.group;  // last key this row sees
+          const bool row_ok = r < rows;
+          if (!(row_ok && tok_a < n && tok_a <= lim)) s0 = -INFINITY;
+          if (!(row_ok && tok_b < n && tok_b <= lim)) s1 = -INFINITY;
+        }
+        sc[nt][e] = s0;
+        sc[nt][2 + e] = s1;
+        float mx = fmaxf(s0, s1);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        tmax[nt][e] = mx;
+      }
+    }
+    // value scales of this thread's two tokens (tokens past the end count as 0)
+    float vs_a, vs_b, vz_a, vz_b;
+    {
+      const uint32_t wa = *reinterpret_cast<const uint32_t*>(tile + tau_a * CELL + p.vs_off);
+      const uint32_t wb = *reinterpret_cast<const uint32_t*>(tile + tau_b * CELL + p.vs_off);
+      vs_a = tok_a < n ? __uint_as_float(wa & 0xFFFFFFF0u) : 0.f;
+      vs_b = tok_b < n ? __uint_as_float(wb & 0xFFFFFFF0u) : 0.f;
+      vz_a = static_cast<float>(wa & 0xFu);
+      vz_b = static_cast<float>(wb & 0xFu);
+    }
+    {
+      const float vm = warp_max(fmaxf(vs_a, vs_b));
+      if (g == 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          red[warp * DEC_MAX_ROWS + 8 * nt + 2 * t] = tmax[nt][0];
+          red[warp * DEC_MAX_ROWS + 8 * nt + 2 * t + 1] = tmax[nt][1];
+        }
+      }
+      if (lane == 0) red_vs[warp] = vm;
+    }
+    // (A) row maxima visible; every warp is done with tile i - 1
+    if (__syncthreads_or(failed)) {
+      failed = true;
+      fail_tile = i;
+      break;
+    }
+    if (tid == 0 && i >= 1 && i - 1 + DEC_STAGES < ntl) {
+      issue_tile(i - 1 + DEC_STAGES);
+      ++issued;
+    }
+
+    // running max, value range, rescale
+    {
+      const float vmax = fmaxf(fmaxf(red_vs[0], red_vs[1]), fmaxf(red_vs[2], red_vs[3]));
+      int e_tile = -1000;
+      if (vmax > 0.f) frexpf(vmax, &e_tile);  // vmax < 2^e_tile
+      const int e_new = max(e_run, e_tile);
+      const float o_range = e_run == -1000 ? 1.f : ldexpf(1.f, e_run - e_new);
+      const float pv_mul = e_new == -1000 ? 0.f : ldexpf(1.f, -e_new);
+      e_run = e_new;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int r = 8 * nt + 2 * t + e;
+          const float mt_ = fmaxf(fmaxf(red[r], red[DEC_MAX_ROWS + r]),
+                                  fmaxf(red[2 * DEC_MAX_ROWS + r], red[3 * DEC_MAX_ROWS + r]));
+          const float m_new = fmaxf(m_run[nt][e], mt_);
+          const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run[nt][e] - m_new);
+          const float base = m_new == -INFINITY ? 0.f : m_new;
+          m_run[nt][e] = m_new;
+          const float ao = alpha * o_range;
+          l_part[nt][e] *= alpha;
+          c_part[nt][e] *= ao;
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt) {
+            o[mt][nt][e] *= ao;
+            o[mt][nt][2 + e] *= ao;
+          }
+          const float pa = exp2f(sc[nt][e] - base);
+          const float pb = exp2f(sc[nt][2 + e] - base);
+          l_part[nt][e] += pa + pb;
+          sc[nt][e] = pa * vs_a * pv_mul;  // P_v, fp32
+          sc[nt][2 + e] = pb * vs_b * pv_mul;
+        }
+        // round P_v to fp16 (the values the MMA uses); zero-point sums from the same rounded values
+        const __half2 ha = __floats2half2_rn(sc[nt][0], sc[nt][1]);
+        const __half2 hb = __floats2half2_rn(sc[nt][2], sc[nt][3]);
+        const float2 fa = __half22float2(ha), fb = __half22float2(hb);
+        c_part[nt][0] += fa.x * vz_a + fb.x * vz_b;
+        c_part[nt][1] += fa.y * vz_a + fb.y * vz_b;
+        *reinterpret_cast<__half2*>(psm + pv_k_of_token(tau_a) * PSTRIDE + (8 * nt + 2 * t) * 2) = ha;
+        *reinterpret_cast<__half2*>(psm + pv_k_of_token(tau_b) * PSTRIDE + (8 * nt + 2 * t) * 2) = hb;
+      }
+    }
+    __syncthreads();  // (B) P^T visible
+
+    // ---------------- PV: warp handles channels 64 warp + [0, 64) ----------------
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t bf[NT][2];
+      {
+        const int mi = lane >> 3;
+        const int krow = 16 * kk + (mi & 1) * 8 + (lane & 7);
+        if constexpr (NT == 1) {
+          ldmatrix_x2_trans(bf[0][0], bf[0][1], psm_base + krow * PSTRIDE);
+        } else {
+          ldmatrix_x4_trans(bf[0][0], bf[0][1], bf[1][0], bf[1][1], psm_base + krow * PSTRIDE + (mi >> 1) * 16);
+          if constexpr (NT == 3) {
+            ldmatrix_x2_trans(bf[2][0], bf[2][1], psm_base + krow * PSTRIDE + 32);
+          } else if constexpr (NT == 4) {
+            ldmatrix_x4_trans(bf[2][0], bf[2][1], bf[3][0], bf[3][1], psm_base + krow * PSTRIDE + 32 + (mi >> 1) * 16);
+          }
+        }
+      }
+      const uint8_t* vbase = tile + p.v_off + 4 * (8 * warp + g);
+      const int tau0 = 16 * kk + 4 * t;
+      const uint32_t w0 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 0) * CELL);
+      const uint32_t w1 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 1) * CELL);
+      const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 2) * CELL);
+      const uint32_t w3 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 3) * CELL);
+      // f = 0: tokens (tau0, tau0 + 1); f = 1: tokens (tau0 + 2, tau0 + 3)
+      uint32_t vr[2][8];  // [f][channel offset 0..7]
+#pragma unroll
+      for (int f = 0; f < 2; ++f) {
+        const uint32_t wa = f ? w2 : w0, wb = f ? w3 : w1;
+        const uint32_t x = prmt(wa, wb, 0x5410u), y = prmt(wa, wb, 0x7632u);
+        const uint32_t x8 = x >> 8, y8 = y >> 8;
+        vr[f][0] = nib_lo(x);
+        vr[f][1] = nib_hi(x);
+        vr[f][2] = nib_lo(x8);
+        vr[f][3] = nib_hi(x8);
+        vr[f][4] = nib_lo(y);
+        vr[f][5] = nib_hi(y);
+        vr[f][6] = nib_lo(y8);
+        vr[f][7] = nib_hi(y8);
+      }
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        const uint32_t A[4] = {vr[0][2 * mt], vr[0][2 * mt + 1], vr[1][2 * mt], vr[1][2 * mt + 1]};
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_f16_16816(o[mt][nt], A, bf[nt][0], bf[nt][1]);
+      }
+    }
+  }
+
+  if (failed) {
+    // give the copies still in flight a bounded chance to land before the CTA's shared memory goes away
+    if (tid == 0) {
+      for (int j = fail_tile; j < issued; ++j)
+        mbar_wait_bounded(&bars[j % DEC_STAGES], (j / DEC_STAGES) & 1, 100000000ull);
+    }
+    __syncthreads();
+    return;
+  }
+
+  // --- epilogue: totals of l and the zero-point sums, normalised partial O and lse -------------------------
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float l = l_part[nt][e], c = c_part[nt][e];
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        l += __shfl_xor_sync(0xffffffffu, l, off);
+        c += __shfl_xor_sync(0xffffffffu, c, off);
+      }
+      l_part[nt][e] = l;
+      c_part[nt][e] = c;
+    }
+  __syncthreads();
+  float* red_l = red;                            // [4][32]
+  float* red_c = reinterpret_cast<float*>(psm);  // [4][32]: P^T is no longer needed
+  if (g == 0) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        red_l[warp * DEC_MAX_ROWS + 8 * nt + 2 * t + e] = l_part[nt][e];
+        red_c[warp * DEC_MAX_ROWS + 8 * nt + 2 * t + e] = c_part[nt][e];
+      }
+  }
+  __syncthreads();
+  const float o_unit = e_run == -1000 ? 0.f : ldexpf(1.f, e_run);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int r = 8 * nt + 2 * t + e;
+      if (r >= rows) continue;
+      const float l = red_l[r] + red_l[DEC_MAX_ROWS + r] + red_l[2 * DEC_MAX_ROWS + r] + red_l[3 * DEC_MAX_ROWS + r];
+      const float c = red_c[r] + red_c[DEC_MAX_ROWS + r] + red_c[2 * DEC_MAX_ROWS + r] + red_c[3 * DEC_MAX_ROWS + r];
+      const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
+      const int64_t prow = (static_cast<int64_t>(tok) * p.nq + qh) * p.num_splits + split;
+      const float inv = l > 0.f ? o_unit / l : 0.f;
+      float v[8];
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        v[2 * mt] = (o[mt][nt][e] - c) * inv;
+        v[2 * mt + 1] = (o[mt][nt][2 + e] - c) * inv;
+      }
+      float4* dst = reinterpret_cast<float4*>(p.part_o + prow * DEC_HS + 64 * warp + 8 * g);
+      dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+      dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+      if (warp == 0 && g == 0) p.part_lse[prow] = l > 0.f ? m_run[nt][e] + log2f(l) : -INFINITY;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------- K2 merge
+struct MergeParams {
+  const float* part_o;
+  const float* part_lse;     // log2 units
+  int64_t po_t, po_h, po_s;  // element strides of part_o (token, head, part); channel stride 1
+  int64_t pl_t, pl_h, pl_s;
+  int num_splits;
+  int nq;
+  int mode;  // 0: inverse RHT / head, cast to the model dtype; 1: fp32 RHT-domain O and lse (log2) out
+  void* out;
+  int64_t out_st, out_sh;  // element strides of out
+  float* lse_out;          // mode 1 (may be null)
+  int64_t lo_t, lo_h;
+  const uint32_t* sign_bits;
+  float out_scale;  // multiplies the output (mode 0: 1 / head)
+};
+
+template <int DT, int HS>
+__global__ void __launch_bounds__(256) merge_kernel(const MergeParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  constexpr int C4 = HS / 4;    // float4 groups per row
+  constexpr int SG = 256 / C4;  // split groups
+  __shared__ float w_sm[1024];
+  __shared__ __align__(16) float acc_sm[SG][HS];
+  __shared__ float red[8];
+  __shared__ float tot_sm;
+  const int tok = blockIdx.x, qh = blockIdx.y, tid = threadIdx.x;
+  const float* lse = p.part_lse + tok * p.pl_t + qh * p.pl_h;
+  float mx = -INFINITY;
+  for (int s = tid; s < p.num_splits; s += 256) mx = fmaxf(mx, lse[s * p.pl_s]);
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  float M = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) M = fmaxf(M, red[i]);
+  float tot = 0.f;
+  for (int s = tid; s < p.num_splits; s += 256) {
+    const float l = lse[s * p.pl_s];
+    const float w = (M == -INFINITY || l == -INFINITY) ? 0.f : exp2f(l - M);
+    w_sm[s] = w;
+    tot += w;
+  }
+  tot = warp_sum(tot);
+  __syncthreads();
+  if ((tid & 31) == 0) red[tid >> 5] = tot;
+  __syncthreads();
+  if (tid == 0) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += red[i];
+    tot_sm = s;
+  }
+  const int c4 = tid % C4, sg = tid / C4;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float* po = p.part_o + tok * p.po_t + qh * p.po_h + 4 * c4;
+#pragma unroll 4
+  for (int s = sg; s < p.num_splits; s += SG) {
+    const float w = w_sm[s];
+    if (w == 0.f) continue;
+    const float4 v = *reinterpret_cast<const float4*>(po + s * p.po_s);
+    a.x = fmaf(w, v.x, a.x);
+    a.y = fmaf(w, v.y, a.y);
+    a.z = fmaf(w, v.z, a.z);
+    a.w = fmaf(w, v.w, a.w);
+  }
+  *reinterpret_cast<float4*>(&acc_sm[sg][4 * c4]) = a;
+  __syncthreads();
+  const float T = tot_sm;
+  const float inv = T > 0.f ? 1.f / T : 0.f;
+  if (p.mode == 1) {
+    for (int c = tid; c < HS; c += 256) {
+      float v = 0.f;
+#pragma unroll
+      for (int s = 0; s < SG; ++s) v += acc_sm[s][c];
+      reinterpret_cast<float*>(p.out)[tok * p.out_st + qh * p.out_sh + c] = v * inv;
+    }
+    if (tid == 0 && p.lse_out) p.lse_out[tok * p.lo_t + qh * p.lo_h] = T > 0.f ? M + log2f(T) : -INFINITY;
+    return;
+  }
+  if (tid < 32) {
+    constexpr int E = HS / 32;
+    float x[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      float v = 0.f;
+#pragma unroll
+      for (int s = 0; s < SG; ++s) v += acc_sm[s][tid * E + i];
+      x[i] = v * inv;
+    }
+    warp_wht<E>(x, tid);
+    apply_signs<E>(x, p.sign_bits, tid);
+    using EL = Elem<DT>;
+    typename EL::T* dst = reinterpret_cast<typename EL::T*>(p.out) + tok * p.out_st + qh * p.out_sh + tid * E;
+#pragma unroll
+    for (int i = 0; i < E; ++i) dst[i] = EL::from_f(x[i] * p.out_scale);
+  }
+}
+
+template <int DT, int HS>
+static int launch_merge(const MergeParams& mp, int num_tokens, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(num_tokens), static_cast<unsigned>(mp.nq));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, merge_kernel<DT, HS>, mp);
+  if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "merge launch: %s", cudaGetErrorString(e));
+  return QP_OK;
+}
+
+static int merge_dispatch(const MergeParams& mp, int dtype, int head_size, int64_t num_tokens, cudaStream_t st,
+                          bool pdl) {
+  if (num_tokens == 0) return QP_OK;
+  if (mp.num_splits > 1024) return set_error(QP_ERR_UNSUPPORTED, "merge: %d partials > 1024", mp.num_splits);
+  if (num_tokens > 0x7fffffff) return set_error(QP_ERR_UNSUPPORTED, "merge: too many tokens");
+  const int nt = static_cast<int>(num_tokens);
+  switch (head_size) {
+    case 256:
+      return dtype == DT_BF16 ? launch_merge<DT_BF16, 256>(mp, nt, st, pdl) : launch_merge<DT_F16, 256>(mp, nt, st, pdl);
+    case 512:
+      return dtype == DT_BF16 ? launch_merge<DT_BF16, 512>(mp, nt, st, pdl) : launch_merge<DT_F16, 512>(mp, nt, st, pdl);
+    case 128:
+      return dtype == DT_BF16 ? launch_merge<DT_BF16, 128>(mp, nt, st, pdl) : launch_merge<DT_F16, 128>(mp, nt, st, pdl);
+    default:
+      return set_error(QP_ERR_UNSUPPORTED, "merge: head size %d", head_size);
+  }
+}
+
+template <int FMT, int DT, int NT>
+static int launch_decode_t(const DecodeParams& dp, int num_seqs, cudaStream_t st) {
+  using SM = DecSmem<FMT, NT>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(decode_kernel<FMT, DT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES);
+    if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode smem attribute: %s", cudaGetErrorString(e));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const dim3 grid(static_cast<unsigned>(dp.num_splits), static_cast<unsigned>(dp.nkv), static_cast<unsigned>(num_seqs));
+  decode_kernel<FMT, DT, NT><<<grid, DEC_THREADS, SM::BYTES, st>>>(dp);
+  return check_launch("decode");
+}
+
+template <int FMT, int DT>
+static int launch_decode_nt(const DecodeParams& dp, int nt, int num_seqs, cudaStream_t st) {
+  switch (nt) {
+    case 1: return launch_decode_t<FMT, DT, 1>(dp, num_seqs, st);
+    case 2: return launch_decode_t<FMT, DT, 2>(dp, num_seqs, st);
+    case 3: return launch_decode_t<FMT, DT, 3>(dp, num_seqs, st);
+    default: return launch_decode_t<FMT, DT, 4>(dp, num_seqs, st);
+  }
+}
+
+}  // namespace qp
+
+using namespace qp;
+
+// Split-count heuristic: whole waves of 2 CTAs per SM, a fixed cost per CTA, at least 4 tiles per split.
+extern "C" int qp_decode_num_splits(int num_seqs, int num_kv_heads, int max_seqlen_k, int sm_count) {
+  if (sm_count <= 0) sm_count = device_sm_count();
+  const int pairs = max(1, num_seqs * num_kv_heads);
+  const int tiles = max(1, (max_seqlen_k + DEC_TILE - 1) / DEC_TILE);
+  const int slots = 2 * sm_count;
+  const int max_splits = max(1, min(1024, tiles / 4));
+  int best = 1;
+  double best_cost = 1e30;
+  for (int s = 1; s <= max_splits; ++s) {
+    const long ctas = static_cast<long>(pairs) * s;
+    const long waves = (ctas + slots - 1) / slots;
+    const double cost = waves * (static_cast<double>((tiles + s - 1) / s) + 6.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
+extern "C" int64_t qp_decode_workspace_bytes(int64_t num_q_tokens, int num_q_heads, int head_size, int num_splits) {
+  const int64_t rows = num_q_tokens * num_q_heads * static_cast<int64_t>(num_splits);
+  return rows * head_size * 4 + ((rows * 4 + 255) / 256) * 256;
+}
+
+extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                               void* out, int64_t out_stride_token, int64_t out_stride_head, int64_t num_q_tokens,
+                               int num_seqs, const int32_t* cu_seqlens_q, const int32_t* seqused_k, int max_seqlen_q,
+                               const int32_t* block_table, int64_t block_table_stride, const void* cache,
+                               int block_size, int64_t block_stride, int64_t head_stride, int64_t slot_stride,
+                               int64_t k_off, int64_t ks_off, int64_t v_off, int64_t vs_off, int num_q_heads,
+                               int num_kv_heads, int head_size, float softmax_scale, const uint32_t* rht_sign_bits,
+                               int q_rotated, int out_mode, float* lse_out, int num_splits, void* workspace,
+                               int64_t workspace_bytes, void* stream) {
+  if (fmt != FMT_INT4 && fmt != FMT_K8V4) return set_error(QP_ERR_UNSUPPORTED, "decode: format %d", fmt);
+  if (dtype != DT_BF16 && dtype != DT_F16) return set_error(QP_ERR_UNSUPPORTED, "decode: dtype %d", dtype);
+  if (head_size != DEC_HS) return set_error(QP_ERR_UNSUPPORTED, "decode: head size %d (this build: 256)", head_size);
+  if (num_seqs < 0 || num_q_tokens < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads)
+    return set_error(QP_ERR_INVALID, "decode: bad sizes (seqs %d, tokens %lld, heads %d/%d)", num_seqs,
+                     (long long)num_q_tokens, num_q_heads, num_kv_heads);
+  if (num_seqs == 0 || num_q_tokens == 0) return QP_OK;
+  if (num_seqs > 65535 || num_kv_heads > 65535) return set_error(QP_ERR_UNSUPPORTED, "decode: grid too large");
+  const int group = num_q_heads / num_kv_heads;
+  if (max_seqlen_q < 1 || max_seqlen_q * group > DEC_MAX_ROWS)
+    return set_error(QP_ERR_UNSUPPORTED, "decode: %d query tokens x %d heads per KV head > %d rows", max_seqlen_q,
+                     group, DEC_MAX_ROWS);
+  if (out_mode < 0 || out_mode > 2) return set_error(QP_ERR_INVALID, "decode: out_mode %d", out_mode);
+  const int cell = fmt == FMT_INT4 ? DEC_HS + 8 : DEC_HS * 3 / 2 + 8;
+  if (slot_stride != cell)
+    return set_error(QP_ERR_LAYOUT, "decode: cells of a (block, head) must be contiguous (slot stride %lld, cell %d)",
+                     (long long)slot_stride, cell);
+  const int kb = fmt == FMT_INT4 ? DEC_HS / 2 : DEC_HS;
+  if (k_off != 0 || ks_off != kb || v_off != kb + 4 || vs_off != kb + 4 + DEC_HS / 2)
+    return set_error(QP_ERR_LAYOUT, "decode: unexpected cell field offsets");
+  if (block_size <= 0 || block_size % 16 || (reinterpret_cast<uintptr_t>(cache) & 15) || (block_stride & 15) ||
+      (head_stride & 15))
+    return set_error(QP_ERR_LAYOUT, "decode: block size must be a multiple of 16 and the cache 16-byte aligned");
+  if (num_splits <= 0) return set_error(QP_ERR_INVALID, "decode: num_splits %d", num_splits);
+  if (num_splits > 1024) return set_error(QP_ERR_UNSUPPORTED, "decode: num_splits %d > 1024", num_splits);
+  if (!q || !out || !cu_seqlens_q || !seqused_k || !block_table || !cache || !rht_sign_bits || !workspace)
+    return set_error(QP_ERR_INVALID, "decode: null pointer");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15) ||
+      workspace_bytes < qp_decode_workspace_bytes(num_q_tokens, num_q_heads, head_size, num_splits))
+    return set_error(QP_ERR_WORKSPACE, "decode: workspace of %lld bytes < %lld", (long long)workspace_bytes,
+                     (long long)qp_decode_workspace_bytes(num_q_tokens, num_q_heads, head_size, num_splits));
+
+  DecodeParams dp{};
+  dp.q = q;
+  dp.q_st = q_stride_token;
+  dp.q_sh = q_stride_head;
+  dp.cu_seqlens_q = cu_seqlens_q;
+  dp.seqused_k = seqused_k;
+  dp.block_table = block_table;
+  dp.bt_stride = block_table_stride;
+  dp.cache = static_cast<const uint8_t*>(cache);
+  dp.block_size = block_size;
+  dp.block_stride = block_stride;
+  dp.head_stride = head_stride;
+  dp.ks_off = static_cast<int>(ks_off);
+  dp.v_off = static_cast<int>(v_off);
+  dp.vs_off = static_cast<int>(vs_off);
+  dp.nq = num_q_heads;
+  dp.nkv = num_kv_heads;
+  dp.group = group;
+  dp.qk_scale = softmax_scale / static_cast<float>(head_size) * LOG2E;
+  dp.sign_bits = rht_sign_bits;
+  dp.q_rotated = q_rotated;
+  dp.num_splits = num_splits;
+  const int64_t rows = num_q_tokens * num_q_heads * static_cast<int64_t>(num_splits);
+  dp.part_o = static_cast<float*>(workspace);
+  dp.part_lse = dp.part_o + rows * head_size;
+
+  const int nt = (max_seqlen_q * group + 7) / 8;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc;
+  if (fmt == FMT_INT4)
+    rc = dtype == DT_BF16 ? launch_decode_nt<FMT_INT4, DT_BF16>(dp, nt, num_seqs, st)
+                          : launch_decode_nt<FMT_INT4, DT_F16>(dp, nt, num_seqs, st);
+  else
+    rc = dtype == DT_BF16 ? launch_decode_nt<FMT_K8V4, DT_BF16>(dp, nt, num_seqs, st)
+                          : launch_decode_nt<FMT_K8V4, DT_F16>(dp, nt, num_seqs, st);
+  if (rc) return rc;
+  if (out_mode == 2) return QP_OK;  // split partials stay in the workspace
+
+  MergeParams mp{};
+  mp.part_o = dp.part_o;
+  mp.part_lse = dp.part_lse;
+  mp.po_t = static_cast<int64_t>(num_q_heads) * num_splits * head_size;
+  mp.po_h = static_cast<int64_t>(num_splits) * head_size;
+  mp.po_s = head_size;
+  mp.pl_t = static_cast<int64_t>(num_q_heads) * num_splits;
+  mp.pl_h = num_splits;
+  mp.pl_s = 1;
+  mp.num_splits = num_splits;
+  mp.nq = num_q_heads;
+  mp.mode = out_mode;
+  mp.out = out;
+  mp.out_st = out_stride_token;
+  mp.out_sh = out_stride_head;
+  mp.lse_out = lse_out;
+  mp.lo_t = num_q_heads;
+  mp.lo_h = 1;
+  mp.sign_bits = rht_sign_bits;
+  mp.out_scale = 1.f / static_cast<float>(head_size);
+  return merge_dispatch(mp, dtype, head_size, num_q_tokens, st, true);
+}
+
+extern "C" int qp_merge_attn_partials(int dtype, int head_size, int64_t num_tokens, int num_q_heads, int num_parts,
+                                      const float* part_o, int64_t po_stride_token, int64_t po_stride_head,
+                                      int64_t po_stride_part, const float* part_lse, int64_t pl_stride_token,
+                                      int64_t pl_stride_head, int64_t pl_stride_part, int out_mode, void* out,
+                                      int64_t out_stride_token, int64_t out_stride_head, float* lse_out,
+                                      const uint32_t* rht_sign_bits, void* stream) {
+  if (num_tokens < 0 || num_q_heads <= 0 || num_parts <= 0) return set_error(QP_ERR_INVALID, "merge: bad sizes");
+  if (num_tokens == 0) return QP_OK;
+  if (out_mode != 0 && out_mode != 1) return set_error(QP_ERR_INVALID, "merge: out_mode %d", out_mode);
+  if (out_mode == 0 && dtype != DT_BF16 && dtype != DT_F16)
+    return set_error(QP_ERR_UNSUPPORTED, "merge: dtype %d", dtype);
+  if (!part_o || !part_lse || !out || (out_mode == 0 && !rht_sign_bits))
+    return set_error(QP_ERR_INVALID, "merge: null pointer");
+  if (((po_stride_token | po_stride_head | po_stride_part) & 3) || (reinterpret_cast<uintptr_t>(part_o) & 15))
+    return set_error(QP_ERR_LAYOUT, "merge: partial rows must be 16-byte aligned");
+  MergeParams mp{};
+  mp.part_o = part_o;
+  mp.part_lse = part_lse;
+  mp.po_t = po_stride_token;
+  mp.po_h = po_stride_head;
+  mp.po_s = po_stride_part;
+  mp.pl_t = pl_stride_token;
+  mp.pl_h = pl_stride_head;
+  mp.pl_s = pl_stride_part;
+  mp.num_splits = num_parts;
+  mp.nq = num_q_heads;
+  mp.mode = out_mode;
+  mp.out = out;
+  mp.out_st = out_stride_token;
+  mp.out_sh = out_stride_head;
+  mp.lse_out = lse_out;
+  mp.lo_t = num_q_heads;
+  mp.lo_h = 1;
+  mp.sign_bits = rht_sign_bits;
+  mp.out_scale = 1.f / static_cast<float>(head_size);
+  return merge_dispatch(mp, out_mode == 1 ? DT_BF16 : dtype, head_size, num_tokens, static_cast<cudaStream_t>(stream),
+                        false);
+}
