@@ -17,9 +17,12 @@
 //   nibbles become fp16 by the exponent-bias trick ((w & 0x000F000F) | 0x64006400 = 1024 + u): one lop3 per two
 //   values, the bias removed once per score (Q.1024 is a per-row constant);
 // - softmax in log2 units with the row max exchanged through shared memory, the V scale folded into P (P_v16 in fp16
-//   with a running power-of-two range), the V zero point folded out as a per-row sum of P_v16 zp;
+//   with a running power-of-two range);
 // - PV: mma.sync with the head dimension as M (64 channels per warp) and the query rows as N; the value nibbles of
-//   two tokens are interleaved by prmt so each register holds one channel of two tokens;
+//   two tokens are interleaved by prmt so each register holds one channel of two tokens, converted to the exact
+//   fp16 (u - zp) of each token. The zero point sits in the operand, so the accumulator that runs over the whole
+//   segment only ever holds the signal; the reference subtracts sum(P_v16 zp) once per tile instead
+//   (int4_kv.py:90-92), which a running accumulator over many tiles cannot do without its rounding bias showing;
 // - each split writes its normalised partial O (fp32, RHT domain) and its log2-sum-exp; K2 folds the splits and
 //   applies the inverse RHT / head, launched with programmatic dependent launch so its launch overlaps K1.
 #include <math.h>
@@ -111,12 +114,19 @@ __device__ __forceinline__ int pv_k_of_token(int tau) {
   return 16 * kk + 2 * t + e + 8 * f;
 }
 
-// fp16 pair -> exact nibble values: low-nibble form (1024 + u) minus 1024; high-nibble form (1024 + 16 u) / 16 - 64.
-__device__ __forceinline__ uint32_t nib_lo(uint32_t x) {
-  return hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), 0x64006400u);
+// fp16 pair -> exact (nibble - zero point) of two tokens a, b: the low-nibble form (1024 + u) minus (1024 + zp), the
+// high-nibble form (1024 + 16 u) / 16 - (64 + zp). The zero point enters the operand itself (not a correction summed
+// apart), so the fp32 accumulator only ever holds the signal sum P (u - zp).
+__device__ __forceinline__ uint32_t nib_lo(uint32_t x, uint32_t lo_bias) {
+  return hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_bias);
 }
-__device__ __forceinline__ uint32_t nib_hi(uint32_t x) {
-  return hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u /* 1/16 */, 0xD400D400u /* -64 */);
+__device__ __forceinline__ uint32_t nib_hi(uint32_t x, uint32_t hi_bias) {
+  return hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u /* 1/16 */, hi_bias);
+}
+// fp16x2 {1024 + za, 1024 + zb} and {-(64 + za), -(64 + zb)} for zero points za, zb in [0, 15].
+__device__ __forceinline__ uint32_t zp_lo_bias(uint32_t za, uint32_t zb) { return 0x64006400u | za | (zb << 16); }
+__device__ __forceinline__ uint32_t zp_hi_bias(uint32_t za, uint32_t zb) {
+  return 0xD400D400u | (za << 4) | (zb << 20);
 }
 
 template <int FMT, int DT, int NT>
@@ -263,14 +273,13 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int c = 0; c < 4; ++c) o[mt][nt][c] = 0.f;
-  float m_run[NT][2], l_part[NT][2], c_part[NT][2];
+  float m_run[NT][2], l_part[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       m_run[nt][e] = -INFINITY;
       l_part[nt][e] = 0.f;
-      c_part[nt][e] = 0.f;
     }
   int e_run = -1000;                     // running power-of-two range of P_v (value scales)
   const int causal_from = n - qlen + 1;  // keys >= this are hidden from some query token
@@ -396,14 +405,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
       }
     }
     // value scales of this thread's two tokens (tokens past the end count as 0)
-    float vs_a, vs_b, vz_a, vz_b;
+    float vs_a, vs_b;
     {
       const uint32_t wa = *reinterpret_cast<const uint32_t*>(tile + tau_a * CELL + p.vs_off);
       const uint32_t wb = *reinterpret_cast<const uint32_t*>(tile + tau_b * CELL + p.vs_off);
       vs_a = tok_a < n ? __uint_as_float(wa & 0xFFFFFFF0u) : 0.f;
       vs_b = tok_b < n ? __uint_as_float(wb & 0xFFFFFFF0u) : 0.f;
-      vz_a = static_cast<float>(wa & 0xFu);
-      vz_b = static_cast<float>(wb & 0xFu);
     }
     {
       const float vm = warp_max(fmaxf(vs_a, vs_b));
@@ -449,7 +456,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
           m_run[nt][e] = m_new;
           const float ao = alpha * o_range;
           l_part[nt][e] *= alpha;
-          c_part[nt][e] *= ao;
 #pragma unroll
           for (int mt = 0; mt < 4; ++mt) {
             o[mt][nt][e] *= ao;
@@ -461,12 +467,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
           sc[nt][e] = pa * vs_a * pv_mul;  // P_v, fp32
           sc[nt][2 + e] = pb * vs_b * pv_mul;
         }
-        // round P_v to fp16 (the values the MMA uses); zero-point sums from the same rounded values
+        // P_v rounded to fp16: the operand of the PV MMA
         const __half2 ha = __floats2half2_rn(sc[nt][0], sc[nt][1]);
         const __half2 hb = __floats2half2_rn(sc[nt][2], sc[nt][3]);
-        const float2 fa = __half22float2(ha), fb = __half22float2(hb);
-        c_part[nt][0] += fa.x * vz_a + fb.x * vz_b;
-        c_part[nt][1] += fa.y * vz_a + fb.y * vz_b;
         *reinterpret_cast<__half2*>(psm + pv_k_of_token(tau_a) * PSTRIDE + (8 * nt + 2 * t) * 2) = ha;
         *reinterpret_cast<__half2*>(psm + pv_k_of_token(tau_b) * PSTRIDE + (8 * nt + 2 * t) * 2) = hb;
       }
@@ -497,21 +500,26 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
       const uint32_t w1 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 1) * CELL);
       const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 2) * CELL);
       const uint32_t w3 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 3) * CELL);
+      const uint8_t* zbase = tile + p.vs_off;
+      uint32_t z[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) z[j] = *reinterpret_cast<const uint32_t*>(zbase + (tau0 + j) * CELL) & 0xFu;
       // f = 0: tokens (tau0, tau0 + 1); f = 1: tokens (tau0 + 2, tau0 + 3)
       uint32_t vr[2][8];  // [f][channel offset 0..7]
 #pragma unroll
       for (int f = 0; f < 2; ++f) {
         const uint32_t wa = f ? w2 : w0, wb = f ? w3 : w1;
+        const uint32_t lo_b = zp_lo_bias(z[2 * f], z[2 * f + 1]), hi_b = zp_hi_bias(z[2 * f], z[2 * f + 1]);
         const uint32_t x = prmt(wa, wb, 0x5410u), y = prmt(wa, wb, 0x7632u);
         const uint32_t x8 = x >> 8, y8 = y >> 8;
-        vr[f][0] = nib_lo(x);
-        vr[f][1] = nib_hi(x);
-        vr[f][2] = nib_lo(x8);
-        vr[f][3] = nib_hi(x8);
-        vr[f][4] = nib_lo(y);
-        vr[f][5] = nib_hi(y);
-        vr[f][6] = nib_lo(y8);
-        vr[f][7] = nib_hi(y8);
+        vr[f][0] = nib_lo(x, lo_b);
+        vr[f][1] = nib_hi(x, hi_b);
+        vr[f][2] = nib_lo(x8, lo_b);
+        vr[f][3] = nib_hi(x8, hi_b);
+        vr[f][4] = nib_lo(y, lo_b);
+        vr[f][5] = nib_hi(y, hi_b);
+        vr[f][6] = nib_lo(y8, lo_b);
+        vr[f][7] = nib_hi(y8, hi_b);
       }
 #pragma unroll
       for (int mt = 0; mt < 4; ++mt) {
@@ -532,31 +540,23 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
     return;
   }
 
-  // --- epilogue: totals of l and the zero-point sums, normalised partial O and lse -------------------------
+  // --- epilogue: totals of l, normalised partial O and lse ---------------------------------------------------
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      float l = l_part[nt][e], c = c_part[nt][e];
+      float l = l_part[nt][e];
 #pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        l += __shfl_xor_sync(0xffffffffu, l, off);
-        c += __shfl_xor_sync(0xffffffffu, c, off);
-      }
+      for (int off = 4; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
       l_part[nt][e] = l;
-      c_part[nt][e] = c;
     }
   __syncthreads();
-  float* red_l = red;                            // [4][32]
-  float* red_c = reinterpret_cast<float*>(psm);  // [4][32]: P^T is no longer needed
+  float* red_l = red;  // [4][32]
   if (g == 0) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        red_l[warp * DEC_MAX_ROWS + 8 * nt + 2 * t + e] = l_part[nt][e];
-        red_c[warp * DEC_MAX_ROWS + 8 * nt + 2 * t + e] = c_part[nt][e];
-      }
+      for (int e = 0; e < 2; ++e) red_l[warp * DEC_MAX_ROWS + 8 * nt + 2 * t + e] = l_part[nt][e];
   }
   __syncthreads();
   const float o_unit = e_run == -1000 ? 0.f : ldexpf(1.f, e_run);
@@ -567,15 +567,14 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
       const int r = 8 * nt + 2 * t + e;
       if (r >= rows) continue;
       const float l = red_l[r] + red_l[DEC_MAX_ROWS + r] + red_l[2 * DEC_MAX_ROWS + r] + red_l[3 * DEC_MAX_ROWS + r];
-      const float c = red_c[r] + red_c[DEC_MAX_ROWS + r] + red_c[2 * DEC_MAX_ROWS + r] + red_c[3 * DEC_MAX_ROWS + r];
       const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
       const int64_t prow = (static_cast<int64_t>(tok) * p.nq + qh) * p.num_splits + split;
       const float inv = l > 0.f ? o_unit / l : 0.f;
       float v[8];
 #pragma unroll
       for (int mt = 0; mt < 4; ++mt) {
-        v[2 * mt] = (o[mt][nt][e] - c) * inv;
-        v[2 * mt + 1] = (o[mt][nt][2 + e] - c) * inv;
+        v[2 * mt] = o[mt][nt][e] * inv;
+        v[2 * mt + 1] = o[mt][nt][2 + e] * inv;
       }
       float4* dst = reinterpret_cast<float4*>(p.part_o + prow * DEC_HS + 64 * warp + 8 * g);
       dst[0] = make_float4(v[0], v[1], v[2], v[3]);
