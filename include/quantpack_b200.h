@@ -110,6 +110,25 @@ int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stride_token, i
                     float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated, int out_mode, float* lse_out,
                     int num_splits, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Bytes of the library's static decode scratch used by qp_paged_decode_static. */
+#define QP_STATIC_DECODE_SCRATCH_BYTES (32ll << 20)
+
+/* qp_paged_decode without a workspace argument, for callers that cannot allocate device memory (an engine that owns
+ * every byte of device memory in its own pool, embedded code with no device allocator). The split partials go to a
+ * fixed 32 MiB array inside the library, reserved on every GPU that loads it until the process exits; calls whose
+ * partials (qp_decode_workspace_bytes) exceed it return QP_ERR_WORKSPACE. The first call on a device looks the array
+ * up (cudaGetSymbolAddress) with that device current: make it before any stream capture. All calls on a device share
+ * the array and it keeps the last call's contents (nothing in it needs to start at zero); calls that overlap on the
+ * GPU race on it, so serialize them. Allocates nothing. No counterpart in the reference. */
+int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                           void* out, int64_t out_stride_token, int64_t out_stride_head, int64_t num_q_tokens,
+                           int num_seqs, const int32_t* cu_seqlens_q, const int32_t* seqused_k, int max_seqlen_q,
+                           const int32_t* block_table, int64_t block_table_stride, const void* cache, int block_size,
+                           int64_t block_stride, int64_t head_stride, int64_t slot_stride, int64_t k_off,
+                           int64_t ks_off, int64_t v_off, int64_t vs_off, int num_q_heads, int num_kv_heads,
+                           int head_size, float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated,
+                           int out_mode, float* lse_out, int num_splits, void* stream);
+
 /* Log-sum-exp fold of num_parts attention partials per (token, query head): part_o fp32 (RHT domain, normalised),
  * part_lse base-2. out_mode 0: inverse RHT / head_size into `out` in dtype; out_mode 1: fp32 RHT-domain O into
  * `out` and the folded lse into lse_out. Replaces the fold of vllm_quantpack/attention/int4_prefill.py:223-230 and

@@ -1,0 +1,79 @@
+"""qp_paged_decode_static: the split-KV decode for callers that cannot allocate device memory.
+
+Some hosts of this library never call cudaMalloc after start-up (an engine that owns all device memory in its own
+pool, embedded code with no device allocator), so they cannot hand qp_paged_decode a workspace. The static variant
+keeps its split partials in a fixed 32 MiB array inside the library. These tests call it through the C ABI and check
+that two calls in a row (the second one finds the first call's partials still in the array) give the output of the
+workspace entry point, within the tolerance of the decode tests; and that a request whose partials do not fit is
+refused with a clear error. This file is collected last on purpose."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import quantpack_oracle as qo
+
+import qp_testutil as U
+
+pytestmark = pytest.mark.gpu
+TOL = 5e-3          # the decode tests' tolerance (tests/test_decode_gpu.py)
+
+
+def _static_decode(lib, cache, q, out, cu, used, table, qlen, num_splits):
+    from vllm_quantpack_b200.attention import ops, rht
+    kc, vc, ks, vs = cache.views
+    lay = ops.CacheLayout(kc, vc, ks, vs, U.HS)
+    return lib.qp_paged_decode_static(
+        lay.fmt, 0, q.data_ptr(), q.stride(0), q.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
+        q.shape[0], cu.shape[0] - 1, cu.data_ptr(), used.data_ptr(), qlen, table.data_ptr(), table.stride(0),
+        *lay.args(), U.NQ, U.NKV, U.HS, ctypes.c_float(U.HS ** -0.5), rht.device_sign_bits(U.HS, q.device).data_ptr(),
+        0, 0, None, num_splits, torch.cuda.current_stream(q.device).cuda_stream)
+
+
+@pytest.mark.parametrize("fmt", ["int4", "k8v4"])
+def test_static_scratch_decode_matches_workspace_decode(device, fmt):
+    from vllm_quantpack_b200 import _lib
+    from vllm_quantpack_b200.attention import ops
+    lib = _lib.load()
+    qlens, lens = [4, 1, 3], [20000, 777, 4096]
+    table_np, nblocks = U.block_tables(lens, 16)
+    cache = U.Cache(fmt, nblocks, 16, device)
+    for i, n in enumerate(lens):
+        cache.fill(table_np[i], n, seed=40 + i)
+    kc, vc, ks, vs = cache.views
+    q = U.to_torch(U.make_queries(qlens, seed=8), device)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(qlens)]), dtype=torch.int32, device=device)
+    used = torch.tensor(lens, dtype=torch.int32, device=device)
+    table = torch.from_numpy(table_np).to(device)
+    splits = ops.decode_num_splits(len(lens), U.NKV, max(lens), ops.sm_count(device))
+    want = torch.empty_like(q)
+    ops.paged_decode(q, kc, vc, want, cu_seqlens_q=cu, max_seqlen_q=max(qlens), seqused_k=used,
+                     max_seqlen_k=max(lens), softmax_scale=U.HS ** -0.5, block_table=table, k_scale_cache=ks,
+                     v_scale_cache=vs, num_splits=splits)
+    want = want.float().cpu().numpy()
+    for call in range(2):
+        out = torch.full_like(q, float("nan"))
+        rc = _static_decode(lib, cache, q, out, cu, used, table, max(qlens), splits)
+        assert rc == 0, lib.qp_last_error().decode()
+        torch.cuda.synchronize()
+        got = out.float().cpu().numpy()
+        assert np.isfinite(got).all(), f"call {call}: output not written"
+        err = qo.relerr(got, want)
+        assert err < TOL, f"call {call}: static-scratch decode differs from the workspace decode by {err:.3e}"
+    assert _lib.device_error() == 0
+
+
+def test_static_scratch_refuses_requests_that_do_not_fit(device):
+    from vllm_quantpack_b200 import _lib
+    lib = _lib.load()
+    cache = U.Cache("int4", 4, 16, device)
+    q = torch.zeros((4096, U.NQ, U.HS), dtype=torch.bfloat16, device=device)
+    out = torch.empty_like(q)
+    cu = torch.tensor([0, 4096], dtype=torch.int32, device=device)
+    used = torch.tensor([64], dtype=torch.int32, device=device)
+    table = torch.zeros((1, 4), dtype=torch.int32, device=device)
+    # 4096 tokens x 24 heads x 64 splits of partials is ~100 MB: more than the 32 MiB array
+    rc = _static_decode(lib, cache, q, out, cu, used, table, 1, 64)
+    assert rc == 4, rc
+    assert b"static scratch" in lib.qp_last_error()

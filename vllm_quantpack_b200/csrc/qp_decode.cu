@@ -914,3 +914,56 @@ extern "C" int qp_merge_attn_partials(int dtype, int head_size, int64_t num_toke
   return merge_dispatch(mp, out_mode == 1 ? DT_BF16 : dtype, head_size, num_tokens, static_cast<cudaStream_t>(stream),
                         false);
 }
+
+// ---------------------------------------------------------------------------------------------------------------
+// Split-KV decode for callers that cannot allocate device memory.
+//
+// Some hosts of this library never call cudaMalloc once they are running: an engine that hands all device memory to
+// its own pool at start-up and forbids allocations afterwards, or embedded C code with no device allocator at all.
+// qp_paged_decode needs a workspace for its split partials; this variant takes it from a fixed array that lives in
+// the library itself (QP_STATIC_DECODE_SCRATCH_BYTES, 32 MiB), so the call allocates nothing.
+// - The array is reserved on every GPU that loads this library, for as long as the process lives.
+// - Its device address is looked up (cudaGetSymbolAddress) on the first call on each device, with that device
+//   current; make that first call before any stream capture.
+// - Every call on a device uses the same array and it keeps the last call's contents. Nothing in it has to start at
+//   zero (each call writes every partial it later reads), but calls that overlap on the GPU (two streams, two host
+//   threads) race on it: serialize them.
+// - Sizes whose partials exceed the array are rejected with QP_ERR_WORKSPACE.
+static constexpr int64_t kStaticDecodeScratchBytes = 32ll << 20;
+static __device__ __align__(256) uint8_t g_static_decode_scratch[kStaticDecodeScratchBytes];
+static void* g_static_decode_scratch_addr[64] = {};
+
+extern "C" int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t q_stride_token,
+                                      int64_t q_stride_head, void* out, int64_t out_stride_token,
+                                      int64_t out_stride_head, int64_t num_q_tokens, int num_seqs,
+                                      const int32_t* cu_seqlens_q, const int32_t* seqused_k, int max_seqlen_q,
+                                      const int32_t* block_table, int64_t block_table_stride, const void* cache,
+                                      int block_size, int64_t block_stride, int64_t head_stride, int64_t slot_stride,
+                                      int64_t k_off, int64_t ks_off, int64_t v_off, int64_t vs_off, int num_q_heads,
+                                      int num_kv_heads, int head_size, float softmax_scale,
+                                      const uint32_t* rht_sign_bits, int q_rotated, int out_mode, float* lse_out,
+                                      int num_splits, void* stream) {
+  const int64_t need = qp_decode_workspace_bytes(num_q_tokens, num_q_heads, head_size, num_splits);
+  if (need > kStaticDecodeScratchBytes)
+    return set_error(QP_ERR_WORKSPACE,
+                     "decode (static scratch): the split partials need %lld bytes, the library's static scratch "
+                     "holds %lld; lower num_splits or the batch, or call qp_paged_decode with a workspace",
+                     (long long)need, (long long)kStaticDecodeScratchBytes);
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode (static scratch): cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(QP_ERR_UNSUPPORTED, "decode (static scratch): device %d >= 64", dev);
+  if (g_static_decode_scratch_addr[dev] == nullptr) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_static_decode_scratch);
+    if (e != cudaSuccess || addr == nullptr)
+      return set_error(QP_ERR_CUDA, "decode (static scratch): cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_static_decode_scratch_addr[dev] = addr;
+  }
+  return qp_paged_decode(fmt, dtype, q, q_stride_token, q_stride_head, out, out_stride_token, out_stride_head,
+                         num_q_tokens, num_seqs, cu_seqlens_q, seqused_k, max_seqlen_q, block_table,
+                         block_table_stride, cache, block_size, block_stride, head_stride, slot_stride, k_off, ks_off,
+                         v_off, vs_off, num_q_heads, num_kv_heads, head_size, softmax_scale, rht_sign_bits, q_rotated,
+                         out_mode, lse_out, num_splits, g_static_decode_scratch_addr[dev], kStaticDecodeScratchBytes,
+                         stream);
+}
