@@ -33,7 +33,7 @@
 namespace qp {
 
 constexpr int DEC_TILE = 64;
-constexpr int DEC_STAGES = 4;
+constexpr int DEC_STAGES = 3;
 constexpr int DEC_THREADS = 128;
 constexpr int DEC_HS = 256;
 constexpr int DEC_MAX_ROWS = 32;
@@ -74,14 +74,16 @@ struct PLayout {
 template <int FMT, int NT>
 struct DecSmem {
   static constexpr int CELL = Cell<FMT>::BYTES;
+  static constexpr int ROWS = 8 * NT;  // query rows held (padded to whole n-tiles)
   static constexpr int STAGE_BYTES = DEC_TILE * CELL;
   static constexpr int OFF_STAGES = 0;
   static constexpr int OFF_Q = OFF_STAGES + DEC_STAGES * STAGE_BYTES;
-  static constexpr int OFF_P = OFF_Q + DEC_MAX_ROWS * Q_STRIDE;
-  static constexpr int OFF_RED = OFF_P + DEC_TILE * PLayout<NT>::STRIDE;  // [4][32] f32
-  static constexpr int OFF_VS = OFF_RED + 4 * DEC_MAX_ROWS * 4;           // [4] f32
-  static constexpr int OFF_ROWP = OFF_VS + 16;                            // qscale, cq, qsum: [3][32]
-  static constexpr int OFF_BAR = (OFF_ROWP + 3 * DEC_MAX_ROWS * 4 + 7) / 8 * 8;
+  static constexpr int OFF_P = OFF_Q + ROWS * Q_STRIDE;
+  static constexpr int OFF_RED = OFF_P + DEC_TILE * PLayout<NT>::STRIDE;  // [ROWS][4 warps] f32 (row max, then l)
+  static constexpr int OFF_VS = OFF_RED + ROWS * 4 * 4;                   // [4] f32 (value-scale max per warp)
+  static constexpr int OFF_ZB = OFF_VS + 16;                              // [2][64] u16 zero-point biases
+  static constexpr int OFF_ROWP = OFF_ZB + 2 * DEC_TILE * 2;              // qscale, cq, qsum: [3][ROWS]
+  static constexpr int OFF_BAR = (OFF_ROWP + 3 * ROWS * 4 + 7) / 8 * 8;
   static constexpr int BYTES = OFF_BAR + DEC_STAGES * 8;
 };
 
@@ -123,16 +125,16 @@ __device__ __forceinline__ uint32_t nib_lo(uint32_t x, uint32_t lo_bias) {
 __device__ __forceinline__ uint32_t nib_hi(uint32_t x, uint32_t hi_bias) {
   return hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u /* 1/16 */, hi_bias);
 }
-// fp16x2 {1024 + za, 1024 + zb} and {-(64 + za), -(64 + zb)} for zero points za, zb in [0, 15].
-__device__ __forceinline__ uint32_t zp_lo_bias(uint32_t za, uint32_t zb) { return 0x64006400u | za | (zb << 16); }
-__device__ __forceinline__ uint32_t zp_hi_bias(uint32_t za, uint32_t zb) {
-  return 0xD400D400u | (za << 4) | (zb << 20);
-}
+
+// Online softmax with a lazy maximum: P = exp2(s - m_used) is allowed up to 2^RESCALE_SLACK, so the O accumulators
+// are rescaled only when a row maximum grows by more than that (rare after the first tiles), not every tile.
+constexpr float RESCALE_SLACK = 8.f;
 
 template <int FMT, int DT, int NT>
-__global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodeParams p) {
   using SM = DecSmem<FMT, NT>;
   constexpr int CELL = SM::CELL;
+  constexpr int ROWS = SM::ROWS;
   constexpr int PSTRIDE = PLayout<NT>::STRIDE;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem + SM::OFF_STAGES;
@@ -140,9 +142,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
   uint8_t* psm = smem + SM::OFF_P;
   float* red = reinterpret_cast<float*>(smem + SM::OFF_RED);
   float* red_vs = reinterpret_cast<float*>(smem + SM::OFF_VS);
+  uint16_t* zb_lo = reinterpret_cast<uint16_t*>(smem + SM::OFF_ZB);
+  uint16_t* zb_hi = zb_lo + DEC_TILE;
   float* row_qscale = reinterpret_cast<float*>(smem + SM::OFF_ROWP);
-  float* row_cq = row_qscale + DEC_MAX_ROWS;
-  float* row_qsum = row_cq + DEC_MAX_ROWS;
+  float* row_cq = row_qscale + ROWS;
+  float* row_qsum = row_cq + ROWS;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::OFF_BAR);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -176,22 +180,36 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
   const uint8_t* head_base = p.cache + static_cast<int64_t>(kvh) * p.head_stride;
 
   // --- producer: one thread issues the bulk copies of a tile (whole 16-token runs; block_size % 16 == 0, so a run
-  // never crosses a block, and the last run of a sequence stays inside the block that holds its last token) -----
-  auto issue_tile = [&](int i) {
+  // never crosses a block, and the last run of a sequence stays inside the block that holds its last token). The
+  // block-table entries of a tile (one per 16-token group) are loaded a tile ahead of the copies that use them. ----
+  auto load_blocks = [&](int i, int (&blk)[4]) {
+    const int tok_begin = (tile0 + i) * DEC_TILE;
+    const int groups = (min(tok_begin + DEC_TILE, n) - tok_begin + 15) >> 4;
+#pragma unroll
+    for (int gi = 0; gi < 4; ++gi) blk[gi] = gi < groups ? __ldg(btab + (tok_begin + 16 * gi) / p.block_size) : 0;
+  };
+  auto issue_tile = [&](int i, const int (&blk)[4]) {
     const int stage = i % DEC_STAGES;
     const int tok_begin = (tile0 + i) * DEC_TILE;
     const int tok_end = min(tok_begin + DEC_TILE, n);
     const int groups = (tok_end - tok_begin + 15) >> 4;
     mbar_arrive_expect_tx(&bars[stage], static_cast<uint32_t>(groups * 16 * CELL));
     uint8_t* dst = stages + stage * SM::STAGE_BYTES;
-    for (int gi = 0; gi < groups;) {
+#pragma unroll
+    for (int gi = 0; gi < 4; ++gi) {
       const int tok = tok_begin + gi * 16;
-      const int blk = btab[tok / p.block_size];
       const int in_blk = tok % p.block_size;
-      const int run = min(groups - gi, (p.block_size - in_blk) >> 4);
-      const uint8_t* src = head_base + static_cast<int64_t>(blk) * p.block_stride + static_cast<int64_t>(in_blk) * CELL;
-      bulk_g2s(dst + gi * 16 * CELL, src, static_cast<uint32_t>(run * 16 * CELL), &bars[stage]);
-      gi += run;
+      // a group continues the previous copy when it is the next run of the same block
+      const bool starts = gi == 0 || in_blk == 0 || blk[gi] != blk[gi - 1];
+      if (gi < groups && starts) {
+        int run = 1;
+#pragma unroll
+        for (int k = gi + 1; k < 4; ++k)
+          if (k < groups && run == k - gi && blk[k] == blk[gi] && (tok + 16 * (k - gi)) % p.block_size != 0) ++run;
+        const uint8_t* src =
+            head_base + static_cast<int64_t>(blk[gi]) * p.block_stride + static_cast<int64_t>(in_blk) * CELL;
+        bulk_g2s(dst + gi * 16 * CELL, src, static_cast<uint32_t>(run * 16 * CELL), &bars[stage]);
+      }
     }
   };
 
@@ -200,16 +218,22 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
     fence_mbar_init();
   }
   __syncthreads();
-  int issued = 0;  // tiles whose copies thread 0 has issued
+  int issued = 0;        // tiles whose copies thread 0 has issued
+  int next_blk[4] = {};  // block-table entries of tile `issued` (thread 0)
   if (tid == 0) {
     issued = min(ntl, DEC_STAGES);
-    for (int i = 0; i < issued; ++i) issue_tile(i);
+    for (int i = 0; i < issued; ++i) {
+      int blk[4];
+      load_blocks(i, blk);
+      issue_tile(i, blk);
+    }
+    if (issued < ntl) load_blocks(issued, next_blk);
   }
 
   // --- Q: rotate, scale to fp16 with a per-row power of two, permute channels ------------------------------
   {
     using EL = Elem<DT>;
-    for (int r = warp; r < DEC_MAX_ROWS; r += 4) {
+    for (int r = warp; r < ROWS; r += 4) {
       __half* qrow = reinterpret_cast<__half*>(qsm + r * Q_STRIDE);
       if (r >= rows) {
         for (int c = lane; c < DEC_HS; c += 32) qrow[c] = __float2half_rn(0.f);
@@ -265,7 +289,19 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
   }
   __syncthreads();
 
-  // --- per-thread state ------------------------------------------------------------------------------------
+  // --- per-thread state: this thread's query rows are r = 8 nt + 2 t + e ------------------------------------
+  float qsc[NT][2], qcq[NT][2], qsum[NT][2];
+  int lim[NT][2];  // last key position each row sees (-1 for padding rows)
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int r = 8 * nt + 2 * t + e;
+      qsc[nt][e] = row_qscale[r];
+      qcq[nt][e] = row_cq[r];
+      qsum[nt][e] = row_qsum[r];
+      lim[nt][e] = r < rows ? n - qlen + r / p.group : -1;
+    }
   float o[4][NT][4];
 #pragma unroll
   for (int mt = 0; mt < 4; ++mt)
@@ -273,18 +309,21 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int c = 0; c < 4; ++c) o[mt][nt][c] = 0.f;
-  float m_run[NT][2], l_part[NT][2];
+  float m_used[NT][2], l_part[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      m_run[nt][e] = -INFINITY;
+      m_used[nt][e] = -INFINITY;
       l_part[nt][e] = 0.f;
     }
-  int e_run = -1000;                     // running power-of-two range of P_v (value scales)
+  int e_run = -1000;      // running power-of-two range of P_v (value scales)
+  float pv_mul = 0.f;     // 2^-e_run
   const int causal_from = n - qlen + 1;  // keys >= this are hidden from some query token
   const uint32_t qsm_base = smem_u32(qsm);
   const uint32_t psm_base = smem_u32(psm);
+  const int tau_a = 16 * warp + g, tau_b = tau_a + 8;
+  const int pk_a = pv_k_of_token(tau_a) * PSTRIDE, pk_b = pv_k_of_token(tau_b) * PSTRIDE;
   bool failed = false;
   int fail_tile = ntl;
 
@@ -302,7 +341,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int c = 0; c < 4; ++c) sacc[nt][c] = 0.f;
-    const uint8_t* rowg = tile + (16 * warp + g) * CELL;
+    const uint8_t* rowg = tile + tau_a * CELL;
     const uint8_t* rowg8 = rowg + 8 * CELL;
     if constexpr (FMT == FMT_INT4) {
 #pragma unroll
@@ -362,7 +401,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
     }
 
     // ---------------- scores (log2 units), masks, tile row max ----------------
-    const int tau_a = 16 * warp + g, tau_b = tau_a + 8;
     const int tok_a = tok_base + tau_a, tok_b = tok_base + tau_b;
     float ks_a, ks_b, kz_a = 0.f, kz_b = 0.f;
     {
@@ -380,20 +418,16 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
     }
     const bool need_mask = tok_base + DEC_TILE > causal_from;
     float sc[NT][4];
-    float tmax[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
+      float tm[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int r = 8 * nt + 2 * t + e;
-        const float qsc = row_qscale[r], cq = row_cq[r], qsum = row_qsum[r];
-        float s0 = (sacc[nt][e] - fmaf(kz_a, qsum, cq)) * (ks_a * qsc);
-        float s1 = (sacc[nt][2 + e] - fmaf(kz_b, qsum, cq)) * (ks_b * qsc);
+        float s0 = (sacc[nt][e] - fmaf(kz_a, qsum[nt][e], qcq[nt][e])) * (ks_a * qsc[nt][e]);
+        float s1 = (sacc[nt][2 + e] - fmaf(kz_b, qsum[nt][e], qcq[nt][e])) * (ks_b * qsc[nt][e]);
         if (need_mask) {
-          const int lim = n - qlen + r / p.group;  // last key this row sees
-          const bool row_ok = r < rows;
-          if (!(row_ok && tok_a < n && tok_a <= lim)) s0 = -INFINITY;
-          if (!(row_ok && tok_b < n && tok_b <= lim)) s1 = -INFINITY;
+          if (tok_a > lim[nt][e]) s0 = -INFINITY;  // also past the context: lim <= n - 1
+          if (tok_b > lim[nt][e]) s1 = -INFINITY;
         }
         sc[nt][e] = s0;
         sc[nt][2 + e] = s1;
@@ -401,26 +435,24 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        tmax[nt][e] = mx;
+        tm[e] = mx;
+      }
+      if (g == 0) {
+        red[(8 * nt + 2 * t) * 4 + warp] = tm[0];
+        red[(8 * nt + 2 * t + 1) * 4 + warp] = tm[1];
       }
     }
-    // value scales of this thread's two tokens (tokens past the end count as 0)
+    // value scales and zero points of this thread's two tokens (tokens past the end count as scale 0)
     float vs_a, vs_b;
+    uint32_t vz_a, vz_b;
     {
       const uint32_t wa = *reinterpret_cast<const uint32_t*>(tile + tau_a * CELL + p.vs_off);
       const uint32_t wb = *reinterpret_cast<const uint32_t*>(tile + tau_b * CELL + p.vs_off);
       vs_a = tok_a < n ? __uint_as_float(wa & 0xFFFFFFF0u) : 0.f;
       vs_b = tok_b < n ? __uint_as_float(wb & 0xFFFFFFF0u) : 0.f;
-    }
-    {
+      vz_a = wa & 0xFu;
+      vz_b = wb & 0xFu;
       const float vm = warp_max(fmaxf(vs_a, vs_b));
-      if (g == 0) {
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          red[warp * DEC_MAX_ROWS + 8 * nt + 2 * t] = tmax[nt][0];
-          red[warp * DEC_MAX_ROWS + 8 * nt + 2 * t + 1] = tmax[nt][1];
-        }
-      }
       if (lane == 0) red_vs[warp] = vm;
     }
     // (A) row maxima visible; every warp is done with tile i - 1
@@ -430,51 +462,75 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
       break;
     }
     if (tid == 0 && i >= 1 && i - 1 + DEC_STAGES < ntl) {
-      issue_tile(i - 1 + DEC_STAGES);
+      issue_tile(issued, next_blk);  // issued == i - 1 + DEC_STAGES
       ++issued;
+      if (issued < ntl) load_blocks(issued, next_blk);
+    }
+    if (t == 0) {  // zero-point biases of the value operand, per token (read by the PV phase after barrier B)
+      zb_lo[tau_a] = static_cast<uint16_t>(0x6400u | vz_a);
+      zb_lo[tau_b] = static_cast<uint16_t>(0x6400u | vz_b);
+      zb_hi[tau_a] = static_cast<uint16_t>(0xD400u | (vz_a << 4));
+      zb_hi[tau_b] = static_cast<uint16_t>(0xD400u | (vz_b << 4));
     }
 
-    // running max, value range, rescale
+    // ---------------- lazy rescale, P, P_v ----------------
     {
-      const float vmax = fmaxf(fmaxf(red_vs[0], red_vs[1]), fmaxf(red_vs[2], red_vs[3]));
-      int e_tile = -1000;
-      if (vmax > 0.f) frexpf(vmax, &e_tile);  // vmax < 2^e_tile
-      const int e_new = max(e_run, e_tile);
-      const float o_range = e_run == -1000 ? 1.f : ldexpf(1.f, e_run - e_new);
-      const float pv_mul = e_new == -1000 ? 0.f : ldexpf(1.f, -e_new);
-      e_run = e_new;
+      float m_tile[NT][2];
+      bool grow = false;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int r = 8 * nt + 2 * t + e;
-          const float mt_ = fmaxf(fmaxf(red[r], red[DEC_MAX_ROWS + r]),
-                                  fmaxf(red[2 * DEC_MAX_ROWS + r], red[3 * DEC_MAX_ROWS + r]));
-          const float m_new = fmaxf(m_run[nt][e], mt_);
-          const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run[nt][e] - m_new);
-          const float base = m_new == -INFINITY ? 0.f : m_new;
-          m_run[nt][e] = m_new;
-          const float ao = alpha * o_range;
-          l_part[nt][e] *= alpha;
+          const float4 mv = *reinterpret_cast<const float4*>(red + (8 * nt + 2 * t + e) * 4);
+          m_tile[nt][e] = fmaxf(fmaxf(mv.x, mv.y), fmaxf(mv.z, mv.w));
+          grow |= m_tile[nt][e] > m_used[nt][e] + RESCALE_SLACK;
+        }
+      const float4 vv = *reinterpret_cast<const float4*>(red_vs);
+      const float vmax = fmaxf(fmaxf(vv.x, vv.y), fmaxf(vv.z, vv.w));
+      int e_tile = -1000;
+      if (vmax > 0.f) frexpf(vmax, &e_tile);  // vmax < 2^e_tile
+      const bool vgrow = e_tile > e_run;      // the same for every thread of the CTA
+      if (__any_sync(0xffffffffu, grow) || vgrow) {
+        const int e_new = max(e_run, e_tile);
+        const float o_range = e_run == -1000 ? 0.f : ldexpf(1.f, e_run - e_new);
+        e_run = e_new;
+        pv_mul = e_new == -1000 ? 0.f : ldexpf(1.f, -e_new);
 #pragma unroll
-          for (int mt = 0; mt < 4; ++mt) {
-            o[mt][nt][e] *= ao;
-            o[mt][nt][2 + e] *= ao;
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float mt_ = m_tile[nt][e];
+            const float m_new = mt_ > m_used[nt][e] + RESCALE_SLACK ? mt_ : m_used[nt][e];
+            const float alpha = m_new == m_used[nt][e] ? 1.f : exp2f(m_used[nt][e] - m_new);
+            m_used[nt][e] = m_new;
+            const float ao = alpha * o_range;
+            l_part[nt][e] *= alpha;
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+              o[mt][nt][e] *= ao;
+              o[mt][nt][2 + e] *= ao;
+            }
           }
+      }
+      const float va = vs_a * pv_mul, vb = vs_b * pv_mul;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float pv[4];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float base = m_used[nt][e] == -INFINITY ? 0.f : m_used[nt][e];
           const float pa = exp2f(sc[nt][e] - base);
           const float pb = exp2f(sc[nt][2 + e] - base);
           l_part[nt][e] += pa + pb;
-          sc[nt][e] = pa * vs_a * pv_mul;  // P_v, fp32
-          sc[nt][2 + e] = pb * vs_b * pv_mul;
+          pv[e] = pa * va;
+          pv[2 + e] = pb * vb;
         }
         // P_v rounded to fp16: the operand of the PV MMA
-        const __half2 ha = __floats2half2_rn(sc[nt][0], sc[nt][1]);
-        const __half2 hb = __floats2half2_rn(sc[nt][2], sc[nt][3]);
-        *reinterpret_cast<__half2*>(psm + pv_k_of_token(tau_a) * PSTRIDE + (8 * nt + 2 * t) * 2) = ha;
-        *reinterpret_cast<__half2*>(psm + pv_k_of_token(tau_b) * PSTRIDE + (8 * nt + 2 * t) * 2) = hb;
+        *reinterpret_cast<__half2*>(psm + pk_a + (8 * nt + 2 * t) * 2) = __floats2half2_rn(pv[0], pv[1]);
+        *reinterpret_cast<__half2*>(psm + pk_b + (8 * nt + 2 * t) * 2) = __floats2half2_rn(pv[2], pv[3]);
       }
     }
-    __syncthreads();  // (B) P^T visible
+    __syncthreads();  // (B) P^T and the zero-point biases visible
 
     // ---------------- PV: warp handles channels 64 warp + [0, 64) ----------------
 #pragma unroll
@@ -500,16 +556,14 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
       const uint32_t w1 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 1) * CELL);
       const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 2) * CELL);
       const uint32_t w3 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 3) * CELL);
-      const uint8_t* zbase = tile + p.vs_off;
-      uint32_t z[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) z[j] = *reinterpret_cast<const uint32_t*>(zbase + (tau0 + j) * CELL) & 0xFu;
+      const uint2 blo = *reinterpret_cast<const uint2*>(zb_lo + tau0);  // {tau0, tau0+1}, {tau0+2, tau0+3}
+      const uint2 bhi = *reinterpret_cast<const uint2*>(zb_hi + tau0);
       // f = 0: tokens (tau0, tau0 + 1); f = 1: tokens (tau0 + 2, tau0 + 3)
       uint32_t vr[2][8];  // [f][channel offset 0..7]
 #pragma unroll
       for (int f = 0; f < 2; ++f) {
         const uint32_t wa = f ? w2 : w0, wb = f ? w3 : w1;
-        const uint32_t lo_b = zp_lo_bias(z[2 * f], z[2 * f + 1]), hi_b = zp_hi_bias(z[2 * f], z[2 * f + 1]);
+        const uint32_t lo_b = f ? blo.y : blo.x, hi_b = f ? bhi.y : bhi.x;
         const uint32_t x = prmt(wa, wb, 0x5410u), y = prmt(wa, wb, 0x7632u);
         const uint32_t x8 = x >> 8, y8 = y >> 8;
         vr[f][0] = nib_lo(x, lo_b);
@@ -551,12 +605,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
       l_part[nt][e] = l;
     }
   __syncthreads();
-  float* red_l = red;  // [4][32]
   if (g == 0) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) red_l[warp * DEC_MAX_ROWS + 8 * nt + 2 * t + e] = l_part[nt][e];
+      for (int e = 0; e < 2; ++e) red[(8 * nt + 2 * t + e) * 4 + warp] = l_part[nt][e];
   }
   __syncthreads();
   const float o_unit = e_run == -1000 ? 0.f : ldexpf(1.f, e_run);
@@ -566,7 +619,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
     for (int e = 0; e < 2; ++e) {
       const int r = 8 * nt + 2 * t + e;
       if (r >= rows) continue;
-      const float l = red_l[r] + red_l[DEC_MAX_ROWS + r] + red_l[2 * DEC_MAX_ROWS + r] + red_l[3 * DEC_MAX_ROWS + r];
+      const float4 lv = *reinterpret_cast<const float4*>(red + r * 4);
+      const float l = (lv.x + lv.y) + (lv.z + lv.w);
       const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
       const int64_t prow = (static_cast<int64_t>(tok) * p.nq + qh) * p.num_splits + split;
       const float inv = l > 0.f ? o_unit / l : 0.f;
@@ -579,7 +633,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(const DecodePara
       float4* dst = reinterpret_cast<float4*>(p.part_o + prow * DEC_HS + 64 * warp + 8 * g);
       dst[0] = make_float4(v[0], v[1], v[2], v[3]);
       dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-      if (warp == 0 && g == 0) p.part_lse[prow] = l > 0.f ? m_run[nt][e] + log2f(l) : -INFINITY;
+      if (warp == 0 && g == 0) p.part_lse[prow] = l > 0.f ? m_used[nt][e] + log2f(l) : -INFINITY;
     }
 }
 
@@ -748,12 +802,12 @@ static int launch_decode_nt(const DecodeParams& dp, int nt, int num_seqs, cudaSt
 
 using namespace qp;
 
-// Split-count heuristic: whole waves of 2 CTAs per SM, a fixed cost per CTA, at least 4 tiles per split.
+// Split-count heuristic: whole waves of 3 CTAs per SM, a fixed cost per CTA, at least 4 tiles per split.
 extern "C" int qp_decode_num_splits(int num_seqs, int num_kv_heads, int max_seqlen_k, int sm_count) {
   if (sm_count <= 0) sm_count = device_sm_count();
   const int pairs = max(1, num_seqs * num_kv_heads);
   const int tiles = max(1, (max_seqlen_k + DEC_TILE - 1) / DEC_TILE);
-  const int slots = 2 * sm_count;
+  const int slots = 3 * sm_count;
   const int max_splits = max(1, min(1024, tiles / 4));
   int best = 1;
   double best_cost = 1e30;
