@@ -114,7 +114,7 @@ def build_request(torch, ops, w, device, seqs, seed=0):
     """A paged cache holding `seqs` requests of the workload, filled through the B200 store, plus the call args."""
     from vllm_quantpack_b200.attention import k8v4_kv
     ctx, qlen, fmt = w["ctx"], w["qlen"], w["fmt"]
-    nb_per = ctx // BS
+    nb_per = (ctx + BS - 1) // BS
     nblocks = seqs * nb_per + 8
     perm = torch.randperm(nblocks, generator=torch.Generator().manual_seed(seed + 1)).to(torch.int32)
     table = perm[: seqs * nb_per].view(seqs, nb_per).to(device)

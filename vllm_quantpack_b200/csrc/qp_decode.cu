@@ -76,13 +76,14 @@ struct DecSmem {
   static constexpr int CELL = Cell<FMT>::BYTES;
   static constexpr int ROWS = 8 * NT;  // query rows held (padded to whole n-tiles)
   static constexpr int STAGE_BYTES = DEC_TILE * CELL;
+  static constexpr int P_BYTES = DEC_TILE * PLayout<NT>::STRIDE;
   static constexpr int OFF_STAGES = 0;
   static constexpr int OFF_Q = OFF_STAGES + DEC_STAGES * STAGE_BYTES;
-  static constexpr int OFF_P = OFF_Q + ROWS * Q_STRIDE;
-  static constexpr int OFF_RED = OFF_P + DEC_TILE * PLayout<NT>::STRIDE;  // [ROWS][4 warps] f32 (row max, then l)
-  static constexpr int OFF_VS = OFF_RED + ROWS * 4 * 4;                   // [4] f32 (value-scale max per warp)
-  static constexpr int OFF_ZB = OFF_VS + 16;                              // [2][64] u16 zero-point biases
-  static constexpr int OFF_ROWP = OFF_ZB + 2 * DEC_TILE * 2;              // qscale, cq, qsum: [3][ROWS]
+  static constexpr int OFF_P = OFF_Q + ROWS * Q_STRIDE;       // 2 buffers (alternate tiles)
+  static constexpr int OFF_RED = OFF_P + 2 * P_BYTES;         // [ROWS][4 warps] f32 (row max, then l)
+  static constexpr int OFF_VS = OFF_RED + ROWS * 4 * 4;       // [4] f32 (value-scale max per warp)
+  static constexpr int OFF_ZB = OFF_VS + 16;                  // [2 buffers][lo, hi][64] u16 zero-point biases
+  static constexpr int OFF_ROWP = OFF_ZB + 2 * 2 * DEC_TILE * 2;  // qscale, cq, qsum: [3][ROWS]
   static constexpr int OFF_BAR = (OFF_ROWP + 3 * ROWS * 4 + 7) / 8 * 8;
   static constexpr int BYTES = OFF_BAR + DEC_STAGES * 8;
 };
@@ -127,11 +128,20 @@ __device__ __forceinline__ uint32_t nib_hi(uint32_t x, uint32_t hi_bias) {
 }
 
 // Online softmax with a lazy maximum: P = exp2(s - m_used) is allowed up to 2^RESCALE_SLACK, so the O accumulators
-// are rescaled only when a row maximum grows by more than that (rare after the first tiles), not every tile.
+// are rescaled only when a row maximum grows by more than that (rare after the first tiles), not every tile. Every
+// thread checks its own scores against m_used; only when some score (or value scale) leaves the allowed range does
+// the CTA take the slow path that exchanges the exact tile maxima.
 constexpr float RESCALE_SLACK = 8.f;
 
+// 2^x in one MUFU instruction (ex2.approx; x <= RESCALE_SLACK here, very negative x flush to 0)
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <int FMT, int DT, int NT>
-__global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(const DecodeParams p) {
   using SM = DecSmem<FMT, NT>;
   constexpr int CELL = SM::CELL;
   constexpr int ROWS = SM::ROWS;
@@ -139,11 +149,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodePara
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem + SM::OFF_STAGES;
   uint8_t* qsm = smem + SM::OFF_Q;
-  uint8_t* psm = smem + SM::OFF_P;
   float* red = reinterpret_cast<float*>(smem + SM::OFF_RED);
   float* red_vs = reinterpret_cast<float*>(smem + SM::OFF_VS);
-  uint16_t* zb_lo = reinterpret_cast<uint16_t*>(smem + SM::OFF_ZB);
-  uint16_t* zb_hi = zb_lo + DEC_TILE;
+  uint16_t* zbuf = reinterpret_cast<uint16_t*>(smem + SM::OFF_ZB);  // [buf][lo/hi][64]
   float* row_qscale = reinterpret_cast<float*>(smem + SM::OFF_ROWP);
   float* row_cq = row_qscale + ROWS;
   float* row_qsum = row_cq + ROWS;
@@ -179,35 +187,43 @@ __global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodePara
   const int32_t* btab = p.block_table + static_cast<int64_t>(seq) * p.bt_stride;
   const uint8_t* head_base = p.cache + static_cast<int64_t>(kvh) * p.head_stride;
 
-  // --- producer: one thread issues the bulk copies of a tile (whole 16-token runs; block_size % 16 == 0, so a run
-  // never crosses a block, and the last run of a sequence stays inside the block that holds its last token). The
-  // block-table entries of a tile (one per 16-token group) are loaded a tile ahead of the copies that use them. ----
-  auto load_blocks = [&](int i, int (&blk)[4]) {
+  // --- producer (thread 0): bulk copies of whole 16-token runs (block_size % 16 == 0, so a run never crosses a block
+  // and the last run of a sequence stays inside the block that holds its last token). The block of each 16-token
+  // group is tracked incrementally (no division) and its table entry loaded one tile ahead of the copy. ----------
+  int nb_idx = 0, nb_off = 0;  // block-table index / in-block token offset of the first token of tile `issued`
+  auto tile_groups = [&](int i) {
     const int tok_begin = (tile0 + i) * DEC_TILE;
-    const int groups = (min(tok_begin + DEC_TILE, n) - tok_begin + 15) >> 4;
-#pragma unroll
-    for (int gi = 0; gi < 4; ++gi) blk[gi] = gi < groups ? __ldg(btab + (tok_begin + 16 * gi) / p.block_size) : 0;
+    return (min(tok_begin + DEC_TILE, n) - tok_begin + 15) >> 4;
   };
-  auto issue_tile = [&](int i, const int (&blk)[4]) {
+  auto load_blocks = [&](int i, int (&blk)[4], int (&inb)[4]) {
+    const int groups = tile_groups(i);
+#pragma unroll
+    for (int gi = 0; gi < 4; ++gi) {
+      blk[gi] = gi < groups ? __ldg(btab + nb_idx) : 0;
+      inb[gi] = nb_off;
+      nb_off += 16;
+      if (nb_off == p.block_size) {
+        nb_off = 0;
+        ++nb_idx;
+      }
+    }
+  };
+  auto issue_tile = [&](int i, const int (&blk)[4], const int (&inb)[4]) {
     const int stage = i % DEC_STAGES;
-    const int tok_begin = (tile0 + i) * DEC_TILE;
-    const int tok_end = min(tok_begin + DEC_TILE, n);
-    const int groups = (tok_end - tok_begin + 15) >> 4;
+    const int groups = tile_groups(i);
     mbar_arrive_expect_tx(&bars[stage], static_cast<uint32_t>(groups * 16 * CELL));
     uint8_t* dst = stages + stage * SM::STAGE_BYTES;
 #pragma unroll
     for (int gi = 0; gi < 4; ++gi) {
-      const int tok = tok_begin + gi * 16;
-      const int in_blk = tok % p.block_size;
       // a group continues the previous copy when it is the next run of the same block
-      const bool starts = gi == 0 || in_blk == 0 || blk[gi] != blk[gi - 1];
+      const bool starts = gi == 0 || inb[gi] == 0 || blk[gi] != blk[gi - 1];
       if (gi < groups && starts) {
         int run = 1;
 #pragma unroll
         for (int k = gi + 1; k < 4; ++k)
-          if (k < groups && run == k - gi && blk[k] == blk[gi] && (tok + 16 * (k - gi)) % p.block_size != 0) ++run;
+          if (k < groups && run == k - gi && blk[k] == blk[gi] && inb[k] != 0) ++run;
         const uint8_t* src =
-            head_base + static_cast<int64_t>(blk[gi]) * p.block_stride + static_cast<int64_t>(in_blk) * CELL;
+            head_base + static_cast<int64_t>(blk[gi]) * p.block_stride + static_cast<int64_t>(inb[gi]) * CELL;
         bulk_g2s(dst + gi * 16 * CELL, src, static_cast<uint32_t>(run * 16 * CELL), &bars[stage]);
       }
     }
@@ -218,16 +234,18 @@ __global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodePara
     fence_mbar_init();
   }
   __syncthreads();
-  int issued = 0;        // tiles whose copies thread 0 has issued
-  int next_blk[4] = {};  // block-table entries of tile `issued` (thread 0)
+  int issued = 0;                        // tiles whose copies thread 0 has issued
+  int next_blk[4] = {}, next_inb[4] = {};  // block-table entries of tile `issued` (thread 0)
   if (tid == 0) {
+    nb_idx = tile0 * DEC_TILE / p.block_size;
+    nb_off = tile0 * DEC_TILE - nb_idx * p.block_size;
     issued = min(ntl, DEC_STAGES);
     for (int i = 0; i < issued; ++i) {
-      int blk[4];
-      load_blocks(i, blk);
-      issue_tile(i, blk);
+      int blk[4], inb[4];
+      load_blocks(i, blk, inb);
+      issue_tile(i, blk, inb);
     }
-    if (issued < ntl) load_blocks(issued, next_blk);
+    if (issued < ntl) load_blocks(issued, next_blk, next_inb);
   }
 
   // --- Q: rotate, scale to fp16 with a per-row power of two, permute channels ------------------------------
@@ -291,7 +309,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodePara
 
   // --- per-thread state: this thread's query rows are r = 8 nt + 2 t + e ------------------------------------
   float qsc[NT][2], qcq[NT][2], qsum[NT][2];
-  int lim[NT][2];  // last key position each row sees (-1 for padding rows)
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -300,7 +317,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodePara
       qsc[nt][e] = row_qscale[r];
       qcq[nt][e] = row_cq[r];
       qsum[nt][e] = row_qsum[r];
-      lim[nt][e] = r < rows ? n - qlen + r / p.group : -1;
     }
   float o[4][NT][4];
 #pragma unroll
@@ -317,11 +333,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodePara
       m_used[nt][e] = -INFINITY;
       l_part[nt][e] = 0.f;
     }
-  int e_run = -1000;      // running power-of-two range of P_v (value scales)
-  float pv_mul = 0.f;     // 2^-e_run
+  int e_run = -1000;    // running power-of-two range of P_v (value scales): every value scale < 2^e_run
+  float pv_mul = 0.f;   // 2^-e_run
+  float v_limit = 0.f;  // 2^e_run
   const int causal_from = n - qlen + 1;  // keys >= this are hidden from some query token
   const uint32_t qsm_base = smem_u32(qsm);
-  const uint32_t psm_base = smem_u32(psm);
   const int tau_a = 16 * warp + g, tau_b = tau_a + 8;
   const int pk_a = pv_k_of_token(tau_a) * PSTRIDE, pk_b = pv_k_of_token(tau_b) * PSTRIDE;
   bool failed = false;
@@ -329,8 +345,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodePara
 
   for (int i = 0; i < ntl; ++i) {
     const int stage = i % DEC_STAGES;
+    const int buf = i & 1;
+    uint8_t* psm = smem + SM::OFF_P + buf * SM::P_BYTES;
+    uint16_t* zb_lo = zbuf + buf * 2 * DEC_TILE;
+    uint16_t* zb_hi = zb_lo + DEC_TILE;
     // A thread whose wait runs out keeps going on whatever the stage holds (nothing reaches global memory before
-    // the epilogue); the CTA leaves together at barrier (A), so no thread skips a __syncthreads.
+    // the epilogue); the CTA leaves together at barrier (B), so no thread skips a __syncthreads.
     failed |= !mbar_wait_bounded(&bars[stage], (i / DEC_STAGES) & 1);
     const uint8_t* tile = stages + stage * SM::STAGE_BYTES;
     const int tok_base = (tile0 + i) * DEC_TILE;
@@ -400,118 +420,55 @@ __global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodePara
       }
     }
 
-    // ---------------- scores (log2 units), masks, tile row max ----------------
+    // ---------------- scores (log2 units) and masks ----------------
     const int tok_a = tok_base + tau_a, tok_b = tok_base + tau_b;
+    const uint32_t kwa = *reinterpret_cast<const uint32_t*>(tile + tau_a * CELL + p.ks_off);
+    const uint32_t kwb = *reinterpret_cast<const uint32_t*>(tile + tau_b * CELL + p.ks_off);
+    const uint32_t vwa = *reinterpret_cast<const uint32_t*>(tile + tau_a * CELL + p.vs_off);
+    const uint32_t vwb = *reinterpret_cast<const uint32_t*>(tile + tau_b * CELL + p.vs_off);
     float ks_a, ks_b, kz_a = 0.f, kz_b = 0.f;
-    {
-      const uint32_t wa = *reinterpret_cast<const uint32_t*>(tile + tau_a * CELL + p.ks_off);
-      const uint32_t wb = *reinterpret_cast<const uint32_t*>(tile + tau_b * CELL + p.ks_off);
-      if constexpr (FMT == FMT_INT4) {
-        ks_a = __uint_as_float(wa & 0xFFFFFFF0u);
-        ks_b = __uint_as_float(wb & 0xFFFFFFF0u);
-        kz_a = static_cast<float>(wa & 0xFu);
-        kz_b = static_cast<float>(wb & 0xFu);
-      } else {
-        ks_a = __uint_as_float(wa);
-        ks_b = __uint_as_float(wb);
-      }
+    if constexpr (FMT == FMT_INT4) {
+      ks_a = __uint_as_float(kwa & 0xFFFFFFF0u);
+      ks_b = __uint_as_float(kwb & 0xFFFFFFF0u);
+      kz_a = static_cast<float>(kwa & 0xFu);
+      kz_b = static_cast<float>(kwb & 0xFu);
+    } else {
+      ks_a = __uint_as_float(kwa);
+      ks_b = __uint_as_float(kwb);
+    }
+    // value scales of this thread's two tokens (tokens past the end count as scale 0)
+    const float vs_a = tok_a < n ? __uint_as_float(vwa & 0xFFFFFFF0u) : 0.f;
+    const float vs_b = tok_b < n ? __uint_as_float(vwb & 0xFFFFFFF0u) : 0.f;
+    if (t == 0) {  // zero-point biases of the value operand, per token (read by the PV phase after barrier B)
+      zb_lo[tau_a] = static_cast<uint16_t>(0x6400u | (vwa & 0xFu));
+      zb_lo[tau_b] = static_cast<uint16_t>(0x6400u | (vwb & 0xFu));
+      zb_hi[tau_a] = static_cast<uint16_t>(0xD400u | ((vwa & 0xFu) << 4));
+      zb_hi[tau_b] = static_cast<uint16_t>(0xD400u | ((vwb & 0xFu) << 4));
     }
     const bool need_mask = tok_base + DEC_TILE > causal_from;
     float sc[NT][4];
+    bool grow = vs_a >= v_limit || vs_b >= v_limit;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      float tm[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         float s0 = (sacc[nt][e] - fmaf(kz_a, qsum[nt][e], qcq[nt][e])) * (ks_a * qsc[nt][e]);
         float s1 = (sacc[nt][2 + e] - fmaf(kz_b, qsum[nt][e], qcq[nt][e])) * (ks_b * qsc[nt][e]);
         if (need_mask) {
-          if (tok_a > lim[nt][e]) s0 = -INFINITY;  // also past the context: lim <= n - 1
-          if (tok_b > lim[nt][e]) s1 = -INFINITY;
+          const int r = 8 * nt + 2 * t + e;
+          const int lim = r < rows ? n - qlen + r / p.group : -1;  // last key this row sees
+          if (tok_a > lim) s0 = -INFINITY;                          // also past the context: lim <= n - 1
+          if (tok_b > lim) s1 = -INFINITY;
         }
         sc[nt][e] = s0;
         sc[nt][2 + e] = s1;
-        float mx = fmaxf(s0, s1);
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        tm[e] = mx;
+        grow |= fmaxf(s0, s1) > m_used[nt][e] + RESCALE_SLACK;
       }
-      if (g == 0) {
-        red[(8 * nt + 2 * t) * 4 + warp] = tm[0];
-        red[(8 * nt + 2 * t + 1) * 4 + warp] = tm[1];
-      }
-    }
-    // value scales and zero points of this thread's two tokens (tokens past the end count as scale 0)
-    float vs_a, vs_b;
-    uint32_t vz_a, vz_b;
-    {
-      const uint32_t wa = *reinterpret_cast<const uint32_t*>(tile + tau_a * CELL + p.vs_off);
-      const uint32_t wb = *reinterpret_cast<const uint32_t*>(tile + tau_b * CELL + p.vs_off);
-      vs_a = tok_a < n ? __uint_as_float(wa & 0xFFFFFFF0u) : 0.f;
-      vs_b = tok_b < n ? __uint_as_float(wb & 0xFFFFFFF0u) : 0.f;
-      vz_a = wa & 0xFu;
-      vz_b = wb & 0xFu;
-      const float vm = warp_max(fmaxf(vs_a, vs_b));
-      if (lane == 0) red_vs[warp] = vm;
-    }
-    // (A) row maxima visible; every warp is done with tile i - 1
-    if (__syncthreads_or(failed)) {
-      failed = true;
-      fail_tile = i;
-      break;
-    }
-    if (tid == 0 && i >= 1 && i - 1 + DEC_STAGES < ntl) {
-      issue_tile(issued, next_blk);  // issued == i - 1 + DEC_STAGES
-      ++issued;
-      if (issued < ntl) load_blocks(issued, next_blk);
-    }
-    if (t == 0) {  // zero-point biases of the value operand, per token (read by the PV phase after barrier B)
-      zb_lo[tau_a] = static_cast<uint16_t>(0x6400u | vz_a);
-      zb_lo[tau_b] = static_cast<uint16_t>(0x6400u | vz_b);
-      zb_hi[tau_a] = static_cast<uint16_t>(0xD400u | (vz_a << 4));
-      zb_hi[tau_b] = static_cast<uint16_t>(0xD400u | (vz_b << 4));
     }
 
-    // ---------------- lazy rescale, P, P_v ----------------
-    {
-      float m_tile[NT][2];
-      bool grow = false;
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float4 mv = *reinterpret_cast<const float4*>(red + (8 * nt + 2 * t + e) * 4);
-          m_tile[nt][e] = fmaxf(fmaxf(mv.x, mv.y), fmaxf(mv.z, mv.w));
-          grow |= m_tile[nt][e] > m_used[nt][e] + RESCALE_SLACK;
-        }
-      const float4 vv = *reinterpret_cast<const float4*>(red_vs);
-      const float vmax = fmaxf(fmaxf(vv.x, vv.y), fmaxf(vv.z, vv.w));
-      int e_tile = -1000;
-      if (vmax > 0.f) frexpf(vmax, &e_tile);  // vmax < 2^e_tile
-      const bool vgrow = e_tile > e_run;      // the same for every thread of the CTA
-      if (__any_sync(0xffffffffu, grow) || vgrow) {
-        const int e_new = max(e_run, e_tile);
-        const float o_range = e_run == -1000 ? 0.f : ldexpf(1.f, e_run - e_new);
-        e_run = e_new;
-        pv_mul = e_new == -1000 ? 0.f : ldexpf(1.f, -e_new);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float mt_ = m_tile[nt][e];
-            const float m_new = mt_ > m_used[nt][e] + RESCALE_SLACK ? mt_ : m_used[nt][e];
-            const float alpha = m_new == m_used[nt][e] ? 1.f : exp2f(m_used[nt][e] - m_new);
-            m_used[nt][e] = m_new;
-            const float ao = alpha * o_range;
-            l_part[nt][e] *= alpha;
-#pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
-              o[mt][nt][e] *= ao;
-              o[mt][nt][2 + e] *= ao;
-            }
-          }
-      }
+    // ---------------- P with the current maximum and value range (optimistic) ----------------
+    float psum[NT][2];
+    auto make_p = [&]() {
       const float va = vs_a * pv_mul, vb = vs_b * pv_mul;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
@@ -519,9 +476,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodePara
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const float base = m_used[nt][e] == -INFINITY ? 0.f : m_used[nt][e];
-          const float pa = exp2f(sc[nt][e] - base);
-          const float pb = exp2f(sc[nt][2 + e] - base);
-          l_part[nt][e] += pa + pb;
+          const float pa = fast_exp2(sc[nt][e] - base);
+          const float pb = fast_exp2(sc[nt][2 + e] - base);
+          psum[nt][e] = pa + pb;
           pv[e] = pa * va;
           pv[2 + e] = pb * vb;
         }
@@ -529,10 +486,86 @@ __global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodePara
         *reinterpret_cast<__half2*>(psm + pk_a + (8 * nt + 2 * t) * 2) = __floats2half2_rn(pv[0], pv[1]);
         *reinterpret_cast<__half2*>(psm + pk_b + (8 * nt + 2 * t) * 2) = __floats2half2_rn(pv[2], pv[3]);
       }
+    };
+    make_p();
+
+    // this thread's value words for the PV phase: word 8 warp + g of tokens 16 kk + 4 t + j
+    uint32_t vw[4][4];
+    {
+      const uint8_t* vbase = tile + p.v_off + 4 * (8 * warp + g);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) vw[kk][j] = *reinterpret_cast<const uint32_t*>(vbase + (16 * kk + 4 * t + j) * CELL);
     }
-    __syncthreads();  // (B) P^T and the zero-point biases visible
+
+    // (B) P^T and the zero-point biases visible; the stage is no longer read
+    if (__syncthreads_or(grow || failed)) {
+      if (__syncthreads_or(failed)) {
+        failed = true;
+        fail_tile = i;
+        break;
+      }
+      // slow path: exact tile maxima and value range, rescale, recompute P
+      float tm[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float mx = fmaxf(sc[nt][e], sc[nt][2 + e]);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          tm[nt][e] = mx;
+          if (g == 0) red[(8 * nt + 2 * t + e) * 4 + warp] = mx;
+        }
+      const float vm = warp_max(fmaxf(vs_a, vs_b));
+      if (lane == 0) red_vs[warp] = vm;
+      __syncthreads();
+      const float4 vv = *reinterpret_cast<const float4*>(red_vs);
+      const float vmax = fmaxf(fmaxf(vv.x, vv.y), fmaxf(vv.z, vv.w));
+      int e_tile = -1000;
+      if (vmax > 0.f) frexpf(vmax, &e_tile);  // vmax < 2^e_tile
+      const int e_new = max(e_run, e_tile);
+      const float o_range = e_run == -1000 ? 0.f : ldexpf(1.f, e_run - e_new);
+      e_run = e_new;
+      pv_mul = e_new == -1000 ? 0.f : ldexpf(1.f, -e_new);
+      v_limit = e_new == -1000 ? 0.f : ldexpf(1.f, e_new);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float4 mv = *reinterpret_cast<const float4*>(red + (8 * nt + 2 * t + e) * 4);
+          const float mt_ = fmaxf(fmaxf(mv.x, mv.y), fmaxf(mv.z, mv.w));
+          const float m_new = mt_ > m_used[nt][e] + RESCALE_SLACK ? mt_ : m_used[nt][e];
+          const float alpha = m_new == m_used[nt][e] ? 1.f : fast_exp2(m_used[nt][e] - m_new);
+          m_used[nt][e] = m_new;
+          const float ao = alpha * o_range;
+          l_part[nt][e] *= alpha;
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt) {
+            o[mt][nt][e] *= ao;
+            o[mt][nt][2 + e] *= ao;
+          }
+        }
+      (void)tm;
+      make_p();
+      __syncthreads();  // the recomputed P^T visible
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) l_part[nt][e] += psum[nt][e];
+
+    // the stage is free: refill it with tile i + DEC_STAGES
+    if (tid == 0 && issued < ntl) {
+      issue_tile(issued, next_blk, next_inb);  // issued == i + DEC_STAGES
+      ++issued;
+      if (issued < ntl) load_blocks(issued, next_blk, next_inb);
+    }
 
     // ---------------- PV: warp handles channels 64 warp + [0, 64) ----------------
+    const uint32_t psm_base = smem_u32(psm);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       uint32_t bf[NT][2];
@@ -550,19 +583,14 @@ __global__ void __launch_bounds__(DEC_THREADS, 3) decode_kernel(const DecodePara
           }
         }
       }
-      const uint8_t* vbase = tile + p.v_off + 4 * (8 * warp + g);
       const int tau0 = 16 * kk + 4 * t;
-      const uint32_t w0 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 0) * CELL);
-      const uint32_t w1 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 1) * CELL);
-      const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 2) * CELL);
-      const uint32_t w3 = *reinterpret_cast<const uint32_t*>(vbase + (tau0 + 3) * CELL);
       const uint2 blo = *reinterpret_cast<const uint2*>(zb_lo + tau0);  // {tau0, tau0+1}, {tau0+2, tau0+3}
       const uint2 bhi = *reinterpret_cast<const uint2*>(zb_hi + tau0);
       // f = 0: tokens (tau0, tau0 + 1); f = 1: tokens (tau0 + 2, tau0 + 3)
       uint32_t vr[2][8];  // [f][channel offset 0..7]
 #pragma unroll
       for (int f = 0; f < 2; ++f) {
-        const uint32_t wa = f ? w2 : w0, wb = f ? w3 : w1;
+        const uint32_t wa = vw[kk][2 * f], wb = vw[kk][2 * f + 1];
         const uint32_t lo_b = f ? blo.y : blo.x, hi_b = f ? bhi.y : bhi.x;
         const uint32_t x = prmt(wa, wb, 0x5410u), y = prmt(wa, wb, 0x7632u);
         const uint32_t x8 = x >> 8, y8 = y >> 8;
