@@ -356,11 +356,11 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
     const int tok_base = (tile0 + i) * DEC_TILE;
 
     // ---------------- QK: warp handles tokens 16 warp + [0, 16) ----------------
-    float sacc[NT][4];
+    float sacc[NT][4], sacc2[NT][4];  // two accumulator chains (even / odd k-steps), summed after the loop
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) sacc[nt][c] = 0.f;
+      for (int c = 0; c < 4; ++c) sacc[nt][c] = sacc2[nt][c] = 0.f;
     const uint8_t* rowg = tile + tau_a * CELL;
     const uint8_t* rowg8 = rowg + 8 * CELL;
     if constexpr (FMT == FMT_INT4) {
@@ -387,7 +387,7 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
             uint32_t b0, b1, b2, b3;
             ldmatrix_x4(b0, b1, b2, b3, qsm_base + (8 * nt + (lane & 7)) * Q_STRIDE + (32 * j + 8 * (lane >> 3)) * 2);
             mma_f16_16816(sacc[nt], A0, b0, b1);
-            mma_f16_16816(sacc[nt], A1, b2, b3);
+            mma_f16_16816(sacc2[nt], A1, b2, b3);
           }
         }
       }
@@ -414,11 +414,15 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
             uint32_t b0, b1, b2, b3;
             ldmatrix_x4(b0, b1, b2, b3, qsm_base + (8 * nt + (lane & 7)) * Q_STRIDE + (16 * s0 + 8 * (lane >> 3)) * 2);
             mma_f16_16816(sacc[nt], A[0], b0, b1);
-            mma_f16_16816(sacc[nt], A[1], b2, b3);
+            mma_f16_16816(sacc2[nt], A[1], b2, b3);
           }
         }
       }
     }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sacc[nt][c] += sacc2[nt][c];
 
     // ---------------- scores (log2 units) and masks ----------------
     const int tok_a = tok_base + tau_a, tok_b = tok_base + tau_b;
@@ -682,27 +686,30 @@ struct MergeParams {
   float out_scale;  // multiplies the output (mode 0: 1 / head)
 };
 
+constexpr int MERGE_THREADS = 512;
+
 template <int DT, int HS>
-__global__ void __launch_bounds__(256) merge_kernel(const MergeParams p) {
+__global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(const MergeParams p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  constexpr int C4 = HS / 4;    // float4 groups per row
-  constexpr int SG = 256 / C4;  // split groups
+  constexpr int C4 = HS / 4;              // float4 groups per row
+  constexpr int SG = MERGE_THREADS / C4;  // split groups
+  constexpr int NW = MERGE_THREADS / 32;
   __shared__ float w_sm[1024];
   __shared__ __align__(16) float acc_sm[SG][HS];
-  __shared__ float red[8];
+  __shared__ float red[NW];
   __shared__ float tot_sm;
   const int tok = blockIdx.x, qh = blockIdx.y, tid = threadIdx.x;
   const float* lse = p.part_lse + tok * p.pl_t + qh * p.pl_h;
   float mx = -INFINITY;
-  for (int s = tid; s < p.num_splits; s += 256) mx = fmaxf(mx, lse[s * p.pl_s]);
+  for (int s = tid; s < p.num_splits; s += MERGE_THREADS) mx = fmaxf(mx, lse[s * p.pl_s]);
   mx = warp_max(mx);
   if ((tid & 31) == 0) red[tid >> 5] = mx;
   __syncthreads();
   float M = red[0];
 #pragma unroll
-  for (int i = 1; i < 8; ++i) M = fmaxf(M, red[i]);
+  for (int i = 1; i < NW; ++i) M = fmaxf(M, red[i]);
   float tot = 0.f;
-  for (int s = tid; s < p.num_splits; s += 256) {
+  for (int s = tid; s < p.num_splits; s += MERGE_THREADS) {
     const float l = lse[s * p.pl_s];
     const float w = (M == -INFINITY || l == -INFINITY) ? 0.f : exp2f(l - M);
     w_sm[s] = w;
@@ -715,28 +722,36 @@ __global__ void __launch_bounds__(256) merge_kernel(const MergeParams p) {
   if (tid == 0) {
     float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s += red[i];
+    for (int i = 0; i < NW; ++i) s += red[i];
     tot_sm = s;
   }
   const int c4 = tid % C4, sg = tid / C4;
   float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
   const float* po = p.part_o + tok * p.po_t + qh * p.po_h + 4 * c4;
-#pragma unroll 4
-  for (int s = sg; s < p.num_splits; s += SG) {
-    const float w = w_sm[s];
-    if (w == 0.f) continue;
-    const float4 v = *reinterpret_cast<const float4*>(po + s * p.po_s);
-    a.x = fmaf(w, v.x, a.x);
-    a.y = fmaf(w, v.y, a.y);
-    a.z = fmaf(w, v.z, a.z);
-    a.w = fmaf(w, v.w, a.w);
+  // 8 partials per round, loads issued before any is used (the partials are L2-resident: latency-bound)
+  for (int s0 = sg; s0 < p.num_splits; s0 += 8 * SG) {
+    float4 v[8];
+    float w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int s = s0 + k * SG;
+      w[k] = s < p.num_splits ? w_sm[s] : 0.f;
+      v[k] = w[k] != 0.f ? *reinterpret_cast<const float4*>(po + s * p.po_s) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      a.x = fmaf(w[k], v[k].x, a.x);
+      a.y = fmaf(w[k], v[k].y, a.y);
+      a.z = fmaf(w[k], v[k].z, a.z);
+      a.w = fmaf(w[k], v[k].w, a.w);
+    }
   }
   *reinterpret_cast<float4*>(&acc_sm[sg][4 * c4]) = a;
   __syncthreads();
   const float T = tot_sm;
   const float inv = T > 0.f ? 1.f / T : 0.f;
   if (p.mode == 1) {
-    for (int c = tid; c < HS; c += 256) {
+    for (int c = tid; c < HS; c += MERGE_THREADS) {
       float v = 0.f;
 #pragma unroll
       for (int s = 0; s < SG; ++s) v += acc_sm[s][c];
@@ -768,7 +783,7 @@ template <int DT, int HS>
 static int launch_merge(const MergeParams& mp, int num_tokens, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(num_tokens), static_cast<unsigned>(mp.nq));
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(MERGE_THREADS);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
