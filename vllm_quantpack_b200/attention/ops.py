@@ -211,3 +211,37 @@ def merge_attn_partials(part_o, part_lse, out, lse_out=None):
               part_o.stride(0), part_lse.data_ptr(), part_lse.stride(1), part_lse.stride(2), part_lse.stride(0), mode,
               out.data_ptr(), out.stride(0), out.stride(1), lptr, sbits, _stream(out.device))
     return out
+
+
+# ------------------------------------------------------------------------------------------------------ prefill
+
+
+def prefill(q, key_cache, value_cache, out, *, block_row, n, softmax_scale, k_scale_cache, v_scale_cache,
+            q_rotated=False, out_fp32_lse=None, ws=None):
+    """Chunk prefill of one sequence on the tensor cores: q (qlen, query heads, hs) are the last qlen positions of a
+    context of n cached tokens (causal among themselves); block_row is the sequence's int32 block-table row.
+    `out` gets the model-domain output in q's dtype, or with `out_fp32_lse` the fp32 RHT-domain output and its
+    base-2 lse (vllm_quantpack/attention/int4_prefill.py:203-232 returns the RHT-domain output for rotated queries)."""
+    hs, nq, qlen = q.shape[-1], q.shape[1], q.shape[0]
+    lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
+    if block_row.dtype != torch.int32 or block_row.stride(-1) != 1:
+        raise TypeError("block_row must be a contiguous int32 row")
+    if q.stride(-1) != 1 or out.stride(-1) != 1:
+        raise ValueError("q / out rows must be contiguous")
+    dt = _dtype_code(q, "prefill")
+    wbytes = _lib.load().qp_prefill_workspace_bytes(qlen, int(n), nq, lay.nkv, hs)
+    if ws is None:
+        ws = workspace(q.device, wbytes)
+    if out_fp32_lse is not None:
+        if out.dtype != torch.float32 or out_fp32_lse.dtype != torch.float32 or not out_fp32_lse.is_contiguous():
+            raise TypeError("out and lse must be fp32 (lse contiguous) for the RHT-domain output")
+        mode, lse_ptr = 1, out_fp32_lse.data_ptr()
+    else:
+        if out.dtype != q.dtype:
+            raise TypeError("out dtype must match q")
+        mode, lse_ptr = 0, None
+    _lib.call("qp_prefill", lay.fmt, dt, q.data_ptr(), q.stride(0), q.stride(1), out.data_ptr(), out.stride(0),
+              out.stride(1), qlen, int(n), block_row.data_ptr(), *lay.args(), nq, lay.nkv, hs, float(softmax_scale),
+              rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)), mode, lse_ptr, ws.data_ptr(),
+              ws.numel() * ws.element_size(), _stream(q.device))
+    return out
