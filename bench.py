@@ -39,6 +39,7 @@ WORKLOADS = {
     "c1": dict(fmt="int4", seqs=1, ctx=131072, qlen=2),
     "c2b": dict(fmt="int4", seqs=32, ctx=32768, qlen=2),
     "c4": dict(fmt="k8v4", seqs=1, ctx=262144, qlen=4),
+    "c3": dict(fmt="int4", seqs=1, ctx=229376 + 1024, qlen=1024, prefill=True),
 }
 CELL = {"int4": HS + 8, "k8v4": HS * 3 // 2 + 8}
 
@@ -47,6 +48,12 @@ def algorithmic_bytes(w, seqs=None):
     """Bytes one attention call must move: every cached cell once, plus q and out (bf16)."""
     seqs = w["seqs"] if seqs is None else seqs
     return seqs * (w["ctx"] * NKV * CELL[w["fmt"]] + 2 * w["qlen"] * NQ * HS * 2)
+
+
+def prefill_flops(w):
+    """QK and PV flops of one chunk, causal counted exactly: 4 * nq * hs * sum_i (ctx - qlen + i + 1)."""
+    ctx, qlen = w["ctx"], w["qlen"]
+    return 4 * NQ * HS * (qlen * (ctx - qlen) + qlen * (qlen + 1) // 2)
 
 
 def peaks():
@@ -222,6 +229,60 @@ def run_reference(args, w, rank, world):
 # ---------------------------------------------------------------------------------------------------- GPU arm
 
 
+def run_prefill(args, w, rank, world, local_rank):
+    """Chunk prefill (c3): one request, qlen queries over the cached context, on the tensor cores."""
+    import torch
+    from vllm_quantpack_b200 import _lib
+    from vllm_quantpack_b200.attention import ops
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    R = build_request(torch, ops, w, device, 1, seed=rank)
+    kc, vc, ks, vs = R["views"]
+    q = R["q"]
+    out = torch.empty_like(q)
+    row = R["table"][0].contiguous()
+    call = dict(block_row=row, n=w["ctx"], softmax_scale=HS ** -0.5, k_scale_cache=ks, v_scale_cache=vs)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    q_dev = torch.empty_like(q)
+
+    def step():
+        ops.prefill(q, kc, vc, out, **call)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        ops.prefill(q_dev, kc, vc, out, **call)
+        out_host.copy_(out, non_blocking=True)
+
+    with Clocks(local_rank) as clk:
+        t = timed_steps(torch, step, args.steps, args.warmup, flush)
+    t_e2e = timed_steps(torch, e2e_step, args.steps, args.warmup, flush)
+    dev_err = _lib.device_error()
+    ms, ms_e = statistics.mean(t), statistics.mean(t_e2e)
+    if rank != 0:
+        return
+    flops = prefill_flops(w)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            peak, kind = float(json.load(fh)["bf16_tflops"]), "measured"
+    except Exception:
+        peak, kind = 1590.0, "fallback"
+    achieved = flops / (ms * 1e-3) / 1e12
+    line = {"metric": "prefill_tok_s", "value": w["qlen"] / (ms * 1e-3), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4+f16", "data": "synthetic",
+            "config": {"workload": args.workload, **w, "nq": NQ, "nkv": NKV, "head_size": HS, "block_size": BS,
+                       "l2": "flushed before every step (256 MB write); cache larger than L2"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "prefill_kernel (q prep + merge included)",
+                         "algorithmic_flops_per_launch": flops, "peak_kind": kind},
+            "e2e": {"value": w["qlen"] / (ms_e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": q.numel() * 2,
+                    "d2h_bytes_per_step": out.numel() * 2},
+            "gpu_launches": 3 * args.steps, "clocks": clk.summary(), "device_error": dev_err}
+    print(json.dumps(line), flush=True)
+
+
 def run_b200(args, w, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -362,7 +423,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_b200(args, w, rank, world, local_rank)
+        if w.get("prefill"):
+            run_prefill(args, w, rank, world, local_rank)
+        else:
+            run_b200(args, w, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

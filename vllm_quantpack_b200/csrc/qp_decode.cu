@@ -133,12 +133,6 @@ __device__ __forceinline__ uint32_t nib_hi(uint32_t x, uint32_t hi_bias) {
 // the CTA take the slow path that exchanges the exact tile maxima.
 constexpr float RESCALE_SLACK = 8.f;
 
-// 2^x in one MUFU instruction (ex2.approx; x <= RESCALE_SLACK here, very negative x flush to 0)
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 template <int FMT, int DT, int NT>
 __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(const DecodeParams p) {

@@ -12,15 +12,16 @@
 //               layout) once per M-tile;
 //   warp 1      MMA issuer (one thread): S = Q K^T (M 128 rows, N 64 keys, K 256) into TMEM, then O += P V (M 128,
 //               N 256 channels, K 64 keys) into TMEM, each finished with tcgen05.commit onto mbarriers;
-//   warps 2-5   dequant: raw cells -> fp16 operands in shared memory, 128B-swizzled canonical UMMA layouts. Keys and
-//               values both become the exact small integers (u - zp) (int4) or the int8 codes (k8v4 keys); one lop3
-//               turns two nibbles into fp16, one f16x2 subtract removes 1024 + zp. The channel order inside every 8
-//               channels is [0 4 1 5 2 6 3 7] (what one lop3 pair yields), the same for Q and K (a dot product does not
-//               see the order) and undone on O in the epilogue;
-//   warps 6-9   softmax: one thread per TMEM lane (= query row). Scores = S x key scale x (softmax_scale / head x
-//               log2 e x 2^-row exponent); the running maximum is lazy and per thread (P may reach 2^8 before O is
-//               rescaled, and the rescale of O in TMEM is rare); P_v = P x value scale in fp16 is written K-major as
-//               the A operand of the PV MMA. The epilogue reads O from TMEM and writes fp32 partials + base-2 lse.
+//   warps 2-5   dequant: raw cells -> fp16 operands in shared memory, 128B-swizzled canonical UMMA layouts. One lop3
+//               turns two nibbles into fp16, one f16x2 subtract makes the exact (u - zp) (int8 codes for k8v4 keys),
+//               one f16x2 multiply applies the token's scale over a power of two (the tile's largest key scale; the
+//               piece's running largest value scale), so the softmax never touches per-key scales. The channel order
+//               inside every 8 channels is [0 4 1 5 2 6 3 7] (what one lop3 pair yields), the same for Q and K (a dot
+//               product does not see the order) and undone on O in the epilogue;
+//   warps 6-9   softmax: one thread per TMEM lane (= query row). Scores in log2 units = S x (softmax_scale / head x
+//               log2 e x 2^-row exponent x 2^key-tile exponent); the running maximum is lazy and per thread (P may
+//               reach 2^8 before O is rescaled in TMEM, which is rare); P in fp16 is written K-major as the A operand
+//               of the PV MMA. The epilogue reads O from TMEM and writes fp32 partials + base-2 lse.
 // Rows of an M-tile are (query token, query head of the KV head's group) pairs, head fastest: the 6 heads of a group
 // share every dequantised key / value tile. The (M-tile, key-tile) space is split evenly over the CTAs (stream-K):
 // an M-tile may be finished by two CTAs, whose partials the merge kernel folds (with the inverse RHT).
@@ -52,8 +53,9 @@ struct PfCfg {
   static constexpr int OFF_V = OFF_K + 32768;           // 4 N-blocks x 8 key groups x 1024 B = 32 KB
   static constexpr int OFF_P = OFF_V + 32768;           // 2 buffers x 128 rows x 128 B = 32 KB
   static constexpr int OFF_RAW = OFF_P + 32768;         // RS x RAW_BYTES
-  static constexpr int OFF_SC = OFF_RAW + RS * RAW_BYTES;  // [2 buffers][ks 64 | vs 64] f32
-  static constexpr int OFF_BAR = OFF_SC + 2 * 2 * PF_BN * 4;
+  static constexpr int OFF_SC = OFF_RAW + RS * RAW_BYTES;  // [2 buffers][key factor 2^F, value exponent E] (16 B)
+  static constexpr int OFF_XCH = OFF_SC + 2 * 16;          // [k / v][2 buffers][2 warps] tile maxima exchange
+  static constexpr int OFF_BAR = OFF_XCH + 2 * 2 * 2 * 4;
   static constexpr int NBAR = 32;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_TMEM + 16;
@@ -505,39 +507,69 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------------ dequant (warps 2..5)
-    const int dq = tid - 64;           // 0..127
-    const int kr = dq & 63;            // key row of the tile
-    const bool is_k = dq < 64;         // warps 2, 3: keys; warps 4, 5: values
+    // keys:   K_op = (u - zp) * ks * 2^-F  (F: exponent of the tile's largest key scale; 2^F goes to the softmax)
+    // values: V_op = (u - zp) * vs * 2^-E  (E: running exponent of the piece's largest value scale; O is rescaled by
+    //         the softmax when E grows). Every operand is then <= 15 in magnitude and exact up to one fp16 rounding.
+    const int dq = tid - 64;     // 0..127
+    const int kr = dq & 63;      // key row of the tile
+    const bool is_k = dq < 64;   // warps 2, 3: keys; warps 4, 5: values
+    const int wpair = (warp - 2) & 1;
     uint8_t* kop = smem + C::OFF_K;
     uint8_t* vop = smem + C::OFF_V;
+    float* xch = reinterpret_cast<float*>(smem + C::OFF_XCH) + (is_k ? 0 : 4);
+    int e_run_v = -1000;
     int64_t j = 0;
     for (; !sch.done() && !failed; sch.next(), ++j) {
       const Walk w = sch.current();
       const int stage = static_cast<int>(j % C::RS);
       const int b = static_cast<int>(j & 1);
+      if (w.first_of_piece) e_run_v = -1000;
       failed |= !mbar_wait_bounded(&bars[B_RAW_FULL + stage], (j / C::RS) & 1);
       const uint8_t* cell = smem + C::OFF_RAW + stage * C::RAW_BYTES + kr * C::CELL;
       const int tok = w.kt * PF_BN + kr;
-      // scale arrays of this tile (double-buffered with the softmax)
+      const uint32_t sw = *reinterpret_cast<const uint32_t*>(cell + (is_k ? C::KB : C::KB + 4 + PF_HS / 2));
+      const float scl = tok < p.n ? __uint_as_float((FMT == FMT_INT4 || !is_k) ? (sw & 0xFFFFFFF0u) : sw) : 0.f;
+      const uint32_t zp = (FMT == FMT_INT4 || !is_k) ? (sw & 0xFu) : 0u;
+      // tile maximum of this half's scales (two warps)
+      const float wm = warp_max(scl);
+      if (lane == 0) xch[b * 2 + wpair] = wm;
+      // the two warps of this half leave together if either gave up a wait (a bar.sync has no time bound)
+      if (named_bar_or(is_k ? 1 : 2, 64, failed)) {
+        failed = true;
+        break;
+      }
+      const float tmax = fmaxf(xch[b * 2], xch[b * 2 + 1]);
+      int ex = -1000;
+      if (tmax > 0.f) frexpf(tmax, &ex);  // tmax < 2^ex
+      if (!is_k) {
+        e_run_v = max(e_run_v, ex);
+        ex = e_run_v;
+      }
+      const float q = ex == -1000 ? 0.f : ldexpf(scl, -ex);
+      const __half2 qh2 = __floats2half2_rn(q, q);
+      const uint32_t q2 = *reinterpret_cast<const uint32_t*>(&qh2);
       if (j >= 2) failed |= !mbar_wait_bounded(&bars[B_SC_FREE + b], ((j >> 1) - 1) & 1);
+      if (kr == 0 && (warp == 2 || warp == 4)) {
+        float* scb = reinterpret_cast<float*>(smem + C::OFF_SC) + b * 4;
+        if (is_k)
+          scb[0] = ex == -1000 ? 0.f : ldexpf(1.f, ex);
+        else
+          scb[1] = __int_as_float(ex);
+      }
+      const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
       if (is_k) {
-        const uint32_t kw = *reinterpret_cast<const uint32_t*>(cell + C::KB);
-        float ks = FMT == FMT_INT4 ? __uint_as_float(kw & 0xFFFFFFF0u) : __uint_as_float(kw);
-        sc[b * 128 + kr] = tok < p.n ? ks : 0.f;
         if (j >= 1) failed |= !mbar_wait_bounded(&bars[B_K_FREE], (j - 1) & 1);
         if constexpr (FMT == FMT_INT4) {
-          const uint32_t zp = kw & 0xFu;
-          const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
 #pragma unroll 4
           for (int i = 0; i < 32; ++i) {
             const int W = (i + kr) & 31;  // rotated order: conflict-free shared loads across the warp
             const uint32_t x = *reinterpret_cast<const uint32_t*>(cell + 4 * W);
             const uint32_t x8 = x >> 8;
             uint4 v;
-            v.x = hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b);    // channels 0, 4
-            v.y = hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b);  // 1, 5
-            v.z = hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b);   // 2, 6
-            v.w = hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b);  // 3, 7
+            v.x = hmul2_u32(hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b), q2);  // channels 0, 4
+            v.y = hmul2_u32(hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);  // 1, 5
+            v.z = hmul2_u32(hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b), q2);  // 2, 6
+            v.w = hmul2_u32(hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);  // 3, 7
             *reinterpret_cast<uint4*>(kop + (W >> 3) * 8192 + sw128_off(kr, W & 7)) = v;
           }
         } else {
@@ -546,11 +578,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
             const int C8 = (i + kr) & 31;  // 8 channels 8 C8 .. 8 C8 + 7 (two words)
             const uint2 x2 = *reinterpret_cast<const uint2*>(cell + 8 * C8);
             const uint32_t a = x2.x ^ 0x80808080u, c = x2.y ^ 0x80808080u;
-            uint4 v;
-            v.x = hsub2_u32(prmt(a, 0x64646464u, 0x4140u), 0x64806480u);  // {c0, c1} = (1152 + c) - 1152
-            v.y = hsub2_u32(prmt(a, 0x64646464u, 0x4342u), 0x64806480u);
-            v.z = hsub2_u32(prmt(c, 0x64646464u, 0x4140u), 0x64806480u);
-            v.w = hsub2_u32(prmt(c, 0x64646464u, 0x4342u), 0x64806480u);
+            uint4 v;  // (1152 + code) - 1152 = code, exact; then the scale
+            v.x = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4140u), 0x64806480u), q2);
+            v.y = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4342u), 0x64806480u), q2);
+            v.z = hmul2_u32(hsub2_u32(prmt(c, 0x64646464u, 0x4140u), 0x64806480u), q2);
+            v.w = hmul2_u32(hsub2_u32(prmt(c, 0x64646464u, 0x4342u), 0x64806480u), q2);
             *reinterpret_cast<uint4*>(kop + (C8 >> 3) * 8192 + sw128_off(kr, C8 & 7)) = v;
           }
         }
@@ -558,21 +590,17 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[B_K_FULL]);
       } else {
-        const uint32_t vw = *reinterpret_cast<const uint32_t*>(cell + C::KB + 4 + PF_HS / 2);
-        sc[b * 128 + 64 + kr] = tok < p.n ? __uint_as_float(vw & 0xFFFFFFF0u) : 0.f;
         if (j >= 1) failed |= !mbar_wait_bounded(&bars[B_V_FREE], (j - 1) & 1);
-        const uint32_t zp = vw & 0xFu;
-        const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
 #pragma unroll 4
         for (int i = 0; i < 32; ++i) {
           const int W = (i + kr) & 31;
           const uint32_t x = *reinterpret_cast<const uint32_t*>(cell + C::KB + 4 + 4 * W);
           const uint32_t x8 = x >> 8;
           uint4 v;
-          v.x = hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b);
-          v.y = hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b);
-          v.z = hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b);
-          v.w = hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b);
+          v.x = hmul2_u32(hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b), q2);
+          v.y = hmul2_u32(hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
+          v.z = hmul2_u32(hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b), q2);
+          v.w = hmul2_u32(hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
           *reinterpret_cast<uint4*>(vop + (W >> 3) * 8192 + sw128_off(kr, W & 7)) = v;
         }
         fence_async_smem();
@@ -592,9 +620,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     uint8_t* p_tile = smem + C::OFF_P;
     int64_t j = 0;
-    int qcount = 0, pieces = 0;
-    float m_used = -INFINITY, l = 0.f, qsc = 0.f, pv_mul = 0.f, v_limit = 0.f;
-    int e_run = -1000, lim = -1, tok = 0, qh = 0;
+    int qcount = 0;
+    float m_used = -INFINITY, l = 0.f, qsc = 0.f;
+    int e_used = -1000, lim = -1, tok = 0, qh = 0;
     bool row_ok = false;
     int64_t t_in_piece = 0;
     for (; !sch.done() && !failed; sch.next(), ++j) {
@@ -613,9 +641,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       if (w.first_of_piece) {
         m_used = -INFINITY;
         l = 0.f;
-        e_run = -1000;
-        pv_mul = 0.f;
-        v_limit = 0.f;
+        e_used = -1000;
         t_in_piece = 0;
       }
       // scores of this row for the tile's 64 keys
@@ -627,35 +653,29 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_S_FREE + b]);
       failed |= !mbar_wait_bounded(&bars[B_SC_FULL + b], (j >> 1) & 1);
-      const float* ks = sc + b * 128;
-      const float* vs = ks + 64;
+      const float* scb = reinterpret_cast<const float*>(smem + C::OFF_SC) + b * 4;
+      const float qs_t = qsc * scb[0];               // x 2^F of the key operand
+      const int ev = __float_as_int(scb[1]);         // value exponent of this tile's operand
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[B_SC_FREE + b]);
       const int key0 = w.kt * PF_BN;
       const bool masked = key0 + PF_BN - 1 > p.n - p.qlen;  // some row of the chunk cannot see some key here
+      if (masked) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (key0 + c > lim) s[c] = -INFINITY;
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        float y = s[c] * ks[c];
-        if (masked && key0 + c > lim) y = -INFINITY;
-        s[c] = y;
-        mx = fmaxf(mx, y);
-      }
-      float vmax = 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) vmax = fmaxf(vmax, vs[c]);
-      const float mrow = mx * qsc;
+      for (int c = 0; c < 64; ++c) mx = fmaxf(mx, s[c]);
+      const float mrow = mx * qs_t;
       const bool grow = mrow > m_used + PF_SLACK;
-      const bool vgrow = vmax >= v_limit;  // the same for every thread
+      const bool vgrow = ev > e_used;  // the same for every thread
       if (__any_sync(0xffffffffu, grow) || vgrow) {
         // rescale this row's O in TMEM (after the previous PV of the piece completed)
         const float m_new = grow ? mrow : m_used;
-        int e_new = e_run;
-        if (vgrow) {
-          int e_tile = -1000;
-          if (vmax > 0.f) frexpf(vmax, &e_tile);
-          e_new = max(e_run, e_tile);
-        }
         const float alpha = m_new == m_used ? 1.f : exp2f(m_used - m_new);
-        const float o_range = e_run == -1000 ? 0.f : ldexpf(1.f, e_run - e_new);
+        const float o_range = e_used == -1000 ? 0.f : ldexpf(1.f, e_used - ev);
         const float ao = alpha * o_range;
         if (t_in_piece > 0) {
           failed |= !mbar_wait_bounded(&bars[B_O_DONE], (j - 1) & 1);
@@ -671,25 +691,32 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         }
         l *= alpha;
         m_used = m_new;
-        e_run = e_new;
-        pv_mul = e_new == -1000 ? 0.f : ldexpf(1.f, -e_new);
-        v_limit = e_new == -1000 ? 0.f : ldexpf(1.f, e_new);
+        e_used = ev;
       }
-      // P = 2^(s qsc - m), P_v = P v_scale 2^-e_run in fp16, K-major row of the PV A operand
+      // P = 2^(s qs_t - m) <= 2^8 in fp16, K-major row of the PV A operand
       const float base = m_used == -INFINITY ? 0.f : m_used;
       float lsum = 0.f;
       uint32_t pw[32];
+      if (masked) {
 #pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        const float p0 = exp2f(fmaf(s[c], qsc, -base));
-        const float p1 = exp2f(fmaf(s[c + 1], qsc, -base));
-        lsum += p0 + p1;
-        const __half2 h = __floats2half2_rn(p0 * vs[c] * pv_mul, p1 * vs[c + 1] * pv_mul);
-        pw[c >> 1] = *reinterpret_cast<const uint32_t*>(&h);
+        for (int c = 0; c < 64; c += 2) {
+          const float p0 = s[c] == -INFINITY ? 0.f : fast_exp2(fmaf(s[c], qs_t, -base));
+          const float p1 = s[c + 1] == -INFINITY ? 0.f : fast_exp2(fmaf(s[c + 1], qs_t, -base));
+          lsum += p0 + p1;
+          const __half2 h = __floats2half2_rn(p0, p1);
+          pw[c >> 1] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) {
+          const float p0 = fast_exp2(fmaf(s[c], qs_t, -base));
+          const float p1 = fast_exp2(fmaf(s[c + 1], qs_t, -base));
+          lsum += p0 + p1;
+          const __half2 h = __floats2half2_rn(p0, p1);
+          pw[c >> 1] = *reinterpret_cast<const uint32_t*>(&h);
+        }
       }
       l += lsum;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[B_SC_FREE + b]);
       if (j >= 2) failed |= !mbar_wait_bounded(&bars[B_P_FREE + b], ((j >> 1) - 1) & 1);
       uint8_t* prow = p_tile + b * 16384;
 #pragma unroll
@@ -706,7 +733,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         // epilogue: O of this piece -> normalised fp32 partial (channel order restored) + base-2 lse
         failed |= !mbar_wait_bounded(&bars[B_O_DONE], j & 1);
         tc_fence_after();
-        const float o_unit = e_run == -1000 ? 0.f : ldexpf(1.f, e_run);
+        const float o_unit = e_used == -1000 ? 0.f : ldexpf(1.f, e_used);
         const float inv = l > 0.f ? o_unit / l : 0.f;
         const int64_t prow_i = (static_cast<int64_t>(tok) * p.nq + qh) * p.parts + w.piece;
 #pragma unroll 1
@@ -727,10 +754,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[B_O_FREE]);
-        ++pieces;
       }
     }
-    (void)pieces;
   }
 
   if (failed) atomicCAS(&g_device_error, DEV_ERR_NONE, DEV_ERR_WAIT_TIMEOUT);
