@@ -562,7 +562,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         if constexpr (FMT == FMT_INT4) {
 #pragma unroll 4
           for (int i = 0; i < 32; ++i) {
-            const int W = (i + kr) & 31;  // rotated order: conflict-free shared loads across the warp
+            const int W = (i + (kr >> 4)) & 31;  // odd word for lanes 16..31: conflict-free loads and stores
             const uint32_t x = *reinterpret_cast<const uint32_t*>(cell + 4 * W);
             const uint32_t x8 = x >> 8;
             uint4 v;
@@ -575,7 +575,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         } else {
 #pragma unroll 4
           for (int i = 0; i < 32; ++i) {
-            const int C8 = (i + kr) & 31;  // 8 channels 8 C8 .. 8 C8 + 7 (two words)
+            const int C8 = i;  // 8 channels 8 C8 .. 8 C8 + 7 (two words); 392-byte cells: no bank conflict
             const uint2 x2 = *reinterpret_cast<const uint2*>(cell + 8 * C8);
             const uint32_t a = x2.x ^ 0x80808080u, c = x2.y ^ 0x80808080u;
             uint4 v;  // (1152 + code) - 1152 = code, exact; then the scale
@@ -593,7 +593,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         if (j >= 1) failed |= !mbar_wait_bounded(&bars[B_V_FREE], (j - 1) & 1);
 #pragma unroll 4
         for (int i = 0; i < 32; ++i) {
-          const int W = (i + kr) & 31;
+          const int W = (i + (kr >> 4)) & 31;
           const uint32_t x = *reinterpret_cast<const uint32_t*>(cell + C::KB + 4 + 4 * W);
           const uint32_t x8 = x >> 8;
           uint4 v;
