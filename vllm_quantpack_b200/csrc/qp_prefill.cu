@@ -556,6 +556,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         else
           scb[1] = __int_as_float(ex);
       }
+      // the softmax needs only these factors: release them now, not after the (longer) operand conversion
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[B_SC_FULL + b]);
       const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
       if (is_k) {
         if (j >= 1) failed |= !mbar_wait_bounded(&bars[B_K_FREE], (j - 1) & 1);
@@ -608,10 +611,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         if (lane == 0) mbar_arrive(&bars[B_V_FULL]);
       }
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bars[B_SC_FULL + b]);
-        mbar_arrive(&bars[B_RAW_EMPTY + stage]);
-      }
+      if (lane == 0) mbar_arrive(&bars[B_RAW_EMPTY + stage]);
     }
   } else {
     // ------------------------------------------------------------------ softmax / epilogue (warps 6..9)
