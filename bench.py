@@ -369,23 +369,26 @@ def run_b200(args, w, rank, world, local_rank):
 
 
 def run_seq_parallel(args, torch, dist, ops, w, device, rank, world, flush):
-    """One request of the workload split by sequence range over the ranks: each rank holds ctx / world cached tokens,
-    computes its partial (O fp32 in the RHT domain, base-2 LSE) for all query tokens, the partials are all-gathered
-    over NCCL and every rank folds them (the same fold as the split-KV merge)."""
+    """One request of the workload split by sequence range over the ranks: rank r holds cached tokens
+    [r * ctx / N, (r + 1) * ctx / N), computes its partial (O fp32 in the RHT domain, base-2 LSE) for all query
+    tokens (causal mask shifted by the tokens held after its range), the partials are all-gathered over NCCL and
+    every rank folds them (the same fold as the split-KV merge)."""
     from vllm_quantpack_b200.attention import seq_parallel as sp
+    lo, hi, after = sp.sequence_range(w["ctx"], rank, world)
     part = dict(w)
-    part["ctx"] = w["ctx"] // world
+    part["ctx"] = hi - lo
     R = build_request(torch, ops, part, device, 1, seed=100 + rank)
+    dist.broadcast(R["q"], 0)  # one request: every rank holds the same query tokens
     kc, vc, ks, vs = R["views"]
-    runner = sp.SequenceParallelDecode(dist.group.WORLD, rank, world, R["q"].shape[0], NQ, HS, device)
+    runner = sp.SequenceParallelAttention(dist.group.WORLD, R["q"].shape[0], NQ, HS, device)
     out = torch.empty_like(R["q"])
     nsplit = ops.decode_num_splits(1, NKV, part["ctx"], ops.sm_count(device))
     call = dict(cu_seqlens_q=R["cu"], max_seqlen_q=w["qlen"], seqused_k=R["used"], max_seqlen_k=part["ctx"],
                 softmax_scale=HS ** -0.5, block_table=R["table"], k_scale_cache=ks, v_scale_cache=vs,
-                num_splits=nsplit, total_context=w["ctx"])
+                num_splits=nsplit, tokens_after_keys=after)
 
     def step():
-        runner(R["q"], kc, vc, out, **call)
+        runner.decode(R["q"], kc, vc, out, **call)
 
     dist.barrier()
     t = timed_steps(torch, step, args.steps, args.warmup, flush)

@@ -93,6 +93,9 @@ int64_t qp_decode_workspace_bytes(int64_t num_q_tokens, int num_q_heads, int hea
  * block_table[b]. q (tokens, num_q_heads, head_size) in dtype; out likewise. max_seqlen_q * (num_q_heads /
  * num_kv_heads) <= 32. The RHT is applied to q (unless q_rotated) and inverted on the output, which is divided by
  * head_size; scores use softmax_scale / head_size (vllm_quantpack/attention/int4_kv.py:326-329).
+ * tokens_after_keys: tokens of every sequence that follow its seqused_k cached keys here (a sequence-parallel rank
+ * holding an earlier range of the sequence): query token i then sees key k iff k <= seqused_k - qlen + i +
+ * tokens_after_keys; 0 for an ordinary call, >= qlen - 1 lifts the causal mask.
  * out_mode 0: out in dtype, model domain. out_mode 1: out fp32 in the RHT domain and lse_out (tokens, num_q_heads)
  * the base-2 log-sum-exp of the scaled scores (the partial a sequence-parallel rank exchanges). out_mode 2: the
  * split partials only, left in the workspace as part_o (tokens, num_q_heads, num_splits, head_size) fp32 followed by
@@ -107,17 +110,20 @@ int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stride_token, i
                     const int32_t* block_table, int64_t block_table_stride, const void* cache, int block_size,
                     int64_t block_stride, int64_t head_stride, int64_t slot_stride, int64_t k_off, int64_t ks_off,
                     int64_t v_off, int64_t vs_off, int num_q_heads, int num_kv_heads, int head_size,
-                    float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated, int out_mode, float* lse_out,
-                    int num_splits, void* workspace, int64_t workspace_bytes, void* stream);
+                    float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated, int tokens_after_keys,
+                    int out_mode, float* lse_out, int num_splits, void* workspace, int64_t workspace_bytes,
+                    void* stream);
 
 /* Bytes of workspace qp_prefill needs for a chunk of qlen queries over a context of n tokens (prepared query tiles
  * and per-piece partials). */
-int64_t qp_prefill_workspace_bytes(int qlen, int n, int num_q_heads, int num_kv_heads, int head_size);
+int64_t qp_prefill_workspace_bytes(int qlen, int n, int num_q_heads, int num_kv_heads, int head_size,
+                                   int tokens_after_keys);
 
 /* Long-chunk prefill of one sequence: the qlen queries q (the last qlen positions of a context of n tokens, causal
  * among themselves) attend to the whole cached context through block_row (that sequence's block-table row), on the
  * tcgen05 tensor cores with every key / value tile dequantised in shared memory (no scratch unpack of the cache).
- * out_mode / lse_out / q_rotated as in qp_paged_decode; head_size 256; HND cells, block_size % 16 == 0.
+ * out_mode / lse_out / q_rotated / tokens_after_keys as in qp_paged_decode (n >= qlen - tokens_after_keys);
+ * head_size 256; HND cells, block_size % 16 == 0.
  * Replaces vllm_quantpack/attention/int4_prefill.py:203-232 `prefill_sequence` (16k-token bf16 unpacks +
  * FlashAttention 2 + log-sum-exp fold) and the Triton 2D path of int4_kv.py:113-119, reached through
  * `unified_attention_int4` (int4_kv.py:308-329). */
@@ -125,8 +131,9 @@ int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_
                int64_t out_stride_token, int64_t out_stride_head, int qlen, int n, const int32_t* block_row,
                const void* cache, int block_size, int64_t block_stride, int64_t head_stride, int64_t slot_stride,
                int64_t k_off, int64_t ks_off, int64_t v_off, int64_t vs_off, int num_q_heads, int num_kv_heads,
-               int head_size, float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated, int out_mode,
-               float* lse_out, void* workspace, int64_t workspace_bytes, void* stream);
+               int head_size, float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated,
+               int tokens_after_keys, int out_mode, float* lse_out, void* workspace, int64_t workspace_bytes,
+               void* stream);
 
 /* Bytes of the library's static decode scratch used by qp_paged_decode_static. */
 #define QP_STATIC_DECODE_SCRATCH_BYTES (32ll << 20)

@@ -1,0 +1,342 @@
+"""The plugin boundary on the CPU: registration, environment switches, the segment table, the k8v4 page cell and
+views, and the routing of `unified_attention_int4` (decode batch / prefill chunks / stock fallback) with the
+kernels replaced by recorders. Mirrors the reference's CPU tests (tests/test_int4_kv.py:1-87,
+tests/test_k8v4_kv.py:16-53); the kernels themselves are checked on a GPU in test_*_gpu.py."""
+import logging
+import sys
+import tomllib
+import types
+
+import pytest
+import torch
+
+import vllm_quantpack_b200
+from vllm_quantpack_b200.attention import int4_kv, int4_prefill, k8v4_kv, ops
+
+LOG = logging.getLogger("test")
+NQ, NKV, HS = 24, 4, 256
+
+
+# ---------------------------------------------------------------- registration and switches
+def test_entry_point_names_register():
+    with open(__file__.rsplit("/tests/", 1)[0] + "/pyproject.toml", "rb") as fh:
+        eps = tomllib.load(fh)["project"]["entry-points"]["vllm.general_plugins"]
+    assert eps == {"quantpack_b200": "vllm_quantpack_b200:register"}
+    assert callable(vllm_quantpack_b200.register)
+
+
+def test_register_can_be_disabled(monkeypatch):
+    monkeypatch.setenv("VLLM_QUANTPACK_B200", "0")
+    assert vllm_quantpack_b200.register() is False
+
+
+def test_disabled_by_environment(monkeypatch):
+    monkeypatch.setenv("VLLM_QUANTPACK_INT4_KV", "0")
+    assert int4_kv.patch_int4_kv(LOG) is False
+
+
+def test_vllm_without_int4_mode_leaves_everything(monkeypatch):
+    monkeypatch.setattr(int4_kv, "MODULE", "vllm_quantpack_b200_no_such_module")
+    assert int4_kv.patch_int4_kv(LOG) is False
+
+
+def _fake_stock(monkeypatch):
+    """A stand-in for vllm.v1.attention.ops.int4_per_token_head with recording stock functions."""
+    mod = types.ModuleType("qp_fake_int4_module")
+    mod.calls = []
+    mod.unified_attention_int4 = lambda *a, **k: mod.calls.append(("unified", a, k))
+    mod.reshape_and_cache_int4 = lambda *a, **k: mod.calls.append(("store", a, k))
+    mod.single_rht = lambda x, inverse=False: x
+    mod._launch_packed_attn = lambda **k: mod.calls.append(("launch", k))
+    monkeypatch.setitem(sys.modules, mod.__name__, mod)
+    monkeypatch.setattr(int4_kv, "MODULE", mod.__name__)
+    return mod
+
+
+def test_no_b200_library_or_gpu_leaves_stock(monkeypatch):
+    mod = _fake_stock(monkeypatch)
+    before = (mod.unified_attention_int4, mod.reshape_and_cache_int4, mod.single_rht, mod._launch_packed_attn)
+
+    def not_ready():
+        raise RuntimeError("no CUDA device")
+
+    monkeypatch.setattr(int4_kv, "_b200_ready", not_ready)
+    assert int4_kv.patch_int4_kv(LOG) is False
+    assert (mod.unified_attention_int4, mod.reshape_and_cache_int4, mod.single_rht, mod._launch_packed_attn) == before
+
+
+def test_patch_installs_marked_ops_once(monkeypatch):
+    mod = _fake_stock(monkeypatch)
+    launch = mod._launch_packed_attn
+    monkeypatch.setattr(int4_kv, "_b200_ready", lambda: 148)
+    assert int4_kv.patch_int4_kv(LOG) is True
+    for fn in (mod.unified_attention_int4, mod.reshape_and_cache_int4, mod.single_rht):
+        assert fn._quantpack and fn._quantpack_b200
+    assert mod._launch_packed_attn is launch   # only the stock path reaches the stock launcher
+    installed = mod.unified_attention_int4
+    assert int4_kv.patch_int4_kv(LOG) is True and mod.unified_attention_int4 is installed
+
+
+# ---------------------------------------------------------------- segment buffers and tiles
+def _fake_triton_attn(monkeypatch):
+    """A stand-in for vllm.v1.attention.backends.triton_attn whose builder records the segment count it saw."""
+    mod = types.ModuleType("vllm.v1.attention.backends.triton_attn")
+    mod.NUM_PAR_SOFTMAX_SEGMENTS = 16
+
+    class Builder:
+        def __init__(self, kv_cache_spec, layer_names, vllm_config, device):
+            self.num_par_softmax_segments = mod.NUM_PAR_SOFTMAX_SEGMENTS
+
+    mod.TritonAttentionMetadataBuilder = Builder
+    for name in ("vllm", "vllm.v1", "vllm.v1.attention", "vllm.v1.attention.backends"):
+        monkeypatch.setitem(sys.modules, name, sys.modules.get(name) or types.ModuleType(name))
+    monkeypatch.setitem(sys.modules, mod.__name__, mod)
+    monkeypatch.setattr(sys.modules["vllm.v1.attention.backends"], "triton_attn", mod, raising=False)
+    return mod
+
+
+def _config(dtype):
+    return types.SimpleNamespace(cache_config=types.SimpleNamespace(cache_dtype=dtype))
+
+
+def test_decode_segments_only_for_packed_caches(monkeypatch):
+    mod = _fake_triton_attn(monkeypatch)
+    assert int4_kv._patch_decode_segments(64, LOG) == 64
+    B = mod.TritonAttentionMetadataBuilder
+    assert B(None, [], _config("int4_per_token_head"), None).num_par_softmax_segments == 64
+    assert B(None, [], _config("k8v4_per_token_head"), None).num_par_softmax_segments == 64
+    assert B(None, [], _config("auto"), None).num_par_softmax_segments == 16
+    assert mod.NUM_PAR_SOFTMAX_SEGMENTS == 16
+
+
+def test_decode_segments_not_power_of_two_left_stock(monkeypatch):
+    mod = _fake_triton_attn(monkeypatch)
+    assert int4_kv._patch_decode_segments(48, LOG) == 0
+    assert mod.TritonAttentionMetadataBuilder(None, [], _config("int4_per_token_head"),
+                                              None).num_par_softmax_segments == 16
+
+
+def test_decode_override_from_environment(monkeypatch):
+    monkeypatch.setenv("VLLM_QUANTPACK_INT4_DECODE", "32,8,32")
+    assert int4_kv.decode_tiles(188) == (32, 8, 32)
+    assert int4_kv.decode_splits_override() == 32
+    monkeypatch.setenv("VLLM_QUANTPACK_INT4_DECODE", "64,4,auto")
+    assert int4_kv.decode_tiles(84) == (64, 4, 32)
+    assert int4_kv.decode_splits_override() is None
+
+
+def test_decode_override_accepts_query_row_cap(monkeypatch):
+    monkeypatch.setenv("VLLM_QUANTPACK_INT4_DECODE", "64,4,auto,16")
+    assert int4_kv.decode_tiles(188) == (64, 4, 64, 16)
+    monkeypatch.setenv("VLLM_QUANTPACK_INT4_DECODE", "64,4,32,32")
+    assert int4_kv.decode_tiles(84) == (64, 4, 32, 32)
+
+
+@pytest.mark.parametrize("sms,segments", [(188, 64), (84, 32), (36, 16), (8, 16), (132, 64), (512, 128),
+                                          (148, 64)],
+                         ids=["rtx-pro-6000", "a40", "rtx-5060-ti", "tiny", "h100", "cap", "b200"])
+def test_segments_follow_sm_count(monkeypatch, sms, segments):
+    monkeypatch.delenv("VLLM_QUANTPACK_INT4_DECODE", raising=False)
+    assert int4_kv.decode_tiles(sms) == (64, 4, segments)
+
+
+def test_prefill_tiles_override_is_read(monkeypatch):
+    monkeypatch.setenv("VLLM_QUANTPACK_INT4_TILES", "64,64,8,2")
+    assert int4_kv.prefill_tiles(10) == (64, 64, 8, 2)
+    monkeypatch.delenv("VLLM_QUANTPACK_INT4_TILES")
+    assert int4_kv.prefill_tiles(10) == int4_kv.PREFILL_TILES_DEFAULT
+
+
+def test_prefill_thresholds_match_the_plugin():
+    assert (int4_prefill.MAX_HEAD, int4_prefill.SEGMENT, int4_prefill.MIN_QUERY, int4_prefill.MIN_CONTEXT) == \
+        (256, 16384, 64, 8192)
+
+
+def test_decode_workspace_bound_covers_every_batch(monkeypatch):
+    monkeypatch.delenv("VLLM_QUANTPACK_INT4_DECODE", raising=False)
+    from vllm_quantpack_b200 import _lib
+    lib = _lib.load()
+    bound = int4_kv.decode_workspace_bound(64, NQ, NKV, 262144, 148)
+    for seqs in (1, 2, 5, 16, 64):
+        tokens = min(64, 4 * seqs)
+        need = lib.qp_decode_workspace_bytes(tokens, NQ, HS, lib.qp_decode_num_splits(seqs, NKV, 262144, 148))
+        assert need <= bound
+    assert bound < 64 << 20   # a few tens of MB, not the 1024-split worst case
+
+
+# ---------------------------------------------------------------- k8v4 page cell and views
+def test_cell_is_key_bytes_plus_packed_value_plus_two_scales():
+    assert k8v4_kv.cell_bytes(256, 256) == 392
+    assert k8v4_kv.cell_bytes(128, 64) == 168
+
+
+@pytest.mark.parametrize("layout", ["hnd", "nhd"])
+def test_views_cover_the_cell_without_overlap(layout):
+    nb, nkv, bs, hs = 3, 2, 4, 16
+    cell = k8v4_kv.cell_bytes(hs, hs)
+    if layout == "hnd":
+        kv = torch.zeros((nb, nkv, bs, cell), dtype=torch.int8)
+    else:
+        kv = torch.zeros((nb, bs, nkv, cell), dtype=torch.int8).transpose(1, 2)
+    key, value, ks, vs = k8v4_kv.views(kv, hs)
+    assert key.shape == (nb, bs, nkv, hs) and key.dtype == torch.int8
+    assert value.shape == (nb, bs, nkv, hs // 2) and value.dtype == torch.uint8
+    assert ks.shape == vs.shape == (nb, bs, nkv) and ks.dtype == torch.float32
+    key.fill_(1)
+    ks.view(torch.int32).fill_(0x02020202)
+    value.fill_(3)
+    vs.view(torch.int32).fill_(0x04040404)
+    want = torch.tensor([1] * hs + [2] * 4 + [3] * (hs // 2) + [4] * 4, dtype=torch.int8)
+    assert (kv == want).all()
+    ks[1, 2, 1] = 7.0
+    assert kv[1, 1, 2, hs:hs + 4].view(torch.float32).item() == 7.0
+
+
+def test_views_reject_another_cell_size():
+    with pytest.raises(ValueError, match="expected 392"):
+        k8v4_kv.views(torch.zeros((1, 4, 16, 264), dtype=torch.int8), 256)
+
+
+def test_int4_cache_views_are_not_taken_for_k8v4():
+    assert not k8v4_kv.is_k8v4(torch.zeros(1, dtype=torch.uint8))
+    assert k8v4_kv.is_k8v4(torch.zeros(1, dtype=torch.int8))
+
+
+def test_cache_layout_from_views_matches_cells():
+    kv = torch.zeros((5, NKV, 16, k8v4_kv.cell_bytes(HS, HS)), dtype=torch.int8)
+    lay = ops.CacheLayout(*k8v4_kv.views(kv, HS), HS)
+    assert (lay.fmt, lay.cell, lay.ks_off, lay.v_off, lay.vs_off, lay.hnd) == (ops.FMT_K8V4, 392, 256, 260, 388, True)
+    phs = HS // 2 + 4
+    kv4 = torch.zeros((5, NKV, 16, 2 * phs), dtype=torch.uint8)
+    base = torch.tensor([], dtype=torch.float32).set_(kv4.untyped_storage())
+    st = [s // 4 for s in kv4.stride()]
+    ks = torch.as_strided(base, (5, 16, NKV), (st[0], st[2], st[1]), HS // 2 // 4)
+    vs = torch.as_strided(base, (5, 16, NKV), (st[0], st[2], st[1]), (phs + HS // 2) // 4)
+    kc, vc = kv4.transpose(1, 2).split(phs, dim=-1)
+    lay = ops.CacheLayout(kc, vc, ks, vs, HS)
+    assert (lay.fmt, lay.cell, lay.ks_off, lay.v_off, lay.vs_off) == (ops.FMT_INT4, 264, 128, 132, 260)
+    with pytest.raises(ValueError):
+        ops.CacheLayout(kc, vc, vs, ks, HS)      # scale views swapped: fields out of place
+
+
+# ---------------------------------------------------------------- routing of unified_attention_int4
+class Recorder:
+    """Replaces ops.paged_decode / ops.prefill: records each launch and writes the request index + 1 into out."""
+
+    def __init__(self, monkeypatch):
+        self.calls = []
+        monkeypatch.setattr(ops, "paged_decode", self.decode)
+        monkeypatch.setattr(ops, "prefill", self.prefill)
+
+    def decode(self, q, kc, vc, out, *, cu_seqlens_q, seqused_k, block_table, max_seqlen_q, num_splits, **kw):
+        self.calls.append(("decode", q.shape[0], cu_seqlens_q.tolist(), seqused_k.tolist(), max_seqlen_q,
+                           num_splits))
+        for b in range(len(seqused_k)):
+            out[cu_seqlens_q[b]:cu_seqlens_q[b + 1]] = float(block_table[b, 0])
+        return out
+
+    def prefill(self, q, kc, vc, out, *, block_row, n, **kw):
+        self.calls.append(("prefill", q.shape[0], n))
+        out[:] = float(block_row[0])
+        return out
+
+
+def _step(qlens, used, window=(-1, -1), dtype=torch.float32):
+    T = sum(qlens)
+    cu = torch.tensor([0] + list(torch.tensor(qlens).cumsum(0)), dtype=torch.int32)
+    q = torch.randn((T + 3, NQ, HS), dtype=dtype)   # 3 padding rows past cu[-1] stay untouched
+    out = torch.full_like(q, -7.0)
+    table = torch.tensor([[i + 1] + [0] * 3 for i in range(len(qlens))], dtype=torch.int32)
+    kc = torch.zeros((4, 16, NKV, HS // 2 + 4), dtype=torch.uint8)
+    args = dict(cu_seqlens_q=cu, max_seqlen_q=max(qlens), seqused_k=torch.tensor(used, dtype=torch.int32),
+                max_seqlen_k=max(used), softmax_scale=HS ** -0.5, window_size=window, block_table=table,
+                softcap=0.0, sinks=None, alibi_slopes=None, use_alibi_sqrt=False, qq_bias=None, output_scale=None,
+                mm_prefix_range=None, k_scale_cache=None, v_scale_cache=None, seq_threshold_3D=32,
+                num_par_softmax_segments=64, softmax_segm_output=None, softmax_segm_max=None,
+                softmax_segm_expsum=None)
+    return q, kc, out, args
+
+
+def _stock_recorder():
+    calls = []
+
+    def stock(q, k, v, out, **kw):
+        calls.append((q.shape[0], kw["cu_seqlens_q"].tolist(), kw["seqused_k"].tolist()))
+        out[:] = 99.0
+    return stock, calls
+
+
+def test_decode_step_is_one_launch_without_host_read(monkeypatch):
+    rec = Recorder(monkeypatch)
+    stock, stock_calls = _stock_recorder()
+    fn = int4_kv.make_unified_attention(stock)
+    monkeypatch.setattr(int4_kv, "_step_lengths", lambda *a: pytest.fail("decode steps must not read lengths"))
+    q, kc, out, args = _step([4, 3, 1, 0, 4], [20000, 9000, 16384, 5, 3072])
+    fn(q, kc, kc, out, **args)
+    assert rec.calls == [("decode", q.shape[0], [0, 4, 7, 8, 8, 12], [20000, 9000, 16384, 5, 3072], 4, None)]
+    assert not stock_calls
+    assert (out[:4] == 1).all() and (out[4:7] == 2).all() and (out[7] == 3).all() and (out[8:12] == 5).all()
+    assert (out[12:] == -7).all()
+
+
+def test_mixed_step_splits_decode_prefill(monkeypatch):
+    rec = Recorder(monkeypatch)
+    stock, stock_calls = _stock_recorder()
+    fn = int4_kv.make_unified_attention(stock)
+    q, kc, out, args = _step([256, 2, 4, 40], [40000, 20000, 100, 300])
+    fn(q, kc, kc, out, **args)
+    assert ("decode", 6, [0, 2, 6], [20000, 100], 4, None) in rec.calls
+    assert ("prefill", 256, 40000) in rec.calls and ("prefill", 40, 300) in rec.calls
+    assert len(rec.calls) == 3 and not stock_calls
+    assert (out[:256] == 1).all() and (out[256:258] == 2).all() and (out[258:262] == 3).all()
+    assert (out[262:302] == 4).all() and (out[302:] == -7).all()
+
+
+def test_unsupported_features_go_to_the_stock_path(monkeypatch):
+    rec = Recorder(monkeypatch)
+    stock, stock_calls = _stock_recorder()
+    fn = int4_kv.make_unified_attention(stock)
+    q, kc, out, args = _step([4], [5000], window=(4096, 0))
+    fn(q, kc, kc, out, **args)
+    assert not rec.calls and len(stock_calls) == 1
+    q, kc, out, args = _step([4], [5000])
+    fn(q, kc, kc, out, **dict(args, softcap=30.0))
+    assert not rec.calls and len(stock_calls) == 2
+
+
+def test_prefill_routing_off_sends_chunks_to_stock(monkeypatch):
+    rec = Recorder(monkeypatch)
+    stock, stock_calls = _stock_recorder()
+    fn = int4_kv.make_unified_attention(stock, prefill_on=False)
+    q, kc, out, args = _step([256, 2], [40000, 20000])
+    fn(q, kc, kc, out, **args)
+    assert rec.calls == [("decode", 2, [0, 2], [20000], 2, None)]
+    assert stock_calls == [(256, [0, 256], [40000])]
+    assert (out[:256] == 99).all() and (out[256:258] == 2).all()
+
+
+def test_decode_split_count_from_environment(monkeypatch):
+    monkeypatch.setenv("VLLM_QUANTPACK_INT4_DECODE", "64,4,32")
+    rec = Recorder(monkeypatch)
+    fn = int4_kv.make_unified_attention(_stock_recorder()[0])
+    q, kc, out, args = _step([2], [262144])
+    fn(q, kc, kc, out, **args)
+    assert rec.calls[0][-1] == 32
+
+
+def test_store_dispatch(monkeypatch):
+    calls = []
+    monkeypatch.setattr(ops, "reshape_and_cache_int4", lambda *a, **k: calls.append("b200"))
+    stock_calls = []
+    store = int4_kv.make_reshape_and_cache(lambda *a, **k: stock_calls.append("stock"))
+    k = torch.zeros((3, NKV, HS))
+    kc8 = torch.zeros((2, 16, NKV, HS), dtype=torch.int8)
+    kc4 = torch.zeros((2, 16, NKV, HS // 2), dtype=torch.uint8)
+    store(k, k, kc4, kc4, torch.zeros(3, dtype=torch.int64), k_scale_cache=None, v_scale_cache=None)
+    store(k, k, kc8, kc8, torch.zeros(3, dtype=torch.int64), k_scale_cache=None, v_scale_cache=None)
+    assert calls == ["b200", "b200"] and not stock_calls
+    k96 = torch.zeros((3, NKV, 96))
+    store(k96, k96, kc4, kc4, torch.zeros(3, dtype=torch.int64), k_scale_cache=None, v_scale_cache=None)
+    assert stock_calls == ["stock"]
+    with pytest.raises(ValueError, match="k8v4"):
+        store(k96, k96, kc8, kc8, torch.zeros(3, dtype=torch.int64), k_scale_cache=None, v_scale_cache=None)

@@ -1,0 +1,328 @@
+"""int4_per_token_head / k8v4_per_token_head attention on vLLM's Triton backend, served by B200 kernels.
+
+The drop-in counterpart of the plugin module vllm_quantpack/attention/int4_kv.py. The reference generates a patched
+copy of vLLM's Triton kernel and launcher; this module instead replaces the stock module's entry points
+(`vllm.v1.attention.ops.int4_per_token_head`) with thin launches of libquantpack_b200.so:
+
+  unified_attention_int4   decode steps (<= MAX_Q_SPLIT_KV query tokens per request, graph-capturable, no host
+                           sync) -> split-KV decode kernel + merge; steps with prefill chunks -> one host read of the
+                           step's lengths, decode rows as a sub-batch, every other request -> the tcgen05 prefill
+                           kernel (int4_kv.py:281-333 routes only long chunks to FlashAttention)
+  reshape_and_cache_int4   fused RHT + quantize + pack store, int4 and k8v4 (k8v4_kv.py:152-163)
+  single_rht               the transform both of the above apply, so any stock path left in use stays consistent
+
+Calls the B200 path does not cover (sliding window, softcap, sinks, ALiBi, qq_bias, FP8 output, mm_prefix ranges, a
+head size other than 256) go to the stock `unified_attention_int4`, unchanged. The stock `_launch_packed_attn` is
+left in place: only that stock path reaches it. The same environment switches are honoured:
+VLLM_QUANTPACK_INT4_KV=0 (no patch), VLLM_QUANTPACK_INT4_FA_PREFILL=0 (prefill chunks stay stock),
+VLLM_QUANTPACK_INT4_DECODE="tile,warps,segments[,rows]" (segments: split count of the decode, "auto" = per call),
+VLLM_QUANTPACK_INT4_TILES (accepted; the B200 prefill tiles are fixed at 128 x 64).
+"""
+import importlib
+import itertools
+import os
+
+MODULE = "vllm.v1.attention.ops.int4_per_token_head"
+PACKED_DTYPES = ("int4_per_token_head", "k8v4_per_token_head")   # caches served by the B200 kernels
+MAX_Q_SPLIT_KV = 4               # MTP / EAGLE verification with up to 3 draft tokens
+MAX_DECODE_ROWS = 32             # query tokens x query heads per KV head one decode CTA holds
+HEAD_SIZE = 256                  # the attention kernels' head size
+PREFILL_TILES_DEFAULT = (128, 64, 10, 1)   # (BLOCK_M, TILE, warps, CTAs per SM) of the tcgen05 prefill kernel
+DECODE_TILES_DEFAULT = (64, 4, "auto")
+DECODE_MAX_M = 32
+MIN_SEGMENTS, MAX_SEGMENTS = 16, 128
+
+
+def prefill_tiles(major):
+    """The prefill tiling, for the reference's VLLM_QUANTPACK_INT4_TILES override (int4_kv.py:67-71). The B200
+    kernel's tiles are fixed; an override is reported and not applied."""
+    env = os.environ.get("VLLM_QUANTPACK_INT4_TILES")
+    if env:
+        return tuple(int(x) for x in env.split(","))
+    return PREFILL_TILES_DEFAULT
+
+
+def segments_for(sms):
+    """Split-KV segments per sequence vLLM's metadata builder sizes its buffers for (int4_kv.py:74-77): next power
+    of two of SMs / 4, between 16 and 128."""
+    n = 1 << max(0, -(-sms // 4) - 1).bit_length()
+    return min(MAX_SEGMENTS, max(MIN_SEGMENTS, n))
+
+
+def decode_tiles(sms):
+    """(tile, warps, segments[, rows]) of the split-KV decode (int4_kv.py:80-85 semantics). The B200 decode kernel
+    runs 64-token tiles with 4 warps whatever the tuple says; an integer segment count fixes its split count,
+    "auto" lets `qp_decode_num_splits` choose per call (reported here as segments_for(sms))."""
+    env = os.environ.get("VLLM_QUANTPACK_INT4_DECODE")
+    tile, warps, segments, *max_m = env.split(",") if env else DECODE_TILES_DEFAULT
+    segments = segments_for(sms) if str(segments).strip() == "auto" else int(segments)
+    return (int(tile), int(warps), segments) + tuple(int(m) for m in max_m[:1])
+
+
+def decode_splits_override():
+    """The decode split count fixed by VLLM_QUANTPACK_INT4_DECODE, or None for the per-call choice."""
+    env = os.environ.get("VLLM_QUANTPACK_INT4_DECODE")
+    if not env:
+        return None
+    parts = env.split(",")
+    if len(parts) < 3 or parts[2].strip() == "auto":
+        return None
+    return int(parts[2])
+
+
+def _plain(q, window_size, softcap, sinks, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
+    """True when the call uses no feature outside the B200 kernels (int4_kv.py:304-305)."""
+    return (window_size is None or window_size[0] < 0) and not softcap and sinks is None and alibi_slopes is None \
+        and qq_bias is None and output_scale is None and mm_prefix_range is None and q.shape[2] == HEAD_SIZE
+
+
+def _step_lengths(cu_seqlens_q, seqused_k):
+    """cu_seqlens_q and seqused_k as host lists, copied once per forward step: every attention layer of a step gets
+    the same tensors, so the lists are kept on the step's forward context keyed by the tensors themselves
+    (int4_kv.py:260-278)."""
+    try:
+        from vllm.forward_context import get_forward_context, is_forward_context_available
+        step = get_forward_context() if is_forward_context_available() else None
+    except Exception:
+        step = None
+    hit = getattr(step, "_quantpack_int4_lengths", None)
+    if hit is not None and hit[0] is cu_seqlens_q and hit[1] is seqused_k:
+        return hit[2], hit[3]
+    cu, used = cu_seqlens_q.tolist(), seqused_k.tolist()
+    if step is not None:
+        try:
+            step._quantpack_int4_lengths = (cu_seqlens_q, seqused_k, cu, used)
+        except Exception:
+            pass
+    return cu, used
+
+
+def split_step(cu, used, group, prefill_on=True):
+    """Requests of one step by path: (decode, prefill, stock) index lists. Decode: 1..MAX_Q_SPLIT_KV query tokens
+    whose rows fit one decode CTA; prefill: every other request with queries (the tcgen05 kernel), or the stock path
+    when prefill routing is off. Requests without queries are left out."""
+    dec, pre, stock = [], [], []
+    for i in range(len(used)):
+        ql = cu[i + 1] - cu[i]
+        if ql <= 0:
+            continue
+        if ql <= MAX_Q_SPLIT_KV and ql * group <= MAX_DECODE_ROWS:
+            dec.append(i)
+        elif prefill_on:
+            pre.append(i)
+        else:
+            stock.append(i)
+    return dec, pre, stock
+
+
+def make_unified_attention(stock_unified, prefill_on=True):
+    """The replacement of `unified_attention_int4` (signature of int4_kv.py:294-301), falling back to
+    `stock_unified` for what the B200 kernels do not cover."""
+    import torch
+
+    from . import ops
+
+    def _sub_batch(fn, q, out, idx, cu, used, args):
+        """Run fn(q_rows, out_rows, args) on the requests `idx` of the step gathered into a sub-batch."""
+        rows = torch.cat([torch.arange(cu[i], cu[i + 1], device=q.device) for i in idx])
+        lens = [cu[i + 1] - cu[i] for i in idx]
+        sub_cu = torch.tensor([0, *itertools.accumulate(lens)], dtype=torch.int32, device=q.device)
+        sel = torch.tensor(idx, device=q.device)
+        sub_out = torch.empty((len(rows),) + tuple(out.shape[1:]), dtype=out.dtype, device=out.device)
+        sub = dict(args, cu_seqlens_q=sub_cu, max_seqlen_q=max(lens), seqused_k=args["seqused_k"][sel],
+                   block_table=args["block_table"][sel], max_seqlen_k=max(used[i] for i in idx))
+        fn(q[rows], sub_out, sub)
+        out[rows] = sub_out
+
+    def unified_attention_int4(q, k_cache, v_cache, out, *, cu_seqlens_q, max_seqlen_q, seqused_k, max_seqlen_k,
+                               softmax_scale, window_size, block_table, softcap, sinks, alibi_slopes, use_alibi_sqrt,
+                               qq_bias, output_scale, mm_prefix_range, k_scale_cache, v_scale_cache, **kw):
+        args = dict(cu_seqlens_q=cu_seqlens_q, max_seqlen_q=max_seqlen_q, seqused_k=seqused_k,
+                    max_seqlen_k=max_seqlen_k, softmax_scale=softmax_scale, window_size=window_size,
+                    block_table=block_table, softcap=softcap, sinks=sinks, alibi_slopes=alibi_slopes,
+                    use_alibi_sqrt=use_alibi_sqrt, qq_bias=qq_bias, output_scale=output_scale,
+                    mm_prefix_range=mm_prefix_range, k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache, **kw)
+        if not _plain(q, window_size, softcap, sinks, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
+            return stock_unified(q, k_cache, v_cache, out, **args)
+        group = q.shape[1] // k_cache.shape[2]
+        splits = decode_splits_override()
+
+        def decode(qs, outs, a):
+            ops.paged_decode(qs, k_cache, v_cache, outs, cu_seqlens_q=a["cu_seqlens_q"],
+                             max_seqlen_q=a["max_seqlen_q"], seqused_k=a["seqused_k"], max_seqlen_k=a["max_seqlen_k"],
+                             softmax_scale=softmax_scale, block_table=a["block_table"], k_scale_cache=k_scale_cache,
+                             v_scale_cache=v_scale_cache, num_splits=splits)
+
+        if max_seqlen_q <= MAX_Q_SPLIT_KV and max_seqlen_q * group <= MAX_DECODE_ROWS:
+            # a decode step: no host read of the lengths (CUDA-graph capturable)
+            return decode(q, out, args)
+        cu, used = _step_lengths(cu_seqlens_q, seqused_k)
+        dec, pre, rest = split_step(cu, used, group, prefill_on)
+        if dec:
+            _sub_batch(decode, q, out, dec, cu, used, args)
+        if rest:
+            def stock(qs, outs, a):
+                stock_unified(qs, k_cache, v_cache, outs, **a)
+            _sub_batch(stock, q, out, rest, cu, used, args)
+        for i in pre:
+            ops.prefill(q[cu[i]:cu[i + 1]], k_cache, v_cache, out[cu[i]:cu[i + 1]], block_row=block_table[i],
+                        n=used[i], softmax_scale=softmax_scale, k_scale_cache=k_scale_cache,
+                        v_scale_cache=v_scale_cache)
+        return out
+
+    unified_attention_int4._quantpack = True           # the plugin's idempotence marker (int4_kv.py:198, 215)
+    unified_attention_int4._quantpack_b200 = True      # this build's (the reference's own patch also sets _quantpack)
+    return unified_attention_int4
+
+
+def make_reshape_and_cache(stock_store):
+    """The replacement of `reshape_and_cache_int4` (k8v4_kv.py:152-163): the fused B200 store for int4 (uint8 views)
+    and k8v4 (int8 views) caches. Head sizes other than 128 / 256 / 512 go to the stock store (int4) or raise
+    (k8v4, which the stock store does not know)."""
+    from . import k8v4_kv, ops
+
+    def reshape_and_cache_int4(key, value, key_cache, value_cache, slot_mapping, *, k_scale_cache, v_scale_cache):
+        if key.shape[-1] not in (128, 256, 512) or value.shape[-1] != key.shape[-1]:
+            if k8v4_kv.is_k8v4(key_cache):
+                raise ValueError(f"{k8v4_kv.NAME}: head sizes {key.shape[-1]} / {value.shape[-1]} not supported")
+            return stock_store(key, value, key_cache, value_cache, slot_mapping, k_scale_cache=k_scale_cache,
+                               v_scale_cache=v_scale_cache)
+        ops.reshape_and_cache_int4(key, value, key_cache, value_cache, slot_mapping, k_scale_cache=k_scale_cache,
+                                   v_scale_cache=v_scale_cache)
+
+    reshape_and_cache_int4._quantpack = True           # the plugin's idempotence marker (int4_kv.py:198, 215)
+    reshape_and_cache_int4._quantpack_b200 = True      # this build's (the reference's own patch also sets _quantpack)
+    return reshape_and_cache_int4
+
+
+def make_single_rht():
+    from . import ops
+
+    def single_rht(x, inverse=False):
+        return ops.single_rht(x.float(), inverse=inverse)
+
+    single_rht._quantpack = True           # the plugin's idempotence marker (int4_kv.py:198, 215)
+    single_rht._quantpack_b200 = True      # this build's (the reference's own patch also sets _quantpack)
+    return single_rht
+
+
+def _b200_ready():
+    """SM count of device 0; raises unless the B200 library loads and device 0 is an sm_100 GPU."""
+    import torch
+
+    from .. import _lib
+    _lib.load()
+    if not torch.cuda.is_available():
+        raise RuntimeError("no CUDA device")
+    cap = torch.cuda.get_device_capability(0)
+    if cap[0] != 10:
+        raise RuntimeError(f"compute capability {cap[0]}.{cap[1]}: the B200 kernels need sm_100")
+    return torch.cuda.get_device_properties(0).multi_processor_count
+
+
+def patch_int4_kv(logger):
+    """Install the B200 ops into the stock int4 module (int4_kv.py:190-226). Returns True when patched (or already
+    patched), False when disabled, when vLLM lacks the int4 mode, or when the B200 library / GPU is unavailable (the
+    stock path then stays, with a warning)."""
+    if os.environ.get("VLLM_QUANTPACK_INT4_KV", "1") == "0":
+        return False
+    try:
+        stock = importlib.import_module(MODULE)
+    except Exception as e:      # vLLM without the int4 KV mode
+        logger.debug("vllm-quantpack-b200: int4 KV attention not patched (%s)", e)
+        return False
+    if getattr(getattr(stock, "unified_attention_int4", None), "_quantpack_b200", False):
+        return True
+    try:
+        sms = _b200_ready()
+        decode = decode_tiles(sms)
+        if os.environ.get("VLLM_QUANTPACK_INT4_TILES"):
+            logger.info("vllm-quantpack-b200: VLLM_QUANTPACK_INT4_TILES ignored (fixed 128 x 64 tcgen05 tiles)")
+        if decode[:2] != (64, 4):
+            logger.info("vllm-quantpack-b200: decode tile / warps %s ignored (fixed 64-token tiles, 4 warps)",
+                        decode[:2])
+        prefill_on = os.environ.get("VLLM_QUANTPACK_INT4_FA_PREFILL", "1") != "0"
+        unified = make_unified_attention(stock.unified_attention_int4, prefill_on=prefill_on)
+        store = make_reshape_and_cache(stock.reshape_and_cache_int4)
+        rht_fn = make_single_rht()
+    except Exception as e:
+        logger.warning("vllm-quantpack-b200: int4_per_token_head attention left stock (%s)", e)
+        return False
+    from . import k8v4_kv
+    stock.single_rht = rht_fn
+    stock.reshape_and_cache_int4 = store
+    stock.unified_attention_int4 = unified
+    segments = _patch_decode_segments(decode[2], logger)
+    k8v4 = k8v4_kv.patch_backend(stock, logger) and k8v4_kv.register_dtype(logger)
+    logger.info("vllm-quantpack-b200: int4_per_token_head KV attention on B200 kernels (split-KV decode up to %d "
+                "tokens, %s splits; tcgen05 prefill%s; segment buffers for %s)", MAX_Q_SPLIT_KV,
+                decode[2] if decode_splits_override() else "auto", "" if prefill_on else " off",
+                segments or "stock")
+    if k8v4:
+        logger.info("vllm-quantpack-b200: KV cache dtype %s available (int8 keys, int4 values)", k8v4_kv.NAME)
+    return True
+
+
+def _patch_decode_segments(segments, logger):
+    """Size vLLM's split-KV segment buffers for `segments` segments for int4 / k8v4 caches (int4_kv.py:229-257),
+    and reserve this process's decode workspace on the builder's device for the largest decode batch it plans
+    (seq_threshold_3D query rows at the largest split count), so that CUDA-graph capture never grows it."""
+    try:
+        from vllm.v1.attention.backends import triton_attn
+        builder = triton_attn.TritonAttentionMetadataBuilder
+        stock_init = builder.__init__
+        triton_attn.NUM_PAR_SOFTMAX_SEGMENTS   # the anchor this relies on
+    except Exception as e:
+        logger.info("vllm-quantpack-b200: int4 split-KV segments left stock (%s)", e)
+        return 0
+    if getattr(stock_init, "_quantpack_b200", False):
+        return segments
+    if segments < 1 or segments & (segments - 1):
+        logger.warning("vllm-quantpack-b200: int4 split-KV segments must be a power of two, got %d: left stock",
+                       segments)
+        return 0
+
+    def __init__(self, kv_cache_spec, layer_names, vllm_config, device):
+        if vllm_config.cache_config.cache_dtype not in PACKED_DTYPES:
+            return stock_init(self, kv_cache_spec, layer_names, vllm_config, device)
+        saved = triton_attn.NUM_PAR_SOFTMAX_SEGMENTS
+        triton_attn.NUM_PAR_SOFTMAX_SEGMENTS = segments   # read once, in __init__, to size the buffers
+        try:
+            stock_init(self, kv_cache_spec, layer_names, vllm_config, device)
+        finally:
+            triton_attn.NUM_PAR_SOFTMAX_SEGMENTS = saved
+        reserve_decode_workspace(self, vllm_config, device)
+
+    __init__._quantpack = True
+    __init__._quantpack_b200 = True
+    builder.__init__ = __init__
+    return segments
+
+
+def reserve_decode_workspace(builder, vllm_config, device):
+    """Grow the decode workspace of `device` to the builder's largest decode batch (best effort: the sizes come
+    from vLLM attributes that may be absent, in which case the workspace grows on first use)."""
+    try:
+        from .. import _lib
+        from . import ops
+        rows = int(getattr(builder, "seq_threshold_3D"))
+        model = vllm_config.model_config
+        nq = int(model.get_num_attention_heads(vllm_config.parallel_config))
+        nkv = int(model.get_num_kv_heads(vllm_config.parallel_config))
+        max_len = int(getattr(model, "max_model_len", 1 << 20))
+        ops.workspace(device, decode_workspace_bound(rows, nq, nkv, max_len, ops.sm_count(device)))
+    except Exception:
+        pass
+
+
+def decode_workspace_bound(max_tokens, num_q_heads, num_kv_heads, max_seqlen_k, sms):
+    """Largest decode workspace (bytes) a batch of at most `max_tokens` query tokens can need: over every batch size,
+    the tokens it can hold times the split count the library (or the environment) gives it."""
+    from .. import _lib
+    lib = _lib.load()
+    fixed = decode_splits_override()
+    worst = 0
+    for seqs in range(1, max(1, max_tokens) + 1):
+        splits = fixed or lib.qp_decode_num_splits(seqs, num_kv_heads, max_seqlen_k, sms)
+        worst = max(worst, min(max_tokens, MAX_Q_SPLIT_KV * seqs) * splits)
+    return lib.qp_decode_workspace_bytes(worst, num_q_heads, HEAD_SIZE, 1)

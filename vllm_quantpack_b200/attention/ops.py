@@ -124,13 +124,19 @@ _ws_lock = threading.Lock()
 _workspaces = {}
 
 
+_retired = []
+
+
 def workspace(device, nbytes):
-    """A per-device scratch buffer for the split-KV partials, grown geometrically and kept for the process. Growing
-    it inside a CUDA-graph capture allocates from the graph's pool: warm up with the largest batch first."""
+    """A per-device scratch buffer for the split-KV partials, grown geometrically and kept for the process. A
+    buffer that is outgrown stays allocated too: a CUDA graph captured earlier may still hold its address. Growing
+    it inside a CUDA-graph capture allocates from the graph's pool: reserve the largest size before capturing."""
     key = str(torch.device(device))
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
+            if ws is not None:
+                _retired.append(ws)
             size = max(nbytes, 2 * (ws.numel() if ws is not None else 0), 1 << 20)
             ws = torch.empty(size, dtype=torch.uint8, device=device)
             _workspaces[key] = ws
@@ -147,13 +153,15 @@ def decode_num_splits(num_seqs, num_kv_heads, max_seqlen_k, sms):
 
 def paged_decode(q, key_cache, value_cache, out, *, cu_seqlens_q, max_seqlen_q, seqused_k, max_seqlen_k,
                  softmax_scale, block_table, k_scale_cache, v_scale_cache, num_splits=None, q_rotated=False,
-                 out_fp32_lse=None, ws=None, partials_only=False):
+                 out_fp32_lse=None, ws=None, partials_only=False, tokens_after_keys=0):
     """Split-KV decode of up to 32 query rows per KV head (4 MTP tokens x 6 heads) over the paged cache.
 
     q / out (tokens, query heads, hs). When `out_fp32_lse` is a tensor (tokens, query heads) fp32, `out` must be fp32
     and receives the RHT-domain output with its base-2 log-sum-exp in `out_fp32_lse` (the partial a sequence-parallel
     rank exchanges); otherwise `out` gets the model-domain output in q's dtype. partials_only=True launches the split
-    kernel alone and leaves its partials in the workspace (returned)."""
+    kernel alone and leaves its partials in the workspace (returned). tokens_after_keys: sequence tokens that follow
+    the cached keys given here (a sequence-parallel rank holding an earlier range): query token i of a sequence sees
+    key k iff k <= seqused_k - qlen + i + tokens_after_keys."""
     hs = q.shape[-1]
     nq = q.shape[1]
     lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
@@ -187,7 +195,8 @@ def paged_decode(q, key_cache, value_cache, out, *, cu_seqlens_q, max_seqlen_q, 
     _lib.call("qp_paged_decode", lay.fmt, dt, q.data_ptr(), q.stride(0), q.stride(1), out.data_ptr(), out.stride(0),
               out.stride(1), q.shape[0], num_seqs, cu_seqlens_q.data_ptr(), seqused_k.data_ptr(), int(max_seqlen_q),
               block_table.data_ptr(), block_table.stride(0), *lay.args(), nq, nkv, hs, float(softmax_scale),
-              rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)), mode, lse_ptr, int(num_splits),
+              rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)), int(tokens_after_keys), mode,
+              lse_ptr, int(num_splits),
               ws.data_ptr(), ws.numel() * ws.element_size(), _stream(q.device))
     return ws if partials_only else out
 
@@ -217,11 +226,12 @@ def merge_attn_partials(part_o, part_lse, out, lse_out=None):
 
 
 def prefill(q, key_cache, value_cache, out, *, block_row, n, softmax_scale, k_scale_cache, v_scale_cache,
-            q_rotated=False, out_fp32_lse=None, ws=None):
+            q_rotated=False, out_fp32_lse=None, ws=None, tokens_after_keys=0):
     """Chunk prefill of one sequence on the tensor cores: q (qlen, query heads, hs) are the last qlen positions of a
     context of n cached tokens (causal among themselves); block_row is the sequence's int32 block-table row.
     `out` gets the model-domain output in q's dtype, or with `out_fp32_lse` the fp32 RHT-domain output and its
-    base-2 lse (vllm_quantpack/attention/int4_prefill.py:203-232 returns the RHT-domain output for rotated queries)."""
+    base-2 lse (vllm_quantpack/attention/int4_prefill.py:203-232 returns the RHT-domain output for rotated queries).
+    tokens_after_keys as in paged_decode (n >= qlen - tokens_after_keys)."""
     hs, nq, qlen = q.shape[-1], q.shape[1], q.shape[0]
     lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
     if block_row.dtype != torch.int32 or block_row.stride(-1) != 1:
@@ -229,7 +239,7 @@ def prefill(q, key_cache, value_cache, out, *, block_row, n, softmax_scale, k_sc
     if q.stride(-1) != 1 or out.stride(-1) != 1:
         raise ValueError("q / out rows must be contiguous")
     dt = _dtype_code(q, "prefill")
-    wbytes = _lib.load().qp_prefill_workspace_bytes(qlen, int(n), nq, lay.nkv, hs)
+    wbytes = _lib.load().qp_prefill_workspace_bytes(qlen, int(n), nq, lay.nkv, hs, int(tokens_after_keys))
     if ws is None:
         ws = workspace(q.device, wbytes)
     if out_fp32_lse is not None:
@@ -242,6 +252,6 @@ def prefill(q, key_cache, value_cache, out, *, block_row, n, softmax_scale, k_sc
         mode, lse_ptr = 0, None
     _lib.call("qp_prefill", lay.fmt, dt, q.data_ptr(), q.stride(0), q.stride(1), out.data_ptr(), out.stride(0),
               out.stride(1), qlen, int(n), block_row.data_ptr(), *lay.args(), nq, lay.nkv, hs, float(softmax_scale),
-              rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)), mode, lse_ptr, ws.data_ptr(),
-              ws.numel() * ws.element_size(), _stream(q.device))
+              rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)), int(tokens_after_keys), mode,
+              lse_ptr, ws.data_ptr(), ws.numel() * ws.element_size(), _stream(q.device))
     return out

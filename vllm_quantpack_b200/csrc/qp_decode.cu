@@ -55,6 +55,7 @@ struct DecodeParams {
   float qk_scale;      // softmax_scale / head_size * log2(e)
   const uint32_t* sign_bits;
   int q_rotated;  // q already in the RHT domain
+  int tokens_after;  // sequence tokens after this call's keys (held by other ranks), clamped to max_seqlen_q
   int num_splits;
   float* part_o;    // [tokens][nq][splits][HS]
   float* part_lse;  // [tokens][nq][splits], log2 units
@@ -330,7 +331,10 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
   int e_run = -1000;    // running power-of-two range of P_v (value scales): every value scale < 2^e_run
   float pv_mul = 0.f;   // 2^-e_run
   float v_limit = 0.f;  // 2^e_run
-  const int causal_from = n - qlen + 1;  // keys >= this are hidden from some query token
+  // query token i sits at position n - qlen + i + tokens_after of the keys; keys >= causal_from are hidden from some
+  // row or lie past the context
+  const int vis_base = n - qlen + p.tokens_after;  // last key query token 0 sees (before clamping to n - 1)
+  const int causal_from = min(n, vis_base + 1);
   const uint32_t qsm_base = smem_u32(qsm);
   const int tau_a = 16 * warp + g, tau_b = tau_a + 8;
   const int pk_a = pv_k_of_token(tau_a) * PSTRIDE, pk_b = pv_k_of_token(tau_b) * PSTRIDE;
@@ -454,8 +458,8 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
         float s1 = (sacc[nt][2 + e] - fmaf(kz_b, qsum[nt][e], qcq[nt][e])) * (ks_b * qsc[nt][e]);
         if (need_mask) {
           const int r = 8 * nt + 2 * t + e;
-          const int lim = r < rows ? n - qlen + r / p.group : -1;  // last key this row sees
-          if (tok_a > lim) s0 = -INFINITY;                          // also past the context: lim <= n - 1
+          const int lim = r < rows ? min(n - 1, vis_base + r / p.group) : -1;  // last key this row sees
+          if (tok_a > lim) s0 = -INFINITY;                                      // also past the context
           if (tok_b > lim) s1 = -INFINITY;
         }
         sc[nt][e] = s0;
@@ -872,8 +876,8 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
                                int block_size, int64_t block_stride, int64_t head_stride, int64_t slot_stride,
                                int64_t k_off, int64_t ks_off, int64_t v_off, int64_t vs_off, int num_q_heads,
                                int num_kv_heads, int head_size, float softmax_scale, const uint32_t* rht_sign_bits,
-                               int q_rotated, int out_mode, float* lse_out, int num_splits, void* workspace,
-                               int64_t workspace_bytes, void* stream) {
+                               int q_rotated, int tokens_after_keys, int out_mode, float* lse_out, int num_splits,
+                               void* workspace, int64_t workspace_bytes, void* stream) {
   if (fmt != FMT_INT4 && fmt != FMT_K8V4) return set_error(QP_ERR_UNSUPPORTED, "decode: format %d", fmt);
   if (dtype != DT_BF16 && dtype != DT_F16) return set_error(QP_ERR_UNSUPPORTED, "decode: dtype %d", dtype);
   if (head_size != DEC_HS) return set_error(QP_ERR_UNSUPPORTED, "decode: head size %d (this build: 256)", head_size);
@@ -887,6 +891,7 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
     return set_error(QP_ERR_UNSUPPORTED, "decode: %d query tokens x %d heads per KV head > %d rows", max_seqlen_q,
                      group, DEC_MAX_ROWS);
   if (out_mode < 0 || out_mode > 2) return set_error(QP_ERR_INVALID, "decode: out_mode %d", out_mode);
+  if (tokens_after_keys < 0) return set_error(QP_ERR_INVALID, "decode: tokens_after_keys %d", tokens_after_keys);
   const int cell = fmt == FMT_INT4 ? DEC_HS + 8 : DEC_HS * 3 / 2 + 8;
   if (slot_stride != cell)
     return set_error(QP_ERR_LAYOUT, "decode: cells of a (block, head) must be contiguous (slot stride %lld, cell %d)",
@@ -927,6 +932,7 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
   dp.qk_scale = softmax_scale / static_cast<float>(head_size) * LOG2E;
   dp.sign_bits = rht_sign_bits;
   dp.q_rotated = q_rotated;
+  dp.tokens_after = tokens_after_keys < max_seqlen_q ? tokens_after_keys : max_seqlen_q;  // >= qlen - 1: no mask
   dp.num_splits = num_splits;
   const int64_t rows = num_q_tokens * num_q_heads * static_cast<int64_t>(num_splits);
   dp.part_o = static_cast<float*>(workspace);
@@ -1055,6 +1061,6 @@ extern "C" int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t
                          num_q_tokens, num_seqs, cu_seqlens_q, seqused_k, max_seqlen_q, block_table,
                          block_table_stride, cache, block_size, block_stride, head_stride, slot_stride, k_off, ks_off,
                          v_off, vs_off, num_q_heads, num_kv_heads, head_size, softmax_scale, rht_sign_bits, q_rotated,
-                         out_mode, lse_out, num_splits, g_static_decode_scratch_addr[dev], kStaticDecodeScratchBytes,
+                         0, out_mode, lse_out, num_splits, g_static_decode_scratch_addr[dev], kStaticDecodeScratchBytes,
                          stream);
 }

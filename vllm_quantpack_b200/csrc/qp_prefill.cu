@@ -89,6 +89,7 @@ struct PrefillParams {
   const int32_t* block_row;  // block table row of the sequence
   int n;                     // context length (the chunk's keys included)
   int qlen;
+  int vis_base;              // last key query token 0 sees: n - qlen + tokens after the keys (may exceed n - 1)
   int nq, nkv, group;
   int mt_per_kv;             // M-tiles per KV head
   const uint8_t* qprep;      // [nkv][mt_per_kv][65536 B] operand-layout Q tiles
@@ -208,11 +209,11 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
 __device__ __forceinline__ int perm8_pos(int c) { return 2 * (c & 3) + ((c >> 2) & 1); }
 
 // ---------------------------------------------------------------------------------------------------- schedule
-// Key tiles the rows of M-tile m (of any KV head) attend to: keys 0 .. n - qlen + i_hi.
+// Key tiles the rows of M-tile m (of any KV head) attend to: keys 0 .. min(n - 1, vis_base + i_hi).
 __device__ __forceinline__ int mtile_key_tiles(const PrefillParams& p, int m) {
   const int rows = p.qlen * p.group;
   const int r_hi = min(rows - 1, m * PF_BM + PF_BM - 1);
-  const int keys = p.n - p.qlen + r_hi / p.group + 1;
+  const int keys = min(p.n, p.vis_base + r_hi / p.group + 1);
   return (keys + PF_BN - 1) / PF_BN;
 }
 
@@ -636,7 +637,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         row_ok = rg < p.qlen * p.group;
         tok = rg / p.group;
         qh = w.kvh * p.group + rg % p.group;
-        lim = row_ok ? p.n - p.qlen + tok : -1;
+        lim = row_ok ? min(p.n - 1, p.vis_base + tok) : -1;
       }
       if (w.first_of_piece) {
         m_used = -INFINITY;
@@ -659,7 +660,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_SC_FREE + b]);
       const int key0 = w.kt * PF_BN;
-      const bool masked = key0 + PF_BN - 1 > p.n - p.qlen;  // some row of the chunk cannot see some key here
+      const bool masked = key0 + PF_BN - 1 > min(p.n - 1, p.vis_base);  // some row cannot see some key here
       if (masked) {
 #pragma unroll
         for (int c = 0; c < 64; ++c)
@@ -773,15 +774,15 @@ using namespace qp;
 // [part_lse qlen*nq*parts f32], each 256-byte aligned.
 static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
-static void prefill_plan(int qlen, int n, int nkv, int group, int sms, int* mt_per_kv, int64_t* total, int* ctas,
-                         int* parts) {
+static void prefill_plan(int qlen, int n, int after, int nkv, int group, int sms, int* mt_per_kv, int64_t* total,
+                         int* ctas, int* parts) {
   const int rows = qlen * group;
   *mt_per_kv = (rows + PF_BM - 1) / PF_BM;
   int64_t tot = 0;
   int maxt = 0;
   for (int m = 0; m < *mt_per_kv; ++m) {
     const int r_hi = std::min(rows - 1, m * PF_BM + PF_BM - 1);
-    const int t = (n - qlen + r_hi / group + 1 + PF_BN - 1) / PF_BN;
+    const int t = (std::min(n, n - qlen + after + r_hi / group + 1) + PF_BN - 1) / PF_BN;
     tot += t;
     maxt = std::max(maxt, t);
   }
@@ -792,11 +793,13 @@ static void prefill_plan(int qlen, int n, int nkv, int group, int sms, int* mt_p
   *parts = static_cast<int>(std::min<int64_t>(*ctas, (maxt + per - 1) / per + 1));
 }
 
-extern "C" int64_t qp_prefill_workspace_bytes(int qlen, int n, int num_q_heads, int num_kv_heads, int head_size) {
-  if (qlen <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return 0;
+extern "C" int64_t qp_prefill_workspace_bytes(int qlen, int n, int num_q_heads, int num_kv_heads, int head_size,
+                                              int tokens_after_keys) {
+  if (qlen <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || tokens_after_keys < 0) return 0;
+  const int after = std::min(tokens_after_keys, qlen);
   int mt, ctas, parts;
   int64_t total;
-  prefill_plan(qlen, n, num_kv_heads, num_q_heads / num_kv_heads, device_sm_count(), &mt, &total, &ctas, &parts);
+  prefill_plan(qlen, n, after, num_kv_heads, num_q_heads / num_kv_heads, device_sm_count(), &mt, &total, &ctas, &parts);
   const int64_t nt = static_cast<int64_t>(num_kv_heads) * mt;
   return align256(nt * 65536) + align256(nt * PF_BM * 4) +
          align256(static_cast<int64_t>(qlen) * num_q_heads * parts * head_size * 4) +
@@ -831,12 +834,14 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
                           const int32_t* block_row, const void* cache, int block_size, int64_t block_stride,
                           int64_t head_stride, int64_t slot_stride, int64_t k_off, int64_t ks_off, int64_t v_off,
                           int64_t vs_off, int num_q_heads, int num_kv_heads, int head_size, float softmax_scale,
-                          const uint32_t* rht_sign_bits, int q_rotated, int out_mode, float* lse_out, void* workspace,
-                          int64_t workspace_bytes, void* stream) {
+                          const uint32_t* rht_sign_bits, int q_rotated, int tokens_after_keys, int out_mode,
+                          float* lse_out, void* workspace, int64_t workspace_bytes, void* stream) {
   if (fmt != FMT_INT4 && fmt != FMT_K8V4) return set_error(QP_ERR_UNSUPPORTED, "prefill: format %d", fmt);
   if (dtype != DT_BF16 && dtype != DT_F16) return set_error(QP_ERR_UNSUPPORTED, "prefill: dtype %d", dtype);
   if (head_size != PF_HS) return set_error(QP_ERR_UNSUPPORTED, "prefill: head size %d (this build: 256)", head_size);
-  if (qlen < 0 || n < qlen || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads)
+  const int after = std::min(std::max(tokens_after_keys, 0), std::max(qlen, 0));  // >= qlen: nothing masked
+  if (tokens_after_keys < 0 || qlen < 0 || n < qlen - after || (qlen > 0 && n <= 0) || num_kv_heads <= 0 ||
+      num_q_heads <= 0 || num_q_heads % num_kv_heads)
     return set_error(QP_ERR_INVALID, "prefill: bad sizes (qlen %d, n %d, heads %d/%d)", qlen, n, num_q_heads,
                      num_kv_heads);
   if (qlen == 0) return QP_OK;
@@ -857,8 +862,8 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
   const int group = num_q_heads / num_kv_heads;
   int mt, ctas, parts;
   int64_t total;
-  prefill_plan(qlen, n, num_kv_heads, group, device_sm_count(), &mt, &total, &ctas, &parts);
-  const int64_t need = qp_prefill_workspace_bytes(qlen, n, num_q_heads, num_kv_heads, head_size);
+  prefill_plan(qlen, n, after, num_kv_heads, group, device_sm_count(), &mt, &total, &ctas, &parts);
+  const int64_t need = qp_prefill_workspace_bytes(qlen, n, num_q_heads, num_kv_heads, head_size, tokens_after_keys);
   if (workspace_bytes < need)
     return set_error(QP_ERR_WORKSPACE, "prefill: workspace of %lld bytes < %lld", (long long)workspace_bytes,
                      (long long)need);
@@ -895,6 +900,7 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
   pp.block_row = block_row;
   pp.n = n;
   pp.qlen = qlen;
+  pp.vis_base = n - qlen + after;
   pp.nq = num_q_heads;
   pp.nkv = num_kv_heads;
   pp.group = group;
