@@ -8,17 +8,19 @@
 //
 // B200 design (one persistent CTA of 10 warps per SM):
 //   warp 0      producer: 1-D bulk copies of the raw 264 / 392-byte cells of a 64-key tile (whole 16-key runs) into a
-//               ring of raw stages, and of the prepared Q tile (128 query rows x 256 fp16, already in the operand
-//               layout) once per M-tile;
-//   warp 1      MMA issuer (one thread): S = Q K^T (M 128 rows, N 64 keys, K 256) into TMEM, then O += P V (M 128,
-//               N 256 channels, K 64 keys) into TMEM, each finished with tcgen05.commit onto mbarriers;
-//   warps 2-5   dequant: raw cells -> fp16 operands in shared memory, 128B-swizzled canonical UMMA layouts. One lop3
+//               ring of raw stages;
+//   warp 1      MMA issuer (one thread): S = Q K^T (M 128 rows, N 64 keys, K 256; Q read from TMEM) into TMEM, then
+//               O += P V (M 128, N 256 channels, K 64 keys) into TMEM, each finished with tcgen05.commit onto
+//               mbarriers;
+//   warps 2-5   dequant into double-buffered key and value operand tiles (the conversion of tile j + 1 overlaps the
+//               MMAs of tile j): raw cells -> fp16 operands in shared memory, 128B-swizzled canonical UMMA layouts. One lop3
 //               turns two nibbles into fp16, one f16x2 subtract makes the exact (u - zp) (int8 codes for k8v4 keys),
 //               one f16x2 multiply applies the token's scale over a power of two (the tile's largest key scale; the
 //               piece's running largest value scale), so the softmax never touches per-key scales. The channel order
 //               inside every 8 channels is [0 4 1 5 2 6 3 7] (what one lop3 pair yields), the same for Q and K (a dot
 //               product does not see the order) and undone on O in the epilogue;
-//   warps 6-9   softmax: one thread per TMEM lane (= query row). Scores in log2 units = S x (softmax_scale / head x
+//   warps 6-9   softmax: one thread per TMEM lane (= query row); at the start of each piece it stores its row of the
+//               prepared Q tile into TMEM (columns 128-255). Scores in log2 units = S x (softmax_scale / head x
 //               log2 e x 2^-row exponent x 2^key-tile exponent); the running maximum is lazy and per thread (P may
 //               reach 2^8 before O is rescaled in TMEM, which is rare); P in fp16 is written K-major as the A operand
 //               of the PV MMA. The epilogue reads O from TMEM and writes fp32 partials + base-2 lse.
@@ -47,39 +49,37 @@ struct PfCfg {
   static constexpr int KB = FMT == FMT_INT4 ? PF_HS / 2 : PF_HS;  // key bytes in a cell
   static constexpr int RS = FMT == FMT_INT4 ? 3 : 2;               // raw stages
   static constexpr int RAW_BYTES = PF_BN * CELL;
-  // shared memory map (operand tiles 1024-byte aligned for the 128B swizzle)
-  static constexpr int OFF_Q = 0;                       // 4 K-blocks x 128 rows x 128 B = 64 KB
-  static constexpr int OFF_K = OFF_Q + 65536;           // 4 K-blocks x 64 keys x 128 B = 32 KB
-  static constexpr int OFF_V = OFF_K + 32768;           // 4 N-blocks x 8 key groups x 1024 B = 32 KB
-  static constexpr int OFF_P = OFF_V + 32768;           // 2 buffers x 128 rows x 128 B = 32 KB
+  // shared memory map (operand tiles 1024-byte aligned for the 128B swizzle); Q lives in TMEM
+  static constexpr int OFF_K = 0;                       // 2 buffers x 4 K-blocks x 64 keys x 128 B = 64 KB
+  static constexpr int OFF_V = OFF_K + 65536;           // 2 buffers x 4 N-blocks x 8 key groups x 1024 B = 64 KB
+  static constexpr int OFF_P = OFF_V + 65536;           // 2 buffers x 128 rows x 128 B = 32 KB
   static constexpr int OFF_RAW = OFF_P + 32768;         // RS x RAW_BYTES
   static constexpr int OFF_SC = OFF_RAW + RS * RAW_BYTES;  // [2 buffers][key factor 2^F, value exponent E] (16 B)
   static constexpr int OFF_XCH = OFF_SC + 2 * 16;          // [k / v][2 buffers][2 warps] tile maxima exchange
   static constexpr int OFF_BAR = OFF_XCH + 2 * 2 * 2 * 4;
-  static constexpr int NBAR = 32;
+  static constexpr int NBAR = 40;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_TMEM + 16;
 };
 
 // barrier slots
 enum {
-  B_RAW_FULL = 0,    // [RS]
-  B_RAW_EMPTY = 3,   // [RS]
-  B_Q_FULL = 6,
-  B_Q_EMPTY = 7,
-  B_K_FULL = 8,
-  B_K_FREE = 9,
-  B_V_FULL = 10,
-  B_V_FREE = 11,
-  B_S_FULL = 12,     // [2]
-  B_S_FREE = 14,     // [2]
-  B_P_FULL = 16,     // [2]
-  B_P_FREE = 18,     // [2]
-  B_SC_FULL = 20,    // [2]
-  B_SC_FREE = 22,    // [2]
-  B_O_DONE = 24,
-  B_O_FREE = 25,
-  B_FINAL = 26,      // the MMA thread's last commit: every tcgen05.mma done before TMEM is released
+  B_RAW_FULL = 0,    // [RS <= 4]
+  B_RAW_EMPTY = 4,   // [RS <= 4]
+  B_Q_FULL = 8,      // the piece's Q rows are in TMEM (4 softmax warps)
+  B_K_FULL = 10,     // [2] key operand buffers
+  B_K_FREE = 12,     // [2]
+  B_V_FULL = 14,     // [2] value operand buffers
+  B_V_FREE = 16,     // [2]
+  B_S_FULL = 18,     // [2]
+  B_S_FREE = 20,     // [2]
+  B_P_FULL = 22,     // [2]
+  B_P_FREE = 24,     // [2]
+  B_SC_FULL = 26,    // [2]
+  B_SC_FREE = 28,    // [2]
+  B_O_DONE = 30,
+  B_O_FREE = 31,
+  B_FINAL = 32,      // the MMA thread's last commit: every tcgen05.mma done before TMEM is released
 };
 
 struct PrefillParams {
@@ -124,6 +124,16 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]: A (M rows = TMEM lanes, K along columns, two fp16 per 32-bit column)
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // arrive on `bar` once every tcgen05 op this thread issued so far has completed
@@ -186,6 +196,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,"
+      "%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
 }
 
 // 128B-swizzled canonical UMMA shared-memory descriptor (sm_100 version 1). K-major: SBO = 8-row group stride;
@@ -293,8 +315,9 @@ struct Sched {
 
 // ---------------------------------------------------------------------------------------------------- Q prep
 // One warp per (M-tile row): rotate (unless already rotated), scale to fp16 by a per-row power of two, write the row
-// into its M-tile in the K-major 128B-swizzled operand layout with the channel order of the key operand; record the
-// row's score scale; padding rows become zeros. Also sets every lse partial to -inf (absent pieces).
+// (512 bytes, the channel order of the key operand) into its M-tile, ready to be stored as the A operand in TMEM
+// (lane = row, two fp16 per column); record the row's score scale; padding rows become zeros. Also sets every lse
+// partial to -inf (absent pieces).
 template <int FMT, int DT>
 __global__ void __launch_bounds__(256) prefill_qprep_kernel(const void* q, int64_t q_st, int64_t q_sh, int qlen,
                                                             int nq, int nkv, int group, int mt_per_kv,
@@ -349,7 +372,7 @@ __global__ void __launch_bounds__(256) prefill_qprep_kernel(const void* q, int64
   v.y = *reinterpret_cast<uint32_t*>(&h[2]);
   v.z = *reinterpret_cast<uint32_t*>(&h[4]);
   v.w = *reinterpret_cast<uint32_t*>(&h[6]);
-  *reinterpret_cast<uint4*>(tile + (lane >> 3) * 16384 + sw128_off(r, lane & 7)) = v;
+  *reinterpret_cast<uint4*>(tile + r * (PF_HS * 2) + lane * 16) = v;
   if (lane == 0) qs[r] = mr < qlen * group ? ldexpf(qk_scale, -ex) : 0.f;
 }
 
@@ -368,13 +391,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       mbar_init(&bars[B_RAW_FULL + s], 1);
       mbar_init(&bars[B_RAW_EMPTY + s], 4);
     }
-    mbar_init(&bars[B_Q_FULL], 1);
-    mbar_init(&bars[B_Q_EMPTY], 1);
-    mbar_init(&bars[B_K_FULL], 2);
-    mbar_init(&bars[B_K_FREE], 1);
-    mbar_init(&bars[B_V_FULL], 2);
-    mbar_init(&bars[B_V_FREE], 1);
+    mbar_init(&bars[B_Q_FULL], 4);
     for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars[B_K_FULL + b], 2);
+      mbar_init(&bars[B_K_FREE + b], 1);
+      mbar_init(&bars[B_V_FULL + b], 2);
+      mbar_init(&bars[B_V_FREE + b], 1);
       mbar_init(&bars[B_S_FULL + b], 1);
       mbar_init(&bars[B_S_FREE + b], 4);
       mbar_init(&bars[B_P_FULL + b], 4);
@@ -396,6 +418,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tm_s[2] = {tmem, tmem + 64};  // S buffers: columns [0, 64), [64, 128)
+  const uint32_t tm_q = tmem + 128;            // Q (A operand of S = Q K^T): columns [128, 256)
   const uint32_t tm_o = tmem + 256;            // O: columns [256, 512)
 
   Sched sch;
@@ -406,17 +429,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
       int64_t j = 0;        // global tile counter (raw ring)
-      int qcount = 0;       // Q tiles loaded
       for (; !sch.done() && !failed; sch.next(), ++j) {
         const Walk w = sch.current();
-        if (w.new_mtile) {
-          if (qcount > 0) failed |= !mbar_wait_bounded(&bars[B_Q_EMPTY], (qcount - 1) & 1);
-          const int64_t mt = static_cast<int64_t>(w.kvh) * p.mt_per_kv + w.m;
-          mbar_arrive_expect_tx(&bars[B_Q_FULL], 65536);
-          for (int c = 0; c < 4; ++c)
-            bulk_g2s(smem + C::OFF_Q + c * 16384, p.qprep + mt * 65536 + c * 16384, 16384, &bars[B_Q_FULL]);
-          ++qcount;
-        }
         const int stage = static_cast<int>(j % C::RS);
         if (j >= C::RS) failed |= !mbar_wait_bounded(&bars[B_RAW_EMPTY + stage], ((j / C::RS) - 1) & 1);
         const int tok_begin = w.kt * PF_BN;
@@ -444,22 +458,23 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
     if (lane == 0) {
       constexpr uint32_t ID_QK = f16_idesc(PF_BM, PF_BN, false);
       constexpr uint32_t ID_PV = f16_idesc(PF_BM, PF_HS, true);
-      const uint32_t q_base = smem_u32(smem + C::OFF_Q), k_base = smem_u32(smem + C::OFF_K);
-      const uint32_t v_base = smem_u32(smem + C::OFF_V), p_base = smem_u32(smem + C::OFF_P);
+      const uint32_t k_base = smem_u32(smem + C::OFF_K), v_base = smem_u32(smem + C::OFF_V);
+      const uint32_t p_base = smem_u32(smem + C::OFF_P);
       int64_t j = 0;
       int qcount = 0, pieces = 0;
       int64_t pv_pending = -1;  // tile whose PV is still to be issued
       bool pv_first = false, pv_last = false;
       auto issue_pv = [&](int64_t t, bool first) {
         const int b = static_cast<int>(t & 1);
-        failed |= !mbar_wait_bounded(&bars[B_V_FULL], t & 1);
+        failed |= !mbar_wait_bounded(&bars[B_V_FULL + b], (t >> 1) & 1);
         failed |= !mbar_wait_bounded(&bars[B_P_FULL + b], (t >> 1) & 1);
         tc_fence_after();
+        const uint32_t vb = v_base + b * 32768;
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          umma_f16(tm_o, sw128_desc(p_base + b * 16384 + s * 32, 16, 1024),
-                   sw128_desc(v_base + 2 * s * 1024, 8192, 1024), ID_PV, (first && s == 0) ? 0u : 1u);
-        umma_commit(&bars[B_V_FREE]);
+          umma_f16(tm_o, sw128_desc(p_base + b * 16384 + s * 32, 16, 1024), sw128_desc(vb + 2 * s * 1024, 8192, 1024),
+                   ID_PV, (first && s == 0) ? 0u : 1u);
+        umma_commit(&bars[B_V_FREE + b]);
         umma_commit(&bars[B_P_FREE + b]);
         umma_commit(&bars[B_O_DONE]);
       };
@@ -471,19 +486,18 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         }
         // S(j) = Q K(j)^T
         const int b = static_cast<int>(j & 1);
-        failed |= !mbar_wait_bounded(&bars[B_K_FULL], j & 1);
+        failed |= !mbar_wait_bounded(&bars[B_K_FULL + b], (j >> 1) & 1);
         if (j >= 2) failed |= !mbar_wait_bounded(&bars[B_S_FREE + b], ((j >> 1) - 1) & 1);
         tc_fence_after();
+        const uint32_t kb = k_base + b * 32768;
 #pragma unroll
-        for (int s = 0; s < 16; ++s) {
-          const uint32_t koff = (s >> 2) * 8192 + (s & 3) * 32;
-          const uint32_t qoff = (s >> 2) * 16384 + (s & 3) * 32;
-          umma_f16(tm_s[b], sw128_desc(q_base + qoff, 16, 1024), sw128_desc(k_base + koff, 16, 1024), ID_QK,
-                   s > 0 ? 1u : 0u);
-        }
-        umma_commit(&bars[B_K_FREE]);
+        for (int s = 0; s < 16; ++s)  // K step s: 16 channels = 8 TMEM columns of Q
+          umma_f16_ts(tm_s[b], tm_q + 8 * s, sw128_desc(kb + (s >> 2) * 8192 + (s & 3) * 32, 16, 1024), ID_QK,
+                      s > 0 ? 1u : 0u);
+        umma_commit(&bars[B_K_FREE + b]);
         umma_commit(&bars[B_S_FULL + b]);
-        if (w.last_of_piece) umma_commit(&bars[B_Q_EMPTY]);  // the next piece may bring another Q tile
+        // Q of this piece is free once S of its last tile is complete: the softmax, which waits for that S before
+        // it stores the next piece's Q, needs no other signal
         // O += P(j-1) V(j-1), one tile behind so the softmax of tile j overlaps it
         if (pv_pending >= 0) {
           issue_pv(pv_pending, pv_first);
@@ -515,8 +529,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
     const int kr = dq & 63;      // key row of the tile
     const bool is_k = dq < 64;   // warps 2, 3: keys; warps 4, 5: values
     const int wpair = (warp - 2) & 1;
-    uint8_t* kop = smem + C::OFF_K;
-    uint8_t* vop = smem + C::OFF_V;
+    uint8_t* const kop0 = smem + C::OFF_K;
+    uint8_t* const vop0 = smem + C::OFF_V;
     float* xch = reinterpret_cast<float*>(smem + C::OFF_XCH) + (is_k ? 0 : 4);
     int e_run_v = -1000;
     int64_t j = 0;
@@ -561,55 +575,82 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_SC_FULL + b]);
       const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
+      // Each thread converts its key row: every 8-byte load of the row is issued before any conversion (the
+      // stores below could alias them for the compiler, which would otherwise serialise load -> convert -> store
+      // per word). Cells are 8-byte aligned (264 / 392 B) and the 8-byte loads of 16 consecutive rows fall in 16
+      // distinct bank pairs; the stores of 8 consecutive rows hit 8 distinct 16-byte bank groups (swizzle).
+      const uint32_t rbase = (kr >> 3) * 1024 + (kr & 7) * 128, rxor = (kr & 7) << 4;
       if (is_k) {
-        if (j >= 1) failed |= !mbar_wait_bounded(&bars[B_K_FREE], (j - 1) & 1);
+        if (j >= 2) failed |= !mbar_wait_bounded(&bars[B_K_FREE + b], ((j >> 1) - 1) & 1);
+        uint8_t* const kop = kop0 + b * 32768;
         if constexpr (FMT == FMT_INT4) {
-#pragma unroll 4
-          for (int i = 0; i < 32; ++i) {
-            const int W = (i + (kr >> 4)) & 31;  // odd word for lanes 16..31: conflict-free loads and stores
-            const uint32_t x = *reinterpret_cast<const uint32_t*>(cell + 4 * W);
-            const uint32_t x8 = x >> 8;
-            uint4 v;
-            v.x = hmul2_u32(hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b), q2);  // channels 0, 4
-            v.y = hmul2_u32(hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);  // 1, 5
-            v.z = hmul2_u32(hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b), q2);  // 2, 6
-            v.w = hmul2_u32(hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);  // 3, 7
-            *reinterpret_cast<uint4*>(kop + (W >> 3) * 8192 + sw128_off(kr, W & 7)) = v;
+#pragma unroll 1
+          for (int kb = 0; kb < 4; ++kb) {  // K-block kb: words 8 kb .. 8 kb + 7 (channels 64 kb ..)
+            uint2 kw[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) kw[k] = *reinterpret_cast<const uint2*>(cell + 32 * kb + 8 * k);
+            uint8_t* const dst = kop + kb * 8192 + rbase;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {  // word: channels 8 (8 kb + i) .. + 7 = chunk i of the K-block
+              const uint32_t x = (i & 1) ? kw[i >> 1].y : kw[i >> 1].x;
+              const uint32_t x8 = x >> 8;
+              uint4 v;
+              v.x = hmul2_u32(hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b), q2);  // channels 0, 4
+              v.y = hmul2_u32(hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);  // 1, 5
+              v.z = hmul2_u32(hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b), q2);  // 2, 6
+              v.w = hmul2_u32(hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);  // 3, 7
+              *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(i) << 4) ^ rxor)) = v;
+            }
           }
         } else {
-#pragma unroll 4
-          for (int i = 0; i < 32; ++i) {
-            const int C8 = i;  // 8 channels 8 C8 .. 8 C8 + 7 (two words); 392-byte cells: no bank conflict
-            const uint2 x2 = *reinterpret_cast<const uint2*>(cell + 8 * C8);
-            const uint32_t a = x2.x ^ 0x80808080u, c = x2.y ^ 0x80808080u;
-            uint4 v;  // (1152 + code) - 1152 = code, exact; then the scale
-            v.x = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4140u), 0x64806480u), q2);
-            v.y = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4342u), 0x64806480u), q2);
-            v.z = hmul2_u32(hsub2_u32(prmt(c, 0x64646464u, 0x4140u), 0x64806480u), q2);
-            v.w = hmul2_u32(hsub2_u32(prmt(c, 0x64646464u, 0x4342u), 0x64806480u), q2);
-            *reinterpret_cast<uint4*>(kop + (C8 >> 3) * 8192 + sw128_off(kr, C8 & 7)) = v;
+#pragma unroll 1
+          for (int h = 0; h < 4; ++h) {  // K-block h: codes 64 h .. 64 h + 63, 8 loads of 8 bytes in flight
+            uint2 kw[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) kw[k] = *reinterpret_cast<const uint2*>(cell + 64 * h + 8 * k);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {  // 8 channels 8 C8 .. 8 C8 + 7 (two words)
+              const int C8 = 8 * h + k;
+              const uint32_t a = kw[k].x ^ 0x80808080u, c = kw[k].y ^ 0x80808080u;
+              uint4 v;  // (1152 + code) - 1152 = code, exact; then the scale
+              v.x = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4140u), 0x64806480u), q2);
+              v.y = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4342u), 0x64806480u), q2);
+              v.z = hmul2_u32(hsub2_u32(prmt(c, 0x64646464u, 0x4140u), 0x64806480u), q2);
+              v.w = hmul2_u32(hsub2_u32(prmt(c, 0x64646464u, 0x4342u), 0x64806480u), q2);
+              *reinterpret_cast<uint4*>(kop + (C8 >> 3) * 8192 +
+                                        (rbase + ((static_cast<uint32_t>(C8 & 7) << 4) ^ rxor))) = v;
+            }
           }
         }
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[B_K_FULL]);
+        if (lane == 0) mbar_arrive(&bars[B_K_FULL + b]);
       } else {
-        if (j >= 1) failed |= !mbar_wait_bounded(&bars[B_V_FREE], (j - 1) & 1);
-#pragma unroll 4
-        for (int i = 0; i < 32; ++i) {
-          const int W = (i + (kr >> 4)) & 31;
-          const uint32_t x = *reinterpret_cast<const uint32_t*>(cell + C::KB + 4 + 4 * W);
-          const uint32_t x8 = x >> 8;
-          uint4 v;
-          v.x = hmul2_u32(hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b), q2);
-          v.y = hmul2_u32(hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
-          v.z = hmul2_u32(hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b), q2);
-          v.w = hmul2_u32(hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
-          *reinterpret_cast<uint4*>(vop + (W >> 3) * 8192 + sw128_off(kr, W & 7)) = v;
+        if (j >= 2) failed |= !mbar_wait_bounded(&bars[B_V_FREE + b], ((j >> 1) - 1) & 1);
+        uint8_t* const vop = vop0 + b * 32768;
+        // the value words start 4 bytes past an 8-byte boundary: 8-byte loads from the key scale on give the pairs
+        // (key scale, V0), (V1, V2), ..., (V31, value scale)
+#pragma unroll 1
+        for (int kb = 0; kb < 4; ++kb) {  // N-block kb: words 8 kb .. 8 kb + 7; loads at 8-byte offsets 4 kb ..
+          uint2 vw[5];
+#pragma unroll
+          for (int k = 0; k < 5; ++k) vw[k] = *reinterpret_cast<const uint2*>(cell + C::KB + 32 * kb + 8 * k);
+          uint8_t* const dst = vop + kb * 8192 + rbase;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint32_t x = (i & 1) ? vw[(i + 1) >> 1].x : vw[i >> 1].y;
+            const uint32_t x8 = x >> 8;
+            uint4 v;
+            v.x = hmul2_u32(hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b), q2);
+            v.y = hmul2_u32(hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
+            v.z = hmul2_u32(hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b), q2);
+            v.w = hmul2_u32(hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
+            *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(i) << 4) ^ rxor)) = v;
+          }
         }
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[B_V_FULL]);
+        if (lane == 0) mbar_arrive(&bars[B_V_FULL + b]);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_RAW_EMPTY + stage]);
@@ -621,7 +662,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     uint8_t* p_tile = smem + C::OFF_P;
     int64_t j = 0;
-    int qcount = 0;
     float m_used = -INFINITY, l = 0.f, qsc = 0.f;
     int e_used = -1000, lim = -1, tok = 0, qh = 0;
     bool row_ok = false;
@@ -630,9 +670,28 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       const Walk w = sch.current();
       const int b = static_cast<int>(j & 1);
       if (w.new_mtile) {
-        failed |= !mbar_wait_bounded(&bars[B_Q_FULL], qcount & 1);
-        ++qcount;
-        qsc = p.qscale[(static_cast<int64_t>(w.kvh) * p.mt_per_kv + w.m) * PF_BM + row];
+        // this row of the piece's Q tile -> TMEM columns [128, 256) of its lane (the previous piece's QKs are
+        // complete: this thread consumed the S of its last tile)
+        const int64_t mt = static_cast<int64_t>(w.kvh) * p.mt_per_kv + w.m;
+        const uint4* qrow = reinterpret_cast<const uint4*>(p.qprep + mt * 65536 + row * (PF_HS * 2));
+#pragma unroll 1
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t qw[32];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint4 v = __ldg(qrow + c0 / 4 + i);
+            qw[4 * i] = v.x;
+            qw[4 * i + 1] = v.y;
+            qw[4 * i + 2] = v.z;
+            qw[4 * i + 3] = v.w;
+          }
+          tmem_st32u(tm_q + lane_off + c0, qw);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[B_Q_FULL]);
+        qsc = p.qscale[mt * PF_BM + row];
         const int rg = w.m * PF_BM + row;
         row_ok = rg < p.qlen * p.group;
         tok = rg / p.group;
