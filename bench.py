@@ -14,7 +14,8 @@ At N > 1 each rank serves its own request(s) of the workload (batch sharded by r
 scaling); the line also carries `seq_parallel`: one request split by sequence range over the N ranks, each rank's
 partial (O, LSE) all-gathered over NCCL and merged (strong scaling of a single request).
 
-The cache (>= 138 MB) is larger than L2 and L2 is flushed (256 MB write) before every timed step; each step is timed
+The cache (>= 138 MB) is larger than L2 and L2 is flushed (256 MB written, then another 256 MB read so that the
+write-back of the dirty lines happens before the timed region) before every timed step; each step is timed
 on the device with CUDA events on the launching stream, max over ranks.
 
 `--impl reference` times the reference algorithm on the host cores instead: the CPU oracle (a restatement of the
@@ -42,6 +43,10 @@ WORKLOADS = {
     "c3": dict(fmt="int4", seqs=1, ctx=229376 + 1024, qlen=1024, prefill=True),
 }
 CELL = {"int4": HS + 8, "k8v4": HS * 3 // 2 + 8}
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture (profiles/): the decode kernel
+# captured at c1 (131,072 tokens: 138.54 MB read, 4.29 MB written) and scaled by the cache bytes to 262,144 tokens
+# plus that workload's split partials; the prefill kernel captured at c3 itself.
+TRAFFIC = {"c2a": 2 * 138.54e6 + 4 * 24 * 111 * 1028, "c1": 138.54e6 + 4.29e6, "c3": 10.279e9 + 0.0335e9}
 
 
 def algorithmic_bytes(w, seqs=None):
@@ -156,6 +161,18 @@ def build_request(torch, ops, w, device, seqs, seed=0):
     return dict(kv=kv, views=(kc, vc, ks, vs), table=table, q=q, cu=cu, used=used, seqs=seqs)
 
 
+FLUSH_BYTES = 256 << 20   # each half of the flush buffer is twice the 126 MB L2
+
+
+def l2_flush(flush):
+    """Evict L2: write one half of `flush` (> L2), then read the other half (> L2), so the dirty lines of the write
+    are written back here and not during the next timed step (a write-only flush leaves ~126 MB of dirty lines whose
+    write-back the timed kernel would pay)."""
+    half = flush.numel() // 2
+    flush[:half].zero_()
+    flush[half:].view(-1, 8).max(dim=0)
+
+
 def timed_steps(torch, fn, steps, warmup, flush):
     """Run `warmup` untimed steps, then `steps` steps each timed by CUDA events (L2 flushed before each)."""
     for _ in range(warmup):
@@ -163,7 +180,7 @@ def timed_steps(torch, fn, steps, warmup, flush):
     torch.cuda.synchronize()
     times = []
     for _ in range(steps):
-        flush.zero_()
+        l2_flush(flush)
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
@@ -242,7 +259,7 @@ def run_prefill(args, w, rank, world, local_rank):
     out = torch.empty_like(q)
     row = R["table"][0].contiguous()
     call = dict(block_row=row, n=w["ctx"], softmax_scale=HS ** -0.5, k_scale_cache=ks, v_scale_cache=vs)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    flush = torch.empty(2 * FLUSH_BYTES, dtype=torch.uint8, device=device)
     q_host = q.cpu().pin_memory()
     out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
     q_dev = torch.empty_like(q)
@@ -273,9 +290,11 @@ def run_prefill(args, w, rank, world, local_rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int4+f16", "data": "synthetic",
             "config": {"workload": args.workload, **w, "nq": NQ, "nkv": NKV, "head_size": HS, "block_size": BS,
-                       "l2": "flushed before every step (256 MB write); cache larger than L2"},
+                       "l2": "flushed before every step (256 MB write, then 256 MB read); cache larger than L2"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None, "kernel": "prefill_kernel (q prep + merge included)",
+                         "frac": achieved / peak, "traffic": TRAFFIC.get(args.workload),
+                         "traffic_unit": "bytes per launch (ncu dram__bytes_read + write)",
+                         "kernel": "prefill_kernel (q prep + merge included)",
                          "algorithmic_flops_per_launch": flops, "peak_kind": kind},
             "e2e": {"value": w["qlen"] / (ms_e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": q.numel() * 2,
                     "d2h_bytes_per_step": out.numel() * 2},
@@ -298,7 +317,7 @@ def run_b200(args, w, rank, world, local_rank):
     nsplit = ops.decode_num_splits(seqs, NKV, w["ctx"], ops.sm_count(device))
     call = dict(cu_seqlens_q=cu, max_seqlen_q=w["qlen"], seqused_k=used, max_seqlen_k=w["ctx"],
                 softmax_scale=HS ** -0.5, block_table=table, k_scale_cache=ks, v_scale_cache=vs, num_splits=nsplit)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    flush = torch.empty(2 * FLUSH_BYTES, dtype=torch.uint8, device=device)
 
     def step():
         ops.paged_decode(q, kc, vc, out, **call)
@@ -350,15 +369,17 @@ def run_b200(args, w, rank, world, local_rank):
         "data": "synthetic",
         "config": {"workload": args.workload, **w, "nq": NQ, "nkv": NKV, "head_size": HS, "block_size": BS,
                    "num_splits": nsplit, "parallelism": f"requests sharded over {world} GPU(s)" if world > 1 else
-                   "1 GPU", "l2": "flushed before every step (256 MB write); cache larger than L2"},
+                   "1 GPU", "l2": "flushed before every step (256 MB write, then 256 MB read); cache larger than L2"},
         "hbm_gbs": bytes_call * world / (ms * 1e-3) / 1e9 / world,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "kernel": "decode_kernel (split-KV, without the merge)",
+                     "traffic": TRAFFIC.get(args.workload),
+                     "traffic_unit": "bytes per launch (ncu dram__bytes_read + write)",
+                     "kernel": "decode_kernel (split-KV, with its query-row prep kernel, without the merge)",
                      "algorithmic_bytes_per_launch": bytes_call, "kernel_ms": ms_k, "peak_kind": peak_kind},
         "cpu_baseline": cpu,
         "e2e": {"value": tokens / (ms_e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": q.numel() * 2,
                 "d2h_bytes_per_step": out.numel() * 2},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": 3 * args.steps,  # query prep, split-KV decode, merge
         "clocks": clk.summary(),
         "device_error": dev_err,
         "x16_layers_ms": ms * 16,

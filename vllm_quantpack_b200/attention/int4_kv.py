@@ -324,5 +324,6 @@ def decode_workspace_bound(max_tokens, num_q_heads, num_kv_heads, max_seqlen_k, 
     worst = 0
     for seqs in range(1, max(1, max_tokens) + 1):
         splits = fixed or lib.qp_decode_num_splits(seqs, num_kv_heads, max_seqlen_k, sms)
-        worst = max(worst, min(max_tokens, MAX_Q_SPLIT_KV * seqs) * splits)
-    return lib.qp_decode_workspace_bytes(worst, num_q_heads, HEAD_SIZE, 1)
+        tokens = min(max_tokens, MAX_Q_SPLIT_KV * seqs)
+        worst = max(worst, lib.qp_decode_workspace_bytes(tokens, num_q_heads, HEAD_SIZE, splits))
+    return worst

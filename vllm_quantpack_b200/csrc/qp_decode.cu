@@ -9,10 +9,13 @@
 // out += P_v16 u - sum(P_v16 zp) with the same rounded P_v16 in both terms (int4_kv.py:80-94).
 //
 // B200 design:
-// - one CTA (4 warps) per (split, KV head, sequence); the segment's cells stream through a 4-stage shared-memory
-//   ring filled by 1-D bulk copies (TMA engine) of whole 16-token runs, completing on mbarriers;
-// - Q is rotated (RHT) and scaled once per CTA into fp16 with a per-row power of two, its channels permuted so that
-//   the nibble extraction below needs no shuffles; odd (high-nibble) channels carry a factor 1/16;
+// - one CTA (4 warps) per (split, KV head, sequence); the segment's cells stream through a 3-stage shared-memory
+//   ring filled by 1-D bulk copies (TMA engine), each warp copying its own 16-token group of a tile, completing on
+//   mbarriers;
+// - K0q (a small kernel before K1) rotates (RHT) and scales every query row once into fp16 with a per-row power of
+//   two, its channels permuted so that the nibble extraction below needs no shuffles (odd, high-nibble, channels
+//   carry a factor 1/16), and stores it as the exact shared-memory image of the row; K1 starts under programmatic
+//   dependent launch, issues its first cache copies, then waits for K0q and fetches its rows with one bulk copy;
 // - QK: mma.sync m16n8k16 with the keys as M (16 tokens per warp) and the query rows as N (8 per n-tile). Key
 //   nibbles become fp16 by the exponent-bias trick ((w & 0x000F000F) | 0x64006400 = 1024 + u): one lop3 per two
 //   values, the bias removed once per score (Q.1024 is a per-row constant);
@@ -55,6 +58,8 @@ struct DecodeParams {
   float qk_scale;      // softmax_scale / head_size * log2(e)
   const uint32_t* sign_bits;
   int q_rotated;  // q already in the RHT domain
+  const uint8_t* qrec;  // prepared query rows: [kv head][token][query head of the group] x Q_STRIDE bytes
+  int64_t num_tokens;
   int tokens_after;  // sequence tokens after this call's keys (held by other ranks), clamped to max_seqlen_q
   int num_splits;
   float* part_o;    // [tokens][nq][splits][HS]
@@ -84,9 +89,8 @@ struct DecSmem {
   static constexpr int OFF_RED = OFF_P + 2 * P_BYTES;         // [ROWS][4 warps] f32 (row max, then l)
   static constexpr int OFF_VS = OFF_RED + ROWS * 4 * 4;       // [4] f32 (value-scale max per warp)
   static constexpr int OFF_ZB = OFF_VS + 16;                  // [2 buffers][lo, hi][64] u16 zero-point biases
-  static constexpr int OFF_ROWP = OFF_ZB + 2 * 2 * DEC_TILE * 2;  // qscale, cq, qsum: [3][ROWS]
-  static constexpr int OFF_BAR = (OFF_ROWP + 3 * ROWS * 4 + 7) / 8 * 8;
-  static constexpr int BYTES = OFF_BAR + DEC_STAGES * 8;
+  static constexpr int OFF_BAR = (OFF_ZB + 2 * 2 * DEC_TILE * 2 + 7) / 8 * 8;
+  static constexpr int BYTES = OFF_BAR + (DEC_STAGES + 1) * 8;  // stage barriers, then the Q-rows barrier
 };
 
 // k index (0..255) of the QK MMA that carries channel c (see the fragment mapping in decode_kernel).
@@ -135,6 +139,69 @@ __device__ __forceinline__ uint32_t nib_hi(uint32_t x, uint32_t hi_bias) {
 constexpr float RESCALE_SLACK = 8.f;
 
 
+// ---------------------------------------------------------------------------------------------------- K0q
+// One warp per (query token, query head): the row as the decode kernel holds it in shared memory (Q_STRIDE bytes):
+// 256 fp16 in the k order of the QK MMA, scaled by a power of two (|q| < 2^14), odd int4 channels x 1/16; then the
+// row's score scale (softmax_scale / head x log2 e x 2^-exponent), its bias sum (Q . 1024 / 64 / 1152 per channel
+// kind) and its plain sum, as fp32 at byte 512. Written once per call; every split of the row's KV head reads it.
+template <int FMT, int DT>
+__global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_t q_st, int64_t q_sh, int64_t T,
+                                                           int nq, int nkv, const uint32_t* sign_bits, int q_rotated,
+                                                           float qk_scale, uint8_t* qrec) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  using EL = Elem<DT>;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= T * nq) return;
+  const int64_t tok = row / nq;
+  const int qh = static_cast<int>(row % nq);
+  const int group = nq / nkv, kvh = qh / group, hg = qh % group;
+  uint8_t* rec = qrec + ((static_cast<int64_t>(kvh) * T + tok) * group + hg) * Q_STRIDE;
+  __half* qrow = reinterpret_cast<__half*>(rec);
+  const typename EL::T* src = reinterpret_cast<const typename EL::T*>(q) + tok * q_st + qh * q_sh + lane * 8;
+  float x[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = EL::to_f(src[i]);
+  if (!q_rotated) {
+    apply_signs<8>(x, sign_bits, lane);
+    warp_wht<8>(x, lane);
+  }
+  float am = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(x[i]));
+  am = warp_max(am);
+  int ex = 0;
+  if (am > 0.f) {
+    frexpf(am, &ex);  // am < 2^ex
+    ex = 14 - ex;     // am * 2^ex in [2^13, 2^14)
+  }
+  float cq = 0.f, qs = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c = lane * 8 + i;
+    const __half h = __float2half_rn(ldexpf(x[i], ex));
+    const float hv = __half2float(h);
+    qs += hv;
+    if constexpr (FMT == FMT_INT4) {
+      const bool odd = c & 1;
+      cq += odd ? 64.f * hv : 1024.f * hv;
+      qrow[qk_k_of_channel<FMT>(c)] = odd ? __float2half_rn(hv * 0.0625f) : h;
+    } else {
+      cq += 1152.f * hv;
+      qrow[qk_k_of_channel<FMT>(c)] = h;
+    }
+  }
+  cq = warp_sum(cq);
+  qs = warp_sum(qs);
+  if (lane == 0) {
+    float* rc = reinterpret_cast<float*>(rec + 2 * DEC_HS);
+    rc[0] = ldexpf(qk_scale, -ex);
+    rc[1] = cq;
+    rc[2] = qs;
+    rc[3] = 0.f;
+  }
+}
+
 template <int FMT, int DT, int NT>
 __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(const DecodeParams p) {
   using SM = DecSmem<FMT, NT>;
@@ -147,9 +214,6 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
   float* red = reinterpret_cast<float*>(smem + SM::OFF_RED);
   float* red_vs = reinterpret_cast<float*>(smem + SM::OFF_VS);
   uint16_t* zbuf = reinterpret_cast<uint16_t*>(smem + SM::OFF_ZB);  // [buf][lo/hi][64]
-  float* row_qscale = reinterpret_cast<float*>(smem + SM::OFF_ROWP);
-  float* row_cq = row_qscale + ROWS;
-  float* row_qsum = row_cq + ROWS;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::OFF_BAR);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -182,124 +246,59 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
   const int32_t* btab = p.block_table + static_cast<int64_t>(seq) * p.bt_stride;
   const uint8_t* head_base = p.cache + static_cast<int64_t>(kvh) * p.head_stride;
 
-  // --- producer (thread 0): bulk copies of whole 16-token runs (block_size % 16 == 0, so a run never crosses a block
-  // and the last run of a sequence stays inside the block that holds its last token). The block of each 16-token
-  // group is tracked incrementally (no division) and its table entry loaded one tile ahead of the copy. ----------
-  int nb_idx = 0, nb_off = 0;  // block-table index / in-block token offset of the first token of tile `issued`
-  auto tile_groups = [&](int i) {
-    const int tok_begin = (tile0 + i) * DEC_TILE;
-    return (min(tok_begin + DEC_TILE, n) - tok_begin + 15) >> 4;
-  };
-  auto load_blocks = [&](int i, int (&blk)[4], int (&inb)[4]) {
-    const int groups = tile_groups(i);
-#pragma unroll
-    for (int gi = 0; gi < 4; ++gi) {
-      blk[gi] = gi < groups ? __ldg(btab + nb_idx) : 0;
-      inb[gi] = nb_off;
-      nb_off += 16;
-      if (nb_off == p.block_size) {
-        nb_off = 0;
-        ++nb_idx;
-      }
+  // --- copies: warp w copies 16-token group w of every tile (block_size % 16 == 0, so a group never crosses a block),
+  // one bulk copy each, arriving with its byte count on the tile's stage barrier (4 arrivals per phase); the block
+  // of the group is loaded one tile ahead.
+  auto group_block = [&](int i, int& blk, int& inb) {
+    const int tok = (tile0 + i) * DEC_TILE + 16 * warp;
+    blk = -1;
+    inb = 0;
+    if (i < ntl && tok < n) {
+      const int bi = tok / p.block_size;
+      inb = tok - bi * p.block_size;
+      blk = __ldg(btab + bi);
     }
   };
-  auto issue_tile = [&](int i, const int (&blk)[4], const int (&inb)[4]) {
+  auto issue_group = [&](int i, int blk, int inb) {
     const int stage = i % DEC_STAGES;
-    const int groups = tile_groups(i);
-    mbar_arrive_expect_tx(&bars[stage], static_cast<uint32_t>(groups * 16 * CELL));
-    uint8_t* dst = stages + stage * SM::STAGE_BYTES;
-#pragma unroll
-    for (int gi = 0; gi < 4; ++gi) {
-      // a group continues the previous copy when it is the next run of the same block
-      const bool starts = gi == 0 || inb[gi] == 0 || blk[gi] != blk[gi - 1];
-      if (gi < groups && starts) {
-        int run = 1;
-#pragma unroll
-        for (int k = gi + 1; k < 4; ++k)
-          if (k < groups && run == k - gi && blk[k] == blk[gi] && inb[k] != 0) ++run;
-        const uint8_t* src =
-            head_base + static_cast<int64_t>(blk[gi]) * p.block_stride + static_cast<int64_t>(inb[gi]) * CELL;
-        bulk_g2s(dst + gi * 16 * CELL, src, static_cast<uint32_t>(run * 16 * CELL), &bars[stage]);
+    if (lane == 0) {
+      if (blk >= 0) {
+        mbar_arrive_expect_tx(&bars[stage], static_cast<uint32_t>(16 * CELL));
+        bulk_g2s(stages + stage * SM::STAGE_BYTES + warp * 16 * CELL,
+                 head_base + static_cast<int64_t>(blk) * p.block_stride + static_cast<int64_t>(inb) * CELL,
+                 static_cast<uint32_t>(16 * CELL), &bars[stage]);
+      } else {
+        mbar_arrive(&bars[stage]);
       }
     }
   };
 
   if (tid == 0) {
-    for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&bars[s], 4);
+    mbar_init(&bars[DEC_STAGES], 1);
     fence_mbar_init();
   }
   __syncthreads();
-  int issued = 0;                        // tiles whose copies thread 0 has issued
-  int next_blk[4] = {}, next_inb[4] = {};  // block-table entries of tile `issued` (thread 0)
-  if (tid == 0) {
-    nb_idx = tile0 * DEC_TILE / p.block_size;
-    nb_off = tile0 * DEC_TILE - nb_idx * p.block_size;
-    issued = min(ntl, DEC_STAGES);
-    for (int i = 0; i < issued; ++i) {
-      int blk[4], inb[4];
-      load_blocks(i, blk, inb);
-      issue_tile(i, blk, inb);
-    }
-    if (issued < ntl) load_blocks(issued, next_blk, next_inb);
+  const int issued0 = min(ntl, DEC_STAGES);
+  int issued = issued0;          // tiles whose copies every warp has issued
+  int next_blk = -1, next_inb = 0;  // this warp's group of tile `issued`
+  for (int i = 0; i < issued0; ++i) {
+    int blk, inb;
+    group_block(i, blk, inb);
+    issue_group(i, blk, inb);
   }
+  group_block(issued, next_blk, next_inb);
 
-  // --- Q: rotate, scale to fp16 with a per-row power of two, permute channels ------------------------------
-  {
-    using EL = Elem<DT>;
-    for (int r = warp; r < ROWS; r += 4) {
-      __half* qrow = reinterpret_cast<__half*>(qsm + r * Q_STRIDE);
-      if (r >= rows) {
-        for (int c = lane; c < DEC_HS; c += 32) qrow[c] = __float2half_rn(0.f);
-        if (lane == 0) {
-          row_qscale[r] = 0.f;
-          row_cq[r] = 0.f;
-          row_qsum[r] = 0.f;
-        }
-        continue;
-      }
-      const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
-      const typename EL::T* src = reinterpret_cast<const typename EL::T*>(p.q) + tok * p.q_st + qh * p.q_sh + lane * 8;
-      float x[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = EL::to_f(src[i]);
-      if (!p.q_rotated) {
-        apply_signs<8>(x, p.sign_bits, lane);
-        warp_wht<8>(x, lane);
-      }
-      float am = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(x[i]));
-      am = warp_max(am);
-      int ex = 0;
-      if (am > 0.f) {
-        frexpf(am, &ex);  // am < 2^ex
-        ex = 14 - ex;     // am * 2^ex in [2^13, 2^14)
-      }
-      float cq = 0.f, qs = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int c = lane * 8 + i;
-        const __half h = __float2half_rn(ldexpf(x[i], ex));
-        const float hv = __half2float(h);
-        qs += hv;
-        if constexpr (FMT == FMT_INT4) {
-          const bool odd = c & 1;
-          cq += odd ? 64.f * hv : 1024.f * hv;
-          qrow[qk_k_of_channel<FMT>(c)] = odd ? __float2half_rn(hv * 0.0625f) : h;
-        } else {
-          cq += 1152.f * hv;
-          qrow[qk_k_of_channel<FMT>(c)] = h;
-        }
-      }
-      cq = warp_sum(cq);
-      qs = warp_sum(qs);
-      if (lane == 0) {
-        row_qscale[r] = ldexpf(p.qk_scale, -ex);
-        row_cq[r] = cq;
-        row_qsum[r] = qs;
-      }
-    }
+  // --- Q rows: prepared by K0q (programmatic dependent launch: wait for it only now) --------------------------
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (tid == 0) {
+    const uint8_t* src = p.qrec + ((static_cast<int64_t>(kvh) * p.num_tokens + q0) * p.group) * Q_STRIDE;
+    mbar_arrive_expect_tx(&bars[DEC_STAGES], static_cast<uint32_t>(rows * Q_STRIDE));
+    bulk_g2s(qsm, src, static_cast<uint32_t>(rows * Q_STRIDE), &bars[DEC_STAGES]);
   }
+  for (int idx = rows * (Q_STRIDE / 16) + tid; idx < ROWS * (Q_STRIDE / 16); idx += DEC_THREADS)
+    reinterpret_cast<uint4*>(qsm)[idx] = make_uint4(0u, 0u, 0u, 0u);  // padding rows: zero
+  bool failed = !mbar_wait_bounded(&bars[DEC_STAGES], 0);
   __syncthreads();
 
   // --- per-thread state: this thread's query rows are r = 8 nt + 2 t + e ------------------------------------
@@ -308,10 +307,10 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const int r = 8 * nt + 2 * t + e;
-      qsc[nt][e] = row_qscale[r];
-      qcq[nt][e] = row_cq[r];
-      qsum[nt][e] = row_qsum[r];
+      const float* rc = reinterpret_cast<const float*>(qsm + (8 * nt + 2 * t + e) * Q_STRIDE + 2 * DEC_HS);
+      qsc[nt][e] = rc[0];
+      qcq[nt][e] = rc[1];
+      qsum[nt][e] = rc[2];
     }
   float o[4][NT][4];
 #pragma unroll
@@ -338,7 +337,6 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
   const uint32_t qsm_base = smem_u32(qsm);
   const int tau_a = 16 * warp + g, tau_b = tau_a + 8;
   const int pk_a = pv_k_of_token(tau_a) * PSTRIDE, pk_b = pv_k_of_token(tau_b) * PSTRIDE;
-  bool failed = false;
   int fail_tile = ntl;
 
   for (int i = 0; i < ntl; ++i) {
@@ -559,11 +557,11 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
 #pragma unroll
       for (int e = 0; e < 2; ++e) l_part[nt][e] += psum[nt][e];
 
-    // the stage is free: refill it with tile i + DEC_STAGES
-    if (tid == 0 && issued < ntl) {
-      issue_tile(issued, next_blk, next_inb);  // issued == i + DEC_STAGES
+    // the stage is free: every warp refills its group with tile i + DEC_STAGES
+    if (issued < ntl) {
+      issue_group(issued, next_blk, next_inb);  // issued == i + DEC_STAGES
       ++issued;
-      if (issued < ntl) load_blocks(issued, next_blk, next_inb);
+      group_block(issued, next_blk, next_inb);
     }
 
     // ---------------- PV: warp handles channels 64 warp + [0, 64) ----------------
@@ -619,6 +617,7 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
     if (tid == 0) {
       for (int j = fail_tile; j < issued; ++j)
         mbar_wait_bounded(&bars[j % DEC_STAGES], (j / DEC_STAGES) & 1, 100000000ull);
+      mbar_wait_bounded(&bars[DEC_STAGES], 0, 100000000ull);
     }
     __syncthreads();
     return;
@@ -824,9 +823,21 @@ static int launch_decode_t(const DecodeParams& dp, int num_seqs, cudaStream_t st
     if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode smem attribute: %s", cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  const dim3 grid(static_cast<unsigned>(dp.num_splits), static_cast<unsigned>(dp.nkv), static_cast<unsigned>(num_seqs));
-  decode_kernel<FMT, DT, NT><<<grid, DEC_THREADS, SM::BYTES, st>>>(dp);
-  return check_launch("decode");
+  // programmatic dependent launch: the CTAs start their cache copies while K0q finishes (they wait for it before
+  // reading the query rows)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(dp.num_splits), static_cast<unsigned>(dp.nkv), static_cast<unsigned>(num_seqs));
+  cfg.blockDim = dim3(DEC_THREADS);
+  cfg.dynamicSmemBytes = SM::BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<FMT, DT, NT>, dp);
+  if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
+  return QP_OK;
 }
 
 template <int FMT, int DT>
@@ -864,9 +875,16 @@ extern "C" int qp_decode_num_splits(int num_seqs, int num_kv_heads, int max_seql
   return best;
 }
 
-extern "C" int64_t qp_decode_workspace_bytes(int64_t num_q_tokens, int num_q_heads, int head_size, int num_splits) {
+// Workspace of qp_paged_decode: [part_o rows x head fp32][part_lse rows fp32, 256-aligned][prepared query rows
+// tokens x q heads x Q_STRIDE bytes], rows = tokens x q heads x splits.
+static int64_t decode_qrec_offset(int64_t num_q_tokens, int num_q_heads, int head_size, int num_splits) {
   const int64_t rows = num_q_tokens * num_q_heads * static_cast<int64_t>(num_splits);
   return rows * head_size * 4 + ((rows * 4 + 255) / 256) * 256;
+}
+
+extern "C" int64_t qp_decode_workspace_bytes(int64_t num_q_tokens, int num_q_heads, int head_size, int num_splits) {
+  return decode_qrec_offset(num_q_tokens, num_q_heads, head_size, num_splits) +
+         num_q_tokens * num_q_heads * static_cast<int64_t>(Q_STRIDE);
 }
 
 extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head,
@@ -932,6 +950,9 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
   dp.qk_scale = softmax_scale / static_cast<float>(head_size) * LOG2E;
   dp.sign_bits = rht_sign_bits;
   dp.q_rotated = q_rotated;
+  dp.qrec = static_cast<const uint8_t*>(workspace) +
+            decode_qrec_offset(num_q_tokens, num_q_heads, head_size, num_splits);
+  dp.num_tokens = num_q_tokens;
   dp.tokens_after = tokens_after_keys < max_seqlen_q ? tokens_after_keys : max_seqlen_q;  // >= qlen - 1: no mask
   dp.num_splits = num_splits;
   const int64_t rows = num_q_tokens * num_q_heads * static_cast<int64_t>(num_splits);
@@ -940,6 +961,23 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
 
   const int nt = (max_seqlen_q * group + 7) / 8;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  {
+    uint8_t* qrec = const_cast<uint8_t*>(dp.qrec);
+    const int64_t qrows = num_q_tokens * num_q_heads;
+    if ((qrows + 7) / 8 > 0x7fffffff) return set_error(QP_ERR_UNSUPPORTED, "decode: too many query rows");
+    const unsigned qgrid = static_cast<unsigned>((qrows + 7) / 8);
+#define QP_DQPREP(F, D)                                                                                      \
+  decode_qprep_kernel<F, D><<<qgrid, 256, 0, st>>>(q, q_stride_token, q_stride_head, num_q_tokens, num_q_heads, \
+                                                   num_kv_heads, rht_sign_bits, q_rotated, dp.qk_scale, qrec)
+    if (fmt == FMT_INT4) {
+      if (dtype == DT_BF16) QP_DQPREP(FMT_INT4, DT_BF16); else QP_DQPREP(FMT_INT4, DT_F16);
+    } else {
+      if (dtype == DT_BF16) QP_DQPREP(FMT_K8V4, DT_BF16); else QP_DQPREP(FMT_K8V4, DT_F16);
+    }
+#undef QP_DQPREP
+    const int rc0 = check_launch("decode q prep");
+    if (rc0) return rc0;
+  }
   int rc;
   if (fmt == FMT_INT4)
     rc = dtype == DT_BF16 ? launch_decode_nt<FMT_INT4, DT_BF16>(dp, nt, num_seqs, st)
