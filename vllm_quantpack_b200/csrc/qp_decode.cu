@@ -247,20 +247,22 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
   const uint8_t* head_base = p.cache + static_cast<int64_t>(kvh) * p.head_stride;
 
   // --- copies: warp w copies 16-token group w of every tile (block_size % 16 == 0, so a group never crosses a block),
-  // one bulk copy each, arriving with its byte count on the tile's stage barrier (4 arrivals per phase); the block
-  // of the group is loaded one tile ahead.
-  auto group_block = [&](int i, int& blk, int& inb) {
-    const int tok = (tile0 + i) * DEC_TILE + 16 * warp;
-    blk = -1;
-    inb = 0;
-    if (i < ntl && tok < n) {
-      const int bi = tok / p.block_size;
-      inb = tok - bi * p.block_size;
-      blk = __ldg(btab + bi);
+  // one bulk copy each, arriving with its byte count on the tile's stage barrier (4 arrivals per phase). The group's
+  // block-table index and in-block offset advance by one tile at a time (no division in the loop); its block entry
+  // is loaded one tile ahead.
+  int gb_tok = tile0 * DEC_TILE + 16 * warp;  // first token of this warp's group of the tile to fetch next
+  int gb_idx = gb_tok / p.block_size;
+  int gb_off = gb_tok - gb_idx * p.block_size;
+  auto advance_group = [&]() {
+    gb_tok += DEC_TILE;
+    gb_off += DEC_TILE;
+    while (gb_off >= p.block_size) {
+      gb_off -= p.block_size;
+      ++gb_idx;
     }
   };
-  auto issue_group = [&](int i, int blk, int inb) {
-    const int stage = i % DEC_STAGES;
+  auto fetch_block = [&](int i) { return (i < ntl && gb_tok < n) ? __ldg(btab + gb_idx) : -1; };
+  auto issue_group = [&](int stage, int blk, int inb) {
     if (lane == 0) {
       if (blk >= 0) {
         mbar_arrive_expect_tx(&bars[stage], static_cast<uint32_t>(16 * CELL));
@@ -280,14 +282,20 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
   }
   __syncthreads();
   const int issued0 = min(ntl, DEC_STAGES);
-  int issued = issued0;          // tiles whose copies every warp has issued
-  int next_blk = -1, next_inb = 0;  // this warp's group of tile `issued`
-  for (int i = 0; i < issued0; ++i) {
-    int blk, inb;
-    group_block(i, blk, inb);
-    issue_group(i, blk, inb);
+  int issued = issued0;  // tiles whose copies every warp has issued
+  {
+    int blk[DEC_STAGES], off[DEC_STAGES];
+#pragma unroll
+    for (int i = 0; i < DEC_STAGES; ++i) {
+      blk[i] = fetch_block(i);
+      off[i] = gb_off;
+      advance_group();
+    }
+#pragma unroll
+    for (int i = 0; i < DEC_STAGES; ++i)
+      if (i < issued0) issue_group(i, blk[i], off[i]);
   }
-  group_block(issued, next_blk, next_inb);
+  int next_blk = fetch_block(issued), next_inb = gb_off;  // this warp's group of tile `issued`
 
   // --- Q rows: prepared by K0q (programmatic dependent launch: wait for it only now) --------------------------
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -339,15 +347,16 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
   const int pk_a = pv_k_of_token(tau_a) * PSTRIDE, pk_b = pv_k_of_token(tau_b) * PSTRIDE;
   int fail_tile = ntl;
 
+  int stage = 0;         // i % DEC_STAGES
+  uint32_t sphase = 0;   // (i / DEC_STAGES) & 1
   for (int i = 0; i < ntl; ++i) {
-    const int stage = i % DEC_STAGES;
     const int buf = i & 1;
     uint8_t* psm = smem + SM::OFF_P + buf * SM::P_BYTES;
     uint16_t* zb_lo = zbuf + buf * 2 * DEC_TILE;
     uint16_t* zb_hi = zb_lo + DEC_TILE;
     // A thread whose wait runs out keeps going on whatever the stage holds (nothing reaches global memory before
     // the epilogue); the CTA leaves together at barrier (B), so no thread skips a __syncthreads.
-    failed |= !mbar_wait_bounded(&bars[stage], (i / DEC_STAGES) & 1);
+    failed |= !mbar_wait_bounded(&bars[stage], sphase);
     const uint8_t* tile = stages + stage * SM::STAGE_BYTES;
     const int tok_base = (tile0 + i) * DEC_TILE;
 
@@ -559,9 +568,15 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
 
     // the stage is free: every warp refills its group with tile i + DEC_STAGES
     if (issued < ntl) {
-      issue_group(issued, next_blk, next_inb);  // issued == i + DEC_STAGES
+      issue_group(stage, next_blk, next_inb);  // issued == i + DEC_STAGES: the stage of this tile
+      advance_group();
       ++issued;
-      group_block(issued, next_blk, next_inb);
+      next_blk = fetch_block(issued);
+      next_inb = gb_off;
+    }
+    if (++stage == DEC_STAGES) {
+      stage = 0;
+      sphase ^= 1u;
     }
 
     // ---------------- PV: warp handles channels 64 warp + [0, 64) ----------------
