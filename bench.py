@@ -196,17 +196,24 @@ def timed_steps(torch, fn, steps, warmup, flush):
 
 def cpu_sample(w, budget_s=15.0):
     """Time the CPU oracle (fp64 attention from the cache bytes, all host threads for the BLAS part) on a bounded
-    sample of the workload: the same head shape and query tokens over a shorter context, scaled to the full context
-    (the work is linear in the context). Returns (tokens/s at the full context, sample description, threads)."""
+    sample of the workload: the same head shape over a 16,384-token context, scaled to the full workload by the
+    number of (query, key) pairs (the work is linear in them). A decode sample keeps the workload's query tokens; a
+    prefill chunk is sampled by 16 query tokens. Returns (tokens/s of the full workload, sample description,
+    threads)."""
     from oracle import quantpack_oracle as qo
     ctx = 16384
+    qlen = 16 if w.get("prefill") else w["qlen"]
+
+    def pairs(q, n):  # (query, key) pairs of q queries that are the last q positions of an n-token context
+        return q * (n - q) + q * (q + 1) // 2
+
     fmt = w["fmt"]
     layout = qo.CacheLayout(fmt, ctx // BS, NKV, BS, HS)
     cache = np.zeros(layout.nbytes, dtype=np.uint8)
     kb, vb = qo.synthetic_kv(ctx, NKV, HS, seed=0)
     qo.store(fmt, kb, vb, np.arange(ctx), cache, layout, qo.rht_signs(HS))
     table = np.arange(ctx // BS)
-    q = qo.f32_to_bf16(np.random.default_rng(1).standard_normal((w["qlen"], NQ, HS)).astype(np.float32))
+    q = qo.f32_to_bf16(np.random.default_rng(1).standard_normal((qlen, NQ, HS)).astype(np.float32))
     signs = qo.rht_signs(HS)
     reps, t0 = 0, time.perf_counter()
     while True:
@@ -217,10 +224,12 @@ def cpu_sample(w, budget_s=15.0):
         el = time.perf_counter() - t0
         if el > budget_s or reps >= 50:
             break
-    per_call_full = el / reps * (w["ctx"] / ctx) * w["seqs"]
+    scale = w["seqs"] * pairs(w["qlen"], w["ctx"]) / pairs(qlen, ctx)
+    per_call_full = el / reps * scale
     tok_s = w["seqs"] * w["qlen"] / per_call_full
-    return tok_s, f"{reps} calls of 1 request x {w['qlen']} tokens over a {ctx}-token context, scaled x{w['ctx'] // ctx}" \
-                  f" to {w['ctx']}" + (f" and x{w['seqs']} requests" if w["seqs"] > 1 else ""), os.cpu_count()
+    desc = (f"{reps} calls of 1 request x {qlen} query tokens over a {ctx}-token context, scaled x{scale:.1f} by "
+            f"(query, key) pairs to {w['seqs']} x {w['qlen']} tokens over {w['ctx']}")
+    return tok_s, desc, os.cpu_count()
 
 
 def run_reference(args, w, rank, world):
@@ -234,7 +243,7 @@ def run_reference(args, w, rank, world):
         v, desc, cores = cpu_sample(w, budget_s=max(2.0, 20.0 / max(1, args.steps)))
         steps.append(v)
     value = statistics.median(steps)
-    line = {"impl": "reference", "metric": "decode_tok_s", "value": value, "unit": "tok/s", "n_gpus": world,
+    line = {"impl": "reference", "metric": "prefill_tok_s" if w.get("prefill") else "decode_tok_s", "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * w["qlen"] * w["seqs"] / value,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
             "config": {"workload": args.workload, **w, "nq": NQ, "nkv": NKV, "head_size": HS, "block_size": BS},
@@ -286,6 +295,10 @@ def run_prefill(args, w, rank, world, local_rank):
     except Exception:
         peak, kind = 1590.0, "fallback"
     achieved = flops / (ms * 1e-3) / 1e12
+    cpu = None
+    if not args.no_cpu:
+        v, desc, cores = cpu_sample(w)
+        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
     line = {"metric": "prefill_tok_s", "value": w["qlen"] / (ms * 1e-3), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int4+f16", "data": "synthetic",
@@ -296,6 +309,7 @@ def run_prefill(args, w, rank, world, local_rank):
                          "traffic_unit": "bytes per launch (ncu dram__bytes_read + write)",
                          "kernel": "prefill_kernel (q prep + merge included)",
                          "algorithmic_flops_per_launch": flops, "peak_kind": kind},
+            "cpu_baseline": cpu,
             "e2e": {"value": w["qlen"] / (ms_e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": q.numel() * 2,
                     "d2h_bytes_per_step": out.numel() * 2},
             "gpu_launches": 3 * args.steps, "clocks": clk.summary(), "device_error": dev_err}
