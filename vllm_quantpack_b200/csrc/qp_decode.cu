@@ -9,7 +9,7 @@
 // out += P_v16 u - sum(P_v16 zp) with the same rounded P_v16 in both terms (int4_kv.py:80-94).
 //
 // B200 design:
-// - one CTA (4 warps) per (split, KV head, sequence); the segment's cells stream through a 3-stage shared-memory
+// - one CTA (4 warps) per (split, KV head, sequence); the segment's cells stream through a 2-stage shared-memory
 //   ring filled by 1-D bulk copies (TMA engine), each warp copying its own 16-token group of a tile, completing on
 //   mbarriers;
 // - K0q (a small kernel before K1) rotates (RHT) and scales every query row once into fp16 with a per-row power of
@@ -36,7 +36,7 @@
 namespace qp {
 
 constexpr int DEC_TILE = 64;
-constexpr int DEC_STAGES = 3;
+constexpr int DEC_STAGES = 2;
 constexpr int DEC_THREADS = 128;
 constexpr int DEC_HS = 256;
 constexpr int DEC_MAX_ROWS = 32;

@@ -22,8 +22,9 @@
 //   warps 6-9   softmax: one thread per TMEM lane (= query row); at the start of each piece it stores its row of the
 //               prepared Q tile into TMEM (columns 128-255). Scores in log2 units = S x (softmax_scale / head x
 //               log2 e x 2^-row exponent x 2^key-tile exponent); the running maximum is lazy and per thread (P may
-//               reach 2^8 before O is rescaled in TMEM, which is rare); P in fp16 is written K-major as the A operand
-//               of the PV MMA. The epilogue reads O from TMEM and writes fp32 partials + base-2 lse.
+//               reach 2^8 before O is rescaled in TMEM, which is rare); P in fp16 is stored back into TMEM over the
+//               S buffer it came from, as the A operand of the PV MMA (no shared-memory round trip). The epilogue
+//               reads O from TMEM and writes fp32 partials + base-2 lse.
 // Rows of an M-tile are (query token, query head of the KV head's group) pairs, head fastest: the 6 heads of a group
 // share every dequantised key / value tile. The (M-tile, key-tile) space is split evenly over the CTAs (stream-K):
 // an M-tile may be finished by two CTAs, whose partials the merge kernel folds (with the inverse RHT).
@@ -47,13 +48,12 @@ template <int FMT>
 struct PfCfg {
   static constexpr int CELL = FMT == FMT_INT4 ? PF_HS + 8 : PF_HS * 3 / 2 + 8;
   static constexpr int KB = FMT == FMT_INT4 ? PF_HS / 2 : PF_HS;  // key bytes in a cell
-  static constexpr int RS = FMT == FMT_INT4 ? 3 : 2;               // raw stages
+  static constexpr int RS = FMT == FMT_INT4 ? 4 : 3;               // raw stages
   static constexpr int RAW_BYTES = PF_BN * CELL;
-  // shared memory map (operand tiles 1024-byte aligned for the 128B swizzle); Q lives in TMEM
+  // shared memory map (operand tiles 1024-byte aligned for the 128B swizzle); Q, S, P and O live in TMEM
   static constexpr int OFF_K = 0;                       // 2 buffers x 4 K-blocks x 64 keys x 128 B = 64 KB
   static constexpr int OFF_V = OFF_K + 65536;           // 2 buffers x 4 N-blocks x 8 key groups x 1024 B = 64 KB
-  static constexpr int OFF_P = OFF_V + 65536;           // 2 buffers x 128 rows x 128 B = 32 KB
-  static constexpr int OFF_RAW = OFF_P + 32768;         // RS x RAW_BYTES
+  static constexpr int OFF_RAW = OFF_V + 65536;         // RS x RAW_BYTES
   static constexpr int OFF_SC = OFF_RAW + RS * RAW_BYTES;  // [2 buffers][key factor 2^F, value exponent E] (16 B)
   static constexpr int OFF_XCH = OFF_SC + 2 * 16;          // [k / v][2 buffers][2 warps] tile maxima exchange
   static constexpr int OFF_BAR = OFF_XCH + 2 * 2 * 2 * 4;
@@ -72,9 +72,7 @@ enum {
   B_V_FULL = 14,     // [2] value operand buffers
   B_V_FREE = 16,     // [2]
   B_S_FULL = 18,     // [2]
-  B_S_FREE = 20,     // [2]
-  B_P_FULL = 22,     // [2]
-  B_P_FREE = 24,     // [2]
+  B_P_FULL = 22,     // [2] P of the tile stored in TMEM over its S buffer (the softmax is done with that S)
   B_SC_FULL = 26,    // [2]
   B_SC_FREE = 28,    // [2]
   B_O_DONE = 30,
@@ -398,9 +396,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       mbar_init(&bars[B_V_FULL + b], 2);
       mbar_init(&bars[B_V_FREE + b], 1);
       mbar_init(&bars[B_S_FULL + b], 1);
-      mbar_init(&bars[B_S_FREE + b], 4);
       mbar_init(&bars[B_P_FULL + b], 4);
-      mbar_init(&bars[B_P_FREE + b], 1);
       mbar_init(&bars[B_SC_FULL + b], 4);
       mbar_init(&bars[B_SC_FREE + b], 4);
     }
@@ -417,7 +413,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tm_s[2] = {tmem, tmem + 64};  // S buffers: columns [0, 64), [64, 128)
+  // S buffers: columns [0, 64), [64, 128); P of a tile (fp16 pairs) is stored over the first 32 columns of its S
+  // buffer as the A operand of the PV MMA (no shared-memory round trip)
+  const uint32_t tm_s[2] = {tmem, tmem + 64};
   const uint32_t tm_q = tmem + 128;            // Q (A operand of S = Q K^T): columns [128, 256)
   const uint32_t tm_o = tmem + 256;            // O: columns [256, 512)
 
@@ -459,7 +457,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       constexpr uint32_t ID_QK = f16_idesc(PF_BM, PF_BN, false);
       constexpr uint32_t ID_PV = f16_idesc(PF_BM, PF_HS, true);
       const uint32_t k_base = smem_u32(smem + C::OFF_K), v_base = smem_u32(smem + C::OFF_V);
-      const uint32_t p_base = smem_u32(smem + C::OFF_P);
       int64_t j = 0;
       int qcount = 0, pieces = 0;
       int64_t pv_pending = -1;  // tile whose PV is still to be issued
@@ -470,12 +467,13 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         failed |= !mbar_wait_bounded(&bars[B_P_FULL + b], (t >> 1) & 1);
         tc_fence_after();
         const uint32_t vb = v_base + b * 32768;
+        // P(t) in TMEM, K step s (16 keys) = 8 columns; S(t + 2) overwrites these columns with MMAs issued after
+        // these (the tcgen05.mma of one thread execute in issue order)
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          umma_f16(tm_o, sw128_desc(p_base + b * 16384 + s * 32, 16, 1024), sw128_desc(vb + 2 * s * 1024, 8192, 1024),
-                   ID_PV, (first && s == 0) ? 0u : 1u);
+          umma_f16_ts(tm_o, tm_s[b] + 8 * s, sw128_desc(vb + 2 * s * 1024, 8192, 1024), ID_PV,
+                      (first && s == 0) ? 0u : 1u);
         umma_commit(&bars[B_V_FREE + b]);
-        umma_commit(&bars[B_P_FREE + b]);
         umma_commit(&bars[B_O_DONE]);
       };
       for (; !sch.done() && !failed; sch.next(), ++j) {
@@ -487,7 +485,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         // S(j) = Q K(j)^T
         const int b = static_cast<int>(j & 1);
         failed |= !mbar_wait_bounded(&bars[B_K_FULL + b], (j >> 1) & 1);
-        if (j >= 2) failed |= !mbar_wait_bounded(&bars[B_S_FREE + b], ((j >> 1) - 1) & 1);
+        // S buffer b last held S(j - 2) and P(j - 2): the PV of that tile, issued before these MMAs, waited for the
+        // softmax to finish with it
         tc_fence_after();
         const uint32_t kb = k_base + b * 32768;
 #pragma unroll
@@ -660,8 +659,14 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // TMEM lane = M-tile row
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    uint8_t* p_tile = smem + C::OFF_P;
     int64_t j = 0;
+    // PV completions seen so far. O_DONE completes one phase per tile (its PV); a parity wait is exact only while
+    // the barrier is at most one phase ahead of the phase waited for, so the phases are consumed in order: PV(j - 1)
+    // before P(j) is stored (S_FULL(j) already implies PV(j - 2)), PV(j) in the epilogue.
+    int64_t pv_seen = 0;
+    auto wait_pv = [&](int64_t t) {  // until PV(t) is complete
+      for (; pv_seen <= t; ++pv_seen) failed |= !mbar_wait_bounded(&bars[B_O_DONE], static_cast<uint32_t>(pv_seen & 1));
+    };
     float m_used = -INFINITY, l = 0.f, qsc = 0.f;
     int e_used = -1000, lim = -1, tok = 0, qh = 0;
     bool row_ok = false;
@@ -709,9 +714,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       tc_fence_after();
       float s[64];
       tmem_ld64(tm_s[b] + lane_off, s);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[B_S_FREE + b]);
       failed |= !mbar_wait_bounded(&bars[B_SC_FULL + b], (j >> 1) & 1);
       const float* scb = reinterpret_cast<const float*>(smem + C::OFF_SC) + b * 4;
       const float qs_t = qsc * scb[0];               // x 2^F of the key operand
@@ -738,7 +740,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         const float o_range = e_used == -1000 ? 0.f : ldexpf(1.f, e_used - ev);
         const float ao = alpha * o_range;
         if (t_in_piece > 0) {
-          failed |= !mbar_wait_bounded(&bars[B_O_DONE], (j - 1) & 1);
+          wait_pv(j - 1);
           tc_fence_after();
 #pragma unroll 1
           for (int c0 = 0; c0 < PF_HS; c0 += 32) {
@@ -777,13 +779,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         }
       }
       l += lsum;
-      if (j >= 2) failed |= !mbar_wait_bounded(&bars[B_P_FREE + b], ((j >> 1) - 1) & 1);
-      uint8_t* prow = p_tile + b * 16384;
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        *reinterpret_cast<uint4*>(prow + sw128_off(row, ch)) =
-            make_uint4(pw[4 * ch], pw[4 * ch + 1], pw[4 * ch + 2], pw[4 * ch + 3]);
-      fence_async_smem();
+      wait_pv(j - 1);
+      // P -> TMEM over the first 32 columns of this tile's S buffer: the A operand of its PV MMA
+      tmem_st32u(tm_s[b] + lane_off, pw);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_P_FULL + b]);
@@ -791,7 +790,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
 
       if (w.last_of_piece) {
         // epilogue: O of this piece -> normalised fp32 partial (channel order restored) + base-2 lse
-        failed |= !mbar_wait_bounded(&bars[B_O_DONE], j & 1);
+        wait_pv(j);
         tc_fence_after();
         const float o_unit = e_used == -1000 ? 0.f : ldexpf(1.f, e_used);
         const float inv = l > 0.f ? o_unit / l : 0.f;
