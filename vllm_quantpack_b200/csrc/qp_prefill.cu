@@ -40,7 +40,7 @@ namespace qp {
 constexpr int PF_HS = 256;
 constexpr int PF_BM = 128;  // query rows per M-tile (TMEM lanes)
 constexpr int PF_BN = 64;   // keys per tile
-constexpr int PF_THREADS = 320;
+constexpr int PF_THREADS = 448;  // 14 warps: producer, MMA, 4 dequant, 8 softmax
 constexpr float PF_SLACK = 8.f;
 constexpr float PF_LOG2E = 1.4426950408889634f;
 
@@ -56,7 +56,9 @@ struct PfCfg {
   static constexpr int OFF_RAW = OFF_V + 65536;         // RS x RAW_BYTES
   static constexpr int OFF_SC = OFF_RAW + RS * RAW_BYTES;  // [2 buffers][key factor 2^F, value exponent E] (16 B)
   static constexpr int OFF_XCH = OFF_SC + 2 * 16;          // [k / v][2 buffers][2 warps] tile maxima exchange
-  static constexpr int OFF_BAR = OFF_XCH + 2 * 2 * 2 * 4;
+  static constexpr int OFF_HX = OFF_XCH + 2 * 2 * 2 * 4;  // softmax pairs: [2 buffers][2 halves][128] row maxima,
+                                                         // then [2 halves][128] row sums
+  static constexpr int OFF_BAR = OFF_HX + (2 * 2 * 128 + 2 * 128) * 4;
   static constexpr int NBAR = 40;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_TMEM + 16;
@@ -205,6 +207,14 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[3
       "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
       "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
       "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
 }
 
@@ -389,19 +399,19 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       mbar_init(&bars[B_RAW_FULL + s], 1);
       mbar_init(&bars[B_RAW_EMPTY + s], 4);
     }
-    mbar_init(&bars[B_Q_FULL], 4);
+    mbar_init(&bars[B_Q_FULL], 8);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars[B_K_FULL + b], 2);
       mbar_init(&bars[B_K_FREE + b], 1);
       mbar_init(&bars[B_V_FULL + b], 2);
       mbar_init(&bars[B_V_FREE + b], 1);
       mbar_init(&bars[B_S_FULL + b], 1);
-      mbar_init(&bars[B_P_FULL + b], 4);
+      mbar_init(&bars[B_P_FULL + b], 8);
       mbar_init(&bars[B_SC_FULL + b], 4);
-      mbar_init(&bars[B_SC_FREE + b], 4);
+      mbar_init(&bars[B_SC_FREE + b], 8);
     }
     mbar_init(&bars[B_O_DONE], 1);
-    mbar_init(&bars[B_O_FREE], 4);
+    mbar_init(&bars[B_O_FREE], 8);
     mbar_init(&bars[B_FINAL], 1);
     fence_mbar_init();
   }
@@ -655,10 +665,17 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       if (lane == 0) mbar_arrive(&bars[B_RAW_EMPTY + stage]);
     }
   } else {
-    // ------------------------------------------------------------------ softmax / epilogue (warps 6..9)
+    // ------------------------------------------------------------------ softmax / epilogue (warps 6..13)
+    // Two warps per TMEM lane quarter (32 query rows): warps 6-9 take keys 0-31 of every tile and channels 0-127 of
+    // O, warps 10-13 keys 32-63 and channels 128-255. The two threads of a row agree on its maximum through shared
+    // memory (a named barrier per pair of warps) and add their partial sums in the epilogue.
     const int quarter = warp & 3;
+    const int half = (warp - 6) >> 2;
     const int row = quarter * 32 + lane;  // TMEM lane = M-tile row
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const int pair_bar = 3 + quarter;     // named barriers 1, 2: dequant pairs
+    float* hmax = reinterpret_cast<float*>(smem + C::OFF_HX);  // [buffer][half][row]
+    float* hsum = hmax + 2 * 2 * 128;                              // [half][row]
     int64_t j = 0;
     // PV completions seen so far. O_DONE completes one phase per tile (its PV); a parity wait is exact only while
     // the barrier is at most one phase ahead of the phase waited for, so the phases are consumed in order: PV(j - 1)
@@ -675,12 +692,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       const Walk w = sch.current();
       const int b = static_cast<int>(j & 1);
       if (w.new_mtile) {
-        // this row of the piece's Q tile -> TMEM columns [128, 256) of its lane (the previous piece's QKs are
-        // complete: this thread consumed the S of its last tile)
+        // this thread's half of its row of the piece's Q tile -> TMEM columns 128 + [64 half, 64 half + 64) of its
+        // lane (the previous piece's QKs are complete: this thread consumed the S of its last tile)
         const int64_t mt = static_cast<int64_t>(w.kvh) * p.mt_per_kv + w.m;
         const uint4* qrow = reinterpret_cast<const uint4*>(p.qprep + mt * 65536 + row * (PF_HS * 2));
 #pragma unroll 1
-        for (int c0 = 0; c0 < 128; c0 += 32) {
+        for (int c0 = 64 * half; c0 < 64 * half + 64; c0 += 32) {
           uint32_t qw[32];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -709,32 +726,39 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         e_used = -1000;
         t_in_piece = 0;
       }
-      // scores of this row for the tile's 64 keys
+      // this row's scores for keys 32 half .. 32 half + 31 of the tile
       failed |= !mbar_wait_bounded(&bars[B_S_FULL + b], (j >> 1) & 1);
       tc_fence_after();
-      float s[64];
-      tmem_ld64(tm_s[b] + lane_off, s);
+      float s[32];
+      tmem_ld32(tm_s[b] + lane_off + 32 * half, s);
       failed |= !mbar_wait_bounded(&bars[B_SC_FULL + b], (j >> 1) & 1);
       const float* scb = reinterpret_cast<const float*>(smem + C::OFF_SC) + b * 4;
       const float qs_t = qsc * scb[0];               // x 2^F of the key operand
       const int ev = __float_as_int(scb[1]);         // value exponent of this tile's operand
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_SC_FREE + b]);
-      const int key0 = w.kt * PF_BN;
-      const bool masked = key0 + PF_BN - 1 > min(p.n - 1, p.vis_base);  // some row cannot see some key here
+      const int key0 = w.kt * PF_BN + 32 * half;
+      const bool masked = w.kt * PF_BN + PF_BN - 1 > min(p.n - 1, p.vis_base);  // some row cannot see some key
       if (masked) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
+        for (int c = 0; c < 32; ++c)
           if (key0 + c > lim) s[c] = -INFINITY;
       }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) mx = fmaxf(mx, s[c]);
+      for (int c = 0; c < 32; ++c) mx = fmaxf(mx, s[c]);
+      hmax[(b * 2 + half) * 128 + row] = mx;
+      // the pair leaves together if either gave up a wait (a bar.sync has no time bound)
+      if (named_bar_or(pair_bar, 64, failed)) {
+        failed = true;
+        break;
+      }
+      mx = fmaxf(mx, hmax[(b * 2 + (half ^ 1)) * 128 + row]);
       const float mrow = mx * qs_t;
-      const bool grow = mrow > m_used + PF_SLACK;
-      const bool vgrow = ev > e_used;  // the same for every thread
+      const bool grow = mrow > m_used + PF_SLACK;  // the same in both threads of the row
+      const bool vgrow = ev > e_used;              // the same for every thread
       if (__any_sync(0xffffffffu, grow) || vgrow) {
-        // rescale this row's O in TMEM (after the previous PV of the piece completed)
+        // rescale this thread's half of the row's O in TMEM (after the previous PV of the piece completed)
         const float m_new = grow ? mrow : m_used;
         const float alpha = m_new == m_used ? 1.f : exp2f(m_used - m_new);
         const float o_range = e_used == -1000 ? 0.f : ldexpf(1.f, e_used - ev);
@@ -743,7 +767,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
           wait_pv(j - 1);
           tc_fence_after();
 #pragma unroll 1
-          for (int c0 = 0; c0 < PF_HS; c0 += 32) {
+          for (int c0 = 128 * half; c0 < 128 * half + 128; c0 += 32) {
             float o[32];
             tmem_ld32(tm_o + lane_off + c0, o);
 #pragma unroll
@@ -755,13 +779,13 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         m_used = m_new;
         e_used = ev;
       }
-      // P = 2^(s qs_t - m) <= 2^8 in fp16, K-major row of the PV A operand
+      // P = 2^(s qs_t - m) <= 2^8 in fp16
       const float base = m_used == -INFINITY ? 0.f : m_used;
       float lsum = 0.f;
-      uint32_t pw[32];
+      uint32_t pw[16];
       if (masked) {
 #pragma unroll
-        for (int c = 0; c < 64; c += 2) {
+        for (int c = 0; c < 32; c += 2) {
           const float p0 = s[c] == -INFINITY ? 0.f : fast_exp2(fmaf(s[c], qs_t, -base));
           const float p1 = s[c + 1] == -INFINITY ? 0.f : fast_exp2(fmaf(s[c + 1], qs_t, -base));
           lsum += p0 + p1;
@@ -770,7 +794,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < 64; c += 2) {
+        for (int c = 0; c < 32; c += 2) {
           const float p0 = fast_exp2(fmaf(s[c], qs_t, -base));
           const float p1 = fast_exp2(fmaf(s[c + 1], qs_t, -base));
           lsum += p0 + p1;
@@ -780,8 +804,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       }
       l += lsum;
       wait_pv(j - 1);
-      // P -> TMEM over the first 32 columns of this tile's S buffer: the A operand of its PV MMA
-      tmem_st32u(tm_s[b] + lane_off, pw);
+      // P -> TMEM over columns 16 half + [0, 16) of this tile's S buffer: the A operand of its PV MMA
+      tmem_st16u(tm_s[b] + lane_off + 16 * half, pw);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
@@ -790,13 +814,19 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
 
       if (w.last_of_piece) {
         // epilogue: O of this piece -> normalised fp32 partial (channel order restored) + base-2 lse
+        hsum[half * 128 + row] = l;
+        if (named_bar_or(pair_bar, 64, failed)) {
+          failed = true;
+          break;
+        }
+        const float l_row = l + hsum[(half ^ 1) * 128 + row];
         wait_pv(j);
         tc_fence_after();
         const float o_unit = e_used == -1000 ? 0.f : ldexpf(1.f, e_used);
-        const float inv = l > 0.f ? o_unit / l : 0.f;
+        const float inv = l_row > 0.f ? o_unit / l_row : 0.f;
         const int64_t prow_i = (static_cast<int64_t>(tok) * p.nq + qh) * p.parts + w.piece;
 #pragma unroll 1
-        for (int c0 = 0; c0 < PF_HS; c0 += 32) {
+        for (int c0 = 128 * half; c0 < 128 * half + 128; c0 += 32) {
           float o[32];
           tmem_ld32(tm_o + lane_off + c0, o);
           if (row_ok && w.piece < p.parts) {
@@ -809,7 +839,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
             }
           }
         }
-        if (row_ok && w.piece < p.parts) p.part_lse[prow_i] = l > 0.f ? m_used + log2f(l) : -INFINITY;
+        if (half == 0 && row_ok && w.piece < p.parts) p.part_lse[prow_i] = l_row > 0.f ? m_used + log2f(l_row) : -INFINITY;
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[B_O_FREE]);
