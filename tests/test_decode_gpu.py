@@ -144,3 +144,40 @@ def test_no_device_timeouts(device):
     from vllm_quantpack_b200 import _lib
     run_case(device, "int4", [4], [5000], 16)
     assert _lib.device_error() == 0
+
+
+def test_decode_step_in_cuda_graph(device):
+    """The decode path is graph-capturable (no host sync, preallocated workspace): a captured step replays to the
+    same output as a direct call, and a replay after new query values reflects them."""
+    from vllm_quantpack_b200.attention import ops
+    n, qlen = 8192, 4
+    table, nblocks = U.block_tables([n], 16)
+    cache = U.Cache("int4", nblocks, 16, device)
+    cache.fill(table[0], n, seed=2)
+    kc, vc, ks, vs = cache.views
+    q = U.to_torch(U.make_queries([qlen], seed=4), device)
+    out = torch.empty_like(q)
+    args = dict(cu_seqlens_q=torch.tensor([0, qlen], dtype=torch.int32, device=device), max_seqlen_q=qlen,
+                seqused_k=torch.tensor([n], dtype=torch.int32, device=device), max_seqlen_k=n,
+                softmax_scale=U.HS ** -0.5, block_table=torch.from_numpy(table).to(device), k_scale_cache=ks,
+                v_scale_cache=vs)
+    ops.paged_decode(q, kc, vc, out, **args)  # warm-up: workspace and sign vector allocated outside the capture
+    torch.cuda.synchronize()
+    ref = out.clone()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g):
+            ops.paged_decode(q, kc, vc, out, **args)
+    torch.cuda.current_stream().wait_stream(s)
+    out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    q.copy_(U.to_torch(U.make_queries([qlen], seed=5), device))
+    g.replay()
+    direct = torch.empty_like(out)
+    ops.paged_decode(q, kc, vc, direct, **args)
+    torch.cuda.synchronize()
+    assert torch.equal(out, direct) and not torch.equal(out, ref)
