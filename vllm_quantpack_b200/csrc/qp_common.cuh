@@ -114,6 +114,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return true;
 }
 
+// Same bound as mbar_wait_bounded, but polling without the suspend hint: for warp-specialised pipelines where every
+// hand-off sits on the critical path and the wake-up latency of a suspended waiter costs more than its issue slots.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > limit_ns) {
+      atomicCAS(&g_device_error, DEV_ERR_NONE, DEV_ERR_WAIT_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
 // 1-D bulk copy (TMA engine, no tensor map, no multicast) global -> this CTA's shared memory, completing on `bar`.
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

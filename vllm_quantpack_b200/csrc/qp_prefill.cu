@@ -310,7 +310,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       for (; !sch.done() && !failed; sch.next(), ++j) {
         const Walk w = sch.current();
         const int stage = static_cast<int>(j % C::RS);
-        if (j >= C::RS) failed |= !mbar_wait_bounded(&bars[B_RAW_EMPTY + stage], ((j / C::RS) - 1) & 1);
+        if (j >= C::RS) failed |= !mbar_wait_spin(&bars[B_RAW_EMPTY + stage], ((j / C::RS) - 1) & 1);
         const int tok_begin = w.kt * PF_BN;
         const int groups = (min(tok_begin + PF_BN, p.n) - tok_begin + 15) >> 4;
         mbar_arrive_expect_tx(&bars[B_RAW_FULL + stage], static_cast<uint32_t>(groups * 16 * C::CELL));
@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       }
       // the copies in flight land before the CTA's shared memory can go away
       for (int64_t k = (j > C::RS ? j - C::RS : 0); k < j; ++k)
-        mbar_wait_bounded(&bars[B_RAW_FULL + (k % C::RS)], (k / C::RS) & 1, 100000000ull);
+        mbar_wait_spin(&bars[B_RAW_FULL + (k % C::RS)], (k / C::RS) & 1, 100000000ull);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -343,8 +343,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       bool pv_first = false, pv_last = false;
       auto issue_pv = [&](int64_t t, bool first) {
         const int b = static_cast<int>(t & 1);
-        failed |= !mbar_wait_bounded(&bars[B_V_FULL + b], (t >> 1) & 1);
-        failed |= !mbar_wait_bounded(&bars[B_P_FULL + b], (t >> 1) & 1);
+        failed |= !mbar_wait_spin(&bars[B_V_FULL + b], (t >> 1) & 1);
+        failed |= !mbar_wait_spin(&bars[B_P_FULL + b], (t >> 1) & 1);
         tc_fence_after();
         const uint32_t vb = v_base + b * 32768;
         // P(t) in TMEM, K step s (16 keys) = 8 columns; S(t + 2) overwrites these columns with MMAs issued after
@@ -359,12 +359,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       for (; !sch.done() && !failed; sch.next(), ++j) {
         const Walk w = sch.current();
         if (w.new_mtile) {
-          failed |= !mbar_wait_bounded(&bars[B_Q_FULL], qcount & 1);
+          failed |= !mbar_wait_spin(&bars[B_Q_FULL], qcount & 1);
           ++qcount;
         }
         // S(j) = Q K(j)^T
         const int b = static_cast<int>(j & 1);
-        failed |= !mbar_wait_bounded(&bars[B_K_FULL + b], (j >> 1) & 1);
+        failed |= !mbar_wait_spin(&bars[B_K_FULL + b], (j >> 1) & 1);
         // S buffer b last held S(j - 2) and P(j - 2): the PV of that tile, issued before these MMAs, waited for the
         // softmax to finish with it
         tc_fence_after();
@@ -384,7 +384,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         }
         if (w.first_of_piece && pieces > 0) {
           // O is overwritten by this piece's first PV: the previous piece's epilogue must have read it
-          failed |= !mbar_wait_bounded(&bars[B_O_FREE], (pieces - 1) & 1);
+          failed |= !mbar_wait_spin(&bars[B_O_FREE], (pieces - 1) & 1);
         }
         if (w.first_of_piece) ++pieces;
         pv_pending = j;
@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       }
       (void)pv_last;
       umma_commit(&bars[B_FINAL]);
-      mbar_wait_bounded(&bars[B_FINAL], 0, 100000000ull);
+      mbar_wait_spin(&bars[B_FINAL], 0, 100000000ull);
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------------ dequant (warps 2..5)
@@ -418,7 +418,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       const int stage = static_cast<int>(j % C::RS);
       const int b = static_cast<int>(j & 1);
       if (w.first_of_piece) e_run_v = -1000;
-      failed |= !mbar_wait_bounded(&bars[B_RAW_FULL + stage], (j / C::RS) & 1);
+      failed |= !mbar_wait_spin(&bars[B_RAW_FULL + stage], (j / C::RS) & 1);
       const uint8_t* cell = smem + C::OFF_RAW + stage * C::RAW_BYTES + kr * C::CELL;
       const int tok = w.kt * PF_BN + kr;
       const uint32_t sw = *reinterpret_cast<const uint32_t*>(cell + (is_k ? C::KB : C::KB + 4 + PF_HS / 2));
@@ -442,7 +442,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       const float q = ex == -1000 ? 0.f : ldexpf(scl, -ex);
       const __half2 qh2 = __floats2half2_rn(q, q);
       const uint32_t q2 = *reinterpret_cast<const uint32_t*>(&qh2);
-      if (j >= 2) failed |= !mbar_wait_bounded(&bars[B_SC_FREE + b], ((j >> 1) - 1) & 1);
+      if (j >= 2) failed |= !mbar_wait_spin(&bars[B_SC_FREE + b], ((j >> 1) - 1) & 1);
       if (kr == 0 && (warp == 2 || warp == 4)) {
         float* scb = reinterpret_cast<float*>(smem + C::OFF_SC) + b * 4;
         if (is_k)
@@ -460,7 +460,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       // distinct bank pairs; the stores of 8 consecutive rows hit 8 distinct 16-byte bank groups (swizzle).
       const uint32_t rbase = (kr >> 3) * 1024 + (kr & 7) * 128, rxor = (kr & 7) << 4;
       if (is_k) {
-        if (j >= 2) failed |= !mbar_wait_bounded(&bars[B_K_FREE + b], ((j >> 1) - 1) & 1);
+        if (j >= 2) failed |= !mbar_wait_spin(&bars[B_K_FREE + b], ((j >> 1) - 1) & 1);
         uint8_t* const kop = kop0 + b * 32768;
         if constexpr (FMT == FMT_INT4) {
 #pragma unroll 1
@@ -505,7 +505,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[B_K_FULL + b]);
       } else {
-        if (j >= 2) failed |= !mbar_wait_bounded(&bars[B_V_FREE + b], ((j >> 1) - 1) & 1);
+        if (j >= 2) failed |= !mbar_wait_spin(&bars[B_V_FREE + b], ((j >> 1) - 1) & 1);
         uint8_t* const vop = vop0 + b * 32768;
         // the value words start 4 bytes past an 8-byte boundary: 8-byte loads from the key scale on give the pairs
         // (key scale, V0), (V1, V2), ..., (V31, value scale)
@@ -552,7 +552,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
     // before P(j) is stored (S_FULL(j) already implies PV(j - 2)), PV(j) in the epilogue.
     int64_t pv_seen = 0;
     auto wait_pv = [&](int64_t t) {  // until PV(t) is complete
-      for (; pv_seen <= t; ++pv_seen) failed |= !mbar_wait_bounded(&bars[B_O_DONE], static_cast<uint32_t>(pv_seen & 1));
+      for (; pv_seen <= t; ++pv_seen) failed |= !mbar_wait_spin(&bars[B_O_DONE], static_cast<uint32_t>(pv_seen & 1));
     };
     float m_used = -INFINITY, l = 0.f, qsc = 0.f;
     int e_used = -1000, lim = -1, tok = 0, qh = 0;
@@ -597,11 +597,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         t_in_piece = 0;
       }
       // this row's scores for keys 32 half .. 32 half + 31 of the tile
-      failed |= !mbar_wait_bounded(&bars[B_S_FULL + b], (j >> 1) & 1);
+      failed |= !mbar_wait_spin(&bars[B_S_FULL + b], (j >> 1) & 1);
       tc_fence_after();
       float s[32];
       tmem_ld32(tm_s[b] + lane_off + 32 * half, s);
-      failed |= !mbar_wait_bounded(&bars[B_SC_FULL + b], (j >> 1) & 1);
+      failed |= !mbar_wait_spin(&bars[B_SC_FULL + b], (j >> 1) & 1);
       const float* scb = reinterpret_cast<const float*>(smem + C::OFF_SC) + b * 4;
       const float qs_t = qsc * scb[0];               // x 2^F of the key operand
       const int ev = __float_as_int(scb[1]);         // value exponent of this tile's operand
