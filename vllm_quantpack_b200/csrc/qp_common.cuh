@@ -215,6 +215,11 @@ __device__ __forceinline__ bool named_bar_or(int id, int threads, bool pred) {
   return r != 0;
 }
 
+// 2^e exactly, e in [-149, 127] (subnormal results below 2^-126), by building the float's bits
+__device__ __forceinline__ float exp2_int(int e) {
+  return e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23) : __uint_as_float(1u << (e + 149));
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

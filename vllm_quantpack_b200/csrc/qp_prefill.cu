@@ -6,12 +6,12 @@
 // context, causal inside the chunk, RHT domain, scale softmax_scale / head), which the reference runs as 16k-token
 // bf16 unpacks + FlashAttention 2 + an fp32 log-sum-exp fold, and the 2D Triton path (int4_kv.py:113-119).
 //
-// B200 design (one persistent CTA of 10 warps per SM):
+// B200 design (one persistent CTA of 14 warps per SM):
 //   warp 0      producer: 1-D bulk copies of the raw 264 / 392-byte cells of a 64-key tile (whole 16-key runs) into a
 //               ring of raw stages;
-//   warp 1      MMA issuer (one thread): S = Q K^T (M 128 rows, N 64 keys, K 256; Q read from TMEM) into TMEM, then
-//               O += P V (M 128, N 256 channels, K 64 keys) into TMEM, each finished with tcgen05.commit onto
-//               mbarriers;
+//   warp 1      MMA issuer (one thread): S = Q K^T (M 128 rows, N 64 keys, K 256; Q read from TMEM) into TMEM as two
+//               interleaved accumulation chains over the two channel halves, then O += P V (M 128, N 256 channels,
+//               K 64 keys; P from shared memory) into TMEM, each finished with tcgen05.commit onto mbarriers;
 //   warps 2-5   dequant into double-buffered key and value operand tiles (the conversion of tile j + 1 overlaps the
 //               MMAs of tile j): raw cells -> fp16 operands in shared memory, 128B-swizzled canonical UMMA layouts. One lop3
 //               turns two nibbles into fp16, one f16x2 subtract makes the exact (u - zp) (int8 codes for k8v4 keys),
@@ -19,12 +19,13 @@
 //               piece's running largest value scale), so the softmax never touches per-key scales. The channel order
 //               inside every 8 channels is [0 4 1 5 2 6 3 7] (what one lop3 pair yields), the same for Q and K (a dot
 //               product does not see the order) and undone on O in the epilogue;
-//   warps 6-9   softmax: one thread per TMEM lane (= query row); at the start of each piece it stores its row of the
-//               prepared Q tile into TMEM (columns 128-255). Scores in log2 units = S x (softmax_scale / head x
-//               log2 e x 2^-row exponent x 2^key-tile exponent); the running maximum is lazy and per thread (P may
-//               reach 2^8 before O is rescaled in TMEM, which is rare); P in fp16 is stored back into TMEM over the
-//               S buffer it came from, as the A operand of the PV MMA (no shared-memory round trip). The epilogue
-//               reads O from TMEM and writes fp32 partials + base-2 lse.
+//   warps 6-13  softmax: two threads per TMEM lane (= query row), 32 keys each; at the start of each piece they store
+//               their row of the prepared Q tile into TMEM (columns 0-127). S is read into registers and released at
+//               once (the next tile's QK runs behind the PV of the previous one meanwhile). Scores in log2 units =
+//               S x (softmax_scale / head x log2 e x 2^-row exponent x 2^key-tile exponent); the running maximum is
+//               lazy and per row (P may reach 2^8 before O is rescaled in TMEM, which is rare); P in fp16 goes to
+//               shared memory as the A operand of the PV MMA. The epilogue reads O from TMEM and writes fp32
+//               partials + base-2 lse.
 // Rows of an M-tile are (query token, query head of the KV head's group) pairs, head fastest: the 6 heads of a group
 // share every dequantised key / value tile. The (M-tile, key-tile) space is split evenly over the CTAs (stream-K):
 // an M-tile may be finished by two CTAs, whose partials the merge kernel folds (with the inverse RHT).
@@ -52,18 +53,19 @@ struct PfCfg {
   static constexpr int KB = FMT == FMT_INT4 ? PF_HS / 2 : PF_HS;  // key bytes in a cell
   static constexpr int RS = FMT == FMT_INT4 ? 4 : 3;               // raw stages
   static constexpr int RAW_BYTES = PF_BN * CELL;
-  // shared memory map (operand tiles 1024-byte aligned for the 128B swizzle); Q, S, P and O live in TMEM
+  // shared memory map (operand tiles 1024-byte aligned for the 128B swizzle); Q, S and O live in TMEM
   static constexpr int OFF_K = 0;                       // 2 buffers x 4 K-blocks x 64 keys x 128 B = 64 KB
   static constexpr int OFF_V = OFF_K + 65536;           // 2 buffers x 4 N-blocks x 8 key groups x 1024 B = 64 KB
-  static constexpr int OFF_RAW = OFF_V + 65536;         // RS x RAW_BYTES
+  static constexpr int OFF_P = OFF_V + 65536;           // P: 128 rows x 64 keys fp16, K-major, 128B-swizzled = 16 KB
+  static constexpr int OFF_RAW = OFF_P + 16384;         // RS x RAW_BYTES
   static constexpr int OFF_SC = OFF_RAW + RS * RAW_BYTES;  // [2 buffers][key factor 2^F, value exponent E] (16 B)
-  static constexpr int OFF_XCH = OFF_SC + 2 * 16;          // [k / v][2 buffers][2 warps] tile maxima exchange
-  static constexpr int OFF_HX = OFF_XCH + 2 * 2 * 2 * 4;  // softmax pairs: [2 buffers][2 halves][128] row maxima,
+  static constexpr int OFF_HX = OFF_SC + 2 * 16;          // softmax pairs: [2 buffers][2 halves][128] row maxima,
                                                          // then [2 halves][128] row sums
   static constexpr int OFF_BAR = OFF_HX + (2 * 2 * 128 + 2 * 128) * 4;
   static constexpr int NBAR = 40;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_TMEM + 16;
+  static_assert(BYTES <= 232448, "dynamic shared memory above the 227 KB a CTA may hold");
 };
 
 // barrier slots
@@ -75,13 +77,15 @@ enum {
   B_K_FREE = 12,     // [2]
   B_V_FULL = 14,     // [2] value operand buffers
   B_V_FREE = 16,     // [2]
-  B_S_FULL = 18,     // [2]
-  B_P_FULL = 22,     // [2] P of the tile stored in TMEM over its S buffer (the softmax is done with that S)
-  B_SC_FULL = 26,    // [2]
+  B_S_FULL = 18,     // S (both channel halves) of the tile is in TMEM
+  B_S_FREE = 19,     // the softmax has read S into registers (8 softmax warps)
+  B_P_FULL = 22,     // P of the tile is in shared memory (8 softmax warps)
+  B_SC_FULL = 26,    // [2] the tile's key factor 2^F (key warps)
   B_SC_FREE = 28,    // [2]
   B_O_DONE = 30,
   B_O_FREE = 31,
   B_FINAL = 32,      // the MMA thread's last commit: every tcgen05.mma done before TMEM is released
+  B_SCV_FULL = 33,   // [2] the tile's value exponent E (value warps)
 };
 
 struct PrefillParams {
@@ -128,6 +132,7 @@ struct Sched {
   int64_t m_start;   // global index of the M-tile's first tile
   int m_tiles;       // key tiles of the current M-tile
   int first_kt;      // first key tile of this CTA inside the current M-tile
+  int piece;         // index of this CTA's piece of the current M-tile
   int cta, ctas;
 
   __device__ void init(const PrefillParams& prm, int cta_, int ctas_) {
@@ -150,25 +155,22 @@ struct Sched {
       m_tiles = mtile_key_tiles(prm, m);
     }
     first_kt = static_cast<int>(g - m_start);
+    // piece index inside the first M-tile: CTAs whose range starts inside it before this one. The CTA covering
+    // m_start is the largest c with total * c / ctas <= m_start. (Computed once: 64-bit divisions are long
+    // instruction sequences; every later M-tile of this CTA starts with this CTA, piece 0.)
+    int c0 = static_cast<int>((m_start * ctas) / prm.total_tiles);
+    while (c0 + 1 < ctas && prm.total_tiles * (c0 + 1) / ctas <= m_start) ++c0;
+    while (c0 > 0 && prm.total_tiles * c0 / ctas > m_start) --c0;
+    piece = cta - c0;
   }
   __device__ bool done() const { return g >= g_end; }
-  // piece index of this CTA inside the current M-tile: CTAs whose range starts inside it before this one
-  __device__ int piece() const {
-    const int64_t start = m_start + first_kt;
-    // the CTA covering m_start: largest c with total * c / ctas <= m_start
-    int c0 = static_cast<int>((m_start * ctas) / p->total_tiles);
-    while (c0 + 1 < ctas && p->total_tiles * (c0 + 1) / ctas <= m_start) ++c0;
-    while (c0 > 0 && p->total_tiles * c0 / ctas > m_start) --c0;
-    (void)start;
-    return cta - c0;
-  }
   __device__ Walk current() const {
     Walk w;
     w.kvh = kvh;
     w.m = m;
     w.kt = static_cast<int>(g - m_start);
     w.kt_end = m_tiles;
-    w.piece = piece();
+    w.piece = piece;
     w.first_of_piece = w.kt == first_kt;
     w.last_of_piece = (w.kt + 1 == m_tiles) || (g + 1 == g_end);
     w.new_mtile = w.first_of_piece;
@@ -184,6 +186,7 @@ struct Sched {
       }
       m_tiles = mtile_key_tiles(*p, m);
       first_kt = 0;
+      piece = 0;
     }
   }
 };
@@ -275,11 +278,13 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       mbar_init(&bars[B_K_FREE + b], 1);
       mbar_init(&bars[B_V_FULL + b], 2);
       mbar_init(&bars[B_V_FREE + b], 1);
-      mbar_init(&bars[B_S_FULL + b], 1);
-      mbar_init(&bars[B_P_FULL + b], 8);
-      mbar_init(&bars[B_SC_FULL + b], 4);
+      mbar_init(&bars[B_SC_FULL + b], 2);
+      mbar_init(&bars[B_SCV_FULL + b], 2);
       mbar_init(&bars[B_SC_FREE + b], 8);
     }
+    mbar_init(&bars[B_S_FULL], 1);
+    mbar_init(&bars[B_S_FREE], 8);
+    mbar_init(&bars[B_P_FULL], 8);
     mbar_init(&bars[B_O_DONE], 1);
     mbar_init(&bars[B_O_FREE], 8);
     mbar_init(&bars[B_FINAL], 1);
@@ -293,10 +298,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // S buffers: columns [0, 64), [64, 128); P of a tile (fp16 pairs) is stored over the first 32 columns of its S
-  // buffer as the A operand of the PV MMA (no shared-memory round trip)
-  const uint32_t tm_s[2] = {tmem, tmem + 64};
-  const uint32_t tm_q = tmem + 128;            // Q (A operand of S = Q K^T): columns [128, 256)
+  // S = Q K^T is two independent accumulation chains, one per half of the channels (the tensor pipe overlaps two
+  // chains; one chain of dependent MMAs runs at about 60 % of the rate). The softmax adds the halves.
+  const uint32_t tm_q = tmem;                  // Q (A operand of S = Q K^T): columns [0, 128)
+  const uint32_t tm_sa = tmem + 128;           // S over channels 0..127: columns [128, 192)
+  const uint32_t tm_sb = tmem + 192;           // S over channels 128..255: columns [192, 256)
   const uint32_t tm_o = tmem + 256;            // O: columns [256, 512)
 
   Sched sch;
@@ -333,84 +339,101 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t ID_QK = f16_idesc(PF_BM, PF_BN, false);
-      constexpr uint32_t ID_PV = f16_idesc(PF_BM, PF_HS, true);
-      const uint32_t k_base = smem_u32(smem + C::OFF_K), v_base = smem_u32(smem + C::OFF_V);
-      int64_t j = 0;
-      int qcount = 0, pieces = 0;
-      int64_t pv_pending = -1;  // tile whose PV is still to be issued
-      bool pv_first = false, pv_last = false;
-      auto issue_pv = [&](int64_t t, bool first) {
-        const int b = static_cast<int>(t & 1);
-        failed |= !mbar_wait_spin(&bars[B_V_FULL + b], (t >> 1) & 1);
-        failed |= !mbar_wait_spin(&bars[B_P_FULL + b], (t >> 1) & 1);
-        tc_fence_after();
-        const uint32_t vb = v_base + b * 32768;
-        // P(t) in TMEM, K step s (16 keys) = 8 columns; S(t + 2) overwrites these columns with MMAs issued after
-        // these (the tcgen05.mma of one thread execute in issue order)
+    // The whole warp walks the schedule and waits (convergent, so the descriptors and TMEM addresses are warp-uniform
+    // values); one elected lane issues. A tcgen05.mma issued from a one-lane branch costs tens of cycles of operand
+    // moves each, which starves the tensor pipe.
+    constexpr uint32_t ID_QK = f16_idesc(PF_BM, PF_BN, false);
+    constexpr uint32_t ID_PV = f16_idesc(PF_BM, PF_HS, true);
+    const uint32_t k_base = smem_u32(smem + C::OFF_K), v_base = smem_u32(smem + C::OFF_V);
+    const uint32_t p_base = smem_u32(smem + C::OFF_P);
+    int64_t j = 0;
+    int qcount = 0, pieces = 0;
+    int64_t pv_pending = -1;  // tile whose PV is still to be issued
+    bool pv_first = false;
+    // every lane runs the same bounded waits; the vote keeps the warp's view (and its control flow) uniform
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+      const bool ok = mbar_wait_spin(bar, parity);
+      failed |= __any_sync(0xffffffffu, !ok);
+    };
+    auto issue_pv = [&](int64_t t, bool first) {
+      const int b = static_cast<int>(t & 1);
+      wait_all(&bars[B_V_FULL + b], (t >> 1) & 1);
+      wait_all(&bars[B_P_FULL], static_cast<uint32_t>(t & 1));
+      tc_fence_after();
+      const uint32_t vb = v_base + b * 32768;
+      if (elect_one()) {
+        // P(t) in shared memory, K step s = 16 keys = 32 bytes of each 128-byte row
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          umma_f16_ts(tm_o, tm_s[b] + 8 * s, sw128_desc(vb + 2 * s * 1024, 8192, 1024), ID_PV,
-                      (first && s == 0) ? 0u : 1u);
+          umma_f16(tm_o, sw128_desc(p_base + 32 * s, 16, 1024), sw128_desc(vb + 2 * s * 1024, 8192, 1024), ID_PV,
+                   (first && s == 0) ? 0u : 1u);
         umma_commit(&bars[B_V_FREE + b]);
         umma_commit(&bars[B_O_DONE]);
-      };
-      for (; !sch.done() && !failed; sch.next(), ++j) {
-        const Walk w = sch.current();
-        if (w.new_mtile) {
-          failed |= !mbar_wait_spin(&bars[B_Q_FULL], qcount & 1);
-          ++qcount;
-        }
-        // S(j) = Q K(j)^T
-        const int b = static_cast<int>(j & 1);
-        failed |= !mbar_wait_spin(&bars[B_K_FULL + b], (j >> 1) & 1);
-        // S buffer b last held S(j - 2) and P(j - 2): the PV of that tile, issued before these MMAs, waited for the
-        // softmax to finish with it
-        tc_fence_after();
-        const uint32_t kb = k_base + b * 32768;
-#pragma unroll
-        for (int s = 0; s < 16; ++s)  // K step s: 16 channels = 8 TMEM columns of Q
-          umma_f16_ts(tm_s[b], tm_q + 8 * s, sw128_desc(kb + (s >> 2) * 8192 + (s & 3) * 32, 16, 1024), ID_QK,
-                      s > 0 ? 1u : 0u);
-        umma_commit(&bars[B_K_FREE + b]);
-        umma_commit(&bars[B_S_FULL + b]);
-        // Q of this piece is free once S of its last tile is complete: the softmax, which waits for that S before
-        // it stores the next piece's Q, needs no other signal
-        // O += P(j-1) V(j-1), one tile behind so the softmax of tile j overlaps it
-        if (pv_pending >= 0) {
-          issue_pv(pv_pending, pv_first);
-          pv_pending = -1;
-        }
-        if (w.first_of_piece && pieces > 0) {
-          // O is overwritten by this piece's first PV: the previous piece's epilogue must have read it
-          failed |= !mbar_wait_spin(&bars[B_O_FREE], (pieces - 1) & 1);
-        }
-        if (w.first_of_piece) ++pieces;
-        pv_pending = j;
-        pv_first = w.first_of_piece;
-        pv_last = w.last_of_piece;
-        if (w.last_of_piece) {  // the epilogue waits for this PV: issue it now
-          issue_pv(pv_pending, pv_first);
-          pv_pending = -1;
-        }
       }
-      (void)pv_last;
-      umma_commit(&bars[B_FINAL]);
-      mbar_wait_spin(&bars[B_FINAL], 0, 100000000ull);
+      __syncwarp();
+    };
+    for (; !sch.done() && !failed; sch.next(), ++j) {
+      const Walk w = sch.current();
+      if (w.new_mtile) {
+        wait_all(&bars[B_Q_FULL], qcount & 1);
+        ++qcount;
+      }
+      // S(j) = Q K(j)^T
+      const int b = static_cast<int>(j & 1);
+      wait_all(&bars[B_K_FULL + b], (j >> 1) & 1);
+      // S(j - 1) has been read by the softmax (it releases S before its exponentials: the PV issued just before
+      // keeps the tensor pipe busy meanwhile)
+      if (j > 0) wait_all(&bars[B_S_FREE], static_cast<uint32_t>((j - 1) & 1));
+      tc_fence_after();
+      const uint32_t kb = k_base + b * 32768;
+      if (elect_one()) {
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {  // K step s of each half: 16 channels = 8 TMEM columns of Q
+          umma_f16_ts(tm_sa, tm_q + 8 * s, sw128_desc(kb + (s >> 2) * 8192 + (s & 3) * 32, 16, 1024), ID_QK,
+                      s > 0 ? 1u : 0u);
+          umma_f16_ts(tm_sb, tm_q + 64 + 8 * s, sw128_desc(kb + 16384 + (s >> 2) * 8192 + (s & 3) * 32, 16, 1024),
+                      ID_QK, s > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars[B_K_FREE + b]);
+        umma_commit(&bars[B_S_FULL]);
+      }
+      __syncwarp();
+      // Q of this piece is free once S of its last tile is complete: the softmax, which waits for that S before
+      // it stores the next piece's Q, needs no other signal
+      // O += P(j-1) V(j-1), one tile behind so the softmax of tile j overlaps it
+      if (pv_pending >= 0) {
+        issue_pv(pv_pending, pv_first);
+        pv_pending = -1;
+      }
+      if (w.first_of_piece && pieces > 0) {
+        // O is overwritten by this piece's first PV: the previous piece's epilogue must have read it
+        wait_all(&bars[B_O_FREE], (pieces - 1) & 1);
+      }
+      if (w.first_of_piece) ++pieces;
+      pv_pending = j;
+      pv_first = w.first_of_piece;
+      if (w.last_of_piece) {  // the epilogue waits for this PV: issue it now
+        issue_pv(pv_pending, pv_first);
+        pv_pending = -1;
+      }
     }
+    if (elect_one()) umma_commit(&bars[B_FINAL]);
+    __syncwarp();
+    mbar_wait_spin(&bars[B_FINAL], 0, 100000000ull);
   } else if (warp < 6) {
     // ------------------------------------------------------------------ dequant (warps 2..5)
     // keys:   K_op = (u - zp) * ks * 2^-F  (F: exponent of the tile's largest key scale; 2^F goes to the softmax)
     // values: V_op = (u - zp) * vs * 2^-E  (E: running exponent of the piece's largest value scale; O is rescaled by
     //         the softmax when E grows). Every operand is then <= 15 in magnitude and exact up to one fp16 rounding.
-    const int dq = tid - 64;     // 0..127
-    const int kr = dq & 63;      // key row of the tile
-    const bool is_k = dq < 64;   // warps 2, 3: keys; warps 4, 5: values
-    const int wpair = (warp - 2) & 1;
+    // Warps 2 / 3 convert channels 0-127 / 128-255 of the tile's 64 keys, warps 4 / 5 the same of its values; lane l
+    // takes rows l and l + 32. Every warp sees all 64 scales of its operand: the tile maximum is one warp reduction,
+    // with no exchange between warps.
+    const bool is_k = warp < 4;
+    const int chalf = (warp - 2) & 1;  // K-blocks / N-blocks 2 chalf and 2 chalf + 1
     uint8_t* const kop0 = smem + C::OFF_K;
     uint8_t* const vop0 = smem + C::OFF_V;
-    float* xch = reinterpret_cast<float*>(smem + C::OFF_XCH) + (is_k ? 0 : 4);
+    const int sc_off = is_k ? C::KB : C::KB + 4 + PF_HS / 2;
+    const bool packed = FMT == FMT_INT4 || !is_k;  // the scale carries the zero point in its low 4 mantissa bits
     int e_run_v = -1000;
     int64_t j = 0;
     for (; !sch.done() && !failed; sch.next(), ++j) {
@@ -419,56 +442,54 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       const int b = static_cast<int>(j & 1);
       if (w.first_of_piece) e_run_v = -1000;
       failed |= !mbar_wait_spin(&bars[B_RAW_FULL + stage], (j / C::RS) & 1);
-      const uint8_t* cell = smem + C::OFF_RAW + stage * C::RAW_BYTES + kr * C::CELL;
-      const int tok = w.kt * PF_BN + kr;
-      const uint32_t sw = *reinterpret_cast<const uint32_t*>(cell + (is_k ? C::KB : C::KB + 4 + PF_HS / 2));
-      const float scl = tok < p.n ? __uint_as_float((FMT == FMT_INT4 || !is_k) ? (sw & 0xFFFFFFF0u) : sw) : 0.f;
-      const uint32_t zp = (FMT == FMT_INT4 || !is_k) ? (sw & 0xFu) : 0u;
-      // tile maximum of this half's scales (two warps)
-      const float wm = warp_max(scl);
-      if (lane == 0) xch[b * 2 + wpair] = wm;
-      // the two warps of this half leave together if either gave up a wait (a bar.sync has no time bound)
-      if (named_bar_or(is_k ? 1 : 2, 64, failed)) {
-        failed = true;
-        break;
-      }
-      const float tmax = fmaxf(xch[b * 2], xch[b * 2 + 1]);
-      int ex = -1000;
-      if (tmax > 0.f) frexpf(tmax, &ex);  // tmax < 2^ex
+      const uint8_t* const raw = smem + C::OFF_RAW + stage * C::RAW_BYTES;
+      const int tok0 = w.kt * PF_BN + lane;
+      const uint32_t sw0 = *reinterpret_cast<const uint32_t*>(raw + lane * C::CELL + sc_off);
+      const uint32_t sw1 = *reinterpret_cast<const uint32_t*>(raw + (lane + 32) * C::CELL + sc_off);
+      const float scl0 = tok0 < p.n ? __uint_as_float(packed ? (sw0 & 0xFFFFFFF0u) : sw0) : 0.f;
+      const float scl1 = tok0 + 32 < p.n ? __uint_as_float(packed ? (sw1 & 0xFFFFFFF0u) : sw1) : 0.f;
+      const float tmax = warp_max(fmaxf(scl0, scl1));  // scales are >= 0
+      // tmax < 2^ex (the exponent field; subnormals give -126, still a bound)
+      int ex = tmax > 0.f ? static_cast<int>((__float_as_uint(tmax) >> 23) & 0xFFu) - 126 : -1000;
       if (!is_k) {
         e_run_v = max(e_run_v, ex);
         ex = e_run_v;
       }
-      const float q = ex == -1000 ? 0.f : ldexpf(scl, -ex);
-      const __half2 qh2 = __floats2half2_rn(q, q);
-      const uint32_t q2 = *reinterpret_cast<const uint32_t*>(&qh2);
+      const float inv = ex == -1000 ? 0.f : exp2_int(-ex);
+      const __half2 qa = __floats2half2_rn(scl0 * inv, scl0 * inv), qb = __floats2half2_rn(scl1 * inv, scl1 * inv);
+      const uint32_t q2_0 = *reinterpret_cast<const uint32_t*>(&qa), q2_1 = *reinterpret_cast<const uint32_t*>(&qb);
+      const uint32_t zp_0 = packed ? (sw0 & 0xFu) : 0u, zp_1 = packed ? (sw1 & 0xFu) : 0u;
       if (j >= 2) failed |= !mbar_wait_spin(&bars[B_SC_FREE + b], ((j >> 1) - 1) & 1);
-      if (kr == 0 && (warp == 2 || warp == 4)) {
+      if (lane == 0 && chalf == 0) {
         float* scb = reinterpret_cast<float*>(smem + C::OFF_SC) + b * 4;
         if (is_k)
-          scb[0] = ex == -1000 ? 0.f : ldexpf(1.f, ex);
+          scb[0] = ex == -1000 ? 0.f : exp2_int(ex);
         else
           scb[1] = __int_as_float(ex);
       }
       // the softmax needs only these factors: release them now, not after the (longer) operand conversion
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[B_SC_FULL + b]);
-      const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
-      // Each thread converts its key row: every 8-byte load of the row is issued before any conversion (the
-      // stores below could alias them for the compiler, which would otherwise serialise load -> convert -> store
-      // per word). Cells are 8-byte aligned (264 / 392 B) and the 8-byte loads of 16 consecutive rows fall in 16
-      // distinct bank pairs; the stores of 8 consecutive rows hit 8 distinct 16-byte bank groups (swizzle).
-      const uint32_t rbase = (kr >> 3) * 1024 + (kr & 7) * 128, rxor = (kr & 7) << 4;
+      if (lane == 0) mbar_arrive(&bars[is_k ? B_SC_FULL + b : B_SCV_FULL + b]);
+      // Each pass converts 64 channels of one row: all its loads are issued before any conversion (the stores could
+      // alias them for the compiler, which would otherwise serialise load -> convert -> store per word). Cells are
+      // 8-byte aligned (264 / 392 B): the 8-byte loads of 16 consecutive rows fall in 16 distinct bank pairs; the
+      // 16-byte stores of 8 consecutive rows hit 8 distinct bank groups (swizzle).
       if (is_k) {
         if (j >= 2) failed |= !mbar_wait_spin(&bars[B_K_FREE + b], ((j >> 1) - 1) & 1);
         uint8_t* const kop = kop0 + b * 32768;
-        if constexpr (FMT == FMT_INT4) {
 #pragma unroll 1
-          for (int kb = 0; kb < 4; ++kb) {  // K-block kb: words 8 kb .. 8 kb + 7 (channels 64 kb ..)
+        for (int it = 0; it < 4; ++it) {
+          const int r = it >> 1, kb = 2 * chalf + (it & 1);  // row lane + 32 r, K-block kb (channels 64 kb ..)
+          const int kr = lane + 32 * r;
+          const uint8_t* const cell = raw + kr * C::CELL;
+          const uint32_t q2 = r ? q2_1 : q2_0, zp = r ? zp_1 : zp_0;
+          const uint32_t rbase = (kr >> 3) * 1024 + (kr & 7) * 128, rxor = (kr & 7) << 4;
+          uint8_t* const dst = kop + kb * 8192 + rbase;
+          if constexpr (FMT == FMT_INT4) {
+            const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
             uint2 kw[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) kw[k] = *reinterpret_cast<const uint2*>(cell + 32 * kb + 8 * k);
-            uint8_t* const dst = kop + kb * 8192 + rbase;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {  // word: channels 8 (8 kb + i) .. + 7 = chunk i of the K-block
               const uint32_t x = (i & 1) ? kw[i >> 1].y : kw[i >> 1].x;
@@ -480,24 +501,19 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
               v.w = hmul2_u32(hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);  // 3, 7
               *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(i) << 4) ^ rxor)) = v;
             }
-          }
-        } else {
-#pragma unroll 1
-          for (int h = 0; h < 4; ++h) {  // K-block h: codes 64 h .. 64 h + 63, 8 loads of 8 bytes in flight
-            uint2 kw[8];
+          } else {
+            uint2 kw[8];  // codes 64 kb .. 64 kb + 63
 #pragma unroll
-            for (int k = 0; k < 8; ++k) kw[k] = *reinterpret_cast<const uint2*>(cell + 64 * h + 8 * k);
+            for (int k = 0; k < 8; ++k) kw[k] = *reinterpret_cast<const uint2*>(cell + 64 * kb + 8 * k);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {  // 8 channels 8 C8 .. 8 C8 + 7 (two words)
-              const int C8 = 8 * h + k;
-              const uint32_t a = kw[k].x ^ 0x80808080u, c = kw[k].y ^ 0x80808080u;
+            for (int k = 0; k < 8; ++k) {  // chunk k: channels 8 (8 kb + k) .. + 7 (two words)
+              const uint32_t a = kw[k].x ^ 0x80808080u, cc = kw[k].y ^ 0x80808080u;
               uint4 v;  // (1152 + code) - 1152 = code, exact; then the scale
               v.x = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4140u), 0x64806480u), q2);
               v.y = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4342u), 0x64806480u), q2);
-              v.z = hmul2_u32(hsub2_u32(prmt(c, 0x64646464u, 0x4140u), 0x64806480u), q2);
-              v.w = hmul2_u32(hsub2_u32(prmt(c, 0x64646464u, 0x4342u), 0x64806480u), q2);
-              *reinterpret_cast<uint4*>(kop + (C8 >> 3) * 8192 +
-                                        (rbase + ((static_cast<uint32_t>(C8 & 7) << 4) ^ rxor))) = v;
+              v.z = hmul2_u32(hsub2_u32(prmt(cc, 0x64646464u, 0x4140u), 0x64806480u), q2);
+              v.w = hmul2_u32(hsub2_u32(prmt(cc, 0x64646464u, 0x4342u), 0x64806480u), q2);
+              *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(k) << 4) ^ rxor)) = v;
             }
           }
         }
@@ -507,14 +523,20 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       } else {
         if (j >= 2) failed |= !mbar_wait_spin(&bars[B_V_FREE + b], ((j >> 1) - 1) & 1);
         uint8_t* const vop = vop0 + b * 32768;
-        // the value words start 4 bytes past an 8-byte boundary: 8-byte loads from the key scale on give the pairs
-        // (key scale, V0), (V1, V2), ..., (V31, value scale)
 #pragma unroll 1
-        for (int kb = 0; kb < 4; ++kb) {  // N-block kb: words 8 kb .. 8 kb + 7; loads at 8-byte offsets 4 kb ..
+        for (int it = 0; it < 4; ++it) {
+          const int r = it >> 1, kb = 2 * chalf + (it & 1);  // row lane + 32 r, N-block kb (channels 64 kb ..)
+          const int kr = lane + 32 * r;
+          const uint8_t* const cell = raw + kr * C::CELL;
+          const uint32_t q2 = r ? q2_1 : q2_0, zp = r ? zp_1 : zp_0;
+          const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
+          const uint32_t rbase = (kr >> 3) * 1024 + (kr & 7) * 128, rxor = (kr & 7) << 4;
+          uint8_t* const dst = vop + kb * 8192 + rbase;
+          // the value words start 4 bytes past an 8-byte boundary: 8-byte loads from the key scale on give the
+          // pairs (key scale, V0), (V1, V2), ..., (V31, value scale)
           uint2 vw[5];
 #pragma unroll
           for (int k = 0; k < 5; ++k) vw[k] = *reinterpret_cast<const uint2*>(cell + C::KB + 32 * kb + 8 * k);
-          uint8_t* const dst = vop + kb * 8192 + rbase;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const uint32_t x = (i & 1) ? vw[(i + 1) >> 1].x : vw[i >> 1].y;
@@ -596,17 +618,18 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         e_used = -1000;
         t_in_piece = 0;
       }
-      // this row's scores for keys 32 half .. 32 half + 31 of the tile
-      failed |= !mbar_wait_spin(&bars[B_S_FULL + b], (j >> 1) & 1);
+      // this row's scores for keys 32 half .. 32 half + 31 of the tile (sum of the two channel halves), then S is
+      // released to the next tile's QK
+      failed |= !mbar_wait_spin(&bars[B_S_FULL], static_cast<uint32_t>(j & 1));
       tc_fence_after();
       float s[32];
-      tmem_ld32(tm_s[b] + lane_off + 32 * half, s);
+      tmem_ld32_sum2(tm_sa + lane_off + 32 * half, tm_sb + lane_off + 32 * half, s);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[B_S_FREE]);
       failed |= !mbar_wait_spin(&bars[B_SC_FULL + b], (j >> 1) & 1);
       const float* scb = reinterpret_cast<const float*>(smem + C::OFF_SC) + b * 4;
       const float qs_t = qsc * scb[0];               // x 2^F of the key operand
-      const int ev = __float_as_int(scb[1]);         // value exponent of this tile's operand
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[B_SC_FREE + b]);
       const int key0 = w.kt * PF_BN + 32 * half;
       const bool masked = w.kt * PF_BN + PF_BN - 1 > min(p.n - 1, p.vis_base);  // some row cannot see some key
       if (masked) {
@@ -614,9 +637,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         for (int c = 0; c < 32; ++c)
           if (key0 + c > lim) s[c] = -INFINITY;
       }
-      float mx = -INFINITY;
+      float mx4[4] = {s[0], s[1], s[2], s[3]};  // four independent chains
 #pragma unroll
-      for (int c = 0; c < 32; ++c) mx = fmaxf(mx, s[c]);
+      for (int c = 4; c < 32; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       hmax[(b * 2 + half) * 128 + row] = mx;
       // the pair leaves together if either gave up a wait (a bar.sync has no time bound)
       if (named_bar_or(pair_bar, 64, failed)) {
@@ -626,15 +650,48 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       mx = fmaxf(mx, hmax[(b * 2 + (half ^ 1)) * 128 + row]);
       const float mrow = mx * qs_t;
       const bool grow = mrow > m_used + PF_SLACK;  // the same in both threads of the row
-      const bool vgrow = ev > e_used;              // the same for every thread
-      if (__any_sync(0xffffffffu, grow) || vgrow) {
-        // rescale this thread's half of the row's O in TMEM (after the previous PV of the piece completed)
-        const float m_new = grow ? mrow : m_used;
-        const float alpha = m_new == m_used ? 1.f : exp2f(m_used - m_new);
-        const float o_range = e_used == -1000 ? 0.f : ldexpf(1.f, e_used - ev);
-        const float ao = alpha * o_range;
+      float alpha = 1.f;
+      if (grow) {
+        alpha = exp2f(m_used - mrow);
+        m_used = mrow;
+        l *= alpha;
+      }
+      // P = 2^(s qs_t - m) <= 2^8 in fp16
+      const float base = m_used == -INFINITY ? 0.f : m_used;
+      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pw[16];
+      if (masked) {
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float p0 = s[c] == -INFINITY ? 0.f : fast_exp2(fmaf(s[c], qs_t, -base));
+          const float p1 = s[c + 1] == -INFINITY ? 0.f : fast_exp2(fmaf(s[c + 1], qs_t, -base));
+          ls4[(c >> 1) & 3] += p0 + p1;
+          const __half2 h = __floats2half2_rn(p0, p1);
+          pw[c >> 1] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float p0 = fast_exp2(fmaf(s[c], qs_t, -base));
+          const float p1 = fast_exp2(fmaf(s[c + 1], qs_t, -base));
+          ls4[(c >> 1) & 3] += p0 + p1;
+          const __half2 h = __floats2half2_rn(p0, p1);
+          pw[c >> 1] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+      }
+      l += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+      // the value exponent is needed only now, for the O rescale: the value warps publish it separately, so the
+      // exponentials above do not wait for them
+      failed |= !mbar_wait_spin(&bars[B_SCV_FULL + b], (j >> 1) & 1);
+      const int ev = __float_as_int(scb[1]);  // value exponent of this tile's operand
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[B_SC_FREE + b]);
+      const bool vgrow = ev > e_used;  // the same for every thread
+      wait_pv(j - 1);  // PV(j - 1) has read P(j - 1) and added into O
+      if (__any_sync(0xffffffffu, alpha != 1.f) || vgrow) {
+        // rescale this thread's half of the row's O in TMEM: new running maximum and / or value exponent
+        const float ao = alpha * (!vgrow ? 1.f : e_used == -1000 ? 0.f : ldexpf(1.f, e_used - ev));
         if (t_in_piece > 0) {
-          wait_pv(j - 1);
           tc_fence_after();
 #pragma unroll 1
           for (int c0 = 128 * half; c0 < 128 * half + 128; c0 += 32) {
@@ -645,41 +702,20 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
             tmem_st32(tm_o + lane_off + c0, o);
           }
         }
-        l *= alpha;
-        m_used = m_new;
-        e_used = ev;
+        if (vgrow) e_used = ev;
       }
-      // P = 2^(s qs_t - m) <= 2^8 in fp16
-      const float base = m_used == -INFINITY ? 0.f : m_used;
-      float lsum = 0.f;
-      uint32_t pw[16];
-      if (masked) {
+      // P -> shared memory, row `row`, keys 32 half .. + 31 = 16-byte chunks 4 half .. 4 half + 3 of the row (the
+      // A operand of the PV MMA, K-major, 128B-swizzled; the 8 rows of a store phase hit 8 distinct bank groups)
+      {
+        uint8_t* const prow = smem + C::OFF_P;
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float p0 = s[c] == -INFINITY ? 0.f : fast_exp2(fmaf(s[c], qs_t, -base));
-          const float p1 = s[c + 1] == -INFINITY ? 0.f : fast_exp2(fmaf(s[c + 1], qs_t, -base));
-          lsum += p0 + p1;
-          const __half2 h = __floats2half2_rn(p0, p1);
-          pw[c >> 1] = *reinterpret_cast<const uint32_t*>(&h);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float p0 = fast_exp2(fmaf(s[c], qs_t, -base));
-          const float p1 = fast_exp2(fmaf(s[c + 1], qs_t, -base));
-          lsum += p0 + p1;
-          const __half2 h = __floats2half2_rn(p0, p1);
-          pw[c >> 1] = *reinterpret_cast<const uint32_t*>(&h);
-        }
+        for (int i = 0; i < 4; ++i)
+          *reinterpret_cast<uint4*>(prow + sw128_off(row, 4 * half + i)) =
+              make_uint4(pw[4 * i], pw[4 * i + 1], pw[4 * i + 2], pw[4 * i + 3]);
       }
-      l += lsum;
-      wait_pv(j - 1);
-      // P -> TMEM over columns 16 half + [0, 16) of this tile's S buffer: the A operand of its PV MMA
-      tmem_st16u(tm_s[b] + lane_off + 16 * half, pw);
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      tc_fence_before();
+      fence_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[B_P_FULL + b]);
+      if (lane == 0) mbar_arrive(&bars[B_P_FULL]);
       ++t_in_piece;
 
       if (w.last_of_piece) {
@@ -803,7 +839,7 @@ __device__ __forceinline__ int mpair_key_tiles(const Prefill2Params& p, int m) {
 struct Sched2 {
   const Prefill2Params* p;
   int64_t g, g_end, m_start;
-  int kvh, m, m_tiles, first_kt, cta, ctas;
+  int kvh, m, m_tiles, first_kt, piece, cta, ctas;
   __device__ void init(const Prefill2Params& prm, int cta_, int ctas_) {
     p = &prm;
     cta = cta_;
@@ -823,6 +859,11 @@ struct Sched2 {
       m_tiles = mpair_key_tiles(prm, m);
     }
     first_kt = static_cast<int>(g - m_start);
+    // piece index inside the first M-tile (once; later M-tiles start with this pair, piece 0)
+    int c0 = static_cast<int>((m_start * ctas) / prm.total_tiles);
+    while (c0 + 1 < ctas && prm.total_tiles * (c0 + 1) / ctas <= m_start) ++c0;
+    while (c0 > 0 && prm.total_tiles * c0 / ctas > m_start) --c0;
+    piece = cta - c0;
   }
   __device__ bool done() const { return g >= g_end; }
   __device__ Walk current() const {
@@ -831,10 +872,7 @@ struct Sched2 {
     w.m = m;
     w.kt = static_cast<int>(g - m_start);
     w.kt_end = m_tiles;
-    int c0 = static_cast<int>((m_start * ctas) / p->total_tiles);
-    while (c0 + 1 < ctas && p->total_tiles * (c0 + 1) / ctas <= m_start) ++c0;
-    while (c0 > 0 && p->total_tiles * c0 / ctas > m_start) --c0;
-    w.piece = cta - c0;
+    w.piece = piece;
     w.first_of_piece = w.kt == first_kt;
     w.last_of_piece = (w.kt + 1 == m_tiles) || (g + 1 == g_end);
     w.new_mtile = w.first_of_piece;
@@ -850,6 +888,7 @@ struct Sched2 {
       }
       m_tiles = mpair_key_tiles(*p, m);
       first_kt = 0;
+      piece = 0;
     }
   }
 };

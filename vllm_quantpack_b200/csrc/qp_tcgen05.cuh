@@ -21,6 +21,17 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// true in one lane of the (converged, full) warp: the lane that issues a tcgen05.mma / commit for the whole warp
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // D[tmem] (+)= A[smem desc] * B[smem desc], fp16 operands, fp32 accumulate
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate) {
@@ -82,6 +93,34 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+// v = (32 columns at ta) + (32 columns at tb): both loads in flight before the one wait (the wait names every
+// destination register, so no use of them can be scheduled above it)
+__device__ __forceinline__ void tmem_ld32_sum2(uint32_t ta, uint32_t tb, float (&v)[32]) {
+  uint32_t r[32], u[32];
+#define QP_LD32(R, ADDR)                                                                                             \
+  asm volatile(                                                                                                      \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "                                                                      \
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,"  \
+      "%29,%30,%31}, [%32];"                                                                                         \
+      : "=r"(R[0]), "=r"(R[1]), "=r"(R[2]), "=r"(R[3]), "=r"(R[4]), "=r"(R[5]), "=r"(R[6]), "=r"(R[7]), "=r"(R[8]), \
+        "=r"(R[9]), "=r"(R[10]), "=r"(R[11]), "=r"(R[12]), "=r"(R[13]), "=r"(R[14]), "=r"(R[15]), "=r"(R[16]),      \
+        "=r"(R[17]), "=r"(R[18]), "=r"(R[19]), "=r"(R[20]), "=r"(R[21]), "=r"(R[22]), "=r"(R[23]), "=r"(R[24]),     \
+        "=r"(R[25]), "=r"(R[26]), "=r"(R[27]), "=r"(R[28]), "=r"(R[29]), "=r"(R[30]), "=r"(R[31])                   \
+      : "r"(ADDR))
+  QP_LD32(r, ta);
+  QP_LD32(u, tb);
+#undef QP_LD32
+#define QP_W8(R, o) "+r"(R[o]), "+r"(R[o + 1]), "+r"(R[o + 2]), "+r"(R[o + 3]), "+r"(R[o + 4]), "+r"(R[o + 5]), \
+                    "+r"(R[o + 6]), "+r"(R[o + 7])
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : QP_W8(r, 0), QP_W8(r, 8), QP_W8(r, 16), QP_W8(r, 24), QP_W8(u, 0), QP_W8(u, 8), QP_W8(u, 16),
+                 QP_W8(u, 24)
+               :
+               : "memory");
+#undef QP_W8
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + __uint_as_float(u[i]);
 }
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
