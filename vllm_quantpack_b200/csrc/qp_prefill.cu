@@ -43,7 +43,19 @@ namespace qp {
 constexpr int PF_HS = 256;
 constexpr int PF_BM = 128;  // query rows per M-tile (TMEM lanes)
 constexpr int PF_BN = 64;   // keys per tile
-constexpr int PF_THREADS = 448;  // 14 warps: producer, MMA, 4 dequant, 8 softmax
+constexpr int PF_THREADS = 448;  // CTA-pair kernel: 14 warps: producer, MMA, 4 dequant, 8 softmax
+#ifndef QP_PF_DQ_WARPS
+#define QP_PF_DQ_WARPS 8
+#endif
+// single-CTA kernel: producer, MMA, PF_DQ dequant warps (half keys, half values; each converts 8 / PF_DQ of the
+// tile's 64-channel blocks), 8 softmax warps
+constexpr int PF_DQ = QP_PF_DQ_WARPS;
+static_assert(PF_DQ == 4 || PF_DQ == 8, "dequant warps: 4 or 8");
+constexpr int PF_SM0 = 2 + PF_DQ;                // first softmax warp
+constexpr int PF1_THREADS = 32 * (PF_SM0 + 8);
+// registers per thread one CTA may hold: the register file is split over the 4 sub-partitions (16384 each), and a
+// sub-partition hosts every fourth warp
+constexpr int PF1_REGS = (16384 / (32 * ((PF1_THREADS / 32 + 3) / 4))) & ~7;
 constexpr float PF_SLACK = 8.f;
 constexpr float PF_LOG2E = 1.4426950408889634f;
 
@@ -259,7 +271,7 @@ __global__ void __launch_bounds__(256) prefill_qprep_kernel(const void* q, int64
 
 // ---------------------------------------------------------------------------------------------------- main kernel
 template <int FMT>
-__global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillParams p) {
+__global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
   using C = PfCfg<FMT>;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -270,16 +282,16 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
   if (tid == 0) {
     for (int s = 0; s < C::RS; ++s) {
       mbar_init(&bars[B_RAW_FULL + s], 1);
-      mbar_init(&bars[B_RAW_EMPTY + s], 4);
+      mbar_init(&bars[B_RAW_EMPTY + s], PF_DQ);
     }
     mbar_init(&bars[B_Q_FULL], 8);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&bars[B_K_FULL + b], 2);
+      mbar_init(&bars[B_K_FULL + b], PF_DQ / 2);
       mbar_init(&bars[B_K_FREE + b], 1);
-      mbar_init(&bars[B_V_FULL + b], 2);
+      mbar_init(&bars[B_V_FULL + b], PF_DQ / 2);
       mbar_init(&bars[B_V_FREE + b], 1);
-      mbar_init(&bars[B_SC_FULL + b], 2);
-      mbar_init(&bars[B_SCV_FULL + b], 2);
+      mbar_init(&bars[B_SC_FULL + b], PF_DQ / 2);
+      mbar_init(&bars[B_SCV_FULL + b], PF_DQ / 2);
       mbar_init(&bars[B_SC_FREE + b], 8);
     }
     mbar_init(&bars[B_S_FULL], 1);
@@ -420,16 +432,18 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
     if (elect_one()) umma_commit(&bars[B_FINAL]);
     __syncwarp();
     mbar_wait_spin(&bars[B_FINAL], 0, 100000000ull);
-  } else if (warp < 6) {
-    // ------------------------------------------------------------------ dequant (warps 2..5)
+  } else if (warp < PF_SM0) {
+    // ------------------------------------------------------------------ dequant (warps 2 .. PF_SM0 - 1)
     // keys:   K_op = (u - zp) * ks * 2^-F  (F: exponent of the tile's largest key scale; 2^F goes to the softmax)
     // values: V_op = (u - zp) * vs * 2^-E  (E: running exponent of the piece's largest value scale; O is rescaled by
     //         the softmax when E grows). Every operand is then <= 15 in magnitude and exact up to one fp16 rounding.
-    // Warps 2 / 3 convert channels 0-127 / 128-255 of the tile's 64 keys, warps 4 / 5 the same of its values; lane l
-    // takes rows l and l + 32. Every warp sees all 64 scales of its operand: the tile maximum is one warp reduction,
-    // with no exchange between warps.
-    const bool is_k = warp < 4;
-    const int chalf = (warp - 2) & 1;  // K-blocks / N-blocks 2 chalf and 2 chalf + 1
+    // The first PF_DQ / 2 warps convert the keys, the others the values; each warp takes BPW of the four 64-channel
+    // blocks for all 64 rows of the tile (lane l: rows l and l + 32). Every warp sees all 64 scales of its operand:
+    // the tile maximum is one warp reduction, with no exchange between warps.
+    constexpr int BPW = 8 / PF_DQ;                 // 64-channel blocks per warp
+    const int dq = warp - 2;
+    const bool is_k = dq < PF_DQ / 2;
+    const int dd = dq % (PF_DQ / 2);               // blocks BPW dd .. BPW dd + BPW - 1
     uint8_t* const kop0 = smem + C::OFF_K;
     uint8_t* const vop0 = smem + C::OFF_V;
     const int sc_off = is_k ? C::KB : C::KB + 4 + PF_HS / 2;
@@ -460,7 +474,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       const uint32_t q2_0 = *reinterpret_cast<const uint32_t*>(&qa), q2_1 = *reinterpret_cast<const uint32_t*>(&qb);
       const uint32_t zp_0 = packed ? (sw0 & 0xFu) : 0u, zp_1 = packed ? (sw1 & 0xFu) : 0u;
       if (j >= 2) failed |= !mbar_wait_spin(&bars[B_SC_FREE + b], ((j >> 1) - 1) & 1);
-      if (lane == 0 && chalf == 0) {
+      if (lane == 0 && dd == 0) {
         float* scb = reinterpret_cast<float*>(smem + C::OFF_SC) + b * 4;
         if (is_k)
           scb[0] = ex == -1000 ? 0.f : exp2_int(ex);
@@ -478,8 +492,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         if (j >= 2) failed |= !mbar_wait_spin(&bars[B_K_FREE + b], ((j >> 1) - 1) & 1);
         uint8_t* const kop = kop0 + b * 32768;
 #pragma unroll 1
-        for (int it = 0; it < 4; ++it) {
-          const int r = it >> 1, kb = 2 * chalf + (it & 1);  // row lane + 32 r, K-block kb (channels 64 kb ..)
+        for (int it = 0; it < 2 * BPW; ++it) {
+          const int r = it / BPW, kb = BPW * dd + it % BPW;  // row lane + 32 r, K-block kb (channels 64 kb ..)
           const int kr = lane + 32 * r;
           const uint8_t* const cell = raw + kr * C::CELL;
           const uint32_t q2 = r ? q2_1 : q2_0, zp = r ? zp_1 : zp_0;
@@ -524,8 +538,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
         if (j >= 2) failed |= !mbar_wait_spin(&bars[B_V_FREE + b], ((j >> 1) - 1) & 1);
         uint8_t* const vop = vop0 + b * 32768;
 #pragma unroll 1
-        for (int it = 0; it < 4; ++it) {
-          const int r = it >> 1, kb = 2 * chalf + (it & 1);  // row lane + 32 r, N-block kb (channels 64 kb ..)
+        for (int it = 0; it < 2 * BPW; ++it) {
+          const int r = it / BPW, kb = BPW * dd + it % BPW;  // row lane + 32 r, N-block kb (channels 64 kb ..)
           const int kr = lane + 32 * r;
           const uint8_t* const cell = raw + kr * C::CELL;
           const uint32_t q2 = r ? q2_1 : q2_0, zp = r ? zp_1 : zp_0;
@@ -557,12 +571,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
       if (lane == 0) mbar_arrive(&bars[B_RAW_EMPTY + stage]);
     }
   } else {
-    // ------------------------------------------------------------------ softmax / epilogue (warps 6..13)
-    // Two warps per TMEM lane quarter (32 query rows): warps 6-9 take keys 0-31 of every tile and channels 0-127 of
-    // O, warps 10-13 keys 32-63 and channels 128-255. The two threads of a row agree on its maximum through shared
+    // ------------------------------------------------------------------ softmax / epilogue (warps PF_SM0 ..)
+    // Two warps per TMEM lane quarter (32 query rows; a warp reaches the quarter warp % 4): the first four take keys
+    // 0-31 of every tile and channels 0-127 of O, the last four keys 32-63 and channels 128-255. The two threads of a row agree on its maximum through shared
     // memory (a named barrier per pair of warps) and add their partial sums in the epilogue.
     const int quarter = warp & 3;
-    const int half = (warp - 6) >> 2;
+    const int half = (warp - PF_SM0) >> 2;
     const int row = quarter * 32 + lane;  // TMEM lane = M-tile row
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const int pair_bar = 3 + quarter;     // named barriers 1, 2: dequant pairs
@@ -1472,7 +1486,7 @@ static int launch_prefill_main(const PrefillParams& pp, int ctas, cudaStream_t s
     if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "prefill smem attribute: %s", cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  prefill_kernel<FMT><<<ctas, PF_THREADS, PfCfg<FMT>::BYTES, st>>>(pp);
+  prefill_kernel<FMT><<<ctas, PF1_THREADS, PfCfg<FMT>::BYTES, st>>>(pp);
   return check_launch("prefill");
 }
 
