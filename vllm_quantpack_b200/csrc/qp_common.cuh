@@ -177,6 +177,12 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return r;
 }
 
+// both halves of an f16x2 set to x (round to nearest)
+__device__ __forceinline__ uint32_t h2_bits(float x) {
+  const __half2 h = __floats2half2_rn(x, x);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));

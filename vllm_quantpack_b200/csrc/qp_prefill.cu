@@ -470,14 +470,22 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
         ex = e_run_v;
       }
       const float inv = ex == -1000 ? 0.f : exp2_int(-ex);
-      const __half2 qa = __floats2half2_rn(scl0 * inv, scl0 * inv), qb = __floats2half2_rn(scl1 * inv, scl1 * inv);
-      const uint32_t q2_0 = *reinterpret_cast<const uint32_t*>(&qa), q2_1 = *reinterpret_cast<const uint32_t*>(&qb);
+      const float q_0 = scl0 * inv, q_1 = scl1 * inv;  // < 1
       const uint32_t zp_0 = packed ? (sw0 & 0xFu) : 0u, zp_1 = packed ? (sw1 & 0xFu) : 0u;
+      // int4 codes: a nibble masked into the low (high) bits of an fp16 is the subnormal u 2^-24 (16 u 2^-24), exact;
+      // one f16x2 fma then gives (u - zp) q 2^-9 = u 2^-24 (q 2^15) - zp q 2^-9 (high nibbles: q 2^11). The 2^-9 goes
+      // into the softmax factor (keys) and the output unit (values).
+      const uint32_t mlo_0 = h2_bits(q_0 * 32768.f), mhi_0 = h2_bits(q_0 * 2048.f);
+      const uint32_t mlo_1 = h2_bits(q_1 * 32768.f), mhi_1 = h2_bits(q_1 * 2048.f);
+      const uint32_t add_0 = h2_bits(-static_cast<float>(zp_0) * q_0 * (1.f / 512.f));
+      const uint32_t add_1 = h2_bits(-static_cast<float>(zp_1) * q_1 * (1.f / 512.f));
+      // int8 codes (k8v4 keys): (1152 + code) - 1152 = code, exact; then the scale q
+      const uint32_t q2_0 = h2_bits(q_0), q2_1 = h2_bits(q_1);
       if (j >= 2) failed |= !mbar_wait_spin(&bars[B_SC_FREE + b], ((j >> 1) - 1) & 1);
       if (lane == 0 && dd == 0) {
         float* scb = reinterpret_cast<float*>(smem + C::OFF_SC) + b * 4;
-        if (is_k)
-          scb[0] = ex == -1000 ? 0.f : exp2_int(ex);
+        if (is_k)  // 2^F (x 2^9 for int4 keys)
+          scb[0] = ex == -1000 ? 0.f : exp2_int(FMT == FMT_INT4 ? ex + 9 : ex);
         else
           scb[1] = __int_as_float(ex);
       }
@@ -496,11 +504,10 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
           const int r = it / BPW, kb = BPW * dd + it % BPW;  // row lane + 32 r, K-block kb (channels 64 kb ..)
           const int kr = lane + 32 * r;
           const uint8_t* const cell = raw + kr * C::CELL;
-          const uint32_t q2 = r ? q2_1 : q2_0, zp = r ? zp_1 : zp_0;
           const uint32_t rbase = (kr >> 3) * 1024 + (kr & 7) * 128, rxor = (kr & 7) << 4;
           uint8_t* const dst = kop + kb * 8192 + rbase;
           if constexpr (FMT == FMT_INT4) {
-            const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
+            const uint32_t mlo = r ? mlo_1 : mlo_0, mhi = r ? mhi_1 : mhi_0, add = r ? add_1 : add_0;
             uint2 kw[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) kw[k] = *reinterpret_cast<const uint2*>(cell + 32 * kb + 8 * k);
@@ -509,13 +516,14 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
               const uint32_t x = (i & 1) ? kw[i >> 1].y : kw[i >> 1].x;
               const uint32_t x8 = x >> 8;
               uint4 v;
-              v.x = hmul2_u32(hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b), q2);  // channels 0, 4
-              v.y = hmul2_u32(hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);  // 1, 5
-              v.z = hmul2_u32(hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b), q2);  // 2, 6
-              v.w = hmul2_u32(hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);  // 3, 7
+              v.x = hfma2_u32(x & 0x000F000Fu, mlo, add);   // channels 0, 4
+              v.y = hfma2_u32(x & 0x00F000F0u, mhi, add);   // 1, 5
+              v.z = hfma2_u32(x8 & 0x000F000Fu, mlo, add);  // 2, 6
+              v.w = hfma2_u32(x8 & 0x00F000F0u, mhi, add);  // 3, 7
               *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(i) << 4) ^ rxor)) = v;
             }
           } else {
+            const uint32_t q2 = r ? q2_1 : q2_0;
             uint2 kw[8];  // codes 64 kb .. 64 kb + 63
 #pragma unroll
             for (int k = 0; k < 8; ++k) kw[k] = *reinterpret_cast<const uint2*>(cell + 64 * kb + 8 * k);
@@ -542,8 +550,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
           const int r = it / BPW, kb = BPW * dd + it % BPW;  // row lane + 32 r, N-block kb (channels 64 kb ..)
           const int kr = lane + 32 * r;
           const uint8_t* const cell = raw + kr * C::CELL;
-          const uint32_t q2 = r ? q2_1 : q2_0, zp = r ? zp_1 : zp_0;
-          const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
+          const uint32_t mlo = r ? mlo_1 : mlo_0, mhi = r ? mhi_1 : mhi_0, add = r ? add_1 : add_0;
           const uint32_t rbase = (kr >> 3) * 1024 + (kr & 7) * 128, rxor = (kr & 7) << 4;
           uint8_t* const dst = vop + kb * 8192 + rbase;
           // the value words start 4 bytes past an 8-byte boundary: 8-byte loads from the key scale on give the
@@ -556,10 +563,10 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
             const uint32_t x = (i & 1) ? vw[(i + 1) >> 1].x : vw[i >> 1].y;
             const uint32_t x8 = x >> 8;
             uint4 v;
-            v.x = hmul2_u32(hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b), q2);
-            v.y = hmul2_u32(hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
-            v.z = hmul2_u32(hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b), q2);
-            v.w = hmul2_u32(hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
+            v.x = hfma2_u32(x & 0x000F000Fu, mlo, add);
+            v.y = hfma2_u32(x & 0x00F000F0u, mhi, add);
+            v.z = hfma2_u32(x8 & 0x000F000Fu, mlo, add);
+            v.w = hfma2_u32(x8 & 0x00F000F0u, mhi, add);
             *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(i) << 4) ^ rxor)) = v;
           }
         }
@@ -742,7 +749,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
         const float l_row = l + hsum[(half ^ 1) * 128 + row];
         wait_pv(j);
         tc_fence_after();
-        const float o_unit = e_used == -1000 ? 0.f : ldexpf(1.f, e_used);
+        const float o_unit = e_used == -1000 ? 0.f : ldexpf(1.f, e_used + 9);  // value operand x 2^-(E + 9)
         const float inv = l_row > 0.f ? o_unit / l_row : 0.f;
         const int64_t prow_i = (static_cast<int64_t>(tok) * p.nq + qh) * p.parts + w.piece;
 #pragma unroll 1
