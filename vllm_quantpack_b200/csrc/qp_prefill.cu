@@ -579,6 +579,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
     }
   } else {
     // ------------------------------------------------------------------ softmax / epilogue (warps PF_SM0 ..)
+    // (waits with the suspend hint: eight polling softmax warps would take issue slots from the dequant warps)
     // Two warps per TMEM lane quarter (32 query rows; a warp reaches the quarter warp % 4): the first four take keys
     // 0-31 of every tile and channels 0-127 of O, the last four keys 32-63 and channels 128-255. The two threads of a row agree on its maximum through shared
     // memory (a named barrier per pair of warps) and add their partial sums in the epilogue.
@@ -595,7 +596,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
     // before P(j) is stored (S_FULL(j) already implies PV(j - 2)), PV(j) in the epilogue.
     int64_t pv_seen = 0;
     auto wait_pv = [&](int64_t t) {  // until PV(t) is complete
-      for (; pv_seen <= t; ++pv_seen) failed |= !mbar_wait_spin(&bars[B_O_DONE], static_cast<uint32_t>(pv_seen & 1));
+      for (; pv_seen <= t; ++pv_seen) failed |= !mbar_wait_bounded(&bars[B_O_DONE], static_cast<uint32_t>(pv_seen & 1));
     };
     float m_used = -INFINITY, l = 0.f, qsc = 0.f;
     int e_used = -1000, lim = -1, tok = 0, qh = 0;
@@ -641,14 +642,14 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       }
       // this row's scores for keys 32 half .. 32 half + 31 of the tile (sum of the two channel halves), then S is
       // released to the next tile's QK
-      failed |= !mbar_wait_spin(&bars[B_S_FULL], static_cast<uint32_t>(j & 1));
+      failed |= !mbar_wait_bounded(&bars[B_S_FULL], static_cast<uint32_t>(j & 1));
       tc_fence_after();
       float s[32];
       tmem_ld32_sum2(tm_sa + lane_off + 32 * half, tm_sb + lane_off + 32 * half, s);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_S_FREE]);
-      failed |= !mbar_wait_spin(&bars[B_SC_FULL + b], (j >> 1) & 1);
+      failed |= !mbar_wait_bounded(&bars[B_SC_FULL + b], (j >> 1) & 1);
       const float* scb = reinterpret_cast<const float*>(smem + C::OFF_SC) + b * 4;
       const float qs_t = qsc * scb[0];               // x 2^F of the key operand
       const int key0 = w.kt * PF_BN + 32 * half;
@@ -703,7 +704,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       l += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       // the value exponent is needed only now, for the O rescale: the value warps publish it separately, so the
       // exponentials above do not wait for them
-      failed |= !mbar_wait_spin(&bars[B_SCV_FULL + b], (j >> 1) & 1);
+      failed |= !mbar_wait_bounded(&bars[B_SCV_FULL + b], (j >> 1) & 1);
       const int ev = __float_as_int(scb[1]);  // value exponent of this tile's operand
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_SC_FREE + b]);
