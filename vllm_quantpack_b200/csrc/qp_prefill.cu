@@ -137,11 +137,13 @@ struct Walk {
   bool first_of_piece, last_of_piece, new_mtile;
 };
 
+// Every warp walks the same schedule each tile, so the walk itself runs in 32-bit counters (the host keeps the
+// tile count below 2^31); 64-bit arithmetic is confined to init().
 struct Sched {
   const PrefillParams* p;
-  int64_t g, g_end;  // current / end global tile index
+  int left;          // tiles of this CTA not yet walked past, the current one included
   int kvh, m;        // current M-tile
-  int64_t m_start;   // global index of the M-tile's first tile
+  int kt;            // current key tile inside the M-tile
   int m_tiles;       // key tiles of the current M-tile
   int first_kt;      // first key tile of this CTA inside the current M-tile
   int piece;         // index of this CTA's piece of the current M-tile
@@ -151,11 +153,12 @@ struct Sched {
     p = &prm;
     cta = cta_;
     ctas = ctas_;
-    g = prm.total_tiles * cta / ctas;
-    g_end = prm.total_tiles * (cta + 1) / ctas;
+    const int64_t g = prm.total_tiles * cta / ctas;
+    const int64_t g_end = prm.total_tiles * (cta + 1) / ctas;
+    left = static_cast<int>(g_end - g);
     kvh = 0;
     m = 0;
-    m_start = 0;
+    int64_t m_start = 0;
     m_tiles = mtile_key_tiles(prm, 0);
     // advance to the M-tile holding g (M-tiles of each KV head in order)
     while (m_start + m_tiles <= g) {
@@ -166,7 +169,7 @@ struct Sched {
       }
       m_tiles = mtile_key_tiles(prm, m);
     }
-    first_kt = static_cast<int>(g - m_start);
+    first_kt = kt = static_cast<int>(g - m_start);
     // piece index inside the first M-tile: CTAs whose range starts inside it before this one. The CTA covering
     // m_start is the largest c with total * c / ctas <= m_start. (Computed once: 64-bit divisions are long
     // instruction sequences; every later M-tile of this CTA starts with this CTA, piece 0.)
@@ -175,29 +178,28 @@ struct Sched {
     while (c0 > 0 && prm.total_tiles * c0 / ctas > m_start) --c0;
     piece = cta - c0;
   }
-  __device__ bool done() const { return g >= g_end; }
+  __device__ bool done() const { return left <= 0; }
   __device__ Walk current() const {
     Walk w;
     w.kvh = kvh;
     w.m = m;
-    w.kt = static_cast<int>(g - m_start);
+    w.kt = kt;
     w.kt_end = m_tiles;
     w.piece = piece;
-    w.first_of_piece = w.kt == first_kt;
-    w.last_of_piece = (w.kt + 1 == m_tiles) || (g + 1 == g_end);
+    w.first_of_piece = kt == first_kt;
+    w.last_of_piece = (kt + 1 == m_tiles) || (left == 1);
     w.new_mtile = w.first_of_piece;
     return w;
   }
   __device__ void next() {
-    ++g;
-    if (g < g_end && g - m_start >= m_tiles) {
-      m_start += m_tiles;
+    --left;
+    if (++kt >= m_tiles && left > 0) {
       if (++m == p->mt_per_kv) {
         m = 0;
         ++kvh;
       }
       m_tiles = mtile_key_tiles(*p, m);
-      first_kt = 0;
+      kt = first_kt = 0;
       piece = 0;
     }
   }
@@ -504,8 +506,8 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
           const int r = it / BPW, kb = BPW * dd + it % BPW;  // row lane + 32 r, K-block kb (channels 64 kb ..)
           const int kr = lane + 32 * r;
           const uint8_t* const cell = raw + kr * C::CELL;
-          const uint32_t rbase = (kr >> 3) * 1024 + (kr & 7) * 128, rxor = (kr & 7) << 4;
-          uint8_t* const dst = kop + kb * 8192 + rbase;
+          // the row's 128-byte line with its swizzle folded in: chunk i of the row sits at d ^ (i << 4)
+          const uint32_t d = static_cast<uint32_t>(kop - smem) + kb * 8192 + (kr >> 3) * 1024 + (kr & 7) * 144;
           if constexpr (FMT == FMT_INT4) {
             const uint32_t mlo = r ? mlo_1 : mlo_0, mhi = r ? mhi_1 : mhi_0, add = r ? add_1 : add_0;
             uint2 kw[4];
@@ -520,7 +522,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
               v.y = hfma2_u32(x & 0x00F000F0u, mhi, add);   // 1, 5
               v.z = hfma2_u32(x8 & 0x000F000Fu, mlo, add);  // 2, 6
               v.w = hfma2_u32(x8 & 0x00F000F0u, mhi, add);  // 3, 7
-              *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(i) << 4) ^ rxor)) = v;
+              *reinterpret_cast<uint4*>(smem + (d ^ (static_cast<uint32_t>(i) << 4))) = v;
             }
           } else {
             const uint32_t q2 = r ? q2_1 : q2_0;
@@ -535,7 +537,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
               v.y = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4342u), 0x64806480u), q2);
               v.z = hmul2_u32(hsub2_u32(prmt(cc, 0x64646464u, 0x4140u), 0x64806480u), q2);
               v.w = hmul2_u32(hsub2_u32(prmt(cc, 0x64646464u, 0x4342u), 0x64806480u), q2);
-              *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(k) << 4) ^ rxor)) = v;
+              *reinterpret_cast<uint4*>(smem + (d ^ (static_cast<uint32_t>(k) << 4))) = v;
             }
           }
         }
@@ -551,8 +553,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
           const int kr = lane + 32 * r;
           const uint8_t* const cell = raw + kr * C::CELL;
           const uint32_t mlo = r ? mlo_1 : mlo_0, mhi = r ? mhi_1 : mhi_0, add = r ? add_1 : add_0;
-          const uint32_t rbase = (kr >> 3) * 1024 + (kr & 7) * 128, rxor = (kr & 7) << 4;
-          uint8_t* const dst = vop + kb * 8192 + rbase;
+          const uint32_t d = static_cast<uint32_t>(vop - smem) + kb * 8192 + (kr >> 3) * 1024 + (kr & 7) * 144;
           // the value words start 4 bytes past an 8-byte boundary: 8-byte loads from the key scale on give the
           // pairs (key scale, V0), (V1, V2), ..., (V31, value scale)
           uint2 vw[5];
@@ -567,7 +568,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
             v.y = hfma2_u32(x & 0x00F000F0u, mhi, add);
             v.z = hfma2_u32(x8 & 0x000F000Fu, mlo, add);
             v.w = hfma2_u32(x8 & 0x00F000F0u, mhi, add);
-            *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(i) << 4) ^ rxor)) = v;
+            *reinterpret_cast<uint4*>(smem + (d ^ (static_cast<uint32_t>(i) << 4))) = v;
           }
         }
         fence_async_smem();
@@ -1547,6 +1548,9 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
     ctas = pairs;
   } else {
     prefill_plan(qlen, n, after, num_kv_heads, group, device_sm_count(), &mt, &total, &ctas, &parts);
+    if (total >= (int64_t(1) << 31))  // the kernel walks its schedule in 32-bit counters
+      return set_error(QP_ERR_UNSUPPORTED, "prefill: %lld (128-query, 64-key) tiles exceed the 2^31 the schedule counts",
+                       (long long)total);
   }
   const int64_t need = qp_prefill_workspace_bytes(qlen, n, num_q_heads, num_kv_heads, head_size, tokens_after_keys);
   if (workspace_bytes < need)
