@@ -51,8 +51,16 @@ constexpr int PF_THREADS = 448;  // CTA-pair kernel: 14 warps: producer, MMA, 4 
 // tile's 64-channel blocks), 8 softmax warps
 constexpr int PF_DQ = QP_PF_DQ_WARPS;
 static_assert(PF_DQ == 4 || PF_DQ == 8, "dequant warps: 4 or 8");
+#ifndef QP_PF_SM_WARPS
+#define QP_PF_SM_WARPS 8
+#endif
+// softmax warps: one or two per TMEM lane quarter (a row's 64 keys and 256 output channels in one thread, or split
+// over two)
+constexpr int PF_SMW = QP_PF_SM_WARPS;
+static_assert(PF_SMW == 4 || PF_SMW == 8, "softmax warps: 4 or 8");
+constexpr int PF_HALVES = PF_SMW / 4;
 constexpr int PF_SM0 = 2 + PF_DQ;                // first softmax warp
-constexpr int PF1_THREADS = 32 * (PF_SM0 + 8);
+constexpr int PF1_THREADS = 32 * (PF_SM0 + PF_SMW);
 // registers per thread one CTA may hold: the register file is split over the 4 sub-partitions (16384 each), and a
 // sub-partition hosts every fourth warp
 constexpr int PF1_REGS = (16384 / (32 * ((PF1_THREADS / 32 + 3) / 4))) & ~7;
@@ -286,7 +294,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       mbar_init(&bars[B_RAW_FULL + s], 1);
       mbar_init(&bars[B_RAW_EMPTY + s], PF_DQ);
     }
-    mbar_init(&bars[B_Q_FULL], 8);
+    mbar_init(&bars[B_Q_FULL], PF_SMW);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars[B_K_FULL + b], PF_DQ / 2);
       mbar_init(&bars[B_K_FREE + b], 1);
@@ -294,13 +302,13 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       mbar_init(&bars[B_V_FREE + b], 1);
       mbar_init(&bars[B_SC_FULL + b], PF_DQ / 2);
       mbar_init(&bars[B_SCV_FULL + b], PF_DQ / 2);
-      mbar_init(&bars[B_SC_FREE + b], 8);
+      mbar_init(&bars[B_SC_FREE + b], PF_SMW);
     }
     mbar_init(&bars[B_S_FULL], 1);
-    mbar_init(&bars[B_S_FREE], 8);
-    mbar_init(&bars[B_P_FULL], 8);
+    mbar_init(&bars[B_S_FREE], PF_SMW);
+    mbar_init(&bars[B_P_FULL], PF_SMW);
     mbar_init(&bars[B_O_DONE], 1);
-    mbar_init(&bars[B_O_FREE], 8);
+    mbar_init(&bars[B_O_FREE], PF_SMW);
     mbar_init(&bars[B_FINAL], 1);
     fence_mbar_init();
   }
@@ -580,21 +588,27 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
     }
   } else {
     // ------------------------------------------------------------------ softmax / epilogue (warps PF_SM0 ..)
-    // (waits with the suspend hint: eight polling softmax warps would take issue slots from the dequant warps)
-    // Two warps per TMEM lane quarter (32 query rows; a warp reaches the quarter warp % 4): the first four take keys
-    // 0-31 of every tile and channels 0-127 of O, the last four keys 32-63 and channels 128-255. The two threads of a row agree on its maximum through shared
-    // memory (a named barrier per pair of warps) and add their partial sums in the epilogue.
+    // (waits with the suspend hint: polling softmax warps would take issue slots from the dequant warps)
+    // PF_HALVES warps per TMEM lane quarter (32 query rows; a warp reaches the quarter warp % 4). With two, the first
+    // four warps take keys 0-31 of every tile and channels 0-127 of O, the last four keys 32-63 and channels
+    // 128-255, and the two threads of a row agree on its maximum through shared memory (a named barrier per pair of
+    // warps) and add their partial sums in the epilogue; with one, a thread owns its whole row.
+    constexpr int KPT = PF_BN / PF_HALVES;   // keys of a tile per thread
+    constexpr int CPT = PF_HS / PF_HALVES;   // output channels per thread
     const int quarter = warp & 3;
-    const int half = (warp - PF_SM0) >> 2;
-    const int row = quarter * 32 + lane;  // TMEM lane = M-tile row
+    const int half = (warp - PF_SM0) >> 2;   // 0 .. PF_HALVES - 1
+    const int row = quarter * 32 + lane;     // TMEM lane = M-tile row
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const int pair_bar = 3 + quarter;     // named barriers 1, 2: dequant pairs
+    const int pair_bar = 3 + quarter;        // named barriers 3 .. 6: the two warps of a lane quarter
     float* hmax = reinterpret_cast<float*>(smem + C::OFF_HX);  // [buffer][half][row]
-    float* hsum = hmax + 2 * 2 * 128;                              // [half][row]
+    float* hsum = hmax + 2 * 2 * 128;                           // [half][row]
+    (void)pair_bar;
+    (void)hmax;
+    (void)hsum;
     int64_t j = 0;
     // PV completions seen so far. O_DONE completes one phase per tile (its PV); a parity wait is exact only while
     // the barrier is at most one phase ahead of the phase waited for, so the phases are consumed in order: PV(j - 1)
-    // before P(j) is stored (S_FULL(j) already implies PV(j - 2)), PV(j) in the epilogue.
+    // before P(j) is stored (PV(j) cannot complete before P(j) exists), PV(j) in the epilogue.
     int64_t pv_seen = 0;
     auto wait_pv = [&](int64_t t) {  // until PV(t) is complete
       for (; pv_seen <= t; ++pv_seen) failed |= !mbar_wait_bounded(&bars[B_O_DONE], static_cast<uint32_t>(pv_seen & 1));
@@ -607,12 +621,12 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       const Walk w = sch.current();
       const int b = static_cast<int>(j & 1);
       if (w.new_mtile) {
-        // this thread's half of its row of the piece's Q tile -> TMEM columns 128 + [64 half, 64 half + 64) of its
-        // lane (the previous piece's QKs are complete: this thread consumed the S of its last tile)
+        // this thread's share of its row of the piece's Q tile -> TMEM columns (128 / PF_HALVES) half + [0, 128 /
+        // PF_HALVES) of its lane (the previous piece's QKs are complete: this thread consumed the S of its last tile)
         const int64_t mt = static_cast<int64_t>(w.kvh) * p.mt_per_kv + w.m;
         const uint4* qrow = reinterpret_cast<const uint4*>(p.qprep + mt * 65536 + row * (PF_HS * 2));
 #pragma unroll 1
-        for (int c0 = 64 * half; c0 < 64 * half + 64; c0 += 32) {
+        for (int c0 = (128 / PF_HALVES) * half; c0 < (128 / PF_HALVES) * (half + 1); c0 += 32) {
           uint32_t qw[32];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -641,36 +655,44 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
         e_used = -1000;
         t_in_piece = 0;
       }
-      // this row's scores for keys 32 half .. 32 half + 31 of the tile (sum of the two channel halves), then S is
-      // released to the next tile's QK
+      // this row's scores for keys KPT half .. KPT half + KPT - 1 of the tile (sum of the two channel-half
+      // accumulators), then S is released to the next tile's QK
       failed |= !mbar_wait_bounded(&bars[B_S_FULL], static_cast<uint32_t>(j & 1));
       tc_fence_after();
-      float s[32];
-      tmem_ld32_sum2(tm_sa + lane_off + 32 * half, tm_sb + lane_off + 32 * half, s);
+      float s[KPT];
+#pragma unroll
+      for (int kk = 0; kk < KPT / 32; ++kk) {
+        float t32[32];
+        tmem_ld32_sum2(tm_sa + lane_off + KPT * half + 32 * kk, tm_sb + lane_off + KPT * half + 32 * kk, t32);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[32 * kk + i] = t32[i];
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_S_FREE]);
       failed |= !mbar_wait_bounded(&bars[B_SC_FULL + b], (j >> 1) & 1);
       const float* scb = reinterpret_cast<const float*>(smem + C::OFF_SC) + b * 4;
       const float qs_t = qsc * scb[0];               // x 2^F of the key operand
-      const int key0 = w.kt * PF_BN + 32 * half;
+      const int key0 = w.kt * PF_BN + KPT * half;
       const bool masked = w.kt * PF_BN + PF_BN - 1 > min(p.n - 1, p.vis_base);  // some row cannot see some key
       if (masked) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c)
+        for (int c = 0; c < KPT; ++c)
           if (key0 + c > lim) s[c] = -INFINITY;
       }
       float mx4[4] = {s[0], s[1], s[2], s[3]};  // four independent chains
 #pragma unroll
-      for (int c = 4; c < 32; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+      for (int c = 4; c < KPT; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
       float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      hmax[(b * 2 + half) * 128 + row] = mx;
-      // the pair leaves together if either gave up a wait (a bar.sync has no time bound)
-      if (named_bar_or(pair_bar, 64, failed)) {
-        failed = true;
-        break;
+      if constexpr (PF_HALVES == 2) {
+        hmax[(b * 2 + half) * 128 + row] = mx;
+        // the pair leaves together if either gave up a wait (a bar.sync has no time bound)
+        if (named_bar_or(pair_bar, 64, failed)) {
+          failed = true;
+          break;
+        }
+        mx = fmaxf(mx, hmax[(b * 2 + (half ^ 1)) * 128 + row]);
       }
-      mx = fmaxf(mx, hmax[(b * 2 + (half ^ 1)) * 128 + row]);
       const float mrow = mx * qs_t;
       const bool grow = mrow > m_used + PF_SLACK;  // the same in both threads of the row
       float alpha = 1.f;
@@ -682,10 +704,10 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       // P = 2^(s qs_t - m) <= 2^8 in fp16
       const float base = m_used == -INFINITY ? 0.f : m_used;
       float ls4[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pw[16];
+      uint32_t pw[KPT / 2];
       if (masked) {
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
+        for (int c = 0; c < KPT; c += 2) {
           const float p0 = s[c] == -INFINITY ? 0.f : fast_exp2(fmaf(s[c], qs_t, -base));
           const float p1 = s[c + 1] == -INFINITY ? 0.f : fast_exp2(fmaf(s[c + 1], qs_t, -base));
           ls4[(c >> 1) & 3] += p0 + p1;
@@ -694,7 +716,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
+        for (int c = 0; c < KPT; c += 2) {
           const float p0 = fast_exp2(fmaf(s[c], qs_t, -base));
           const float p1 = fast_exp2(fmaf(s[c + 1], qs_t, -base));
           ls4[(c >> 1) & 3] += p0 + p1;
@@ -712,12 +734,12 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       const bool vgrow = ev > e_used;  // the same for every thread
       wait_pv(j - 1);  // PV(j - 1) has read P(j - 1) and added into O
       if (__any_sync(0xffffffffu, alpha != 1.f) || vgrow) {
-        // rescale this thread's half of the row's O in TMEM: new running maximum and / or value exponent
+        // rescale this thread's channels of the row's O in TMEM: new running maximum and / or value exponent
         const float ao = alpha * (!vgrow ? 1.f : e_used == -1000 ? 0.f : ldexpf(1.f, e_used - ev));
         if (t_in_piece > 0) {
           tc_fence_after();
 #pragma unroll 1
-          for (int c0 = 128 * half; c0 < 128 * half + 128; c0 += 32) {
+          for (int c0 = CPT * half; c0 < CPT * (half + 1); c0 += 32) {
             float o[32];
             tmem_ld32(tm_o + lane_off + c0, o);
 #pragma unroll
@@ -727,13 +749,13 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
         }
         if (vgrow) e_used = ev;
       }
-      // P -> shared memory, row `row`, keys 32 half .. + 31 = 16-byte chunks 4 half .. 4 half + 3 of the row (the
+      // P -> shared memory, row `row`, keys KPT half .. + KPT - 1 = 16-byte chunks (KPT / 8) half .. of the row (the
       // A operand of the PV MMA, K-major, 128B-swizzled; the 8 rows of a store phase hit 8 distinct bank groups)
       {
         uint8_t* const prow = smem + C::OFF_P;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          *reinterpret_cast<uint4*>(prow + sw128_off(row, 4 * half + i)) =
+        for (int i = 0; i < KPT / 8; ++i)
+          *reinterpret_cast<uint4*>(prow + sw128_off(row, (KPT / 8) * half + i)) =
               make_uint4(pw[4 * i], pw[4 * i + 1], pw[4 * i + 2], pw[4 * i + 3]);
       }
       fence_async_smem();
@@ -743,19 +765,22 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
 
       if (w.last_of_piece) {
         // epilogue: O of this piece -> normalised fp32 partial (channel order restored) + base-2 lse
-        hsum[half * 128 + row] = l;
-        if (named_bar_or(pair_bar, 64, failed)) {
-          failed = true;
-          break;
+        float l_row = l;
+        if constexpr (PF_HALVES == 2) {
+          hsum[half * 128 + row] = l;
+          if (named_bar_or(pair_bar, 64, failed)) {
+            failed = true;
+            break;
+          }
+          l_row += hsum[(half ^ 1) * 128 + row];
         }
-        const float l_row = l + hsum[(half ^ 1) * 128 + row];
         wait_pv(j);
         tc_fence_after();
         const float o_unit = e_used == -1000 ? 0.f : ldexpf(1.f, e_used + 9);  // value operand x 2^-(E + 9)
         const float inv = l_row > 0.f ? o_unit / l_row : 0.f;
         const int64_t prow_i = (static_cast<int64_t>(tok) * p.nq + qh) * p.parts + w.piece;
 #pragma unroll 1
-        for (int c0 = 128 * half; c0 < 128 * half + 128; c0 += 32) {
+        for (int c0 = CPT * half; c0 < CPT * (half + 1); c0 += 32) {
           float o[32];
           tmem_ld32(tm_o + lane_off + c0, o);
           if (row_ok && w.piece < p.parts) {
