@@ -1034,7 +1034,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill2_kernel(const Prefill2P
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (even CTA)
-    if (leader && lane == 0) {
+    // The whole warp walks the schedule and waits (warp-uniform values for the descriptors); one elected lane issues.
+    if (leader) {
       constexpr uint32_t ID_QK = f16_idesc(P2_BM, P2_BN, false);
       constexpr uint32_t ID_PV = f16_idesc(P2_BM, PF_HS, true);
       const uint32_t q_base = smem_u32(smem + C::OFF_Q), k_base = smem_u32(smem + C::OFF_K);
@@ -1043,46 +1044,55 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill2_kernel(const Prefill2P
       int qcount = 0, pieces = 0;
       int64_t pv_pending = -1;
       bool pv_first = false;
+      auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+        const bool ok = mbar_wait_bounded_cluster(bar, parity);
+        failed |= __any_sync(0xffffffffu, !ok);
+      };
       auto issue_pv = [&](int64_t t, bool first) {
         const int b = static_cast<int>(t & 1);
-        failed |= !mbar_wait_bounded_cluster(&bars[C_V_FULL + b], (t >> 1) & 1);
-        failed |= !mbar_wait_bounded_cluster(&bars[C_P_FULL + b], (t >> 1) & 1);
+        wait_all(&bars[C_V_FULL + b], (t >> 1) & 1);
+        wait_all(&bars[C_P_FULL + b], (t >> 1) & 1);
         tc_fence_after();
         const uint32_t vb = v_base + b * 32768;
-        // P(t) in TMEM (each CTA's lanes), K step s = 16 keys = 8 columns; value operand: 2 N-blocks of 64
-        // channels per CTA (stride 16 KB), 8-key groups of 1024 B
+        if (elect_one()) {
+          // P(t) in TMEM (each CTA's lanes), K step s = 16 keys = 8 columns; value operand: 2 N-blocks of 64
+          // channels per CTA (stride 16 KB), 8-key groups of 1024 B
 #pragma unroll
-        for (int s = 0; s < 8; ++s)
-          umma2_f16_ts(tm_o, tmem + 128 * b + 8 * s, sw128_desc(vb + 2 * s * 1024, 16384, 1024), ID_PV,
-                       (first && s == 0) ? 0u : 1u);
-        umma2_commit_mc(&bars[C_V_FREE + b], 3);
-        umma2_commit_mc(&bars[C_O_DONE], 3);
+          for (int s = 0; s < 8; ++s)
+            umma2_f16_ts(tm_o, tmem + 128 * b + 8 * s, sw128_desc(vb + 2 * s * 1024, 16384, 1024), ID_PV,
+                         (first && s == 0) ? 0u : 1u);
+          umma2_commit_mc(&bars[C_V_FREE + b], 3);
+          umma2_commit_mc(&bars[C_O_DONE], 3);
+        }
+        __syncwarp();
       };
       for (; !sch.done() && !failed; sch.next(), ++j) {
         const Walk w = sch.current();
         if (w.new_mtile) {
-          failed |= !mbar_wait_bounded_cluster(&bars[C_Q_BOTH], qcount & 1);
+          wait_all(&bars[C_Q_BOTH], qcount & 1);
           ++qcount;
         }
         const int b = static_cast<int>(j & 1);
-        failed |= !mbar_wait_bounded_cluster(&bars[C_K_FULL + b], (j >> 1) & 1);
+        wait_all(&bars[C_K_FULL + b], (j >> 1) & 1);
         // S buffer b last held S(j - 2) and P(j - 2); the PV of that tile, issued before these MMAs, waited for both
         // CTAs' softmax to finish with it
         tc_fence_after();
         const uint32_t kb = k_base + b * 32768;
+        if (elect_one()) {
 #pragma unroll
-        for (int s = 0; s < 16; ++s)
-          umma2_f16(tmem + 128 * b, sw128_desc(q_base + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024),
-                    sw128_desc(kb + (s >> 2) * 8192 + (s & 3) * 32, 16, 1024), ID_QK, s > 0 ? 1u : 0u);
-        umma2_commit_mc(&bars[C_K_FREE + b], 3);
-        umma2_commit_mc(&bars[C_S_FULL + b], 3);
-        if (w.last_of_piece) umma2_commit_mc(&bars[C_Q_EMPTY], 3);
+          for (int s = 0; s < 16; ++s)
+            umma2_f16(tmem + 128 * b, sw128_desc(q_base + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024),
+                      sw128_desc(kb + (s >> 2) * 8192 + (s & 3) * 32, 16, 1024), ID_QK, s > 0 ? 1u : 0u);
+          umma2_commit_mc(&bars[C_K_FREE + b], 3);
+          umma2_commit_mc(&bars[C_S_FULL + b], 3);
+          if (w.last_of_piece) umma2_commit_mc(&bars[C_Q_EMPTY], 3);
+        }
+        __syncwarp();
         if (pv_pending >= 0) {
           issue_pv(pv_pending, pv_first);
           pv_pending = -1;
         }
-        if (w.first_of_piece && pieces > 0)
-          failed |= !mbar_wait_bounded_cluster(&bars[C_O_FREE], (pieces - 1) & 1);
+        if (w.first_of_piece && pieces > 0) wait_all(&bars[C_O_FREE], (pieces - 1) & 1);
         if (w.first_of_piece) ++pieces;
         pv_pending = j;
         pv_first = w.first_of_piece;
@@ -1091,7 +1101,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill2_kernel(const Prefill2P
           pv_pending = -1;
         }
       }
-      umma2_commit_mc(&bars[C_FINAL], 3);
+      if (elect_one()) umma2_commit_mc(&bars[C_FINAL], 3);
+      __syncwarp();
     }
     if (lane == 0) mbar_wait_bounded(&bars[C_FINAL], 0, 100000000ull);  // both CTAs: every MMA of the pair done
     __syncwarp();
