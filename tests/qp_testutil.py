@@ -64,12 +64,28 @@ class Cache:
         ops.reshape_and_cache_int4(k, v, kc, vc, torch.as_tensor(slots, device=dev), k_scale_cache=ks,
                                    v_scale_cache=vs, rotate=rotate)
 
-    def fill(self, block_row, n, seed, chunk=32768):
-        """Store n seeded tokens (synthetic K/V with outlier channels) at positions 0..n-1 of block_row."""
+    def fill(self, block_row, n, seed, chunk=32768, spread=0.0, grow=0.0):
+        """Store n seeded tokens (synthetic K/V with outlier channels) at positions 0..n-1 of block_row.
+        spread > 0 scales each (token, head) of K and of V by 10^u, u ~ U(-spread, spread) (scales that differ by
+        orders of magnitude inside one tile); grow > 0 multiplies position i by 1 + grow i / n (row maxima and value
+        scales that keep rising, so the kernels' rescale paths run)."""
         row = np.asarray(block_row, dtype=np.int64)
+        rng = np.random.default_rng(seed + 77)
         for s in range(0, n, chunk):
             e = min(n, s + chunk)
             kb, vb = qo.synthetic_kv(e - s, self.nkv, self.hs, seed=seed * 1000 + s // chunk)
+            if spread > 0 or grow > 0:
+                fk = np.ones((e - s, self.nkv, 1), np.float32)
+                fv = np.ones((e - s, self.nkv, 1), np.float32)
+                if spread > 0:
+                    fk *= 10.0 ** rng.uniform(-spread, spread, fk.shape).astype(np.float32)
+                    fv *= 10.0 ** rng.uniform(-spread, spread, fv.shape).astype(np.float32)
+                if grow > 0:
+                    g = (1.0 + grow * np.arange(s, e, dtype=np.float32) / n)[:, None, None]
+                    fk *= g
+                    fv *= g
+                kb = qo.from_f32(qo.to_f32(kb, "bf16") * fk, "bf16")
+                vb = qo.from_f32(qo.to_f32(vb, "bf16") * fv, "bf16")
             pos = np.arange(s, e)
             slots = row[pos // self.block_size] * self.block_size + pos % self.block_size
             self.store(kb, vb, slots)

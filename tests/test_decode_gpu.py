@@ -17,11 +17,11 @@ pytestmark = pytest.mark.gpu
 TOL = 5e-3
 
 
-def run_case(device, fmt, qlens, lens, bs, dtype="bf16", num_splits=None, seed=0):
+def run_case(device, fmt, qlens, lens, bs, dtype="bf16", num_splits=None, seed=0, **fill_kw):
     table, nblocks = U.block_tables(lens, bs, seed=seed + 1)
     cache = U.Cache(fmt, nblocks, bs, device)
     for i, n in enumerate(lens):
-        cache.fill(table[i], n, seed=seed + i)
+        cache.fill(table[i], n, seed=seed + i, **fill_kw)
     qb = U.make_queries(qlens, seed=seed + 5, dtype=dtype)
     out = U.decode(cache, qb, qlens, lens, table, dtype=dtype, num_splits=num_splits)
     ref = U.reference(cache.host_bytes(), cache.layout, qb, qlens, lens, table, dtype=dtype)
@@ -37,6 +37,14 @@ def run_case(device, fmt, qlens, lens, bs, dtype="bf16", num_splits=None, seed=0
 @pytest.mark.parametrize("qlen", [1, 2, 3, 4], ids=["decode", "mtp-decode", "mtp2-decode", "mtp3-decode"])
 def test_decode_matches_fp64(device, fmt, qlen):
     errs = run_case(device, fmt, [qlen], [16384], 16)
+    assert errs[0] < TOL, errs
+
+
+@pytest.mark.parametrize("fmt", ["int4", "k8v4"])
+def test_scales_spread_and_rising(device, fmt):
+    """Per-token K / V magnitudes spread over two orders of magnitude and rising along the context (the lazy
+    maximum and the value range both grow: the rescale slow path runs)."""
+    errs = run_case(device, fmt, [4], [12000], 16, spread=1.0, grow=3.0)
     assert errs[0] < TOL, errs
 
 

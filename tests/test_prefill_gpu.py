@@ -41,10 +41,10 @@ def reference_rows(cache_bytes, layout, table_row, q_bits, n, rows, dtype="bf16"
     return np.concatenate(out)
 
 
-def prefill_case(device, fmt, qlen, n, bs, dtype="bf16", rows=None, seed=0):
+def prefill_case(device, fmt, qlen, n, bs, dtype="bf16", rows=None, seed=0, **fill_kw):
     table, nblocks = U.block_tables([n], bs, seed=seed + 1)
     cache = U.Cache(fmt, nblocks, bs, device)
-    cache.fill(table[0], n, seed=seed)
+    cache.fill(table[0], n, seed=seed, **fill_kw)
     qb = U.make_queries([qlen], seed=seed + 3, dtype=dtype)
     out = run_prefill(device, cache, table[0], qb, n, dtype)
     rows = list(range(qlen)) if rows is None else rows
@@ -60,6 +60,15 @@ def test_small_chunk(device, fmt):
 @pytest.mark.parametrize("fmt", ["int4", "k8v4"])
 def test_chunk_256_over_16k(device, fmt):
     err = prefill_case(device, fmt, 256, 16384, 16, rows=[0, 1, 63, 64, 127, 128, 200, 255])
+    assert err < TOL, err
+
+
+@pytest.mark.parametrize("fmt", ["int4", "k8v4"])
+def test_scales_spread_and_rising(device, fmt):
+    """Per-token K / V magnitudes spread over two orders of magnitude inside every tile and rising along the
+    sequence (row maxima and value exponents keep growing: the O rescale paths run). The operands are fp16 (as the
+    reference's are bf16), so logits many times larger than these leave the 0.5 % bound for any such path."""
+    err = prefill_case(device, fmt, 256, 8192, 16, rows=[0, 1, 100, 128, 255], spread=1.0, grow=3.0)
     assert err < TOL, err
 
 

@@ -78,8 +78,10 @@ struct PfCfg {
   static constexpr int OFF_V = OFF_K + 65536;           // 2 buffers x 4 N-blocks x 8 key groups x 1024 B = 64 KB
   static constexpr int OFF_P = OFF_V + 65536;           // P: 128 rows x 64 keys fp16, K-major, 128B-swizzled = 16 KB
   static constexpr int OFF_RAW = OFF_P + 16384;         // RS x RAW_BYTES
-  static constexpr int OFF_SC = OFF_RAW + RS * RAW_BYTES;  // [2 buffers][key factor 2^F, value exponent E] (16 B)
-  static constexpr int OFF_HX = OFF_SC + 2 * 16;          // softmax pairs: [2 buffers][2 halves][128] row maxima,
+  // [2 buffers][64 key scales (fp32), value exponent E, 3 spare] (272 B each)
+  static constexpr int SC_STRIDE = 68;
+  static constexpr int OFF_SC = OFF_RAW + RS * RAW_BYTES;
+  static constexpr int OFF_HX = OFF_SC + 2 * SC_STRIDE * 4;  // softmax pairs: [2 buffers][2 halves][128] row maxima,
                                                          // then [2 halves][128] row sums
   static constexpr int OFF_BAR = OFF_HX + (2 * 2 * 128 + 2 * 128) * 4;
   static constexpr int NBAR = 40;
@@ -286,7 +288,6 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_TMEM);
-  float* sc = reinterpret_cast<float*>(smem + C::OFF_SC);  // [buf][ks 64 | vs 64]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
@@ -444,9 +445,11 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
     mbar_wait_spin(&bars[B_FINAL], 0, 100000000ull);
   } else if (warp < PF_SM0) {
     // ------------------------------------------------------------------ dequant (warps 2 .. PF_SM0 - 1)
-    // keys:   K_op = (u - zp) * ks * 2^-F  (F: exponent of the tile's largest key scale; 2^F goes to the softmax)
+    // keys:   K_op = u - zp (int4) or the int8 code, exact in fp16; the key scale multiplies the score in fp32 in
+    //         the softmax. (A scale folded into the operand would be one fp16 rounding shared by all 256 channels of
+    //         a key, a relative error of the whole score that the exponential amplifies at large logits.)
     // values: V_op = (u - zp) * vs * 2^-E  (E: running exponent of the piece's largest value scale; O is rescaled by
-    //         the softmax when E grows). Every operand is then <= 15 in magnitude and exact up to one fp16 rounding.
+    //         the softmax when E grows): <= 15 in magnitude, exact up to one fp16 rounding.
     // The first PF_DQ / 2 warps convert the keys, the others the values; each warp takes BPW of the four 64-channel
     // blocks for all 64 rows of the tile (lane l: rows l and l + 32). Every warp sees all 64 scales of its operand:
     // the tile maximum is one warp reduction, with no exchange between warps.
@@ -472,32 +475,31 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       const uint32_t sw1 = *reinterpret_cast<const uint32_t*>(raw + (lane + 32) * C::CELL + sc_off);
       const float scl0 = tok0 < p.n ? __uint_as_float(packed ? (sw0 & 0xFFFFFFF0u) : sw0) : 0.f;
       const float scl1 = tok0 + 32 < p.n ? __uint_as_float(packed ? (sw1 & 0xFFFFFFF0u) : sw1) : 0.f;
-      const float tmax = warp_max(fmaxf(scl0, scl1));  // scales are >= 0
-      // tmax < 2^ex (the exponent field; subnormals give -126, still a bound)
-      int ex = tmax > 0.f ? static_cast<int>((__float_as_uint(tmax) >> 23) & 0xFFu) - 126 : -1000;
+      int ex = -1000;
       if (!is_k) {
+        const float tmax = warp_max(fmaxf(scl0, scl1));  // scales are >= 0
+        // tmax < 2^ex (the exponent field; subnormals give -126, still a bound)
+        if (tmax > 0.f) ex = static_cast<int>((__float_as_uint(tmax) >> 23) & 0xFFu) - 126;
         e_run_v = max(e_run_v, ex);
         ex = e_run_v;
       }
       const float inv = ex == -1000 ? 0.f : exp2_int(-ex);
       const float q_0 = scl0 * inv, q_1 = scl1 * inv;  // < 1
       const uint32_t zp_0 = packed ? (sw0 & 0xFu) : 0u, zp_1 = packed ? (sw1 & 0xFu) : 0u;
-      // int4 codes: a nibble masked into the low (high) bits of an fp16 is the subnormal u 2^-24 (16 u 2^-24), exact;
-      // one f16x2 fma then gives (u - zp) q 2^-9 = u 2^-24 (q 2^15) - zp q 2^-9 (high nibbles: q 2^11). The 2^-9 goes
-      // into the softmax factor (keys) and the output unit (values).
-      const uint32_t mlo_0 = h2_bits(q_0 * 32768.f), mhi_0 = h2_bits(q_0 * 2048.f);
-      const uint32_t mlo_1 = h2_bits(q_1 * 32768.f), mhi_1 = h2_bits(q_1 * 2048.f);
-      const uint32_t add_0 = h2_bits(-static_cast<float>(zp_0) * q_0 * (1.f / 512.f));
-      const uint32_t add_1 = h2_bits(-static_cast<float>(zp_1) * q_1 * (1.f / 512.f));
-      // int8 codes (k8v4 keys): (1152 + code) - 1152 = code, exact; then the scale q
+      // int4 (u - zp) exact from the exponent-bias forms (1024 + u) - (1024 + zp) and (1024 + 16 u) / 16 - (64 + zp),
+      // int8 codes from (1152 + code) - 1152; values then times their fp16 scale q, rounded once. (Folding the zero
+      // point into one fma, u 2^-24 q' - zp q'', rounds the zero-point term on its own: the same error in all
+      // channels of a token.)
       const uint32_t q2_0 = h2_bits(q_0), q2_1 = h2_bits(q_1);
       if (j >= 2) failed |= !mbar_wait_spin(&bars[B_SC_FREE + b], ((j >> 1) - 1) & 1);
-      if (lane == 0 && dd == 0) {
-        float* scb = reinterpret_cast<float*>(smem + C::OFF_SC) + b * 4;
-        if (is_k)  // 2^F (x 2^9 for int4 keys)
-          scb[0] = ex == -1000 ? 0.f : exp2_int(FMT == FMT_INT4 ? ex + 9 : ex);
-        else
-          scb[1] = __int_as_float(ex);
+      if (dd == 0) {
+        float* scb = reinterpret_cast<float*>(smem + C::OFF_SC) + b * C::SC_STRIDE;
+        if (is_k) {  // the 64 key scales of the tile (0 past the context)
+          scb[lane] = scl0;
+          scb[lane + 32] = scl1;
+        } else if (lane == 0) {
+          scb[64] = __int_as_float(ex);
+        }
       }
       // the softmax needs only these factors: release them now, not after the (longer) operand conversion
       __syncwarp();
@@ -517,7 +519,8 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
           // the row's 128-byte line with its swizzle folded in: chunk i of the row sits at d ^ (i << 4)
           const uint32_t d = static_cast<uint32_t>(kop - smem) + kb * 8192 + (kr >> 3) * 1024 + (kr & 7) * 144;
           if constexpr (FMT == FMT_INT4) {
-            const uint32_t mlo = r ? mlo_1 : mlo_0, mhi = r ? mhi_1 : mhi_0, add = r ? add_1 : add_0;
+            const uint32_t zp = r ? zp_1 : zp_0;
+            const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
             uint2 kw[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) kw[k] = *reinterpret_cast<const uint2*>(cell + 32 * kb + 8 * k);
@@ -526,25 +529,24 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
               const uint32_t x = (i & 1) ? kw[i >> 1].y : kw[i >> 1].x;
               const uint32_t x8 = x >> 8;
               uint4 v;
-              v.x = hfma2_u32(x & 0x000F000Fu, mlo, add);   // channels 0, 4
-              v.y = hfma2_u32(x & 0x00F000F0u, mhi, add);   // 1, 5
-              v.z = hfma2_u32(x8 & 0x000F000Fu, mlo, add);  // 2, 6
-              v.w = hfma2_u32(x8 & 0x00F000F0u, mhi, add);  // 3, 7
+              v.x = hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b);                      // channels 0, 4
+              v.y = hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b);         // 1, 5
+              v.z = hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b);                     // 2, 6
+              v.w = hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b);        // 3, 7
               *reinterpret_cast<uint4*>(smem + (d ^ (static_cast<uint32_t>(i) << 4))) = v;
             }
           } else {
-            const uint32_t q2 = r ? q2_1 : q2_0;
             uint2 kw[8];  // codes 64 kb .. 64 kb + 63
 #pragma unroll
             for (int k = 0; k < 8; ++k) kw[k] = *reinterpret_cast<const uint2*>(cell + 64 * kb + 8 * k);
 #pragma unroll
             for (int k = 0; k < 8; ++k) {  // chunk k: channels 8 (8 kb + k) .. + 7 (two words)
               const uint32_t a = kw[k].x ^ 0x80808080u, cc = kw[k].y ^ 0x80808080u;
-              uint4 v;  // (1152 + code) - 1152 = code, exact; then the scale
-              v.x = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4140u), 0x64806480u), q2);
-              v.y = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4342u), 0x64806480u), q2);
-              v.z = hmul2_u32(hsub2_u32(prmt(cc, 0x64646464u, 0x4140u), 0x64806480u), q2);
-              v.w = hmul2_u32(hsub2_u32(prmt(cc, 0x64646464u, 0x4342u), 0x64806480u), q2);
+              uint4 v;  // (1152 + code) - 1152 = code, exact
+              v.x = hsub2_u32(prmt(a, 0x64646464u, 0x4140u), 0x64806480u);
+              v.y = hsub2_u32(prmt(a, 0x64646464u, 0x4342u), 0x64806480u);
+              v.z = hsub2_u32(prmt(cc, 0x64646464u, 0x4140u), 0x64806480u);
+              v.w = hsub2_u32(prmt(cc, 0x64646464u, 0x4342u), 0x64806480u);
               *reinterpret_cast<uint4*>(smem + (d ^ (static_cast<uint32_t>(k) << 4))) = v;
             }
           }
@@ -560,7 +562,8 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
           const int r = it / BPW, kb = BPW * dd + it % BPW;  // row lane + 32 r, N-block kb (channels 64 kb ..)
           const int kr = lane + 32 * r;
           const uint8_t* const cell = raw + kr * C::CELL;
-          const uint32_t mlo = r ? mlo_1 : mlo_0, mhi = r ? mhi_1 : mhi_0, add = r ? add_1 : add_0;
+          const uint32_t q2 = r ? q2_1 : q2_0, zp = r ? zp_1 : zp_0;
+          const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
           const uint32_t d = static_cast<uint32_t>(vop - smem) + kb * 8192 + (kr >> 3) * 1024 + (kr & 7) * 144;
           // the value words start 4 bytes past an 8-byte boundary: 8-byte loads from the key scale on give the
           // pairs (key scale, V0), (V1, V2), ..., (V31, value scale)
@@ -572,10 +575,10 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
             const uint32_t x = (i & 1) ? vw[(i + 1) >> 1].x : vw[i >> 1].y;
             const uint32_t x8 = x >> 8;
             uint4 v;
-            v.x = hfma2_u32(x & 0x000F000Fu, mlo, add);
-            v.y = hfma2_u32(x & 0x00F000F0u, mhi, add);
-            v.z = hfma2_u32(x8 & 0x000F000Fu, mlo, add);
-            v.w = hfma2_u32(x8 & 0x00F000F0u, mhi, add);
+            v.x = hmul2_u32(hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b), q2);
+            v.y = hmul2_u32(hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
+            v.z = hmul2_u32(hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b), q2);
+            v.w = hmul2_u32(hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
             *reinterpret_cast<uint4*>(smem + (d ^ (static_cast<uint32_t>(i) << 4))) = v;
           }
         }
@@ -671,8 +674,17 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_S_FREE]);
       failed |= !mbar_wait_bounded(&bars[B_SC_FULL + b], (j >> 1) & 1);
-      const float* scb = reinterpret_cast<const float*>(smem + C::OFF_SC) + b * 4;
-      const float qs_t = qsc * scb[0];               // x 2^F of the key operand
+      const float* scb = reinterpret_cast<const float*>(smem + C::OFF_SC) + b * C::SC_STRIDE;
+      // the scores in fp32: key operand (exact codes) . Q, times the key's scale
+#pragma unroll
+      for (int c4 = 0; c4 < KPT; c4 += 4) {
+        const float4 f = *reinterpret_cast<const float4*>(scb + KPT * half + c4);
+        s[c4] *= f.x;
+        s[c4 + 1] *= f.y;
+        s[c4 + 2] *= f.z;
+        s[c4 + 3] *= f.w;
+      }
+      const float qs_t = qsc;
       const int key0 = w.kt * PF_BN + KPT * half;
       const bool masked = w.kt * PF_BN + PF_BN - 1 > min(p.n - 1, p.vis_base);  // some row cannot see some key
       if (masked) {
@@ -728,7 +740,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       // the value exponent is needed only now, for the O rescale: the value warps publish it separately, so the
       // exponentials above do not wait for them
       failed |= !mbar_wait_bounded(&bars[B_SCV_FULL + b], (j >> 1) & 1);
-      const int ev = __float_as_int(scb[1]);  // value exponent of this tile's operand
+      const int ev = __float_as_int(scb[64]);  // value exponent of this tile's operand
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_SC_FREE + b]);
       const bool vgrow = ev > e_used;  // the same for every thread
@@ -776,7 +788,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
         }
         wait_pv(j);
         tc_fence_after();
-        const float o_unit = e_used == -1000 ? 0.f : ldexpf(1.f, e_used + 9);  // value operand x 2^-(E + 9)
+        const float o_unit = e_used == -1000 ? 0.f : ldexpf(1.f, e_used);  // value operand x 2^-E
         const float inv = l_row > 0.f ? o_unit / l_row : 0.f;
         const int64_t prow_i = (static_cast<int64_t>(tok) * p.nq + qh) * p.parts + w.piece;
 #pragma unroll 1
