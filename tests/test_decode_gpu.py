@@ -42,9 +42,9 @@ def test_decode_matches_fp64(device, fmt, qlen):
 
 @pytest.mark.parametrize("fmt", ["int4", "k8v4"])
 def test_scales_spread_and_rising(device, fmt):
-    """Per-token K / V magnitudes spread over two orders of magnitude and rising along the context (the lazy
-    maximum and the value range both grow: the rescale slow path runs)."""
-    errs = run_case(device, fmt, [4], [12000], 16, spread=1.0, grow=3.0)
+    """Per-token K / V magnitudes spread over four orders of magnitude and rising sevenfold along the context (the
+    lazy maximum and the value range both grow: the rescale slow path runs)."""
+    errs = run_case(device, fmt, [4], [12000], 16, spread=2.0, grow=6.0)
     assert errs[0] < TOL, errs
 
 
