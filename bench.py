@@ -45,7 +45,7 @@ WORKLOADS = {
 CELL = {"int4": HS + 8, "k8v4": HS * 3 // 2 + 8}
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of that workload (profiles/):
 # decode_kernel at c2a and c1, prefill_kernel at c3.
-TRAFFIC = {"c2a": 277.01e6 + 3.97e6, "c3": 9.930e9 + 0.0370e9}
+TRAFFIC = {"c2a": 277.01e6 + 3.97e6, "c3": 9.940e9 + 0.0340e9}
 
 
 def algorithmic_bytes(w, seqs=None):
