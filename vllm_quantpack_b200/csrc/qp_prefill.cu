@@ -6,26 +6,27 @@
 // context, causal inside the chunk, RHT domain, scale softmax_scale / head), which the reference runs as 16k-token
 // bf16 unpacks + FlashAttention 2 + an fp32 log-sum-exp fold, and the 2D Triton path (int4_kv.py:113-119).
 //
-// B200 design (one persistent CTA of 14 warps per SM):
+// B200 design (one persistent CTA of 18 warps per SM):
 //   warp 0      producer: 1-D bulk copies of the raw 264 / 392-byte cells of a 64-key tile (whole 16-key runs) into a
 //               ring of raw stages;
-//   warp 1      MMA issuer (one thread): S = Q K^T (M 128 rows, N 64 keys, K 256; Q read from TMEM) into TMEM as two
-//               interleaved accumulation chains over the two channel halves, then O += P V (M 128, N 256 channels,
-//               K 64 keys; P from shared memory) into TMEM, each finished with tcgen05.commit onto mbarriers;
-//   warps 2-5   dequant into double-buffered key and value operand tiles (the conversion of tile j + 1 overlaps the
-//               MMAs of tile j): raw cells -> fp16 operands in shared memory, 128B-swizzled canonical UMMA layouts. One lop3
-//               turns two nibbles into fp16, one f16x2 subtract makes the exact (u - zp) (int8 codes for k8v4 keys),
-//               one f16x2 multiply applies the token's scale over a power of two (the tile's largest key scale; the
-//               piece's running largest value scale), so the softmax never touches per-key scales. The channel order
-//               inside every 8 channels is [0 4 1 5 2 6 3 7] (what one lop3 pair yields), the same for Q and K (a dot
-//               product does not see the order) and undone on O in the epilogue;
-//   warps 6-13  softmax: two threads per TMEM lane (= query row), 32 keys each; at the start of each piece they store
+//   warp 1      MMA issuer (convergent; one lane chosen by elect.sync issues): S = Q K^T (M 128 rows, N 64 keys,
+//               K 256; Q read from TMEM) into TMEM as two interleaved accumulation chains over the two channel halves,
+//               then O += P V (M 128, N 256 channels, K 64 keys; P from shared memory) into TMEM, each finished with
+//               tcgen05.commit onto mbarriers;
+//   warps 2-9   dequant (4 key warps, 4 value warps, one 64-channel block of all 64 keys each) into double-buffered
+//               key and value operand tiles (the conversion of tile j + 1 overlaps the MMAs of tile j): raw cells ->
+//               fp16 operands in shared memory, 128B-swizzled canonical UMMA layouts. One lop3 turns two nibbles into
+//               fp16 and one f16x2 subtract makes the exact (u - zp) (int8 codes for k8v4 keys). Key operands stay
+//               exact codes (the 64 key scales of the tile go to shared memory and multiply the scores in fp32); value
+//               operands are multiplied by the token's scale over a power of two (the piece's running largest value
+//               scale). The channel order inside every 8 channels is [0 4 1 5 2 6 3 7] (what one lop3 pair yields),
+//               the same for Q and K (a dot product does not see the order) and undone on O in the epilogue;
+//   warps 10-17 softmax: two threads per TMEM lane (= query row), 32 keys each; at the start of each piece they store
 //               their row of the prepared Q tile into TMEM (columns 0-127). S is read into registers and released at
 //               once (the next tile's QK runs behind the PV of the previous one meanwhile). Scores in log2 units =
-//               S x (softmax_scale / head x log2 e x 2^-row exponent x 2^key-tile exponent); the running maximum is
-//               lazy and per row (P may reach 2^8 before O is rescaled in TMEM, which is rare); P in fp16 goes to
-//               shared memory as the A operand of the PV MMA. The epilogue reads O from TMEM and writes fp32
-//               partials + base-2 lse.
+//               S x key scale x (softmax_scale / head x log2 e x 2^-row exponent); the running maximum is lazy and
+//               per row (P may reach 2^8 before O is rescaled in TMEM, which is rare); P in fp16 goes to shared memory
+//               as the A operand of the PV MMA. The epilogue reads O from TMEM and writes fp32 partials + base-2 lse.
 // Rows of an M-tile are (query token, query head of the KV head's group) pairs, head fastest: the 6 heads of a group
 // share every dequantised key / value tile. The (M-tile, key-tile) space is split evenly over the CTAs (stream-K):
 // an M-tile may be finished by two CTAs, whose partials the merge kernel folds (with the inverse RHT).
@@ -102,7 +103,7 @@ enum {
   B_S_FULL = 18,     // S (both channel halves) of the tile is in TMEM
   B_S_FREE = 19,     // the softmax has read S into registers (8 softmax warps)
   B_P_FULL = 22,     // P of the tile is in shared memory (8 softmax warps)
-  B_SC_FULL = 26,    // [2] the tile's key factor 2^F (key warps)
+  B_SC_FULL = 26,    // [2] the tile's 64 key scales are in shared memory (key warps)
   B_SC_FREE = 28,    // [2]
   B_O_DONE = 30,
   B_O_FREE = 31,
