@@ -307,7 +307,7 @@ def run_prefill(args, w, rank, world, local_rank):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": TRAFFIC.get(args.workload),
                          "traffic_unit": "bytes per launch (ncu dram__bytes_read + write)",
-                         "kernel": "prefill_kernel (q prep + merge included)",
+                         "kernel": "prefill_kernel (q prep + piece fold included)",
                          "algorithmic_flops_per_launch": flops, "peak_kind": kind},
             "cpu_baseline": cpu,
             "e2e": {"value": w["qlen"] / (ms_e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": q.numel() * 2,

@@ -1548,6 +1548,67 @@ static int launch_prefill_main(const PrefillParams& pp, int ctas, cudaStream_t s
   return check_launch("prefill");
 }
 
+// ---------------------------------------------------------------------------------------------------- piece fold
+// The pieces of every M-tile (one per CTA that worked on it, a few at most) folded by log-sum-exp, with the inverse
+// RHT (out_mode 0) or as the fp32 RHT-domain output and its base-2 lse (out_mode 1): one warp per (token, query head)
+// row, lane s reading piece s's lse, lane l holding channels 8 l .. 8 l + 7 (the layout of the warp's 256-point WHT).
+// The general merge (K2) runs one 512-thread CTA per row, sized for decode's hundred splits; over the prefill's
+// tens of thousands of rows of a few pieces each its per-CTA overhead dominated.
+constexpr int FOLD_WARPS = 8;
+constexpr int FOLD_MAX_PARTS = 32;
+
+template <int DT>
+__global__ void __launch_bounds__(32 * FOLD_WARPS) prefill_fold_kernel(const float* part_o, const float* part_lse,
+                                                                        int64_t rows, int nq, int parts, int mode,
+                                                                        void* out, int64_t out_st, int64_t out_sh,
+                                                                        float* lse_out, const uint32_t* sign_bits,
+                                                                        float out_scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * FOLD_WARPS + (threadIdx.x >> 5);  // token * nq + head
+  if (r >= rows) return;
+  const int64_t tok = r / nq;
+  const int qh = static_cast<int>(r % nq);
+  const float l_me = lane < parts ? part_lse[r * parts + lane] : -INFINITY;  // absent pieces hold -inf
+  const float M = warp_max(l_me);
+  const float w_me = (M == -INFINITY || l_me == -INFINITY) ? 0.f : exp2f(l_me - M);
+  const float T = warp_sum(w_me);
+  const float* po = part_o + r * parts * PF_HS + 8 * lane;
+  float x[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = 0.f;
+  for (int s = 0; s < parts; ++s) {
+    const float w = __shfl_sync(0xffffffffu, w_me, s);
+    if (w != 0.f) {  // the same in every lane; an absent piece's partial is never read
+      const float4 a = *reinterpret_cast<const float4*>(po + s * PF_HS);
+      const float4 b = *reinterpret_cast<const float4*>(po + s * PF_HS + 4);
+      x[0] = fmaf(w, a.x, x[0]);
+      x[1] = fmaf(w, a.y, x[1]);
+      x[2] = fmaf(w, a.z, x[2]);
+      x[3] = fmaf(w, a.w, x[3]);
+      x[4] = fmaf(w, b.x, x[4]);
+      x[5] = fmaf(w, b.y, x[5]);
+      x[6] = fmaf(w, b.z, x[6]);
+      x[7] = fmaf(w, b.w, x[7]);
+    }
+  }
+  const float inv = T > 0.f ? 1.f / T : 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] *= inv;
+  if (mode == 1) {
+    float* dst = reinterpret_cast<float*>(out) + tok * out_st + qh * out_sh + 8 * lane;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[i] = x[i];
+    if (lane == 0 && lse_out) lse_out[r] = T > 0.f ? M + log2f(T) : -INFINITY;
+    return;
+  }
+  warp_wht<8>(x, lane);
+  apply_signs<8>(x, sign_bits, lane);
+  using EL = Elem<DT>;
+  typename EL::T* dst = reinterpret_cast<typename EL::T*>(out) + tok * out_st + qh * out_sh + 8 * lane;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) dst[i] = EL::from_f(x[i] * out_scale);
+}
+
 // declared in qp_decode.cu
 extern "C" int qp_merge_attn_partials(int dtype, int head_size, int64_t num_tokens, int num_q_heads, int num_parts,
                                       const float* part_o, int64_t po_stride_token, int64_t po_stride_head,
@@ -1682,6 +1743,22 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
     rc = fmt == FMT_INT4 ? launch_prefill_main<FMT_INT4>(pp, ctas, st) : launch_prefill_main<FMT_K8V4>(pp, ctas, st);
   }
   if (rc) return rc;
+  if (parts <= FOLD_MAX_PARTS) {
+    if (!out || (out_mode == 0 && !rht_sign_bits)) return set_error(QP_ERR_INVALID, "prefill: null output / signs");
+    const int64_t rows = static_cast<int64_t>(qlen) * num_q_heads;
+    const unsigned grid = static_cast<unsigned>((rows + FOLD_WARPS - 1) / FOLD_WARPS);
+    const float out_scale = 1.f / static_cast<float>(head_size);
+    if (dtype == DT_BF16)
+      prefill_fold_kernel<DT_BF16><<<grid, 32 * FOLD_WARPS, 0, st>>>(part_o, part_lse, rows, num_q_heads, parts,
+                                                                     out_mode, out, out_stride_token,
+                                                                     out_stride_head, lse_out, rht_sign_bits,
+                                                                     out_scale);
+    else
+      prefill_fold_kernel<DT_F16><<<grid, 32 * FOLD_WARPS, 0, st>>>(part_o, part_lse, rows, num_q_heads, parts,
+                                                                    out_mode, out, out_stride_token, out_stride_head,
+                                                                    lse_out, rht_sign_bits, out_scale);
+    return check_launch("prefill fold");
+  }
   return qp_merge_attn_partials(dtype, head_size, qlen, num_q_heads, parts, part_o,
                                 static_cast<int64_t>(num_q_heads) * parts * PF_HS, static_cast<int64_t>(parts) * PF_HS,
                                 PF_HS, part_lse, static_cast<int64_t>(num_q_heads) * parts, parts, 1, out_mode, out,
