@@ -1,6 +1,6 @@
 """Benchmark of the B200 quantized KV-cache attention (prints one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload c2a|c1|c2b|c4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload c2a|c1|c2b|c3|c4]
 
 Metric: 262k-context int4-KV decode, query tokens per second of one attention-layer call, and the
 HBM bandwidth it reaches. A step is one attention call (split-KV decode + segment merge) over a resident paged cache
@@ -10,6 +10,8 @@ with a random block table over a shuffled pool. Workloads:
   c1   int4, 1 request, context 131072, 2 query tokens
   c2b  int4, 32 requests x context 32768, 2 query tokens
   c4   k8v4, 1 request, context 262144, 4 query tokens
+  c3   int4 prefill: a 1024-query chunk over 229,376 cached tokens (+ its own 1024), causal in the chunk; metric
+       prefill tokens per second and the dense tensor throughput it reaches
 At N > 1 each rank serves its own request(s) of the workload (batch sharded by request, no collective: weak
 scaling); the line also carries `seq_parallel`: one request split by sequence range over the N ranks, each rank's
 partial (O, LSE) all-gathered over NCCL and merged (strong scaling of a single request).
@@ -44,7 +46,7 @@ WORKLOADS = {
 }
 CELL = {"int4": HS + 8, "k8v4": HS * 3 // 2 + 8}
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of that workload (profiles/):
-# decode_kernel at c2a and c1, prefill_kernel at c3.
+# decode_kernel at c2a, prefill_kernel at c3 (the workloads whose dominant kernel was captured).
 TRAFFIC = {"c2a": 277.01e6 + 3.97e6, "c3": 9.940e9 + 0.0340e9}
 
 
