@@ -17,7 +17,9 @@ import sys
 import numpy as np
 
 os.environ["TRITON_INTERPRET"] = "1"
-REF = os.environ.get("REFERENCE", "/root/reference")
+REF = os.environ.get("REFERENCE")
+if not REF:
+    sys.exit("set REFERENCE to the reference checkout (the directory holding vllm_quantpack/)")
 sys.path.insert(0, REF)
 HERE = os.path.dirname(os.path.abspath(__file__))
 
