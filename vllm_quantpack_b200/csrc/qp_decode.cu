@@ -1,47 +1,64 @@
 // K1: split-KV paged decode over an int4_per_token_head / k8v4_per_token_head cache, up to 32 query rows
-//     (qlen x query heads per KV head) per KV head, 64-token tiles; and K2: log-sum-exp merge of the segments with
-//     the inverse RHT fused in.
+//     (qlen x query heads per KV head) per KV head, on the 5th-generation tensor cores (tcgen05 + TMEM); K0q: the
+//     query preparation it reads; K2: log-sum-exp merge of the segments with the inverse RHT fused in.
 //
 // Reference behaviour (what this computes, not how): the split-KV 3D path of vLLM's int4 kernel as the plugin
-// configures it (vllm_quantpack/attention/int4_kv.py:98-122: 64-token tiles, every query token of a step in one
-// program, segments sized to the SM count) and vLLM's reduce_segments (vllm/v1/attention/ops/
-// triton_unified_attention.py:645-732 in vLLM 0.22). Scores S = (Q.u - Q_sum zp) k_scale scale, P_v = P v_scale,
-// out += P_v16 u - sum(P_v16 zp) with the same rounded P_v16 in both terms (int4_kv.py:80-94).
+// configures it (vllm_quantpack/attention/int4_kv.py:98-122: every query token of a step in one program, segments
+// sized to the SM count) and vLLM's reduce_segments (vllm/v1/attention/ops/triton_unified_attention.py:645-732 in
+// vLLM 0.22). Scores S = (Q.u - Q_sum zp) k_scale scale, out = sum_t P_t v_scale_t (u_t - zp_t) / sum_t P_t
+// (int4_kv.py:80-94; k8v4 keys: S = Q.k8 k_scale scale, int4_kv.py:127-146).
 //
-// B200 design:
-// - one CTA (4 warps) per (split, KV head, sequence); the segment's cells stream through a 2-stage shared-memory
-//   ring filled by 1-D bulk copies (TMA engine), each warp copying its own 16-token group of a tile, completing on
-//   mbarriers;
-// - K0q (a small kernel before K1) rotates (RHT) and scales every query row once into fp16 with a per-row power of
-//   two, its channels permuted so that the nibble extraction below needs no shuffles (odd, high-nibble, channels
-//   carry a factor 1/16), and stores it as the exact shared-memory image of the row; K1 starts under programmatic
-//   dependent launch, issues its first cache copies, then waits for K0q and fetches its rows with one bulk copy;
-// - QK: mma.sync m16n8k16 with the keys as M (16 tokens per warp) and the query rows as N (8 per n-tile). Key
-//   nibbles become fp16 by the exponent-bias trick ((w & 0x000F000F) | 0x64006400 = 1024 + u): one lop3 per two
-//   values, the bias removed once per score (Q.1024 is a per-row constant);
-// - softmax in log2 units with the row max exchanged through shared memory, the V scale folded into P (P_v16 in fp16
-//   with a running power-of-two range);
-// - PV: mma.sync with the head dimension as M (64 channels per warp) and the query rows as N; the value nibbles of
-//   two tokens are interleaved by prmt so each register holds one channel of two tokens, converted to the exact
-//   fp16 (u - zp) of each token. The zero point sits in the operand, so the accumulator that runs over the whole
-//   segment only ever holds the signal; the reference subtracts sum(P_v16 zp) once per tile instead
-//   (int4_kv.py:90-92), which a running accumulator over many tiles cannot do without its rounding bias showing;
-// - each split writes its normalised partial O (fp32, RHT domain) and its log2-sum-exp; K2 folds the splits and
-//   applies the inverse RHT / head, launched with programmatic dependent launch so its launch overlaps K1.
+// B200 design. Decode has 24 query rows per KV head (4 tokens x 6 heads) against 128 keys per tile, so the MMAs
+// are thin (N = 32). A thin MMA runs at the tensor pipe's full rate only when its wide operand comes from TMEM
+// (measured on this part: M 128 x N 32 x K 16 in 16 cycles with A in TMEM, 40 with A in shared memory, whose
+// bandwidth the A operand then saturates). So the keys are the M dimension and both cache operands live in TMEM:
+//   S^T (128 keys x N rows)     = K_op (TMEM, 128 keys x 256 channels)       x Q^T  (shared memory, N x 256)
+//   O^T (2 x 128 channels x N)  = V^T_op (TMEM, 2 x 128 channels x 128 keys)  x P^T  (shared memory, N x 128)
+// One CTA of 14 warps per SM (it holds all 512 TMEM columns) per (split, KV head, sequence):
+//   warp 0      producer: 1-D bulk copies (TMA engine, no tensor map, no multicast) of the tile's raw cells, whole
+//               16-token groups, into a ring of raw stages;
+//   warp 1      MMA issuer (convergent; elect.sync picks the lane): 16 QK MMAs per tile into a double-buffered S,
+//               then the previous tile's 16 PV MMAs, each group finished with tcgen05.commit onto mbarriers;
+//   warps 2-5   key operand: thread = key = TMEM lane; one lop3 turns two nibbles into the fp16 pair 1024 + u (the
+//               odd channel 1024 + 16 u; its query channel carries 1/16), the bias Q.1024 is a per-row constant
+//               removed from the score; k8v4 codes become 1152 + c by one prmt. The key / value scales go to
+//               shared memory for the softmax, the value zero points as paired fp16 operand biases;
+//   warps 6-9   value operand: V^T written with tcgen05.st.16x256b, whose thread layout (lanes i/4 and 8 + i/4,
+//               column pair 2(i%4)) puts one channel of four consecutive keys in each thread: one 32-bit word of
+//               each of four keys, interleaved by prmt, becomes the exact fp16 (u - zp) of every (channel, key).
+//               The zero point sits in the operand, so the running O accumulator only holds the signal; two 64-key
+//               slots let the conversion of one half overlap the MMAs of the other;
+//   warps 10-13 softmax: thread = key; scores in log2 units from S^T, a lazy per-row maximum (P may reach 2^8
+//               before O is rescaled, which happens in TMEM and rarely), P x value scale in fp16 with a running
+//               power-of-two range written as P^T; per-thread row sums reduced once at the end; the epilogue reads
+//               O^T and writes the normalised partial and its log2-sum-exp.
+// Every wait is bounded (a timeout records an error word and the roles leave; the softmax warps leave together).
 #include <math.h>
+
+#include <atomic>
 
 #include "qp_api_internal.h"
 #include "qp_common.cuh"
+#include "qp_tcgen05.cuh"
 
 namespace qp {
 
-constexpr int DEC_TILE = 64;
-constexpr int DEC_STAGES = 2;
-constexpr int DEC_THREADS = 128;
 constexpr int DEC_HS = 256;
+constexpr int DEC_TILE = 128;  // keys per tile (TMEM lanes of the QK accumulator)
 constexpr int DEC_MAX_ROWS = 32;
-constexpr int Q_STRIDE = DEC_HS * 2 + 16;  // bytes per Q row in shared memory (conflict-free ldmatrix)
+constexpr int DEC_WARPS = 14;
+constexpr int DEC_THREADS = 32 * DEC_WARPS;
+// registers per thread one CTA may hold: each SM sub-partition's 16384 registers host every fourth warp
+constexpr int DEC_REGS = (16384 / (32 * ((DEC_WARPS + 3) / 4))) & ~7;
+constexpr int W_MMA = 1, W_VAL = 6, W_SMX = 10;  // warp 0 producer, 2-5 key operand, 6-9 value operand, 10-13 softmax
+constexpr int Q_REC = DEC_HS * 2 + 16;  // prepared query row: 256 fp16 in operand order, then 4 fp32
 constexpr float LOG2E = 1.4426950408889634f;
+constexpr float RESCALE_SLACK = 8.f;
+constexpr int BAR_SMX = 1;  // named barrier of the 4 softmax warps
+
+// TMEM columns (512): key operand double-buffered at [0, 128) and [384, 512); value operand slots (64 keys each,
+// two channel halves of 32 columns) at [128, 256); S double-buffered and O (two channel halves) after it.
+constexpr uint32_t TM_AK0 = 0, TM_AK1 = 384, TM_AV = 128, TM_S = 256;
 
 struct DecodeParams {
   const void* q;
@@ -53,12 +70,11 @@ struct DecodeParams {
   const uint8_t* cache;
   int block_size;
   int64_t block_stride, head_stride;  // bytes; cells of one (block, head) are contiguous (slot stride == cell)
-  int ks_off, v_off, vs_off;
   int nq, nkv, group;  // query heads, KV heads, query heads per KV head
   float qk_scale;      // softmax_scale / head_size * log2(e)
   const uint32_t* sign_bits;
-  int q_rotated;  // q already in the RHT domain
-  const uint8_t* qrec;  // prepared query rows: [kv head][token][query head of the group] x Q_STRIDE bytes
+  int q_rotated;        // q already in the RHT domain
+  const uint8_t* qrec;  // prepared query rows: [kv head][token][query head of the group] x Q_REC bytes
   int64_t num_tokens;
   int tokens_after;  // sequence tokens after this call's keys (held by other ranks), clamped to max_seqlen_q
   int num_splits;
@@ -68,63 +84,53 @@ struct DecodeParams {
 
 template <int FMT>
 struct Cell {
-  static constexpr int BYTES = FMT == FMT_INT4 ? DEC_HS + 8 : DEC_HS * 3 / 2 + 8;
+  static constexpr int KB = FMT == FMT_INT4 ? DEC_HS / 2 : DEC_HS;  // key bytes
+  static constexpr int BYTES = KB + 8 + DEC_HS / 2;
+  static constexpr int KS = KB, V = KB + 4, VS = KB + 4 + DEC_HS / 2;  // field offsets
 };
 
-template <int NT>
-struct PLayout {
-  // P^T in shared memory: [64 tokens][8 NT rows] fp16, row stride chosen for conflict-free ldmatrix.trans
-  static constexpr int STRIDE = NT == 1 ? 16 : (NT == 2 ? 48 : (NT == 3 ? 48 : 80));
-};
-
-template <int FMT, int NT>
+template <int FMT, int NR>
 struct DecSmem {
   static constexpr int CELL = Cell<FMT>::BYTES;
-  static constexpr int ROWS = 8 * NT;  // query rows held (padded to whole n-tiles)
-  static constexpr int STAGE_BYTES = DEC_TILE * CELL;
-  static constexpr int P_BYTES = DEC_TILE * PLayout<NT>::STRIDE;
-  static constexpr int OFF_STAGES = 0;
-  static constexpr int OFF_Q = OFF_STAGES + DEC_STAGES * STAGE_BYTES;
-  static constexpr int OFF_P = OFF_Q + ROWS * Q_STRIDE;       // 2 buffers (alternate tiles)
-  static constexpr int OFF_RED = OFF_P + 2 * P_BYTES;         // [ROWS][4 warps] f32 (row max, then l)
-  static constexpr int OFF_VS = OFF_RED + ROWS * 4 * 4;       // [4] f32 (value-scale max per warp)
-  static constexpr int OFF_ZB = OFF_VS + 16;                  // [2 buffers][lo, hi][64] u16 zero-point biases
-  static constexpr int OFF_BAR = (OFF_ZB + 2 * 2 * DEC_TILE * 2 + 7) / 8 * 8;
-  static constexpr int BYTES = OFF_BAR + (DEC_STAGES + 1) * 8;  // stage barriers, then the Q-rows barrier
+  static constexpr int RS = FMT == FMT_INT4 ? 4 : 3;  // raw stages
+  static constexpr int RAW = DEC_TILE * CELL;
+  static constexpr int ATOM = NR * 128;  // one 64-element column of 128B-swizzle atoms over the NR rows
+  static constexpr int OFF_Q = 0;                          // Q: 4 atoms (256 channels), K-major
+  static constexpr int OFF_P = OFF_Q + 4 * ATOM;           // P^T: 2 buffers x 2 atoms (128 keys), K-major
+  static constexpr int OFF_RAW = OFF_P + 4 * ATOM;         // RS raw stages
+  static constexpr int OFF_KP = OFF_RAW + RS * RAW;        // [2][128] float4: key scale, key zero point, value scale
+  static constexpr int OFF_ZB = OFF_KP + 2 * 128 * 16;     // [2][128] u32: paired value zero-point operand biases
+  static constexpr int OFF_RP = OFF_ZB + 2 * 128 * 4;      // [2][NR] float4: row scale, bias, plain sum, row maximum
+  static constexpr int OFF_LIM = OFF_RP + 2 * NR * 16;     // [NR] int: last key the row sees
+  static constexpr int OFF_RED = OFF_LIM + NR * 4;         // [NR][4] exchange, [4] value-scale maxima, [NR] factors
+  static constexpr int OFF_BAR = (OFF_RED + (NR * 4 + 4 + NR) * 4 + 7) / 8 * 8;
+  static constexpr int NBAR = 32;
+  static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_TMEM + 16;
+  static_assert(BYTES <= 232448, "dynamic shared memory above the 227 KB a CTA may hold");
+  static_assert(RAW % 16 == 0 && OFF_RAW % 1024 == 0, "bulk copy destinations must be 16-byte aligned");
 };
 
-// k index (0..255) of the QK MMA that carries channel c (see the fragment mapping in decode_kernel).
-template <int FMT>
-__device__ __forceinline__ int qk_k_of_channel(int c) {
-  if constexpr (FMT == FMT_INT4) {
-    // word W = 8 t + j of the key row feeds k-steps 2j (h = 0) and 2j + 1 (h = 1) of lane quad t; inside the word,
-    // nibble r = (2h + f) + 4e is element e of register f.
-    const int W = c >> 3, r = c & 7;
-    const int t = W >> 3, j = W & 7;
-    const int h = (r & 3) >> 1, f = r & 1, e = r >> 2;
-    return 16 * (2 * j + h) + 2 * t + e + 8 * f;
-  } else {
-    // word W of the int8 key row: k-step s = W & 7 (W < 32) or 8 + (W & 7) (W >= 32) of lane quad t = (W >> 3) & 3;
-    // byte 2f + e is element e of register f.
-    const int W = c >> 2;
-    const int f = (c >> 1) & 1, e = c & 1;
-    const int t = (W >> 3) & 3;
-    const int s = (W < 32 ? 0 : 8) + (W & 7);
-    return 16 * s + 2 * t + e + 8 * f;
-  }
-}
+// barrier slots
+enum {
+  D_RAW_FULL = 0,    // [RS <= 4] a raw stage landed
+  D_RAW_EMPTY = 4,   // [RS] key and value warps are done with it (8 arrivals)
+  D_Q_FULL = 8,      // Q^T is in shared memory (4 softmax warps)
+  D_AK_FULL = 9,     // [2] key operand in TMEM (4 key warps)
+  D_AK_FREE = 11,    // [2] its QK MMAs completed (commit)
+  D_KP_FULL = 13,    // [2] the tile's scales and zero-point biases are in shared memory (4 key warps)
+  D_KP_FREE = 15,    // [2] the softmax and the value warps read them (8 arrivals)
+  D_AV_FULL = 17,    // [2] value operand slot (64 keys) in TMEM (4 value warps)
+  D_AV_FREE = 19,    // [2] its PV MMAs completed (commit)
+  D_S_FULL = 21,     // [2] S^T of the tile is in TMEM (commit)
+  D_S_FREE = 23,     // [2] the softmax read it (4 softmax warps)
+  D_P_FULL = 25,     // [2] P^T of the tile is in shared memory (4 softmax warps)
+  D_PV_DONE = 27,    // the tile's PV MMAs completed (commit, one phase per tile)
+  D_FINAL = 28,      // every MMA issued has completed (before TMEM is released)
+};
 
-// Row of P^T (the PV MMA's k index inside the tile) that holds tile-local token tau: lane quad t of k-step kk reads
-// tokens 16 kk + 4 t + {0, 1, 2, 3} as k = 2 t, 2 t + 1, 2 t + 8, 2 t + 9.
-__device__ __forceinline__ int pv_k_of_token(int tau) {
-  const int kk = tau >> 4, u = tau & 15;
-  const int t = u >> 2, f = (u >> 1) & 1, e = u & 1;
-  return 16 * kk + 2 * t + e + 8 * f;
-}
-
-// fp16 pair -> exact (nibble - zero point) of two tokens a, b: the low-nibble form (1024 + u) minus (1024 + zp), the
-// high-nibble form (1024 + 16 u) / 16 - (64 + zp). The zero point enters the operand itself (not a correction summed
-// apart), so the fp32 accumulator only ever holds the signal sum P (u - zp).
+// fp16 pair -> exact (nibble - zero point) of two keys a, b: the low-nibble form (1024 + u) minus (1024 + zp), the
+// high-nibble form (1024 + 16 u) / 16 - (64 + zp).
 __device__ __forceinline__ uint32_t nib_lo(uint32_t x, uint32_t lo_bias) {
   return hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_bias);
 }
@@ -132,18 +138,32 @@ __device__ __forceinline__ uint32_t nib_hi(uint32_t x, uint32_t hi_bias) {
   return hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u /* 1/16 */, hi_bias);
 }
 
-// Online softmax with a lazy maximum: P = exp2(s - m_used) is allowed up to 2^RESCALE_SLACK, so the O accumulators
-// are rescaled only when a row maximum grows by more than that (rare after the first tiles), not every tile. Every
-// thread checks its own scores against m_used; only when some score (or value scale) leaves the allowed range does
-// the CTA take the slow path that exchanges the exact tile maxima.
-constexpr float RESCALE_SLACK = 8.f;
+template <int NR>
+__device__ __forceinline__ void tmem_ld_rows(uint32_t taddr, float (&v)[NR]) {
+  if constexpr (NR == 32) tmem_ld32(taddr, v);
+  else tmem_ld16(taddr, v);
+}
+template <int NR>
+__device__ __forceinline__ void tmem_st_rows(uint32_t taddr, const float (&v)[NR]) {
+  if constexpr (NR == 32) tmem_st32(taddr, v);
+  else tmem_st16(taddr, v);
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
 
+// k index (0..255) of the QK operand that carries channel c. int4: column j = 4 w + m of a key's TMEM lane holds
+// the pair lop3'd from word w (shifted right 8 for m >= 2; low nibbles for even m, high for odd), i.e. channels
+// 8 w + m (low half) and 8 w + m + 4 (high half); k8v4: the natural order (prmt takes bytes 0, 1 then 2, 3).
+template <int FMT>
+__host__ __device__ __forceinline__ int qk_k_of_channel(int c) {
+  if constexpr (FMT == FMT_INT4) return 8 * (c >> 3) + 2 * (c & 3) + ((c >> 2) & 1);
+  else return c;
+}
 
 // ---------------------------------------------------------------------------------------------------- K0q
-// One warp per (query token, query head): the row as the decode kernel holds it in shared memory (Q_STRIDE bytes):
-// 256 fp16 in the k order of the QK MMA, scaled by a power of two (|q| < 2^14), odd int4 channels x 1/16; then the
-// row's score scale (softmax_scale / head x log2 e x 2^-exponent), its bias sum (Q . 1024 / 64 / 1152 per channel
-// kind) and its plain sum, as fp32 at byte 512. Written once per call; every split of the row's KV head reads it.
+// One warp per (query token, query head): the row as K1 reads it (Q_REC bytes): 256 fp16 in the k order of the QK
+// operand, scaled by a power of two (|q| < 2^14), odd int4 channels x 1/16; then fp32 row scale A (softmax_scale /
+// head x log2 e x 2^-exponent), bias B = A Q.bias (1024 per int4 operand element, 1152 per k8v4 one) and C =
+// A sum(q). Written once per call; every split of the row's KV head reads it.
 template <int FMT, int DT>
 __global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_t q_st, int64_t q_sh, int64_t T,
                                                            int nq, int nkv, const uint32_t* sign_bits, int q_rotated,
@@ -156,7 +176,7 @@ __global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_
   const int64_t tok = row / nq;
   const int qh = static_cast<int>(row % nq);
   const int group = nq / nkv, kvh = qh / group, hg = qh % group;
-  uint8_t* rec = qrec + ((static_cast<int64_t>(kvh) * T + tok) * group + hg) * Q_STRIDE;
+  uint8_t* rec = qrec + ((static_cast<int64_t>(kvh) * T + tok) * group + hg) * Q_REC;
   __half* qrow = reinterpret_cast<__half*>(rec);
   const typename EL::T* src = reinterpret_cast<const typename EL::T*>(q) + tok * q_st + qh * q_sh + lane * 8;
   float x[8];
@@ -195,29 +215,25 @@ __global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_
   qs = warp_sum(qs);
   if (lane == 0) {
     float* rc = reinterpret_cast<float*>(rec + 2 * DEC_HS);
-    rc[0] = ldexpf(qk_scale, -ex);
-    rc[1] = cq;
-    rc[2] = qs;
+    const float a = ldexpf(qk_scale, -ex);
+    rc[0] = a;
+    rc[1] = a * cq;
+    rc[2] = a * qs;
     rc[3] = 0.f;
   }
 }
 
-template <int FMT, int DT, int NT>
-__global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(const DecodeParams p) {
-  using SM = DecSmem<FMT, NT>;
-  constexpr int CELL = SM::CELL;
-  constexpr int ROWS = SM::ROWS;
-  constexpr int PSTRIDE = PLayout<NT>::STRIDE;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* stages = smem + SM::OFF_STAGES;
-  uint8_t* qsm = smem + SM::OFF_Q;
-  float* red = reinterpret_cast<float*>(smem + SM::OFF_RED);
-  float* red_vs = reinterpret_cast<float*>(smem + SM::OFF_VS);
-  uint16_t* zbuf = reinterpret_cast<uint16_t*>(smem + SM::OFF_ZB);  // [buf][lo/hi][64]
+// ---------------------------------------------------------------------------------------------------- K1
+template <int FMT, int DT, int NR>
+__global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
+  using SM = DecSmem<FMT, NR>;
+  using CL = Cell<FMT>;
+  constexpr int CELL = SM::CELL, RS = SM::RS;
+  constexpr uint32_t TM_O = TM_S + 2 * NR;  // O^T channel half c at TM_O + NR c
+  extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::OFF_BAR);
-
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::OFF_TMEM);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t = lane & 3;
   const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
 
   // Let the merge kernel (launched with programmatic stream serialization) start its launch now; it waits for this
@@ -229,12 +245,10 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
   const int n = p.seqused_k[seq];
   const int rows = qlen * p.group;
   if (qlen <= 0) return;
-
   const int n_tiles = (n + DEC_TILE - 1) / DEC_TILE;
   const int tps = (n_tiles + p.num_splits - 1) / p.num_splits;
   const int tile0 = split * tps;
   const int ntl = max(0, min(tile0 + tps, n_tiles) - tile0);
-
   if (ntl == 0) {  // empty segment: lse = -inf
     for (int r = tid; r < rows; r += DEC_THREADS) {
       const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
@@ -243,442 +257,485 @@ __global__ void __launch_bounds__(DEC_THREADS, NT == 4 ? 2 : 3) decode_kernel(co
     return;
   }
 
-  const int32_t* btab = p.block_table + static_cast<int64_t>(seq) * p.bt_stride;
-  const uint8_t* head_base = p.cache + static_cast<int64_t>(kvh) * p.head_stride;
-
-  // --- copies: warp w copies 16-token group w of every tile (block_size % 16 == 0, so a group never crosses a block),
-  // one bulk copy each, arriving with its byte count on the tile's stage barrier (4 arrivals per phase). The group's
-  // block-table index and in-block offset advance by one tile at a time (no division in the loop); its block entry
-  // is loaded one tile ahead.
-  int gb_tok = tile0 * DEC_TILE + 16 * warp;  // first token of this warp's group of the tile to fetch next
-  int gb_idx = gb_tok / p.block_size;
-  int gb_off = gb_tok - gb_idx * p.block_size;
-  auto advance_group = [&]() {
-    gb_tok += DEC_TILE;
-    gb_off += DEC_TILE;
-    while (gb_off >= p.block_size) {
-      gb_off -= p.block_size;
-      ++gb_idx;
-    }
-  };
-  auto fetch_block = [&](int i) { return (i < ntl && gb_tok < n) ? __ldg(btab + gb_idx) : -1; };
-  auto issue_group = [&](int stage, int blk, int inb) {
-    if (lane == 0) {
-      if (blk >= 0) {
-        mbar_arrive_expect_tx(&bars[stage], static_cast<uint32_t>(16 * CELL));
-        bulk_g2s(stages + stage * SM::STAGE_BYTES + warp * 16 * CELL,
-                 head_base + static_cast<int64_t>(blk) * p.block_stride + static_cast<int64_t>(inb) * CELL,
-                 static_cast<uint32_t>(16 * CELL), &bars[stage]);
-      } else {
-        mbar_arrive(&bars[stage]);
-      }
-    }
-  };
-
   if (tid == 0) {
-    for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&bars[s], 4);
-    mbar_init(&bars[DEC_STAGES], 1);
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&bars[D_RAW_FULL + s], 1);
+      mbar_init(&bars[D_RAW_EMPTY + s], 8);
+    }
+    mbar_init(&bars[D_Q_FULL], 4);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars[D_AK_FULL + b], 4);
+      mbar_init(&bars[D_AK_FREE + b], 1);
+      mbar_init(&bars[D_KP_FULL + b], 4);
+      mbar_init(&bars[D_KP_FREE + b], 8);
+      mbar_init(&bars[D_AV_FULL + b], 4);
+      mbar_init(&bars[D_AV_FREE + b], 1);
+      mbar_init(&bars[D_S_FULL + b], 1);
+      mbar_init(&bars[D_S_FREE + b], 4);
+      mbar_init(&bars[D_P_FULL + b], 4);
+    }
+    mbar_init(&bars[D_PV_DONE], 1);
+    mbar_init(&bars[D_FINAL], 1);
     fence_mbar_init();
   }
-  __syncthreads();
-  const int issued0 = min(ntl, DEC_STAGES);
-  int issued = issued0;  // tiles whose copies every warp has issued
-  {
-    int blk[DEC_STAGES], off[DEC_STAGES];
-#pragma unroll
-    for (int i = 0; i < DEC_STAGES; ++i) {
-      blk[i] = fetch_block(i);
-      off[i] = gb_off;
-      advance_group();
-    }
-#pragma unroll
-    for (int i = 0; i < DEC_STAGES; ++i)
-      if (i < issued0) issue_group(i, blk[i], off[i]);
+  if (warp == W_MMA) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
   }
-  int next_blk = fetch_block(issued), next_inb = gb_off;  // this warp's group of tile `issued`
-
-  // --- Q rows: prepared by K0q (programmatic dependent launch: wait for it only now) --------------------------
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (tid == 0) {
-    const uint8_t* src = p.qrec + ((static_cast<int64_t>(kvh) * p.num_tokens + q0) * p.group) * Q_STRIDE;
-    mbar_arrive_expect_tx(&bars[DEC_STAGES], static_cast<uint32_t>(rows * Q_STRIDE));
-    bulk_g2s(qsm, src, static_cast<uint32_t>(rows * Q_STRIDE), &bars[DEC_STAGES]);
-  }
-  for (int idx = rows * (Q_STRIDE / 16) + tid; idx < ROWS * (Q_STRIDE / 16); idx += DEC_THREADS)
-    reinterpret_cast<uint4*>(qsm)[idx] = make_uint4(0u, 0u, 0u, 0u);  // padding rows: zero
-  bool failed = !mbar_wait_bounded(&bars[DEC_STAGES], 0);
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool failed = false;
 
-  // --- per-thread state: this thread's query rows are r = 8 nt + 2 t + e ------------------------------------
-  float qsc[NT][2], qcq[NT][2], qsum[NT][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float* rc = reinterpret_cast<const float*>(qsm + (8 * nt + 2 * t + e) * Q_STRIDE + 2 * DEC_HS);
-      qsc[nt][e] = rc[0];
-      qcq[nt][e] = rc[1];
-      qsum[nt][e] = rc[2];
-    }
-  float o[4][NT][4];
-#pragma unroll
-  for (int mt = 0; mt < 4; ++mt)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) o[mt][nt][c] = 0.f;
-  float m_used[NT][2], l_part[NT][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      m_used[nt][e] = -INFINITY;
-      l_part[nt][e] = 0.f;
-    }
-  int e_run = -1000;    // running power-of-two range of P_v (value scales): every value scale < 2^e_run
-  float pv_mul = 0.f;   // 2^-e_run
-  float v_limit = 0.f;  // 2^e_run
-  // query token i sits at position n - qlen + i + tokens_after of the keys; keys >= causal_from are hidden from some
-  // row or lie past the context
-  const int vis_base = n - qlen + p.tokens_after;  // last key query token 0 sees (before clamping to n - 1)
-  const int causal_from = min(n, vis_base + 1);
-  const uint32_t qsm_base = smem_u32(qsm);
-  const int tau_a = 16 * warp + g, tau_b = tau_a + 8;
-  const int pk_a = pv_k_of_token(tau_a) * PSTRIDE, pk_b = pv_k_of_token(tau_b) * PSTRIDE;
-  int fail_tile = ntl;
-
-  int stage = 0;         // i % DEC_STAGES
-  uint32_t sphase = 0;   // (i / DEC_STAGES) & 1
-  for (int i = 0; i < ntl; ++i) {
-    const int buf = i & 1;
-    uint8_t* psm = smem + SM::OFF_P + buf * SM::P_BYTES;
-    uint16_t* zb_lo = zbuf + buf * 2 * DEC_TILE;
-    uint16_t* zb_hi = zb_lo + DEC_TILE;
-    // A thread whose wait runs out keeps going on whatever the stage holds (nothing reaches global memory before
-    // the epilogue); the CTA leaves together at barrier (B), so no thread skips a __syncthreads.
-    failed |= !mbar_wait_bounded(&bars[stage], sphase);
-    const uint8_t* tile = stages + stage * SM::STAGE_BYTES;
-    const int tok_base = (tile0 + i) * DEC_TILE;
-
-    // ---------------- QK: warp handles tokens 16 warp + [0, 16) ----------------
-    float sacc[NT][4], sacc2[NT][4];  // two accumulator chains (even / odd k-steps), summed after the loop
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) sacc[nt][c] = sacc2[nt][c] = 0.f;
-    const uint8_t* rowg = tile + tau_a * CELL;
-    const uint8_t* rowg8 = rowg + 8 * CELL;
-    if constexpr (FMT == FMT_INT4) {
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const uint2 wa = *reinterpret_cast<const uint2*>(rowg + 4 * (8 * t + 2 * jj));
-        const uint2 wb = *reinterpret_cast<const uint2*>(rowg8 + 4 * (8 * t + 2 * jj));
-#pragma unroll
-        for (int hw = 0; hw < 2; ++hw) {
-          const int j = 2 * jj + hw;
-          const uint32_t xa = hw ? wa.y : wa.x, xb = hw ? wb.y : wb.x;
-          const uint32_t xa8 = xa >> 8, xb8 = xb >> 8;
-          uint32_t A0[4], A1[4];  // k-steps 2j (h = 0) and 2j + 1 (h = 1)
-          A0[0] = lop3_and_or(xa, 0x000F000Fu, 0x64006400u);
-          A0[1] = lop3_and_or(xb, 0x000F000Fu, 0x64006400u);
-          A0[2] = lop3_and_or(xa, 0x00F000F0u, 0x64006400u);
-          A0[3] = lop3_and_or(xb, 0x00F000F0u, 0x64006400u);
-          A1[0] = lop3_and_or(xa8, 0x000F000Fu, 0x64006400u);
-          A1[1] = lop3_and_or(xb8, 0x000F000Fu, 0x64006400u);
-          A1[2] = lop3_and_or(xa8, 0x00F000F0u, 0x64006400u);
-          A1[3] = lop3_and_or(xb8, 0x00F000F0u, 0x64006400u);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            uint32_t b0, b1, b2, b3;
-            ldmatrix_x4(b0, b1, b2, b3, qsm_base + (8 * nt + (lane & 7)) * Q_STRIDE + (32 * j + 8 * (lane >> 3)) * 2);
-            mma_f16_16816(sacc[nt], A0, b0, b1);
-            mma_f16_16816(sacc2[nt], A1, b2, b3);
-          }
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      const int32_t* btab = p.block_table + static_cast<int64_t>(seq) * p.bt_stride;
+      const uint8_t* head_base = p.cache + static_cast<int64_t>(kvh) * p.head_stride;
+      int i = 0;
+      for (; i < ntl; ++i) {
+        const int stage = i % RS;
+        if (i >= RS && !mbar_wait_bounded(&bars[D_RAW_EMPTY + stage], ((i / RS) - 1) & 1)) break;
+        const int tb = (tile0 + i) * DEC_TILE;
+        const int groups = (min(tb + DEC_TILE, n) - tb + 15) >> 4;
+        mbar_arrive_expect_tx(&bars[D_RAW_FULL + stage], static_cast<uint32_t>(groups * 16 * CELL));
+        uint8_t* dst = smem + SM::OFF_RAW + stage * SM::RAW;
+        for (int gi = 0; gi < groups;) {
+          const int tok = tb + gi * 16;
+          const int bi = tok / p.block_size;
+          const int in_blk = tok - bi * p.block_size;
+          const int blk = __ldg(btab + bi);
+          const int run = min(groups - gi, (p.block_size - in_blk) >> 4);
+          bulk_g2s(dst + gi * 16 * CELL,
+                   head_base + static_cast<int64_t>(blk) * p.block_stride + static_cast<int64_t>(in_blk) * CELL,
+                   static_cast<uint32_t>(run * 16 * CELL), &bars[D_RAW_FULL + stage]);
+          gi += run;
         }
       }
-    } else {
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const int wbase = half * 32 + 8 * t + 2 * jj;  // words wbase, wbase + 1 = k-steps s0, s0 + 1
-          const int s0 = half * 8 + 2 * jj;
-          const uint2 wa = *reinterpret_cast<const uint2*>(rowg + 4 * wbase);
-          const uint2 wb = *reinterpret_cast<const uint2*>(rowg8 + 4 * wbase);
-          uint32_t A[2][4];
-#pragma unroll
-          for (int hw = 0; hw < 2; ++hw) {
-            const uint32_t xa = (hw ? wa.y : wa.x) ^ 0x80808080u, xb = (hw ? wb.y : wb.x) ^ 0x80808080u;
-            A[hw][0] = prmt(xa, 0x64646464u, 0x4140u);  // {1024 + 128 + c0, 1024 + 128 + c1}
-            A[hw][1] = prmt(xb, 0x64646464u, 0x4140u);
-            A[hw][2] = prmt(xa, 0x64646464u, 0x4342u);  // {.. + c2, .. + c3}
-            A[hw][3] = prmt(xb, 0x64646464u, 0x4342u);
-          }
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            uint32_t b0, b1, b2, b3;
-            ldmatrix_x4(b0, b1, b2, b3, qsm_base + (8 * nt + (lane & 7)) * Q_STRIDE + (16 * s0 + 8 * (lane >> 3)) * 2);
-            mma_f16_16816(sacc[nt], A[0], b0, b1);
-            mma_f16_16816(sacc2[nt], A[1], b2, b3);
-          }
-        }
-      }
+      // the copies in flight land before the CTA's shared memory can go away
+      for (int k = max(0, i - RS); k < i; ++k)
+        mbar_wait_bounded(&bars[D_RAW_FULL + k % RS], (k / RS) & 1, 100000000ull);
     }
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) sacc[nt][c] += sacc2[nt][c];
-
-    // ---------------- scores (log2 units) and masks ----------------
-    const int tok_a = tok_base + tau_a, tok_b = tok_base + tau_b;
-    const uint32_t kwa = *reinterpret_cast<const uint32_t*>(tile + tau_a * CELL + p.ks_off);
-    const uint32_t kwb = *reinterpret_cast<const uint32_t*>(tile + tau_b * CELL + p.ks_off);
-    const uint32_t vwa = *reinterpret_cast<const uint32_t*>(tile + tau_a * CELL + p.vs_off);
-    const uint32_t vwb = *reinterpret_cast<const uint32_t*>(tile + tau_b * CELL + p.vs_off);
-    float ks_a, ks_b, kz_a = 0.f, kz_b = 0.f;
-    if constexpr (FMT == FMT_INT4) {
-      ks_a = __uint_as_float(kwa & 0xFFFFFFF0u);
-      ks_b = __uint_as_float(kwb & 0xFFFFFFF0u);
-      kz_a = static_cast<float>(kwa & 0xFu);
-      kz_b = static_cast<float>(kwb & 0xFu);
-    } else {
-      ks_a = __uint_as_float(kwa);
-      ks_b = __uint_as_float(kwb);
-    }
-    // value scales of this thread's two tokens (tokens past the end count as scale 0)
-    const float vs_a = tok_a < n ? __uint_as_float(vwa & 0xFFFFFFF0u) : 0.f;
-    const float vs_b = tok_b < n ? __uint_as_float(vwb & 0xFFFFFFF0u) : 0.f;
-    if (t == 0) {  // zero-point biases of the value operand, per token (read by the PV phase after barrier B)
-      zb_lo[tau_a] = static_cast<uint16_t>(0x6400u | (vwa & 0xFu));
-      zb_lo[tau_b] = static_cast<uint16_t>(0x6400u | (vwb & 0xFu));
-      zb_hi[tau_a] = static_cast<uint16_t>(0xD400u | ((vwa & 0xFu) << 4));
-      zb_hi[tau_b] = static_cast<uint16_t>(0xD400u | ((vwb & 0xFu) << 4));
-    }
-    const bool need_mask = tok_base + DEC_TILE > causal_from;
-    float sc[NT][4];
-    bool grow = vs_a >= v_limit || vs_b >= v_limit;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float s0 = (sacc[nt][e] - fmaf(kz_a, qsum[nt][e], qcq[nt][e])) * (ks_a * qsc[nt][e]);
-        float s1 = (sacc[nt][2 + e] - fmaf(kz_b, qsum[nt][e], qcq[nt][e])) * (ks_b * qsc[nt][e]);
-        if (need_mask) {
-          const int r = 8 * nt + 2 * t + e;
-          const int lim = r < rows ? min(n - 1, vis_base + r / p.group) : -1;  // last key this row sees
-          if (tok_a > lim) s0 = -INFINITY;                                      // also past the context
-          if (tok_b > lim) s1 = -INFINITY;
-        }
-        sc[nt][e] = s0;
-        sc[nt][2 + e] = s1;
-        grow |= fmaxf(s0, s1) > m_used[nt][e] + RESCALE_SLACK;
-      }
-    }
-
-    // ---------------- P with the current maximum and value range (optimistic) ----------------
-    float psum[NT][2];
-    auto make_p = [&]() {
-      const float va = vs_a * pv_mul, vb = vs_b * pv_mul;
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        float pv[4];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float base = m_used[nt][e] == -INFINITY ? 0.f : m_used[nt][e];
-          const float pa = fast_exp2(sc[nt][e] - base);
-          const float pb = fast_exp2(sc[nt][2 + e] - base);
-          psum[nt][e] = pa + pb;
-          pv[e] = pa * va;
-          pv[2 + e] = pb * vb;
-        }
-        // P_v rounded to fp16: the operand of the PV MMA
-        *reinterpret_cast<__half2*>(psm + pk_a + (8 * nt + 2 * t) * 2) = __floats2half2_rn(pv[0], pv[1]);
-        *reinterpret_cast<__half2*>(psm + pk_b + (8 * nt + 2 * t) * 2) = __floats2half2_rn(pv[2], pv[3]);
-      }
+  } else if (warp == W_MMA) {
+    // ------------------------------------------------------------------ MMA issuer
+    // The whole warp waits (convergent, so descriptors and TMEM addresses are warp-uniform); one elected lane issues.
+    constexpr uint32_t ID = f16_idesc(128, NR, false);
+    const uint32_t q_base = smem_u32(smem + SM::OFF_Q), p_base = smem_u32(smem + SM::OFF_P);
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+      const bool ok = mbar_wait_spin(bar, parity);
+      failed |= __any_sync(0xffffffffu, !ok);
     };
-    make_p();
-
-    // this thread's value words for the PV phase: word 8 warp + g of tokens 16 kk + 4 t + j
-    uint32_t vw[4][4];
-    {
-      const uint8_t* vbase = tile + p.v_off + 4 * (8 * warp + g);
+    // O^T += V^T(j) P^T(j), slot by slot (the value warps refill a slot as soon as its MMAs complete)
+    auto issue_pv = [&](int j) {
+      const int bj = j & 1;
+      wait_all(&bars[D_P_FULL + bj], (j >> 1) & 1);
+#pragma unroll 1
+      for (int h = 0; h < 2 && !failed; ++h) {
+        wait_all(&bars[D_AV_FULL + h], j & 1);
+        if (failed) break;
+        tc_fence_after();
+        if (elect_one()) {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) vw[kk][j] = *reinterpret_cast<const uint32_t*>(vbase + (16 * kk + 4 * t + j) * CELL);
+            for (int s = 0; s < 4; ++s)
+              umma_f16_ts(tmem + TM_O + NR * c, tmem + TM_AV + 64 * h + 32 * c + 8 * s,
+                          sw128_desc(p_base + (2 * bj + h) * SM::ATOM + 32 * s, 16, 1024), ID,
+                          (j | h | s) ? 1u : 0u);
+          umma_commit(&bars[D_AV_FREE + h]);
+        }
+        __syncwarp();
+      }
+      if (elect_one()) umma_commit(&bars[D_PV_DONE]);
+      __syncwarp();
+    };
+    wait_all(&bars[D_Q_FULL], 0);
+    for (int i = 0; i < ntl && !failed; ++i) {
+      const int b = i & 1;
+      wait_all(&bars[D_AK_FULL + b], (i >> 1) & 1);
+      if (i >= 2) wait_all(&bars[D_S_FREE + b], ((i - 2) >> 1) & 1);
+      if (failed) break;
+      tc_fence_after();
+      const uint32_t ak = tmem + (b ? TM_AK1 : TM_AK0);
+      if (elect_one()) {
+#pragma unroll
+        for (int s = 0; s < 16; ++s)
+          umma_f16_ts(tmem + TM_S + NR * b, ak + 8 * s,
+                      sw128_desc(q_base + (s >> 2) * SM::ATOM + (s & 3) * 32, 16, 1024), ID, s ? 1u : 0u);
+        umma_commit(&bars[D_AK_FREE + b]);
+        umma_commit(&bars[D_S_FULL + b]);
+      }
+      __syncwarp();
+      if (i >= 1) issue_pv(i - 1);
     }
-
-    // (B) P^T and the zero-point biases visible; the stage is no longer read
-    if (__syncthreads_or(grow || failed)) {
-      if (__syncthreads_or(failed)) {
+    if (!failed) issue_pv(ntl - 1);
+    if (elect_one()) umma_commit(&bars[D_FINAL]);
+    __syncwarp();
+    mbar_wait_spin(&bars[D_FINAL], 0, 100000000ull);
+  } else if (warp < W_VAL) {
+    // ------------------------------------------------------------------ key operand (thread = key = TMEM lane)
+    const int q = warp & 3, kl = 32 * q + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
+    float4* kp = reinterpret_cast<float4*>(smem + SM::OFF_KP);
+    uint32_t* zb = reinterpret_cast<uint32_t*>(smem + SM::OFF_ZB);
+    for (int i = 0; i < ntl; ++i) {
+      const int stage = i % RS, b = i & 1;
+      bool ok = mbar_wait_bounded(&bars[D_RAW_FULL + stage], (i / RS) & 1);
+      if (i >= 2) {
+        ok = ok && mbar_wait_bounded(&bars[D_AK_FREE + b], ((i - 2) >> 1) & 1);
+        ok = ok && mbar_wait_bounded(&bars[D_KP_FREE + b], ((i - 2) >> 1) & 1);
+      }
+      if (__any_sync(0xffffffffu, !ok)) {
         failed = true;
-        fail_tile = i;
         break;
       }
-      // slow path: exact tile maxima and value range, rescale, recompute P
-      float tm[NT][2];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          float mx = fmaxf(sc[nt][e], sc[nt][2 + e]);
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-          tm[nt][e] = mx;
-          if (g == 0) red[(8 * nt + 2 * t + e) * 4 + warp] = mx;
-        }
-      const float vm = warp_max(fmaxf(vs_a, vs_b));
-      if (lane == 0) red_vs[warp] = vm;
-      __syncthreads();
-      const float4 vv = *reinterpret_cast<const float4*>(red_vs);
-      const float vmax = fmaxf(fmaxf(vv.x, vv.y), fmaxf(vv.z, vv.w));
-      int e_tile = -1000;
-      if (vmax > 0.f) frexpf(vmax, &e_tile);  // vmax < 2^e_tile
-      const int e_new = max(e_run, e_tile);
-      const float o_range = e_run == -1000 ? 0.f : ldexpf(1.f, e_run - e_new);
-      e_run = e_new;
-      pv_mul = e_new == -1000 ? 0.f : ldexpf(1.f, -e_new);
-      v_limit = e_new == -1000 ? 0.f : ldexpf(1.f, e_new);
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float4 mv = *reinterpret_cast<const float4*>(red + (8 * nt + 2 * t + e) * 4);
-          const float mt_ = fmaxf(fmaxf(mv.x, mv.y), fmaxf(mv.z, mv.w));
-          const float m_new = mt_ > m_used[nt][e] + RESCALE_SLACK ? mt_ : m_used[nt][e];
-          const float alpha = m_new == m_used[nt][e] ? 1.f : fast_exp2(m_used[nt][e] - m_new);
-          m_used[nt][e] = m_new;
-          const float ao = alpha * o_range;
-          l_part[nt][e] *= alpha;
-#pragma unroll
-          for (int mt = 0; mt < 4; ++mt) {
-            o[mt][nt][e] *= ao;
-            o[mt][nt][2 + e] *= ao;
-          }
-        }
-      (void)tm;
-      make_p();
-      __syncthreads();  // the recomputed P^T visible
-    }
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) l_part[nt][e] += psum[nt][e];
-
-    // the stage is free: every warp refills its group with tile i + DEC_STAGES
-    if (issued < ntl) {
-      issue_group(stage, next_blk, next_inb);  // issued == i + DEC_STAGES: the stage of this tile
-      advance_group();
-      ++issued;
-      next_blk = fetch_block(issued);
-      next_inb = gb_off;
-    }
-    if (++stage == DEC_STAGES) {
-      stage = 0;
-      sphase ^= 1u;
-    }
-
-    // ---------------- PV: warp handles channels 64 warp + [0, 64) ----------------
-    const uint32_t psm_base = smem_u32(psm);
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t bf[NT][2];
+      tc_fence_after();
+      const uint8_t* cell = smem + SM::OFF_RAW + stage * SM::RAW + kl * CELL;
+      const uint32_t kw = *reinterpret_cast<const uint32_t*>(cell + CL::KS);
+      const uint32_t vw = *reinterpret_cast<const uint32_t*>(cell + CL::VS);
+      const bool valid = (tile0 + i) * DEC_TILE + kl < n;
+      float ks, kz = 0.f;
+      if constexpr (FMT == FMT_INT4) {
+        ks = __uint_as_float(kw & 0xFFFFFFF0u);
+        kz = static_cast<float>(kw & 0xFu);
+      } else {
+        ks = __uint_as_float(kw);
+      }
+      kp[b * 128 + kl] = make_float4(ks, kz, valid ? __uint_as_float(vw & 0xFFFFFFF0u) : 0.f, 0.f);
+      // value zero-point operand biases of the key pair (a even, a + 1): key a stores {1024 + zp_a, 1024 + zp_b},
+      // key a + 1 stores {-(64 + zp_a), -(64 + zp_b)} (fp16 pairs, low half = key a)
       {
-        const int mi = lane >> 3;
-        const int krow = 16 * kk + (mi & 1) * 8 + (lane & 7);
-        if constexpr (NT == 1) {
-          ldmatrix_x2_trans(bf[0][0], bf[0][1], psm_base + krow * PSTRIDE);
+        const uint32_t vz = vw & 0xFu;
+        const uint32_t lo16 = 0x6400u | vz, hi16 = 0xD400u | (vz << 4);
+        const uint32_t other = __shfl_xor_sync(0xffffffffu, (lane & 1) ? lo16 : hi16, 1);
+        zb[b * 128 + kl] = (lane & 1) ? (other | (hi16 << 16)) : (lo16 | (other << 16));
+      }
+      const uint32_t dst = tmem + (b ? TM_AK1 : TM_AK0) + lane_off;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {  // 32 TMEM columns (64 channels) per store
+        uint32_t a[32];
+        if constexpr (FMT == FMT_INT4) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint2 w2 = *reinterpret_cast<const uint2*>(cell + 32 * c + 8 * k);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const uint32_t w = e ? w2.y : w2.x, w8 = w >> 8;
+              const int j = 8 * k + 4 * e;
+              a[j + 0] = lop3_and_or(w, 0x000F000Fu, 0x64006400u);
+              a[j + 1] = lop3_and_or(w, 0x00F000F0u, 0x64006400u);
+              a[j + 2] = lop3_and_or(w8, 0x000F000Fu, 0x64006400u);
+              a[j + 3] = lop3_and_or(w8, 0x00F000F0u, 0x64006400u);
+            }
+          }
         } else {
-          ldmatrix_x4_trans(bf[0][0], bf[0][1], bf[1][0], bf[1][1], psm_base + krow * PSTRIDE + (mi >> 1) * 16);
-          if constexpr (NT == 3) {
-            ldmatrix_x2_trans(bf[2][0], bf[2][1], psm_base + krow * PSTRIDE + 32);
-          } else if constexpr (NT == 4) {
-            ldmatrix_x4_trans(bf[2][0], bf[2][1], bf[3][0], bf[3][1], psm_base + krow * PSTRIDE + 32 + (mi >> 1) * 16);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint2 w2 = *reinterpret_cast<const uint2*>(cell + 64 * c + 8 * k);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const uint32_t x = (e ? w2.y : w2.x) ^ 0x80808080u;
+              const int j = 4 * k + 2 * e;
+              a[j] = prmt(x, 0x64646464u, 0x4140u);      // {1152 + c0, 1152 + c1}
+              a[j + 1] = prmt(x, 0x64646464u, 0x4342u);  // {1152 + c2, 1152 + c3}
+            }
+          }
+        }
+        tmem_st32u(dst + 32 * c, a);
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bars[D_AK_FULL + b]);
+        mbar_arrive(&bars[D_KP_FULL + b]);
+        mbar_arrive(&bars[D_RAW_EMPTY + stage]);
+      }
+    }
+  } else if (warp < W_SMX) {
+    // ------------------------------------------------------------------ value operand (V^T, lane = channel)
+    // Thread (g, t) of quarter q converts word 8 q + g (channels 64 q + 8 g + [0, 8)) of keys 4 t + [0, 4) of every
+    // 16-key block. Lane 32 q + g + 8 m of channel half c holds channel 64 q + 8 g + 4 c + m.
+    const int q = warp & 3, g = lane >> 2, t = lane & 3;
+    const int wv = 8 * q + g;
+    const uint32_t* zb = reinterpret_cast<const uint32_t*>(smem + SM::OFF_ZB);
+    for (int i = 0; i < ntl && !failed; ++i) {
+      const int stage = i % RS, b = i & 1;
+      bool ok = mbar_wait_bounded(&bars[D_RAW_FULL + stage], (i / RS) & 1);
+      ok = ok && mbar_wait_bounded(&bars[D_KP_FULL + b], (i >> 1) & 1);
+      if (__any_sync(0xffffffffu, !ok)) {
+        failed = true;
+        break;
+      }
+      const uint8_t* raw = smem + SM::OFF_RAW + stage * SM::RAW + CL::V + 4 * wv;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        if (i >= 1 && __any_sync(0xffffffffu, !mbar_wait_bounded(&bars[D_AV_FREE + h], (i - 1) & 1))) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kb2 = 0; kb2 < 2; ++kb2) {
+          uint32_t r[4][8];  // [store (channel half c, lane half lb)][registers]
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            const int key0 = 16 * (4 * h + 2 * kb2 + rr) + 4 * t;
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const uint32_t*>(raw + (key0 + j) * CELL);
+            const uint4 bz = *reinterpret_cast<const uint4*>(zb + b * 128 + key0);
+#pragma unroll
+            for (int f = 0; f < 2; ++f) {
+              const uint32_t lo_b = f ? bz.z : bz.x, hi_b = f ? bz.w : bz.y;
+              const uint32_t x = prmt(w[2 * f], w[2 * f + 1], 0x5410u), y = prmt(w[2 * f], w[2 * f + 1], 0x7632u);
+              const uint32_t x8 = x >> 8, y8 = y >> 8;
+              r[0][4 * rr + f] = nib_lo(x, lo_b);       // channel half 0, m 0
+              r[0][4 * rr + 2 + f] = nib_hi(x, hi_b);   // half 0, m 1
+              r[1][4 * rr + f] = nib_lo(x8, lo_b);      // half 0, m 2
+              r[1][4 * rr + 2 + f] = nib_hi(x8, hi_b);  // half 0, m 3
+              r[2][4 * rr + f] = nib_lo(y, lo_b);       // half 1, m 0
+              r[2][4 * rr + 2 + f] = nib_hi(y, hi_b);
+              r[3][4 * rr + f] = nib_lo(y8, lo_b);
+              r[3][4 * rr + 2 + f] = nib_hi(y8, hi_b);
+            }
+          }
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {
+            const int c = s >> 1, lb = s & 1;
+            tmem_st_16x256b_x2(tmem + (static_cast<uint32_t>(32 * q + 16 * lb) << 16) + TM_AV + 64 * h + 32 * c +
+                                   16 * kb2,
+                               r[s]);
+          }
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[D_AV_FULL + h]);
+      }
+      if (failed) break;
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bars[D_KP_FREE + b]);
+        mbar_arrive(&bars[D_RAW_EMPTY + stage]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax (thread = key = TMEM lane)
+    const int q = warp & 3, kl = 32 * q + lane, stid = tid - 32 * W_SMX;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
+    // row constants and the running row maxima, double-buffered: a rescale writes the other buffer, then every
+    // softmax thread switches to it after one barrier
+    float4* rp = reinterpret_cast<float4*>(smem + SM::OFF_RP);
+    int* lim = reinterpret_cast<int*>(smem + SM::OFF_LIM);
+    float* red = reinterpret_cast<float*>(smem + SM::OFF_RED);  // [NR][4]
+    float* red_vs = red + NR * 4;                               // [4]
+    float* frow = red_vs + 4;                                   // [NR]
+    const float4* kp = reinterpret_cast<const float4*>(smem + SM::OFF_KP);
+    const int vis_base = n - qlen + p.tokens_after;  // last key query token 0 sees (before clamping to n - 1)
+    const int causal_from = min(n, vis_base + 1);
+    // query rows (prepared by K0q: programmatic dependent launch, wait for it only now) -> Q^T operand, K-major
+    // 128B-swizzled; row constants
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    {
+      const uint8_t* qsrc = p.qrec + ((static_cast<int64_t>(kvh) * p.num_tokens + q0) * p.group) * Q_REC;
+      for (int idx = stid; idx < NR * 32; idx += 128) {
+        const int r = idx >> 5, ch = idx & 31;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (r < rows) v = *reinterpret_cast<const uint4*>(qsrc + r * Q_REC + 16 * ch);
+        *reinterpret_cast<uint4*>(smem + SM::OFF_Q + (ch >> 3) * SM::ATOM + sw128_off(r, ch & 7)) = v;
+      }
+      for (int r = stid; r < NR; r += 128) {
+        float4 c = make_float4(0.f, 0.f, 0.f, -INFINITY);
+        if (r < rows) {
+          const float* rc = reinterpret_cast<const float*>(qsrc + r * Q_REC + 2 * DEC_HS);
+          c = make_float4(rc[0], rc[1], rc[2], -INFINITY);
+        }
+        rp[r] = c;
+        rp[NR + r] = c;
+        lim[r] = r < rows ? min(n - 1, vis_base + r / p.group) : -1;
+      }
+    }
+    fence_async_smem();
+    named_bar_or(BAR_SMX, 128, false);  // row constants visible to every softmax thread
+    if (lane == 0) mbar_arrive(&bars[D_Q_FULL]);
+
+    float l[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) l[r] = 0.f;
+    int mb = 0;           // current row-maximum buffer
+    int e_run = -1000;    // running power-of-two range of the value scales: every one < 2^e_run
+    float pv_mul = 0.f;   // 2^-e_run
+    float v_limit = 0.f;  // 2^e_run
+    // P^T store position of this thread's key: atom kl / 64, 16-byte chunk (kl % 64) / 8 (swizzled by row), column
+    const int patom = (kl >> 6) * SM::ATOM + (kl & 7) * 2, pchunk = (kl & 63) >> 3;
+    for (int i = 0; i < ntl; ++i) {
+      const int b = i & 1;
+      bool ok = mbar_wait_bounded(&bars[D_S_FULL + b], (i >> 1) & 1);
+      ok = ok && mbar_wait_bounded(&bars[D_KP_FULL + b], (i >> 1) & 1);
+      failed |= __any_sync(0xffffffffu, !ok);
+      float s[NR];
+      if (!failed) {
+        tc_fence_after();
+        tmem_ld_rows<NR>(tmem + TM_S + NR * b + lane_off, s);
+      } else {
+#pragma unroll
+        for (int r = 0; r < NR; ++r) s[r] = 0.f;
+      }
+      tc_fence_before();
+      const float4 kv = kp[b * 128 + kl];  // key scale, key zero point, value scale (0 past the context)
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bars[D_S_FREE + b]);
+        mbar_arrive(&bars[D_KP_FREE + b]);
+      }
+      const int tok = (tile0 + i) * DEC_TILE + kl;
+      const bool need_mask = (tile0 + i) * DEC_TILE + DEC_TILE > causal_from;
+      float emax = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        if (r < rows) {
+          const float4 c = rp[mb * NR + r];
+          float lg = fmaf(s[r], c.x, -fmaf(kv.y, c.z, c.y)) * kv.x;
+          if (need_mask && tok > lim[r]) lg = -INFINITY;  // past the row's last key or the context
+          s[r] = lg;
+          emax = fmaxf(emax, lg - c.w);
+        }
+      }
+      const bool grow = emax > RESCALE_SLACK || kv.z >= v_limit;
+      bool rescale = false;
+      // every softmax thread takes the same barriers: a wait that ran out is folded into the vote
+      if (named_bar_or(BAR_SMX, 128, grow || failed)) {
+        if (named_bar_or(BAR_SMX, 128, failed)) {
+          failed = true;
+          break;
+        }
+        // slow path: exact tile maxima and value range, new maxima, rescale factors of O
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+          if (r < rows) {
+            const float mx = warp_max(s[r]);
+            if (lane == 0) red[4 * r + q] = mx;
+          }
+        }
+        {
+          const float vm = warp_max(kv.z);
+          if (lane == 0) red_vs[q] = vm;
+        }
+        named_bar_or(BAR_SMX, 128, false);
+        const float vmax = fmaxf(fmaxf(red_vs[0], red_vs[1]), fmaxf(red_vs[2], red_vs[3]));
+        int e_tile = -1000;
+        if (vmax > 0.f) frexpf(vmax, &e_tile);  // vmax < 2^e_tile
+        const int e_new = max(e_run, e_tile);
+        const float o_range = e_run == -1000 ? 0.f : ldexpf(1.f, e_run - e_new);
+        e_run = e_new;
+        pv_mul = e_new == -1000 ? 0.f : ldexpf(1.f, -e_new);
+        v_limit = e_new == -1000 ? 0.f : ldexpf(1.f, e_new);
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+          float f = 1.f;
+          float4 c = rp[mb * NR + r];
+          if (r < rows) {
+            const float4 mv = *reinterpret_cast<const float4*>(red + 4 * r);
+            const float mt = fmaxf(fmaxf(mv.x, mv.y), fmaxf(mv.z, mv.w));
+            const float mn = (c.w == -INFINITY || mt > c.w + RESCALE_SLACK) ? mt : c.w;
+            const float alpha = mn == c.w ? 1.f : fast_exp2(c.w - mn);
+            c.w = mn;
+            l[r] *= alpha;
+            f = alpha * o_range;
+          }
+          rescale |= f != 1.f;
+          if (stid == 0) {
+            frow[r] = f;
+            rp[(mb ^ 1) * NR + r] = c;
+          }
+        }
+        named_bar_or(BAR_SMX, 128, false);  // exchange read; new maxima and factors visible
+        mb ^= 1;
+      }
+      // the previous tile's PV has completed: P^T buffer b (read by PV(i - 2)) is free, and O may be rescaled
+      if (i >= 1) failed |= !mbar_wait_bounded(&bars[D_PV_DONE], (i - 1) & 1);
+      tc_fence_after();
+      const float vsp = kv.z * pv_mul;
+      uint8_t* pb = smem + SM::OFF_P + 2 * b * SM::ATOM + patom;
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        float pv = 0.f;
+        if (r < rows) {
+          const float mr = rp[mb * NR + r].w;
+          const float pe = fast_exp2(s[r] - (mr == -INFINITY ? 0.f : mr));
+          l[r] += pe;
+          pv = pe * vsp;
+        }
+        *reinterpret_cast<__half*>(pb + (r >> 3) * 1024 + (r & 7) * 128 + ((pchunk ^ (r & 7)) << 4)) =
+            __float2half_rn(pv);
+      }
+      if (rescale && i >= 1) {  // before PV(i), which waits for this tile's P
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float o[NR];
+          tmem_ld_rows<NR>(tmem + TM_O + NR * c + lane_off, o);
+#pragma unroll
+          for (int r = 0; r < NR; ++r) o[r] *= frow[r];
+          tmem_st_rows<NR>(tmem + TM_O + NR * c + lane_off, o);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[D_P_FULL + b]);
+    }
+    // ---- epilogue: row sums, normalised partial O (channel order undone) and its lse
+    if (!named_bar_or(BAR_SMX, 128, failed)) {
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        if (r < rows) {
+          const float lt = warp_sum(l[r]);
+          if (lane == 0) red[4 * r + q] = lt;
+        }
+      }
+      named_bar_or(BAR_SMX, 128, false);
+      const bool ok = mbar_wait_bounded(&bars[D_PV_DONE], (ntl - 1) & 1);
+      tc_fence_after();
+      const float o_unit = e_run == -1000 ? 0.f : ldexpf(1.f, e_run);
+      const int g = lane & 7, mm = lane >> 3;
+#pragma unroll 1
+      for (int c = 0; c < 2 && ok; ++c) {
+        float o[NR];
+        tmem_ld_rows<NR>(tmem + TM_O + NR * c + lane_off, o);
+        const int ch = 64 * q + 8 * g + 4 * c + mm;
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+          if (r < rows) {
+            const float4 lv = *reinterpret_cast<const float4*>(red + 4 * r);
+            const float lt = (lv.x + lv.y) + (lv.z + lv.w);
+            const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
+            const int64_t prow = (static_cast<int64_t>(tok) * p.nq + qh) * p.num_splits + split;
+            p.part_o[prow * DEC_HS + ch] = lt > 0.f ? o[r] * (o_unit / lt) : 0.f;
           }
         }
       }
-      const int tau0 = 16 * kk + 4 * t;
-      const uint2 blo = *reinterpret_cast<const uint2*>(zb_lo + tau0);  // {tau0, tau0+1}, {tau0+2, tau0+3}
-      const uint2 bhi = *reinterpret_cast<const uint2*>(zb_hi + tau0);
-      // f = 0: tokens (tau0, tau0 + 1); f = 1: tokens (tau0 + 2, tau0 + 3)
-      uint32_t vr[2][8];  // [f][channel offset 0..7]
+      if (stid == 0) {
 #pragma unroll
-      for (int f = 0; f < 2; ++f) {
-        const uint32_t wa = vw[kk][2 * f], wb = vw[kk][2 * f + 1];
-        const uint32_t lo_b = f ? blo.y : blo.x, hi_b = f ? bhi.y : bhi.x;
-        const uint32_t x = prmt(wa, wb, 0x5410u), y = prmt(wa, wb, 0x7632u);
-        const uint32_t x8 = x >> 8, y8 = y >> 8;
-        vr[f][0] = nib_lo(x, lo_b);
-        vr[f][1] = nib_hi(x, hi_b);
-        vr[f][2] = nib_lo(x8, lo_b);
-        vr[f][3] = nib_hi(x8, hi_b);
-        vr[f][4] = nib_lo(y, lo_b);
-        vr[f][5] = nib_hi(y, hi_b);
-        vr[f][6] = nib_lo(y8, lo_b);
-        vr[f][7] = nib_hi(y8, hi_b);
-      }
-#pragma unroll
-      for (int mt = 0; mt < 4; ++mt) {
-        const uint32_t A[4] = {vr[0][2 * mt], vr[0][2 * mt + 1], vr[1][2 * mt], vr[1][2 * mt + 1]};
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_f16_16816(o[mt][nt], A, bf[nt][0], bf[nt][1]);
+        for (int r = 0; r < NR; ++r) {
+          if (r < rows) {
+            const float4 lv = *reinterpret_cast<const float4*>(red + 4 * r);
+            const float lt = (lv.x + lv.y) + (lv.z + lv.w);
+            const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
+            p.part_lse[(static_cast<int64_t>(tok) * p.nq + qh) * p.num_splits + split] =
+                lt > 0.f ? rp[mb * NR + r].w + log2f(lt) : -INFINITY;
+          }
+        }
       }
     }
   }
 
-  if (failed) {
-    // give the copies still in flight a bounded chance to land before the CTA's shared memory goes away
-    if (tid == 0) {
-      for (int j = fail_tile; j < issued; ++j)
-        mbar_wait_bounded(&bars[j % DEC_STAGES], (j / DEC_STAGES) & 1, 100000000ull);
-      mbar_wait_bounded(&bars[DEC_STAGES], 0, 100000000ull);
-    }
-    __syncthreads();
-    return;
-  }
-
-  // --- epilogue: totals of l, normalised partial O and lse ---------------------------------------------------
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      float l = l_part[nt][e];
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-      l_part[nt][e] = l;
-    }
+  // every role is done with TMEM (the MMA warp saw its last commit complete)
+  tc_fence_before();
   __syncthreads();
-  if (g == 0) {
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) red[(8 * nt + 2 * t + e) * 4 + warp] = l_part[nt][e];
-  }
-  __syncthreads();
-  const float o_unit = e_run == -1000 ? 0.f : ldexpf(1.f, e_run);
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int r = 8 * nt + 2 * t + e;
-      if (r >= rows) continue;
-      const float4 lv = *reinterpret_cast<const float4*>(red + r * 4);
-      const float l = (lv.x + lv.y) + (lv.z + lv.w);
-      const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
-      const int64_t prow = (static_cast<int64_t>(tok) * p.nq + qh) * p.num_splits + split;
-      const float inv = l > 0.f ? o_unit / l : 0.f;
-      float v[8];
-#pragma unroll
-      for (int mt = 0; mt < 4; ++mt) {
-        v[2 * mt] = o[mt][nt][e] * inv;
-        v[2 * mt + 1] = o[mt][nt][2 + e] * inv;
-      }
-      float4* dst = reinterpret_cast<float4*>(p.part_o + prow * DEC_HS + 64 * warp + 8 * g);
-      dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-      dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-      if (warp == 0 && g == 0) p.part_lse[prow] = l > 0.f ? m_used[nt][e] + log2f(l) : -INFINITY;
-    }
+  tc_fence_after();
+  if (warp == W_MMA) tmem_dealloc(tmem, 512);
 }
 
 // ---------------------------------------------------------------------------------------------------- K2 merge
@@ -826,20 +883,20 @@ static int merge_dispatch(const MergeParams& mp, int dtype, int head_size, int64
   }
 }
 
-template <int FMT, int DT, int NT>
+template <int FMT, int DT, int NR>
 static int launch_decode_t(const DecodeParams& dp, int num_seqs, cudaStream_t st) {
-  using SM = DecSmem<FMT, NT>;
-  static bool configured[64] = {false};
+  using SM = DecSmem<FMT, NR>;
+  static std::atomic<bool> configured[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
+  if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
     cudaError_t e =
-        cudaFuncSetAttribute(decode_kernel<FMT, DT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES);
+        cudaFuncSetAttribute(decode_kernel<FMT, DT, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES);
     if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode smem attribute: %s", cudaGetErrorString(e));
-    if (dev >= 0 && dev < 64) configured[dev] = true;
+    if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
   }
-  // programmatic dependent launch: the CTAs start their cache copies while K0q finishes (they wait for it before
-  // reading the query rows)
+  // programmatic dependent launch: the CTAs start their cache copies while K0q finishes (the softmax warps wait for
+  // it before reading the query rows)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(dp.num_splits), static_cast<unsigned>(dp.nkv), static_cast<unsigned>(num_seqs));
   cfg.blockDim = dim3(DEC_THREADS);
@@ -850,38 +907,33 @@ static int launch_decode_t(const DecodeParams& dp, int num_seqs, cudaStream_t st
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<FMT, DT, NT>, dp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<FMT, DT, NR>, dp);
   if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
   return QP_OK;
 }
 
 template <int FMT, int DT>
-static int launch_decode_nt(const DecodeParams& dp, int nt, int num_seqs, cudaStream_t st) {
-  switch (nt) {
-    case 1: return launch_decode_t<FMT, DT, 1>(dp, num_seqs, st);
-    case 2: return launch_decode_t<FMT, DT, 2>(dp, num_seqs, st);
-    case 3: return launch_decode_t<FMT, DT, 3>(dp, num_seqs, st);
-    default: return launch_decode_t<FMT, DT, 4>(dp, num_seqs, st);
-  }
+static int launch_decode_nr(const DecodeParams& dp, int rows, int num_seqs, cudaStream_t st) {
+  return rows <= 16 ? launch_decode_t<FMT, DT, 16>(dp, num_seqs, st) : launch_decode_t<FMT, DT, 32>(dp, num_seqs, st);
 }
 
 }  // namespace qp
 
 using namespace qp;
 
-// Split-count heuristic: whole waves of 3 CTAs per SM, a fixed cost per CTA, at least 4 tiles per split.
+// Split-count heuristic: one CTA per SM (a CTA holds all of TMEM), whole waves, a fixed cost of about two tiles per
+// CTA (pipeline fill and drain, epilogue), 128-key tiles.
 extern "C" int qp_decode_num_splits(int num_seqs, int num_kv_heads, int max_seqlen_k, int sm_count) {
   if (sm_count <= 0) sm_count = device_sm_count();
   const int pairs = max(1, num_seqs * num_kv_heads);
   const int tiles = max(1, (max_seqlen_k + DEC_TILE - 1) / DEC_TILE);
-  const int slots = 3 * sm_count;
-  const int max_splits = max(1, min(1024, tiles / 4));
+  const int max_splits = max(1, min(1024, tiles / 2));
   int best = 1;
   double best_cost = 1e30;
   for (int s = 1; s <= max_splits; ++s) {
     const long ctas = static_cast<long>(pairs) * s;
-    const long waves = (ctas + slots - 1) / slots;
-    const double cost = waves * (static_cast<double>((tiles + s - 1) / s) + 6.0);
+    const long waves = (ctas + sm_count - 1) / sm_count;
+    const double cost = waves * (static_cast<double>((tiles + s - 1) / s) + 2.0);
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
       best = s;
@@ -891,7 +943,7 @@ extern "C" int qp_decode_num_splits(int num_seqs, int num_kv_heads, int max_seql
 }
 
 // Workspace of qp_paged_decode: [part_o rows x head fp32][part_lse rows fp32, 256-aligned][prepared query rows
-// tokens x q heads x Q_STRIDE bytes], rows = tokens x q heads x splits.
+// tokens x q heads x Q_REC bytes], rows = tokens x q heads x splits.
 static int64_t decode_qrec_offset(int64_t num_q_tokens, int num_q_heads, int head_size, int num_splits) {
   const int64_t rows = num_q_tokens * num_q_heads * static_cast<int64_t>(num_splits);
   return rows * head_size * 4 + ((rows * 4 + 255) / 256) * 256;
@@ -899,7 +951,7 @@ static int64_t decode_qrec_offset(int64_t num_q_tokens, int num_q_heads, int hea
 
 extern "C" int64_t qp_decode_workspace_bytes(int64_t num_q_tokens, int num_q_heads, int head_size, int num_splits) {
   return decode_qrec_offset(num_q_tokens, num_q_heads, head_size, num_splits) +
-         num_q_tokens * num_q_heads * static_cast<int64_t>(Q_STRIDE);
+         num_q_tokens * num_q_heads * static_cast<int64_t>(Q_REC);
 }
 
 extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head,
@@ -956,9 +1008,6 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
   dp.block_size = block_size;
   dp.block_stride = block_stride;
   dp.head_stride = head_stride;
-  dp.ks_off = static_cast<int>(ks_off);
-  dp.v_off = static_cast<int>(v_off);
-  dp.vs_off = static_cast<int>(vs_off);
   dp.nq = num_q_heads;
   dp.nkv = num_kv_heads;
   dp.group = group;
@@ -974,7 +1023,7 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
   dp.part_o = static_cast<float*>(workspace);
   dp.part_lse = dp.part_o + rows * head_size;
 
-  const int nt = (max_seqlen_q * group + 7) / 8;
+  const int max_rows = max_seqlen_q * group;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   {
     uint8_t* qrec = const_cast<uint8_t*>(dp.qrec);
@@ -995,11 +1044,11 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
   }
   int rc;
   if (fmt == FMT_INT4)
-    rc = dtype == DT_BF16 ? launch_decode_nt<FMT_INT4, DT_BF16>(dp, nt, num_seqs, st)
-                          : launch_decode_nt<FMT_INT4, DT_F16>(dp, nt, num_seqs, st);
+    rc = dtype == DT_BF16 ? launch_decode_nr<FMT_INT4, DT_BF16>(dp, max_rows, num_seqs, st)
+                          : launch_decode_nr<FMT_INT4, DT_F16>(dp, max_rows, num_seqs, st);
   else
-    rc = dtype == DT_BF16 ? launch_decode_nt<FMT_K8V4, DT_BF16>(dp, nt, num_seqs, st)
-                          : launch_decode_nt<FMT_K8V4, DT_F16>(dp, nt, num_seqs, st);
+    rc = dtype == DT_BF16 ? launch_decode_nr<FMT_K8V4, DT_BF16>(dp, max_rows, num_seqs, st)
+                          : launch_decode_nr<FMT_K8V4, DT_F16>(dp, max_rows, num_seqs, st);
   if (rc) return rc;
   if (out_mode == 2) return QP_OK;  // split partials stay in the workspace
 
@@ -1076,12 +1125,16 @@ extern "C" int qp_merge_attn_partials(int dtype, int head_size, int64_t num_toke
 // - Its device address is looked up (cudaGetSymbolAddress) on the first call on each device, with that device
 //   current; make that first call before any stream capture.
 // - Every call on a device uses the same array and it keeps the last call's contents. Nothing in it has to start at
-//   zero (each call writes every partial it later reads), but calls that overlap on the GPU (two streams, two host
-//   threads) race on it: serialize them.
-// - Sizes whose partials exceed the array are rejected with QP_ERR_WORKSPACE.
+//   zero (each call writes every partial and query row it later reads), but calls that overlap on the GPU (two
+//   streams, two host threads) race on it: serialize them.
+// - The array holds the split partials and the prepared query rows (qp_decode_workspace_bytes); sizes that need
+//   more are rejected with QP_ERR_WORKSPACE.
+// - Only out_mode 0 and 1 are served (out_mode 2 would leave the partials where no caller can reach them), and the
+//   causal mask assumes the keys given are the sequence's last ones (tokens_after_keys = 0): an ordinary single-GPU
+//   decode, not a sequence-parallel rank holding an earlier range.
 static constexpr int64_t kStaticDecodeScratchBytes = 32ll << 20;
 static __device__ __align__(256) uint8_t g_static_decode_scratch[kStaticDecodeScratchBytes];
-static void* g_static_decode_scratch_addr[64] = {};
+static std::atomic<void*> g_static_decode_scratch_addr[64];
 
 extern "C" int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t q_stride_token,
                                       int64_t q_stride_head, void* out, int64_t out_stride_token,
@@ -1093,6 +1146,9 @@ extern "C" int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t
                                       int num_kv_heads, int head_size, float softmax_scale,
                                       const uint32_t* rht_sign_bits, int q_rotated, int out_mode, float* lse_out,
                                       int num_splits, void* stream) {
+  if (out_mode != 0 && out_mode != 1)
+    return set_error(QP_ERR_INVALID, "decode (static scratch): out_mode %d (0 or 1: the partials stay private)",
+                     out_mode);
   const int64_t need = qp_decode_workspace_bytes(num_q_tokens, num_q_heads, head_size, num_splits);
   if (need > kStaticDecodeScratchBytes)
     return set_error(QP_ERR_WORKSPACE,
@@ -1103,17 +1159,17 @@ extern "C" int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode (static scratch): cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return set_error(QP_ERR_UNSUPPORTED, "decode (static scratch): device %d >= 64", dev);
-  if (g_static_decode_scratch_addr[dev] == nullptr) {
-    void* addr = nullptr;
-    e = cudaGetSymbolAddress(&addr, g_static_decode_scratch);
-    if (e != cudaSuccess || addr == nullptr)
+  void* scratch = g_static_decode_scratch_addr[dev].load(std::memory_order_acquire);
+  if (scratch == nullptr) {
+    // two host threads may both look it up the first time; they store the same address
+    e = cudaGetSymbolAddress(&scratch, g_static_decode_scratch);
+    if (e != cudaSuccess || scratch == nullptr)
       return set_error(QP_ERR_CUDA, "decode (static scratch): cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_static_decode_scratch_addr[dev] = addr;
+    g_static_decode_scratch_addr[dev].store(scratch, std::memory_order_release);
   }
   return qp_paged_decode(fmt, dtype, q, q_stride_token, q_stride_head, out, out_stride_token, out_stride_head,
                          num_q_tokens, num_seqs, cu_seqlens_q, seqused_k, max_seqlen_q, block_table,
                          block_table_stride, cache, block_size, block_stride, head_stride, slot_stride, k_off, ks_off,
                          v_off, vs_off, num_q_heads, num_kv_heads, head_size, softmax_scale, rht_sign_bits, q_rotated,
-                         0, out_mode, lse_out, num_splits, g_static_decode_scratch_addr[dev], kStaticDecodeScratchBytes,
-                         stream);
+                         0, out_mode, lse_out, num_splits, scratch, kStaticDecodeScratchBytes, stream);
 }
