@@ -340,3 +340,94 @@ def test_store_dispatch(monkeypatch):
     assert stock_calls == ["stock"]
     with pytest.raises(ValueError, match="k8v4"):
         store(k96, k96, kc8, kc8, torch.zeros(3, dtype=torch.int64), k_scale_cache=None, v_scale_cache=None)
+
+
+# ---------------------------------------------------------------- k8v4 registration and backend glue (fake vLLM)
+def _fake_vllm_for_k8v4(monkeypatch):
+    """Stand-ins for the vLLM pieces the k8v4 glue touches: the kv-cache dtype registry, KVQuantMode and the Triton
+    attention backend / impl (vllm_quantpack/attention/k8v4_kv.py:89-166 names them)."""
+    import dataclasses
+    import enum
+
+    ns = types.SimpleNamespace(registry={})
+    cache = types.ModuleType("vllm.config.cache")
+    cache.get_kv_cache_dtype_handler = lambda name: ns.registry.get(name)
+    cache.register_kv_cache_dtype = lambda name: (lambda cls: ns.registry.__setitem__(name, cls) or cls)
+    kvi = types.ModuleType("vllm.v1.kv_cache_interface")
+
+    class KVQuantMode(enum.Enum):
+        NONE = 0
+        INT4_PER_TOKEN_HEAD = 5
+
+    kvi.KVQuantMode = KVQuantMode
+    tri = types.ModuleType("vllm.v1.attention.backends.triton_attn")
+
+    @dataclasses.dataclass
+    class Spec:
+        head_size: int
+        head_size_v: int
+        dtype: torch.dtype
+        kv_quant_mode: object
+        state_content_bytes: object = None
+
+    class Backend:
+        supported_kv_cache_dtypes = ["auto", "int4_per_token_head"]
+
+        @classmethod
+        def customize_spec(cls, spec):
+            return dataclasses.replace(spec, state_content_bytes=-1)
+
+    class Impl:
+        def __init__(self, dtype, hs):
+            self.kv_cache_dtype, self.head_size = dtype, hs
+            self._k_scale_cache = self._v_scale_cache = None
+
+        def _ensure_scale_caches(self, kv_cache):
+            self._k_scale_cache = "stock"
+
+        def _pth_key_value_caches(self, kv_cache):
+            return "stock", "stock"
+
+    tri.TritonAttentionBackend, tri.TritonAttentionImpl = Backend, Impl
+    for name in ("vllm", "vllm.config", "vllm.v1", "vllm.v1.attention", "vllm.v1.attention.backends"):
+        monkeypatch.setitem(sys.modules, name, types.ModuleType(name))
+    for mod in (cache, kvi, tri):
+        monkeypatch.setitem(sys.modules, mod.__name__, mod)
+    monkeypatch.setattr(sys.modules["vllm.config"], "cache", cache, raising=False)
+    monkeypatch.setattr(sys.modules["vllm.v1.attention.backends"], "triton_attn", tri, raising=False)
+    ns.Spec, ns.Backend, ns.Impl, ns.mode = Spec, Backend, Impl, KVQuantMode.INT4_PER_TOKEN_HEAD
+    return ns
+
+
+def test_k8v4_dtype_registered_once_with_int8_storage(monkeypatch):
+    ns = _fake_vllm_for_k8v4(monkeypatch)
+    assert k8v4_kv.register_dtype(LOG) is True
+    handler = ns.registry[k8v4_kv.NAME]()
+    assert handler.torch_dtype() == torch.int8 and handler.quant_mode() == ns.mode
+    first = ns.registry[k8v4_kv.NAME]
+    assert k8v4_kv.register_dtype(LOG) is True and ns.registry[k8v4_kv.NAME] is first
+
+
+def test_k8v4_dtype_not_registered_without_registry(monkeypatch):
+    monkeypatch.setitem(sys.modules, "vllm.config.cache", None)
+    assert k8v4_kv.register_dtype(LOG) is False
+
+
+def test_k8v4_backend_patch_sizes_spec_and_serves_views(monkeypatch):
+    ns = _fake_vllm_for_k8v4(monkeypatch)
+    assert k8v4_kv.patch_backend(None, LOG) is True
+    spec = ns.Backend.customize_spec(ns.Spec(256, 256, torch.int8, ns.mode))
+    assert spec.state_content_bytes == 392
+    assert ns.Backend.customize_spec(ns.Spec(256, 256, torch.uint8, ns.mode)).state_content_bytes == -1  # int4: stock
+    assert k8v4_kv.NAME in ns.Backend.supported_kv_cache_dtypes
+    kv = torch.zeros((3, NKV, 16, 392), dtype=torch.int8)
+    layer = ns.Impl(k8v4_kv.NAME, HS)
+    key, value = layer._pth_key_value_caches(kv)
+    assert key.dtype == torch.int8 and key.shape == (3, 16, NKV, HS) and value.shape == (3, 16, NKV, HS // 2)
+    assert (layer._k_scale_cache == 1).all() and (layer._v_scale_cache == 1).all()
+    assert (kv[..., HS:HS + 4].view(torch.float32) == 1).all()      # the scales live inside the cells
+    other = ns.Impl("int4_per_token_head", HS)
+    assert other._pth_key_value_caches(kv) == ("stock", "stock")
+    patched = ns.Impl._pth_key_value_caches
+    assert k8v4_kv.patch_backend(None, LOG) is True and ns.Impl._pth_key_value_caches is patched
+    assert ns.Backend.supported_kv_cache_dtypes.count(k8v4_kv.NAME) == 1
