@@ -270,7 +270,7 @@ def test_decode_step_is_one_launch_without_host_read(monkeypatch):
     rec = Recorder(monkeypatch)
     stock, stock_calls = _stock_recorder()
     fn = int4_kv.make_unified_attention(stock)
-    monkeypatch.setattr(int4_kv, "_step_lengths", lambda *a: pytest.fail("decode steps must not read lengths"))
+    monkeypatch.setattr(int4_kv.StepPlan, "of", lambda *a: pytest.fail("decode steps must not read lengths"))
     q, kc, out, args = _step([4, 3, 1, 0, 4], [20000, 9000, 16384, 5, 3072])
     fn(q, kc, kc, out, **args)
     assert rec.calls == [("decode", q.shape[0], [0, 4, 7, 8, 8, 12], [20000, 9000, 16384, 5, 3072], 4, None)]
@@ -431,3 +431,46 @@ def test_k8v4_backend_patch_sizes_spec_and_serves_views(monkeypatch):
     patched = ns.Impl._pth_key_value_caches
     assert k8v4_kv.patch_backend(None, LOG) is True and ns.Impl._pth_key_value_caches is patched
     assert ns.Backend.supported_kv_cache_dtypes.count(k8v4_kv.NAME) == 1
+
+
+def test_k8v4_call_outside_the_kernels_raises(monkeypatch):
+    """The stock int4 kernel would read a k8v4 cache's int8 keys as nibbles: such calls raise instead."""
+    Recorder(monkeypatch)
+    stock, stock_calls = _stock_recorder()
+    fn = int4_kv.make_unified_attention(stock)
+    q, _, out, args = _step([4], [5000], window=(4096, 0))
+    kc8 = torch.zeros((4, 16, NKV, HS), dtype=torch.int8)
+    with pytest.raises(NotImplementedError, match="k8v4"):
+        fn(q, kc8, kc8, out, **args)
+    with pytest.raises(NotImplementedError, match="k8v4"):
+        fn(q, kc8, kc8, out, **dict(args, softcap=30.0))
+    fn2 = int4_kv.make_unified_attention(stock, prefill_on=False)
+    q, _, out, args = _step([256], [40000])
+    with pytest.raises(NotImplementedError, match="k8v4"):
+        fn2(q, kc8, kc8, out, **args)
+    assert not stock_calls
+
+
+def test_step_plan_is_made_once_per_step(monkeypatch):
+    """Every layer of a step gets the same length tensors: only the first layer reads them (one host read)."""
+    Recorder(monkeypatch)
+    fn = int4_kv.make_unified_attention(_stock_recorder()[0])
+    made = []
+    init = int4_kv.StepPlan.__init__
+
+    def counting(self, *a):
+        made.append(1)
+        init(self, *a)
+
+    monkeypatch.setattr(int4_kv.StepPlan, "__init__", counting)
+    step = types.SimpleNamespace()
+    monkeypatch.setattr(int4_kv, "_forward_step", lambda: step)
+    q, kc, out, args = _step([256, 2], [40000, 20000])
+    for _ in range(3):
+        fn(q, kc, kc, out, **args)
+    assert len(made) == 1
+    step = types.SimpleNamespace()                     # the next step reads its lengths again
+    fn(q, kc, kc, out, **args)
+    assert len(made) == 2
+    fn(q, kc, kc, out, **dict(args, seqused_k=args["seqused_k"].clone()))   # other tensors, same step: new plan
+    assert len(made) == 3

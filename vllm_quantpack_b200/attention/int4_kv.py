@@ -22,6 +22,8 @@ import importlib
 import itertools
 import os
 
+import torch
+
 MODULE = "vllm.v1.attention.ops.int4_per_token_head"
 PACKED_DTYPES = ("int4_per_token_head", "k8v4_per_token_head")   # caches served by the B200 kernels
 MAX_Q_SPLIT_KV = 4               # MTP / EAGLE verification with up to 3 draft tokens
@@ -76,25 +78,73 @@ def _plain(q, window_size, softcap, sinks, alibi_slopes, qq_bias, output_scale, 
         and qq_bias is None and output_scale is None and mm_prefix_range is None and q.shape[2] == HEAD_SIZE
 
 
-def _step_lengths(cu_seqlens_q, seqused_k):
-    """cu_seqlens_q and seqused_k as host lists, copied once per forward step: every attention layer of a step gets
-    the same tensors, so the lists are kept on the step's forward context keyed by the tensors themselves
-    (int4_kv.py:260-278)."""
+def _forward_step():
+    """vLLM's forward context of the running step, or None outside one (tests, eager calls)."""
     try:
         from vllm.forward_context import get_forward_context, is_forward_context_available
-        step = get_forward_context() if is_forward_context_available() else None
+        return get_forward_context() if is_forward_context_available() else None
     except Exception:
-        step = None
-    hit = getattr(step, "_quantpack_int4_lengths", None)
-    if hit is not None and hit[0] is cu_seqlens_q and hit[1] is seqused_k:
-        return hit[2], hit[3]
-    cu, used = cu_seqlens_q.tolist(), seqused_k.tolist()
-    if step is not None:
-        try:
-            step._quantpack_int4_lengths = (cu_seqlens_q, seqused_k, cu, used)
-        except Exception:
-            pass
-    return cu, used
+        return None
+
+
+class StepPlan:
+    """How one forward step's requests split over the kernels, worked out once per step and reused by every attention
+    layer of it (they all get the same cu_seqlens_q / seqused_k tensors): the lengths come to the host in ONE read
+    (the two tensors concatenated on the GPU), and the sub-batch index tensors go to the GPU from pinned memory
+    without a wait. The reference reads both lists per step (int4_kv.py:260-278) and rebuilds its sub-batch indices
+    per layer; here the second and later layers of a step touch no host memory at all."""
+
+    def __init__(self, cu_seqlens_q, seqused_k, group, prefill_on):
+        nseq = seqused_k.shape[0]
+        both = torch.cat([cu_seqlens_q.to(torch.int64), seqused_k.to(torch.int64)]).tolist()
+        self.cu, self.used = both[:nseq + 1], both[nseq + 1:]
+        self.dec, self.pre, self.stock = split_step(self.cu, self.used, group, prefill_on)
+        dev = cu_seqlens_q.device
+        self.dec_batch = _SubBatch(self.dec, self.cu, self.used, dev) if self.dec else None
+        self.stock_batch = _SubBatch(self.stock, self.cu, self.used, dev) if self.stock else None
+
+    @staticmethod
+    def of(cu_seqlens_q, seqused_k, group, prefill_on):
+        """The step's plan, kept on vLLM's forward context (keyed by the length tensors themselves: another KV-cache
+        group of the same step gets other tensors)."""
+        step = _forward_step()
+        plans = getattr(step, "_quantpack_b200_plans", None) if step is not None else None
+        key = (id(cu_seqlens_q), id(seqused_k), group, prefill_on)
+        if plans is not None and key in plans and plans[key][0] is cu_seqlens_q and plans[key][1] is seqused_k:
+            return plans[key][2]
+        plan = StepPlan(cu_seqlens_q, seqused_k, group, prefill_on)
+        if step is not None:
+            try:
+                if plans is None:
+                    plans = step._quantpack_b200_plans = {}
+                plans[key] = (cu_seqlens_q, seqused_k, plan)
+            except Exception:
+                pass
+        return plan
+
+
+class _SubBatch:
+    """Requests `idx` of a step as a batch of their own: gather rows / per-request tensors, scatter the output."""
+
+    def __init__(self, idx, cu, used, device):
+        lens = [cu[i + 1] - cu[i] for i in idx]
+        rows = [r for i in idx for r in range(cu[i], cu[i + 1])]
+        def to_dev(x, dt):
+            t = torch.tensor(x, dtype=dt)
+            return t.pin_memory().to(device, non_blocking=True) if device.type == "cuda" else t.to(device)
+
+        self.rows = to_dev(rows, torch.int64)
+        self.sel = to_dev(idx, torch.int64)
+        self.cu = to_dev([0, *itertools.accumulate(lens)], torch.int32)
+        self.max_q, self.max_k = max(lens), max(used[i] for i in idx)
+
+    def run(self, fn, q, out, args):
+        """fn(q_rows, out_rows, args) with the sub-batch's own lengths, block table and query rows."""
+        sub_out = torch.empty((self.rows.shape[0],) + tuple(out.shape[1:]), dtype=out.dtype, device=out.device)
+        sub = dict(args, cu_seqlens_q=self.cu, max_seqlen_q=self.max_q, seqused_k=args["seqused_k"][self.sel],
+                   block_table=args["block_table"][self.sel], max_seqlen_k=self.max_k)
+        fn(q[self.rows], sub_out, sub)
+        out[self.rows] = sub_out
 
 
 def split_step(cu, used, group, prefill_on=True):
@@ -117,22 +167,9 @@ def split_step(cu, used, group, prefill_on=True):
 
 def make_unified_attention(stock_unified, prefill_on=True):
     """The replacement of `unified_attention_int4` (signature of int4_kv.py:294-301), falling back to
-    `stock_unified` for what the B200 kernels do not cover."""
-    import torch
-
-    from . import ops
-
-    def _sub_batch(fn, q, out, idx, cu, used, args):
-        """Run fn(q_rows, out_rows, args) on the requests `idx` of the step gathered into a sub-batch."""
-        rows = torch.cat([torch.arange(cu[i], cu[i + 1], device=q.device) for i in idx])
-        lens = [cu[i + 1] - cu[i] for i in idx]
-        sub_cu = torch.tensor([0, *itertools.accumulate(lens)], dtype=torch.int32, device=q.device)
-        sel = torch.tensor(idx, device=q.device)
-        sub_out = torch.empty((len(rows),) + tuple(out.shape[1:]), dtype=out.dtype, device=out.device)
-        sub = dict(args, cu_seqlens_q=sub_cu, max_seqlen_q=max(lens), seqused_k=args["seqused_k"][sel],
-                   block_table=args["block_table"][sel], max_seqlen_k=max(used[i] for i in idx))
-        fn(q[rows], sub_out, sub)
-        out[rows] = sub_out
+    `stock_unified` for int4 calls the B200 kernels do not cover. A k8v4 cache has no stock kernel to fall back to
+    (the stock int4 kernel would read its int8 keys as nibbles), so such a call raises instead."""
+    from . import k8v4_kv, ops
 
     def unified_attention_int4(q, k_cache, v_cache, out, *, cu_seqlens_q, max_seqlen_q, seqused_k, max_seqlen_k,
                                softmax_scale, window_size, block_table, softcap, sinks, alibi_slopes, use_alibi_sqrt,
@@ -143,6 +180,11 @@ def make_unified_attention(stock_unified, prefill_on=True):
                     use_alibi_sqrt=use_alibi_sqrt, qq_bias=qq_bias, output_scale=output_scale,
                     mm_prefix_range=mm_prefix_range, k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache, **kw)
         if not _plain(q, window_size, softcap, sinks, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
+            if k8v4_kv.is_k8v4(k_cache):
+                raise NotImplementedError(
+                    f"{k8v4_kv.NAME}: sliding window, softcap, sinks, ALiBi, qq_bias, FP8 output, mm_prefix ranges and "
+                    f"head sizes other than {HEAD_SIZE} are not served by the B200 kernels, and vLLM's stock int4 "
+                    f"kernel cannot read a k8v4 cache")
             return stock_unified(q, k_cache, v_cache, out, **args)
         group = q.shape[1] // k_cache.shape[2]
         splits = decode_splits_override()
@@ -156,15 +198,16 @@ def make_unified_attention(stock_unified, prefill_on=True):
         if max_seqlen_q <= MAX_Q_SPLIT_KV and max_seqlen_q * group <= MAX_DECODE_ROWS:
             # a decode step: no host read of the lengths (CUDA-graph capturable)
             return decode(q, out, args)
-        cu, used = _step_lengths(cu_seqlens_q, seqused_k)
-        dec, pre, rest = split_step(cu, used, group, prefill_on)
-        if dec:
-            _sub_batch(decode, q, out, dec, cu, used, args)
-        if rest:
-            def stock(qs, outs, a):
-                stock_unified(qs, k_cache, v_cache, outs, **a)
-            _sub_batch(stock, q, out, rest, cu, used, args)
-        for i in pre:
+        plan = StepPlan.of(cu_seqlens_q, seqused_k, group, prefill_on)
+        if plan.dec_batch is not None:
+            plan.dec_batch.run(decode, q, out, args)
+        if plan.stock_batch is not None:
+            if k8v4_kv.is_k8v4(k_cache):
+                raise NotImplementedError(f"{k8v4_kv.NAME}: prefill chunks need the B200 prefill kernel "
+                                          f"(VLLM_QUANTPACK_INT4_FA_PREFILL=0 leaves them to the stock int4 kernel)")
+            plan.stock_batch.run(lambda qs, outs, a: stock_unified(qs, k_cache, v_cache, outs, **a), q, out, args)
+        cu, used = plan.cu, plan.used
+        for i in plan.pre:
             ops.prefill(q[cu[i]:cu[i + 1]], k_cache, v_cache, out[cu[i]:cu[i + 1]], block_row=block_table[i],
                         n=used[i], softmax_scale=softmax_scale, k_scale_cache=k_scale_cache,
                         v_scale_cache=v_scale_cache)

@@ -36,6 +36,7 @@
 #include <math.h>
 
 #include <atomic>
+#include <type_traits>
 
 #include "qp_api_internal.h"
 #include "qp_common.cuh"
@@ -46,15 +47,22 @@ namespace qp {
 constexpr int DEC_HS = 256;
 constexpr int DEC_TILE = 128;  // keys per tile (TMEM lanes of the QK accumulator)
 constexpr int DEC_MAX_ROWS = 32;
-constexpr int DEC_WARPS = 14;
+#ifndef QP_DEC_SMX_HALVES
+#define QP_DEC_SMX_HALVES 1
+#endif
+constexpr int SMX_HALVES = QP_DEC_SMX_HALVES;  // softmax warps per TMEM lane quarter (each takes RL / halves rows)
+static_assert(SMX_HALVES == 1 || SMX_HALVES == 2, "one or two softmax warps per lane quarter");
+constexpr int DEC_WARPS = 10 + 4 * SMX_HALVES;
 constexpr int DEC_THREADS = 32 * DEC_WARPS;
 // registers per thread one CTA may hold: each SM sub-partition's 16384 registers host every fourth warp
 constexpr int DEC_REGS = (16384 / (32 * ((DEC_WARPS + 3) / 4))) & ~7;
-constexpr int W_MMA = 1, W_VAL = 6, W_SMX = 10;  // warp 0 producer, 2-5 key operand, 6-9 value operand, 10-13 softmax
+// warp 0 producer, 1 MMA issuer, 2-5 key operand, 6-9 value operand, 10.. softmax (SMX_HALVES per lane quarter)
+constexpr int W_MMA = 1, W_VAL = 6, W_SMX = 10;
+constexpr int SMX_THREADS = 32 * (DEC_WARPS - W_SMX);
 constexpr int Q_REC = DEC_HS * 2 + 16;  // prepared query row: 256 fp16 in operand order, then 4 fp32
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float RESCALE_SLACK = 8.f;
-constexpr int BAR_SMX = 1;  // named barrier of the 4 softmax warps
+constexpr int BAR_SMX = 1;  // named barrier of the softmax warps
 
 // TMEM columns (512): key operand double-buffered at [0, 128) and [384, 512); value operand slots (64 keys each,
 // two channel halves of 32 columns) at [128, 256); S double-buffered and O (two channel halves) after it.
@@ -98,13 +106,15 @@ struct DecSmem {
   static constexpr int OFF_Q = 0;                          // Q: 4 atoms (256 channels), K-major
   static constexpr int OFF_P = OFF_Q + 4 * ATOM;           // P^T: 2 buffers x 2 atoms (128 keys), K-major
   static constexpr int OFF_RAW = OFF_P + 4 * ATOM;         // RS raw stages
-  static constexpr int OFF_KP = OFF_RAW + RS * RAW;        // [2][128] float4: key scale, key zero point, value scale
-  static constexpr int OFF_ZB = OFF_KP + 2 * 128 * 16;     // [2][128] u32: paired value zero-point operand biases
-  static constexpr int OFF_RP = OFF_ZB + 2 * 128 * 4;      // [2][NR] float4: row scale, bias, plain sum, row maximum
-  static constexpr int OFF_LIM = OFF_RP + 2 * NR * 16;     // [NR] int: last key the row sees
-  static constexpr int OFF_RED = OFF_LIM + NR * 4;         // [NR][4] exchange, [4] value-scale maxima, [NR] factors
-  static constexpr int OFF_BAR = (OFF_RED + (NR * 4 + 4 + NR) * 4 + 7) / 8 * 8;
-  static constexpr int NBAR = 32;
+  static constexpr int OFF_KP = OFF_RAW + RS * RAW;        // [RS][128] float4: key scale, key zp, value scale
+  static constexpr int OFF_ZB = OFF_KP + RS * 128 * 16;    // [RS][128] u32: paired value zero-point operand biases
+  static constexpr int OFF_RP = OFF_ZB + RS * 128 * 4;      // [2][NR] float2: row scale, row maximum
+  static constexpr int OFF_LIM = OFF_RP + 2 * NR * 8;      // [NR] int: last key the row sees
+  // [NR][4] (unused), [8] value-scale maxima, [NR] O factors, [NR] float2 (row-sum factor, exp-argument shift)
+  static constexpr int OFF_RED = OFF_LIM + NR * 4;
+  static constexpr int OFF_SB = (OFF_RED + (NR * 4 + 8 + NR + 2 * NR) * 4 + 15) / 16 * 16;  // [NR][128] f32 scores
+  static constexpr int OFF_BAR = OFF_SB + NR * 128 * 4;
+  static constexpr int NBAR = 40;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_TMEM + 16;
   static_assert(BYTES <= 232448, "dynamic shared memory above the 227 KB a CTA may hold");
@@ -115,18 +125,18 @@ struct DecSmem {
 enum {
   D_RAW_FULL = 0,    // [RS <= 4] a raw stage landed
   D_RAW_EMPTY = 4,   // [RS] key and value warps are done with it (8 arrivals)
-  D_Q_FULL = 8,      // Q^T is in shared memory (4 softmax warps)
+  D_Q_FULL = 8,      // Q^T is in shared memory (every softmax warp)
   D_AK_FULL = 9,     // [2] key operand in TMEM (4 key warps)
   D_AK_FREE = 11,    // [2] its QK MMAs completed (commit)
-  D_KP_FULL = 13,    // [2] the tile's scales and zero-point biases are in shared memory (4 key warps)
-  D_KP_FREE = 15,    // [2] the softmax and the value warps read them (8 arrivals)
-  D_AV_FULL = 17,    // [2] value operand slot (64 keys) in TMEM (4 value warps)
-  D_AV_FREE = 19,    // [2] its PV MMAs completed (commit)
-  D_S_FULL = 21,     // [2] S^T of the tile is in TMEM (commit)
-  D_S_FREE = 23,     // [2] the softmax read it (4 softmax warps)
-  D_P_FULL = 25,     // [2] P^T of the tile is in shared memory (4 softmax warps)
-  D_PV_DONE = 27,    // the tile's PV MMAs completed (commit, one phase per tile)
-  D_FINAL = 28,      // every MMA issued has completed (before TMEM is released)
+  D_KP_FULL = 13,    // [RS] the stage's scales and zero-point biases are in shared memory (4 key warps)
+  D_KP_FREE = 17,    // [RS] the softmax and the value warps read them
+  D_AV_FULL = 21,    // [2] value operand slot (64 keys) in TMEM (4 value warps)
+  D_AV_FREE = 23,    // [2] its PV MMAs completed (commit)
+  D_S_FULL = 25,     // [2] S^T of the tile is in TMEM (commit)
+  D_S_FREE = 27,     // [2] the softmax read it (every softmax warp)
+  D_P_FULL = 29,     // [2] P^T of the tile is in shared memory (every softmax warp)
+  D_PV_DONE = 31,    // [2] PV(j) completed: barrier j & 1, one phase per two tiles (commit)
+  D_FINAL = 33,      // every MMA issued has completed (before TMEM is released)
 };
 
 // fp16 pair -> exact (nibble - zero point) of two keys a, b: the low-nibble form (1024 + u) minus (1024 + zp), the
@@ -140,8 +150,7 @@ __device__ __forceinline__ uint32_t nib_hi(uint32_t x, uint32_t hi_bias) {
 
 template <int NR>
 __device__ __forceinline__ void tmem_ld_rows(uint32_t taddr, float (&v)[NR]) {
-  if constexpr (NR == 32) tmem_ld32(taddr, v);
-  else tmem_ld16(taddr, v);
+  tmem_ld_cols<NR>(taddr, v);
 }
 template <int NR>
 __device__ __forceinline__ void tmem_st_rows(uint32_t taddr, const float (&v)[NR]) {
@@ -161,9 +170,8 @@ __host__ __device__ __forceinline__ int qk_k_of_channel(int c) {
 
 // ---------------------------------------------------------------------------------------------------- K0q
 // One warp per (query token, query head): the row as K1 reads it (Q_REC bytes): 256 fp16 in the k order of the QK
-// operand, scaled by a power of two (|q| < 2^14), odd int4 channels x 1/16; then fp32 row scale A (softmax_scale /
-// head x log2 e x 2^-exponent), bias B = A Q.bias (1024 per int4 operand element, 1152 per k8v4 one) and C =
-// A sum(q). Written once per call; every split of the row's KV head reads it.
+// operand, scaled by a power of two (|q| < 2^14); then the fp32 row scale A (softmax_scale / head x log2 e x
+// 2^-exponent) and three zero words. Written once per call; every split of the row's KV head reads it.
 template <int FMT, int DT>
 __global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_t q_st, int64_t q_sh, int64_t T,
                                                            int nq, int nkv, const uint32_t* sign_bits, int q_rotated,
@@ -195,36 +203,17 @@ __global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_
     frexpf(am, &ex);  // am < 2^ex
     ex = 14 - ex;     // am * 2^ex in [2^13, 2^14)
   }
-  float cq = 0.f, qs = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int c = lane * 8 + i;
-    const __half h = __float2half_rn(ldexpf(x[i], ex));
-    const float hv = __half2float(h);
-    qs += hv;
-    if constexpr (FMT == FMT_INT4) {
-      const bool odd = c & 1;
-      cq += odd ? 64.f * hv : 1024.f * hv;
-      qrow[qk_k_of_channel<FMT>(c)] = odd ? __float2half_rn(hv * 0.0625f) : h;
-    } else {
-      cq += 1152.f * hv;
-      qrow[qk_k_of_channel<FMT>(c)] = h;
-    }
-  }
-  cq = warp_sum(cq);
-  qs = warp_sum(qs);
+  for (int i = 0; i < 8; ++i) qrow[qk_k_of_channel<FMT>(lane * 8 + i)] = __float2half_rn(ldexpf(x[i], ex));
   if (lane == 0) {
     float* rc = reinterpret_cast<float*>(rec + 2 * DEC_HS);
-    const float a = ldexpf(qk_scale, -ex);
-    rc[0] = a;
-    rc[1] = a * cq;
-    rc[2] = a * qs;
-    rc[3] = 0.f;
+    rc[0] = ldexpf(qk_scale, -ex);
+    rc[1] = rc[2] = rc[3] = 0.f;
   }
 }
 
 // ---------------------------------------------------------------------------------------------------- K1
-template <int FMT, int DT, int NR>
+template <int FMT, int DT, int NR, int RL>
 __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
   using SM = DecSmem<FMT, NR>;
   using CL = Cell<FMT>;
@@ -261,20 +250,21 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
     for (int s = 0; s < RS; ++s) {
       mbar_init(&bars[D_RAW_FULL + s], 1);
       mbar_init(&bars[D_RAW_EMPTY + s], 8);
+      mbar_init(&bars[D_KP_FULL + s], 4);
+      mbar_init(&bars[D_KP_FREE + s], 4 + 4 * SMX_HALVES);
     }
-    mbar_init(&bars[D_Q_FULL], 4);
+    mbar_init(&bars[D_Q_FULL], 4 * SMX_HALVES);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars[D_AK_FULL + b], 4);
       mbar_init(&bars[D_AK_FREE + b], 1);
-      mbar_init(&bars[D_KP_FULL + b], 4);
-      mbar_init(&bars[D_KP_FREE + b], 8);
       mbar_init(&bars[D_AV_FULL + b], 4);
       mbar_init(&bars[D_AV_FREE + b], 1);
       mbar_init(&bars[D_S_FULL + b], 1);
-      mbar_init(&bars[D_S_FREE + b], 4);
-      mbar_init(&bars[D_P_FULL + b], 4);
+      mbar_init(&bars[D_S_FREE + b], 4 * SMX_HALVES);
+      mbar_init(&bars[D_P_FULL + b], 4 * SMX_HALVES);
     }
     mbar_init(&bars[D_PV_DONE], 1);
+    mbar_init(&bars[D_PV_DONE + 1], 1);
     mbar_init(&bars[D_FINAL], 1);
     fence_mbar_init();
   }
@@ -290,38 +280,47 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
-    if (lane == 0) {
-      const int32_t* btab = p.block_table + static_cast<int64_t>(seq) * p.bt_stride;
-      const uint8_t* head_base = p.cache + static_cast<int64_t>(kvh) * p.head_stride;
-      int i = 0;
-      for (; i < ntl; ++i) {
-        const int stage = i % RS;
-        if (i >= RS && !mbar_wait_bounded(&bars[D_RAW_EMPTY + stage], ((i / RS) - 1) & 1)) break;
-        const int tb = (tile0 + i) * DEC_TILE;
-        const int groups = (min(tb + DEC_TILE, n) - tb + 15) >> 4;
-        mbar_arrive_expect_tx(&bars[D_RAW_FULL + stage], static_cast<uint32_t>(groups * 16 * CELL));
-        uint8_t* dst = smem + SM::OFF_RAW + stage * SM::RAW;
-        for (int gi = 0; gi < groups;) {
-          const int tok = tb + gi * 16;
-          const int bi = tok / p.block_size;
-          const int in_blk = tok - bi * p.block_size;
-          const int blk = __ldg(btab + bi);
-          const int run = min(groups - gi, (p.block_size - in_blk) >> 4);
-          bulk_g2s(dst + gi * 16 * CELL,
-                   head_base + static_cast<int64_t>(blk) * p.block_stride + static_cast<int64_t>(in_blk) * CELL,
-                   static_cast<uint32_t>(run * 16 * CELL), &bars[D_RAW_FULL + stage]);
-          gi += run;
-        }
+    // Lane j copies 16-token group j of each tile (block_size % 16 == 0, so a group never crosses a block); its
+    // block-table entry is loaded one tile ahead, so the eight lookups of a tile are in flight together.
+    const int32_t* btab = p.block_table + static_cast<int64_t>(seq) * p.bt_stride;
+    const uint8_t* head_base = p.cache + static_cast<int64_t>(kvh) * p.head_stride;
+    auto block_of = [&](int i) {
+      const int tok = (tile0 + i) * DEC_TILE + 16 * lane;
+      return (lane < DEC_TILE / 16 && i < ntl && tok < n) ? __ldg(btab + tok / p.block_size) : -1;
+    };
+    int next_blk = block_of(0);
+    int i = 0;
+    for (; i < ntl; ++i) {
+      const int stage = i % RS;
+      if (i >= RS && __any_sync(0xffffffffu, !mbar_wait_bounded(&bars[D_RAW_EMPTY + stage], ((i / RS) - 1) & 1)))
+        break;
+      const int blk = next_blk;
+      next_blk = block_of(i + 1);
+      const int tb = (tile0 + i) * DEC_TILE;
+      const int groups = (min(tb + DEC_TILE, n) - tb + 15) >> 4;
+      if (lane == 0) mbar_arrive_expect_tx(&bars[D_RAW_FULL + stage], static_cast<uint32_t>(groups * 16 * CELL));
+      __syncwarp();
+      if (lane < groups) {
+        const int tok = tb + 16 * lane;
+        const int in_blk = tok - (tok / p.block_size) * p.block_size;
+        bulk_g2s(smem + SM::OFF_RAW + stage * SM::RAW + lane * 16 * CELL,
+                 head_base + static_cast<int64_t>(blk) * p.block_stride + static_cast<int64_t>(in_blk) * CELL,
+                 static_cast<uint32_t>(16 * CELL), &bars[D_RAW_FULL + stage]);
       }
-      // the copies in flight land before the CTA's shared memory can go away
+    }
+    // the copies in flight land before the CTA's shared memory can go away
+    if (lane == 0)
       for (int k = max(0, i - RS); k < i; ++k)
         mbar_wait_bounded(&bars[D_RAW_FULL + k % RS], (k / RS) & 1, 100000000ull);
-    }
   } else if (warp == W_MMA) {
     // ------------------------------------------------------------------ MMA issuer
     // The whole warp waits (convergent, so descriptors and TMEM addresses are warp-uniform); one elected lane issues.
     constexpr uint32_t ID = f16_idesc(128, NR, false);
-    const uint32_t q_base = smem_u32(smem + SM::OFF_Q), p_base = smem_u32(smem + SM::OFF_P);
+    // Every B operand descriptor is the base descriptor of its buffer plus a compile-time start-address offset (the
+    // 14-bit start field holds address / 16 and every shared-memory address here is below 256 KB, so the add
+    // never carries out of it): one integer add per MMA.
+    const uint64_t q_desc = sw128_desc(smem_u32(smem + SM::OFF_Q), 16, 1024);
+    const uint64_t p_desc = sw128_desc(smem_u32(smem + SM::OFF_P), 16, 1024);
     auto wait_all = [&](uint64_t* bar, uint32_t parity) {
       const bool ok = mbar_wait_spin(bar, parity);
       failed |= __any_sync(0xffffffffu, !ok);
@@ -330,8 +329,10 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
     auto issue_pv = [&](int j) {
       const int bj = j & 1;
       wait_all(&bars[D_P_FULL + bj], (j >> 1) & 1);
-#pragma unroll 1
-      for (int h = 0; h < 2 && !failed; ++h) {
+      const uint64_t pd = p_desc + static_cast<uint64_t>((2 * bj * SM::ATOM) >> 4);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (failed) break;
         wait_all(&bars[D_AV_FULL + h], j & 1);
         if (failed) break;
         tc_fence_after();
@@ -340,14 +341,14 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
           for (int c = 0; c < 2; ++c)
 #pragma unroll
             for (int s = 0; s < 4; ++s)
-              umma_f16_ts(tmem + TM_O + NR * c, tmem + TM_AV + 64 * h + 32 * c + 8 * s,
-                          sw128_desc(p_base + (2 * bj + h) * SM::ATOM + 32 * s, 16, 1024), ID,
-                          (j | h | s) ? 1u : 0u);
+              umma_f16_ts(tmem + (TM_O + NR * c), tmem + (TM_AV + 64 * h + 32 * c + 8 * s),
+                          pd + static_cast<uint64_t>((h * SM::ATOM + 32 * s) >> 4), ID,
+                          (h | s) ? 1u : static_cast<uint32_t>(j));
           umma_commit(&bars[D_AV_FREE + h]);
         }
         __syncwarp();
       }
-      if (elect_one()) umma_commit(&bars[D_PV_DONE]);
+      if (elect_one()) umma_commit(&bars[D_PV_DONE + bj]);
       __syncwarp();
     };
     wait_all(&bars[D_Q_FULL], 0);
@@ -357,12 +358,12 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
       if (i >= 2) wait_all(&bars[D_S_FREE + b], ((i - 2) >> 1) & 1);
       if (failed) break;
       tc_fence_after();
-      const uint32_t ak = tmem + (b ? TM_AK1 : TM_AK0);
+      const uint32_t ak = tmem + (b ? TM_AK1 : TM_AK0), sd = tmem + TM_S + NR * b;
       if (elect_one()) {
 #pragma unroll
         for (int s = 0; s < 16; ++s)
-          umma_f16_ts(tmem + TM_S + NR * b, ak + 8 * s,
-                      sw128_desc(q_base + (s >> 2) * SM::ATOM + (s & 3) * 32, 16, 1024), ID, s ? 1u : 0u);
+          umma_f16_ts(sd, ak + 8 * s, q_desc + static_cast<uint64_t>(((s >> 2) * SM::ATOM + (s & 3) * 32) >> 4), ID,
+                      s ? 1u : 0u);
         umma_commit(&bars[D_AK_FREE + b]);
         umma_commit(&bars[D_S_FULL + b]);
       }
@@ -381,11 +382,9 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
     uint32_t* zb = reinterpret_cast<uint32_t*>(smem + SM::OFF_ZB);
     for (int i = 0; i < ntl; ++i) {
       const int stage = i % RS, b = i & 1;
-      bool ok = mbar_wait_bounded(&bars[D_RAW_FULL + stage], (i / RS) & 1);
-      if (i >= 2) {
-        ok = ok && mbar_wait_bounded(&bars[D_AK_FREE + b], ((i - 2) >> 1) & 1);
-        ok = ok && mbar_wait_bounded(&bars[D_KP_FREE + b], ((i - 2) >> 1) & 1);
-      }
+      bool ok = mbar_wait_spin(&bars[D_RAW_FULL + stage], (i / RS) & 1);
+      if (i >= 2) ok = ok && mbar_wait_spin(&bars[D_AK_FREE + b], ((i - 2) >> 1) & 1);
+      if (i >= RS) ok = ok && mbar_wait_spin(&bars[D_KP_FREE + stage], ((i / RS) - 1) & 1);
       if (__any_sync(0xffffffffu, !ok)) {
         failed = true;
         break;
@@ -402,16 +401,19 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
       } else {
         ks = __uint_as_float(kw);
       }
-      kp[b * 128 + kl] = make_float4(ks, kz, valid ? __uint_as_float(vw & 0xFFFFFFF0u) : 0.f, 0.f);
+      kp[stage * 128 + kl] = make_float4(ks, kz, valid ? __uint_as_float(vw & 0xFFFFFFF0u) : 0.f, 0.f);
       // value zero-point operand biases of the key pair (a even, a + 1): key a stores {1024 + zp_a, 1024 + zp_b},
       // key a + 1 stores {-(64 + zp_a), -(64 + zp_b)} (fp16 pairs, low half = key a)
       {
         const uint32_t vz = vw & 0xFu;
         const uint32_t lo16 = 0x6400u | vz, hi16 = 0xD400u | (vz << 4);
         const uint32_t other = __shfl_xor_sync(0xffffffffu, (lane & 1) ? lo16 : hi16, 1);
-        zb[b * 128 + kl] = (lane & 1) ? (other | (hi16 << 16)) : (lo16 | (other << 16));
+        zb[stage * 128 + kl] = (lane & 1) ? (other | (hi16 << 16)) : (lo16 | (other << 16));
       }
       const uint32_t dst = tmem + (b ? TM_AK1 : TM_AK0) + lane_off;
+      // the key's zero point as the fp16 pair biases of nib_lo / nib_hi (int4; unused for k8v4)
+      const uint32_t kz16 = kw & 0xFu;
+      const uint32_t klo = (0x6400u | kz16) * 0x00010001u, khi = (0xD400u | (kz16 << 4)) * 0x00010001u;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {  // 32 TMEM columns (64 channels) per store
         uint32_t a[32];
@@ -423,10 +425,10 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
             for (int e = 0; e < 2; ++e) {
               const uint32_t w = e ? w2.y : w2.x, w8 = w >> 8;
               const int j = 8 * k + 4 * e;
-              a[j + 0] = lop3_and_or(w, 0x000F000Fu, 0x64006400u);
-              a[j + 1] = lop3_and_or(w, 0x00F000F0u, 0x64006400u);
-              a[j + 2] = lop3_and_or(w8, 0x000F000Fu, 0x64006400u);
-              a[j + 3] = lop3_and_or(w8, 0x00F000F0u, 0x64006400u);
+              a[j + 0] = nib_lo(w, klo);   // channels 8 w' + {0, 4}: u - zp, exact
+              a[j + 1] = nib_hi(w, khi);   // {1, 5}
+              a[j + 2] = nib_lo(w8, klo);  // {2, 6}
+              a[j + 3] = nib_hi(w8, khi);  // {3, 7}
             }
           }
         } else {
@@ -437,8 +439,9 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
             for (int e = 0; e < 2; ++e) {
               const uint32_t x = (e ? w2.y : w2.x) ^ 0x80808080u;
               const int j = 4 * k + 2 * e;
-              a[j] = prmt(x, 0x64646464u, 0x4140u);      // {1152 + c0, 1152 + c1}
-              a[j + 1] = prmt(x, 0x64646464u, 0x4342u);  // {1152 + c2, 1152 + c3}
+              // {1152 + c0, 1152 + c1} - 1152: the int8 codes, exact
+              a[j] = hsub2_u32(prmt(x, 0x64646464u, 0x4140u), 0x64806480u);
+              a[j + 1] = hsub2_u32(prmt(x, 0x64646464u, 0x4342u), 0x64806480u);
             }
           }
         }
@@ -449,7 +452,7 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&bars[D_AK_FULL + b]);
-        mbar_arrive(&bars[D_KP_FULL + b]);
+        mbar_arrive(&bars[D_KP_FULL + stage]);
         mbar_arrive(&bars[D_RAW_EMPTY + stage]);
       }
     }
@@ -462,8 +465,8 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
     const uint32_t* zb = reinterpret_cast<const uint32_t*>(smem + SM::OFF_ZB);
     for (int i = 0; i < ntl && !failed; ++i) {
       const int stage = i % RS, b = i & 1;
-      bool ok = mbar_wait_bounded(&bars[D_RAW_FULL + stage], (i / RS) & 1);
-      ok = ok && mbar_wait_bounded(&bars[D_KP_FULL + b], (i >> 1) & 1);
+      bool ok = mbar_wait_spin(&bars[D_RAW_FULL + stage], (i / RS) & 1);
+      ok = ok && mbar_wait_spin(&bars[D_KP_FULL + stage], (i / RS) & 1);
       if (__any_sync(0xffffffffu, !ok)) {
         failed = true;
         break;
@@ -471,7 +474,7 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
       const uint8_t* raw = smem + SM::OFF_RAW + stage * SM::RAW + CL::V + 4 * wv;
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
-        if (i >= 1 && __any_sync(0xffffffffu, !mbar_wait_bounded(&bars[D_AV_FREE + h], (i - 1) & 1))) {
+        if (i >= 1 && __any_sync(0xffffffffu, !mbar_wait_spin(&bars[D_AV_FREE + h], (i - 1) & 1))) {
           failed = true;
           break;
         }
@@ -485,7 +488,7 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
             uint32_t w[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const uint32_t*>(raw + (key0 + j) * CELL);
-            const uint4 bz = *reinterpret_cast<const uint4*>(zb + b * 128 + key0);
+            const uint4 bz = *reinterpret_cast<const uint4*>(zb + stage * 128 + key0);
 #pragma unroll
             for (int f = 0; f < 2; ++f) {
               const uint32_t lo_b = f ? bz.z : bz.x, hi_b = f ? bz.w : bz.y;
@@ -517,21 +520,27 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
       if (failed) break;
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&bars[D_KP_FREE + b]);
+        mbar_arrive(&bars[D_KP_FREE + stage]);
         mbar_arrive(&bars[D_RAW_EMPTY + stage]);
       }
     }
   } else {
     // ------------------------------------------------------------------ softmax (thread = key = TMEM lane)
+    // SMX_HALVES warps per lane quarter, each taking RL / SMX_HALVES of the rows (RL a multiple of 8 covering the
+    // launch's largest row count), with compile-time row indices and no per-row branch. Row states live in rp[].y: the row maximum
+    // (log2 units), 0 before the first tile (whose rescale path always runs, since no value range is known yet), and
+    // +inf for a row past the sequence's rows or one with no key in this split (keys visible to a row are a prefix of
+    // the context, so such a row never gets one later): its scores are -inf and its probabilities 0. The scores are
+    // kept as exp arguments (score minus the row maximum), so the exponentials read no shared memory.
     const int q = warp & 3, kl = 32 * q + lane, stid = tid - 32 * W_SMX;
+    const int hf = (warp - W_SMX) >> 2;
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
-    // row constants and the running row maxima, double-buffered: a rescale writes the other buffer, then every
-    // softmax thread switches to it after one barrier
-    float4* rp = reinterpret_cast<float4*>(smem + SM::OFF_RP);
+    float2* rp = reinterpret_cast<float2*>(smem + SM::OFF_RP);  // [2][NR]: row scale, row maximum
     int* lim = reinterpret_cast<int*>(smem + SM::OFF_LIM);
-    float* red = reinterpret_cast<float*>(smem + SM::OFF_RED);  // [NR][4]
-    float* red_vs = red + NR * 4;                               // [4]
-    float* frow = red_vs + 4;                                   // [NR]
+    float* red_vs = reinterpret_cast<float*>(smem + SM::OFF_RED) + NR * 4;  // [softmax warps]
+    float* frow = red_vs + 8;                                                // [NR]
+    float2* adj = reinterpret_cast<float2*>(frow + NR);                      // [NR]
+    float* sb = reinterpret_cast<float*>(smem + SM::OFF_SB);                 // [NR][128]
     const float4* kp = reinterpret_cast<const float4*>(smem + SM::OFF_KP);
     const int vis_base = n - qlen + p.tokens_after;  // last key query token 0 sees (before clamping to n - 1)
     const int causal_from = min(n, vis_base + 1);
@@ -540,194 +549,232 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     {
       const uint8_t* qsrc = p.qrec + ((static_cast<int64_t>(kvh) * p.num_tokens + q0) * p.group) * Q_REC;
-      for (int idx = stid; idx < NR * 32; idx += 128) {
+      for (int idx = stid; idx < NR * 32; idx += SMX_THREADS) {
         const int r = idx >> 5, ch = idx & 31;
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (r < rows) v = *reinterpret_cast<const uint4*>(qsrc + r * Q_REC + 16 * ch);
         *reinterpret_cast<uint4*>(smem + SM::OFF_Q + (ch >> 3) * SM::ATOM + sw128_off(r, ch & 7)) = v;
       }
-      for (int r = stid; r < NR; r += 128) {
-        float4 c = make_float4(0.f, 0.f, 0.f, -INFINITY);
-        if (r < rows) {
-          const float* rc = reinterpret_cast<const float*>(qsrc + r * Q_REC + 2 * DEC_HS);
-          c = make_float4(rc[0], rc[1], rc[2], -INFINITY);
-        }
+      for (int r = stid; r < NR; r += SMX_THREADS) {
+        float2 c = make_float2(0.f, INFINITY);
+        if (r < rows) c = make_float2(*reinterpret_cast<const float*>(qsrc + r * Q_REC + 2 * DEC_HS), 0.f);
         rp[r] = c;
         rp[NR + r] = c;
         lim[r] = r < rows ? min(n - 1, vis_base + r / p.group) : -1;
+        frow[r] = 1.f;
+      }
+      // P^T rows RL .. NR - 1 are read by the MMAs but never written by the loops below: zero them once
+      if constexpr (RL < NR) {
+        for (int idx = stid; idx < 4 * (NR - RL) * 8; idx += SMX_THREADS) {
+          const int ab = idx / ((NR - RL) * 8), rem = idx % ((NR - RL) * 8), r = RL + rem / 8, ch = rem % 8;
+          *reinterpret_cast<uint4*>(smem + SM::OFF_P + ab * SM::ATOM + sw128_off(r, ch)) = make_uint4(0u, 0u, 0u, 0u);
+        }
       }
     }
     fence_async_smem();
-    named_bar_or(BAR_SMX, 128, false);  // row constants visible to every softmax thread
+    named_bar_or(BAR_SMX, SMX_THREADS, false);  // row constants visible to every softmax thread
     if (lane == 0) mbar_arrive(&bars[D_Q_FULL]);
 
-    float l[NR];
+    auto role = [&](auto half) {
+      constexpr int RH = RL / SMX_HALVES, R0 = decltype(half)::value * RH;  // this warp's rows [R0, R0 + RH)
+      float l[RH];
 #pragma unroll
-    for (int r = 0; r < NR; ++r) l[r] = 0.f;
-    int mb = 0;           // current row-maximum buffer
-    int e_run = -1000;    // running power-of-two range of the value scales: every one < 2^e_run
-    float pv_mul = 0.f;   // 2^-e_run
-    float v_limit = 0.f;  // 2^e_run
-    // P^T store position of this thread's key: atom kl / 64, 16-byte chunk (kl % 64) / 8 (swizzled by row), column
-    const int patom = (kl >> 6) * SM::ATOM + (kl & 7) * 2, pchunk = (kl & 63) >> 3;
-    for (int i = 0; i < ntl; ++i) {
-      const int b = i & 1;
-      bool ok = mbar_wait_bounded(&bars[D_S_FULL + b], (i >> 1) & 1);
-      ok = ok && mbar_wait_bounded(&bars[D_KP_FULL + b], (i >> 1) & 1);
-      failed |= __any_sync(0xffffffffu, !ok);
-      float s[NR];
-      if (!failed) {
-        tc_fence_after();
-        tmem_ld_rows<NR>(tmem + TM_S + NR * b + lane_off, s);
-      } else {
+      for (int r = 0; r < RH; ++r) l[r] = 0.f;
+      int mb = 0;           // current row-state buffer
+      int e_run = -1000;    // running power-of-two range of the value scales: every one < 2^e_run
+      float pv_mul = 0.f;   // 2^-e_run
+      float v_limit = 0.f;  // 2^e_run
+      // P^T store position of this thread's key: atom kl / 64, chunk (kl % 64) / 8 (swizzled by row), column
+      const int patom = (kl >> 6) * SM::ATOM + (kl & 7) * 2, pchunk = (kl & 63) >> 3;
+      for (int i = 0; i < ntl; ++i) {
+        const int b = i & 1;
+        const int stage = i % RS;
+        bool ok = mbar_wait_bounded(&bars[D_S_FULL + b], (i >> 1) & 1);
+        ok = ok && mbar_wait_bounded(&bars[D_KP_FULL + stage], (i / RS) & 1);
+        failed |= __any_sync(0xffffffffu, !ok);
+        float s[RH];
+        if (!failed) {
+          tc_fence_after();
+          tmem_ld_cols<RH>(tmem + TM_S + NR * b + R0 + lane_off, s);
+        } else {
 #pragma unroll
-        for (int r = 0; r < NR; ++r) s[r] = 0.f;
-      }
-      tc_fence_before();
-      const float4 kv = kp[b * 128 + kl];  // key scale, key zero point, value scale (0 past the context)
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bars[D_S_FREE + b]);
-        mbar_arrive(&bars[D_KP_FREE + b]);
-      }
-      const int tok = (tile0 + i) * DEC_TILE + kl;
-      const bool need_mask = (tile0 + i) * DEC_TILE + DEC_TILE > causal_from;
-      float emax = -INFINITY;
-#pragma unroll
-      for (int r = 0; r < NR; ++r) {
-        if (r < rows) {
-          const float4 c = rp[mb * NR + r];
-          float lg = fmaf(s[r], c.x, -fmaf(kv.y, c.z, c.y)) * kv.x;
-          if (need_mask && tok > lim[r]) lg = -INFINITY;  // past the row's last key or the context
-          s[r] = lg;
-          emax = fmaxf(emax, lg - c.w);
+          for (int r = 0; r < RH; ++r) s[r] = 0.f;
         }
-      }
-      const bool grow = emax > RESCALE_SLACK || kv.z >= v_limit;
-      bool rescale = false;
-      // every softmax thread takes the same barriers: a wait that ran out is folded into the vote
-      if (named_bar_or(BAR_SMX, 128, grow || failed)) {
-        if (named_bar_or(BAR_SMX, 128, failed)) {
-          failed = true;
-          break;
+        tc_fence_before();
+        const float4 kv = kp[stage * 128 + kl];  // key scale, key zero point, value scale (0 past the context)
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bars[D_S_FREE + b]);
+          mbar_arrive(&bars[D_KP_FREE + stage]);
         }
-        // slow path: exact tile maxima and value range, new maxima, rescale factors of O
+        const int tok = (tile0 + i) * DEC_TILE + kl;
+        // exp arguments: score (log2 units) minus the row maximum; emax: the largest one
+        float emax = -INFINITY;
+        auto logits = [&](auto masked) {
 #pragma unroll
-        for (int r = 0; r < NR; ++r) {
-          if (r < rows) {
-            const float mx = warp_max(s[r]);
-            if (lane == 0) red[4 * r + q] = mx;
+          for (int r = 0; r < RH; ++r) {
+            if (r % 4 == 0 && r > 0) asm volatile("" ::: "memory");  // 4 rows' constants in flight at a time
+            const float2 c = rp[mb * NR + R0 + r];  // row scale, row maximum
+            float e = fmaf(s[r] * kv.x, c.x, -c.y);
+            if constexpr (decltype(masked)::value) {
+              if (tok > lim[R0 + r]) e = -INFINITY;  // past the row's last key or the context
+            }
+            s[r] = e;
+            emax = fmaxf(emax, e);
           }
-        }
-        {
-          const float vm = warp_max(kv.z);
-          if (lane == 0) red_vs[q] = vm;
-        }
-        named_bar_or(BAR_SMX, 128, false);
-        const float vmax = fmaxf(fmaxf(red_vs[0], red_vs[1]), fmaxf(red_vs[2], red_vs[3]));
-        int e_tile = -1000;
-        if (vmax > 0.f) frexpf(vmax, &e_tile);  // vmax < 2^e_tile
-        const int e_new = max(e_run, e_tile);
-        const float o_range = e_run == -1000 ? 0.f : ldexpf(1.f, e_run - e_new);
-        e_run = e_new;
-        pv_mul = e_new == -1000 ? 0.f : ldexpf(1.f, -e_new);
-        v_limit = e_new == -1000 ? 0.f : ldexpf(1.f, e_new);
+        };
+        if ((tile0 + i) * DEC_TILE + DEC_TILE > causal_from) logits(std::true_type{});
+        else logits(std::false_type{});
+        const bool grow = emax > RESCALE_SLACK || kv.z >= v_limit;
+        bool rescale = false;
+        // every softmax thread takes the same barriers: a wait that ran out is folded into the vote
+        if (named_bar_or(BAR_SMX, SMX_THREADS, grow || failed)) {
+          if (named_bar_or(BAR_SMX, SMX_THREADS, failed)) {
+            failed = true;
+            break;
+          }
+          // slow path: exact tile maxima and value range, new row states, rescale factors. The exp arguments go
+          // through shared memory, so that thread r can take row r's maximum over the 128 keys.
 #pragma unroll
-        for (int r = 0; r < NR; ++r) {
+          for (int r = 0; r < RH; ++r) sb[(R0 + r) * 128 + kl] = s[r];
+          {
+            const float vm = warp_max(kv.z);
+            if (lane == 0) red_vs[warp - W_SMX] = vm;
+          }
+          named_bar_or(BAR_SMX, SMX_THREADS, false);
+          float vmax = red_vs[0];
+#pragma unroll
+          for (int k = 1; k < 4 * SMX_HALVES; ++k) vmax = fmaxf(vmax, red_vs[k]);
+          // e_tile: vmax < 2^e_tile (value scales are normal, positive fp32: exponent field + 1 - bias)
+          const int e_tile = vmax > 0.f ? static_cast<int>((__float_as_uint(vmax) >> 23) & 0xFFu) - 126 : -1000;
+          const bool first = e_run == -1000;
+          const int e_new = max(e_run, e_tile);
+          const float o_range = first ? 0.f : exp2_int(max(e_run - e_new, -149));
+          e_run = e_new;
+          pv_mul = e_new == -1000 ? 0.f : exp2_int(-e_new);
+          v_limit = e_new == -1000 ? 0.f : exp2_int(e_new);
           float f = 1.f;
-          float4 c = rp[mb * NR + r];
-          if (r < rows) {
-            const float4 mv = *reinterpret_cast<const float4*>(red + 4 * r);
-            const float mt = fmaxf(fmaxf(mv.x, mv.y), fmaxf(mv.z, mv.w));
-            const float mn = (c.w == -INFINITY || mt > c.w + RESCALE_SLACK) ? mt : c.w;
-            const float alpha = mn == c.w ? 1.f : fast_exp2(c.w - mn);
-            c.w = mn;
-            l[r] *= alpha;
-            f = alpha * o_range;
-          }
-          rescale |= f != 1.f;
-          if (stid == 0) {
-            frow[r] = f;
+          if (stid < RL) {  // thread r: row r
+            const int r = stid;
+            float2 c = rp[mb * NR + r];
+            float2 ad = make_float2(1.f, 0.f);
+            if (c.y != INFINITY) {  // an open row of the sequence
+              float mx = -INFINITY;
+              const float4* row = reinterpret_cast<const float4*>(sb + r * 128);
+#pragma unroll 8
+              for (int k = 0; k < 32; ++k) {
+                const float4 v = row[(k + r) & 31];  // rotated start: threads read different banks
+                mx = fmaxf(mx, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+              }
+              const float mt = mx + c.y;  // the tile's largest score
+              float mn = c.y;
+              if (first) mn = mt == -INFINITY ? INFINITY : mt;  // no key in this split: the row is closed
+              else if (mt > c.y + RESCALE_SLACK) mn = mt;
+              if (mn != c.y) {
+                ad.x = first ? 0.f : fast_exp2(c.y - mn);
+                ad.y = c.y - mn;  // -inf for a row that closes
+                c.y = mn;
+              }
+              f = ad.x * o_range;
+            }
             rp[(mb ^ 1) * NR + r] = c;
+            frow[r] = f;
+            adj[r] = ad;
+          }
+          rescale = named_bar_or(BAR_SMX, SMX_THREADS, f != 1.f);  // new row states and factors visible
+#pragma unroll
+          for (int r = 0; r < RH; ++r) {  // the arguments come back from shared memory: no registers held across
+            const float2 ad = adj[R0 + r];
+            s[r] = sb[(R0 + r) * 128 + kl] + ad.y;
+            l[r] *= ad.x;
+          }
+          mb ^= 1;
+        }
+        // P^T buffer b is free once PV(i - 2) has completed; O may be rescaled once PV(i - 1) has. (PV(j) completes
+        // phase j / 2 of barrier j % 2, which cannot move on before this thread has stored P(j + 2).)
+        if (i >= 2) failed |= !mbar_wait_bounded(&bars[D_PV_DONE + b], ((i - 2) >> 1) & 1);
+        if (rescale && i >= 1) failed |= !mbar_wait_bounded(&bars[D_PV_DONE + (b ^ 1)], ((i - 1) >> 1) & 1);
+        tc_fence_after();
+        const float vsp = kv.z * pv_mul;
+        uint8_t* pb = smem + SM::OFF_P + 2 * b * SM::ATOM + patom;
+#pragma unroll
+        for (int r = 0; r < RH; ++r) {
+          constexpr int dummy = 0;
+          (void)dummy;
+          const int R = R0 + r;
+          const float pe = fast_exp2(s[r]);
+          l[r] += pe;
+          *reinterpret_cast<__half*>(pb + (R >> 3) * 1024 + (R & 7) * 128 + ((pchunk ^ (R & 7)) << 4)) =
+              __float2half_rn(pe * vsp);
+        }
+        if (rescale && i >= 1) {  // before PV(i), which waits for this tile's P
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            float o[RH];
+            tmem_ld_cols<RH>(tmem + TM_O + NR * c + R0 + lane_off, o);
+#pragma unroll
+            for (int r = 0; r < RH; ++r) o[r] *= frow[R0 + r];
+            tmem_st_cols<RH>(tmem + TM_O + NR * c + R0 + lane_off, o);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
           }
         }
-        named_bar_or(BAR_SMX, 128, false);  // exchange read; new maxima and factors visible
-        mb ^= 1;
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[D_P_FULL + b]);
       }
-      // the previous tile's PV has completed: P^T buffer b (read by PV(i - 2)) is free, and O may be rescaled
-      if (i >= 1) failed |= !mbar_wait_bounded(&bars[D_PV_DONE], (i - 1) & 1);
-      tc_fence_after();
-      const float vsp = kv.z * pv_mul;
-      uint8_t* pb = smem + SM::OFF_P + 2 * b * SM::ATOM + patom;
+      // ---- epilogue: row sums (thread r adds row r's 128 partial sums), normalised partial O (channel order
+      // undone) and its lse
+      if (named_bar_or(BAR_SMX, SMX_THREADS, failed)) return;
 #pragma unroll
-      for (int r = 0; r < NR; ++r) {
-        float pv = 0.f;
+      for (int r = 0; r < RH; ++r) sb[(R0 + r) * 128 + kl] = l[r];
+      named_bar_or(BAR_SMX, SMX_THREADS, false);
+      if (stid < NR) {
+        const int r = stid;
+        float inv = 0.f;
         if (r < rows) {
-          const float mr = rp[mb * NR + r].w;
-          const float pe = fast_exp2(s[r] - (mr == -INFINITY ? 0.f : mr));
-          l[r] += pe;
-          pv = pe * vsp;
+          float lt = 0.f;
+          const float4* row = reinterpret_cast<const float4*>(sb + r * 128);
+#pragma unroll 8
+          for (int k = 0; k < 32; ++k) {
+            const float4 v = row[(k + r) & 31];
+            lt += (v.x + v.y) + (v.z + v.w);
+          }
+          const float o_unit = e_run == -1000 ? 0.f : exp2_int(e_run);
+          inv = lt > 0.f ? o_unit / lt : 0.f;
+          const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
+          p.part_lse[(static_cast<int64_t>(tok) * p.nq + qh) * p.num_splits + split] =
+              lt > 0.f ? rp[mb * NR + r].y + log2f(lt) : -INFINITY;
         }
-        *reinterpret_cast<__half*>(pb + (r >> 3) * 1024 + (r & 7) * 128 + ((pchunk ^ (r & 7)) << 4)) =
-            __float2half_rn(pv);
+        frow[r] = inv;
       }
-      if (rescale && i >= 1) {  // before PV(i), which waits for this tile's P
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          float o[NR];
-          tmem_ld_rows<NR>(tmem + TM_O + NR * c + lane_off, o);
-#pragma unroll
-          for (int r = 0; r < NR; ++r) o[r] *= frow[r];
-          tmem_st_rows<NR>(tmem + TM_O + NR * c + lane_off, o);
-        }
-      }
-      fence_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[D_P_FULL + b]);
-    }
-    // ---- epilogue: row sums, normalised partial O (channel order undone) and its lse
-    if (!named_bar_or(BAR_SMX, 128, failed)) {
-#pragma unroll
-      for (int r = 0; r < NR; ++r) {
-        if (r < rows) {
-          const float lt = warp_sum(l[r]);
-          if (lane == 0) red[4 * r + q] = lt;
-        }
-      }
-      named_bar_or(BAR_SMX, 128, false);
-      const bool ok = mbar_wait_bounded(&bars[D_PV_DONE], (ntl - 1) & 1);
+      named_bar_or(BAR_SMX, SMX_THREADS, false);
+      const bool ok = mbar_wait_bounded(&bars[D_PV_DONE + ((ntl - 1) & 1)], ((ntl - 1) >> 1) & 1);
       tc_fence_after();
-      const float o_unit = e_run == -1000 ? 0.f : ldexpf(1.f, e_run);
       const int g = lane & 7, mm = lane >> 3;
+      const int64_t head_step = static_cast<int64_t>(p.num_splits) * DEC_HS;
+      const int64_t tok_step = (static_cast<int64_t>(p.nq) - p.group + 1) * head_step;
+      const int tok0 = q0 + R0 / p.group, hg0 = R0 % p.group;
 #pragma unroll 1
       for (int c = 0; c < 2 && ok; ++c) {
-        float o[NR];
-        tmem_ld_rows<NR>(tmem + TM_O + NR * c + lane_off, o);
-        const int ch = 64 * q + 8 * g + 4 * c + mm;
+        float o[RH];
+        tmem_ld_cols<RH>(tmem + TM_O + NR * c + R0 + lane_off, o);
+        float* dst = p.part_o + ((static_cast<int64_t>(tok0) * p.nq + kvh * p.group + hg0) * p.num_splits + split) *
+                                    DEC_HS + 64 * q + 8 * g + 4 * c + mm;
+        int hg = hg0;
 #pragma unroll
-        for (int r = 0; r < NR; ++r) {
-          if (r < rows) {
-            const float4 lv = *reinterpret_cast<const float4*>(red + 4 * r);
-            const float lt = (lv.x + lv.y) + (lv.z + lv.w);
-            const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
-            const int64_t prow = (static_cast<int64_t>(tok) * p.nq + qh) * p.num_splits + split;
-            p.part_o[prow * DEC_HS + ch] = lt > 0.f ? o[r] * (o_unit / lt) : 0.f;
-          }
+        for (int r = 0; r < RH; ++r) {
+          if (R0 + r < rows) *dst = o[r] * frow[R0 + r];
+          dst += (++hg == p.group) ? tok_step : head_step;  // next query head, or the next token's first head
+          if (hg == p.group) hg = 0;
         }
       }
-      if (stid == 0) {
-#pragma unroll
-        for (int r = 0; r < NR; ++r) {
-          if (r < rows) {
-            const float4 lv = *reinterpret_cast<const float4*>(red + 4 * r);
-            const float lt = (lv.x + lv.y) + (lv.z + lv.w);
-            const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
-            p.part_lse[(static_cast<int64_t>(tok) * p.nq + qh) * p.num_splits + split] =
-                lt > 0.f ? rp[mb * NR + r].w + log2f(lt) : -INFINITY;
-          }
-        }
-      }
+    };
+    if constexpr (SMX_HALVES == 1) {
+      role(std::integral_constant<int, 0>{});
+    } else {
+      if (hf == 0) role(std::integral_constant<int, 0>{});
+      else role(std::integral_constant<int, 1>{});
     }
   }
 
@@ -883,15 +930,16 @@ static int merge_dispatch(const MergeParams& mp, int dtype, int head_size, int64
   }
 }
 
-template <int FMT, int DT, int NR>
+template <int FMT, int DT, int RL>
 static int launch_decode_t(const DecodeParams& dp, int num_seqs, cudaStream_t st) {
+  constexpr int NR = RL <= 16 ? 16 : 32;  // the MMAs' N: a multiple of 16 at M 128
   using SM = DecSmem<FMT, NR>;
   static std::atomic<bool> configured[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
     cudaError_t e =
-        cudaFuncSetAttribute(decode_kernel<FMT, DT, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES);
+        cudaFuncSetAttribute(decode_kernel<FMT, DT, NR, RL>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES);
     if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode smem attribute: %s", cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
   }
@@ -907,14 +955,17 @@ static int launch_decode_t(const DecodeParams& dp, int num_seqs, cudaStream_t st
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<FMT, DT, NR>, dp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<FMT, DT, NR, RL>, dp);
   if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
   return QP_OK;
 }
 
 template <int FMT, int DT>
 static int launch_decode_nr(const DecodeParams& dp, int rows, int num_seqs, cudaStream_t st) {
-  return rows <= 16 ? launch_decode_t<FMT, DT, 16>(dp, num_seqs, st) : launch_decode_t<FMT, DT, 32>(dp, num_seqs, st);
+  if (rows <= 8) return launch_decode_t<FMT, DT, 8>(dp, num_seqs, st);
+  if (rows <= 16) return launch_decode_t<FMT, DT, 16>(dp, num_seqs, st);
+  if (rows <= 24) return launch_decode_t<FMT, DT, 24>(dp, num_seqs, st);
+  return launch_decode_t<FMT, DT, 32>(dp, num_seqs, st);
 }
 
 }  // namespace qp

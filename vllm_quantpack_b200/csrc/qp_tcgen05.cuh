@@ -154,18 +154,56 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[3
       : "memory");
 }
 
-// 32 lanes x 16 columns of fp32 from TMEM (this warp's lane quarter)
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+// Loads of 32 lanes x 8 / 16 columns into registers, and a wait that names those registers as read-write operands:
+// without them in the wait's operand list, the compiler may schedule a use of a destination register above the
+// wait, reading it before the load has landed.
+#define QP_TLD8(R, o, ADDR)                                                                                       \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"                           \
+               : "=r"(R[o]), "=r"(R[o + 1]), "=r"(R[o + 2]), "=r"(R[o + 3]), "=r"(R[o + 4]), "=r"(R[o + 5]),      \
+                 "=r"(R[o + 6]), "=r"(R[o + 7])                                                                   \
+               : "r"(ADDR))
+#define QP_TLD16(R, o, ADDR)                                                                                      \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "  \
+               "[%16];"                                                                                           \
+               : "=r"(R[o]), "=r"(R[o + 1]), "=r"(R[o + 2]), "=r"(R[o + 3]), "=r"(R[o + 4]), "=r"(R[o + 5]),      \
+                 "=r"(R[o + 6]), "=r"(R[o + 7]), "=r"(R[o + 8]), "=r"(R[o + 9]), "=r"(R[o + 10]), "=r"(R[o + 11]), \
+                 "=r"(R[o + 12]), "=r"(R[o + 13]), "=r"(R[o + 14]), "=r"(R[o + 15])                               \
+               : "r"(ADDR))
+#define QP_TLD4(R, o, ADDR)                                                                                       \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"                                       \
+               : "=r"(R[o]), "=r"(R[o + 1]), "=r"(R[o + 2]), "=r"(R[o + 3])                                       \
+               : "r"(ADDR))
+#define QP_TW4(R, o) "+r"(R[o]), "+r"(R[o + 1]), "+r"(R[o + 2]), "+r"(R[o + 3])
+#define QP_TW8(R, o) "+r"(R[o]), "+r"(R[o + 1]), "+r"(R[o + 2]), "+r"(R[o + 3]), "+r"(R[o + 4]), "+r"(R[o + 5]), \
+                     "+r"(R[o + 6]), "+r"(R[o + 7])
+// N (4, 8, 12, 16, 24 or 32) columns of fp32 from TMEM (this warp's lane quarter), waited for
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[N]) {
+  static_assert(N == 4 || N == 8 || N == 12 || N == 16 || N == 24 || N == 32, "4, 8, 12, 16, 24 or 32 columns");
+  uint32_t r[32];
+  if constexpr (N >= 16) QP_TLD16(r, 0, taddr);
+  if constexpr (N == 8 || N == 12) QP_TLD8(r, 0, taddr);
+  if constexpr (N == 4) QP_TLD4(r, 0, taddr);
+  if constexpr (N == 12) QP_TLD4(r, 8, taddr + 8);
+  if constexpr (N == 24) QP_TLD8(r, 16, taddr + 16);
+  if constexpr (N == 32) QP_TLD16(r, 16, taddr + 16);
+  if constexpr (N == 4) asm volatile("tcgen05.wait::ld.sync.aligned;" : QP_TW4(r, 0) : : "memory");
+  if constexpr (N == 12) asm volatile("tcgen05.wait::ld.sync.aligned;" : QP_TW8(r, 0), QP_TW4(r, 8) : : "memory");
+  if constexpr (N == 8) asm volatile("tcgen05.wait::ld.sync.aligned;" : QP_TW8(r, 0) : : "memory");
+  if constexpr (N == 16) asm volatile("tcgen05.wait::ld.sync.aligned;" : QP_TW8(r, 0), QP_TW8(r, 8) : : "memory");
+  if constexpr (N == 24)
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : QP_TW8(r, 0), QP_TW8(r, 8), QP_TW8(r, 16) : : "memory");
+  if constexpr (N == 32)
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : QP_TW8(r, 0), QP_TW8(r, 8), QP_TW8(r, 16), QP_TW8(r, 24) : :
+                 "memory");
 #pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < N; ++i) v[i] = __uint_as_float(r[i]);
 }
+#undef QP_TW8
+#undef QP_TW4
+#undef QP_TLD16
+#undef QP_TLD8
+#undef QP_TLD4
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
@@ -176,6 +214,17 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
       "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
       "r"(__float_as_uint(v[15]))
       : "memory");
+}
+// N (4, 8, 12, 16, 24 or 32) columns of fp32 into TMEM (this warp's lane quarter); the caller waits (wait::st)
+template <int N>
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const float (&v)[N]) {
+  static_assert(N % 4 == 0 && N <= 32, "a multiple of 4 columns, at most 32");
+#pragma unroll
+  for (int c = 0; c < N; c += 4)
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr + c),
+                 "r"(__float_as_uint(v[c])), "r"(__float_as_uint(v[c + 1])), "r"(__float_as_uint(v[c + 2])),
+                 "r"(__float_as_uint(v[c + 3]))
+                 : "memory");
 }
 // 16 lanes x 256 bits, two repetitions along the columns: thread i writes v[4r], v[4r + 1] to lane i / 4, columns
 // 8 r + 2 (i % 4) + {0, 1}, and v[4r + 2], v[4r + 3] to lane 8 + i / 4, the same columns (r = 0, 1); lanes counted
