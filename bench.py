@@ -1,24 +1,30 @@
 """Benchmark of the B200 quantized KV-cache attention (prints one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload c2a|c1|c2b|c3|c4]
+                    [--no-cpu] [--no-prefill]
 
-Metric: 262k-context int4-KV decode, query tokens per second of one attention-layer call, and the
-HBM bandwidth it reaches. A step is one attention call (split-KV decode + segment merge) over a resident paged cache
-of synthetic data (K, V ~ N(0, 1) with 2 % outlier channels x8, written by the B200 store; q ~ N(0, 1); seeds 0 / 1),
-with a random block table over a shuffled pool. Workloads:
-  c2a  int4, 1 request, context 262144, 4 query tokens (3 MTP drafts)     [default, the N=1 headline]
+Metric: 262k-context int4-KV decode, query tokens per second of one attention-layer call and the
+HBM bandwidth it reaches; prefill tokens per second and the tensor throughput it reaches. A step is one attention call
+over a resident paged cache of synthetic data (K, V ~ N(0, 1) with 2 % outlier channels x8, written by the B200
+store; q ~ N(0, 1); seeded), with a random block table over a shuffled pool. Workloads:
+  c2a  int4, 1 request, context 262144, 4 query tokens (3 MTP drafts)     [default, the headline]
   c1   int4, 1 request, context 131072, 2 query tokens
   c2b  int4, 32 requests x context 32768, 2 query tokens
   c4   k8v4, 1 request, context 262144, 4 query tokens
-  c3   int4 prefill: a 1024-query chunk over 229,376 cached tokens (+ its own 1024), causal in the chunk; metric
-       prefill tokens per second and the dense tensor throughput it reaches
-At N > 1 each rank serves its own request(s) of the workload (batch sharded by request, no collective: weak
-scaling); the line also carries `seq_parallel`: one request split by sequence range over the N ranks, each rank's
-partial (O, LSE) all-gathered over NCCL and merged (strong scaling of a single request).
+  c3   int4 prefill: a 1024-query chunk over 229,376 cached tokens (+ its own 1024), causal in the chunk
+The default c2a line also carries `prefill`: the c3 chunk measured the same way (its own roofline, e2e and clocks),
+and, next to it, the reference's own production prefill (its `prefill_sequence`, FlashAttention 2) timed on the same
+cache bytes when the reference is installed in baseline/_ref.
 
-The cache (>= 138 MB) is larger than L2 and L2 is flushed (256 MB written, then another 256 MB read so that the
-write-back of the dirty lines happens before the timed region) before every timed step; each step is timed
-on the device with CUDA events on the launching stream, max over ranks.
+At N > 1 (one process per GPU) the headline is ONE request split by sequence range over the N GPUs: rank r holds
+cached tokens [r ctx / N, (r + 1) ctx / N), attends every query token over its range, and the partial (O, LSE) are
+all-gathered over NCCL and folded (strong scaling). The side key `batch_sharded` has each GPU serve its own full
+request(s) with no collective (weak scaling). The prefill chunk is split the same way.
+
+The caches (>= 138 MB) are larger than L2 and L2 is flushed (256 MB written, then another 256 MB read so that the
+write-back of the dirty lines happens before the timed region) before every timed step; each step is timed on the
+device with CUDA events on the launching stream, max over ranks. Clocks are sampled while at least one second of
+back-to-back steps and then the timed steps run.
 
 `--impl reference` times the reference algorithm on the host cores instead: the CPU oracle (a restatement of the
 reference's fp64 attention-from-cache, tests/test_int4_kv.py:115-133) on a bounded sample of the workload.
@@ -175,6 +181,19 @@ def l2_flush(flush):
     flush[half:].view(torch.int64).sum()
 
 
+def sustain(torch, fn, seconds=1.0):
+    """Back-to-back steps for at least `seconds` (the clock sampler sees the GPU under this load, not idle)."""
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < seconds:
+        for _ in range(16):
+            fn()
+        n += 16
+        torch.cuda.synchronize()
+    return n
+
+
 def timed_steps(torch, fn, steps, warmup, flush):
     """Run `warmup` untimed steps, then `steps` steps each timed by CUDA events (L2 flushed before each)."""
     for _ in range(warmup):
@@ -257,123 +276,257 @@ def run_reference(args, w, rank, world):
 # ---------------------------------------------------------------------------------------------------- GPU arm
 
 
-def run_prefill(args, w, rank, world, local_rank):
-    """Chunk prefill (c3): one request, qlen queries over the cached context, on the tensor cores."""
-    import torch
-    from vllm_quantpack_b200 import _lib
-    from vllm_quantpack_b200.attention import ops
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    R = build_request(torch, ops, w, device, 1, seed=rank)
+def tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def max_over_ranks(torch, dist, world, device, values):
+    if world == 1:
+        return values
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def reference_fa2_prefill(torch, ops, R, w, flush, args):
+    """The reference's production long-chunk prefill (vllm_quantpack/attention/int4_prefill.py:203-232: 16k-token
+    bf16 unpacks + FlashAttention 2 + fp32 fold, run through its own `prefill_sequence`) on the same cache bytes and
+    the same rotated queries, timed like this build's prefill. vLLM's FA2 build carries sm_80 code only; the image's
+    flash_attn 2.8 varlen forward stands in for it. None when the reference (baseline/_ref) or flash_attn is absent."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "vllm_quantpack")):
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    try:
+        if ref not in sys.path:
+            sys.path.insert(0, ref)
+        from vllm_quantpack.attention import int4_prefill as rp
+        from flash_attn import flash_attn_varlen_func
+    except Exception as e:
+        return {"unavailable": f"reference prefill not importable: {e}"[:200]}
+
+    def fa(q, k, v, *, max_seqlen_q, cu_seqlens_q, max_seqlen_k, cu_seqlens_k, softmax_scale, causal,
+           return_softmax_lse, fa_version):
+        o, lse, _ = flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
+                                           softmax_scale=softmax_scale, causal=causal, return_attn_probs=True)
+        return o, lse
+
+    kc, vc, ks, vs = R["views"]
+    row = R["table"][0].contiguous()
+    q_rot = ops.single_rht(R["q"].float()).to(R["q"].dtype)
+
+    def step():
+        rp.prefill_sequence(q_rot, kc, vc, ks, vs, row, w["ctx"], HS ** -0.5 / HS, fa)
+
+    t = timed_steps(torch, step, max(3, args.steps // 2), 3, flush)
+    ms = statistics.mean(t)
+    return {"ms_per_step": ms, "value": w["qlen"] / (ms * 1e-3), "unit": "tok/s",
+            "path": "reference prefill_sequence (Triton unpack + flash_attn 2.8 varlen FA2 + fp32 fold)"}
+
+
+def measure_prefill(args, torch, dist, ops, lib, w, device, rank, world, flush, with_reference):
+    """Chunk prefill (c3) on the tensor cores. N = 1: the whole chunk. N > 1: the request's cached context split by
+    sequence range over the ranks (each rank attends every query of the chunk over its range; [O | LSE] partials
+    all-gathered over NCCL and folded), strong scaling of the one chunk. Returns the JSON object (rank 0)."""
+    from vllm_quantpack_b200.attention import seq_parallel as sp
+    lo, hi, after = sp.sequence_range(w["ctx"], rank, world)
+    part = dict(w, ctx=hi - lo)
+    R = build_request(torch, ops, part, device, 1, seed=7 + rank)
+    if world > 1:
+        dist.broadcast(R["q"], 0)
     kc, vc, ks, vs = R["views"]
     q = R["q"]
     out = torch.empty_like(q)
-    row = R["table"][0].contiguous()
-    call = dict(block_row=row, n=w["ctx"], softmax_scale=HS ** -0.5, k_scale_cache=ks, v_scale_cache=vs)
-    flush = torch.empty(2 * FLUSH_BYTES, dtype=torch.uint8, device=device)
+    call = dict(block_row=R["table"][0].contiguous(), n=part["ctx"], softmax_scale=HS ** -0.5, k_scale_cache=ks,
+                v_scale_cache=vs)
+    runner = sp.SequenceParallelAttention(dist.group.WORLD, q.shape[0], NQ, HS, device) if world > 1 else None
     q_host = q.cpu().pin_memory()
     out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
     q_dev = torch.empty_like(q)
 
+    def kernel_only():          # this rank's chunk prefill over its range
+        if runner is None:
+            ops.prefill(q, kc, vc, out, **call)
+        else:
+            ops.prefill(q, kc, vc, runner.exchange.o, out_fp32_lse=runner.exchange.lse, tokens_after_keys=after,
+                        **call)
+
     def step():
-        ops.prefill(q, kc, vc, out, **call)
+        if runner is None:
+            ops.prefill(q, kc, vc, out, **call)
+        else:
+            runner.prefill(q, kc, vc, out, tokens_after_keys=after, **call)
 
     def e2e_step():
         q_dev.copy_(q_host, non_blocking=True)
-        ops.prefill(q_dev, kc, vc, out, **call)
+        if runner is None:
+            ops.prefill(q_dev, kc, vc, out, **call)
+        else:
+            runner.prefill(q_dev, kc, vc, out, tokens_after_keys=after, **call)
         out_host.copy_(out, non_blocking=True)
 
-    with Clocks(local_rank) as clk:
+    if world > 1:
+        dist.barrier()
+    with Clocks(device.index) as clk:
+        sustain(torch, step, 1.0)
         t = timed_steps(torch, step, args.steps, args.warmup, flush)
-    t_e2e = timed_steps(torch, e2e_step, args.steps, args.warmup, flush)
-    dev_err = _lib.device_error()
-    ms, ms_e = statistics.mean(t), statistics.mean(t_e2e)
+    t_k = timed_steps(torch, kernel_only, args.steps, args.warmup, flush)
+    t_e = timed_steps(torch, e2e_step, args.steps, args.warmup, flush)
+    ms, ms_k, ms_e = max_over_ranks(torch, dist, world, device,
+                                    [statistics.mean(t), statistics.mean(t_k), statistics.mean(t_e)])
+    refl = reference_fa2_prefill(torch, ops, R, w, flush, args) if with_reference and world == 1 else None
+    dev_err = lib.device_error()
     if rank != 0:
-        return
-    flops = prefill_flops(w)
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
-            peak, kind = float(json.load(fh)["bf16_tflops"]), "measured"
-    except Exception:
-        peak, kind = 1590.0, "fallback"
-    achieved = flops / (ms * 1e-3) / 1e12
-    cpu = None
-    if not args.no_cpu:
-        v, desc, cores = cpu_sample(w)
-        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
-    line = {"metric": "prefill_tok_s", "value": w["qlen"] / (ms * 1e-3), "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int4+f16", "data": "synthetic",
-            "config": {"workload": args.workload, **w, "nq": NQ, "nkv": NKV, "head_size": HS, "block_size": BS,
-                       "l2": "flushed before every step (256 MB write, then 256 MB read); cache larger than L2"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": TRAFFIC.get(args.workload),
-                         "traffic_unit": "bytes per launch (ncu dram__bytes_read + write)",
-                         "kernel": "prefill_kernel (q prep + piece fold included)",
-                         "algorithmic_flops_per_launch": flops, "peak_kind": kind},
-            "cpu_baseline": cpu,
-            "e2e": {"value": w["qlen"] / (ms_e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": q.numel() * 2,
-                    "d2h_bytes_per_step": out.numel() * 2},
-            "gpu_launches": 3 * args.steps, "clocks": clk.summary(), "device_error": dev_err}
-    print(json.dumps(line), flush=True)
+        return None
+    peak, kind = tensor_peak()
+    achieved = prefill_flops(w) / world / (ms_k * 1e-3) / 1e12
+    obj = {"metric": "prefill_tok_s", "value": w["qlen"] / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms,
+           "higher_is_better": True, "scaling": "strong" if world > 1 else "single chunk",
+           "config": {"workload": "c3", **w, "nq": NQ, "nkv": NKV, "head_size": HS, "block_size": BS,
+                      "parallelism": f"context split by sequence range over {world} GPUs, NCCL all-gather of "
+                      f"[O | LSE] partials" if world > 1 else "1 GPU",
+                      "l2": "flushed before every step; cache larger than L2"},
+           "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                        "frac": achieved / peak, "traffic": TRAFFIC.get("c3") if world == 1 else None,
+                        "traffic_unit": "bytes per launch (ncu dram__bytes_read + write)",
+                        "kernel": "prefill_kernel (q prep + piece fold included)" + (
+                            "; per rank: its range, flops of the whole chunk / N" if world > 1 else ""),
+                        "algorithmic_flops_per_launch": prefill_flops(w) / world, "kernel_ms": ms_k,
+                        "peak_kind": kind},
+           "e2e": {"value": w["qlen"] / (ms_e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": q.numel() * 2,
+                   "d2h_bytes_per_step": out.numel() * 2},
+           "gpu_launches": (3 if world == 1 else 4) * args.steps, "clocks": clk.summary(), "device_error": dev_err}
+    if refl is not None:
+        if "ms_per_step" in refl:
+            refl["speedup_of_this_build"] = refl["ms_per_step"] / ms
+        obj["reference_gpu"] = refl
+    return obj
 
 
-def run_b200(args, w, rank, world, local_rank):
+def run_prefill(args, w, rank, world, local_rank):
+    """--workload c3: the chunk prefill as the headline line."""
     import torch
     import torch.distributed as dist
     from vllm_quantpack_b200 import _lib
     from vllm_quantpack_b200.attention import ops
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
-    seqs = w["seqs"]
-    R = build_request(torch, ops, w, device, seqs, seed=rank)
+    flush = torch.empty(2 * FLUSH_BYTES, dtype=torch.uint8, device=device)
+    obj = measure_prefill(args, torch, dist, ops, _lib, w, device, rank, world, flush, with_reference=True)
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        v, desc, cores = cpu_sample(w)
+        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
+    line = {"metric": obj.pop("metric"), "value": obj.pop("value"), "unit": obj.pop("unit"), "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": obj.pop("ms_per_step"),
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "int4+f16", "data": "synthetic", "config": obj.pop("config"), "cpu_baseline": cpu, **obj}
+    print(json.dumps(line), flush=True)
+
+
+def decode_request_step(torch, ops, R, w, nsplit, runner=None, after=0):
+    """(step, kernel_only, e2e_step, q, out) closures of one decode call over the request(s) of R."""
     kc, vc, ks, vs = R["views"]
     q, cu, used, table = R["q"], R["cu"], R["used"], R["table"]
     out = torch.empty_like(q)
-    nsplit = ops.decode_num_splits(seqs, NKV, w["ctx"], ops.sm_count(device))
-    call = dict(cu_seqlens_q=cu, max_seqlen_q=w["qlen"], seqused_k=used, max_seqlen_k=w["ctx"],
+    ctx = int(R["ctx"])
+    call = dict(cu_seqlens_q=cu, max_seqlen_q=w["qlen"], seqused_k=used, max_seqlen_k=ctx,
                 softmax_scale=HS ** -0.5, block_table=table, k_scale_cache=ks, v_scale_cache=vs, num_splits=nsplit)
-    flush = torch.empty(2 * FLUSH_BYTES, dtype=torch.uint8, device=device)
-
-    def step():
-        ops.paged_decode(q, kc, vc, out, **call)
-
-    def kernel_only():
-        ops.paged_decode(q, kc, vc, out, partials_only=True, **call)
-
-    # e2e: host q (pinned) -> device, the public op, out -> pinned host; cache resident in HBM
     q_host = q.cpu().pin_memory()
     out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
     q_dev = torch.empty_like(q)
 
+    def run(qq):
+        if runner is None:
+            ops.paged_decode(qq, kc, vc, out, **call)
+        else:
+            runner.decode(qq, kc, vc, out, tokens_after_keys=after, **call)
+
+    def step():
+        run(q)
+
+    def kernel_only():
+        if runner is None:
+            ops.paged_decode(q, kc, vc, out, partials_only=True, **call)
+        else:
+            ops.paged_decode(q, kc, vc, runner.exchange.o, out_fp32_lse=runner.exchange.lse, tokens_after_keys=after,
+                             partials_only=True, **call)
+
     def e2e_step():
         q_dev.copy_(q_host, non_blocking=True)
-        ops.paged_decode(q_dev, kc, vc, out, **call)
+        run(q_dev)
         out_host.copy_(out, non_blocking=True)
 
+    return step, kernel_only, e2e_step, q, out
+
+
+def run_b200(args, w, rank, world, local_rank):
+    """Decode workloads. N = 1: one call over the workload's request(s). N > 1: the headline is ONE request of the
+    workload split by sequence range over the N GPUs (strong scaling: partial (O, LSE) all-gathered over NCCL and
+    folded); the requests sharded over the GPUs (weak scaling, no collective) are the side key `batch_sharded`."""
+    import torch
+    import torch.distributed as dist
+    from vllm_quantpack_b200 import _lib
+    from vllm_quantpack_b200.attention import ops
+    from vllm_quantpack_b200.attention import seq_parallel as sp
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    flush = torch.empty(2 * FLUSH_BYTES, dtype=torch.uint8, device=device)
+    seqs = w["seqs"]
+    sms = ops.sm_count(device)
+    # the headline request(s): the whole workload (N = 1), or this rank's sequence range of it (N > 1)
+    if world == 1:
+        part, after, runner = dict(w), 0, None
+        R = build_request(torch, ops, part, device, seqs, seed=0)
+    else:
+        lo, hi, after = sp.sequence_range(w["ctx"], rank, world)
+        part = dict(w, ctx=hi - lo)
+        R = build_request(torch, ops, part, device, seqs, seed=100 + rank)
+        dist.broadcast(R["q"], 0)  # the same query tokens on every rank
+        runner = sp.SequenceParallelAttention(dist.group.WORLD, R["q"].shape[0], NQ, HS, device)
+    R["ctx"] = part["ctx"]
+    nsplit = ops.decode_num_splits(seqs, NKV, part["ctx"], sms)
+    step, kernel_only, e2e_step, q, out = decode_request_step(torch, ops, R, w, nsplit, runner, after)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     with Clocks(local_rank) as clk:
+        sustain(torch, step, 1.0)
         t_step = timed_steps(torch, step, args.steps, args.warmup, flush)
     t_kernel = timed_steps(torch, kernel_only, args.steps, args.warmup, flush)
     t_e2e = timed_steps(torch, e2e_step, args.steps, args.warmup, flush)
     torch.cuda.synchronize()
+    ms, ms_k, ms_e = max_over_ranks(torch, dist, world, device,
+                                    [statistics.mean(t_step), statistics.mean(t_kernel), statistics.mean(t_e2e)])
+    batch = None
+    if world > 1:   # side key: each rank serves its own full request(s) of the workload, no collective
+        del R
+        Rb = build_request(torch, ops, w, device, seqs, seed=rank)
+        Rb["ctx"] = w["ctx"]
+        nb = ops.decode_num_splits(seqs, NKV, w["ctx"], sms)
+        bstep, _, _, _, _ = decode_request_step(torch, ops, Rb, w, nb)
+        dist.barrier()
+        tb = timed_steps(torch, bstep, args.steps, args.warmup, flush)
+        (msb,) = max_over_ranks(torch, dist, world, device, [statistics.mean(tb)])
+        batch = {"value": world * seqs * w["qlen"] / (msb * 1e-3), "unit": "tok/s", "ms_per_step": msb,
+                 "scaling": "weak", "parallelism": f"requests sharded over {world} GPUs, no collective"}
+        del Rb
+    pf = None
+    if args.workload == "c2a" and not args.no_prefill:
+        pf = measure_prefill(args, torch, dist, ops, _lib, WORKLOADS["c3"], device, rank, world, flush,
+                             with_reference=not args.no_cpu)
     dev_err = _lib.device_error()
-    ms = statistics.mean(t_step)
-    ms_k = statistics.mean(t_kernel)
-    ms_e = statistics.mean(t_e2e)
-    if world > 1:
-        t = torch.tensor([ms, ms_k, ms_e], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, ms_k, ms_e = t.tolist()
-    seq_parallel = run_seq_parallel(args, torch, dist, ops, w, device, rank, world, flush) if world > 1 else None
     if rank != 0:
         return
-    tokens = world * seqs * w["qlen"]
-    bytes_call = algorithmic_bytes(w)
+    tokens = seqs * w["qlen"]
+    bytes_rank = algorithmic_bytes(part)
     peak, peak_kind = peaks()
-    achieved = bytes_call / (ms_k * 1e-3) / 1e9
+    achieved = bytes_rank / (ms_k * 1e-3) / 1e9
     cpu = None
     if world == 1 and not args.no_cpu:
         v, desc, cores = cpu_sample(w)
@@ -381,17 +534,19 @@ def run_b200(args, w, rank, world, local_rank):
     line = {
         "metric": "decode_tok_s", "value": tokens / (ms * 1e-3), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int4+f16" if w["fmt"] == "int4" else "k8v4+f16",
-        "data": "synthetic",
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "int4+f16" if w["fmt"] == "int4" else "k8v4+f16", "data": "synthetic",
         "config": {"workload": args.workload, **w, "nq": NQ, "nkv": NKV, "head_size": HS, "block_size": BS,
-                   "num_splits": nsplit, "parallelism": f"requests sharded over {world} GPU(s)" if world > 1 else
-                   "1 GPU", "l2": "flushed before every step (256 MB write, then 256 MB read); cache larger than L2"},
-        "hbm_gbs": bytes_call * world / (ms * 1e-3) / 1e9 / world,
+                   "num_splits": nsplit, "parallelism": f"one request split by sequence range over {world} GPUs "
+                   f"({part['ctx']} tokens each), NCCL all-gather of [O | LSE] partials" if world > 1 else "1 GPU",
+                   "l2": "flushed before every step (256 MB write, then 256 MB read); cache larger than L2"},
+        "hbm_gbs": bytes_rank / (ms * 1e-3) / 1e9,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": TRAFFIC.get(args.workload),
+                     "traffic": TRAFFIC.get(args.workload) if world == 1 else None,
                      "traffic_unit": "bytes per launch (ncu dram__bytes_read + write)",
-                     "kernel": "decode_kernel (split-KV, with its query-row prep kernel, without the merge)",
-                     "algorithmic_bytes_per_launch": bytes_call, "kernel_ms": ms_k, "peak_kind": peak_kind},
+                     "kernel": "decode_kernel (split-KV, with its query-row prep kernel, without the merge)" + (
+                         "; per rank over its range" if world > 1 else ""),
+                     "algorithmic_bytes_per_launch": bytes_rank, "kernel_ms": ms_k, "peak_kind": peak_kind},
         "cpu_baseline": cpu,
         "e2e": {"value": tokens / (ms_e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": q.numel() * 2,
                 "d2h_bytes_per_step": out.numel() * 2},
@@ -400,40 +555,11 @@ def run_b200(args, w, rank, world, local_rank):
         "device_error": dev_err,
         "x16_layers_ms": ms * 16,
     }
-    if seq_parallel is not None:
-        line["seq_parallel"] = seq_parallel
+    if batch is not None:
+        line["batch_sharded"] = batch
+    if pf is not None:
+        line["prefill"] = pf
     print(json.dumps(line), flush=True)
-
-
-def run_seq_parallel(args, torch, dist, ops, w, device, rank, world, flush):
-    """One request of the workload split by sequence range over the ranks: rank r holds cached tokens
-    [r * ctx / N, (r + 1) * ctx / N), computes its partial (O fp32 in the RHT domain, base-2 LSE) for all query
-    tokens (causal mask shifted by the tokens held after its range), the partials are all-gathered over NCCL and
-    every rank folds them (the same fold as the split-KV merge)."""
-    from vllm_quantpack_b200.attention import seq_parallel as sp
-    lo, hi, after = sp.sequence_range(w["ctx"], rank, world)
-    part = dict(w)
-    part["ctx"] = hi - lo
-    R = build_request(torch, ops, part, device, 1, seed=100 + rank)
-    dist.broadcast(R["q"], 0)  # one request: every rank holds the same query tokens
-    kc, vc, ks, vs = R["views"]
-    runner = sp.SequenceParallelAttention(dist.group.WORLD, R["q"].shape[0], NQ, HS, device)
-    out = torch.empty_like(R["q"])
-    nsplit = ops.decode_num_splits(1, NKV, part["ctx"], ops.sm_count(device))
-    call = dict(cu_seqlens_q=R["cu"], max_seqlen_q=w["qlen"], seqused_k=R["used"], max_seqlen_k=part["ctx"],
-                softmax_scale=HS ** -0.5, block_table=R["table"], k_scale_cache=ks, v_scale_cache=vs,
-                num_splits=nsplit, tokens_after_keys=after)
-
-    def step():
-        runner.decode(R["q"], kc, vc, out, **call)
-
-    dist.barrier()
-    t = timed_steps(torch, step, args.steps, args.warmup, flush)
-    ms = torch.tensor([statistics.mean(t)], dtype=torch.float64, device=device)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = ms.item()
-    return {"value": w["qlen"] / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms, "scaling": "strong",
-            "context_per_rank": part["ctx"], "collective": "NCCL all_gather of [O fp32 | LSE] per rank"}
 
 
 def main():
@@ -443,7 +569,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="c2a", choices=sorted(WORKLOADS))
-    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample (and the reference prefill)")
+    ap.add_argument("--no-prefill", action="store_true", help="c2a: leave out the nested c3 prefill object")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     w = WORKLOADS[args.workload]
