@@ -127,12 +127,3 @@ def test_no_device_timeouts(device):
     from vllm_quantpack_b200 import _lib
     prefill_case(device, "int4", 40, 300, 16)
     assert _lib.device_error() == 0
-
-
-@pytest.mark.parametrize("fmt", ["int4", "k8v4"])
-def test_cta_pair_kernel(device, fmt, monkeypatch):
-    """The CTA-pair (cta_group::2) prefill kernel, selected by QP_PREFILL_PAIRS=1, on a multi-piece chunk and a
-    first chunk."""
-    monkeypatch.setenv("QP_PREFILL_PAIRS", "1")
-    assert prefill_case(device, fmt, 300, 5000, 16, rows=[0, 100, 299]) < TOL
-    assert prefill_case(device, fmt, 64, 64, 16) < TOL

@@ -44,7 +44,6 @@ namespace qp {
 constexpr int PF_HS = 256;
 constexpr int PF_BM = 128;  // query rows per M-tile (TMEM lanes)
 constexpr int PF_BN = 64;   // keys per tile
-constexpr int PF_THREADS = 448;  // CTA-pair kernel: 14 warps: producer, MMA, 4 dequant, 8 softmax
 #ifndef QP_PF_DQ_WARPS
 #define QP_PF_DQ_WARPS 8
 #endif
@@ -221,7 +220,7 @@ struct Sched {
 // (512 bytes, the channel order of the key operand) into its M-tile, ready to be stored as the A operand in TMEM
 // (lane = row, two fp16 per column); record the row's score scale; padding rows become zeros. Also sets every lse
 // partial to -inf (absent pieces).
-template <int FMT, int DT, bool SWZ = false>
+template <int FMT, int DT>
 __global__ void __launch_bounds__(256) prefill_qprep_kernel(const void* q, int64_t q_st, int64_t q_sh, int qlen,
                                                             int nq, int nkv, int group, int mt_per_kv,
                                                             const uint32_t* sign_bits, int q_rotated, float qk_scale,
@@ -275,10 +274,7 @@ __global__ void __launch_bounds__(256) prefill_qprep_kernel(const void* q, int64
   v.y = *reinterpret_cast<uint32_t*>(&h[2]);
   v.z = *reinterpret_cast<uint32_t*>(&h[4]);
   v.w = *reinterpret_cast<uint32_t*>(&h[6]);
-  if constexpr (SWZ)  // K-major 128B-swizzled operand layout (A operand read from shared memory)
-    *reinterpret_cast<uint4*>(tile + (lane >> 3) * 16384 + sw128_off(r, lane & 7)) = v;
-  else  // plain rows, stored into TMEM by the kernel
-    *reinterpret_cast<uint4*>(tile + r * (PF_HS * 2) + lane * 16) = v;
+  *reinterpret_cast<uint4*>(tile + r * (PF_HS * 2) + lane * 16) = v;  // plain rows, stored into TMEM by the kernel
   if (lane == 0) qs[r] = mr < qlen * group ? ldexpf(qk_scale, -ex) : 0.f;
 }
 
@@ -822,616 +818,6 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
 }
 
 
-// ======================================================================================================================
-// K3 on CTA pairs (cta_group::2): a cluster of two CTAs shares every 128-key tile. MMAs are M 256 (128 query rows per
-// CTA) x N 128 keys (QK: each CTA supplies 64 keys of the key operand) and M 256 x N 256 channels (PV: each CTA
-// supplies 128 channels of the value operand), issued by one thread of the even CTA; every M128 x N64 MMA of the
-// single-CTA kernel becomes a quarter of one full-rate MMA, and each CTA converts half of every key / value tile.
-// Roles per CTA as in prefill_kernel (producer, MMA issuer (even CTA), 4 dequant warps, 8 softmax warps); a CTA's
-// raw cells are read by both CTAs (the peer's value half, its key scales), so raw stages are released by the
-// readers of both CTAs, and operand-ready / P-ready signals of the odd CTA arrive on the even CTA's barriers.
-constexpr int P2_BM = 256;  // query rows of a pair M-tile (128 per CTA)
-constexpr int P2_BN = 128;  // keys per tile
-constexpr int P2_RH = 32;   // cells per raw half-stage (a CTA loads 64 cells of a tile: two half-stages)
-
-template <int FMT>
-struct Pf2Cfg {
-  static constexpr int CELL = FMT == FMT_INT4 ? PF_HS + 8 : PF_HS * 3 / 2 + 8;
-  static constexpr int KB = FMT == FMT_INT4 ? PF_HS / 2 : PF_HS;
-  static constexpr int RS = FMT == FMT_INT4 ? 3 : 2;  // raw half-stages
-  static constexpr int RAW_BYTES = P2_RH * CELL;
-  static constexpr int OFF_Q = 0;                      // 128 rows x 256 fp16, K-major 128B swizzle: 64 KB
-  static constexpr int OFF_K = OFF_Q + 65536;          // 2 x (this CTA's 64 keys x 256 channels, K-major) = 64 KB
-  static constexpr int OFF_V = OFF_K + 65536;          // 2 x (128 keys x this CTA's 128 channels, MN-major) = 64 KB
-  static constexpr int OFF_RAW = OFF_V + 65536;        // RS x RAW_BYTES
-  static constexpr int OFF_SC = OFF_RAW + RS * RAW_BYTES;
-  static constexpr int OFF_XCH = OFF_SC + 2 * 16;
-  static constexpr int OFF_HX = OFF_XCH + 2 * 2 * 2 * 4;
-  static constexpr int OFF_BAR = OFF_HX + (2 * 2 * 128 + 2 * 128) * 4;
-  static constexpr int NBAR = 40;
-  static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
-  static constexpr int BYTES = OFF_TMEM + 16;
-};
-
-enum {
-  C_RAW_FULL = 0,    // [RS <= 3] local: the half-stage's bulk copies landed
-  C_RAW_PEER = 3,    // [RS] local: the PEER's half-stage with this index landed (arrived by the peer)
-  C_RAW_EMPTY = 6,   // [RS] local: read by own key / value warp and the peer's (4 arrivals)
-  C_Q_FULL = 9,      // local: this CTA's Q tile landed
-  C_Q_BOTH = 10,     // even CTA: both CTAs' Q tiles landed (2 arrivals)
-  C_Q_EMPTY = 11,    // both (multicast commit): the QK MMAs of the piece are complete
-  C_K_FULL = 12,     // [2] even CTA: key operand of both CTAs written (4 arrivals)
-  C_K_FREE = 14,     // [2] both (multicast commit)
-  C_V_FULL = 16,     // [2] even CTA: value operand written (4 arrivals)
-  C_V_FREE = 18,     // [2] both
-  C_S_FULL = 20,     // [2] both
-  C_P_FULL = 22,     // [2] even CTA: P stored by both CTAs' softmax warps (16 arrivals)
-  C_SC_FULL = 24,    // [2] local: tile scale factors written (4 dequant warps)
-  C_SC_FREE = 26,    // [2] local: read by the 8 softmax warps
-  C_O_DONE = 28,     // both: PV of a tile complete
-  C_O_FREE = 29,     // even CTA: both CTAs' epilogues read O (16 arrivals)
-  C_FINAL = 30,      // both: every MMA of the pair complete
-};
-
-struct Prefill2Params {
-  const uint8_t* cache;
-  int block_size;
-  int64_t block_stride, head_stride;
-  const int32_t* block_row;
-  int n, qlen, vis_base;
-  int nq, nkv, group;
-  int mp_per_kv;           // pair M-tiles per KV head (2 prepared Q tiles each)
-  const uint8_t* qprep;    // [nkv][2 mp_per_kv][65536 B], swizzled operand layout
-  const float* qscale;     // [nkv][2 mp_per_kv][128]
-  float* part_o;
-  float* part_lse;
-  int parts;
-  int64_t total_tiles;
-};
-
-__device__ __forceinline__ int mpair_key_tiles(const Prefill2Params& p, int m) {
-  const int rows = p.qlen * p.group;
-  const int r_hi = min(rows - 1, m * P2_BM + P2_BM - 1);
-  const int keys = min(p.n, p.vis_base + r_hi / p.group + 1);
-  return (keys + P2_BN - 1) / P2_BN;
-}
-
-// stream-K walk over (KV head, pair M-tile, key tile) for pair `cta` of `ctas` (the same in both CTAs of a pair)
-struct Sched2 {
-  const Prefill2Params* p;
-  int64_t g, g_end, m_start;
-  int kvh, m, m_tiles, first_kt, piece, cta, ctas;
-  __device__ void init(const Prefill2Params& prm, int cta_, int ctas_) {
-    p = &prm;
-    cta = cta_;
-    ctas = ctas_;
-    g = prm.total_tiles * cta / ctas;
-    g_end = prm.total_tiles * (cta + 1) / ctas;
-    kvh = 0;
-    m = 0;
-    m_start = 0;
-    m_tiles = mpair_key_tiles(prm, 0);
-    while (m_start + m_tiles <= g) {
-      m_start += m_tiles;
-      if (++m == prm.mp_per_kv) {
-        m = 0;
-        ++kvh;
-      }
-      m_tiles = mpair_key_tiles(prm, m);
-    }
-    first_kt = static_cast<int>(g - m_start);
-    // piece index inside the first M-tile (once; later M-tiles start with this pair, piece 0)
-    int c0 = static_cast<int>((m_start * ctas) / prm.total_tiles);
-    while (c0 + 1 < ctas && prm.total_tiles * (c0 + 1) / ctas <= m_start) ++c0;
-    while (c0 > 0 && prm.total_tiles * c0 / ctas > m_start) --c0;
-    piece = cta - c0;
-  }
-  __device__ bool done() const { return g >= g_end; }
-  __device__ Walk current() const {
-    Walk w;
-    w.kvh = kvh;
-    w.m = m;
-    w.kt = static_cast<int>(g - m_start);
-    w.kt_end = m_tiles;
-    w.piece = piece;
-    w.first_of_piece = w.kt == first_kt;
-    w.last_of_piece = (w.kt + 1 == m_tiles) || (g + 1 == g_end);
-    w.new_mtile = w.first_of_piece;
-    return w;
-  }
-  __device__ void next() {
-    ++g;
-    if (g < g_end && g - m_start >= m_tiles) {
-      m_start += m_tiles;
-      if (++m == p->mp_per_kv) {
-        m = 0;
-        ++kvh;
-      }
-      m_tiles = mpair_key_tiles(*p, m);
-      first_kt = 0;
-      piece = 0;
-    }
-  }
-};
-
-template <int FMT>
-__global__ void __launch_bounds__(PF_THREADS, 1) prefill2_kernel(const Prefill2Params p) {
-  using C = Pf2Cfg<FMT>;
-  extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_TMEM);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t rank = cluster_ctarank();
-  const uint32_t peer = rank ^ 1u;
-  const bool leader = rank == 0;
-
-  if (tid == 0) {
-    for (int s = 0; s < C::RS; ++s) {
-      mbar_init(&bars[C_RAW_FULL + s], 1);
-      mbar_init(&bars[C_RAW_PEER + s], 1);
-      mbar_init(&bars[C_RAW_EMPTY + s], 4);
-    }
-    mbar_init(&bars[C_Q_FULL], 1);
-    mbar_init(&bars[C_Q_BOTH], 2);
-    mbar_init(&bars[C_Q_EMPTY], 1);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&bars[C_K_FULL + b], 4);
-      mbar_init(&bars[C_K_FREE + b], 1);
-      mbar_init(&bars[C_V_FULL + b], 4);
-      mbar_init(&bars[C_V_FREE + b], 1);
-      mbar_init(&bars[C_S_FULL + b], 1);
-      mbar_init(&bars[C_P_FULL + b], 16);
-      mbar_init(&bars[C_SC_FULL + b], 4);
-      mbar_init(&bars[C_SC_FREE + b], 8);
-    }
-    mbar_init(&bars[C_O_DONE], 1);
-    mbar_init(&bars[C_O_FREE], 16);
-    mbar_init(&bars[C_FINAL], 1);
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc2(tmem_slot, 512);
-    tmem_relinquish2();
-  }
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();  // both CTAs' barriers initialised before any arrival crosses the pair
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t tm_o = tmem + 256;  // S buffers: columns [0, 128), [128, 256) (P over their first 64); O [256, 512)
-
-  Sched2 sch;
-  sch.init(p, blockIdx.x >> 1, gridDim.x >> 1);
-  bool failed = false;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------------ producer: this CTA's 64 cells of a tile
-    if (lane == 0) {
-      int64_t j = 0;
-      int qcount = 0;
-      for (; !sch.done() && !failed; sch.next(), ++j) {
-        const Walk w = sch.current();
-        if (w.new_mtile) {
-          if (qcount > 0) failed |= !mbar_wait_bounded(&bars[C_Q_EMPTY], (qcount - 1) & 1);
-          const int64_t mt = static_cast<int64_t>(w.kvh) * (2 * p.mp_per_kv) + 2 * w.m + rank;
-          mbar_arrive_expect_tx(&bars[C_Q_FULL], 65536);
-          for (int c = 0; c < 4; ++c)
-            bulk_g2s(smem + C::OFF_Q + c * 16384, p.qprep + mt * 65536 + c * 16384, 16384, &bars[C_Q_FULL]);
-          failed |= !mbar_wait_bounded(&bars[C_Q_FULL], qcount & 1);  // once per piece
-          mbar_arrive_cluster(&bars[C_Q_BOTH], 0);
-          ++qcount;
-        }
-        const uint8_t* head_base = p.cache + static_cast<int64_t>(w.kvh) * p.head_stride;
-        for (int hh = 0; hh < 2; ++hh) {
-          const int64_t u = 2 * j + hh;  // half-stage use counter
-          const int hs = static_cast<int>(u % C::RS);
-          if (u >= C::RS) failed |= !mbar_wait_bounded(&bars[C_RAW_EMPTY + hs], static_cast<uint32_t>(((u / C::RS) - 1) & 1));
-          const int tok_begin = w.kt * P2_BN + 64 * static_cast<int>(rank) + P2_RH * hh;
-          const int groups = max(0, (min(tok_begin + P2_RH, p.n) - tok_begin + 15) >> 4);
-          mbar_arrive_expect_tx(&bars[C_RAW_FULL + hs], static_cast<uint32_t>(groups * 16 * C::CELL));
-          uint8_t* dst = smem + C::OFF_RAW + hs * C::RAW_BYTES;
-          for (int gi = 0; gi < groups; ++gi) {
-            const int tok = tok_begin + gi * 16;
-            const int blk = __ldg(p.block_row + tok / p.block_size);
-            bulk_g2s(dst + gi * 16 * C::CELL,
-                     head_base + static_cast<int64_t>(blk) * p.block_stride +
-                         static_cast<int64_t>(tok % p.block_size) * C::CELL,
-                     static_cast<uint32_t>(16 * C::CELL), &bars[C_RAW_FULL + hs]);
-          }
-        }
-      }
-      // copies in flight land before shared memory can go away
-      const int64_t uses = 2 * j;
-      for (int64_t u = (uses > C::RS ? uses - C::RS : 0); u < uses; ++u)
-        mbar_wait_bounded(&bars[C_RAW_FULL + (u % C::RS)], static_cast<uint32_t>((u / C::RS) & 1), 100000000ull);
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer (even CTA)
-    // The whole warp walks the schedule and waits (warp-uniform values for the descriptors); one elected lane issues.
-    if (leader) {
-      constexpr uint32_t ID_QK = f16_idesc(P2_BM, P2_BN, false);
-      constexpr uint32_t ID_PV = f16_idesc(P2_BM, PF_HS, true);
-      const uint32_t q_base = smem_u32(smem + C::OFF_Q), k_base = smem_u32(smem + C::OFF_K);
-      const uint32_t v_base = smem_u32(smem + C::OFF_V);
-      int64_t j = 0;
-      int qcount = 0, pieces = 0;
-      int64_t pv_pending = -1;
-      bool pv_first = false;
-      auto wait_all = [&](uint64_t* bar, uint32_t parity) {
-        const bool ok = mbar_wait_bounded_cluster(bar, parity);
-        failed |= __any_sync(0xffffffffu, !ok);
-      };
-      auto issue_pv = [&](int64_t t, bool first) {
-        const int b = static_cast<int>(t & 1);
-        wait_all(&bars[C_V_FULL + b], (t >> 1) & 1);
-        wait_all(&bars[C_P_FULL + b], (t >> 1) & 1);
-        tc_fence_after();
-        const uint32_t vb = v_base + b * 32768;
-        if (elect_one()) {
-          // P(t) in TMEM (each CTA's lanes), K step s = 16 keys = 8 columns; value operand: 2 N-blocks of 64
-          // channels per CTA (stride 16 KB), 8-key groups of 1024 B
-#pragma unroll
-          for (int s = 0; s < 8; ++s)
-            umma2_f16_ts(tm_o, tmem + 128 * b + 8 * s, sw128_desc(vb + 2 * s * 1024, 16384, 1024), ID_PV,
-                         (first && s == 0) ? 0u : 1u);
-          umma2_commit_mc(&bars[C_V_FREE + b], 3);
-          umma2_commit_mc(&bars[C_O_DONE], 3);
-        }
-        __syncwarp();
-      };
-      for (; !sch.done() && !failed; sch.next(), ++j) {
-        const Walk w = sch.current();
-        if (w.new_mtile) {
-          wait_all(&bars[C_Q_BOTH], qcount & 1);
-          ++qcount;
-        }
-        const int b = static_cast<int>(j & 1);
-        wait_all(&bars[C_K_FULL + b], (j >> 1) & 1);
-        // S buffer b last held S(j - 2) and P(j - 2); the PV of that tile, issued before these MMAs, waited for both
-        // CTAs' softmax to finish with it
-        tc_fence_after();
-        const uint32_t kb = k_base + b * 32768;
-        if (elect_one()) {
-#pragma unroll
-          for (int s = 0; s < 16; ++s)
-            umma2_f16(tmem + 128 * b, sw128_desc(q_base + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024),
-                      sw128_desc(kb + (s >> 2) * 8192 + (s & 3) * 32, 16, 1024), ID_QK, s > 0 ? 1u : 0u);
-          umma2_commit_mc(&bars[C_K_FREE + b], 3);
-          umma2_commit_mc(&bars[C_S_FULL + b], 3);
-          if (w.last_of_piece) umma2_commit_mc(&bars[C_Q_EMPTY], 3);
-        }
-        __syncwarp();
-        if (pv_pending >= 0) {
-          issue_pv(pv_pending, pv_first);
-          pv_pending = -1;
-        }
-        if (w.first_of_piece && pieces > 0) wait_all(&bars[C_O_FREE], (pieces - 1) & 1);
-        if (w.first_of_piece) ++pieces;
-        pv_pending = j;
-        pv_first = w.first_of_piece;
-        if (w.last_of_piece) {
-          issue_pv(pv_pending, pv_first);
-          pv_pending = -1;
-        }
-      }
-      if (elect_one()) umma2_commit_mc(&bars[C_FINAL], 3);
-      __syncwarp();
-    }
-    if (lane == 0) mbar_wait_bounded(&bars[C_FINAL], 0, 100000000ull);  // both CTAs: every MMA of the pair done
-    __syncwarp();
-  } else if (warp < 6) {
-    // ------------------------------------------------------------------ dequant (warps 2..5)
-    // key warps 2, 3: this CTA's keys 32 (warp - 2) + lane of the tile (own raw half-stage warp - 2) -> key operand
-    //   rows; the tile's key factor 2^F is the largest scale over all 128 keys (own and the peer's cells).
-    // value warps 4, 5: keys 32 (warp - 4) + lane of both CTAs' raw half-stages, this CTA's 128 channels -> value
-    //   operand rows (tile keys 64 rank' + 32 hh + lane); E is the running largest value scale over all 128 keys.
-    const int hh = (warp - 2) & 1;
-    const bool is_k = warp < 4;
-    const int wpair = hh;
-    uint8_t* const kop0 = smem + C::OFF_K;
-    uint8_t* const vop0 = smem + C::OFF_V;
-    float* xch = reinterpret_cast<float*>(smem + C::OFF_XCH) + (is_k ? 0 : 4);
-    int e_run_v = -1000;
-    int64_t j = 0;
-    for (; !sch.done() && !failed; sch.next(), ++j) {
-      const Walk w = sch.current();
-      const int b = static_cast<int>(j & 1);
-      const int64_t u = 2 * j + hh;
-      const int hs = static_cast<int>(u % C::RS);
-      const uint32_t ph = static_cast<uint32_t>((u / C::RS) & 1);
-      if (w.first_of_piece) e_run_v = -1000;
-      failed |= !mbar_wait_bounded(&bars[C_RAW_FULL + hs], ph);
-      // the key warp of this half tells the peer that this half-stage of ours has landed
-      if (is_k && lane == 0) mbar_arrive_cluster(&bars[C_RAW_PEER + hs], peer);
-      failed |= !mbar_wait_bounded_cluster(&bars[C_RAW_PEER + hs], ph);
-      const uint8_t* cell = smem + C::OFF_RAW + hs * C::RAW_BYTES + lane * C::CELL;
-      const uint32_t pcell = mapa_shared(smem_u32(cell), peer);
-      const int tok_own = w.kt * P2_BN + 64 * static_cast<int>(rank) + P2_RH * hh + lane;
-      const int tok_peer = w.kt * P2_BN + 64 * static_cast<int>(peer) + P2_RH * hh + lane;
-      const int soff = is_k ? C::KB : C::KB + 4 + PF_HS / 2;
-      const uint32_t sw_own = *reinterpret_cast<const uint32_t*>(cell + soff);
-      const uint32_t sw_peer = ld_shared_cluster_u32(pcell + soff);
-      const bool zp_scale = FMT == FMT_INT4 || !is_k;
-      const float s_own = tok_own < p.n ? __uint_as_float(zp_scale ? (sw_own & 0xFFFFFFF0u) : sw_own) : 0.f;
-      const float s_peer = tok_peer < p.n ? __uint_as_float(zp_scale ? (sw_peer & 0xFFFFFFF0u) : sw_peer) : 0.f;
-      const float wm = warp_max(fmaxf(s_own, s_peer));
-      if (lane == 0) xch[b * 2 + wpair] = wm;
-      if (named_bar_or(is_k ? 1 : 2, 64, failed)) {
-        failed = true;
-        break;
-      }
-      const float tmax = fmaxf(xch[b * 2], xch[b * 2 + 1]);
-      int ex = -1000;
-      if (tmax > 0.f) frexpf(tmax, &ex);
-      if (!is_k) {
-        e_run_v = max(e_run_v, ex);
-        ex = e_run_v;
-      }
-      if (j >= 2) failed |= !mbar_wait_bounded(&bars[C_SC_FREE + b], ((j >> 1) - 1) & 1);
-      if (lane == 0 && (warp == 2 || warp == 4)) {
-        float* scb = reinterpret_cast<float*>(smem + C::OFF_SC) + b * 4;
-        if (is_k)
-          scb[0] = ex == -1000 ? 0.f : ldexpf(1.f, ex);
-        else
-          scb[1] = __int_as_float(ex);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[C_SC_FULL + b]);
-      auto q2_of = [&](float scl) {
-        const float q = ex == -1000 ? 0.f : ldexpf(scl, -ex);
-        const __half2 qh2 = __floats2half2_rn(q, q);
-        return *reinterpret_cast<const uint32_t*>(&qh2);
-      };
-      if (is_k) {
-        if (j >= 2) failed |= !mbar_wait_bounded(&bars[C_K_FREE + b], ((j >> 1) - 1) & 1);
-        uint8_t* const kop = kop0 + b * 32768;
-        const int kr = P2_RH * hh + lane;  // key operand row
-        const uint32_t rbase = (kr >> 3) * 1024 + (kr & 7) * 128, rxor = (kr & 7) << 4;
-        const uint32_t q2 = q2_of(s_own);
-        const uint32_t zp = FMT == FMT_INT4 ? (sw_own & 0xFu) : 0u;
-        const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
-        if constexpr (FMT == FMT_INT4) {
-#pragma unroll 1
-          for (int kb = 0; kb < 4; ++kb) {
-            uint2 kw[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) kw[k] = *reinterpret_cast<const uint2*>(cell + 32 * kb + 8 * k);
-            uint8_t* const dst = kop + kb * 8192 + rbase;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const uint32_t x = (i & 1) ? kw[i >> 1].y : kw[i >> 1].x;
-              const uint32_t x8 = x >> 8;
-              uint4 v;
-              v.x = hmul2_u32(hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b), q2);
-              v.y = hmul2_u32(hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
-              v.z = hmul2_u32(hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b), q2);
-              v.w = hmul2_u32(hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
-              *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(i) << 4) ^ rxor)) = v;
-            }
-          }
-        } else {
-#pragma unroll 1
-          for (int h4 = 0; h4 < 4; ++h4) {
-            uint2 kw[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) kw[k] = *reinterpret_cast<const uint2*>(cell + 64 * h4 + 8 * k);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int C8 = 8 * h4 + k;
-              const uint32_t a = kw[k].x ^ 0x80808080u, c = kw[k].y ^ 0x80808080u;
-              uint4 v;
-              v.x = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4140u), 0x64806480u), q2);
-              v.y = hmul2_u32(hsub2_u32(prmt(a, 0x64646464u, 0x4342u), 0x64806480u), q2);
-              v.z = hmul2_u32(hsub2_u32(prmt(c, 0x64646464u, 0x4140u), 0x64806480u), q2);
-              v.w = hmul2_u32(hsub2_u32(prmt(c, 0x64646464u, 0x4342u), 0x64806480u), q2);
-              *reinterpret_cast<uint4*>(kop + (C8 >> 3) * 8192 + (rbase + ((static_cast<uint32_t>(C8 & 7) << 4) ^ rxor))) = v;
-            }
-          }
-        }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(&bars[C_K_FULL + b], 0);
-      } else {
-        if (j >= 2) failed |= !mbar_wait_bounded(&bars[C_V_FREE + b], ((j >> 1) - 1) & 1);
-        uint8_t* const vop = vop0 + b * 32768;
-        // this CTA's value bytes of a cell: [KB + 4 + 64 rank, + 64); 8-byte loads from KB + 64 rank give the pairs
-        // (w - 1, w) of value words shifted by one
-        const int vbyte = C::KB + 64 * static_cast<int>(rank);
-#pragma unroll 1
-        for (int side = 0; side < 2; ++side) {  // own key, then the peer's key of this lane
-          const bool own = side == 0;
-          const int key = 64 * static_cast<int>(own ? rank : peer) + P2_RH * hh + lane;  // tile key = operand row
-          const uint32_t swv = own ? sw_own : sw_peer;
-          const uint32_t q2 = q2_of(own ? s_own : s_peer);
-          const uint32_t zp = swv & 0xFu;
-          const uint32_t lo_b = 0x64006400u | zp | (zp << 16), hi_b = 0xD400D400u | (zp << 4) | (zp << 20);
-          uint2 vw[9];
-          if (own) {
-#pragma unroll
-            for (int k = 0; k < 9; ++k) vw[k] = *reinterpret_cast<const uint2*>(cell + vbyte + 8 * k);
-          } else {
-#pragma unroll
-            for (int k = 0; k < 9; ++k) vw[k] = ld_shared_cluster_v2(pcell + vbyte + 8 * k);
-          }
-          const uint32_t rbase = (key >> 3) * 1024 + (key & 7) * 128, rxor = (key & 7) << 4;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {  // value word i: channels 128 rank + 8 i .. + 7 -> N-block i / 8, chunk i % 8
-            const uint32_t x = (i & 1) ? vw[(i + 1) >> 1].x : vw[i >> 1].y;
-            const uint32_t x8 = x >> 8;
-            uint4 v;
-            v.x = hmul2_u32(hsub2_u32(lop3_and_or(x, 0x000F000Fu, 0x64006400u), lo_b), q2);
-            v.y = hmul2_u32(hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
-            v.z = hmul2_u32(hsub2_u32(lop3_and_or(x8, 0x000F000Fu, 0x64006400u), lo_b), q2);
-            v.w = hmul2_u32(hfma2_u32(lop3_and_or(x8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, hi_b), q2);
-            *reinterpret_cast<uint4*>(vop + (i >> 3) * 16384 + (rbase + ((static_cast<uint32_t>(i & 7) << 4) ^ rxor))) = v;
-          }
-        }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(&bars[C_V_FULL + b], 0);
-      }
-      // this warp is done with both CTAs' half-stage hs: release it in both
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bars[C_RAW_EMPTY + hs]);
-        mbar_arrive_cluster(&bars[C_RAW_EMPTY + hs], peer);
-      }
-    }
-  } else {
-    // ------------------------------------------------------------------ softmax / epilogue (warps 6..13)
-    // this CTA's 128 rows (TMEM lanes); warps 6-9 keys 0-63 of a tile and channels 0-127, warps 10-13 keys 64-127
-    // and channels 128-255 (two threads per row, maxima and sums exchanged through shared memory)
-    const int quarter = warp & 3;
-    const int half = (warp - 6) >> 2;
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const int pair_bar = 3 + quarter;
-    float* hmax = reinterpret_cast<float*>(smem + C::OFF_HX);
-    float* hsum = hmax + 2 * 2 * 128;
-    int64_t j = 0;
-    int64_t pv_seen = 0;  // O_DONE phases consumed in order (see prefill_kernel)
-    auto wait_pv = [&](int64_t t) {
-      for (; pv_seen <= t; ++pv_seen) failed |= !mbar_wait_bounded(&bars[C_O_DONE], static_cast<uint32_t>(pv_seen & 1));
-    };
-    float m_used = -INFINITY, l = 0.f, qsc = 0.f;
-    int e_used = -1000, lim = -1, tok = 0, qh = 0;
-    bool row_ok = false;
-    int64_t t_in_piece = 0;
-    for (; !sch.done() && !failed; sch.next(), ++j) {
-      const Walk w = sch.current();
-      const int b = static_cast<int>(j & 1);
-      const uint32_t tm_s = tmem + 128 * b;
-      if (w.new_mtile) {
-        const int mrow = 2 * w.m + static_cast<int>(rank);  // this CTA's 128-row M-tile
-        qsc = p.qscale[(static_cast<int64_t>(w.kvh) * (2 * p.mp_per_kv) + mrow) * PF_BM + row];
-        const int rg = mrow * PF_BM + row;
-        row_ok = rg < p.qlen * p.group;
-        tok = rg / p.group;
-        qh = w.kvh * p.group + rg % p.group;
-        lim = row_ok ? min(p.n - 1, p.vis_base + tok) : -1;
-      }
-      if (w.first_of_piece) {
-        m_used = -INFINITY;
-        l = 0.f;
-        e_used = -1000;
-        t_in_piece = 0;
-      }
-      failed |= !mbar_wait_bounded(&bars[C_S_FULL + b], (j >> 1) & 1);
-      tc_fence_after();
-      float s[64];
-      tmem_ld64(tm_s + lane_off + 64 * half, s);
-      failed |= !mbar_wait_bounded(&bars[C_SC_FULL + b], (j >> 1) & 1);
-      const float* scb = reinterpret_cast<const float*>(smem + C::OFF_SC) + b * 4;
-      const float qs_t = qsc * scb[0];
-      const int ev = __float_as_int(scb[1]);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[C_SC_FREE + b]);
-      const int key0 = w.kt * P2_BN + 64 * half;
-      const bool masked = w.kt * P2_BN + P2_BN - 1 > min(p.n - 1, p.vis_base);
-      if (masked) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (key0 + c > lim) s[c] = -INFINITY;
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) mx = fmaxf(mx, s[c]);
-      hmax[(b * 2 + half) * 128 + row] = mx;
-      if (named_bar_or(pair_bar, 64, failed)) {
-        failed = true;
-        break;
-      }
-      mx = fmaxf(mx, hmax[(b * 2 + (half ^ 1)) * 128 + row]);
-      const float mrow_v = mx * qs_t;
-      const bool grow = mrow_v > m_used + PF_SLACK;
-      const bool vgrow = ev > e_used;
-      if (__any_sync(0xffffffffu, grow) || vgrow) {
-        const float m_new = grow ? mrow_v : m_used;
-        const float alpha = m_new == m_used ? 1.f : exp2f(m_used - m_new);
-        const float o_range = e_used == -1000 ? 0.f : ldexpf(1.f, e_used - ev);
-        const float ao = alpha * o_range;
-        if (t_in_piece > 0) {
-          wait_pv(j - 1);
-          tc_fence_after();
-#pragma unroll 1
-          for (int c0 = 128 * half; c0 < 128 * half + 128; c0 += 32) {
-            float o[32];
-            tmem_ld32(tm_o + lane_off + c0, o);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= ao;
-            tmem_st32(tm_o + lane_off + c0, o);
-          }
-        }
-        l *= alpha;
-        m_used = m_new;
-        e_used = ev;
-      }
-      const float base = m_used == -INFINITY ? 0.f : m_used;
-      float lsum = 0.f;
-      wait_pv(j - 1);
-#pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {  // P of keys 64 half + 32 c2 .. -> TMEM columns 32 half + 16 c2 ..
-        uint32_t pw[16];
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float a0 = s[32 * c2 + c], a1 = s[32 * c2 + c + 1];
-          const float p0 = a0 == -INFINITY ? 0.f : fast_exp2(fmaf(a0, qs_t, -base));
-          const float p1 = a1 == -INFINITY ? 0.f : fast_exp2(fmaf(a1, qs_t, -base));
-          lsum += p0 + p1;
-          const __half2 h = __floats2half2_rn(p0, p1);
-          pw[c >> 1] = *reinterpret_cast<const uint32_t*>(&h);
-        }
-        tmem_st16u(tm_s + lane_off + 32 * half + 16 * c2, pw);
-      }
-      l += lsum;
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(&bars[C_P_FULL + b], 0);
-      ++t_in_piece;
-
-      if (w.last_of_piece) {
-        hsum[half * 128 + row] = l;
-        if (named_bar_or(pair_bar, 64, failed)) {
-          failed = true;
-          break;
-        }
-        const float l_row = l + hsum[(half ^ 1) * 128 + row];
-        wait_pv(j);
-        tc_fence_after();
-        const float o_unit = e_used == -1000 ? 0.f : ldexpf(1.f, e_used);
-        const float inv = l_row > 0.f ? o_unit / l_row : 0.f;
-        const int64_t prow_i = (static_cast<int64_t>(tok) * p.nq + qh) * p.parts + w.piece;
-#pragma unroll 1
-        for (int c0 = 128 * half; c0 < 128 * half + 128; c0 += 32) {
-          float o[32];
-          tmem_ld32(tm_o + lane_off + c0, o);
-          if (row_ok && w.piece < p.parts) {
-            float* dst = p.part_o + prow_i * PF_HS + c0;
-#pragma unroll
-            for (int g8 = 0; g8 < 4; ++g8) {
-              const float* og = o + 8 * g8;
-              reinterpret_cast<float4*>(dst + 8 * g8)[0] = make_float4(og[0] * inv, og[2] * inv, og[4] * inv, og[6] * inv);
-              reinterpret_cast<float4*>(dst + 8 * g8)[1] = make_float4(og[1] * inv, og[3] * inv, og[5] * inv, og[7] * inv);
-            }
-          }
-        }
-        if (half == 0 && row_ok && w.piece < p.parts) p.part_lse[prow_i] = l_row > 0.f ? m_used + log2f(l_row) : -INFINITY;
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(&bars[C_O_FREE], 0);
-      }
-    }
-  }
-
-  if (failed) atomicCAS(&g_device_error, DEV_ERR_NONE, DEV_ERR_WAIT_TIMEOUT);
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();  // the peer is done with this CTA's shared memory and barriers, every MMA of the pair complete
-  tc_fence_after();
-  if (warp == 1) tmem_dealloc2(tmem, 512);
-}
-
 }  // namespace qp
 
 using namespace qp;
@@ -1459,32 +845,6 @@ static void prefill_plan(int qlen, int n, int after, int nkv, int group, int sms
   *parts = static_cast<int>(std::min<int64_t>(*ctas, (maxt + per - 1) / per + 1));
 }
 
-// The same for the CTA-pair kernel: pair M-tiles of 256 rows, 128-key tiles, one stream-K range per pair.
-static void prefill_plan2(int qlen, int n, int after, int nkv, int group, int sms, int* mp_per_kv, int64_t* total,
-                          int* pairs, int* parts) {
-  const int rows = qlen * group;
-  *mp_per_kv = (rows + P2_BM - 1) / P2_BM;
-  int64_t tot = 0;
-  int maxt = 0;
-  for (int m = 0; m < *mp_per_kv; ++m) {
-    const int r_hi = std::min(rows - 1, m * P2_BM + P2_BM - 1);
-    const int t = (std::min(n, n - qlen + after + r_hi / group + 1) + P2_BN - 1) / P2_BN;
-    tot += t;
-    maxt = std::max(maxt, t);
-  }
-  tot *= nkv;
-  *total = tot;
-  *pairs = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sms / 2, tot)));
-  const int64_t per = std::max<int64_t>(1, tot / *pairs);
-  *parts = static_cast<int>(std::min<int64_t>(*pairs, (maxt + per - 1) / per + 1));
-}
-
-// the single-CTA kernel serves every chunk unless QP_PREFILL_PAIRS=1 selects the CTA-pair kernel
-static bool prefill_use_pairs() {
-  const char* e = getenv("QP_PREFILL_PAIRS");
-  return e && e[0] == '1';
-}
-
 static int64_t prefill_ws_bytes(int qlen, int nq, int64_t nt, int parts) {
   return align256(nt * 65536) + align256(nt * PF_BM * 4) +
          align256(static_cast<int64_t>(qlen) * nq * parts * PF_HS * 4) +
@@ -1497,40 +857,10 @@ extern "C" int64_t qp_prefill_workspace_bytes(int qlen, int n, int num_q_heads, 
   (void)head_size;
   const int after = std::min(tokens_after_keys, qlen);
   const int group = num_q_heads / num_kv_heads;
-  int mt, ctas, parts, mp, pairs, parts2;
-  int64_t total, total2;
+  int mt, ctas, parts;
+  int64_t total;
   prefill_plan(qlen, n, after, num_kv_heads, group, device_sm_count(), &mt, &total, &ctas, &parts);
-  prefill_plan2(qlen, n, after, num_kv_heads, group, device_sm_count(), &mp, &total2, &pairs, &parts2);
-  return std::max(prefill_ws_bytes(qlen, num_q_heads, static_cast<int64_t>(num_kv_heads) * mt, parts),
-                  prefill_ws_bytes(qlen, num_q_heads, static_cast<int64_t>(num_kv_heads) * 2 * mp, parts2));
-}
-
-template <int FMT>
-static int launch_prefill2(const Prefill2Params& pp, int pairs, cudaStream_t st) {
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(prefill2_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Pf2Cfg<FMT>::BYTES);
-    if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "prefill (pairs) smem attribute: %s", cudaGetErrorString(e));
-    if (dev >= 0 && dev < 64) configured[dev] = true;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
-  cfg.blockDim = dim3(PF_THREADS);
-  cfg.dynamicSmemBytes = Pf2Cfg<FMT>::BYTES;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, prefill2_kernel<FMT>, pp);
-  if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "prefill (pairs) launch: %s", cudaGetErrorString(e));
-  return QP_OK;
+  return prefill_ws_bytes(qlen, num_q_heads, static_cast<int64_t>(num_kv_heads) * mt, parts);
 }
 
 template <int FMT>
@@ -1648,20 +978,12 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
     return set_error(QP_ERR_INVALID, "prefill: null pointer");
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(QP_ERR_WORKSPACE, "prefill: workspace alignment");
   const int group = num_q_heads / num_kv_heads;
-  const bool pairs_path = prefill_use_pairs();
   int mt, ctas, parts;
   int64_t total;
-  if (pairs_path) {
-    int mp, pairs;
-    prefill_plan2(qlen, n, after, num_kv_heads, group, device_sm_count(), &mp, &total, &pairs, &parts);
-    mt = 2 * mp;  // prepared 128-row Q tiles per KV head
-    ctas = pairs;
-  } else {
-    prefill_plan(qlen, n, after, num_kv_heads, group, device_sm_count(), &mt, &total, &ctas, &parts);
-    if (total >= (int64_t(1) << 31))  // the kernel walks its schedule in 32-bit counters
-      return set_error(QP_ERR_UNSUPPORTED, "prefill: %lld (128-query, 64-key) tiles exceed the 2^31 the schedule counts",
-                       (long long)total);
-  }
+  prefill_plan(qlen, n, after, num_kv_heads, group, device_sm_count(), &mt, &total, &ctas, &parts);
+  if (total >= (int64_t(1) << 31))  // the kernel walks its schedule in 32-bit counters
+    return set_error(QP_ERR_UNSUPPORTED, "prefill: %lld (128-query, 64-key) tiles exceed the 2^31 the schedule counts",
+                     (long long)total);
   const int64_t need = qp_prefill_workspace_bytes(qlen, n, num_q_heads, num_kv_heads, head_size, tokens_after_keys);
   if (workspace_bytes < need)
     return set_error(QP_ERR_WORKSPACE, "prefill: workspace of %lld bytes < %lld", (long long)workspace_bytes,
@@ -1678,22 +1000,14 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
   const int64_t qrows = nt * PF_BM;
   const int64_t lse_count = static_cast<int64_t>(qlen) * num_q_heads * parts;
   const unsigned qgrid = static_cast<unsigned>((qrows + 7) / 8);
-#define QP_QPREP(F, D, SW)                                                                                     \
-  prefill_qprep_kernel<F, D, SW><<<qgrid, 256, 0, st>>>(q, q_stride_token, q_stride_head, qlen, num_q_heads,   \
+#define QP_QPREP(F, D)                                                                                         \
+  prefill_qprep_kernel<F, D><<<qgrid, 256, 0, st>>>(q, q_stride_token, q_stride_head, qlen, num_q_heads,   \
                                                         num_kv_heads, group, mt, rht_sign_bits, q_rotated,      \
                                                         qk_scale, qprep, qscale, part_lse, lse_count)
-  if (pairs_path) {
-    if (fmt == FMT_INT4) {
-      if (dtype == DT_BF16) QP_QPREP(FMT_INT4, DT_BF16, true); else QP_QPREP(FMT_INT4, DT_F16, true);
-    } else {
-      if (dtype == DT_BF16) QP_QPREP(FMT_K8V4, DT_BF16, true); else QP_QPREP(FMT_K8V4, DT_F16, true);
-    }
+  if (fmt == FMT_INT4) {
+    if (dtype == DT_BF16) QP_QPREP(FMT_INT4, DT_BF16); else QP_QPREP(FMT_INT4, DT_F16);
   } else {
-    if (fmt == FMT_INT4) {
-      if (dtype == DT_BF16) QP_QPREP(FMT_INT4, DT_BF16, false); else QP_QPREP(FMT_INT4, DT_F16, false);
-    } else {
-      if (dtype == DT_BF16) QP_QPREP(FMT_K8V4, DT_BF16, false); else QP_QPREP(FMT_K8V4, DT_F16, false);
-    }
+    if (dtype == DT_BF16) QP_QPREP(FMT_K8V4, DT_BF16); else QP_QPREP(FMT_K8V4, DT_F16);
   }
 #undef QP_QPREP
   int rc = check_launch("prefill q prep");
@@ -1718,30 +1032,7 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
   pp.part_lse = part_lse;
   pp.parts = parts;
   pp.total_tiles = total;
-  if (pairs_path) {
-    Prefill2Params p2{};
-    p2.cache = pp.cache;
-    p2.block_size = block_size;
-    p2.block_stride = block_stride;
-    p2.head_stride = head_stride;
-    p2.block_row = block_row;
-    p2.n = n;
-    p2.qlen = qlen;
-    p2.vis_base = pp.vis_base;
-    p2.nq = num_q_heads;
-    p2.nkv = num_kv_heads;
-    p2.group = group;
-    p2.mp_per_kv = mt / 2;
-    p2.qprep = qprep;
-    p2.qscale = qscale;
-    p2.part_o = part_o;
-    p2.part_lse = part_lse;
-    p2.parts = parts;
-    p2.total_tiles = total;
-    rc = fmt == FMT_INT4 ? launch_prefill2<FMT_INT4>(p2, ctas, st) : launch_prefill2<FMT_K8V4>(p2, ctas, st);
-  } else {
-    rc = fmt == FMT_INT4 ? launch_prefill_main<FMT_INT4>(pp, ctas, st) : launch_prefill_main<FMT_K8V4>(pp, ctas, st);
-  }
+  rc = fmt == FMT_INT4 ? launch_prefill_main<FMT_INT4>(pp, ctas, st) : launch_prefill_main<FMT_K8V4>(pp, ctas, st);
   if (rc) return rc;
   if (parts <= FOLD_MAX_PARTS) {
     if (!out || (out_mode == 0 && !rht_sign_bits)) return set_error(QP_ERR_INVALID, "prefill: null output / signs");
