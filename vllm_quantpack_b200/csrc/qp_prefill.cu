@@ -34,6 +34,7 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <vector>
 
 #include "qp_api_internal.h"
 #include "qp_common.cuh"
@@ -126,6 +127,8 @@ struct PrefillParams {
   float* part_lse;           // [qlen][nq][parts]
   int parts;
   int64_t total_tiles;       // (M-tile, key-tile) pairs over all KV heads
+  int chunk_tiles;           // key tiles of one key chunk (the walk is chunk-major, see Sched)
+  int piece_stride;          // piece slots per key chunk of an M-tile
 };
 
 // position of channel c inside its group of 8 in the operand order [0 4 1 5 2 6 3 7]
@@ -140,10 +143,21 @@ __device__ __forceinline__ int mtile_key_tiles(const PrefillParams& p, int m) {
   return (keys + PF_BN - 1) / PF_BN;
 }
 
-// Walk of the tiles of this CTA: [g_begin, g_end) of the flattened (KV head, M-tile, key tile) space.
+// Key tiles [*lo, *lo + result) of M-tile m that fall in key chunk j.
+__device__ __forceinline__ int run_tiles(const PrefillParams& p, int j, int m, int* lo) {
+  const int a = j * p.chunk_tiles;
+  *lo = a;
+  return max(0, min(mtile_key_tiles(p, m), a + p.chunk_tiles) - a);
+}
+
+// Walk of the tiles of this CTA: [g_begin, g_end) of the flattened (key chunk, KV head, M-tile, key tile) space.
+// Key chunk major: the CTAs running at one time work on the M-tiles of the same key chunk, so every key tile is
+// fetched from HBM about once and the M-tiles of its KV head read it from L2 (a walk with the key tiles of one M-tile
+// innermost had every M-tile re-read its head's whole cache). A run (one M-tile's tiles inside one chunk) split by CTA
+// boundaries gives several pieces; piece slots j * piece_stride + i keep the pieces of different chunks apart.
 struct Walk {
   int kvh, m, kt, kt_end;  // current M-tile and key tile
-  int piece;               // index of this CTA's piece of the M-tile
+  int piece;               // partial slot of this CTA's piece of the M-tile
   bool first_of_piece, last_of_piece, new_mtile;
 };
 
@@ -152,12 +166,21 @@ struct Walk {
 struct Sched {
   const PrefillParams* p;
   int left;          // tiles of this CTA not yet walked past, the current one included
-  int kvh, m;        // current M-tile
-  int kt;            // current key tile inside the M-tile
-  int m_tiles;       // key tiles of the current M-tile
-  int first_kt;      // first key tile of this CTA inside the current M-tile
-  int piece;         // index of this CTA's piece of the current M-tile
+  int j, kvh, m;     // current run: key chunk, M-tile
+  int kt, kt_hi;     // current key tile inside the M-tile, end of the run
+  int first_kt;      // first key tile of this CTA inside the current run
+  int piece;         // partial slot of this CTA's piece of the current run
   int cta, ctas;
+
+  __device__ void advance_run() {
+    if (++m == p->mt_per_kv) {
+      m = 0;
+      if (++kvh == p->nkv) {
+        kvh = 0;
+        ++j;
+      }
+    }
+  }
 
   __device__ void init(const PrefillParams& prm, int cta_, int ctas_) {
     p = &prm;
@@ -166,27 +189,24 @@ struct Sched {
     const int64_t g = prm.total_tiles * cta / ctas;
     const int64_t g_end = prm.total_tiles * (cta + 1) / ctas;
     left = static_cast<int>(g_end - g);
-    kvh = 0;
-    m = 0;
-    int64_t m_start = 0;
-    m_tiles = mtile_key_tiles(prm, 0);
-    // advance to the M-tile holding g (M-tiles of each KV head in order)
-    while (m_start + m_tiles <= g) {
-      m_start += m_tiles;
-      if (++m == prm.mt_per_kv) {
-        m = 0;
-        ++kvh;
-      }
-      m_tiles = mtile_key_tiles(prm, m);
+    j = kvh = m = 0;
+    int64_t start = 0;
+    int lo = 0;
+    int len = run_tiles(prm, 0, 0, &lo);
+    while (start + len <= g && left > 0) {  // to the run holding g (empty runs are skipped)
+      start += len;
+      advance_run();
+      len = run_tiles(prm, j, m, &lo);
     }
-    first_kt = kt = static_cast<int>(g - m_start);
-    // piece index inside the first M-tile: CTAs whose range starts inside it before this one. The CTA covering
-    // m_start is the largest c with total * c / ctas <= m_start. (Computed once: 64-bit divisions are long
-    // instruction sequences; every later M-tile of this CTA starts with this CTA, piece 0.)
-    int c0 = static_cast<int>((m_start * ctas) / prm.total_tiles);
-    while (c0 + 1 < ctas && prm.total_tiles * (c0 + 1) / ctas <= m_start) ++c0;
-    while (c0 > 0 && prm.total_tiles * c0 / ctas > m_start) --c0;
-    piece = cta - c0;
+    kt = first_kt = lo + static_cast<int>(g - start);
+    kt_hi = lo + len;
+    // piece inside the run: CTAs whose range starts inside it before this one. The CTA covering `start` is the
+    // largest c with total * c / ctas <= start. (Computed once: 64-bit divisions are long instruction sequences;
+    // every later run of this CTA starts with this CTA, piece 0.)
+    int c0 = static_cast<int>((start * ctas) / prm.total_tiles);
+    while (c0 + 1 < ctas && prm.total_tiles * (c0 + 1) / ctas <= start) ++c0;
+    while (c0 > 0 && prm.total_tiles * c0 / ctas > start) --c0;
+    piece = j * prm.piece_stride + (cta - c0);
   }
   __device__ bool done() const { return left <= 0; }
   __device__ Walk current() const {
@@ -194,23 +214,24 @@ struct Sched {
     w.kvh = kvh;
     w.m = m;
     w.kt = kt;
-    w.kt_end = m_tiles;
+    w.kt_end = kt_hi;
     w.piece = piece;
     w.first_of_piece = kt == first_kt;
-    w.last_of_piece = (kt + 1 == m_tiles) || (left == 1);
+    w.last_of_piece = (kt + 1 == kt_hi) || (left == 1);
     w.new_mtile = w.first_of_piece;
     return w;
   }
   __device__ void next() {
     --left;
-    if (++kt >= m_tiles && left > 0) {
-      if (++m == p->mt_per_kv) {
-        m = 0;
-        ++kvh;
-      }
-      m_tiles = mtile_key_tiles(*p, m);
-      kt = first_kt = 0;
-      piece = 0;
+    if (++kt >= kt_hi && left > 0) {
+      int lo = 0, len = 0;
+      do {
+        advance_run();
+        len = run_tiles(*p, j, m, &lo);
+      } while (len == 0);
+      kt = first_kt = lo;
+      kt_hi = lo + len;
+      piece = j * p->piece_stride;
     }
   }
 };
@@ -826,23 +847,56 @@ using namespace qp;
 // [part_lse qlen*nq*parts f32], each 256-byte aligned.
 static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
-static void prefill_plan(int qlen, int n, int after, int nkv, int group, int sms, int* mt_per_kv, int64_t* total,
-                         int* ctas, int* parts) {
+// Key chunks of a chunk prefill: the cache of all KV heads in pieces of at most 64 MB (so that the chunk the CTAs work
+// on, and the next one, stay in the 126 MB L2), at most 8.
+static int prefill_chunks(int n, int nkv, int cell) {
+  const int64_t bytes = static_cast<int64_t>(n) * nkv * cell;
+  return static_cast<int>(std::min<int64_t>(8, std::max<int64_t>(1, (bytes + (64ll << 20) - 1) / (64ll << 20))));
+}
+
+struct PrefillPlan {
+  int mt_per_kv, ctas, parts, chunk_tiles, piece_stride;
+  int64_t total;
+};
+
+static PrefillPlan prefill_plan(int qlen, int n, int after, int nkv, int group, int sms, int cell) {
+  PrefillPlan pl{};
   const int rows = qlen * group;
-  *mt_per_kv = (rows + PF_BM - 1) / PF_BM;
+  pl.mt_per_kv = (rows + PF_BM - 1) / PF_BM;
+  std::vector<int> tiles(pl.mt_per_kv);
   int64_t tot = 0;
   int maxt = 0;
-  for (int m = 0; m < *mt_per_kv; ++m) {
+  for (int m = 0; m < pl.mt_per_kv; ++m) {
     const int r_hi = std::min(rows - 1, m * PF_BM + PF_BM - 1);
-    const int t = (std::min(n, n - qlen + after + r_hi / group + 1) + PF_BN - 1) / PF_BN;
-    tot += t;
-    maxt = std::max(maxt, t);
+    tiles[m] = (std::min(n, n - qlen + after + r_hi / group + 1) + PF_BN - 1) / PF_BN;
+    tot += tiles[m];
+    maxt = std::max(maxt, tiles[m]);
   }
   tot *= nkv;
-  *total = tot;
-  *ctas = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sms, tot)));
-  const int64_t per = std::max<int64_t>(1, tot / *ctas);
-  *parts = static_cast<int>(std::min<int64_t>(*ctas, (maxt + per - 1) / per + 1));
+  pl.total = tot;
+  pl.ctas = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sms, tot)));
+  const int chunks = prefill_chunks(n, nkv, cell);
+  pl.chunk_tiles = std::max(1, (maxt + chunks - 1) / chunks);
+  // pieces of a run: the CTAs covering it (the CTA of tile g: the largest c with total * c / ctas <= g)
+  auto cta_of = [&](int64_t g) {
+    int c = static_cast<int>(g * pl.ctas / std::max<int64_t>(1, tot));
+    while (c + 1 < pl.ctas && tot * (c + 1) / pl.ctas <= g) ++c;
+    while (c > 0 && tot * c / pl.ctas > g) --c;
+    return c;
+  };
+  int stride = 1;
+  int64_t start = 0;
+  for (int j = 0; j < chunks; ++j)
+    for (int h = 0; h < nkv; ++h)
+      for (int m = 0; m < pl.mt_per_kv; ++m) {
+        const int a = j * pl.chunk_tiles;
+        const int len = std::max(0, std::min(tiles[m], a + pl.chunk_tiles) - a);
+        if (len > 0) stride = std::max(stride, cta_of(start + len - 1) - cta_of(start) + 1);
+        start += len;
+      }
+  pl.piece_stride = stride;
+  pl.parts = chunks * stride;
+  return pl;
 }
 
 static int64_t prefill_ws_bytes(int qlen, int nq, int64_t nt, int parts) {
@@ -857,10 +911,14 @@ extern "C" int64_t qp_prefill_workspace_bytes(int qlen, int n, int num_q_heads, 
   (void)head_size;
   const int after = std::min(tokens_after_keys, qlen);
   const int group = num_q_heads / num_kv_heads;
-  int mt, ctas, parts;
-  int64_t total;
-  prefill_plan(qlen, n, after, num_kv_heads, group, device_sm_count(), &mt, &total, &ctas, &parts);
-  return prefill_ws_bytes(qlen, num_q_heads, static_cast<int64_t>(num_kv_heads) * mt, parts);
+  // either cache format (the chunk count depends on the cell size)
+  int64_t need = 0;
+  for (int cell : {PF_HS + 8, PF_HS * 3 / 2 + 8}) {
+    const PrefillPlan pl = prefill_plan(qlen, n, after, num_kv_heads, group, device_sm_count(), cell);
+    need = std::max(need, prefill_ws_bytes(qlen, num_q_heads, static_cast<int64_t>(num_kv_heads) * pl.mt_per_kv,
+                                           pl.parts));
+  }
+  return need;
 }
 
 template <int FMT>
@@ -978,9 +1036,9 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
     return set_error(QP_ERR_INVALID, "prefill: null pointer");
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(QP_ERR_WORKSPACE, "prefill: workspace alignment");
   const int group = num_q_heads / num_kv_heads;
-  int mt, ctas, parts;
-  int64_t total;
-  prefill_plan(qlen, n, after, num_kv_heads, group, device_sm_count(), &mt, &total, &ctas, &parts);
+  const PrefillPlan pl = prefill_plan(qlen, n, after, num_kv_heads, group, device_sm_count(), cell);
+  const int mt = pl.mt_per_kv, ctas = pl.ctas, parts = pl.parts;
+  const int64_t total = pl.total;
   if (total >= (int64_t(1) << 31))  // the kernel walks its schedule in 32-bit counters
     return set_error(QP_ERR_UNSUPPORTED, "prefill: %lld (128-query, 64-key) tiles exceed the 2^31 the schedule counts",
                      (long long)total);
@@ -1032,6 +1090,8 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
   pp.part_lse = part_lse;
   pp.parts = parts;
   pp.total_tiles = total;
+  pp.chunk_tiles = pl.chunk_tiles;
+  pp.piece_stride = pl.piece_stride;
   rc = fmt == FMT_INT4 ? launch_prefill_main<FMT_INT4>(pp, ctas, st) : launch_prefill_main<FMT_K8V4>(pp, ctas, st);
   if (rc) return rc;
   if (parts <= FOLD_MAX_PARTS) {
