@@ -4,13 +4,24 @@
 // One warp per (token, KV head): the warp holds the head's hs values (lane L: elements [E L, E L + E)), rotates them
 // in fp32, rounds them to the model dtype (as `single_rht(x.float()).to(x.dtype)`,
 // vllm_quantpack/attention/k8v4_kv.py:71-72), then quantizes with warp reductions for min / max / absmax and writes
-// the packed codes and scale words into the cell. Every fp32 operation of the quantizer is the IEEE op the
-// reference's source names (vllm_quantpack/attention/k8v4_ops.py:30-63), never contracted into an FMA, so codes and
-// scale words are bit-exact with the reference evaluated in IEEE fp32.
+// the packed codes and scale words into the cell. The quantizer performs the fp32 operations of the reference's
+// source (vllm_quantpack/attention/k8v4_ops.py:30-63) the way Triton compiles them for the GPU: every `/` is PTX
+// div.full.f32 (Triton's plain fp32 division; its IEEE-rounded one is the separate tl.math.div_rn), and
+// v * (1 / scale) + zp is one FMA (Triton fuses by default). Codes and scale words are then bit-exact with the
+// reference's store as it runs on the B200 (measured); against the same source evaluated in IEEE fp32 (Triton's
+// interpreter, the CPU oracle) they differ only next to rounding ties, by one code step or a couple of ulp.
 #include "qp_api_internal.h"
 #include "qp_common.cuh"
 
 namespace qp {
+
+// The division the reference's compiled store performs: Triton lowers a plain fp32 `/` to PTX div.full.f32 (its
+// IEEE-rounded division is the separate tl.math.div_rn), so the same instruction gives the same codes and scales.
+__device__ __forceinline__ float div_full(float a, float b) {
+  float r;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
 
 struct StoreParams {
   const void* key;
@@ -56,13 +67,13 @@ __device__ __forceinline__ void quant_store_int4(const float (&x)[E], uint8_t* c
     mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   }
-  const float scale = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), 15.0f), 1e-6f);
-  const float zp = fminf(fmaxf(round_half_away(__fdiv_rn(-mn, scale)), 0.0f), 15.0f);
-  const float inv = __fdiv_rn(1.0f, scale);
+  const float scale = fmaxf(div_full(__fsub_rn(mx, mn), 15.0f), 1e-6f);
+  const float zp = fminf(fmaxf(round_half_away(div_full(-mn, scale)), 0.0f), 15.0f);
+  const float inv = div_full(1.0f, scale);
   uint32_t packed[E / 8 > 0 ? E / 8 : 1] = {};
 #pragma unroll
   for (int i = 0; i < E; ++i) {
-    float q = round_half_away(__fadd_rn(__fmul_rn(x[i], inv), zp));
+    float q = round_half_away(__fmaf_rn(x[i], inv, zp));
     q = fminf(fmaxf(q, 0.0f), 15.0f);
     packed[i / 8] |= (static_cast<uint32_t>(q) & 0xFu) << (4 * (i % 8));
   }
@@ -89,11 +100,11 @@ __device__ __forceinline__ void quant_store_int8(const float (&x)[E], uint8_t* c
 #pragma unroll
   for (int i = 0; i < E; ++i) am = fmaxf(am, fabsf(x[i]));
   am = warp_max(am);
-  const float scale = fmaxf(__fdiv_rn(am, 127.0f), 1e-6f);
+  const float scale = fmaxf(div_full(am, 127.0f), 1e-6f);
   uint32_t words[E / 4] = {};
 #pragma unroll
   for (int i = 0; i < E; ++i) {
-    float q = round_half_away(__fdiv_rn(x[i], scale));
+    float q = round_half_away(div_full(x[i], scale));
     q = fminf(fmaxf(q, -127.0f), 127.0f);
     words[i / 4] |= (static_cast<uint32_t>(static_cast<int>(q)) & 0xFFu) << (8 * (i % 4));
   }
