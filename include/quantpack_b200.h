@@ -144,7 +144,10 @@ int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_
  * partials (qp_decode_workspace_bytes) exceed it return QP_ERR_WORKSPACE. The first call on a device looks the array
  * up (cudaGetSymbolAddress) with that device current: make it before any stream capture. All calls on a device share
  * the array and it keeps the last call's contents (nothing in it needs to start at zero); calls that overlap on the
- * GPU race on it, so serialize them. Allocates nothing. No counterpart in the reference. */
+ * GPU race on it, so serialize them. The array holds the split partials and the prepared query rows. Only out_mode 0
+ * and 1 are served (QP_ERR_INVALID for 2: the partials would stay where no caller can reach them), and the keys are
+ * taken as the sequence's last ones (tokens_after_keys 0): a single-GPU decode, not a rank of a sequence split.
+ * Allocates nothing. No counterpart in the reference. */
 int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head,
                            void* out, int64_t out_stride_token, int64_t out_stride_head, int64_t num_q_tokens,
                            int num_seqs, const int32_t* cu_seqlens_q, const int32_t* seqused_k, int max_seqlen_q,
