@@ -311,6 +311,49 @@ def relerr(o, ref):
     return float(np.linalg.norm(o - ref) / np.linalg.norm(ref))
 
 
+def check_store_agreement(got, want, layout, max_code_frac=0.01):
+    """Compare cache bytes `got` written by a store that divides like the reference's COMPILED store (Triton lowers
+    the fp32 `/` of `k8v4_ops.py:33-63` to PTX div.full.f32, within 2 ulp of the IEEE quotient, and fuses
+    v * (1 / scale) + zp into one FMA) with `want`, this module's IEEE fp32 restatement of the same source. A scale
+    may differ by a couple of ulp in any cell; a code moves only where its quotient sits next to a rounding tie.
+    Raises AssertionError unless every code is within one step, every scale within 2 ulp (int4: the word with its
+    zero-point bits masked within 2 x 16, the zero point within 1) and at most `max_code_frac` of the codes differ.
+    Returns (cells that differ, codes that differ)."""
+    hs, cell = layout.head_size, layout.cell
+    kb = hs if layout.fmt == "k8v4" else hs // 2
+    g = np.asarray(got, np.uint8).reshape(-1, cell)
+    w = np.asarray(want, np.uint8).reshape(-1, cell)
+
+    def nibbles(x):
+        return np.concatenate([(x & 0xF).astype(np.int16), (x >> 4).astype(np.int16)], axis=1)
+
+    def words(x, at):
+        return x[:, at:at + 4].copy().view(np.uint32)[:, 0].astype(np.int64)
+
+    def scale_word(at, what):
+        gw, ww = words(g, at), words(w, at)
+        if layout.fmt == "k8v4" and at == kb:
+            assert np.abs(gw - ww).max(initial=0) <= 2, f"a {what} scale moved by more than 2 ulp"
+            return
+        assert np.abs((gw & ~0xF) - (ww & ~0xF)).max(initial=0) <= 32, f"a {what} scale moved by more than 2 ulp"
+        assert np.abs((gw & 0xF) - (ww & 0xF)).max(initial=0) <= 1, f"a {what} zero point moved by more than one"
+
+    if layout.fmt == "k8v4":
+        dk = np.abs(g[:, :kb].view(np.int8).astype(np.int16) - w[:, :kb].view(np.int8).astype(np.int16))
+    else:
+        dk = np.abs(nibbles(g[:, :kb]) - nibbles(w[:, :kb]))
+    assert dk.max(initial=0) <= 1, "a key code moved by more than one step"
+    scale_word(kb, "key")
+    v0 = kb + 4
+    dv = np.abs(nibbles(g[:, v0:v0 + hs // 2]) - nibbles(w[:, v0:v0 + hs // 2]))
+    assert dv.max(initial=0) <= 1, "a value code moved by more than one step"
+    scale_word(v0 + hs // 2, "value")
+    codes = int((dk != 0).sum() + (dv != 0).sum())
+    total = dk.size + dv.size
+    assert codes <= max_code_frac * total, f"{codes} of {total} codes differ"
+    return int((g != w).any(axis=1).sum()), codes
+
+
 # ---------------------------------------------------------------------------------------------------- inputs
 
 

@@ -156,12 +156,13 @@ def test_decode_workspace_bound_covers_every_batch(monkeypatch):
     monkeypatch.delenv("VLLM_QUANTPACK_INT4_DECODE", raising=False)
     from vllm_quantpack_b200 import _lib
     lib = _lib.load()
-    bound = int4_kv.decode_workspace_bound(64, NQ, NKV, 262144, 148)
-    for seqs in (1, 2, 5, 16, 64):
-        tokens = min(64, 4 * seqs)
-        need = lib.qp_decode_workspace_bytes(tokens, NQ, HS, lib.qp_decode_num_splits(seqs, NKV, 262144, 148))
-        assert need <= bound
-    assert bound < 64 << 20   # a few tens of MB, not the 1024-split worst case
+    for nq, nkv, hs in ((NQ, NKV, HS), (16, 2, 512)):
+        bound = int4_kv.decode_workspace_bound(64, nq, nkv, 262144, 148, hs)
+        for seqs in (1, 2, 5, 16, 64):
+            tokens = min(64, 4 * seqs)
+            need = lib.qp_decode_workspace_bytes(tokens, nq, hs, lib.qp_decode_num_splits(seqs, nkv, 262144, 148))
+            assert need <= bound
+        assert bound < hs << 18   # tens of MB (64 MB at head 256), not the 1024-split worst case
 
 
 # ---------------------------------------------------------------- k8v4 page cell and views
@@ -241,15 +242,15 @@ class Recorder:
         return out
 
 
-def _step(qlens, used, window=(-1, -1), dtype=torch.float32):
+def _step(qlens, used, window=(-1, -1), dtype=torch.float32, nq=NQ, nkv=NKV, hs=HS):
     T = sum(qlens)
     cu = torch.tensor([0] + list(torch.tensor(qlens).cumsum(0)), dtype=torch.int32)
-    q = torch.randn((T + 3, NQ, HS), dtype=dtype)   # 3 padding rows past cu[-1] stay untouched
+    q = torch.randn((T + 3, nq, hs), dtype=dtype)   # 3 padding rows past cu[-1] stay untouched
     out = torch.full_like(q, -7.0)
     table = torch.tensor([[i + 1] + [0] * 3 for i in range(len(qlens))], dtype=torch.int32)
-    kc = torch.zeros((4, 16, NKV, HS // 2 + 4), dtype=torch.uint8)
+    kc = torch.zeros((4, 16, nkv, hs // 2 + 4), dtype=torch.uint8)
     args = dict(cu_seqlens_q=cu, max_seqlen_q=max(qlens), seqused_k=torch.tensor(used, dtype=torch.int32),
-                max_seqlen_k=max(used), softmax_scale=HS ** -0.5, window_size=window, block_table=table,
+                max_seqlen_k=max(used), softmax_scale=hs ** -0.5, window_size=window, block_table=table,
                 softcap=0.0, sinks=None, alibi_slopes=None, use_alibi_sqrt=False, qq_bias=None, output_scale=None,
                 mm_prefix_range=None, k_scale_cache=None, v_scale_cache=None, seq_threshold_3D=32,
                 num_par_softmax_segments=64, softmax_segm_output=None, softmax_segm_max=None,
@@ -302,6 +303,26 @@ def test_unsupported_features_go_to_the_stock_path(monkeypatch):
     q, kc, out, args = _step([4], [5000])
     fn(q, kc, kc, out, **dict(args, softcap=30.0))
     assert not rec.calls and len(stock_calls) == 2
+
+
+def test_head_512_is_served_and_other_head_sizes_go_stock(monkeypatch):
+    """Gemma 4 global layers (16 query heads over 2 KV heads, head 512): decodes of up to 4 tokens (32 rows) and
+    prefill chunks run on the B200 kernels; a head size the kernels lack (128) stays on the stock int4 path."""
+    rec = Recorder(monkeypatch)
+    stock, stock_calls = _stock_recorder()
+    fn = int4_kv.make_unified_attention(stock)
+    q, kc, out, args = _step([4, 1], [16384, 700], nq=16, nkv=2, hs=512)
+    fn(q, kc, kc, out, **args)
+    assert rec.calls == [("decode", q.shape[0], [0, 4, 5], [16384, 700], 4, None)] and not stock_calls
+    rec.calls.clear()
+    q, kc, out, args = _step([256, 2], [40000, 9000], nq=16, nkv=2, hs=512)
+    fn(q, kc, kc, out, **args)
+    assert ("prefill", 256, 40000) in rec.calls and ("decode", 2, [0, 2], [9000], 2, None) in rec.calls
+    assert not stock_calls
+    rec.calls.clear()
+    q, kc, out, args = _step([4], [5000], hs=128)
+    fn(q, kc, kc, out, **args)
+    assert not rec.calls and len(stock_calls) == 1
 
 
 def test_prefill_routing_off_sends_chunks_to_stock(monkeypatch):

@@ -11,8 +11,9 @@ copy of vLLM's Triton kernel and launcher; this module instead replaces the stoc
   reshape_and_cache_int4   fused RHT + quantize + pack store, int4 and k8v4 (k8v4_kv.py:152-163)
   single_rht               the transform both of the above apply, so any stock path left in use stays consistent
 
-Calls the B200 path does not cover (sliding window, softcap, sinks, ALiBi, qq_bias, FP8 output, mm_prefix ranges, a
-head size other than 256) go to the stock `unified_attention_int4`, unchanged. The stock `_launch_packed_attn` is
+Head sizes 256 and 512 (Gemma 4's global layers, int4_kv.py:302-305) are served. Calls the B200 path does not cover
+(sliding window, softcap, sinks, ALiBi, qq_bias, FP8 output, mm_prefix ranges, another head size) go to the stock
+`unified_attention_int4`, unchanged, for an int4 cache, and raise for a k8v4 cache (no stock kernel reads it). The stock `_launch_packed_attn` is
 left in place: only that stock path reaches it. The same environment switches are honoured:
 VLLM_QUANTPACK_INT4_KV=0 (no patch), VLLM_QUANTPACK_INT4_FA_PREFILL=0 (prefill chunks stay stock),
 VLLM_QUANTPACK_INT4_DECODE="tile,warps,segments[,rows]" (segments: split count of the decode, "auto" = per call),
@@ -28,7 +29,7 @@ MODULE = "vllm.v1.attention.ops.int4_per_token_head"
 PACKED_DTYPES = ("int4_per_token_head", "k8v4_per_token_head")   # caches served by the B200 kernels
 MAX_Q_SPLIT_KV = 4               # MTP / EAGLE verification with up to 3 draft tokens
 MAX_DECODE_ROWS = 32             # query tokens x query heads per KV head one decode CTA holds
-HEAD_SIZE = 256                  # the attention kernels' head size
+HEAD_SIZES = (256, 512)          # head sizes of the attention kernels
 PREFILL_TILES_DEFAULT = (128, 64, 10, 1)   # (BLOCK_M, TILE, warps, CTAs per SM) of the tcgen05 prefill kernel
 DECODE_TILES_DEFAULT = (64, 4, "auto")
 DECODE_MAX_M = 32
@@ -75,7 +76,7 @@ def decode_splits_override():
 def _plain(q, window_size, softcap, sinks, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
     """True when the call uses no feature outside the B200 kernels (int4_kv.py:304-305)."""
     return (window_size is None or window_size[0] < 0) and not softcap and sinks is None and alibi_slopes is None \
-        and qq_bias is None and output_scale is None and mm_prefix_range is None and q.shape[2] == HEAD_SIZE
+        and qq_bias is None and output_scale is None and mm_prefix_range is None and q.shape[2] in HEAD_SIZES
 
 
 def _forward_step():
@@ -183,7 +184,7 @@ def make_unified_attention(stock_unified, prefill_on=True):
             if k8v4_kv.is_k8v4(k_cache):
                 raise NotImplementedError(
                     f"{k8v4_kv.NAME}: sliding window, softcap, sinks, ALiBi, qq_bias, FP8 output, mm_prefix ranges and "
-                    f"head sizes other than {HEAD_SIZE} are not served by the B200 kernels, and vLLM's stock int4 "
+                    f"head sizes other than {HEAD_SIZES} are not served by the B200 kernels, and vLLM's stock int4 "
                     f"kernel cannot read a k8v4 cache")
             return stock_unified(q, k_cache, v_cache, out, **args)
         group = q.shape[1] // k_cache.shape[2]
@@ -353,12 +354,16 @@ def reserve_decode_workspace(builder, vllm_config, device):
         nq = int(model.get_num_attention_heads(vllm_config.parallel_config))
         nkv = int(model.get_num_kv_heads(vllm_config.parallel_config))
         max_len = int(getattr(model, "max_model_len", 1 << 20))
-        ops.workspace(device, decode_workspace_bound(rows, nq, nkv, max_len, ops.sm_count(device)))
+        try:
+            head = int(model.get_head_size())
+        except Exception:
+            head = max(HEAD_SIZES)
+        ops.workspace(device, decode_workspace_bound(rows, nq, nkv, max_len, ops.sm_count(device), head))
     except Exception:
         pass
 
 
-def decode_workspace_bound(max_tokens, num_q_heads, num_kv_heads, max_seqlen_k, sms):
+def decode_workspace_bound(max_tokens, num_q_heads, num_kv_heads, max_seqlen_k, sms, head_size=max(HEAD_SIZES)):
     """Largest decode workspace (bytes) a batch of at most `max_tokens` query tokens can need: over every batch size,
     the tokens it can hold times the split count the library (or the environment) gives it."""
     from .. import _lib
@@ -368,5 +373,5 @@ def decode_workspace_bound(max_tokens, num_q_heads, num_kv_heads, max_seqlen_k, 
     for seqs in range(1, max(1, max_tokens) + 1):
         splits = fixed or lib.qp_decode_num_splits(seqs, num_kv_heads, max_seqlen_k, sms)
         tokens = min(max_tokens, MAX_Q_SPLIT_KV * seqs)
-        worst = max(worst, lib.qp_decode_workspace_bytes(tokens, num_q_heads, HEAD_SIZE, splits))
+        worst = max(worst, lib.qp_decode_workspace_bytes(tokens, num_q_heads, head_size, splits))
     return worst

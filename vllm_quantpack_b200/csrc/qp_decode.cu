@@ -1,6 +1,8 @@
 // K1: split-KV paged decode over an int4_per_token_head / k8v4_per_token_head cache, up to 32 query rows
-//     (qlen x query heads per KV head) per KV head, on the 5th-generation tensor cores (tcgen05 + TMEM); K0q: the
-//     query preparation it reads; K2: log-sum-exp merge of the segments with the inverse RHT fused in.
+//     (qlen x query heads per KV head) per KV head, head size 256 or 512, on the 5th-generation tensor cores
+//     (tcgen05 + TMEM); K0q: the query preparation it reads; K2: log-sum-exp merge of the segments with the inverse
+//     RHT fused in. At head 512 the same kernel also serves chunk prefill, as decodes of a few query tokens each
+//     over the chunk's causal prefixes (qp_prefill).
 //
 // Reference behaviour (what this computes, not how): the split-KV 3D path of vLLM's int4 kernel as the plugin
 // configures it (vllm_quantpack/attention/int4_kv.py:98-122: every query token of a step in one program, segments
@@ -12,22 +14,25 @@
 // are thin (N = 32). A thin MMA runs at the tensor pipe's full rate only when its wide operand comes from TMEM
 // (measured on this part: M 128 x N 32 x K 16 in 16 cycles with A in TMEM, 40 with A in shared memory, whose
 // bandwidth the A operand then saturates). So the keys are the M dimension and both cache operands live in TMEM:
-//   S^T (128 keys x N rows)     = K_op (TMEM, 128 keys x 256 channels)       x Q^T  (shared memory, N x 256)
-//   O^T (2 x 128 channels x N)  = V^T_op (TMEM, 2 x 128 channels x 128 keys)  x P^T  (shared memory, N x 128)
+//   S^T (128 keys x N rows)          = K_op (TMEM, 128 keys x HS channels)          x Q^T (shared memory, N x HS)
+//   O^T (HS/128 x 128 channels x N)  = V^T_op (TMEM, HS/128 x 128 channels x keys)  x P^T (shared memory, N x keys)
 // One CTA of 14 warps per SM (it holds all 512 TMEM columns) per (split, KV head, sequence):
 //   warp 0      producer: 1-D bulk copies (TMA engine, no tensor map, no multicast) of the tile's raw cells, whole
-//               16-token groups, into a ring of raw stages;
-//   warp 1      MMA issuer (convergent; elect.sync picks the lane): 16 QK MMAs per tile into a double-buffered S,
-//               then the previous tile's 16 PV MMAs, each group finished with tcgen05.commit onto mbarriers;
-//   warps 2-5   key operand: thread = key = TMEM lane; one lop3 turns two nibbles into the fp16 pair 1024 + u (the
-//               odd channel 1024 + 16 u; its query channel carries 1/16), the bias Q.1024 is a per-row constant
-//               removed from the score; k8v4 codes become 1152 + c by one prmt. The key / value scales go to
-//               shared memory for the softmax, the value zero points as paired fp16 operand biases;
+//               16-token groups, into a ring of raw stages (a stage holds the tile, or at head 512 half of it);
+//   warp 1      MMA issuer (convergent; elect.sync picks the lane): HS/16 QK MMAs per tile into a double-buffered S,
+//               then the previous tile's PV MMAs, each group finished with tcgen05.commit onto mbarriers;
+//   warps 2-5   key operand: thread = key = TMEM lane; lop3 + one fp16 add (or fma) per channel pair gives the exact
+//               fp16 (u - zp) of two channels; k8v4 codes become 1152 + c by one prmt, minus 1152. The operand is
+//               written in 256-channel chunks (128 TMEM columns) into a ring of two chunk slots (one at head 512
+//               with 32 rows, where TMEM has no room for two), so the conversion of one chunk overlaps the MMAs of
+//               the other. The key / value scales go to shared memory for the softmax, the value zero points as
+//               paired fp16 operand biases;
 //   warps 6-9   value operand: V^T written with tcgen05.st.16x256b, whose thread layout (lanes i/4 and 8 + i/4,
 //               column pair 2(i%4)) puts one channel of four consecutive keys in each thread: one 32-bit word of
 //               each of four keys, interleaved by prmt, becomes the exact fp16 (u - zp) of every (channel, key).
-//               The zero point sits in the operand, so the running O accumulator only holds the signal; two 64-key
-//               slots let the conversion of one half overlap the MMAs of the other;
+//               The zero point sits in the operand, so the running O accumulator only holds the signal; two value
+//               slots (64 keys at head 256; 32 at head 512, where O^T takes four channel tiles) let the conversion
+//               of one slot overlap the MMAs of the other;
 //   warps 10-13 softmax: thread = key; scores in log2 units from S^T, a lazy per-row maximum (P may reach 2^8
 //               before O is rescaled, which happens in TMEM and rarely), P x value scale in fp16 with a running
 //               power-of-two range written as P^T; per-thread row sums reduced once at the end; the epilogue reads
@@ -44,7 +49,6 @@
 
 namespace qp {
 
-constexpr int DEC_HS = 256;
 constexpr int DEC_TILE = 128;  // keys per tile (TMEM lanes of the QK accumulator)
 constexpr int DEC_MAX_ROWS = 32;
 #ifndef QP_DEC_SMX_HALVES
@@ -59,14 +63,11 @@ constexpr int DEC_REGS = (16384 / (32 * ((DEC_WARPS + 3) / 4))) & ~7;
 // warp 0 producer, 1 MMA issuer, 2-5 key operand, 6-9 value operand, 10.. softmax (SMX_HALVES per lane quarter)
 constexpr int W_MMA = 1, W_VAL = 6, W_SMX = 10;
 constexpr int SMX_THREADS = 32 * (DEC_WARPS - W_SMX);
-constexpr int Q_REC = DEC_HS * 2 + 16;  // prepared query row: 256 fp16 in operand order, then 4 fp32
+// prepared query row: HS fp16 in operand order, then 4 fp32 (row scale, three zero words)
+constexpr int q_rec_bytes(int hs) { return hs * 2 + 16; }
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float RESCALE_SLACK = 8.f;
 constexpr int BAR_SMX = 1;  // named barrier of the softmax warps
-
-// TMEM columns (512): key operand double-buffered at [0, 128) and [384, 512); value operand slots (64 keys each,
-// two channel halves of 32 columns) at [128, 256); S double-buffered and O (two channel halves) after it.
-constexpr uint32_t TM_AK0 = 0, TM_AK1 = 384, TM_AV = 128, TM_S = 256;
 
 struct DecodeParams {
   const void* q;
@@ -82,55 +83,88 @@ struct DecodeParams {
   float qk_scale;      // softmax_scale / head_size * log2(e)
   const uint32_t* sign_bits;
   int q_rotated;        // q already in the RHT domain
-  const uint8_t* qrec;  // prepared query rows: [kv head][token][query head of the group] x Q_REC bytes
+  const uint8_t* qrec;  // prepared query rows: [kv head][token][query head of the group] x q_rec_bytes(HS)
   int64_t num_tokens;
-  int tokens_after;  // sequence tokens after this call's keys (held by other ranks), clamped to max_seqlen_q
+  int tokens_after;  // sequence tokens after this call's keys (held by other ranks), clamped to the query tokens
+  // chunk_q > 0: the num_tokens query tokens are ONE sequence's chunk (its last positions, causal among themselves)
+  // over chunk_n cached keys through block-table row 0, served as sub-sequences of chunk_q tokens (grid z), each
+  // reading only the keys its last token sees. cu_seqlens_q / seqused_k are not read.
+  int chunk_q, chunk_n;
   int num_splits;
   float* part_o;    // [tokens][nq][splits][HS]
   float* part_lse;  // [tokens][nq][splits], log2 units
 };
 
-template <int FMT>
+template <int FMT, int HS>
 struct Cell {
-  static constexpr int KB = FMT == FMT_INT4 ? DEC_HS / 2 : DEC_HS;  // key bytes
-  static constexpr int BYTES = KB + 8 + DEC_HS / 2;
-  static constexpr int KS = KB, V = KB + 4, VS = KB + 4 + DEC_HS / 2;  // field offsets
+  static constexpr int KB = FMT == FMT_INT4 ? HS / 2 : HS;  // key bytes
+  static constexpr int BYTES = KB + 8 + HS / 2;
+  static constexpr int KS = KB, V = KB + 4, VS = KB + 4 + HS / 2;  // field offsets
 };
 
-template <int FMT, int NR>
+// TMEM columns (512) of the head size's operands and accumulators.
+//   HS 256: key operand chunks at [0, 128) and [384, 512); two 64-key value slots (two channel tiles of 32 columns)
+//           at [128, 256); S (2 x NR) and O^T (2 channel tiles x NR) from 256.
+//   HS 512: key operand chunks (channels 0-255, then 256-511 of a tile) in AKS slots of 128 columns from 0; two
+//           32-key value slots (four channel tiles of 16 columns) after them; S and O^T (4 channel tiles x NR) last.
+//           At NR 32 only one key slot fits (448 columns; with two, the value slots would hold 16 keys, and the
+//           value warps could then release a raw stage only after the PV MMAs of its tile started, which the
+//           three-stage k8v4 ring cannot wait for: the next tile's QK needs two fresh stages first).
+template <int HS, int NR>
+struct DecTmem {
+  static constexpr int NCH = HS / 256;                       // key operand chunks per tile
+  static constexpr int MT = HS / 128;                        // channel tiles of V^T and O^T
+  static constexpr int AKS = (HS == 256 || NR <= 16) ? 2 : 1;  // key operand chunk slots
+  static constexpr int VK = HS == 256 ? 64 : 32;             // keys per value slot
+  static constexpr int VSLOTS = DEC_TILE / VK;               // value slots per tile
+  static constexpr int SLOT = MT * VK / 2;                   // TMEM columns of a value slot
+  static constexpr uint32_t AK0 = 0, AK1 = HS == 256 ? 384 : 128;
+  static constexpr uint32_t AV = HS == 256 ? 128 : 128 * AKS;
+  static constexpr uint32_t S = AV + 2 * SLOT;
+  static constexpr uint32_t O = S + 2 * NR;  // channel tile t at O + NR t
+  static_assert(HS == 256 || HS == 512, "head size 256 or 512");
+  static_assert(O + MT * NR <= (HS == 256 ? AK1 : 512u), "TMEM columns overlap");
+  static_assert(VK % 16 == 0 && DEC_TILE % VK == 0, "value slots of whole 16-key blocks");
+};
+
+template <int FMT, int HS, int NR>
 struct DecSmem {
-  static constexpr int CELL = Cell<FMT>::BYTES;
-  static constexpr int RS = FMT == FMT_INT4 ? 4 : 3;  // raw stages
-  static constexpr int RAW = DEC_TILE * CELL;
+  static constexpr int CELL = Cell<FMT, HS>::BYTES;
+  static constexpr int SK = HS == 256 ? DEC_TILE : DEC_TILE / 2;  // keys per raw stage
+  static constexpr int SPT = DEC_TILE / SK;                        // raw stages per tile
+  static constexpr int RS = FMT == FMT_INT4 ? 4 : 3;               // raw stages
+  static constexpr int KPS = HS == 256 ? RS : 3;                   // tiles of key / value scales in flight
+  static constexpr int RAW = SK * CELL;
   static constexpr int ATOM = NR * 128;  // one 64-element column of 128B-swizzle atoms over the NR rows
-  static constexpr int OFF_Q = 0;                          // Q: 4 atoms (256 channels), K-major
-  static constexpr int OFF_P = OFF_Q + 4 * ATOM;           // P^T: 2 buffers x 2 atoms (128 keys), K-major
+  static constexpr int OFF_Q = 0;                          // Q: HS / 64 atoms, K-major
+  static constexpr int OFF_P = OFF_Q + HS / 64 * ATOM;     // P^T: 2 buffers x 2 atoms (128 keys), K-major
   static constexpr int OFF_RAW = OFF_P + 4 * ATOM;         // RS raw stages
-  static constexpr int OFF_KP = OFF_RAW + RS * RAW;        // [RS][128] float4: key scale, key zp, value scale
-  static constexpr int OFF_ZB = OFF_KP + RS * 128 * 16;    // [RS][128] u32: paired value zero-point operand biases
-  static constexpr int OFF_RP = OFF_ZB + RS * 128 * 4;      // [2][NR] float2: row scale, row maximum
+  static constexpr int OFF_KP = OFF_RAW + RS * RAW;        // [KPS][128] float4: key scale, key zp, value scale
+  static constexpr int OFF_ZB = OFF_KP + KPS * 128 * 16;   // [KPS][128] u32: paired value zero-point operand biases
+  static constexpr int OFF_RP = OFF_ZB + KPS * 128 * 4;    // [2][NR] float2: row scale, row maximum
   static constexpr int OFF_LIM = OFF_RP + 2 * NR * 8;      // [NR] int: last key the row sees
-  // [NR][4] (unused), [8] value-scale maxima, [NR] O factors, [NR] float2 (row-sum factor, exp-argument shift)
+  // [8] value-scale maxima, [NR] O factors, [NR] float2 (row-sum factor, exp-argument shift)
   static constexpr int OFF_RED = OFF_LIM + NR * 4;
-  static constexpr int OFF_SB = (OFF_RED + (NR * 4 + 8 + NR + 2 * NR) * 4 + 15) / 16 * 16;  // [NR][128] f32 scores
+  static constexpr int OFF_SB = (OFF_RED + (8 + NR + 2 * NR) * 4 + 15) / 16 * 16;  // [NR][128] f32 scores
   static constexpr int OFF_BAR = OFF_SB + NR * 128 * 4;
   static constexpr int NBAR = 40;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_TMEM + 16;
   static_assert(BYTES <= 232448, "dynamic shared memory above the 227 KB a CTA may hold");
   static_assert(RAW % 16 == 0 && OFF_RAW % 1024 == 0, "bulk copy destinations must be 16-byte aligned");
+  static_assert(RS <= 4 && KPS <= 4, "barrier slots");
 };
 
 // barrier slots
 enum {
   D_RAW_FULL = 0,    // [RS <= 4] a raw stage landed
-  D_RAW_EMPTY = 4,   // [RS] key and value warps are done with it (8 arrivals)
+  D_RAW_EMPTY = 4,   // [RS] the key warps of its keys and the value warps are done with it
   D_Q_FULL = 8,      // Q^T is in shared memory (every softmax warp)
-  D_AK_FULL = 9,     // [2] key operand in TMEM (4 key warps)
+  D_AK_FULL = 9,     // [2] key operand chunk in TMEM (4 key warps)
   D_AK_FREE = 11,    // [2] its QK MMAs completed (commit)
-  D_KP_FULL = 13,    // [RS] the stage's scales and zero-point biases are in shared memory (4 key warps)
-  D_KP_FREE = 17,    // [RS] the softmax and the value warps read them
-  D_AV_FULL = 21,    // [2] value operand slot (64 keys) in TMEM (4 value warps)
+  D_KP_FULL = 13,    // [KPS <= 4] the tile's scales and zero-point biases are in shared memory (4 key warps)
+  D_KP_FREE = 17,    // [KPS] the softmax and the value warps read them
+  D_AV_FULL = 21,    // [2] value operand slot in TMEM (4 value warps)
   D_AV_FREE = 23,    // [2] its PV MMAs completed (commit)
   D_S_FULL = 25,     // [2] S^T of the tile is in TMEM (commit)
   D_S_FREE = 27,     // [2] the softmax read it (every softmax warp)
@@ -159,7 +193,7 @@ __device__ __forceinline__ void tmem_st_rows(uint32_t taddr, const float (&v)[NR
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// k index (0..255) of the QK operand that carries channel c. int4: column j = 4 w + m of a key's TMEM lane holds
+// k index (0..HS-1) of the QK operand that carries channel c. int4: column j = 4 w + m of a key's TMEM lane holds
 // the pair lop3'd from word w (shifted right 8 for m >= 2; low nibbles for even m, high for odd), i.e. channels
 // 8 w + m (low half) and 8 w + m + 4 (high half); k8v4: the natural order (prmt takes bytes 0, 1 then 2, 3).
 template <int FMT>
@@ -169,34 +203,35 @@ __host__ __device__ __forceinline__ int qk_k_of_channel(int c) {
 }
 
 // ---------------------------------------------------------------------------------------------------- K0q
-// One warp per (query token, query head): the row as K1 reads it (Q_REC bytes): 256 fp16 in the k order of the QK
-// operand, scaled by a power of two (|q| < 2^14); then the fp32 row scale A (softmax_scale / head x log2 e x
+// One warp per (query token, query head): the row as K1 reads it (q_rec_bytes(HS)): HS fp16 in the k order of the
+// QK operand, scaled by a power of two (|q| < 2^14); then the fp32 row scale A (softmax_scale / head x log2 e x
 // 2^-exponent) and three zero words. Written once per call; every split of the row's KV head reads it.
-template <int FMT, int DT>
+template <int FMT, int DT, int HS>
 __global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_t q_st, int64_t q_sh, int64_t T,
                                                            int nq, int nkv, const uint32_t* sign_bits, int q_rotated,
                                                            float qk_scale, uint8_t* qrec) {
   asm volatile("griddepcontrol.launch_dependents;");
   using EL = Elem<DT>;
+  constexpr int E = HS / 32;  // elements per lane
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= T * nq) return;
   const int64_t tok = row / nq;
   const int qh = static_cast<int>(row % nq);
   const int group = nq / nkv, kvh = qh / group, hg = qh % group;
-  uint8_t* rec = qrec + ((static_cast<int64_t>(kvh) * T + tok) * group + hg) * Q_REC;
+  uint8_t* rec = qrec + ((static_cast<int64_t>(kvh) * T + tok) * group + hg) * q_rec_bytes(HS);
   __half* qrow = reinterpret_cast<__half*>(rec);
-  const typename EL::T* src = reinterpret_cast<const typename EL::T*>(q) + tok * q_st + qh * q_sh + lane * 8;
-  float x[8];
+  const typename EL::T* src = reinterpret_cast<const typename EL::T*>(q) + tok * q_st + qh * q_sh + lane * E;
+  float x[E];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) x[i] = EL::to_f(src[i]);
+  for (int i = 0; i < E; ++i) x[i] = EL::to_f(src[i]);
   if (!q_rotated) {
-    apply_signs<8>(x, sign_bits, lane);
-    warp_wht<8>(x, lane);
+    apply_signs<E>(x, sign_bits, lane);
+    warp_wht<E>(x, lane);
   }
   float am = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(x[i]));
+  for (int i = 0; i < E; ++i) am = fmaxf(am, fabsf(x[i]));
   am = warp_max(am);
   int ex = 0;
   if (am > 0.f) {
@@ -204,21 +239,23 @@ __global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_
     ex = 14 - ex;     // am * 2^ex in [2^13, 2^14)
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) qrow[qk_k_of_channel<FMT>(lane * 8 + i)] = __float2half_rn(ldexpf(x[i], ex));
+  for (int i = 0; i < E; ++i) qrow[qk_k_of_channel<FMT>(lane * E + i)] = __float2half_rn(ldexpf(x[i], ex));
   if (lane == 0) {
-    float* rc = reinterpret_cast<float*>(rec + 2 * DEC_HS);
+    float* rc = reinterpret_cast<float*>(rec + 2 * HS);
     rc[0] = ldexpf(qk_scale, -ex);
     rc[1] = rc[2] = rc[3] = 0.f;
   }
 }
 
 // ---------------------------------------------------------------------------------------------------- K1
-template <int FMT, int DT, int NR, int RL>
+template <int FMT, int DT, int HS, int NR, int RL>
 __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
-  using SM = DecSmem<FMT, NR>;
-  using CL = Cell<FMT>;
-  constexpr int CELL = SM::CELL, RS = SM::RS;
-  constexpr uint32_t TM_O = TM_S + 2 * NR;  // O^T channel half c at TM_O + NR c
+  using SM = DecSmem<FMT, HS, NR>;
+  using CL = Cell<FMT, HS>;
+  using TM = DecTmem<HS, NR>;
+  constexpr int CELL = SM::CELL, RS = SM::RS, KPS = SM::KPS, SK = SM::SK, SPT = SM::SPT;
+  constexpr int NCH = TM::NCH, MT = TM::MT, VK = TM::VK, VSLOTS = TM::VSLOTS, AKS = TM::AKS;
+  constexpr int QREC = q_rec_bytes(HS);
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::OFF_TMEM);
@@ -229,9 +266,23 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
   // grid's completion before reading anything.
   asm volatile("griddepcontrol.launch_dependents;");
 
-  const int q0 = p.cu_seqlens_q[seq];
-  const int qlen = p.cu_seqlens_q[seq + 1] - q0;
-  const int n = p.seqused_k[seq];
+  // the sequence's query tokens [q0, q0 + qlen), its keys [0, n), the last key its first token sees (before clamping
+  // to n - 1) and its block-table row
+  int q0, qlen, n, vis_base;
+  const int32_t* btab;
+  if (p.chunk_q > 0) {
+    q0 = seq * p.chunk_q;
+    qlen = min(p.chunk_q, static_cast<int>(p.num_tokens) - q0);
+    vis_base = p.chunk_n - static_cast<int>(p.num_tokens) + q0 + p.tokens_after;
+    n = min(p.chunk_n, vis_base + qlen);
+    btab = p.block_table;
+  } else {
+    q0 = p.cu_seqlens_q[seq];
+    qlen = p.cu_seqlens_q[seq + 1] - q0;
+    n = p.seqused_k[seq];
+    vis_base = n - qlen + p.tokens_after;
+    btab = p.block_table + static_cast<int64_t>(seq) * p.bt_stride;
+  }
   const int rows = qlen * p.group;
   if (qlen <= 0) return;
   const int n_tiles = (n + DEC_TILE - 1) / DEC_TILE;
@@ -249,7 +300,9 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
   if (tid == 0) {
     for (int s = 0; s < RS; ++s) {
       mbar_init(&bars[D_RAW_FULL + s], 1);
-      mbar_init(&bars[D_RAW_EMPTY + s], 8);
+      mbar_init(&bars[D_RAW_EMPTY + s], 4 / SPT + 4);  // the key warps of the stage's keys, every value warp
+    }
+    for (int s = 0; s < KPS; ++s) {
       mbar_init(&bars[D_KP_FULL + s], 4);
       mbar_init(&bars[D_KP_FREE + s], 4 + 4 * SMX_HALVES);
     }
@@ -280,24 +333,26 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
-    // Lane j copies 16-token group j of each tile (block_size % 16 == 0, so a group never crosses a block); its
-    // block-table entry is loaded one tile ahead, so the eight lookups of a tile are in flight together.
-    const int32_t* btab = p.block_table + static_cast<int64_t>(seq) * p.bt_stride;
+    // Fill u of the ring holds keys [(u % SPT) SK, + SK) of tile u / SPT. Lane j copies 16-token group j of it
+    // (block_size % 16 == 0, so a group never crosses a block); its block-table entry is loaded one fill ahead, so
+    // the lookups of a fill are in flight together. A fill past the context lands at once (no bytes expected).
     const uint8_t* head_base = p.cache + static_cast<int64_t>(kvh) * p.head_stride;
-    auto block_of = [&](int i) {
-      const int tok = (tile0 + i) * DEC_TILE + 16 * lane;
-      return (lane < DEC_TILE / 16 && i < ntl && tok < n) ? __ldg(btab + tok / p.block_size) : -1;
+    const int nu = ntl * SPT;
+    auto first_key = [&](int u) { return (tile0 + u / SPT) * DEC_TILE + (u % SPT) * SK; };
+    auto block_of = [&](int u) {
+      const int tok = first_key(u) + 16 * lane;
+      return (lane < SK / 16 && u < nu && tok < n) ? __ldg(btab + tok / p.block_size) : -1;
     };
     int next_blk = block_of(0);
-    int i = 0;
-    for (; i < ntl; ++i) {
-      const int stage = i % RS;
-      if (i >= RS && __any_sync(0xffffffffu, !mbar_wait_bounded(&bars[D_RAW_EMPTY + stage], ((i / RS) - 1) & 1)))
+    int u = 0;
+    for (; u < nu; ++u) {
+      const int stage = u % RS;
+      if (u >= RS && __any_sync(0xffffffffu, !mbar_wait_bounded(&bars[D_RAW_EMPTY + stage], ((u / RS) - 1) & 1)))
         break;
       const int blk = next_blk;
-      next_blk = block_of(i + 1);
-      const int tb = (tile0 + i) * DEC_TILE;
-      const int groups = (min(tb + DEC_TILE, n) - tb + 15) >> 4;
+      next_blk = block_of(u + 1);
+      const int tb = first_key(u);
+      const int groups = max(0, (min(tb + SK, n) - tb + 15) >> 4);
       if (lane == 0) mbar_arrive_expect_tx(&bars[D_RAW_FULL + stage], static_cast<uint32_t>(groups * 16 * CELL));
       __syncwarp();
       if (lane < groups) {
@@ -310,7 +365,7 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
     }
     // the copies in flight land before the CTA's shared memory can go away
     if (lane == 0)
-      for (int k = max(0, i - RS); k < i; ++k)
+      for (int k = max(0, u - RS); k < u; ++k)
         mbar_wait_bounded(&bars[D_RAW_FULL + k % RS], (k / RS) & 1, 100000000ull);
   } else if (warp == W_MMA) {
     // ------------------------------------------------------------------ MMA issuer
@@ -331,20 +386,23 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
       wait_all(&bars[D_P_FULL + bj], (j >> 1) & 1);
       const uint64_t pd = p_desc + static_cast<uint64_t>((2 * bj * SM::ATOM) >> 4);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < VSLOTS; ++h) {  // slot h: keys [h VK, h VK + VK) of the tile, TMEM slot k & 1
         if (failed) break;
-        wait_all(&bars[D_AV_FULL + h], j & 1);
+        const int k = j * VSLOTS + h, sl = k & 1;
+        wait_all(&bars[D_AV_FULL + sl], (k >> 1) & 1);
         if (failed) break;
         tc_fence_after();
         if (elect_one()) {
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < MT; ++c)
 #pragma unroll
-            for (int s = 0; s < 4; ++s)
-              umma_f16_ts(tmem + (TM_O + NR * c), tmem + (TM_AV + 64 * h + 32 * c + 8 * s),
-                          pd + static_cast<uint64_t>((h * SM::ATOM + 32 * s) >> 4), ID,
+            for (int s = 0; s < VK / 16; ++s) {
+              const int key = h * VK + 16 * s;  // P^T: 64 keys per atom
+              umma_f16_ts(tmem + (TM::O + NR * c), tmem + (TM::AV + TM::SLOT * sl + (VK / 2) * c + 8 * s),
+                          pd + static_cast<uint64_t>(((key >> 6) * SM::ATOM + (key & 63) * 2) >> 4), ID,
                           (h | s) ? 1u : static_cast<uint32_t>(j));
-          umma_commit(&bars[D_AV_FREE + h]);
+            }
+          umma_commit(&bars[D_AV_FREE + sl]);
         }
         __syncwarp();
       }
@@ -354,20 +412,27 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
     wait_all(&bars[D_Q_FULL], 0);
     for (int i = 0; i < ntl && !failed; ++i) {
       const int b = i & 1;
-      wait_all(&bars[D_AK_FULL + b], (i >> 1) & 1);
       if (i >= 2) wait_all(&bars[D_S_FREE + b], ((i - 2) >> 1) & 1);
-      if (failed) break;
-      tc_fence_after();
-      const uint32_t ak = tmem + (b ? TM_AK1 : TM_AK0), sd = tmem + TM_S + NR * b;
-      if (elect_one()) {
+      const uint32_t sd = tmem + TM::S + NR * b;
 #pragma unroll
-        for (int s = 0; s < 16; ++s)
-          umma_f16_ts(sd, ak + 8 * s, q_desc + static_cast<uint64_t>(((s >> 2) * SM::ATOM + (s & 3) * 32) >> 4), ID,
-                      s ? 1u : 0u);
-        umma_commit(&bars[D_AK_FREE + b]);
-        umma_commit(&bars[D_S_FULL + b]);
+      for (int ch = 0; ch < NCH; ++ch) {  // key operand chunk ch: channels [256 ch, 256 ch + 256), slot k % AKS
+        const int k = i * NCH + ch, sl = k % AKS;
+        wait_all(&bars[D_AK_FULL + sl], (k / AKS) & 1);
+        if (failed) break;
+        tc_fence_after();
+        const uint32_t ak = tmem + (sl ? TM::AK1 : TM::AK0);
+        if (elect_one()) {
+#pragma unroll
+          for (int s = 0; s < 16; ++s)
+            umma_f16_ts(sd, ak + 8 * s,
+                        q_desc + static_cast<uint64_t>(((4 * ch + (s >> 2)) * SM::ATOM + (s & 3) * 32) >> 4), ID,
+                        (ch | s) ? 1u : 0u);
+          umma_commit(&bars[D_AK_FREE + sl]);
+          if (ch == NCH - 1) umma_commit(&bars[D_S_FULL + b]);
+        }
+        __syncwarp();
       }
-      __syncwarp();
+      if (failed) break;
       if (i >= 1) issue_pv(i - 1);
     }
     if (!failed) issue_pv(ntl - 1);
@@ -377,20 +442,19 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
   } else if (warp < W_VAL) {
     // ------------------------------------------------------------------ key operand (thread = key = TMEM lane)
     const int q = warp & 3, kl = 32 * q + lane;
+    const int part = q / (4 / SPT);  // the raw stage of this warp's keys within the tile
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
     float4* kp = reinterpret_cast<float4*>(smem + SM::OFF_KP);
     uint32_t* zb = reinterpret_cast<uint32_t*>(smem + SM::OFF_ZB);
     for (int i = 0; i < ntl; ++i) {
-      const int stage = i % RS, b = i & 1;
-      bool ok = mbar_wait_spin(&bars[D_RAW_FULL + stage], (i / RS) & 1);
-      if (i >= 2) ok = ok && mbar_wait_spin(&bars[D_AK_FREE + b], ((i - 2) >> 1) & 1);
-      if (i >= RS) ok = ok && mbar_wait_spin(&bars[D_KP_FREE + stage], ((i / RS) - 1) & 1);
+      const int u = i * SPT + part, stage = u % RS, ki = i % KPS;
+      bool ok = mbar_wait_spin(&bars[D_RAW_FULL + stage], (u / RS) & 1);
+      if (i >= KPS) ok = ok && mbar_wait_spin(&bars[D_KP_FREE + ki], ((i / KPS) - 1) & 1);
       if (__any_sync(0xffffffffu, !ok)) {
         failed = true;
         break;
       }
-      tc_fence_after();
-      const uint8_t* cell = smem + SM::OFF_RAW + stage * SM::RAW + kl * CELL;
+      const uint8_t* cell = smem + SM::OFF_RAW + stage * SM::RAW + (kl - part * SK) * CELL;
       const uint32_t kw = *reinterpret_cast<const uint32_t*>(cell + CL::KS);
       const uint32_t vw = *reinterpret_cast<const uint32_t*>(cell + CL::VS);
       const bool valid = (tile0 + i) * DEC_TILE + kl < n;
@@ -401,128 +465,156 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
       } else {
         ks = __uint_as_float(kw);
       }
-      kp[stage * 128 + kl] = make_float4(ks, kz, valid ? __uint_as_float(vw & 0xFFFFFFF0u) : 0.f, 0.f);
+      kp[ki * 128 + kl] = make_float4(ks, kz, valid ? __uint_as_float(vw & 0xFFFFFFF0u) : 0.f, 0.f);
       // value zero-point operand biases of the key pair (a even, a + 1): key a stores {1024 + zp_a, 1024 + zp_b},
       // key a + 1 stores {-(64 + zp_a), -(64 + zp_b)} (fp16 pairs, low half = key a)
       {
         const uint32_t vz = vw & 0xFu;
         const uint32_t lo16 = 0x6400u | vz, hi16 = 0xD400u | (vz << 4);
         const uint32_t other = __shfl_xor_sync(0xffffffffu, (lane & 1) ? lo16 : hi16, 1);
-        zb[stage * 128 + kl] = (lane & 1) ? (other | (hi16 << 16)) : (lo16 | (other << 16));
+        zb[ki * 128 + kl] = (lane & 1) ? (other | (hi16 << 16)) : (lo16 | (other << 16));
       }
-      const uint32_t dst = tmem + (b ? TM_AK1 : TM_AK0) + lane_off;
       // the key's zero point as the fp16 pair biases of nib_lo / nib_hi (int4; unused for k8v4)
       const uint32_t kz16 = kw & 0xFu;
       const uint32_t klo = (0x6400u | kz16) * 0x00010001u, khi = (0xD400u | (kz16 << 4)) * 0x00010001u;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {  // 32 TMEM columns (64 channels) per store
-        uint32_t a[32];
-        if constexpr (FMT == FMT_INT4) {
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint2 w2 = *reinterpret_cast<const uint2*>(cell + 32 * c + 8 * k);
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const uint32_t w = e ? w2.y : w2.x, w8 = w >> 8;
-              const int j = 8 * k + 4 * e;
-              a[j + 0] = nib_lo(w, klo);   // channels 8 w' + {0, 4}: u - zp, exact
-              a[j + 1] = nib_hi(w, khi);   // {1, 5}
-              a[j + 2] = nib_lo(w8, klo);  // {2, 6}
-              a[j + 3] = nib_hi(w8, khi);  // {3, 7}
-            }
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint2 w2 = *reinterpret_cast<const uint2*>(cell + 64 * c + 8 * k);
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const uint32_t x = (e ? w2.y : w2.x) ^ 0x80808080u;
-              const int j = 4 * k + 2 * e;
-              // {1152 + c0, 1152 + c1} - 1152: the int8 codes, exact
-              a[j] = hsub2_u32(prmt(x, 0x64646464u, 0x4140u), 0x64806480u);
-              a[j + 1] = hsub2_u32(prmt(x, 0x64646464u, 0x4342u), 0x64806480u);
-            }
-          }
+      for (int ch = 0; ch < NCH; ++ch) {  // 256 channels (128 TMEM columns) per chunk
+        const int k = i * NCH + ch, sl = k % AKS;
+        if (k >= AKS && __any_sync(0xffffffffu, !mbar_wait_spin(&bars[D_AK_FREE + sl], ((k - AKS) / AKS) & 1))) {
+          failed = true;
+          break;
         }
-        tmem_st32u(dst + 32 * c, a);
+        tc_fence_after();
+        const uint32_t dst = tmem + (sl ? TM::AK1 : TM::AK0) + lane_off;
+        const uint8_t* kc = cell + ch * (CL::KB / NCH);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // 32 TMEM columns (64 channels) per store
+          uint32_t a[32];
+          if constexpr (FMT == FMT_INT4) {
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4) {
+              const uint2 w2 = *reinterpret_cast<const uint2*>(kc + 32 * c + 8 * k4);
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const uint32_t w = e ? w2.y : w2.x, w8 = w >> 8;
+                const int j = 8 * k4 + 4 * e;
+                a[j + 0] = nib_lo(w, klo);   // channels 8 w' + {0, 4}: u - zp, exact
+                a[j + 1] = nib_hi(w, khi);   // {1, 5}
+                a[j + 2] = nib_lo(w8, klo);  // {2, 6}
+                a[j + 3] = nib_hi(w8, khi);  // {3, 7}
+              }
+            }
+          } else {
+#pragma unroll
+            for (int k8 = 0; k8 < 8; ++k8) {
+              const uint2 w2 = *reinterpret_cast<const uint2*>(kc + 64 * c + 8 * k8);
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const uint32_t x = (e ? w2.y : w2.x) ^ 0x80808080u;
+                const int j = 4 * k8 + 2 * e;
+                // {1152 + c0, 1152 + c1} - 1152: the int8 codes, exact
+                a[j] = hsub2_u32(prmt(x, 0x64646464u, 0x4140u), 0x64806480u);
+                a[j + 1] = hsub2_u32(prmt(x, 0x64646464u, 0x4342u), 0x64806480u);
+              }
+            }
+          }
+          tmem_st32u(dst + 32 * c, a);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[D_AK_FULL + sl]);
       }
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      tc_fence_before();
+      if (failed) break;
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&bars[D_AK_FULL + b]);
-        mbar_arrive(&bars[D_KP_FULL + stage]);
+        mbar_arrive(&bars[D_KP_FULL + ki]);
         mbar_arrive(&bars[D_RAW_EMPTY + stage]);
       }
     }
   } else if (warp < W_SMX) {
     // ------------------------------------------------------------------ value operand (V^T, lane = channel)
-    // Thread (g, t) of quarter q converts word 8 q + g (channels 64 q + 8 g + [0, 8)) of keys 4 t + [0, 4) of every
-    // 16-key block. Lane 32 q + g + 8 m of channel half c holds channel 64 q + 8 g + 4 c + m.
+    // Thread (g, t) of quarter q converts the words wv = 8 (q HS/256 + v) + g, v < HS/256 (channels 8 wv + [0, 8)),
+    // of keys 4 t + [0, 4) of every 16-key block. Lane 32 q + g + 8 m of channel tile 2 v + c holds channel
+    // 8 wv + 4 c + m = 64 (q HS/256 + v) + 8 g + 4 c + m.
+    constexpr int WPT = HS / 256;
+    constexpr int NB = VK >= 32 ? 2 : 1;  // 16-key blocks per TMEM store
     const int q = warp & 3, g = lane >> 2, t = lane & 3;
-    const int wv = 8 * q + g;
     const uint32_t* zb = reinterpret_cast<const uint32_t*>(smem + SM::OFF_ZB);
     for (int i = 0; i < ntl && !failed; ++i) {
-      const int stage = i % RS, b = i & 1;
-      bool ok = mbar_wait_spin(&bars[D_RAW_FULL + stage], (i / RS) & 1);
-      ok = ok && mbar_wait_spin(&bars[D_KP_FULL + stage], (i / RS) & 1);
-      if (__any_sync(0xffffffffu, !ok)) {
+      const int ki = i % KPS;
+      if (__any_sync(0xffffffffu, !mbar_wait_spin(&bars[D_KP_FULL + ki], (i / KPS) & 1))) {
         failed = true;
         break;
       }
-      const uint8_t* raw = smem + SM::OFF_RAW + stage * SM::RAW + CL::V + 4 * wv;
+      int stage = 0;
 #pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        if (i >= 1 && __any_sync(0xffffffffu, !mbar_wait_spin(&bars[D_AV_FREE + h], (i - 1) & 1))) {
+      for (int h = 0; h < VSLOTS; ++h) {  // slot h: keys [h VK, h VK + VK) of the tile, TMEM slot k & 1
+        const int part = h * VK / SK;
+        if ((h * VK) % SK == 0) {  // the slot starts a raw stage
+          const int u = i * SPT + part;
+          stage = u % RS;
+          if (__any_sync(0xffffffffu, !mbar_wait_spin(&bars[D_RAW_FULL + stage], (u / RS) & 1))) {
+            failed = true;
+            break;
+          }
+        }
+        const int k = i * VSLOTS + h, sl = k & 1;
+        if (k >= 2 && __any_sync(0xffffffffu, !mbar_wait_spin(&bars[D_AV_FREE + sl], ((k - 2) >> 1) & 1))) {
           failed = true;
           break;
         }
         tc_fence_after();
+        const uint8_t* raw = smem + SM::OFF_RAW + stage * SM::RAW + CL::V + 32 * q * WPT + 4 * g;
 #pragma unroll
-        for (int kb2 = 0; kb2 < 2; ++kb2) {
-          uint32_t r[4][8];  // [store (channel half c, lane half lb)][registers]
+        for (int v = 0; v < WPT; ++v) {
 #pragma unroll
-          for (int rr = 0; rr < 2; ++rr) {
-            const int key0 = 16 * (4 * h + 2 * kb2 + rr) + 4 * t;
-            uint32_t w[4];
+          for (int kb = 0; kb < VK / (16 * NB); ++kb) {
+            uint32_t r[4][4 * NB];  // [store (channel tile 2 v + c, lane half lb)][registers]
 #pragma unroll
-            for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const uint32_t*>(raw + (key0 + j) * CELL);
-            const uint4 bz = *reinterpret_cast<const uint4*>(zb + stage * 128 + key0);
+            for (int rr = 0; rr < NB; ++rr) {
+              const int kt = h * VK + 16 * (NB * kb + rr) + 4 * t;  // first of the thread's 4 keys in the tile
+              const uint8_t* src = raw + 32 * v + (kt - part * SK) * CELL;
+              uint32_t w[4];
 #pragma unroll
-            for (int f = 0; f < 2; ++f) {
-              const uint32_t lo_b = f ? bz.z : bz.x, hi_b = f ? bz.w : bz.y;
-              const uint32_t x = prmt(w[2 * f], w[2 * f + 1], 0x5410u), y = prmt(w[2 * f], w[2 * f + 1], 0x7632u);
-              const uint32_t x8 = x >> 8, y8 = y >> 8;
-              r[0][4 * rr + f] = nib_lo(x, lo_b);       // channel half 0, m 0
-              r[0][4 * rr + 2 + f] = nib_hi(x, hi_b);   // half 0, m 1
-              r[1][4 * rr + f] = nib_lo(x8, lo_b);      // half 0, m 2
-              r[1][4 * rr + 2 + f] = nib_hi(x8, hi_b);  // half 0, m 3
-              r[2][4 * rr + f] = nib_lo(y, lo_b);       // half 1, m 0
-              r[2][4 * rr + 2 + f] = nib_hi(y, hi_b);
-              r[3][4 * rr + f] = nib_lo(y8, lo_b);
-              r[3][4 * rr + 2 + f] = nib_hi(y8, hi_b);
+              for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const uint32_t*>(src + j * CELL);
+              const uint4 bz = *reinterpret_cast<const uint4*>(zb + ki * 128 + kt);
+#pragma unroll
+              for (int f = 0; f < 2; ++f) {
+                const uint32_t lo_b = f ? bz.z : bz.x, hi_b = f ? bz.w : bz.y;
+                const uint32_t x = prmt(w[2 * f], w[2 * f + 1], 0x5410u), y = prmt(w[2 * f], w[2 * f + 1], 0x7632u);
+                const uint32_t x8 = x >> 8, y8 = y >> 8;
+                r[0][4 * rr + f] = nib_lo(x, lo_b);       // channel tile 2 v, m 0
+                r[0][4 * rr + 2 + f] = nib_hi(x, hi_b);   // tile 2 v, m 1
+                r[1][4 * rr + f] = nib_lo(x8, lo_b);      // tile 2 v, m 2
+                r[1][4 * rr + 2 + f] = nib_hi(x8, hi_b);  // tile 2 v, m 3
+                r[2][4 * rr + f] = nib_lo(y, lo_b);       // tile 2 v + 1, m 0
+                r[2][4 * rr + 2 + f] = nib_hi(y, hi_b);
+                r[3][4 * rr + f] = nib_lo(y8, lo_b);
+                r[3][4 * rr + 2 + f] = nib_hi(y8, hi_b);
+              }
             }
-          }
 #pragma unroll
-          for (int s = 0; s < 4; ++s) {
-            const int c = s >> 1, lb = s & 1;
-            tmem_st_16x256b_x2(tmem + (static_cast<uint32_t>(32 * q + 16 * lb) << 16) + TM_AV + 64 * h + 32 * c +
-                                   16 * kb2,
-                               r[s]);
+            for (int st = 0; st < 4; ++st) {
+              const int c = st >> 1, lb = st & 1;
+              const uint32_t addr = tmem + (static_cast<uint32_t>(32 * q + 16 * lb) << 16) + TM::AV + TM::SLOT * sl +
+                                    (VK / 2) * (2 * v + c) + 8 * NB * kb;
+              if constexpr (NB == 2) tmem_st_16x256b_x2(addr, r[st]);
+              else tmem_st_16x256b_x1(addr, r[st]);
+            }
           }
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[D_AV_FULL + h]);
+        if (lane == 0) {
+          mbar_arrive(&bars[D_AV_FULL + sl]);
+          if (((h + 1) * VK) % SK == 0) mbar_arrive(&bars[D_RAW_EMPTY + stage]);  // the stage's last slot
+        }
       }
       if (failed) break;
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bars[D_KP_FREE + stage]);
-        mbar_arrive(&bars[D_RAW_EMPTY + stage]);
-      }
+      if (lane == 0) mbar_arrive(&bars[D_KP_FREE + ki]);
     }
   } else {
     // ------------------------------------------------------------------ softmax (thread = key = TMEM lane)
@@ -537,27 +629,26 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
     float2* rp = reinterpret_cast<float2*>(smem + SM::OFF_RP);  // [2][NR]: row scale, row maximum
     int* lim = reinterpret_cast<int*>(smem + SM::OFF_LIM);
-    float* red_vs = reinterpret_cast<float*>(smem + SM::OFF_RED) + NR * 4;  // [softmax warps]
+    float* red_vs = reinterpret_cast<float*>(smem + SM::OFF_RED);  // [softmax warps]
     float* frow = red_vs + 8;                                                // [NR]
     float2* adj = reinterpret_cast<float2*>(frow + NR);                      // [NR]
     float* sb = reinterpret_cast<float*>(smem + SM::OFF_SB);                 // [NR][128]
     const float4* kp = reinterpret_cast<const float4*>(smem + SM::OFF_KP);
-    const int vis_base = n - qlen + p.tokens_after;  // last key query token 0 sees (before clamping to n - 1)
     const int causal_from = min(n, vis_base + 1);
     // query rows (prepared by K0q: programmatic dependent launch, wait for it only now) -> Q^T operand, K-major
     // 128B-swizzled; row constants
     asm volatile("griddepcontrol.wait;" ::: "memory");
     {
-      const uint8_t* qsrc = p.qrec + ((static_cast<int64_t>(kvh) * p.num_tokens + q0) * p.group) * Q_REC;
-      for (int idx = stid; idx < NR * 32; idx += SMX_THREADS) {
-        const int r = idx >> 5, ch = idx & 31;
+      const uint8_t* qsrc = p.qrec + ((static_cast<int64_t>(kvh) * p.num_tokens + q0) * p.group) * QREC;
+      for (int idx = stid; idx < NR * (HS / 8); idx += SMX_THREADS) {
+        const int r = idx / (HS / 8), ch = idx % (HS / 8);  // 16-byte chunk ch (8 channels) of row r
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (r < rows) v = *reinterpret_cast<const uint4*>(qsrc + r * Q_REC + 16 * ch);
+        if (r < rows) v = *reinterpret_cast<const uint4*>(qsrc + r * QREC + 16 * ch);
         *reinterpret_cast<uint4*>(smem + SM::OFF_Q + (ch >> 3) * SM::ATOM + sw128_off(r, ch & 7)) = v;
       }
       for (int r = stid; r < NR; r += SMX_THREADS) {
         float2 c = make_float2(0.f, INFINITY);
-        if (r < rows) c = make_float2(*reinterpret_cast<const float*>(qsrc + r * Q_REC + 2 * DEC_HS), 0.f);
+        if (r < rows) c = make_float2(*reinterpret_cast<const float*>(qsrc + r * QREC + 2 * HS), 0.f);
         rp[r] = c;
         rp[NR + r] = c;
         lim[r] = r < rows ? min(n - 1, vis_base + r / p.group) : -1;
@@ -588,24 +679,24 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
       const int patom = (kl >> 6) * SM::ATOM + (kl & 7) * 2, pchunk = (kl & 63) >> 3;
       for (int i = 0; i < ntl; ++i) {
         const int b = i & 1;
-        const int stage = i % RS;
+        const int ki = i % KPS;
         bool ok = mbar_wait_bounded(&bars[D_S_FULL + b], (i >> 1) & 1);
-        ok = ok && mbar_wait_bounded(&bars[D_KP_FULL + stage], (i / RS) & 1);
+        ok = ok && mbar_wait_bounded(&bars[D_KP_FULL + ki], (i / KPS) & 1);
         failed |= __any_sync(0xffffffffu, !ok);
         float s[RH];
         if (!failed) {
           tc_fence_after();
-          tmem_ld_cols<RH>(tmem + TM_S + NR * b + R0 + lane_off, s);
+          tmem_ld_cols<RH>(tmem + TM::S + NR * b + R0 + lane_off, s);
         } else {
 #pragma unroll
           for (int r = 0; r < RH; ++r) s[r] = 0.f;
         }
         tc_fence_before();
-        const float4 kv = kp[stage * 128 + kl];  // key scale, key zero point, value scale (0 past the context)
+        const float4 kv = kp[ki * 128 + kl];  // key scale, key zero point, value scale (0 past the context)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&bars[D_S_FREE + b]);
-          mbar_arrive(&bars[D_KP_FREE + stage]);
+          mbar_arrive(&bars[D_KP_FREE + ki]);
         }
         const int tok = (tile0 + i) * DEC_TILE + kl;
         // exp arguments: score (log2 units) minus the row maximum; emax: the largest one
@@ -699,8 +790,6 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
         uint8_t* pb = smem + SM::OFF_P + 2 * b * SM::ATOM + patom;
 #pragma unroll
         for (int r = 0; r < RH; ++r) {
-          constexpr int dummy = 0;
-          (void)dummy;
           const int R = R0 + r;
           const float pe = fast_exp2(s[r]);
           l[r] += pe;
@@ -709,12 +798,12 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
         }
         if (rescale && i >= 1) {  // before PV(i), which waits for this tile's P
 #pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < MT; ++c) {
             float o[RH];
-            tmem_ld_cols<RH>(tmem + TM_O + NR * c + R0 + lane_off, o);
+            tmem_ld_cols<RH>(tmem + TM::O + NR * c + R0 + lane_off, o);
 #pragma unroll
             for (int r = 0; r < RH; ++r) o[r] *= frow[R0 + r];
-            tmem_st_cols<RH>(tmem + TM_O + NR * c + R0 + lane_off, o);
+            tmem_st_cols<RH>(tmem + TM::O + NR * c + R0 + lane_off, o);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
           }
         }
@@ -752,15 +841,15 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
       const bool ok = mbar_wait_bounded(&bars[D_PV_DONE + ((ntl - 1) & 1)], ((ntl - 1) >> 1) & 1);
       tc_fence_after();
       const int g = lane & 7, mm = lane >> 3;
-      const int64_t head_step = static_cast<int64_t>(p.num_splits) * DEC_HS;
+      const int64_t head_step = static_cast<int64_t>(p.num_splits) * HS;
       const int64_t tok_step = (static_cast<int64_t>(p.nq) - p.group + 1) * head_step;
       const int tok0 = q0 + R0 / p.group, hg0 = R0 % p.group;
 #pragma unroll 1
-      for (int c = 0; c < 2 && ok; ++c) {
+      for (int c = 0; c < MT && ok; ++c) {  // channel tile c: channels 64 (q HS/256 + c / 2) + 8 g + 4 (c % 2) + mm
         float o[RH];
-        tmem_ld_cols<RH>(tmem + TM_O + NR * c + R0 + lane_off, o);
+        tmem_ld_cols<RH>(tmem + TM::O + NR * c + R0 + lane_off, o);
         float* dst = p.part_o + ((static_cast<int64_t>(tok0) * p.nq + kvh * p.group + hg0) * p.num_splits + split) *
-                                    DEC_HS + 64 * q + 8 * g + 4 * c + mm;
+                                    HS + 64 * (q * (HS / 256) + (c >> 1)) + 8 * g + 4 * (c & 1) + mm;
         int hg = hg0;
 #pragma unroll
         for (int r = 0; r < RH; ++r) {
@@ -930,23 +1019,23 @@ static int merge_dispatch(const MergeParams& mp, int dtype, int head_size, int64
   }
 }
 
-template <int FMT, int DT, int RL>
-static int launch_decode_t(const DecodeParams& dp, int num_seqs, cudaStream_t st) {
+template <int FMT, int DT, int HS, int RL>
+static int launch_decode_t(const DecodeParams& dp, int grid_z, cudaStream_t st) {
   constexpr int NR = RL <= 16 ? 16 : 32;  // the MMAs' N: a multiple of 16 at M 128
-  using SM = DecSmem<FMT, NR>;
+  using SM = DecSmem<FMT, HS, NR>;
   static std::atomic<bool> configured[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
-    cudaError_t e =
-        cudaFuncSetAttribute(decode_kernel<FMT, DT, NR, RL>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES);
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<FMT, DT, HS, NR, RL>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES);
     if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode smem attribute: %s", cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
   }
   // programmatic dependent launch: the CTAs start their cache copies while K0q finishes (the softmax warps wait for
   // it before reading the query rows)
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(dp.num_splits), static_cast<unsigned>(dp.nkv), static_cast<unsigned>(num_seqs));
+  cfg.gridDim = dim3(static_cast<unsigned>(dp.num_splits), static_cast<unsigned>(dp.nkv), static_cast<unsigned>(grid_z));
   cfg.blockDim = dim3(DEC_THREADS);
   cfg.dynamicSmemBytes = SM::BYTES;
   cfg.stream = st;
@@ -955,17 +1044,39 @@ static int launch_decode_t(const DecodeParams& dp, int num_seqs, cudaStream_t st
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<FMT, DT, NR, RL>, dp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<FMT, DT, HS, NR, RL>, dp);
   if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
   return QP_OK;
 }
 
-template <int FMT, int DT>
-static int launch_decode_nr(const DecodeParams& dp, int rows, int num_seqs, cudaStream_t st) {
-  if (rows <= 8) return launch_decode_t<FMT, DT, 8>(dp, num_seqs, st);
-  if (rows <= 16) return launch_decode_t<FMT, DT, 16>(dp, num_seqs, st);
-  if (rows <= 24) return launch_decode_t<FMT, DT, 24>(dp, num_seqs, st);
-  return launch_decode_t<FMT, DT, 32>(dp, num_seqs, st);
+// K0q, then K1 with the smallest row count (a multiple of 8) that covers `rows`
+template <int FMT, int DT, int HS>
+static int launch_decode_hs(const DecodeParams& dp, int rows, int grid_z, cudaStream_t st) {
+  const int64_t qrows = dp.num_tokens * dp.nq;
+  if ((qrows + 7) / 8 > 0x7fffffff) return set_error(QP_ERR_UNSUPPORTED, "decode: too many query rows");
+  decode_qprep_kernel<FMT, DT, HS><<<static_cast<unsigned>((qrows + 7) / 8), 256, 0, st>>>(
+      dp.q, dp.q_st, dp.q_sh, dp.num_tokens, dp.nq, dp.nkv, dp.sign_bits, dp.q_rotated, dp.qk_scale,
+      const_cast<uint8_t*>(dp.qrec));
+  const int rc = check_launch("decode q prep");
+  if (rc) return rc;
+  if (rows <= 8) return launch_decode_t<FMT, DT, HS, 8>(dp, grid_z, st);
+  if (rows <= 16) return launch_decode_t<FMT, DT, HS, 16>(dp, grid_z, st);
+  if (rows <= 24) return launch_decode_t<FMT, DT, HS, 24>(dp, grid_z, st);
+  return launch_decode_t<FMT, DT, HS, 32>(dp, grid_z, st);
+}
+
+template <int FMT>
+static int launch_decode_fmt(int dtype, int hs, const DecodeParams& dp, int rows, int grid_z, cudaStream_t st) {
+  if (hs == 512)
+    return dtype == DT_BF16 ? launch_decode_hs<FMT, DT_BF16, 512>(dp, rows, grid_z, st)
+                            : launch_decode_hs<FMT, DT_F16, 512>(dp, rows, grid_z, st);
+  return dtype == DT_BF16 ? launch_decode_hs<FMT, DT_BF16, 256>(dp, rows, grid_z, st)
+                          : launch_decode_hs<FMT, DT_F16, 256>(dp, rows, grid_z, st);
+}
+
+static int launch_decode(int fmt, int dtype, int hs, const DecodeParams& dp, int rows, int grid_z, cudaStream_t st) {
+  return fmt == FMT_INT4 ? launch_decode_fmt<FMT_INT4>(dtype, hs, dp, rows, grid_z, st)
+                         : launch_decode_fmt<FMT_K8V4>(dtype, hs, dp, rows, grid_z, st);
 }
 
 }  // namespace qp
@@ -994,7 +1105,7 @@ extern "C" int qp_decode_num_splits(int num_seqs, int num_kv_heads, int max_seql
 }
 
 // Workspace of qp_paged_decode: [part_o rows x head fp32][part_lse rows fp32, 256-aligned][prepared query rows
-// tokens x q heads x Q_REC bytes], rows = tokens x q heads x splits.
+// tokens x q heads x q_rec_bytes(head) bytes], rows = tokens x q heads x splits.
 static int64_t decode_qrec_offset(int64_t num_q_tokens, int num_q_heads, int head_size, int num_splits) {
   const int64_t rows = num_q_tokens * num_q_heads * static_cast<int64_t>(num_splits);
   return rows * head_size * 4 + ((rows * 4 + 255) / 256) * 256;
@@ -1002,7 +1113,61 @@ static int64_t decode_qrec_offset(int64_t num_q_tokens, int num_q_heads, int hea
 
 extern "C" int64_t qp_decode_workspace_bytes(int64_t num_q_tokens, int num_q_heads, int head_size, int num_splits) {
   return decode_qrec_offset(num_q_tokens, num_q_heads, head_size, num_splits) +
-         num_q_tokens * num_q_heads * static_cast<int64_t>(Q_REC);
+         num_q_tokens * num_q_heads * static_cast<int64_t>(q_rec_bytes(head_size));
+}
+
+// Checks shared by the decode entry points: formats, head size, cache layout.
+static int decode_check_cache(const char* who, int fmt, int dtype, int head_size, const void* cache, int block_size,
+                              int64_t block_stride, int64_t head_stride, int64_t slot_stride, int64_t k_off,
+                              int64_t ks_off, int64_t v_off, int64_t vs_off) {
+  if (fmt != FMT_INT4 && fmt != FMT_K8V4) return set_error(QP_ERR_UNSUPPORTED, "%s: format %d", who, fmt);
+  if (dtype != DT_BF16 && dtype != DT_F16) return set_error(QP_ERR_UNSUPPORTED, "%s: dtype %d", who, dtype);
+  if (head_size != 256 && head_size != 512)
+    return set_error(QP_ERR_UNSUPPORTED, "%s: head size %d (this build: 256, 512)", who, head_size);
+  const int kb = fmt == FMT_INT4 ? head_size / 2 : head_size;
+  const int cell = kb + 8 + head_size / 2;
+  if (slot_stride != cell)
+    return set_error(QP_ERR_LAYOUT, "%s: cells of a (block, head) must be contiguous (slot stride %lld, cell %d)", who,
+                     (long long)slot_stride, cell);
+  if (k_off != 0 || ks_off != kb || v_off != kb + 4 || vs_off != kb + 4 + head_size / 2)
+    return set_error(QP_ERR_LAYOUT, "%s: unexpected cell field offsets", who);
+  if (block_size <= 0 || block_size % 16 || (reinterpret_cast<uintptr_t>(cache) & 15) || (block_stride & 15) ||
+      (head_stride & 15))
+    return set_error(QP_ERR_LAYOUT, "%s: block size must be a multiple of 16 and the cache 16-byte aligned", who);
+  return QP_OK;
+}
+
+static MergeParams decode_merge_params(const DecodeParams& dp, int head_size, int out_mode, void* out,
+                                       int64_t out_stride_token, int64_t out_stride_head, float* lse_out) {
+  MergeParams mp{};
+  mp.part_o = dp.part_o;
+  mp.part_lse = dp.part_lse;
+  mp.po_t = static_cast<int64_t>(dp.nq) * dp.num_splits * head_size;
+  mp.po_h = static_cast<int64_t>(dp.num_splits) * head_size;
+  mp.po_s = head_size;
+  mp.pl_t = static_cast<int64_t>(dp.nq) * dp.num_splits;
+  mp.pl_h = dp.num_splits;
+  mp.pl_s = 1;
+  mp.num_splits = dp.num_splits;
+  mp.nq = dp.nq;
+  mp.mode = out_mode;
+  mp.out = out;
+  mp.out_st = out_stride_token;
+  mp.out_sh = out_stride_head;
+  mp.lse_out = lse_out;
+  mp.lo_t = dp.nq;
+  mp.lo_h = 1;
+  mp.sign_bits = dp.sign_bits;
+  mp.out_scale = 1.f / static_cast<float>(head_size);
+  return mp;
+}
+
+// Points dp's partials and prepared query rows into `workspace` (qp_decode_workspace_bytes layout).
+static void decode_bind_workspace(DecodeParams& dp, void* workspace, int head_size) {
+  const int64_t rows = dp.num_tokens * dp.nq * static_cast<int64_t>(dp.num_splits);
+  dp.part_o = static_cast<float*>(workspace);
+  dp.part_lse = dp.part_o + rows * head_size;
+  dp.qrec = static_cast<const uint8_t*>(workspace) + decode_qrec_offset(dp.num_tokens, dp.nq, head_size, dp.num_splits);
 }
 
 extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head,
@@ -1014,9 +1179,9 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
                                int num_kv_heads, int head_size, float softmax_scale, const uint32_t* rht_sign_bits,
                                int q_rotated, int tokens_after_keys, int out_mode, float* lse_out, int num_splits,
                                void* workspace, int64_t workspace_bytes, void* stream) {
-  if (fmt != FMT_INT4 && fmt != FMT_K8V4) return set_error(QP_ERR_UNSUPPORTED, "decode: format %d", fmt);
-  if (dtype != DT_BF16 && dtype != DT_F16) return set_error(QP_ERR_UNSUPPORTED, "decode: dtype %d", dtype);
-  if (head_size != DEC_HS) return set_error(QP_ERR_UNSUPPORTED, "decode: head size %d (this build: 256)", head_size);
+  int rc = decode_check_cache("decode", fmt, dtype, head_size, cache, block_size, block_stride, head_stride,
+                              slot_stride, k_off, ks_off, v_off, vs_off);
+  if (rc) return rc;
   if (num_seqs < 0 || num_q_tokens < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads)
     return set_error(QP_ERR_INVALID, "decode: bad sizes (seqs %d, tokens %lld, heads %d/%d)", num_seqs,
                      (long long)num_q_tokens, num_q_heads, num_kv_heads);
@@ -1028,16 +1193,6 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
                      group, DEC_MAX_ROWS);
   if (out_mode < 0 || out_mode > 2) return set_error(QP_ERR_INVALID, "decode: out_mode %d", out_mode);
   if (tokens_after_keys < 0) return set_error(QP_ERR_INVALID, "decode: tokens_after_keys %d", tokens_after_keys);
-  const int cell = fmt == FMT_INT4 ? DEC_HS + 8 : DEC_HS * 3 / 2 + 8;
-  if (slot_stride != cell)
-    return set_error(QP_ERR_LAYOUT, "decode: cells of a (block, head) must be contiguous (slot stride %lld, cell %d)",
-                     (long long)slot_stride, cell);
-  const int kb = fmt == FMT_INT4 ? DEC_HS / 2 : DEC_HS;
-  if (k_off != 0 || ks_off != kb || v_off != kb + 4 || vs_off != kb + 4 + DEC_HS / 2)
-    return set_error(QP_ERR_LAYOUT, "decode: unexpected cell field offsets");
-  if (block_size <= 0 || block_size % 16 || (reinterpret_cast<uintptr_t>(cache) & 15) || (block_stride & 15) ||
-      (head_stride & 15))
-    return set_error(QP_ERR_LAYOUT, "decode: block size must be a multiple of 16 and the cache 16-byte aligned");
   if (num_splits <= 0) return set_error(QP_ERR_INVALID, "decode: num_splits %d", num_splits);
   if (num_splits > 1024) return set_error(QP_ERR_UNSUPPORTED, "decode: num_splits %d > 1024", num_splits);
   if (!q || !out || !cu_seqlens_q || !seqused_k || !block_table || !cache || !rht_sign_bits || !workspace)
@@ -1065,65 +1220,83 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
   dp.qk_scale = softmax_scale / static_cast<float>(head_size) * LOG2E;
   dp.sign_bits = rht_sign_bits;
   dp.q_rotated = q_rotated;
-  dp.qrec = static_cast<const uint8_t*>(workspace) +
-            decode_qrec_offset(num_q_tokens, num_q_heads, head_size, num_splits);
   dp.num_tokens = num_q_tokens;
   dp.tokens_after = tokens_after_keys < max_seqlen_q ? tokens_after_keys : max_seqlen_q;  // >= qlen - 1: no mask
   dp.num_splits = num_splits;
-  const int64_t rows = num_q_tokens * num_q_heads * static_cast<int64_t>(num_splits);
-  dp.part_o = static_cast<float*>(workspace);
-  dp.part_lse = dp.part_o + rows * head_size;
+  decode_bind_workspace(dp, workspace, head_size);
 
-  const int max_rows = max_seqlen_q * group;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  {
-    uint8_t* qrec = const_cast<uint8_t*>(dp.qrec);
-    const int64_t qrows = num_q_tokens * num_q_heads;
-    if ((qrows + 7) / 8 > 0x7fffffff) return set_error(QP_ERR_UNSUPPORTED, "decode: too many query rows");
-    const unsigned qgrid = static_cast<unsigned>((qrows + 7) / 8);
-#define QP_DQPREP(F, D)                                                                                      \
-  decode_qprep_kernel<F, D><<<qgrid, 256, 0, st>>>(q, q_stride_token, q_stride_head, num_q_tokens, num_q_heads, \
-                                                   num_kv_heads, rht_sign_bits, q_rotated, dp.qk_scale, qrec)
-    if (fmt == FMT_INT4) {
-      if (dtype == DT_BF16) QP_DQPREP(FMT_INT4, DT_BF16); else QP_DQPREP(FMT_INT4, DT_F16);
-    } else {
-      if (dtype == DT_BF16) QP_DQPREP(FMT_K8V4, DT_BF16); else QP_DQPREP(FMT_K8V4, DT_F16);
-    }
-#undef QP_DQPREP
-    const int rc0 = check_launch("decode q prep");
-    if (rc0) return rc0;
-  }
-  int rc;
-  if (fmt == FMT_INT4)
-    rc = dtype == DT_BF16 ? launch_decode_nr<FMT_INT4, DT_BF16>(dp, max_rows, num_seqs, st)
-                          : launch_decode_nr<FMT_INT4, DT_F16>(dp, max_rows, num_seqs, st);
-  else
-    rc = dtype == DT_BF16 ? launch_decode_nr<FMT_K8V4, DT_BF16>(dp, max_rows, num_seqs, st)
-                          : launch_decode_nr<FMT_K8V4, DT_F16>(dp, max_rows, num_seqs, st);
+  rc = launch_decode(fmt, dtype, head_size, dp, max_seqlen_q * group, num_seqs, st);
   if (rc) return rc;
   if (out_mode == 2) return QP_OK;  // split partials stay in the workspace
+  return merge_dispatch(decode_merge_params(dp, head_size, out_mode, out, out_stride_token, out_stride_head, lse_out),
+                        dtype, head_size, num_q_tokens, st, true);
+}
 
-  MergeParams mp{};
-  mp.part_o = dp.part_o;
-  mp.part_lse = dp.part_lse;
-  mp.po_t = static_cast<int64_t>(num_q_heads) * num_splits * head_size;
-  mp.po_h = static_cast<int64_t>(num_splits) * head_size;
-  mp.po_s = head_size;
-  mp.pl_t = static_cast<int64_t>(num_q_heads) * num_splits;
-  mp.pl_h = num_splits;
-  mp.pl_s = 1;
-  mp.num_splits = num_splits;
-  mp.nq = num_q_heads;
-  mp.mode = out_mode;
-  mp.out = out;
-  mp.out_st = out_stride_token;
-  mp.out_sh = out_stride_head;
-  mp.lse_out = lse_out;
-  mp.lo_t = num_q_heads;
-  mp.lo_h = 1;
-  mp.sign_bits = rht_sign_bits;
-  mp.out_scale = 1.f / static_cast<float>(head_size);
-  return merge_dispatch(mp, dtype, head_size, num_q_tokens, st, true);
+// ---------------------------------------------------------------------------------------------------------------
+// Chunk prefill through K1 (the head-512 path of qp_prefill): the chunk's qlen query tokens become sub-sequences of
+// chunk_q = 32 / group tokens (32 query rows each), every one a split-KV decode over the keys its last token sees.
+// The sub-sequences of one KV head start on the same key tiles and move through them at the same pace, so the keys
+// are read from HBM about once and shared through L2.
+static int chunk_q_of(int group) { return group > DEC_MAX_ROWS ? 0 : DEC_MAX_ROWS / group; }
+
+static int chunk_num_splits(int qlen, int n, int num_q_heads, int num_kv_heads) {
+  const int cq = chunk_q_of(num_q_heads / num_kv_heads);
+  return qp_decode_num_splits((qlen + cq - 1) / cq, num_kv_heads, n, 0);
+}
+
+int64_t decode_chunk_workspace_bytes(int qlen, int n, int num_q_heads, int num_kv_heads, int head_size) {
+  if (qlen <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || !chunk_q_of(num_q_heads / num_kv_heads))
+    return 0;
+  return qp_decode_workspace_bytes(qlen, num_q_heads, head_size, chunk_num_splits(qlen, n, num_q_heads, num_kv_heads));
+}
+
+int decode_chunk_prefill(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head, void* out,
+                         int64_t out_stride_token, int64_t out_stride_head, int qlen, int n, const int32_t* block_row,
+                         const void* cache, int block_size, int64_t block_stride, int64_t head_stride,
+                         int64_t slot_stride, int64_t k_off, int64_t ks_off, int64_t v_off, int64_t vs_off,
+                         int num_q_heads, int num_kv_heads, int head_size, float softmax_scale,
+                         const uint32_t* rht_sign_bits, int q_rotated, int tokens_after_keys, int out_mode,
+                         float* lse_out, void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = decode_check_cache("prefill", fmt, dtype, head_size, cache, block_size, block_stride, head_stride,
+                              slot_stride, k_off, ks_off, v_off, vs_off);
+  if (rc) return rc;
+  const int group = num_q_heads / num_kv_heads;
+  const int cq = chunk_q_of(group);
+  if (!cq) return set_error(QP_ERR_UNSUPPORTED, "prefill: %d query heads per KV head > %d", group, DEC_MAX_ROWS);
+  const int subs = (qlen + cq - 1) / cq;
+  if (subs > 65535 || num_kv_heads > 65535) return set_error(QP_ERR_UNSUPPORTED, "prefill: grid too large");
+  const int splits = chunk_num_splits(qlen, n, num_q_heads, num_kv_heads);
+  const int64_t need = qp_decode_workspace_bytes(qlen, num_q_heads, head_size, splits);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15) || workspace_bytes < need)
+    return set_error(QP_ERR_WORKSPACE, "prefill: workspace of %lld bytes < %lld", (long long)workspace_bytes,
+                     (long long)need);
+  DecodeParams dp{};
+  dp.q = q;
+  dp.q_st = q_stride_token;
+  dp.q_sh = q_stride_head;
+  dp.block_table = block_row;
+  dp.cache = static_cast<const uint8_t*>(cache);
+  dp.block_size = block_size;
+  dp.block_stride = block_stride;
+  dp.head_stride = head_stride;
+  dp.nq = num_q_heads;
+  dp.nkv = num_kv_heads;
+  dp.group = group;
+  dp.qk_scale = softmax_scale / static_cast<float>(head_size) * LOG2E;
+  dp.sign_bits = rht_sign_bits;
+  dp.q_rotated = q_rotated;
+  dp.num_tokens = qlen;
+  dp.tokens_after = tokens_after_keys < qlen ? tokens_after_keys : qlen;  // >= qlen: nothing masked
+  dp.chunk_q = cq;
+  dp.chunk_n = n;
+  dp.num_splits = splits;
+  decode_bind_workspace(dp, workspace, head_size);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = launch_decode(fmt, dtype, head_size, dp, cq * group, subs, st);
+  if (rc) return rc;
+  return merge_dispatch(decode_merge_params(dp, head_size, out_mode, out, out_stride_token, out_stride_head, lse_out),
+                        dtype, head_size, qlen, st, true);
 }
 
 extern "C" int qp_merge_attn_partials(int dtype, int head_size, int64_t num_tokens, int num_q_heads, int num_parts,

@@ -45,6 +45,7 @@ namespace qp {
 constexpr int PF_HS = 256;
 constexpr int PF_BM = 128;  // query rows per M-tile (TMEM lanes)
 constexpr int PF_BN = 64;   // keys per tile
+constexpr int PF_MAX_CHUNKS = 16;  // key chunks of the walk (Sched)
 #ifndef QP_PF_DQ_WARPS
 #define QP_PF_DQ_WARPS 8
 #endif
@@ -126,9 +127,10 @@ struct PrefillParams {
   float* part_o;             // [qlen][nq][parts][256]
   float* part_lse;           // [qlen][nq][parts]
   int parts;
-  int64_t total_tiles;       // (M-tile, key-tile) pairs over all KV heads
   int chunk_tiles;           // key tiles of one key chunk (the walk is chunk-major, see Sched)
   int piece_stride;          // piece slots per key chunk of an M-tile
+  int chunks;                // key chunks (<= PF_MAX_CHUNKS)
+  int64_t chunk_total[PF_MAX_CHUNKS];  // (M-tile, key-tile) pairs of each chunk over all KV heads
 };
 
 // position of channel c inside its group of 8 in the operand order [0 4 1 5 2 6 3 7]
@@ -150,11 +152,13 @@ __device__ __forceinline__ int run_tiles(const PrefillParams& p, int j, int m, i
   return max(0, min(mtile_key_tiles(p, m), a + p.chunk_tiles) - a);
 }
 
-// Walk of the tiles of this CTA: [g_begin, g_end) of the flattened (key chunk, KV head, M-tile, key tile) space.
-// Key chunk major: the CTAs running at one time work on the M-tiles of the same key chunk, so every key tile is
-// fetched from HBM about once and the M-tiles of its KV head read it from L2 (a walk with the key tiles of one M-tile
-// innermost had every M-tile re-read its head's whole cache). A run (one M-tile's tiles inside one chunk) split by CTA
-// boundaries gives several pieces; piece slots j * piece_stride + i keep the pieces of different chunks apart.
+// Walk of the tiles of this CTA over the (key chunk, KV head, M-tile, key tile) space. Every key chunk is split
+// among all CTAs on its own (CTA c takes [T_j c / ctas, T_j (c + 1) / ctas) of chunk j's T_j tiles), and a CTA
+// finishes its share of chunk j before it starts on chunk j + 1: the CTAs running at one time work on the same key
+// chunk, so each key tile is fetched from HBM about once and the other M-tiles of its KV head read it from L2 (a walk
+// with the key tiles of one M-tile innermost had every M-tile re-read its head's whole cache). A run (one M-tile's
+// tiles inside one chunk) split by CTA boundaries gives several pieces; piece slots j * piece_stride + i keep the
+// pieces of different chunks apart.
 struct Walk {
   int kvh, m, kt, kt_end;  // current M-tile and key tile
   int piece;               // partial slot of this CTA's piece of the M-tile
@@ -162,51 +166,58 @@ struct Walk {
 };
 
 // Every warp walks the same schedule each tile, so the walk itself runs in 32-bit counters (the host keeps the
-// tile count below 2^31); 64-bit arithmetic is confined to init().
+// tile count below 2^31); 64-bit arithmetic is confined to the start of each chunk share.
 struct Sched {
   const PrefillParams* p;
-  int left;          // tiles of this CTA not yet walked past, the current one included
+  int left;          // tiles of this CTA's share of chunk j not yet walked past, the current one included
   int j, kvh, m;     // current run: key chunk, M-tile
   int kt, kt_hi;     // current key tile inside the M-tile, end of the run
   int first_kt;      // first key tile of this CTA inside the current run
   int piece;         // partial slot of this CTA's piece of the current run
   int cta, ctas;
 
-  __device__ void advance_run() {
+  __device__ void advance_run() {  // next (KV head, M-tile) inside chunk j
     if (++m == p->mt_per_kv) {
       m = 0;
-      if (++kvh == p->nkv) {
-        kvh = 0;
-        ++j;
-      }
+      ++kvh;
     }
+  }
+
+  // Positions the walk at this CTA's share of chunk j, or of the next chunk with a non-empty share.
+  __device__ void start_chunk() {
+    for (; j < p->chunks; ++j) {
+      const int64_t T = p->chunk_total[j];
+      const int64_t g = T * cta / ctas;
+      left = static_cast<int>(T * (cta + 1) / ctas - g);
+      if (left <= 0) continue;
+      kvh = m = 0;
+      int64_t start = 0;
+      int lo = 0;
+      int len = run_tiles(*p, j, 0, &lo);
+      while (start + len <= g) {  // to the run holding g (empty runs are skipped)
+        start += len;
+        advance_run();
+        len = run_tiles(*p, j, m, &lo);
+      }
+      kt = first_kt = lo + static_cast<int>(g - start);
+      kt_hi = lo + len;
+      // piece inside the run: CTAs whose share starts inside it before this one. The CTA covering `start` is the
+      // largest c with T * c / ctas <= start; every later run of this CTA in the chunk starts with it (piece 0).
+      int c0 = static_cast<int>((start * ctas) / T);
+      while (c0 + 1 < ctas && T * (c0 + 1) / ctas <= start) ++c0;
+      while (c0 > 0 && T * c0 / ctas > start) --c0;
+      piece = j * p->piece_stride + (cta - c0);
+      return;
+    }
+    left = 0;
   }
 
   __device__ void init(const PrefillParams& prm, int cta_, int ctas_) {
     p = &prm;
     cta = cta_;
     ctas = ctas_;
-    const int64_t g = prm.total_tiles * cta / ctas;
-    const int64_t g_end = prm.total_tiles * (cta + 1) / ctas;
-    left = static_cast<int>(g_end - g);
-    j = kvh = m = 0;
-    int64_t start = 0;
-    int lo = 0;
-    int len = run_tiles(prm, 0, 0, &lo);
-    while (start + len <= g && left > 0) {  // to the run holding g (empty runs are skipped)
-      start += len;
-      advance_run();
-      len = run_tiles(prm, j, m, &lo);
-    }
-    kt = first_kt = lo + static_cast<int>(g - start);
-    kt_hi = lo + len;
-    // piece inside the run: CTAs whose range starts inside it before this one. The CTA covering `start` is the
-    // largest c with total * c / ctas <= start. (Computed once: 64-bit divisions are long instruction sequences;
-    // every later run of this CTA starts with this CTA, piece 0.)
-    int c0 = static_cast<int>((start * ctas) / prm.total_tiles);
-    while (c0 + 1 < ctas && prm.total_tiles * (c0 + 1) / ctas <= start) ++c0;
-    while (c0 > 0 && prm.total_tiles * c0 / ctas > start) --c0;
-    piece = j * prm.piece_stride + (cta - c0);
+    j = 0;
+    start_chunk();
   }
   __device__ bool done() const { return left <= 0; }
   __device__ Walk current() const {
@@ -222,8 +233,12 @@ struct Sched {
     return w;
   }
   __device__ void next() {
-    --left;
-    if (++kt >= kt_hi && left > 0) {
+    if (--left == 0) {  // this CTA's share of chunk j is done
+      ++j;
+      start_chunk();
+      return;
+    }
+    if (++kt >= kt_hi) {
       int lo = 0, len = 0;
       do {
         advance_run();
@@ -847,16 +862,19 @@ using namespace qp;
 // [part_lse qlen*nq*parts f32], each 256-byte aligned.
 static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
-// Key chunks of a chunk prefill: the cache of all KV heads in pieces of at most 64 MB (so that the chunk the CTAs work
-// on, and the next one, stay in the 126 MB L2), at most 8.
+// Key chunks of a chunk prefill: the cache of all KV heads in pieces of at most 40 MB, so that the chunk the CTAs work
+// on, and the start of the next one that the first CTAs to finish already read, stay in the 126 MB L2; at most
+// PF_MAX_CHUNKS.
 static int prefill_chunks(int n, int nkv, int cell) {
   const int64_t bytes = static_cast<int64_t>(n) * nkv * cell;
-  return static_cast<int>(std::min<int64_t>(8, std::max<int64_t>(1, (bytes + (64ll << 20) - 1) / (64ll << 20))));
+  const int64_t c = (bytes + (40ll << 20) - 1) / (40ll << 20);
+  return static_cast<int>(std::min<int64_t>(PF_MAX_CHUNKS, std::max<int64_t>(1, c)));
 }
 
 struct PrefillPlan {
-  int mt_per_kv, ctas, parts, chunk_tiles, piece_stride;
+  int mt_per_kv, ctas, parts, chunk_tiles, piece_stride, chunks;
   int64_t total;
+  int64_t chunk_total[PF_MAX_CHUNKS];
 };
 
 static PrefillPlan prefill_plan(int qlen, int n, int after, int nkv, int group, int sms, int cell) {
@@ -875,27 +893,34 @@ static PrefillPlan prefill_plan(int qlen, int n, int after, int nkv, int group, 
   tot *= nkv;
   pl.total = tot;
   pl.ctas = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sms, tot)));
-  const int chunks = prefill_chunks(n, nkv, cell);
-  pl.chunk_tiles = std::max(1, (maxt + chunks - 1) / chunks);
-  // pieces of a run: the CTAs covering it (the CTA of tile g: the largest c with total * c / ctas <= g)
-  auto cta_of = [&](int64_t g) {
-    int c = static_cast<int>(g * pl.ctas / std::max<int64_t>(1, tot));
-    while (c + 1 < pl.ctas && tot * (c + 1) / pl.ctas <= g) ++c;
-    while (c > 0 && tot * c / pl.ctas > g) --c;
-    return c;
-  };
+  const int want = prefill_chunks(n, nkv, cell);
+  pl.chunk_tiles = std::max(1, (maxt + want - 1) / want);
+  pl.chunks = (maxt + pl.chunk_tiles - 1) / pl.chunk_tiles;
+  // chunk j's tiles, then the pieces of each of its runs: the CTAs covering it under chunk j's own split (the CTA of
+  // tile g: the largest c with T_j * c / ctas <= g)
   int stride = 1;
-  int64_t start = 0;
-  for (int j = 0; j < chunks; ++j)
+  for (int j = 0; j < pl.chunks; ++j) {
+    const int a = j * pl.chunk_tiles;
+    int64_t T = 0;
+    for (int m = 0; m < pl.mt_per_kv; ++m) T += std::max(0, std::min(tiles[m], a + pl.chunk_tiles) - a);
+    T *= nkv;
+    pl.chunk_total[j] = T;
+    auto cta_of = [&](int64_t g) {
+      int c = static_cast<int>(g * pl.ctas / std::max<int64_t>(1, T));
+      while (c + 1 < pl.ctas && T * (c + 1) / pl.ctas <= g) ++c;
+      while (c > 0 && T * c / pl.ctas > g) --c;
+      return c;
+    };
+    int64_t start = 0;
     for (int h = 0; h < nkv; ++h)
       for (int m = 0; m < pl.mt_per_kv; ++m) {
-        const int a = j * pl.chunk_tiles;
         const int len = std::max(0, std::min(tiles[m], a + pl.chunk_tiles) - a);
         if (len > 0) stride = std::max(stride, cta_of(start + len - 1) - cta_of(start) + 1);
         start += len;
       }
+  }
   pl.piece_stride = stride;
-  pl.parts = chunks * stride;
+  pl.parts = pl.chunks * stride;
   return pl;
 }
 
@@ -908,7 +933,7 @@ static int64_t prefill_ws_bytes(int qlen, int nq, int64_t nt, int parts) {
 extern "C" int64_t qp_prefill_workspace_bytes(int qlen, int n, int num_q_heads, int num_kv_heads, int head_size,
                                               int tokens_after_keys) {
   if (qlen <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || tokens_after_keys < 0) return 0;
-  (void)head_size;
+  if (head_size == 512) return decode_chunk_workspace_bytes(qlen, n, num_q_heads, num_kv_heads, head_size);
   const int after = std::min(tokens_after_keys, qlen);
   const int group = num_q_heads / num_kv_heads;
   // either cache format (the chunk count depends on the cell size)
@@ -1014,7 +1039,8 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
                           float* lse_out, void* workspace, int64_t workspace_bytes, void* stream) {
   if (fmt != FMT_INT4 && fmt != FMT_K8V4) return set_error(QP_ERR_UNSUPPORTED, "prefill: format %d", fmt);
   if (dtype != DT_BF16 && dtype != DT_F16) return set_error(QP_ERR_UNSUPPORTED, "prefill: dtype %d", dtype);
-  if (head_size != PF_HS) return set_error(QP_ERR_UNSUPPORTED, "prefill: head size %d (this build: 256)", head_size);
+  if (head_size != PF_HS && head_size != 512)
+    return set_error(QP_ERR_UNSUPPORTED, "prefill: head size %d (this build: 256, 512)", head_size);
   const int after = std::min(std::max(tokens_after_keys, 0), std::max(qlen, 0));  // >= qlen: nothing masked
   if (tokens_after_keys < 0 || qlen < 0 || n < qlen - after || (qlen > 0 && n <= 0) || num_kv_heads <= 0 ||
       num_q_heads <= 0 || num_q_heads % num_kv_heads)
@@ -1022,6 +1048,15 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
                      num_kv_heads);
   if (qlen == 0) return QP_OK;
   if (out_mode != 0 && out_mode != 1) return set_error(QP_ERR_INVALID, "prefill: out_mode %d", out_mode);
+  if (head_size == 512) {  // O^T of a 128-query tile would need all of TMEM: the split-KV kernel's chunk mode
+    if (!q || !out || !block_row || !cache || !rht_sign_bits || !workspace)
+      return set_error(QP_ERR_INVALID, "prefill: null pointer");
+    return decode_chunk_prefill(fmt, dtype, q, q_stride_token, q_stride_head, out, out_stride_token, out_stride_head,
+                                qlen, n, block_row, cache, block_size, block_stride, head_stride, slot_stride, k_off,
+                                ks_off, v_off, vs_off, num_q_heads, num_kv_heads, head_size, softmax_scale,
+                                rht_sign_bits, q_rotated, tokens_after_keys, out_mode, lse_out, workspace,
+                                workspace_bytes, stream);
+  }
   const int cell = fmt == FMT_INT4 ? PF_HS + 8 : PF_HS * 3 / 2 + 8;
   const int kb = fmt == FMT_INT4 ? PF_HS / 2 : PF_HS;
   if (slot_stride != cell)
@@ -1089,9 +1124,10 @@ extern "C" int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_to
   pp.part_o = part_o;
   pp.part_lse = part_lse;
   pp.parts = parts;
-  pp.total_tiles = total;
   pp.chunk_tiles = pl.chunk_tiles;
   pp.piece_stride = pl.piece_stride;
+  pp.chunks = pl.chunks;
+  for (int j = 0; j < pl.chunks; ++j) pp.chunk_total[j] = pl.chunk_total[j];
   rc = fmt == FMT_INT4 ? launch_prefill_main<FMT_INT4>(pp, ctas, st) : launch_prefill_main<FMT_K8V4>(pp, ctas, st);
   if (rc) return rc;
   if (parts <= FOLD_MAX_PARTS) {

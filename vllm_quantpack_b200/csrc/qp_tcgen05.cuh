@@ -234,6 +234,12 @@ __device__ __forceinline__ void tmem_st_16x256b_x2(uint32_t taddr, const uint32_
                "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                : "memory");
 }
+// one repetition of the above (r = 0 only: 8 columns)
+__device__ __forceinline__ void tmem_st_16x256b_x1(uint32_t taddr, const uint32_t (&v)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.16x256b.x1.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3])
+               : "memory");
+}
 
 __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
