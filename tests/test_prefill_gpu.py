@@ -29,15 +29,23 @@ def run_prefill(device, cache, table_row, q_bits, n, dtype="bf16"):
 
 
 def reference_rows(cache_bytes, layout, table_row, q_bits, n, rows, dtype="bf16"):
-    """Oracle output of the chunk's query rows `rows`: row i is the last position of a context of n - qlen + i + 1."""
+    """Oracle output of the chunk's query rows `rows`: row i is the last position of a context of n - qlen + i + 1.
+    Each run of consecutive rows is one oracle call (its last row's context, causal inside the run)."""
     hs = layout.head_size
     sg = U.signs(hs)
     qlen = q_bits.shape[0]
     out = []
-    for i in rows:
-        q_rot = qo.single_rht(qo.to_f32(q_bits[i:i + 1], dtype), sg).astype(np.float64)
-        o, _ = qo.attention_from_cache(q_rot, cache_bytes, layout, table_row, n - qlen + i + 1, hs ** -0.5)
+    rows = list(rows)
+    a = 0
+    while a < len(rows):
+        b = a + 1
+        while b < len(rows) and rows[b] == rows[b - 1] + 1:
+            b += 1
+        lo, hi = rows[a], rows[b - 1] + 1
+        q_rot = qo.single_rht(qo.to_f32(q_bits[lo:hi], dtype), sg).astype(np.float64)
+        o, _ = qo.attention_from_cache(q_rot, cache_bytes, layout, table_row, n - qlen + hi, hs ** -0.5)
         out.append(qo.single_rht(o.astype(np.float32), sg, inverse=True).astype(np.float64) / hs)
+        a = b
     return np.concatenate(out)
 
 
@@ -86,9 +94,13 @@ def test_fp16_model(device):
     assert prefill_case(device, "int4", 100, 2000, 16, dtype="f16") < TOL
 
 
-def test_full_size_chunk(device):
-    """c3: 1024 queries over 229,376 cached tokens (+ the chunk's own 1024)."""
-    err = prefill_case(device, "int4", 1024, 229376 + 1024, 16, rows=[0, 511, 1023])
+@pytest.mark.parametrize("fmt", ["int4", "k8v4"])
+def test_full_size_chunk(device, fmt):
+    """c3: 1024 queries over 229,376 cached tokens (+ the chunk's own 1024), both cache formats. Every row (all 24
+    heads) of the first and last 22 tokens: the first and last 128-row M-tiles of every KV head, each summed from
+    pieces of every key chunk and of the CTAs that split a chunk's run, plus a middle token."""
+    rows = list(range(0, 22)) + [511] + list(range(1002, 1024))
+    err = prefill_case(device, fmt, 1024, 229376 + 1024, 16, rows=rows)
     assert err < TOL, err
 
 

@@ -4,8 +4,8 @@ Some hosts of this library never call cudaMalloc after start-up (an engine that 
 pool, embedded code with no device allocator), so they cannot hand qp_paged_decode a workspace. The static variant
 keeps its split partials in a fixed 32 MiB array inside the library. These tests call it through the C ABI and check
 that two calls in a row (the second one finds the first call's partials still in the array) give the output of the
-workspace entry point, within the tolerance of the decode tests; and that a request whose partials do not fit is
-refused with a clear error. This file is collected last on purpose."""
+workspace entry point and of the fp64 oracle, within the tolerance of the decode tests; and that a request whose
+partials do not fit is refused with a clear error. This file is collected last on purpose."""
 import ctypes
 
 import numpy as np
@@ -54,11 +54,13 @@ def test_static_scratch_decode_matches_workspace_decode(device, fmt):
     for i, n in enumerate(lens):
         cache.fill(table_np[i], n, seed=40 + i)
     kc, vc, ks, vs = cache.views
-    q = U.to_torch(U.make_queries(qlens, seed=8), device)
+    qb = U.make_queries(qlens, seed=8)
+    q = U.to_torch(qb, device)
     cu = torch.tensor(np.concatenate([[0], np.cumsum(qlens)]), dtype=torch.int32, device=device)
     used = torch.tensor(lens, dtype=torch.int32, device=device)
     table = torch.from_numpy(table_np).to(device)
     splits = ops.decode_num_splits(len(lens), U.NKV, max(lens), ops.sm_count(device))
+    oracle = U.reference(cache.host_bytes(), cache.layout, qb, qlens, lens, table_np)
     want = torch.empty_like(q)
     ops.paged_decode(q, kc, vc, want, cu_seqlens_q=cu, max_seqlen_q=max(qlens), seqused_k=used,
                      max_seqlen_k=max(lens), softmax_scale=U.HS ** -0.5, block_table=table, k_scale_cache=ks,
@@ -73,6 +75,8 @@ def test_static_scratch_decode_matches_workspace_decode(device, fmt):
         assert np.isfinite(got).all(), f"call {call}: output not written"
         err = qo.relerr(got, want)
         assert err < TOL, f"call {call}: static-scratch decode differs from the workspace decode by {err:.3e}"
+        err = qo.relerr(got, oracle)
+        assert err < TOL, f"call {call}: static-scratch decode differs from the fp64 oracle by {err:.3e}"
         if call == 0:
             # between the two compared calls, a bigger request with more splits and the other cache format fills
             # the array with partials of another shape: the next call must not read any of them

@@ -19,6 +19,7 @@ VLLM_QUANTPACK_INT4_KV=0 (no patch), VLLM_QUANTPACK_INT4_FA_PREFILL=0 (prefill c
 VLLM_QUANTPACK_INT4_DECODE="tile,warps,segments[,rows]" (segments: split count of the decode, "auto" = per call),
 VLLM_QUANTPACK_INT4_TILES (accepted; the B200 prefill tiles are fixed at 128 x 64).
 """
+import contextlib
 import importlib
 import itertools
 import os
@@ -307,39 +308,48 @@ def patch_int4_kv(logger):
     return True
 
 
-def _patch_decode_segments(segments, logger):
-    """Size vLLM's split-KV segment buffers for `segments` segments for int4 / k8v4 caches (int4_kv.py:229-257),
-    and reserve this process's decode workspace on the builder's device for the largest decode batch it plans
-    (seq_threshold_3D query rows at the largest split count), so that CUDA-graph capture never grows it."""
+@contextlib.contextmanager
+def _segment_count(module, segments):
+    """vLLM's Triton metadata builder reads the module constant NUM_PAR_SOFTMAX_SEGMENTS once, while it allocates its
+    split-KV segment buffers: hold it at `segments` for that long."""
+    old = module.NUM_PAR_SOFTMAX_SEGMENTS
+    module.NUM_PAR_SOFTMAX_SEGMENTS = segments
     try:
-        from vllm.v1.attention.backends import triton_attn
-        builder = triton_attn.TritonAttentionMetadataBuilder
-        stock_init = builder.__init__
-        triton_attn.NUM_PAR_SOFTMAX_SEGMENTS   # the anchor this relies on
-    except Exception as e:
-        logger.info("vllm-quantpack-b200: int4 split-KV segments left stock (%s)", e)
-        return 0
-    if getattr(stock_init, "_quantpack_b200", False):
-        return segments
+        yield
+    finally:
+        module.NUM_PAR_SOFTMAX_SEGMENTS = old
+
+
+def _patch_decode_segments(segments, logger):
+    """Builders of int4 / k8v4 caches allocate vLLM's split-KV segment buffers for `segments` segments (the buffers
+    the stock fallback kernel writes; int4_kv.py:229-257), and reserve this process's decode workspace on their device
+    for the largest decode batch they plan (seq_threshold_3D query rows at the largest split count), so that CUDA-graph
+    capture never grows it. Returns the segment count in use, 0 when the builder is left stock."""
     if segments < 1 or segments & (segments - 1):
         logger.warning("vllm-quantpack-b200: int4 split-KV segments must be a power of two, got %d: left stock",
                        segments)
         return 0
+    try:
+        from vllm.v1.attention.backends import triton_attn
+        cls = triton_attn.TritonAttentionMetadataBuilder
+        triton_attn.NUM_PAR_SOFTMAX_SEGMENTS   # the constant the wrapper sets must exist
+    except Exception as e:
+        logger.info("vllm-quantpack-b200: int4 split-KV segments left stock (%s)", e)
+        return 0
+    original = cls.__init__
+    if getattr(original, "_quantpack_b200", False):
+        return segments
 
-    def __init__(self, kv_cache_spec, layer_names, vllm_config, device):
-        if vllm_config.cache_config.cache_dtype not in PACKED_DTYPES:
-            return stock_init(self, kv_cache_spec, layer_names, vllm_config, device)
-        saved = triton_attn.NUM_PAR_SOFTMAX_SEGMENTS
-        triton_attn.NUM_PAR_SOFTMAX_SEGMENTS = segments   # read once, in __init__, to size the buffers
-        try:
-            stock_init(self, kv_cache_spec, layer_names, vllm_config, device)
-        finally:
-            triton_attn.NUM_PAR_SOFTMAX_SEGMENTS = saved
-        reserve_decode_workspace(self, vllm_config, device)
+    def init(builder, kv_cache_spec, layer_names, vllm_config, device):
+        packed = vllm_config.cache_config.cache_dtype in PACKED_DTYPES
+        with _segment_count(triton_attn, segments) if packed else contextlib.nullcontext():
+            original(builder, kv_cache_spec, layer_names, vllm_config, device)
+        if packed:
+            reserve_decode_workspace(builder, vllm_config, device)
 
-    __init__._quantpack = True
-    __init__._quantpack_b200 = True
-    builder.__init__ = __init__
+    init._quantpack = True
+    init._quantpack_b200 = True
+    cls.__init__ = init
     return segments
 
 
