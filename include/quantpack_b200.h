@@ -103,7 +103,7 @@ int64_t qp_decode_workspace_bytes(int64_t num_q_tokens, int num_q_heads, int hea
  * Replaces the plugin's split-KV decode: the patched `_launch_packed_attn` (int4_kv.py:98-122, 212-216) with its 3D
  * kernel `_attn_packed_qp` / `_attn_k8v4_qp` (int4_kv.py:80-146) and vLLM's reduce_segments, reached through
  * `unified_attention_int4` (int4_kv.py:294-307). Needs HND cells (slot_stride == cell bytes), block_size % 16 == 0,
- * head_size 256, a 16-byte aligned cache and qp_decode_workspace_bytes() of workspace. */
+ * head_size 256 or 512, a 16-byte aligned cache and qp_decode_workspace_bytes() of workspace. */
 int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head, void* out,
                     int64_t out_stride_token, int64_t out_stride_head, int64_t num_q_tokens, int num_seqs,
                     const int32_t* cu_seqlens_q, const int32_t* seqused_k, int max_seqlen_q,
@@ -123,7 +123,9 @@ int64_t qp_prefill_workspace_bytes(int qlen, int n, int num_q_heads, int num_kv_
  * among themselves) attend to the whole cached context through block_row (that sequence's block-table row), on the
  * tcgen05 tensor cores with every key / value tile dequantised in shared memory (no scratch unpack of the cache).
  * out_mode / lse_out / q_rotated / tokens_after_keys as in qp_paged_decode (n >= qlen - tokens_after_keys);
- * head_size 256; HND cells, block_size % 16 == 0.
+ * head_size 256, or 512 (there the chunk runs on the split-KV decode kernel as decodes of 32 / (query heads per KV
+ * head) tokens over its causal prefixes: O of a 128-query tile alone would fill TMEM); HND cells,
+ * block_size % 16 == 0.
  * Replaces vllm_quantpack/attention/int4_prefill.py:203-232 `prefill_sequence` (16k-token bf16 unpacks +
  * FlashAttention 2 + log-sum-exp fold) and the Triton 2D path of int4_kv.py:113-119, reached through
  * `unified_attention_int4` (int4_kv.py:308-329). */
@@ -134,6 +136,27 @@ int qp_prefill(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_
                int head_size, float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated,
                int tokens_after_keys, int out_mode, float* lse_out, void* workspace, int64_t workspace_bytes,
                void* stream);
+
+/* Bytes of workspace qp_prefill_varlen needs (its split partials, prepared query rows and sub-sequence table). */
+int64_t qp_prefill_varlen_workspace_bytes(int64_t num_q_tokens, int num_chunks, int num_q_heads, int num_kv_heads,
+                                          int head_size, int max_seqlen_k);
+
+/* Short prefill chunks of several sequences in one launch: chunk i's query tokens q[cu_seqlens_q[i] ..
+ * cu_seqlens_q[i + 1]) are the last positions of its context of seqused_k[i] cached tokens (causal among themselves),
+ * read through block_table[i]; cu_seqlens_q / seqused_k are device int32 arrays (num_chunks + 1 / num_chunks) that
+ * the call never reads back to the host. max_seqlen_k bounds seqused_k (it sizes the split count). The chunks run on
+ * the split-KV decode kernel as sub-sequences of 32 / (query heads per KV head) tokens. out / out_mode / lse_out /
+ * q_rotated as in qp_paged_decode (out_mode 0 or 1); head_size 256 or 512; HND cells, block_size % 16 == 0.
+ * Replaces the Triton 2D sub-batch that the plugin runs for every chunk that is not long (int4_kv.py:113-119,
+ * 313-323). */
+int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head, void* out,
+                      int64_t out_stride_token, int64_t out_stride_head, int64_t num_q_tokens, int num_chunks,
+                      const int32_t* cu_seqlens_q, const int32_t* seqused_k, int max_seqlen_k,
+                      const int32_t* block_table, int64_t block_table_stride, const void* cache, int block_size,
+                      int64_t block_stride, int64_t head_stride, int64_t slot_stride, int64_t k_off, int64_t ks_off,
+                      int64_t v_off, int64_t vs_off, int num_q_heads, int num_kv_heads, int head_size,
+                      float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated, int out_mode, float* lse_out,
+                      void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Bytes of the library's static decode scratch used by qp_paged_decode_static. */
 #define QP_STATIC_DECODE_SCRATCH_BYTES (32ll << 20)

@@ -228,6 +228,7 @@ class Recorder:
         self.calls = []
         monkeypatch.setattr(ops, "paged_decode", self.decode)
         monkeypatch.setattr(ops, "prefill", self.prefill)
+        monkeypatch.setattr(ops, "prefill_varlen", self.varlen)
 
     def decode(self, q, kc, vc, out, *, cu_seqlens_q, seqused_k, block_table, max_seqlen_q, num_splits, **kw):
         self.calls.append(("decode", q.shape[0], cu_seqlens_q.tolist(), seqused_k.tolist(), max_seqlen_q,
@@ -239,6 +240,12 @@ class Recorder:
     def prefill(self, q, kc, vc, out, *, block_row, n, **kw):
         self.calls.append(("prefill", q.shape[0], n))
         out[:] = float(block_row[0])
+        return out
+
+    def varlen(self, q, kc, vc, out, *, cu_seqlens_q, seqused_k, max_seqlen_k, block_table, **kw):
+        self.calls.append(("varlen", q.shape[0], cu_seqlens_q.tolist(), seqused_k.tolist(), max_seqlen_k))
+        for b in range(len(seqused_k)):
+            out[cu_seqlens_q[b]:cu_seqlens_q[b + 1]] = float(block_table[b, 0])
         return out
 
 
@@ -287,7 +294,7 @@ def test_mixed_step_splits_decode_prefill(monkeypatch):
     q, kc, out, args = _step([256, 2, 4, 40], [40000, 20000, 100, 300])
     fn(q, kc, kc, out, **args)
     assert ("decode", 6, [0, 2, 6], [20000, 100], 4, None) in rec.calls
-    assert ("prefill", 256, 40000) in rec.calls and ("prefill", 40, 300) in rec.calls
+    assert ("prefill", 256, 40000) in rec.calls and ("varlen", 40, [0, 40], [300], 300) in rec.calls
     assert len(rec.calls) == 3 and not stock_calls
     assert (out[:256] == 1).all() and (out[256:258] == 2).all() and (out[258:262] == 3).all()
     assert (out[262:302] == 4).all() and (out[302:] == -7).all()
@@ -317,12 +324,34 @@ def test_head_512_is_served_and_other_head_sizes_go_stock(monkeypatch):
     rec.calls.clear()
     q, kc, out, args = _step([256, 2], [40000, 9000], nq=16, nkv=2, hs=512)
     fn(q, kc, kc, out, **args)
-    assert ("prefill", 256, 40000) in rec.calls and ("decode", 2, [0, 2], [9000], 2, None) in rec.calls
+    assert ("varlen", 256, [0, 256], [40000], 40000) in rec.calls and ("decode", 2, [0, 2], [9000], 2, None) in rec.calls
     assert not stock_calls
     rec.calls.clear()
     q, kc, out, args = _step([4], [5000], hs=128)
     fn(q, kc, kc, out, **args)
     assert not rec.calls and len(stock_calls) == 1
+
+
+def test_short_chunks_of_a_step_are_one_launch(monkeypatch):
+    """32 chunks of 100 tokens over short contexts, a long chunk and a decode in one step: the short chunks are ONE
+    varlen launch (the reference's single Triton sub-batch, int4_kv.py:313-323), the long chunk the prefill kernel,
+    the decode the split-KV batch; every output row gets its own request's value."""
+    rec = Recorder(monkeypatch)
+    stock, stock_calls = _stock_recorder()
+    fn = int4_kv.make_unified_attention(stock)
+    qlens = [100] * 32 + [512, 3]
+    used = [300 + 50 * i for i in range(32)] + [600, 20000]
+    q, kc, out, args = _step(qlens, used)
+    args["block_table"] = torch.arange(1, len(qlens) + 1, dtype=torch.int32)[:, None].repeat(1, 4)
+    fn(q, kc, kc, out, **args)
+    varlen = [c for c in rec.calls if c[0] == "varlen"]
+    assert len(varlen) == 1 and varlen[0][1] == 3200 and varlen[0][2] == list(range(0, 3201, 100))
+    assert varlen[0][3] == used[:32] and varlen[0][4] == max(used[:32])
+    assert ("prefill", 512, 600) in rec.calls and ("decode", 3, [0, 3], [20000], 3, None) in rec.calls
+    assert len(rec.calls) == 3 and not stock_calls
+    for i in range(len(qlens)):
+        a = sum(qlens[:i])
+        assert (out[a:a + qlens[i]] == i + 1).all()
 
 
 def test_prefill_routing_off_sends_chunks_to_stock(monkeypatch):

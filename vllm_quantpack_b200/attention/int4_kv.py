@@ -6,15 +6,16 @@ copy of vLLM's Triton kernel and launcher; this module instead replaces the stoc
 
   unified_attention_int4   decode steps (<= MAX_Q_SPLIT_KV query tokens per request, graph-capturable, no host
                            sync) -> split-KV decode kernel + merge; steps with prefill chunks -> one host read of the
-                           step's lengths, decode rows as a sub-batch, every other request -> the tcgen05 prefill
-                           kernel (int4_kv.py:281-333 routes only long chunks to FlashAttention)
+                           step's lengths per step, decode rows as a sub-batch, each long chunk -> the tcgen05
+                           prefill kernel, all other chunks -> one varlen launch of the split-KV kernel
+                           (int4_kv.py:281-333: long chunks to FlashAttention, the rest to one Triton sub-batch)
   reshape_and_cache_int4   fused RHT + quantize + pack store, int4 and k8v4 (k8v4_kv.py:152-163)
   single_rht               the transform both of the above apply, so any stock path left in use stays consistent
 
 Head sizes 256 and 512 (Gemma 4's global layers, int4_kv.py:302-305) are served. Calls the B200 path does not cover
 (sliding window, softcap, sinks, ALiBi, qq_bias, FP8 output, mm_prefix ranges, another head size) go to the stock
-`unified_attention_int4`, unchanged, for an int4 cache, and raise for a k8v4 cache (no stock kernel reads it). The stock `_launch_packed_attn` is
-left in place: only that stock path reaches it. The same environment switches are honoured:
+`unified_attention_int4`, unchanged, for an int4 cache, and raise for a k8v4 cache (no stock kernel reads it). The
+stock `_launch_packed_attn` is left in place: only that stock path reaches it. The same environment switches are honoured:
 VLLM_QUANTPACK_INT4_KV=0 (no patch), VLLM_QUANTPACK_INT4_FA_PREFILL=0 (prefill chunks stay stock),
 VLLM_QUANTPACK_INT4_DECODE="tile,warps,segments[,rows]" (segments: split count of the decode, "auto" = per call),
 VLLM_QUANTPACK_INT4_TILES (accepted; the B200 prefill tiles are fixed at 128 x 64).
@@ -30,6 +31,7 @@ MODULE = "vllm.v1.attention.ops.int4_per_token_head"
 PACKED_DTYPES = ("int4_per_token_head", "k8v4_per_token_head")   # caches served by the B200 kernels
 MAX_Q_SPLIT_KV = 4               # MTP / EAGLE verification with up to 3 draft tokens
 MAX_DECODE_ROWS = 32             # query tokens x query heads per KV head one decode CTA holds
+LONG_ROWS = 2048                 # query rows (tokens x heads per KV head) that make a chunk long at any context
 HEAD_SIZES = (256, 512)          # head sizes of the attention kernels
 PREFILL_TILES_DEFAULT = (128, 64, 10, 1)   # (BLOCK_M, TILE, warps, CTAs per SM) of the tcgen05 prefill kernel
 DECODE_TILES_DEFAULT = (64, 4, "auto")
@@ -96,25 +98,26 @@ class StepPlan:
     without a wait. The reference reads both lists per step (int4_kv.py:260-278) and rebuilds its sub-batch indices
     per layer; here the second and later layers of a step touch no host memory at all."""
 
-    def __init__(self, cu_seqlens_q, seqused_k, group, prefill_on):
+    def __init__(self, cu_seqlens_q, seqused_k, group, prefill_on, head_size=256):
         nseq = seqused_k.shape[0]
         both = torch.cat([cu_seqlens_q.to(torch.int64), seqused_k.to(torch.int64)]).tolist()
         self.cu, self.used = both[:nseq + 1], both[nseq + 1:]
-        self.dec, self.pre, self.stock = split_step(self.cu, self.used, group, prefill_on)
+        self.dec, self.pre, self.short, self.stock = split_step(self.cu, self.used, group, prefill_on, head_size)
         dev = cu_seqlens_q.device
         self.dec_batch = _SubBatch(self.dec, self.cu, self.used, dev) if self.dec else None
+        self.short_batch = _SubBatch(self.short, self.cu, self.used, dev) if self.short else None
         self.stock_batch = _SubBatch(self.stock, self.cu, self.used, dev) if self.stock else None
 
     @staticmethod
-    def of(cu_seqlens_q, seqused_k, group, prefill_on):
+    def of(cu_seqlens_q, seqused_k, group, prefill_on, head_size=256):
         """The step's plan, kept on vLLM's forward context (keyed by the length tensors themselves: another KV-cache
         group of the same step gets other tensors)."""
         step = _forward_step()
         plans = getattr(step, "_quantpack_b200_plans", None) if step is not None else None
-        key = (id(cu_seqlens_q), id(seqused_k), group, prefill_on)
+        key = (id(cu_seqlens_q), id(seqused_k), group, prefill_on, head_size)
         if plans is not None and key in plans and plans[key][0] is cu_seqlens_q and plans[key][1] is seqused_k:
             return plans[key][2]
-        plan = StepPlan(cu_seqlens_q, seqused_k, group, prefill_on)
+        plan = StepPlan(cu_seqlens_q, seqused_k, group, prefill_on, head_size)
         if step is not None:
             try:
                 if plans is None:
@@ -149,22 +152,28 @@ class _SubBatch:
         out[self.rows] = sub_out
 
 
-def split_step(cu, used, group, prefill_on=True):
-    """Requests of one step by path: (decode, prefill, stock) index lists. Decode: 1..MAX_Q_SPLIT_KV query tokens
-    whose rows fit one decode CTA; prefill: every other request with queries (the tcgen05 kernel), or the stock path
-    when prefill routing is off. Requests without queries are left out."""
-    dec, pre, stock = [], [], []
+def split_step(cu, used, group, prefill_on=True, head_size=256):
+    """Requests of one step by path: (decode, long, short, stock) index lists. Decode: 1..MAX_Q_SPLIT_KV query tokens
+    whose rows fit one decode CTA. The other requests with queries are prefill chunks: long ones (at least MIN_QUERY
+    tokens over at least MIN_CONTEXT cached tokens, or enough query rows to fill the machine on their own; head 256)
+    each go to the tcgen05 prefill kernel, the rest together to one varlen launch of the split-KV kernel, as the
+    reference sends its long chunks to FlashAttention and the rest to one Triton sub-batch (int4_kv.py:313-323).
+    With prefill routing off every chunk goes to the stock path. Requests without queries are left out."""
+    from .int4_prefill import MIN_CONTEXT, MIN_QUERY
+    dec, long, short, stock = [], [], [], []
     for i in range(len(used)):
         ql = cu[i + 1] - cu[i]
         if ql <= 0:
             continue
         if ql <= MAX_Q_SPLIT_KV and ql * group <= MAX_DECODE_ROWS:
             dec.append(i)
-        elif prefill_on:
-            pre.append(i)
-        else:
+        elif not prefill_on:
             stock.append(i)
-    return dec, pre, stock
+        elif head_size == 256 and ql >= MIN_QUERY and (used[i] >= MIN_CONTEXT or ql * group >= LONG_ROWS):
+            long.append(i)
+        else:
+            short.append(i)
+    return dec, long, short, stock
 
 
 def make_unified_attention(stock_unified, prefill_on=True):
@@ -200,9 +209,15 @@ def make_unified_attention(stock_unified, prefill_on=True):
         if max_seqlen_q <= MAX_Q_SPLIT_KV and max_seqlen_q * group <= MAX_DECODE_ROWS:
             # a decode step: no host read of the lengths (CUDA-graph capturable)
             return decode(q, out, args)
-        plan = StepPlan.of(cu_seqlens_q, seqused_k, group, prefill_on)
+        plan = StepPlan.of(cu_seqlens_q, seqused_k, group, prefill_on, q.shape[2])
         if plan.dec_batch is not None:
             plan.dec_batch.run(decode, q, out, args)
+        if plan.short_batch is not None:
+            plan.short_batch.run(
+                lambda qs, outs, a: ops.prefill_varlen(
+                    qs, k_cache, v_cache, outs, cu_seqlens_q=a["cu_seqlens_q"], seqused_k=a["seqused_k"],
+                    max_seqlen_k=a["max_seqlen_k"], block_table=a["block_table"], softmax_scale=softmax_scale,
+                    k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache), q, out, args)
         if plan.stock_batch is not None:
             if k8v4_kv.is_k8v4(k_cache):
                 raise NotImplementedError(f"{k8v4_kv.NAME}: prefill chunks need the B200 prefill kernel "

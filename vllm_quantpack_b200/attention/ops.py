@@ -255,3 +255,40 @@ def prefill(q, key_cache, value_cache, out, *, block_row, n, softmax_scale, k_sc
               rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)), int(tokens_after_keys), mode,
               lse_ptr, ws.data_ptr(), ws.numel() * ws.element_size(), _stream(q.device))
     return out
+
+
+def prefill_varlen(q, key_cache, value_cache, out, *, cu_seqlens_q, seqused_k, max_seqlen_k, block_table,
+                   softmax_scale, k_scale_cache, v_scale_cache, q_rotated=False, out_fp32_lse=None, ws=None):
+    """Several short prefill chunks in ONE launch (the reference's Triton sub-batch of the chunks that are not long,
+    vllm_quantpack/attention/int4_kv.py:313-323): request i's query tokens q[cu_seqlens_q[i]:cu_seqlens_q[i + 1]] are
+    the last positions of its context of seqused_k[i] cached tokens, causal among themselves, read through
+    block_table[i]. Split on the device into sub-sequences of 32 / group tokens for the split-KV kernel, so nothing
+    is read back to the host; max_seqlen_k (a host int, an upper bound of seqused_k) sizes the split count.
+    `out` as in prefill."""
+    hs, nq, T = q.shape[-1], q.shape[1], q.shape[0]
+    lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
+    for name, t in (("cu_seqlens_q", cu_seqlens_q), ("seqused_k", seqused_k), ("block_table", block_table)):
+        if t.dtype != torch.int32 or t.stride(-1) != 1:
+            raise TypeError(f"{name} must be int32 with contiguous rows")
+    if q.stride(-1) != 1 or out.stride(-1) != 1:
+        raise ValueError("q / out rows must be contiguous")
+    dt = _dtype_code(q, "prefill_varlen")
+    chunks = seqused_k.shape[0]
+    lib = _lib.load()
+    wbytes = lib.qp_prefill_varlen_workspace_bytes(T, chunks, nq, lay.nkv, hs, int(max_seqlen_k))
+    if ws is None:
+        ws = workspace(q.device, wbytes)
+    if out_fp32_lse is not None:
+        if out.dtype != torch.float32 or out_fp32_lse.dtype != torch.float32 or not out_fp32_lse.is_contiguous():
+            raise TypeError("out and lse must be fp32 (lse contiguous) for the RHT-domain output")
+        mode, lse_ptr = 1, out_fp32_lse.data_ptr()
+    else:
+        if out.dtype != q.dtype:
+            raise TypeError("out dtype must match q")
+        mode, lse_ptr = 0, None
+    _lib.call("qp_prefill_varlen", lay.fmt, dt, q.data_ptr(), q.stride(0), q.stride(1), out.data_ptr(),
+              out.stride(0), out.stride(1), T, chunks, cu_seqlens_q.data_ptr(), seqused_k.data_ptr(),
+              int(max_seqlen_k), block_table.data_ptr(), block_table.stride(0), *lay.args(), nq, lay.nkv, hs,
+              float(softmax_scale), rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)), mode,
+              lse_ptr, ws.data_ptr(), ws.numel() * ws.element_size(), _stream(q.device))
+    return out

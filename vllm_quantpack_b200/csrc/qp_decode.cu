@@ -90,6 +90,10 @@ struct DecodeParams {
   // over chunk_n cached keys through block-table row 0, served as sub-sequences of chunk_q tokens (grid z), each
   // reading only the keys its last token sees. cu_seqlens_q / seqused_k are not read.
   int chunk_q, chunk_n;
+  // subseq != null: sequence z of the grid is subseq[z] = {first query token, query tokens, keys its last token
+  // sees, block-table row}, causal inside it (built on the device by varlen_table_kernel; entries past the real ones
+  // hold 0 query tokens). cu_seqlens_q / seqused_k are not read.
+  const int4* subseq;
   int num_splits;
   float* part_o;    // [tokens][nq][splits][HS]
   float* part_lse;  // [tokens][nq][splits], log2 units
@@ -270,7 +274,14 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
   // to n - 1) and its block-table row
   int q0, qlen, n, vis_base;
   const int32_t* btab;
-  if (p.chunk_q > 0) {
+  if (p.subseq != nullptr) {
+    const int4 e = p.subseq[seq];
+    q0 = e.x;
+    qlen = e.y;
+    n = e.z;
+    vis_base = n - qlen;
+    btab = p.block_table + static_cast<int64_t>(e.w) * p.bt_stride;
+  } else if (p.chunk_q > 0) {
     q0 = seq * p.chunk_q;
     qlen = min(p.chunk_q, static_cast<int>(p.num_tokens) - q0);
     vis_base = p.chunk_n - static_cast<int>(p.num_tokens) + q0 + p.tokens_after;
@@ -412,12 +423,12 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
     wait_all(&bars[D_Q_FULL], 0);
     for (int i = 0; i < ntl && !failed; ++i) {
       const int b = i & 1;
-      if (i >= 2) wait_all(&bars[D_S_FREE + b], ((i - 2) >> 1) & 1);
       const uint32_t sd = tmem + TM::S + NR * b;
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {  // key operand chunk ch: channels [256 ch, 256 ch + 256), slot k % AKS
         const int k = i * NCH + ch, sl = k % AKS;
         wait_all(&bars[D_AK_FULL + sl], (k / AKS) & 1);
+        if (ch == 0 && i >= 2) wait_all(&bars[D_S_FREE + b], ((i - 2) >> 1) & 1);  // S buffer b read by the softmax
         if (failed) break;
         tc_fence_after();
         const uint32_t ak = tmem + (sl ? TM::AK1 : TM::AK0);
@@ -487,8 +498,8 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
         tc_fence_after();
         const uint32_t dst = tmem + (sl ? TM::AK1 : TM::AK0) + lane_off;
         const uint8_t* kc = cell + ch * (CL::KB / NCH);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {  // 32 TMEM columns (64 channels) per store
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {  // 32 TMEM columns (64 channels) per store (a loop: instruction-cache size)
           uint32_t a[32];
           if constexpr (FMT == FMT_INT4) {
 #pragma unroll
@@ -568,8 +579,8 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
         const uint8_t* raw = smem + SM::OFF_RAW + stage * SM::RAW + CL::V + 32 * q * WPT + 4 * g;
 #pragma unroll
         for (int v = 0; v < WPT; ++v) {
-#pragma unroll
-          for (int kb = 0; kb < VK / (16 * NB); ++kb) {
+#pragma unroll 1
+          for (int kb = 0; kb < VK / (16 * NB); ++kb) {  // a loop, not unrolled: instruction-cache size
             uint32_t r[4][4 * NB];  // [store (channel tile 2 v + c, lane half lb)][registers]
 #pragma unroll
             for (int rr = 0; rr < NB; ++rr) {
@@ -1297,6 +1308,131 @@ int decode_chunk_prefill(int fmt, int dtype, const void* q, int64_t q_stride_tok
   if (rc) return rc;
   return merge_dispatch(decode_merge_params(dp, head_size, out_mode, out, out_stride_token, out_stride_head, lse_out),
                         dtype, head_size, qlen, st, true);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Short prefill chunks of several sequences in one launch of K1 (the counterpart of the reference's Triton 2D
+// sub-batch for every chunk that is not long, int4_kv.py:313-323). Chunk i (query tokens [cu[i], cu[i + 1]), its
+// last token seeing used[i] keys through block-table row i) becomes ceil(qlen_i / cq) sub-sequences of cq = 32 /
+// group tokens, causal inside each; the table is built on the device from the same length tensors, so the call reads
+// nothing back to the host. The grid holds an upper bound of sub-sequences computed from host-known sizes; entries
+// past the real ones hold 0 query tokens and their CTAs return at once.
+__global__ void __launch_bounds__(32) varlen_table_kernel(const int32_t* cu, const int32_t* used, int num_chunks,
+                                                          int cq, int upper, int4* table) {
+  const int lane = threadIdx.x;
+  int base = 0;
+  for (int c0 = 0; c0 < num_chunks; c0 += 32) {  // 32 chunks at a time, offsets by a warp scan
+    const int i = c0 + lane;
+    int q0 = 0, ql = 0, n = 0;
+    if (i < num_chunks) {
+      q0 = cu[i];
+      ql = max(0, cu[i + 1] - q0);
+      n = used[i];
+    }
+    const int ns = (ql + cq - 1) / cq;
+    int incl = ns;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += t;
+    }
+    const int off = base + incl - ns;
+    for (int j = 0; j < ns && off + j < upper; ++j) {
+      const int a = j * cq, len = min(cq, ql - a);
+      table[off + j] = make_int4(q0 + a, len, n - ql + a + len, i);  // keys seen by the sub-sequence's last token
+    }
+    base += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  for (int e = base + lane; e < upper; e += 32) table[e] = make_int4(0, 0, 0, 0);
+}
+
+static int varlen_upper(int64_t num_q_tokens, int num_chunks, int cq) {
+  return static_cast<int>((num_q_tokens + cq - 1) / cq + num_chunks);
+}
+
+// [decode workspace of the tokens at the launch's split count][sub-sequence table, upper x 16 B]
+static void varlen_sizes(int64_t num_q_tokens, int num_chunks, int num_q_heads, int num_kv_heads, int head_size,
+                         int max_seqlen_k, int* upper, int* splits, int64_t* table_off) {
+  const int cq = chunk_q_of(num_q_heads / num_kv_heads);
+  *upper = varlen_upper(num_q_tokens, num_chunks, cq);
+  *splits = qp_decode_num_splits(*upper, num_kv_heads, max_seqlen_k, 0);
+  *table_off = (qp_decode_workspace_bytes(num_q_tokens, num_q_heads, head_size, *splits) + 15) / 16 * 16;
+}
+
+extern "C" int64_t qp_prefill_varlen_workspace_bytes(int64_t num_q_tokens, int num_chunks, int num_q_heads,
+                                                     int num_kv_heads, int head_size, int max_seqlen_k) {
+  if (num_q_tokens <= 0 || num_chunks <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads ||
+      !chunk_q_of(num_q_heads / num_kv_heads))
+    return 0;
+  int upper = 0, splits = 0;
+  int64_t off = 0;
+  varlen_sizes(num_q_tokens, num_chunks, num_q_heads, num_kv_heads, head_size, max_seqlen_k, &upper, &splits, &off);
+  return off + static_cast<int64_t>(upper) * 16;
+}
+
+extern "C" int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                                 void* out, int64_t out_stride_token, int64_t out_stride_head, int64_t num_q_tokens,
+                                 int num_chunks, const int32_t* cu_seqlens_q, const int32_t* seqused_k,
+                                 int max_seqlen_k, const int32_t* block_table, int64_t block_table_stride,
+                                 const void* cache, int block_size, int64_t block_stride, int64_t head_stride,
+                                 int64_t slot_stride, int64_t k_off, int64_t ks_off, int64_t v_off, int64_t vs_off,
+                                 int num_q_heads, int num_kv_heads, int head_size, float softmax_scale,
+                                 const uint32_t* rht_sign_bits, int q_rotated, int out_mode, float* lse_out,
+                                 void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = decode_check_cache("prefill varlen", fmt, dtype, head_size, cache, block_size, block_stride, head_stride,
+                              slot_stride, k_off, ks_off, v_off, vs_off);
+  if (rc) return rc;
+  if (num_chunks < 0 || num_q_tokens < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads ||
+      max_seqlen_k < 0)
+    return set_error(QP_ERR_INVALID, "prefill varlen: bad sizes (chunks %d, tokens %lld, heads %d/%d)", num_chunks,
+                     (long long)num_q_tokens, num_q_heads, num_kv_heads);
+  if (num_chunks == 0 || num_q_tokens == 0) return QP_OK;
+  if (out_mode != 0 && out_mode != 1) return set_error(QP_ERR_INVALID, "prefill varlen: out_mode %d", out_mode);
+  const int group = num_q_heads / num_kv_heads;
+  const int cq = chunk_q_of(group);
+  if (!cq) return set_error(QP_ERR_UNSUPPORTED, "prefill varlen: %d query heads per KV head > %d", group, DEC_MAX_ROWS);
+  if (num_q_tokens > 0x7fffffff || varlen_upper(num_q_tokens, num_chunks, cq) > 65535 || num_kv_heads > 65535)
+    return set_error(QP_ERR_UNSUPPORTED, "prefill varlen: grid too large (%lld tokens, %d chunks)",
+                     (long long)num_q_tokens, num_chunks);
+  if (!q || !out || !cu_seqlens_q || !seqused_k || !block_table || !cache || !rht_sign_bits || !workspace)
+    return set_error(QP_ERR_INVALID, "prefill varlen: null pointer");
+  int upper = 0, splits = 0;
+  int64_t table_off = 0;
+  varlen_sizes(num_q_tokens, num_chunks, num_q_heads, num_kv_heads, head_size, max_seqlen_k, &upper, &splits,
+               &table_off);
+  const int64_t need = table_off + static_cast<int64_t>(upper) * 16;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15) || workspace_bytes < need)
+    return set_error(QP_ERR_WORKSPACE, "prefill varlen: workspace of %lld bytes < %lld", (long long)workspace_bytes,
+                     (long long)need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int4* table = reinterpret_cast<int4*>(static_cast<uint8_t*>(workspace) + table_off);
+  varlen_table_kernel<<<1, 32, 0, st>>>(cu_seqlens_q, seqused_k, num_chunks, cq, upper, table);
+  rc = check_launch("prefill varlen table");
+  if (rc) return rc;
+  DecodeParams dp{};
+  dp.q = q;
+  dp.q_st = q_stride_token;
+  dp.q_sh = q_stride_head;
+  dp.block_table = block_table;
+  dp.bt_stride = block_table_stride;
+  dp.cache = static_cast<const uint8_t*>(cache);
+  dp.block_size = block_size;
+  dp.block_stride = block_stride;
+  dp.head_stride = head_stride;
+  dp.nq = num_q_heads;
+  dp.nkv = num_kv_heads;
+  dp.group = group;
+  dp.qk_scale = softmax_scale / static_cast<float>(head_size) * LOG2E;
+  dp.sign_bits = rht_sign_bits;
+  dp.q_rotated = q_rotated;
+  dp.num_tokens = num_q_tokens;
+  dp.subseq = table;
+  dp.num_splits = splits;
+  decode_bind_workspace(dp, workspace, head_size);
+  rc = launch_decode(fmt, dtype, head_size, dp, cq * group, upper, st);
+  if (rc) return rc;
+  return merge_dispatch(decode_merge_params(dp, head_size, out_mode, out, out_stride_token, out_stride_head, lse_out),
+                        dtype, head_size, num_q_tokens, st, true);
 }
 
 extern "C" int qp_merge_attn_partials(int dtype, int head_size, int64_t num_tokens, int num_q_heads, int num_parts,
