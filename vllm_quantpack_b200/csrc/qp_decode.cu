@@ -111,17 +111,19 @@ struct Cell {
 //           at [128, 256); S (2 x NR) and O^T (2 channel tiles x NR) from 256.
 //   HS 512: key operand chunks (channels 0-255, then 256-511 of a tile) in AKS slots of 128 columns from 0; two
 //           32-key value slots (four channel tiles of 16 columns) after them; S and O^T (4 channel tiles x NR) last.
-//           At NR 32 only one key slot fits (448 columns; with two, the value slots would hold 16 keys, and the
-//           value warps could then release a raw stage only after the PV MMAs of its tile started, which the
-//           three-stage k8v4 ring cannot wait for: the next tile's QK needs two fresh stages first).
+//           At NR 32 only one key slot fits (448 columns; the key conversion of a chunk then waits for the previous
+//           chunk's QK MMAs). Two key slots would leave room for 16-key value slots only: the value warps then release
+//           a raw stage only once the PV MMAs of its tile have started, after the next tile's QK, which needs two fresh
+//           raw stages first, so the three-stage k8v4 ring would deadlock; with int4's four stages that plan runs,
+//           but measured slower (262k-token decode 0.214 against 0.193 ms, 1024-query prefill 30.1 against 25.1 ms).
 template <int HS, int NR>
 struct DecTmem {
-  static constexpr int NCH = HS / 256;                       // key operand chunks per tile
-  static constexpr int MT = HS / 128;                        // channel tiles of V^T and O^T
+  static constexpr int NCH = HS / 256;                         // key operand chunks per tile
+  static constexpr int MT = HS / 128;                          // channel tiles of V^T and O^T
   static constexpr int AKS = (HS == 256 || NR <= 16) ? 2 : 1;  // key operand chunk slots
-  static constexpr int VK = HS == 256 ? 64 : 32;             // keys per value slot
-  static constexpr int VSLOTS = DEC_TILE / VK;               // value slots per tile
-  static constexpr int SLOT = MT * VK / 2;                   // TMEM columns of a value slot
+  static constexpr int VK = HS == 256 ? 64 : 32;               // keys per value slot
+  static constexpr int VSLOTS = DEC_TILE / VK;                 // value slots per tile
+  static constexpr int SLOT = MT * VK / 2;                     // TMEM columns of a value slot
   static constexpr uint32_t AK0 = 0, AK1 = HS == 256 ? 384 : 128;
   static constexpr uint32_t AV = HS == 256 ? 128 : 128 * AKS;
   static constexpr uint32_t S = AV + 2 * SLOT;
@@ -257,6 +259,7 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
   using SM = DecSmem<FMT, HS, NR>;
   using CL = Cell<FMT, HS>;
   using TM = DecTmem<HS, NR>;
+  static_assert(TM::VK >= 32 || DecSmem<FMT, HS, NR>::RS >= 4, "16-key value slots need a four-stage raw ring");
   constexpr int CELL = SM::CELL, RS = SM::RS, KPS = SM::KPS, SK = SM::SK, SPT = SM::SPT;
   constexpr int NCH = TM::NCH, MT = TM::MT, VK = TM::VK, VSLOTS = TM::VSLOTS, AKS = TM::AKS;
   constexpr int QREC = q_rec_bytes(HS);

@@ -888,12 +888,13 @@ using namespace qp;
 // [part_lse qlen*nq*parts f32], each 256-byte aligned.
 static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
-// Key chunks of a chunk prefill: the cache of all KV heads in pieces of at most 40 MB, so that the chunk the CTAs work
-// on, and the start of the next one that the first CTAs to finish already read, stay in the 126 MB L2; at most
-// PF_MAX_CHUNKS.
+// Key chunks of a chunk prefill: the cache of all KV heads in pieces of at most 80 MB, so that the chunk the CTAs work
+// on stays in the 126 MB L2; at most PF_MAX_CHUNKS. Measured at c3 (242 MB): 8.05 ms with 80 MB chunks, 8.22 with
+// 40 MB, 8.58 with 20 MB (more pieces to fold and more piece epilogues), 8.06 with one contiguous split (10 GB of
+// DRAM reads, which this kernel, bound by its CUDA-core work, does not feel yet).
 static int prefill_chunks(int n, int nkv, int cell) {
   const int64_t bytes = static_cast<int64_t>(n) * nkv * cell;
-  const int64_t c = (bytes + (40ll << 20) - 1) / (40ll << 20);
+  const int64_t c = (bytes + (80ll << 20) - 1) / (80ll << 20);
   return static_cast<int>(std::min<int64_t>(PF_MAX_CHUNKS, std::max<int64_t>(1, c)));
 }
 
