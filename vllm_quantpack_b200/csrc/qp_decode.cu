@@ -56,13 +56,16 @@ constexpr int DEC_MAX_ROWS = 32;
 #endif
 constexpr int SMX_HALVES = QP_DEC_SMX_HALVES;  // softmax warps per TMEM lane quarter (each takes RL / halves rows)
 static_assert(SMX_HALVES == 1 || SMX_HALVES == 2, "one or two softmax warps per lane quarter");
-constexpr int DEC_WARPS = 10 + 4 * SMX_HALVES;
+constexpr int DEC_WARPS = 11 + 4 * SMX_HALVES;
 constexpr int DEC_THREADS = 32 * DEC_WARPS;
 // registers per thread one CTA may hold: each SM sub-partition's 16384 registers host every fourth warp
 constexpr int DEC_REGS = (16384 / (32 * ((DEC_WARPS + 3) / 4))) & ~7;
-// warp 0 producer, 1 MMA issuer, 2-5 key operand, 6-9 value operand, 10.. softmax (SMX_HALVES per lane quarter)
-constexpr int W_MMA = 1, W_VAL = 6, W_SMX = 10;
-constexpr int SMX_THREADS = 32 * (DEC_WARPS - W_SMX);
+// warp 0 producer, 1 QK issuer, 2-5 key operand, 6-9 value operand, 10.. softmax (SMX_HALVES per lane quarter), last
+// the PV issuer. The two MMA issuers sit on different SM sub-partitions: issuing a tcgen05.mma takes that
+// sub-partition's issue slots from the operand warps beside it, and with all 32 MMAs of a tile on one
+// sub-partition its value warp fell 1,500 cycles behind the other three every tile (clock64 stamps per role).
+constexpr int W_MMA = 1, W_VAL = 6, W_SMX = 10, W_PV = W_SMX + 4 * SMX_HALVES;
+constexpr int SMX_THREADS = 32 * 4 * SMX_HALVES;
 // prepared query row: HS fp16 in operand order, then 4 fp32 (row scale, three zero words)
 constexpr int q_rec_bytes(int hs) { return hs * 2 + 16; }
 constexpr float LOG2E = 1.4426950408889634f;
@@ -332,7 +335,7 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
     }
     mbar_init(&bars[D_PV_DONE], 1);
     mbar_init(&bars[D_PV_DONE + 1], 1);
-    mbar_init(&bars[D_FINAL], 1);
+    mbar_init(&bars[D_FINAL], 2);  // one commit per MMA issuer
     fence_mbar_init();
   }
   if (warp == W_MMA) {
@@ -381,8 +384,8 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
     if (lane == 0)
       for (int k = max(0, u - RS); k < u; ++k)
         mbar_wait_bounded(&bars[D_RAW_FULL + k % RS], (k / RS) & 1, 100000000ull);
-  } else if (warp == W_MMA) {
-    // ------------------------------------------------------------------ MMA issuer
+  } else if (warp == W_MMA || warp == W_PV) {
+    // ------------------------------------------------------------------ MMA issuers (QK, PV)
     // The whole warp waits (convergent, so descriptors and TMEM addresses are warp-uniform); one elected lane issues.
     constexpr uint32_t ID = f16_idesc(128, NR, false);
     // Every B operand descriptor is the base descriptor of its buffer plus a compile-time start-address offset (the
@@ -423,6 +426,11 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
       if (elect_one()) umma_commit(&bars[D_PV_DONE + bj]);
       __syncwarp();
     };
+    if (warp == W_PV) {
+      for (int j = 0; j < ntl && !failed; ++j) issue_pv(j);
+      if (elect_one()) umma_commit(&bars[D_FINAL]);
+      __syncwarp();
+    } else {
     wait_all(&bars[D_Q_FULL], 0);
     for (int i = 0; i < ntl && !failed; ++i) {
       const int b = i & 1;
@@ -446,13 +454,11 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
         }
         __syncwarp();
       }
-      if (failed) break;
-      if (i >= 1) issue_pv(i - 1);
     }
-    if (!failed) issue_pv(ntl - 1);
     if (elect_one()) umma_commit(&bars[D_FINAL]);
     __syncwarp();
-    mbar_wait_spin(&bars[D_FINAL], 0, 100000000ull);
+    mbar_wait_spin(&bars[D_FINAL], 0, 100000000ull);  // both issuers' MMAs have completed
+    }
   } else if (warp < W_VAL) {
     // ------------------------------------------------------------------ key operand (thread = key = TMEM lane)
     const int q = warp & 3, kl = 32 * q + lane;
