@@ -56,16 +56,23 @@ constexpr int DEC_MAX_ROWS = 32;
 #endif
 constexpr int SMX_HALVES = QP_DEC_SMX_HALVES;  // softmax warps per TMEM lane quarter (each takes RL / halves rows)
 static_assert(SMX_HALVES == 1 || SMX_HALVES == 2, "one or two softmax warps per lane quarter");
-constexpr int DEC_WARPS = 11 + 4 * SMX_HALVES;
-constexpr int DEC_THREADS = 32 * DEC_WARPS;
-// registers per thread one CTA may hold: each SM sub-partition's 16384 registers host every fourth warp
-constexpr int DEC_REGS = (16384 / (32 * ((DEC_WARPS + 3) / 4))) & ~7;
-// warp 0 producer, 1 QK issuer, 2-5 key operand, 6-9 value operand, 10.. softmax (SMX_HALVES per lane quarter), last
-// the PV issuer. The two MMA issuers sit on different SM sub-partitions: issuing a tcgen05.mma takes that
-// sub-partition's issue slots from the operand warps beside it, and with all 32 MMAs of a tile on one
-// sub-partition its value warp fell 1,500 cycles behind the other three every tile (clock64 stamps per role).
-constexpr int W_MMA = 1, W_VAL = 6, W_SMX = 10, W_PV = W_SMX + 4 * SMX_HALVES;
+// warp 0 producer, 1 QK issuer, 2-5 key operand, 6-9 value operand, 10.. softmax (SMX_HALVES per lane quarter), then
+// the PV issuer and, at head 256 with up to 24 rows, a second set of four value-operand warps (W_VB..). The two MMA
+// issuers sit on different SM sub-partitions: issuing a tcgen05.mma takes that sub-partition's issue slots from the
+// operand warps beside it, and with all 32 MMAs of a tile on one sub-partition its value warp fell 1,500 cycles
+// behind the other three every tile (clock64 stamps per role). The value conversion sets the tile period, so where
+// the registers allow (96 a thread: the softmax of 32 rows would spill) two warps per lane quarter share it.
+constexpr int W_MMA = 1, W_VAL = 6, W_SMX = 10, W_PV = W_SMX + 4 * SMX_HALVES, W_VB = W_PV + 1;
 constexpr int SMX_THREADS = 32 * 4 * SMX_HALVES;
+
+template <int HS, int RL>
+struct DecWarps {
+  static constexpr int VSETS = (HS == 256 && RL <= 24) ? 2 : 1;  // value-operand warp sets
+  static constexpr int WARPS = W_VB + 4 * (VSETS - 1);
+  static constexpr int THREADS = 32 * WARPS;
+  // registers per thread one CTA may hold: each SM sub-partition's 16384 registers host every fourth warp
+  static constexpr int REGS = (16384 / (32 * ((WARPS + 3) / 4))) & ~7;
+};
 // prepared query row: HS fp16 in operand order, then 4 fp32 (row scale, three zero words)
 constexpr int q_rec_bytes(int hs) { return hs * 2 + 16; }
 constexpr float LOG2E = 1.4426950408889634f;
@@ -264,7 +271,7 @@ __global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_
 
 // ---------------------------------------------------------------------------------------------------- K1
 template <int FMT, int DT, int HS, int NR, int RL>
-__global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
+__global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const DecodeParams p) {
   using SM = DecSmem<FMT, HS, NR>;
   using CL = Cell<FMT, HS>;
   using TM = DecTmem<HS, NR>;
@@ -272,6 +279,7 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
   constexpr int CELL = SM::CELL, RS = SM::RS, KPS = SM::KPS, SK = SM::SK, SPT = SM::SPT;
   constexpr int NCH = TM::NCH, MT = TM::MT, VK = TM::VK, VSLOTS = TM::VSLOTS, AKS = TM::AKS, AVS = TM::AVS;
   constexpr int CHC = TM::CHC;
+  constexpr int VSETS = DecWarps<HS, RL>::VSETS, THREADS = DecWarps<HS, RL>::THREADS;
   constexpr int QREC = q_rec_bytes(HS);
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::OFF_BAR);
@@ -314,7 +322,7 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
   const int tile0 = split * tps;
   const int ntl = max(0, min(tile0 + tps, n_tiles) - tile0);
   if (ntl == 0) {  // empty segment: lse = -inf
-    for (int r = tid; r < rows; r += DEC_THREADS) {
+    for (int r = tid; r < rows; r += THREADS) {
       const int tok = q0 + r / p.group, qh = kvh * p.group + r % p.group;
       p.part_lse[(static_cast<int64_t>(tok) * p.nq + qh) * p.num_splits + split] = -INFINITY;
     }
@@ -324,11 +332,11 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
   if (tid == 0) {
     for (int s = 0; s < RS; ++s) {
       mbar_init(&bars[D_RAW_FULL + s], 1);
-      mbar_init(&bars[D_RAW_EMPTY + s], 4 / SPT + 4);  // the key warps of the stage's keys, every value warp
+      mbar_init(&bars[D_RAW_EMPTY + s], 4 / SPT + 4 * VSETS);  // the key warps of the stage's keys, every value warp
     }
     for (int s = 0; s < KPS; ++s) {
       mbar_init(&bars[D_KP_FULL + s], 4);
-      mbar_init(&bars[D_KP_FREE + s], 4 + 4 * SMX_HALVES);
+      mbar_init(&bars[D_KP_FREE + s], 4 * VSETS + 4 * SMX_HALVES);
     }
     mbar_init(&bars[D_Q_FULL], 4 * SMX_HALVES);
     for (int b = 0; b < 2; ++b) {
@@ -341,7 +349,7 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
       mbar_init(&bars[D_AK_FREE + b], 1);
     }
     for (int b = 0; b < AVS; ++b) {
-      mbar_init(&bars[D_AV_FULL + b], 4);
+      mbar_init(&bars[D_AV_FULL + b], 4 * VSETS);
       mbar_init(&bars[D_AV_FREE + b], 1);
     }
     mbar_init(&bars[D_PV_DONE], 1);
@@ -563,7 +571,7 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
         mbar_arrive(&bars[D_RAW_EMPTY + stage]);
       }
     }
-  } else if (warp < W_SMX) {
+  } else if (warp < W_SMX || warp >= W_VB) {
     // ------------------------------------------------------------------ value operand (V^T, lane = channel)
     // Thread (g, t) of quarter q converts the words wv = 8 (q HS/256 + v) + g, v < HS/256 (channels 8 wv + [0, 8)),
     // of keys 4 t + [0, 4) of every 16-key block. Lane 32 q + g + 8 m of channel tile 2 v + c holds channel
@@ -571,6 +579,9 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
     constexpr int WPT = HS / 256;
     constexpr int NB = VK >= 32 ? 2 : 1;  // 16-key blocks per TMEM store
     const int q = warp & 3, g = lane >> 2, t = lane & 3;
+    constexpr int KBN = VK / (16 * NB);  // block groups (one TMEM store each) per slot, shared by the VSETS sets
+    static_assert(KBN % VSETS == 0, "value block groups split evenly over the warp sets");
+    const int kb0 = (warp >= W_VB ? 1 : 0) * (KBN / VSETS);
     const uint32_t* zb = reinterpret_cast<const uint32_t*>(smem + SM::OFF_ZB);
     for (int i = 0; i < ntl && !failed; ++i) {
       const int ki = i % KPS;
@@ -596,7 +607,7 @@ __global__ void __maxnreg__(DEC_REGS) decode_kernel(const DecodeParams p) {
 #pragma unroll
         for (int v = 0; v < WPT; ++v) {
 #pragma unroll 1
-          for (int kb = 0; kb < VK / (16 * NB); ++kb) {  // a loop, not unrolled: instruction-cache size
+          for (int kb = kb0; kb < kb0 + KBN / VSETS; ++kb) {  // a loop, not unrolled: instruction-cache size
             uint32_t r[4][4 * NB];  // [store (channel tile 2 v + c, lane half lb)][registers]
 #pragma unroll
             for (int rr = 0; rr < NB; ++rr) {
@@ -1063,7 +1074,7 @@ static int launch_decode_t(const DecodeParams& dp, int grid_z, cudaStream_t st) 
   // it before reading the query rows)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(dp.num_splits), static_cast<unsigned>(dp.nkv), static_cast<unsigned>(grid_z));
-  cfg.blockDim = dim3(DEC_THREADS);
+  cfg.blockDim = dim3(DecWarps<HS, RL>::THREADS);
   cfg.dynamicSmemBytes = SM::BYTES;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
