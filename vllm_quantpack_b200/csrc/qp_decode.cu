@@ -56,12 +56,14 @@ constexpr int DEC_MAX_ROWS = 32;
 #endif
 constexpr int SMX_HALVES = QP_DEC_SMX_HALVES;  // softmax warps per TMEM lane quarter (each takes RL / halves rows)
 static_assert(SMX_HALVES == 1 || SMX_HALVES == 2, "one or two softmax warps per lane quarter");
+
 // warp 0 producer, 1 QK issuer, 2-5 key operand, 6-9 value operand, 10.. softmax (SMX_HALVES per lane quarter), then
 // the PV issuer and, at head 256 with up to 24 rows, a second set of four value-operand warps (W_VB..). The two MMA
 // issuers sit on different SM sub-partitions: issuing a tcgen05.mma takes that sub-partition's issue slots from the
 // operand warps beside it, and with all 32 MMAs of a tile on one sub-partition its value warp fell 1,500 cycles
 // behind the other three every tile (clock64 stamps per role). The value conversion sets the tile period, so where
-// the registers allow (96 a thread: the softmax of 32 rows would spill) two warps per lane quarter share it.
+// the registers allow (96 a thread; the softmax of 32 rows would spill) two warps per lane quarter share it, each
+// converting half of every value slot (c2a, same box: 99.1 -> 91.1 us).
 constexpr int W_MMA = 1, W_VAL = 6, W_SMX = 10, W_PV = W_SMX + 4 * SMX_HALVES, W_VB = W_PV + 1;
 constexpr int SMX_THREADS = 32 * 4 * SMX_HALVES;
 
@@ -116,37 +118,31 @@ struct Cell {
   static constexpr int KS = KB, V = KB + 4, VS = KB + 4 + HS / 2;  // field offsets
 };
 
-// TMEM columns (512) of the head size's operands and accumulators: a ring of AKS key-operand chunk slots (a chunk is
-// CHC channels of the tile's 128 keys, CHC / 2 columns), a ring of AVS value slots (VK keys x MT channel tiles, SLOT
-// columns each), S (2 x NR) and O^T (MT channel tiles x NR).
-//   HS 256: three 128-channel key slots [0, 192), three 64-key value slots [192, 384), S and O^T from 384 (all 512
-//           columns at NR 32). With only two value slots a value slot of tile i waited for the PV MMAs of tile i - 1
-//           to free it, and that round trip plus the slot's conversion was the tile period (clock64 stamps per role:
-//           2,720 cycles, of which ~550 waiting); the third slot lets the value warps run a slot ahead of the PVs.
-//   HS 512: 256-channel key slots, two (NR 16) or one (NR 32: 448 columns would not leave room for two with 32-key
-//           value slots); 32-key value slots, three where they fit. Two key slots with 16-key value slots at NR 32
-//           measured slower (262k-token decode 0.214 against 0.193 ms), and with k8v4's three raw stages they would
-//           deadlock: the value warps then release a raw stage only after the PV MMAs of its tile started, which
-//           follows the next tile's QK, which needs two fresh raw stages first.
+// TMEM columns (512) of the head size's operands and accumulators.
+//   HS 256: key operand chunks at [0, 128) and [384, 512); two 64-key value slots (two channel tiles of 32 columns)
+//           at [128, 256); S (2 x NR) and O^T (2 channel tiles x NR) from 256.
+//   HS 512: key operand chunks (channels 0-255, then 256-511 of a tile) in AKS slots of 128 columns from 0; two
+//           32-key value slots (four channel tiles of 16 columns) after them; S and O^T (4 channel tiles x NR) last.
+//           At NR 32 only one key slot fits (448 columns; the key conversion of a chunk then waits for the previous
+//           chunk's QK MMAs). Two key slots would leave room for 16-key value slots only: the value warps then release
+//           a raw stage only once the PV MMAs of its tile have started, after the next tile's QK, which needs two fresh
+//           raw stages first, so the three-stage k8v4 ring would deadlock; with int4's four stages that plan runs,
+//           but measured slower (262k-token decode 0.214 against 0.193 ms, 1024-query prefill 30.1 against 25.1 ms).
 template <int HS, int NR>
 struct DecTmem {
-  static constexpr int CHC = HS == 256 ? 128 : 256;             // channels per key operand chunk
-  static constexpr int NCH = HS / CHC;                          // key operand chunks per tile
-  static constexpr int AKW = CHC / 2;                           // TMEM columns of a key slot
-  static constexpr int AKS = HS == 256 ? 3 : (NR <= 16 ? 2 : 1);  // key slots
-  static constexpr int MT = HS / 128;                           // channel tiles of V^T and O^T
-  static constexpr int VK = HS == 256 ? 64 : 32;                // keys per value slot
-  static constexpr int VSLOTS = DEC_TILE / VK;                  // value slots per tile
-  static constexpr int SLOT = MT * VK / 2;                      // TMEM columns of a value slot
-  static constexpr uint32_t AK = 0;                             // key slot s at AK + AKW s
-  static constexpr uint32_t AV = AKS * AKW;                     // value slot s at AV + SLOT s
-  static constexpr int AVS = (512 - static_cast<int>(AV) - (2 + MT) * NR) / SLOT >= 3 ? 3 : 2;  // value slots
-  static constexpr uint32_t S = AV + AVS * SLOT;
+  static constexpr int NCH = HS / 256;                         // key operand chunks per tile
+  static constexpr int MT = HS / 128;                          // channel tiles of V^T and O^T
+  static constexpr int AKS = (HS == 256 || NR <= 16) ? 2 : 1;  // key operand chunk slots
+  static constexpr int VK = HS == 256 ? 64 : 32;               // keys per value slot
+  static constexpr int VSLOTS = DEC_TILE / VK;                 // value slots per tile
+  static constexpr int SLOT = MT * VK / 2;                     // TMEM columns of a value slot
+  static constexpr uint32_t AK0 = 0, AK1 = HS == 256 ? 384 : 128;
+  static constexpr uint32_t AV = HS == 256 ? 128 : 128 * AKS;
+  static constexpr uint32_t S = AV + 2 * SLOT;
   static constexpr uint32_t O = S + 2 * NR;  // channel tile t at O + NR t
   static_assert(HS == 256 || HS == 512, "head size 256 or 512");
-  static_assert(O + MT * NR <= 512u, "TMEM columns overlap");
-  static_assert(VK % 16 == 0 && DEC_TILE % VK == 0 && CHC % 64 == 0, "whole blocks");
-  static_assert(AKS <= 3 && AVS <= 3, "barrier slots");
+  static_assert(O + MT * NR <= (HS == 256 ? AK1 : 512u), "TMEM columns overlap");
+  static_assert(VK % 16 == 0 && DEC_TILE % VK == 0, "value slots of whole 16-key blocks");
 };
 
 template <int FMT, int HS, int NR>
@@ -182,17 +178,17 @@ enum {
   D_RAW_FULL = 0,    // [RS <= 4] a raw stage landed
   D_RAW_EMPTY = 4,   // [RS] the key warps of its keys and the value warps are done with it
   D_Q_FULL = 8,      // Q^T is in shared memory (every softmax warp)
-  D_AK_FULL = 9,     // [AKS <= 3] key operand chunk in TMEM (4 key warps)
-  D_AK_FREE = 12,    // [AKS] its QK MMAs completed (commit)
-  D_KP_FULL = 15,    // [KPS <= 4] the tile's scales and zero-point biases are in shared memory (4 key warps)
-  D_KP_FREE = 19,    // [KPS] the softmax and the value warps read them
-  D_AV_FULL = 23,    // [AVS <= 3] value operand slot in TMEM (4 value warps)
-  D_AV_FREE = 26,    // [AVS] its PV MMAs completed (commit)
-  D_S_FULL = 29,     // [2] S^T of the tile is in TMEM (commit)
-  D_S_FREE = 31,     // [2] the softmax read it (every softmax warp)
-  D_P_FULL = 33,     // [2] P^T of the tile is in shared memory (every softmax warp)
-  D_PV_DONE = 35,    // [2] PV(j) completed: barrier j & 1, one phase per two tiles (commit)
-  D_FINAL = 37,      // every MMA issued has completed (before TMEM is released)
+  D_AK_FULL = 9,     // [2] key operand chunk in TMEM (4 key warps)
+  D_AK_FREE = 11,    // [2] its QK MMAs completed (commit)
+  D_KP_FULL = 13,    // [KPS <= 4] the tile's scales and zero-point biases are in shared memory (4 key warps)
+  D_KP_FREE = 17,    // [KPS] the softmax and the value warps read them
+  D_AV_FULL = 21,    // [2] value operand slot in TMEM (4 value warps)
+  D_AV_FREE = 23,    // [2] its PV MMAs completed (commit)
+  D_S_FULL = 25,     // [2] S^T of the tile is in TMEM (commit)
+  D_S_FREE = 27,     // [2] the softmax read it (every softmax warp)
+  D_P_FULL = 29,     // [2] P^T of the tile is in shared memory (every softmax warp)
+  D_PV_DONE = 31,    // [2] PV(j) completed: barrier j & 1, one phase per two tiles (commit)
+  D_FINAL = 33,      // every MMA issued has completed (before TMEM is released)
 };
 
 // fp16 pair -> exact (nibble - zero point) of two keys a, b: the low-nibble form (1024 + u) minus (1024 + zp), the
@@ -277,10 +273,9 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
   using TM = DecTmem<HS, NR>;
   static_assert(TM::VK >= 32 || DecSmem<FMT, HS, NR>::RS >= 4, "16-key value slots need a four-stage raw ring");
   constexpr int CELL = SM::CELL, RS = SM::RS, KPS = SM::KPS, SK = SM::SK, SPT = SM::SPT;
-  constexpr int NCH = TM::NCH, MT = TM::MT, VK = TM::VK, VSLOTS = TM::VSLOTS, AKS = TM::AKS, AVS = TM::AVS;
-  constexpr int CHC = TM::CHC;
-  constexpr int VSETS = DecWarps<HS, RL>::VSETS, THREADS = DecWarps<HS, RL>::THREADS;
+  constexpr int NCH = TM::NCH, MT = TM::MT, VK = TM::VK, VSLOTS = TM::VSLOTS, AKS = TM::AKS;
   constexpr int QREC = q_rec_bytes(HS);
+  constexpr int VSETS = DecWarps<HS, RL>::VSETS, THREADS = DecWarps<HS, RL>::THREADS;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::OFF_TMEM);
@@ -340,17 +335,13 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
     }
     mbar_init(&bars[D_Q_FULL], 4 * SMX_HALVES);
     for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars[D_AK_FULL + b], 4);
+      mbar_init(&bars[D_AK_FREE + b], 1);
+      mbar_init(&bars[D_AV_FULL + b], 4 * VSETS);
+      mbar_init(&bars[D_AV_FREE + b], 1);
       mbar_init(&bars[D_S_FULL + b], 1);
       mbar_init(&bars[D_S_FREE + b], 4 * SMX_HALVES);
       mbar_init(&bars[D_P_FULL + b], 4 * SMX_HALVES);
-    }
-    for (int b = 0; b < AKS; ++b) {
-      mbar_init(&bars[D_AK_FULL + b], 4);
-      mbar_init(&bars[D_AK_FREE + b], 1);
-    }
-    for (int b = 0; b < AVS; ++b) {
-      mbar_init(&bars[D_AV_FULL + b], 4 * VSETS);
-      mbar_init(&bars[D_AV_FREE + b], 1);
     }
     mbar_init(&bars[D_PV_DONE], 1);
     mbar_init(&bars[D_PV_DONE + 1], 1);
@@ -422,10 +413,10 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
       wait_all(&bars[D_P_FULL + bj], (j >> 1) & 1);
       const uint64_t pd = p_desc + static_cast<uint64_t>((2 * bj * SM::ATOM) >> 4);
 #pragma unroll
-      for (int h = 0; h < VSLOTS; ++h) {  // slot h: keys [h VK, h VK + VK) of the tile, TMEM slot k % AVS
+      for (int h = 0; h < VSLOTS; ++h) {  // slot h: keys [h VK, h VK + VK) of the tile, TMEM slot k & 1
         if (failed) break;
-        const int k = j * VSLOTS + h, sl = k % AVS;
-        wait_all(&bars[D_AV_FULL + sl], (k / AVS) & 1);
+        const int k = j * VSLOTS + h, sl = k & 1;
+        wait_all(&bars[D_AV_FULL + sl], (k >> 1) & 1);
         if (failed) break;
         tc_fence_after();
         if (elect_one()) {
@@ -455,19 +446,19 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
       const int b = i & 1;
       const uint32_t sd = tmem + TM::S + NR * b;
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) {  // key operand chunk ch: channels [CHC ch, CHC ch + CHC), slot k % AKS
+      for (int ch = 0; ch < NCH; ++ch) {  // key operand chunk ch: channels [256 ch, 256 ch + 256), slot k % AKS
         const int k = i * NCH + ch, sl = k % AKS;
         wait_all(&bars[D_AK_FULL + sl], (k / AKS) & 1);
         if (ch == 0 && i >= 2) wait_all(&bars[D_S_FREE + b], ((i - 2) >> 1) & 1);  // S buffer b read by the softmax
         if (failed) break;
         tc_fence_after();
-        const uint32_t ak = tmem + TM::AK + TM::AKW * sl;
+        const uint32_t ak = tmem + (sl ? TM::AK1 : TM::AK0);
         if (elect_one()) {
 #pragma unroll
-          for (int s = 0; s < CHC / 16; ++s)  // Q^T: 64 channels per atom
+          for (int s = 0; s < 16; ++s)
             umma_f16_ts(sd, ak + 8 * s,
-                        q_desc + static_cast<uint64_t>((((CHC / 64) * ch + (s >> 2)) * SM::ATOM + (s & 3) * 32) >> 4),
-                        ID, (ch | s) ? 1u : 0u);
+                        q_desc + static_cast<uint64_t>(((4 * ch + (s >> 2)) * SM::ATOM + (s & 3) * 32) >> 4), ID,
+                        (ch | s) ? 1u : 0u);
           umma_commit(&bars[D_AK_FREE + sl]);
           if (ch == NCH - 1) umma_commit(&bars[D_S_FULL + b]);
         }
@@ -517,17 +508,17 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
       const uint32_t kz16 = kw & 0xFu;
       const uint32_t klo = (0x6400u | kz16) * 0x00010001u, khi = (0xD400u | (kz16 << 4)) * 0x00010001u;
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) {  // CHC channels (CHC / 2 TMEM columns) per chunk
+      for (int ch = 0; ch < NCH; ++ch) {  // 256 channels (128 TMEM columns) per chunk
         const int k = i * NCH + ch, sl = k % AKS;
         if (k >= AKS && __any_sync(0xffffffffu, !mbar_wait_spin(&bars[D_AK_FREE + sl], ((k - AKS) / AKS) & 1))) {
           failed = true;
           break;
         }
         tc_fence_after();
-        const uint32_t dst = tmem + TM::AK + TM::AKW * sl + lane_off;
+        const uint32_t dst = tmem + (sl ? TM::AK1 : TM::AK0) + lane_off;
         const uint8_t* kc = cell + ch * (CL::KB / NCH);
 #pragma unroll 1
-        for (int c = 0; c < CHC / 64; ++c) {  // 32 TMEM columns (64 channels) per store (a loop: instruction-cache size)
+        for (int c = 0; c < 4; ++c) {  // 32 TMEM columns (64 channels) per store (a loop: instruction-cache size)
           uint32_t a[32];
           if constexpr (FMT == FMT_INT4) {
 #pragma unroll
@@ -589,16 +580,20 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
         failed = true;
         break;
       }
-      // No wait on the raw stage itself: the four key warps arrive on KP_FULL (a release) only after each waited
-      // for the raw stages of its keys (the bulk copies' completion), so the KP_FULL wait above (an acquire) already
-      // orders the copied cells before the reads below. Each mbarrier wait costs a value warp ~200 cycles even when
-      // the phase is complete, and the value warps set the tile period (c2a: 99.4 -> 95.8 us without this one).
+      int stage = 0;
 #pragma unroll 1
-      for (int h = 0; h < VSLOTS; ++h) {  // slot h: keys [h VK, h VK + VK) of the tile, TMEM slot k % AVS
+      for (int h = 0; h < VSLOTS; ++h) {  // slot h: keys [h VK, h VK + VK) of the tile, TMEM slot k & 1
         const int part = h * VK / SK;
-        const int stage = (i * SPT + part) % RS;
-        const int k = i * VSLOTS + h, sl = k % AVS;
-        if (k >= AVS && __any_sync(0xffffffffu, !mbar_wait_spin(&bars[D_AV_FREE + sl], ((k - AVS) / AVS) & 1))) {
+        if ((h * VK) % SK == 0) {  // the slot starts a raw stage
+          const int u = i * SPT + part;
+          stage = u % RS;
+          if (__any_sync(0xffffffffu, !mbar_wait_spin(&bars[D_RAW_FULL + stage], (u / RS) & 1))) {
+            failed = true;
+            break;
+          }
+        }
+        const int k = i * VSLOTS + h, sl = k & 1;
+        if (k >= 2 && __any_sync(0xffffffffu, !mbar_wait_spin(&bars[D_AV_FREE + sl], ((k - 2) >> 1) & 1))) {
           failed = true;
           break;
         }
