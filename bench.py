@@ -194,14 +194,19 @@ def sustain(torch, fn, seconds=1.0):
     return n
 
 
-def timed_steps(torch, fn, steps, warmup, flush):
-    """Run `warmup` untimed steps, then `steps` steps each timed by CUDA events (L2 flushed before each)."""
+def timed_steps(torch, fn, steps, warmup, flush, align=None):
+    """Run `warmup` untimed steps, then `steps` steps each timed by CUDA events (L2 flushed before each). With several
+    ranks, `align` (a one-element all-reduce on the stream) runs after the flush and before the start event, so that
+    every rank starts its timed step when the slowest rank has finished its flush: a step with a collective inside
+    otherwise also times the other rank's flush and host-launch skew."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     times = []
     for _ in range(steps):
         l2_flush(flush)
+        if align is not None:
+            align()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
@@ -210,6 +215,14 @@ def timed_steps(torch, fn, steps, warmup, flush):
         b.synchronize()
         times.append(a.elapsed_time(b))
     return times
+
+
+def rank_aligner(torch, dist, world, device):
+    """None on one GPU; else a callable that all-reduces one element over the default group on the current stream."""
+    if world == 1:
+        return None
+    one = torch.ones(1, device=device)
+    return lambda: dist.all_reduce(one)
 
 
 # ---------------------------------------------------------------------------------------------------- CPU arm
@@ -343,6 +356,7 @@ def measure_prefill(args, torch, dist, ops, lib, w, device, rank, world, flush, 
     call = dict(block_row=R["table"][0].contiguous(), n=part["ctx"], softmax_scale=HS ** -0.5, k_scale_cache=ks,
                 v_scale_cache=vs)
     runner = sp.SequenceParallelAttention(dist.group.WORLD, q.shape[0], NQ, HS, device) if world > 1 else None
+    align = rank_aligner(torch, dist, world, device)
     q_host = q.cpu().pin_memory()
     out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
     q_dev = torch.empty_like(q)
@@ -372,9 +386,9 @@ def measure_prefill(args, torch, dist, ops, lib, w, device, rank, world, flush, 
         dist.barrier()
     with Clocks(device.index) as clk:
         sustain(torch, step, 1.0)
-        t = timed_steps(torch, step, args.steps, args.warmup, flush)
-    t_k = timed_steps(torch, kernel_only, args.steps, args.warmup, flush)
-    t_e = timed_steps(torch, e2e_step, args.steps, args.warmup, flush)
+        t = timed_steps(torch, step, args.steps, args.warmup, flush, align)
+    t_k = timed_steps(torch, kernel_only, args.steps, args.warmup, flush, align)
+    t_e = timed_steps(torch, e2e_step, args.steps, args.warmup, flush, align)
     ms, ms_k, ms_e = max_over_ranks(torch, dist, world, device,
                                     [statistics.mean(t), statistics.mean(t_k), statistics.mean(t_e)])
     refl = reference_fa2_prefill(torch, ops, R, w, flush, args) if with_reference and world == 1 else None
@@ -477,6 +491,7 @@ def run_b200(args, w, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     flush = torch.empty(2 * FLUSH_BYTES, dtype=torch.uint8, device=device)
+    align = rank_aligner(torch, dist, world, device)
     seqs = w["seqs"]
     sms = ops.sm_count(device)
     # the headline request(s): the whole workload (N = 1), or this rank's sequence range of it (N > 1)
@@ -497,9 +512,9 @@ def run_b200(args, w, rank, world, local_rank):
     torch.cuda.synchronize()
     with Clocks(local_rank) as clk:
         sustain(torch, step, 1.0)
-        t_step = timed_steps(torch, step, args.steps, args.warmup, flush)
-    t_kernel = timed_steps(torch, kernel_only, args.steps, args.warmup, flush)
-    t_e2e = timed_steps(torch, e2e_step, args.steps, args.warmup, flush)
+        t_step = timed_steps(torch, step, args.steps, args.warmup, flush, align)
+    t_kernel = timed_steps(torch, kernel_only, args.steps, args.warmup, flush, align)
+    t_e2e = timed_steps(torch, e2e_step, args.steps, args.warmup, flush, align)
     torch.cuda.synchronize()
     ms, ms_k, ms_e = max_over_ranks(torch, dist, world, device,
                                     [statistics.mean(t_step), statistics.mean(t_kernel), statistics.mean(t_e2e)])
@@ -511,7 +526,7 @@ def run_b200(args, w, rank, world, local_rank):
         nb = ops.decode_num_splits(seqs, NKV, w["ctx"], sms)
         bstep, _, _, _, _ = decode_request_step(torch, ops, Rb, w, nb)
         dist.barrier()
-        tb = timed_steps(torch, bstep, args.steps, args.warmup, flush)
+        tb = timed_steps(torch, bstep, args.steps, args.warmup, flush, align)
         (msb,) = max_over_ranks(torch, dist, world, device, [statistics.mean(tb)])
         batch = {"value": world * seqs * w["qlen"] / (msb * 1e-3), "unit": "tok/s", "ms_per_step": msb,
                  "scaling": "weak", "parallelism": f"requests sharded over {world} GPUs, no collective"}
