@@ -63,10 +63,7 @@ constexpr int PF_SMW = QP_PF_SM_WARPS;
 static_assert(PF_SMW == 4 || PF_SMW == 8, "softmax warps: 4 or 8");
 constexpr int PF_HALVES = PF_SMW / 4;
 constexpr int PF_SM0 = 2 + PF_DQ;                // first softmax warp
-// the PV MMAs are issued by a warp of their own after the softmax warps, on another SM sub-partition than the QK
-// issuer (warp 1): issuing tcgen05.mma takes that sub-partition's issue slots from the warps beside it
-constexpr int PF_PV = PF_SM0 + PF_SMW;
-constexpr int PF1_THREADS = 32 * (PF_PV + 1);
+constexpr int PF1_THREADS = 32 * (PF_SM0 + PF_SMW);
 // registers per thread one CTA may hold: the register file is split over the 4 sub-partitions (16384 each), and a
 // sub-partition hosts every fourth warp
 constexpr int PF1_REGS = (16384 / (32 * ((PF1_THREADS / 32 + 3) / 4))) & ~7;
@@ -370,7 +367,7 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
     mbar_init(&bars[B_P_FULL], PF_SMW);
     mbar_init(&bars[B_O_DONE], 1);
     mbar_init(&bars[B_O_FREE], PF_SMW);
-    mbar_init(&bars[B_FINAL], 2);  // one commit per MMA issuer
+    mbar_init(&bars[B_FINAL], 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -422,8 +419,8 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       for (int64_t k = (j > C::RS ? j - C::RS : 0); k < j; ++k)
         mbar_wait_spin(&bars[B_RAW_FULL + (k % C::RS)], (k / C::RS) & 1, 100000000ull);
     }
-  } else if (warp == 1 || warp == PF_PV) {
-    // ------------------------------------------------------------------ MMA issuers (warp 1: QK, PF_PV: PV)
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
     // The whole warp walks the schedule and waits (convergent, so the descriptors and TMEM addresses are warp-uniform
     // values); one elected lane issues. A tcgen05.mma issued from a one-lane branch costs tens of cycles of operand
     // moves each, which starves the tensor pipe.
@@ -433,6 +430,8 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
     const uint32_t p_base = smem_u32(smem + C::OFF_P);
     int64_t j = 0;
     int qcount = 0, pieces = 0;
+    int64_t pv_pending = -1;  // tile whose PV is still to be issued
+    bool pv_first = false;
     // every lane runs the same bounded waits; the vote keeps the warp's view (and its control flow) uniform
     auto wait_all = [&](uint64_t* bar, uint32_t parity) {
       const bool ok = mbar_wait_spin(bar, parity);
@@ -455,17 +454,6 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       }
       __syncwarp();
     };
-    if (warp == PF_PV) {
-      // O += P(j) V(j) for every tile of the walk; the first PV of a piece overwrites O, after the previous piece's
-      // epilogue has read it
-      for (; !sch.done() && !failed; sch.next(), ++j) {
-        const Walk w = sch.current();
-        if (w.first_of_piece && pieces > 0) wait_all(&bars[B_O_FREE], (pieces - 1) & 1);
-        if (w.first_of_piece) ++pieces;
-        if (failed) break;
-        issue_pv(j, w.first_of_piece);
-      }
-    } else {
     for (; !sch.done() && !failed; sch.next(), ++j) {
       const Walk w = sch.current();
       if (w.new_mtile) {
@@ -494,11 +482,26 @@ __global__ void __maxnreg__(PF1_REGS) prefill_kernel(const PrefillParams p) {
       __syncwarp();
       // Q of this piece is free once S of its last tile is complete: the softmax, which waits for that S before
       // it stores the next piece's Q, needs no other signal
-    }
+      // O += P(j-1) V(j-1), one tile behind so the softmax of tile j overlaps it
+      if (pv_pending >= 0) {
+        issue_pv(pv_pending, pv_first);
+        pv_pending = -1;
+      }
+      if (w.first_of_piece && pieces > 0) {
+        // O is overwritten by this piece's first PV: the previous piece's epilogue must have read it
+        wait_all(&bars[B_O_FREE], (pieces - 1) & 1);
+      }
+      if (w.first_of_piece) ++pieces;
+      pv_pending = j;
+      pv_first = w.first_of_piece;
+      if (w.last_of_piece) {  // the epilogue waits for this PV: issue it now
+        issue_pv(pv_pending, pv_first);
+        pv_pending = -1;
+      }
     }
     if (elect_one()) umma_commit(&bars[B_FINAL]);
     __syncwarp();
-    if (warp == 1) mbar_wait_spin(&bars[B_FINAL], 0, 100000000ull);  // both issuers' MMAs have completed
+    mbar_wait_spin(&bars[B_FINAL], 0, 100000000ull);
   } else if (warp < PF_SM0) {
     // ------------------------------------------------------------------ dequant (warps 2 .. PF_SM0 - 1)
     // keys:   K_op = u - zp (int4) or the int8 code, exact in fp16; the key scale multiplies the score in fp32 in
