@@ -62,8 +62,9 @@ static_assert(SMX_HALVES == 1 || SMX_HALVES == 2, "one or two softmax warps per 
 // issuers sit on different SM sub-partitions: issuing a tcgen05.mma takes that sub-partition's issue slots from the
 // operand warps beside it, and with all 32 MMAs of a tile on one sub-partition its value warp fell 1,500 cycles
 // behind the other three every tile (clock64 stamps per role). The value conversion sets the tile period, so where
-// the registers allow (96 a thread; the softmax of 32 rows would spill) two warps per lane quarter share it, each
-// converting half of every value slot (c2a, same box: 99.1 -> 91.1 us).
+// the registers allow (96 a thread; the softmax of 32 rows would spill) two warps per lane quarter share it, each set
+// converting one of the tile's two value slots (c2a, same box: 99.1 -> 90.3 us; splitting every slot between the
+// sets instead measured 91.1, with twice the slot hand-offs per warp).
 constexpr int W_MMA = 1, W_VAL = 6, W_SMX = 10, W_PV = W_SMX + 4 * SMX_HALVES, W_VB = W_PV + 1;
 constexpr int SMX_THREADS = 32 * 4 * SMX_HALVES;
 
@@ -337,7 +338,7 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars[D_AK_FULL + b], 4);
       mbar_init(&bars[D_AK_FREE + b], 1);
-      mbar_init(&bars[D_AV_FULL + b], 4 * VSETS);
+      mbar_init(&bars[D_AV_FULL + b], 4);
       mbar_init(&bars[D_AV_FREE + b], 1);
       mbar_init(&bars[D_S_FULL + b], 1);
       mbar_init(&bars[D_S_FREE + b], 4 * SMX_HALVES);
@@ -570,9 +571,10 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
     constexpr int WPT = HS / 256;
     constexpr int NB = VK >= 32 ? 2 : 1;  // 16-key blocks per TMEM store
     const int q = warp & 3, g = lane >> 2, t = lane & 3;
-    constexpr int KBN = VK / (16 * NB);  // block groups (one TMEM store each) per slot, shared by the VSETS sets
-    static_assert(KBN % VSETS == 0, "value block groups split evenly over the warp sets");
-    const int kb0 = (warp >= W_VB ? 1 : 0) * (KBN / VSETS);
+    constexpr int KBN = VK / (16 * NB);  // block groups (one TMEM store each) per slot
+    // with two sets, set s converts the slots h = s, s + 2, ...: each warp hands over one slot per tile
+    static_assert(VSETS == 1 || (VSLOTS % VSETS == 0 && SPT == 1), "value slots split evenly over the warp sets");
+    const int h0 = warp >= W_VB ? 1 : 0;
     const uint32_t* zb = reinterpret_cast<const uint32_t*>(smem + SM::OFF_ZB);
     for (int i = 0; i < ntl && !failed; ++i) {
       const int ki = i % KPS;
@@ -582,9 +584,9 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
       }
       int stage = 0;
 #pragma unroll 1
-      for (int h = 0; h < VSLOTS; ++h) {  // slot h: keys [h VK, h VK + VK) of the tile, TMEM slot k & 1
+      for (int h = h0; h < VSLOTS; h += VSETS) {  // slot h: keys [h VK, h VK + VK) of the tile, TMEM slot k & 1
         const int part = h * VK / SK;
-        if ((h * VK) % SK == 0) {  // the slot starts a raw stage
+        if ((h * VK) % SK == 0 || h == h0) {  // the slot starts a raw stage, or this warp's first slot
           const int u = i * SPT + part;
           stage = u % RS;
           if (__any_sync(0xffffffffu, !mbar_wait_spin(&bars[D_RAW_FULL + stage], (u / RS) & 1))) {
@@ -602,7 +604,7 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
 #pragma unroll
         for (int v = 0; v < WPT; ++v) {
 #pragma unroll 1
-          for (int kb = kb0; kb < kb0 + KBN / VSETS; ++kb) {  // a loop, not unrolled: instruction-cache size
+          for (int kb = 0; kb < KBN; ++kb) {  // a loop, not unrolled: instruction-cache size
             uint32_t r[4][4 * NB];  // [store (channel tile 2 v + c, lane half lb)][registers]
 #pragma unroll
             for (int rr = 0; rr < NB; ++rr) {
@@ -642,7 +644,8 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&bars[D_AV_FULL + sl]);
-          if (((h + 1) * VK) % SK == 0) mbar_arrive(&bars[D_RAW_EMPTY + stage]);  // the stage's last slot
+          // the stage's last slot (with two sets, each warp's last slot of the tile's single stage)
+          if (VSETS == 2 ? h + VSETS >= VSLOTS : ((h + 1) * VK) % SK == 0) mbar_arrive(&bars[D_RAW_EMPTY + stage]);
         }
       }
       if (failed) break;
