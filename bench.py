@@ -217,6 +217,12 @@ def timed_steps(torch, fn, steps, warmup, flush, align=None):
     return times
 
 
+def exchange_name(runner):
+    if runner is not None and runner.peer is not None:
+        return "[O | LSE] partials folded by one kernel reading the peers' buffers over NVLink (symmetric memory)"
+    return "NCCL all-gather of [O | LSE] partials + merge kernel"
+
+
 def rank_aligner(torch, dist, world, device):
     """None on one GPU; else a callable that all-reduces one element over the default group on the current stream."""
     if world == 1:
@@ -365,7 +371,7 @@ def measure_prefill(args, torch, dist, ops, lib, w, device, rank, world, flush, 
         if runner is None:
             ops.prefill(q, kc, vc, out, **call)
         else:
-            ops.prefill(q, kc, vc, runner.exchange.o, out_fp32_lse=runner.exchange.lse, tokens_after_keys=after,
+            ops.prefill(q, kc, vc, runner.scratch()[0], out_fp32_lse=runner.scratch()[1], tokens_after_keys=after,
                         **call)
 
     def step():
@@ -400,8 +406,8 @@ def measure_prefill(args, torch, dist, ops, lib, w, device, rank, world, flush, 
     obj = {"metric": "prefill_tok_s", "value": w["qlen"] / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms,
            "higher_is_better": True, "scaling": "strong" if world > 1 else "single chunk",
            "config": {"workload": "c3", **w, "nq": NQ, "nkv": NKV, "head_size": HS, "block_size": BS,
-                      "parallelism": f"context split by sequence range over {world} GPUs, NCCL all-gather of "
-                      f"[O | LSE] partials" if world > 1 else "1 GPU",
+                      "parallelism": f"context split by sequence range over {world} GPUs, {exchange_name(runner)}"
+                      if world > 1 else "1 GPU",
                       "l2": "flushed before every step; cache larger than L2"},
            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                         "frac": achieved / peak, "traffic": TRAFFIC.get("c3") if world == 1 else None,
@@ -468,7 +474,7 @@ def decode_request_step(torch, ops, R, w, nsplit, runner=None, after=0):
         if runner is None:
             ops.paged_decode(q, kc, vc, out, partials_only=True, **call)
         else:
-            ops.paged_decode(q, kc, vc, runner.exchange.o, out_fp32_lse=runner.exchange.lse, tokens_after_keys=after,
+            ops.paged_decode(q, kc, vc, runner.scratch()[0], out_fp32_lse=runner.scratch()[1], tokens_after_keys=after,
                              partials_only=True, **call)
 
     def e2e_step():
@@ -553,7 +559,7 @@ def run_b200(args, w, rank, world, local_rank):
         "dtype": "int4+f16" if w["fmt"] == "int4" else "k8v4+f16", "data": "synthetic",
         "config": {"workload": args.workload, **w, "nq": NQ, "nkv": NKV, "head_size": HS, "block_size": BS,
                    "num_splits": nsplit, "parallelism": f"one request split by sequence range over {world} GPUs "
-                   f"({part['ctx']} tokens each), NCCL all-gather of [O | LSE] partials" if world > 1 else "1 GPU",
+                   f"({part['ctx']} tokens each), {exchange_name(runner)}" if world > 1 else "1 GPU",
                    "l2": "flushed before every step (256 MB write, then 256 MB read); cache larger than L2"},
         "hbm_gbs": bytes_rank / (ms * 1e-3) / 1e9,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,

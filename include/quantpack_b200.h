@@ -180,6 +180,23 @@ int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t q_stride_t
                            int head_size, float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated,
                            int out_mode, float* lse_out, int num_splits, void* stream);
 
+/* Bytes of one rank's exchange buffer for qp_fold_peer_partials (num_ranks flags per parity, two partials), and the
+ * offset of its partial of a parity ([O (tokens, q heads, hs) fp32 | lse (tokens, q heads) fp32 base-2]). */
+int64_t qp_peer_exchange_bytes(int num_ranks, int64_t num_tokens, int num_q_heads, int head_size);
+int64_t qp_peer_partial_offset(int num_ranks, int64_t num_tokens, int num_q_heads, int head_size, int parity);
+
+/* Rank fold of a sequence split over GPUs without a collective: every rank has written its partial of call `epoch`
+ * (out_mode 1 of qp_paged_decode / qp_prefill) at qp_peer_partial_offset(..., epoch & 1) of its own exchange buffer,
+ * and bases (a device array of num_ranks addresses) holds every rank's buffer as mapped here (NVLink peer memory,
+ * e.g. torch symmetric memory; the flags zeroed before the first call, epochs counting up from 1). The kernel
+ * publishes this rank's partial through a flag in every buffer, waits (bounded: QP device error on timeout) for the
+ * other ranks' flags and folds the num_ranks partials read over NVLink into `out` (out_mode 0: model domain in dtype;
+ * 1: fp32 RHT domain + lse_out). Replaces the NCCL all-gather + qp_merge_attn_partials of the split; no counterpart
+ * in the reference (which serves one GPU). */
+int qp_fold_peer_partials(int dtype, int head_size, int64_t num_tokens, int num_q_heads, int num_ranks, int rank,
+                          const uint64_t* bases, uint32_t epoch, int out_mode, void* out, int64_t out_stride_token,
+                          int64_t out_stride_head, float* lse_out, const uint32_t* rht_sign_bits, void* stream);
+
 /* Log-sum-exp fold of num_parts attention partials per (token, query head): part_o fp32 (RHT domain, normalised),
  * part_lse base-2. out_mode 0: inverse RHT / head_size into `out` in dtype; out_mode 1: fp32 RHT-domain O into
  * `out` and the folded lse into lse_out. Replaces the fold of vllm_quantpack/attention/int4_prefill.py:223-230 and

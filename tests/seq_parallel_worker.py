@@ -39,31 +39,42 @@ def main():
         sub = torch.from_numpy(np.ascontiguousarray(table[0, lo // BS:(hi + BS - 1) // BS])).to(device)
 
         qlen = 4
-        q = U.to_torch(U.make_queries([qlen], seed=7), device)
-        runner = sp.SequenceParallelAttention(dist.group.WORLD, qlen, U.NQ, U.HS, device)
-        out = torch.empty_like(q)
         cu = torch.tensor([0, qlen], dtype=torch.int32, device=device)
-        runner.decode(q, kc, vc, out, cu_seqlens_q=cu, max_seqlen_q=qlen,
-                      seqused_k=torch.tensor([hi - lo], dtype=torch.int32, device=device), max_seqlen_k=hi - lo,
-                      softmax_scale=U.HS ** -0.5, block_table=sub[None], k_scale_cache=ks, v_scale_cache=vs,
-                      tokens_after_keys=after)
-        whole = torch.empty_like(q)
-        ops.paged_decode(q, kc, vc, whole, cu_seqlens_q=cu, max_seqlen_q=qlen,
-                         seqused_k=torch.tensor([n], dtype=torch.int32, device=device), max_seqlen_k=n,
-                         softmax_scale=U.HS ** -0.5, block_table=torch.from_numpy(table).to(device),
-                         k_scale_cache=ks, v_scale_cache=vs)
-        errs.append(qo.relerr(out.float().cpu().numpy(), whole.float().cpu().numpy()))
+        whole = None
+        # the NVLink fold (symmetric memory; every rank reads the others' partials) and the NCCL all-gather; three
+        # calls in a row with other queries each, so the fold's two partial parities both serve twice
+        for peer in (None, False):
+            runner = sp.SequenceParallelAttention(dist.group.WORLD, qlen, U.NQ, U.HS, device, peer=peer)
+            if rank == 0:
+                print(f"exchange: {'NVLink fold' if runner.peer is not None else 'NCCL all-gather'}", flush=True)
+            for call in range(3):
+                q = U.to_torch(U.make_queries([qlen], seed=7 + call), device)
+                out = torch.empty_like(q)
+                runner.decode(q, kc, vc, out, cu_seqlens_q=cu, max_seqlen_q=qlen,
+                              seqused_k=torch.tensor([hi - lo], dtype=torch.int32, device=device),
+                              max_seqlen_k=hi - lo, softmax_scale=U.HS ** -0.5, block_table=sub[None],
+                              k_scale_cache=ks, v_scale_cache=vs, tokens_after_keys=after)
+                whole = torch.empty_like(q)
+                ops.paged_decode(q, kc, vc, whole, cu_seqlens_q=cu, max_seqlen_q=qlen,
+                                 seqused_k=torch.tensor([n], dtype=torch.int32, device=device), max_seqlen_k=n,
+                                 softmax_scale=U.HS ** -0.5, block_table=torch.from_numpy(table).to(device),
+                                 k_scale_cache=ks, v_scale_cache=vs)
+                errs.append(qo.relerr(out.float().cpu().numpy(), whole.float().cpu().numpy()))
 
         qlen = 256
-        q = U.to_torch(U.make_queries([qlen], seed=9), device)
-        runner = sp.SequenceParallelAttention(dist.group.WORLD, qlen, U.NQ, U.HS, device)
-        out = torch.empty_like(q)
-        runner.prefill(q, kc, vc, out, block_row=sub, n=hi - lo, softmax_scale=U.HS ** -0.5, k_scale_cache=ks,
-                       v_scale_cache=vs, tokens_after_keys=after)
-        whole = torch.empty_like(q)
-        ops.prefill(q, kc, vc, whole, block_row=torch.from_numpy(table[0]).to(device), n=n,
-                    softmax_scale=U.HS ** -0.5, k_scale_cache=ks, v_scale_cache=vs)
-        errs.append(qo.relerr(out.float().cpu().numpy(), whole.float().cpu().numpy()))
+        for peer in (None, False):
+            q = U.to_torch(U.make_queries([qlen], seed=9), device)
+            runner = sp.SequenceParallelAttention(dist.group.WORLD, qlen, U.NQ, U.HS, device, peer=peer)
+            out = torch.empty_like(q)
+            runner.prefill(q, kc, vc, out, block_row=sub, n=hi - lo, softmax_scale=U.HS ** -0.5, k_scale_cache=ks,
+                           v_scale_cache=vs, tokens_after_keys=after)
+            whole = torch.empty_like(q)
+            ops.prefill(q, kc, vc, whole, block_row=torch.from_numpy(table[0]).to(device), n=n,
+                        softmax_scale=U.HS ** -0.5, k_scale_cache=ks, v_scale_cache=vs)
+            errs.append(qo.relerr(out.float().cpu().numpy(), whole.float().cpu().numpy()))
+        from vllm_quantpack_b200 import _lib
+        if _lib.device_error() != 0:
+            raise RuntimeError("a kernel gave up a bounded wait")
         ok = all(e < 2e-3 for e in errs)
     except Exception as exc:  # every rank still takes part in the final all-reduce
         print(f"rank {rank}: {exc!r}", flush=True)

@@ -222,6 +222,23 @@ def merge_attn_partials(part_o, part_lse, out, lse_out=None):
     return out
 
 
+def fold_peer_partials(bases, rank, world, epoch, num_tokens, num_heads, head_size, out, lse_out=None):
+    """Rank fold over NVLink (qp_fold_peer_partials): `bases` an int64 device tensor of the ranks' exchange buffer
+    addresses, every rank's partial of call `epoch` already in its own buffer."""
+    if lse_out is not None:
+        if out.dtype != torch.float32 or not lse_out.is_contiguous():
+            raise TypeError("out must be fp32 and lse_out contiguous")
+        mode, dt, lptr, sbits = 1, 0, lse_out.data_ptr(), None
+    else:
+        mode, dt, lptr = 0, _dtype_code(out, "fold_peer_partials"), None
+        sbits = rht.device_sign_bits(head_size, out.device).data_ptr()
+    if out.stride(-1) != 1:
+        raise ValueError("out rows must be contiguous")
+    _lib.call("qp_fold_peer_partials", dt, head_size, num_tokens, num_heads, world, rank, bases.data_ptr(),
+              epoch & 0xFFFFFFFF, mode, out.data_ptr(), out.stride(0), out.stride(1), lptr, sbits, _stream(out.device))
+    return out
+
+
 # ------------------------------------------------------------------------------------------------------ prefill
 
 

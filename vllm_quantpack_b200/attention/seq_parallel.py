@@ -4,14 +4,16 @@ partials (O fp32 in the RHT domain, base-2 log-sum-exp) are combined exactly by 
 
 The combine is the fold the plugin applies to its 16k-token prefill segments (vllm_quantpack/attention/
 int4_prefill.py:223-230) and vLLM's reduce_segments to decode segments; here the segments live on different GPUs.
-One collective per call: an all-gather (NCCL over NVLink) of each rank's packed [O | lse] buffer, then every rank
-folds the P partials locally with the merge kernel (inverse RHT and 1/head fused). Causality: query token i of a
+The exchange: with torch symmetric memory (every rank maps the others' buffers over NVLink) each rank writes its
+partial into its own exchange buffer and one kernel (ops.fold_peer_partials) publishes it through flags and folds
+all ranks' partials read straight over NVLink, with no collective; otherwise an all-gather (NCCL) of the packed
+[O | lse] buffers and the merge kernel. Causality: query token i of a
 chunk of qlen sits at absolute position n_total - qlen + i; a rank whose keys end `after` tokens before n_total sees
 key k of its range iff k <= n_local - qlen + i + after, which the kernels apply through `tokens_after_keys`; only the
 rank holding the newest tokens (after = 0) masks anything inside a decode step.
 
-There is no TMA multicast and no library kernel reading peer memory: the exchange is a plain NCCL all-gather into
-this GPU's own buffer.
+There is no TMA multicast and no library kernel reading peer memory: the peer reads are plain loads in this build's
+own fold kernel, or the exchange is an NCCL all-gather into this GPU's own buffer.
 """
 import torch
 import torch.distributed as dist
@@ -54,19 +56,92 @@ class PartialExchange:
         return part_o, part_lse
 
 
+class PeerExchange:
+    """This rank's partial in an exchange buffer of torch symmetric memory that every rank of `group` maps; the fold
+    kernel reads the other ranks' partials over NVLink. Raises when symmetric memory is unavailable."""
+
+    def __init__(self, group, num_tokens, num_heads, head_size, device):
+        import torch.distributed._symmetric_memory as symm_mem
+        from .. import _lib
+        lib = _lib.load()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.shape = (num_tokens, num_heads, head_size)
+        nbytes = lib.qp_peer_exchange_bytes(self.world, num_tokens, num_heads, head_size)
+        try:
+            symm_mem.enable_symm_mem_for_group(group.group_name)  # required before rendezvous by older torch
+        except Exception:
+            pass
+        self.buf = symm_mem.empty(nbytes // 4, dtype=torch.float32, device=device)
+        self.buf.zero_()  # flags start below the first epoch
+        handle = symm_mem.rendezvous(self.buf, group)
+        self.bases = torch.tensor(list(handle.buffer_ptrs), dtype=torch.int64, device=device)
+        torch.cuda.synchronize(device)
+        dist.barrier(group)
+        self.views = []
+        n_o = num_tokens * num_heads * head_size
+        for parity in (0, 1):
+            off = lib.qp_peer_partial_offset(self.world, num_tokens, num_heads, head_size, parity) // 4
+            o = self.buf[off: off + n_o].view(self.shape)
+            lse = self.buf[off + n_o: off + n_o + num_tokens * num_heads].view(self.shape[:2])
+            self.views.append((o, lse))
+        self.epoch = 0
+
+    def next_partial(self):
+        """The (O, lse) views this call's partial goes to (the parity of the next epoch)."""
+        self.epoch += 1
+        return self.views[self.epoch & 1]
+
+    def fold(self, out, lse_out=None):
+        return ops.fold_peer_partials(self.bases, self.rank, self.world, self.epoch, *self.shape, out, lse_out)
+
+
 class SequenceParallelAttention:
     """Decode (<= 4 MTP tokens) or chunk prefill of one request whose cache is split by sequence range over the
     ranks of `group` (`sequence_range`). Every rank passes all query tokens; `out` receives the full attention in
     the model domain on every rank. Buffers are sized once for `num_tokens` query tokens."""
 
-    def __init__(self, group, num_tokens, num_q_heads, head_size, device):
-        self.exchange = PartialExchange(group, num_tokens, num_q_heads, head_size, device)
+    def __init__(self, group, num_tokens, num_q_heads, head_size, device, peer=None):
+        """peer: True = the NVLink fold over symmetric memory (raises when unavailable), False = NCCL all-gather,
+        None = the NVLink fold when symmetric memory can be set up on every rank, else NCCL."""
+        self.shape = (num_tokens, num_q_heads, head_size)
+        self.peer = None
+        if peer is not False:
+            try:
+                self.peer = PeerExchange(group, num_tokens, num_q_heads, head_size, device)
+            except Exception:
+                if peer:
+                    raise
+            # every rank must take the same path
+            ok = torch.tensor([1 if self.peer is not None else 0], dtype=torch.int32, device=device)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+            if not ok.item():
+                self.peer = None
+        self.exchange = None if self.peer is not None else PartialExchange(group, num_tokens, num_q_heads,
+                                                                           head_size, device)
 
     def _check(self, q):
-        if tuple(q.shape) != self.exchange.shape:
-            raise ValueError(f"q {tuple(q.shape)}: this runner holds partials for {self.exchange.shape}")
+        if tuple(q.shape) != self.shape:
+            raise ValueError(f"q {tuple(q.shape)}: this runner holds partials for {self.shape}")
+
+    def scratch(self):
+        """(O, lse) buffers of a partial that no other rank reads (for timing the kernels alone)."""
+        if not hasattr(self, "_scratch"):
+            dev = self.peer.buf.device if self.peer is not None else self.exchange.send.device
+            self._scratch = (torch.empty(self.shape, dtype=torch.float32, device=dev),
+                             torch.empty(self.shape[:2], dtype=torch.float32, device=dev))
+        return self._scratch
+
+    def _partial(self):
+        """Where this call's partial goes: (O, lse) views."""
+        if self.peer is not None:
+            return self.peer.next_partial()
+        return self.exchange.o, self.exchange.lse
 
     def combine(self, out):
+        if self.peer is not None:
+            return self.peer.fold(out)
         part_o, part_lse = self.exchange.gather()
         return ops.merge_attn_partials(part_o, part_lse, out)
 
@@ -74,8 +149,8 @@ class SequenceParallelAttention:
         """This rank's split-KV decode over its range (ops.paged_decode arguments, seqused_k = tokens held here),
         then the exchange and fold."""
         self._check(q)
-        x = self.exchange
-        ops.paged_decode(q, key_cache, value_cache, x.o, out_fp32_lse=x.lse, tokens_after_keys=tokens_after_keys,
+        o, lse = self._partial()
+        ops.paged_decode(q, key_cache, value_cache, o, out_fp32_lse=lse, tokens_after_keys=tokens_after_keys,
                          **decode_args)
         return self.combine(out)
 
@@ -83,7 +158,7 @@ class SequenceParallelAttention:
         """This rank's chunk prefill over its range (ops.prefill arguments, n = tokens held here), then the exchange
         and fold."""
         self._check(q)
-        x = self.exchange
-        ops.prefill(q, key_cache, value_cache, x.o, out_fp32_lse=x.lse, tokens_after_keys=tokens_after_keys,
+        o, lse = self._partial()
+        ops.prefill(q, key_cache, value_cache, o, out_fp32_lse=lse, tokens_after_keys=tokens_after_keys,
                     **prefill_args)
         return self.combine(out)

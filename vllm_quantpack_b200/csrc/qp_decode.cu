@@ -1460,6 +1460,177 @@ extern "C" int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_st
                         dtype, head_size, num_q_tokens, st, true);
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Rank fold of a sequence split over GPUs, reading the peers' partials over NVLink (K2p). Every rank keeps its own
+// partial [O (tokens, q heads, hs) fp32 | lse (tokens, q heads) base-2] in an exchange buffer that all ranks have
+// mapped (symmetric memory: the same layout at `bases[r]` for rank r, this rank's own included):
+//   [flags: 2 x P uint32, padded to flag_bytes][partial of parity 0][partial of parity 1]
+// Call e (epoch e, parity e & 1): the kernel that wrote this rank's partial of parity e & 1 has completed (stream
+// order), so CTA 0 publishes it by storing e into flag [parity][rank] of every rank (a system-scope release); each
+// CTA waits (acquire, bounded) until every rank's flag [parity][r] holds e, then folds the P partials of its rows,
+// read straight from the owners' buffers (plain peer loads, no multicast, no library kernel on peer memory). Two
+// parities suffice: a rank writes its parity-p partial again two calls later, after its fold of the call between,
+// which waited for every peer's flag of that call, which each peer stores only after its own fold of this call has
+// completed. The fold: one warp per (token, query head) row, lane l holding channels [l E, l E + E), E = hs / 32
+// (the layout of the warp's Hadamard transform); mode 0 applies the inverse RHT and 1 / hs and casts, mode 1 writes
+// the fp32 RHT-domain output and the folded lse. Replaces the NCCL all-gather + K2 of the split (one launch, no
+// host involvement); a wait that runs out records DEV_ERR_WAIT_TIMEOUT and the CTA leaves.
+struct PeerFoldParams {
+  const uint64_t* bases;  // [P] device address of every rank's exchange buffer
+  int P, rank, parity;
+  uint32_t epoch;
+  int64_t part_off;       // bytes from a base to the partial of parity 0
+  int64_t part_bytes;     // bytes of one partial (the parity stride)
+  int64_t rows;           // tokens x q heads
+  int nq, mode;
+  void* out;
+  int64_t out_st, out_sh;
+  float* lse_out;
+  const uint32_t* sign_bits;
+  float out_scale;
+};
+
+constexpr int PF_FOLD_WARPS = 8;
+constexpr int PEER_MAX = 32;
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <int DT, int HS>
+__global__ void __launch_bounds__(32 * PF_FOLD_WARPS) peer_fold_kernel(const PeerFoldParams p) {
+  constexpr int E = HS / 32;
+  const int lane = threadIdx.x & 31;
+  if (blockIdx.x == 0 && threadIdx.x < p.P) {  // publish this rank's partial to every rank
+    __threadfence_system();
+    uint32_t* f = reinterpret_cast<uint32_t*>(p.bases[threadIdx.x]) + p.parity * p.P + p.rank;
+    st_release_sys(f, p.epoch);
+  }
+  bool ok = true;
+  if (threadIdx.x < p.P && threadIdx.x != p.rank) {  // every peer's partial of this call is published
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(p.bases[p.rank]) + p.parity * p.P + threadIdx.x;
+    if (ld_acquire_sys(f) != p.epoch) {
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_sys(f) != p.epoch) {
+        if (global_timer_ns() - t0 > 2000000000ull) {
+          atomicCAS(&g_device_error, DEV_ERR_NONE, DEV_ERR_WAIT_TIMEOUT);
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  if (__syncthreads_or(!ok)) return;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * PF_FOLD_WARPS + (threadIdx.x >> 5);  // token * nq + head
+  if (r >= p.rows) return;
+  const int64_t lse_off = p.part_off + p.parity * p.part_bytes + p.rows * HS * 4;
+  const int64_t o_off = p.part_off + p.parity * p.part_bytes + r * HS * 4;
+  const float l_me = lane < p.P ? *reinterpret_cast<const float*>(p.bases[lane] + lse_off + r * 4) : -INFINITY;
+  const float M = warp_max(l_me);
+  const float w_me = (M == -INFINITY || l_me == -INFINITY) ? 0.f : exp2f(l_me - M);
+  const float T = warp_sum(w_me);
+  float x[E];
+#pragma unroll
+  for (int i = 0; i < E; ++i) x[i] = 0.f;
+  for (int s = 0; s < p.P; ++s) {
+    const float w = __shfl_sync(0xffffffffu, w_me, s);
+    if (w != 0.f) {  // the same in every lane; a rank with no key for the row contributes nothing
+      const float4* po = reinterpret_cast<const float4*>(p.bases[s] + o_off) + lane * (E / 4);
+#pragma unroll
+      for (int i = 0; i < E / 4; ++i) {
+        const float4 a = po[i];
+        x[4 * i] = fmaf(w, a.x, x[4 * i]);
+        x[4 * i + 1] = fmaf(w, a.y, x[4 * i + 1]);
+        x[4 * i + 2] = fmaf(w, a.z, x[4 * i + 2]);
+        x[4 * i + 3] = fmaf(w, a.w, x[4 * i + 3]);
+      }
+    }
+  }
+  const float inv = T > 0.f ? 1.f / T : 0.f;
+#pragma unroll
+  for (int i = 0; i < E; ++i) x[i] *= inv;
+  const int64_t tok = r / p.nq;
+  const int qh = static_cast<int>(r % p.nq);
+  if (p.mode == 1) {
+    float* dst = reinterpret_cast<float*>(p.out) + tok * p.out_st + qh * p.out_sh + E * lane;
+#pragma unroll
+    for (int i = 0; i < E; ++i) dst[i] = x[i];
+    if (lane == 0 && p.lse_out) p.lse_out[r] = T > 0.f ? M + log2f(T) : -INFINITY;
+    return;
+  }
+  warp_wht<E>(x, lane);
+  apply_signs<E>(x, p.sign_bits, lane);
+  using EL = Elem<DT>;
+  typename EL::T* dst = reinterpret_cast<typename EL::T*>(p.out) + tok * p.out_st + qh * p.out_sh + E * lane;
+#pragma unroll
+  for (int i = 0; i < E; ++i) dst[i] = EL::from_f(x[i] * p.out_scale);
+}
+
+// Bytes of a rank's exchange buffer for K2p: flags (2 x P uint32, padded to 256 bytes) and two partials.
+static int64_t peer_flag_bytes(int P) { return (2 * static_cast<int64_t>(P) * 4 + 255) / 256 * 256; }
+static int64_t peer_part_bytes(int64_t num_tokens, int nq, int hs) {
+  const int64_t rows = num_tokens * nq;
+  return (rows * hs * 4 + rows * 4 + 255) / 256 * 256;
+}
+
+extern "C" int64_t qp_peer_exchange_bytes(int num_ranks, int64_t num_tokens, int num_q_heads, int head_size) {
+  if (num_ranks <= 0 || num_tokens < 0 || num_q_heads <= 0) return 0;
+  return peer_flag_bytes(num_ranks) + 2 * peer_part_bytes(num_tokens, num_q_heads, head_size);
+}
+
+extern "C" int64_t qp_peer_partial_offset(int num_ranks, int64_t num_tokens, int num_q_heads, int head_size,
+                                          int parity) {
+  return peer_flag_bytes(num_ranks) + (parity & 1) * peer_part_bytes(num_tokens, num_q_heads, head_size);
+}
+
+extern "C" int qp_fold_peer_partials(int dtype, int head_size, int64_t num_tokens, int num_q_heads, int num_ranks,
+                                     int rank, const uint64_t* bases, uint32_t epoch, int out_mode, void* out,
+                                     int64_t out_stride_token, int64_t out_stride_head, float* lse_out,
+                                     const uint32_t* rht_sign_bits, void* stream) {
+  if (num_tokens < 0 || num_q_heads <= 0 || num_ranks <= 0 || rank < 0 || rank >= num_ranks)
+    return set_error(QP_ERR_INVALID, "fold peers: bad sizes");
+  if (num_ranks > PEER_MAX) return set_error(QP_ERR_UNSUPPORTED, "fold peers: %d ranks > %d", num_ranks, PEER_MAX);
+  if (head_size != 256 && head_size != 512 && head_size != 128)
+    return set_error(QP_ERR_UNSUPPORTED, "fold peers: head size %d", head_size);
+  if (out_mode != 0 && out_mode != 1) return set_error(QP_ERR_INVALID, "fold peers: out_mode %d", out_mode);
+  if (out_mode == 0 && dtype != DT_BF16 && dtype != DT_F16) return set_error(QP_ERR_UNSUPPORTED, "fold peers: dtype");
+  if (!bases || !out || (out_mode == 0 && !rht_sign_bits)) return set_error(QP_ERR_INVALID, "fold peers: null pointer");
+  if (num_tokens == 0) return QP_OK;
+  PeerFoldParams fp{};
+  fp.bases = bases;
+  fp.P = num_ranks;
+  fp.rank = rank;
+  fp.parity = static_cast<int>(epoch & 1u);
+  fp.epoch = epoch;
+  fp.part_off = peer_flag_bytes(num_ranks);
+  fp.part_bytes = peer_part_bytes(num_tokens, num_q_heads, head_size);
+  fp.rows = num_tokens * num_q_heads;
+  fp.nq = num_q_heads;
+  fp.mode = out_mode;
+  fp.out = out;
+  fp.out_st = out_stride_token;
+  fp.out_sh = out_stride_head;
+  fp.lse_out = lse_out;
+  fp.sign_bits = rht_sign_bits;
+  fp.out_scale = 1.f / static_cast<float>(head_size);
+  const int64_t grid = (fp.rows + PF_FOLD_WARPS - 1) / PF_FOLD_WARPS;
+  if (grid > 0x7fffffff) return set_error(QP_ERR_UNSUPPORTED, "fold peers: too many rows");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 g(static_cast<unsigned>(grid)), b(32 * PF_FOLD_WARPS);
+  const bool bf = out_mode == 1 || dtype == DT_BF16;
+  switch (head_size) {
+    case 128: if (bf) peer_fold_kernel<DT_BF16, 128><<<g, b, 0, st>>>(fp); else peer_fold_kernel<DT_F16, 128><<<g, b, 0, st>>>(fp); break;
+    case 256: if (bf) peer_fold_kernel<DT_BF16, 256><<<g, b, 0, st>>>(fp); else peer_fold_kernel<DT_F16, 256><<<g, b, 0, st>>>(fp); break;
+    default: if (bf) peer_fold_kernel<DT_BF16, 512><<<g, b, 0, st>>>(fp); else peer_fold_kernel<DT_F16, 512><<<g, b, 0, st>>>(fp); break;
+  }
+  return check_launch("fold peers");
+}
+
 extern "C" int qp_merge_attn_partials(int dtype, int head_size, int64_t num_tokens, int num_q_heads, int num_parts,
                                       const float* part_o, int64_t po_stride_token, int64_t po_stride_head,
                                       int64_t po_stride_part, const float* part_lse, int64_t pl_stride_token,
