@@ -35,8 +35,9 @@
 //               of one slot overlap the MMAs of the other;
 //   warps 10-13 softmax: thread = key; scores in log2 units from S^T, a lazy per-row maximum (P may reach 2^8
 //               before O is rescaled, which happens in TMEM and rarely), P x value scale in fp16 with a running
-//               power-of-two range written as P^T; per-thread row sums reduced once at the end; the epilogue reads
-//               O^T and writes the normalised partial and its log2-sum-exp.
+//               power-of-two range written as P^T, MN-major (a key's rows contiguous: 8 rows per 16-byte store);
+//               per-thread row sums reduced once at the end; the epilogue reads O^T and writes the normalised
+//               partial and its log2-sum-exp.
 // Every wait is bounded (a timeout records an error word and the roles leave; the softmax warps leave together).
 #include <math.h>
 
@@ -50,6 +51,8 @@
 namespace qp {
 
 constexpr int DEC_TILE = 128;  // keys per tile (TMEM lanes of the QK accumulator)
+constexpr int P_KGROUP = 128;                    // bytes between the 8-key groups of P^T (LBO of its descriptor)
+constexpr int P_NGROUP = DEC_TILE / 8 * P_KGROUP;  // bytes between its 8-row groups (SBO)
 constexpr int DEC_MAX_ROWS = 32;
 #ifndef QP_DEC_SMX_HALVES
 #define QP_DEC_SMX_HALVES 1
@@ -156,8 +159,14 @@ struct DecSmem {
   static constexpr int RAW = SK * CELL;
   static constexpr int ATOM = NR * 128;  // one 64-element column of 128B-swizzle atoms over the NR rows
   static constexpr int OFF_Q = 0;                          // Q: HS / 64 atoms, K-major
-  static constexpr int OFF_P = OFF_Q + HS / 64 * ATOM;     // P^T: 2 buffers x 2 atoms (128 keys), K-major
+  static constexpr int OFF_P = OFF_Q + HS / 64 * ATOM;     // P^T: 2 buffers x 2 ATOM (128 keys), MN-major (p_off)
   static constexpr int OFF_RAW = OFF_P + 4 * ATOM;         // RS raw stages
+  // P^T (the B operand of the PV MMAs) is MN-major without swizzle: core matrices of 8 keys x 8 rows, 128 bytes
+  // (key k at 16 k, row r at 2 r), the 16 key groups of a tile P_KGROUP apart, the row groups P_NGROUP apart; byte
+  // offset of (buffer b, row, key) from OFF_P
+  static __device__ __forceinline__ int p_off(int b, int row, int key) {
+    return b * 2 * ATOM + (row >> 3) * P_NGROUP + (key >> 3) * P_KGROUP + (key & 7) * 16 + (row & 7) * 2;
+  }
   static constexpr int OFF_KP = OFF_RAW + RS * RAW;        // [KPS][128] float4: key scale, key zp, value scale
   static constexpr int OFF_ZB = OFF_KP + KPS * 128 * 16;   // [KPS][128] u32: paired value zero-point operand biases
   static constexpr int OFF_RP = OFF_ZB + KPS * 128 * 4;    // [2][NR] float2: row scale, row maximum
@@ -398,12 +407,13 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
   } else if (warp == W_MMA || warp == W_PV) {
     // ------------------------------------------------------------------ MMA issuers (QK, PV)
     // The whole warp waits (convergent, so descriptors and TMEM addresses are warp-uniform); one elected lane issues.
-    constexpr uint32_t ID = f16_idesc(128, NR, false);
+    constexpr uint32_t ID = f16_idesc(128, NR, false);      // QK: B = Q^T, K-major
+    constexpr uint32_t ID_PV = f16_idesc(128, NR, true);    // PV: B = P^T, MN-major
     // Every B operand descriptor is the base descriptor of its buffer plus a compile-time start-address offset (the
     // 14-bit start field holds address / 16 and every shared-memory address here is below 256 KB, so the add
     // never carries out of it): one integer add per MMA.
     const uint64_t q_desc = sw128_desc(smem_u32(smem + SM::OFF_Q), 16, 1024);
-    const uint64_t p_desc = sw128_desc(smem_u32(smem + SM::OFF_P), 16, 1024);
+    const uint64_t p_desc = interleave_desc(smem_u32(smem + SM::OFF_P), P_KGROUP, P_NGROUP);
     auto wait_all = [&](uint64_t* bar, uint32_t parity) {
       const bool ok = mbar_wait_spin(bar, parity);
       failed |= __any_sync(0xffffffffu, !ok);
@@ -412,7 +422,7 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
     auto issue_pv = [&](int j) {
       const int bj = j & 1;
       wait_all(&bars[D_P_FULL + bj], (j >> 1) & 1);
-      const uint64_t pd = p_desc + static_cast<uint64_t>((2 * bj * SM::ATOM) >> 4);
+      const uint64_t pd = p_desc + static_cast<uint64_t>(SM::p_off(bj, 0, 0) >> 4);
 #pragma unroll
       for (int h = 0; h < VSLOTS; ++h) {  // slot h: keys [h VK, h VK + VK) of the tile, TMEM slot k & 1
         if (failed) break;
@@ -425,9 +435,9 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
           for (int c = 0; c < MT; ++c)
 #pragma unroll
             for (int s = 0; s < VK / 16; ++s) {
-              const int key = h * VK + 16 * s;  // P^T: 64 keys per atom
+              const int key = h * VK + 16 * s;
               umma_f16_ts(tmem + (TM::O + NR * c), tmem + (TM::AV + TM::SLOT * sl + (VK / 2) * c + 8 * s),
-                          pd + static_cast<uint64_t>(((key >> 6) * SM::ATOM + (key & 63) * 2) >> 4), ID,
+                          pd + static_cast<uint64_t>(SM::p_off(0, 0, key) >> 4), ID_PV,
                           (h | s) ? 1u : static_cast<uint32_t>(j));
             }
           umma_commit(&bars[D_AV_FREE + sl]);
@@ -690,11 +700,13 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
         lim[r] = r < rows ? min(n - 1, vis_base + r / p.group) : -1;
         frow[r] = 1.f;
       }
-      // P^T rows RL .. NR - 1 are read by the MMAs but never written by the loops below: zero them once
+      // P^T rows RL .. NR - 1 (whole 8-row groups: RL is a multiple of 8) are read by the MMAs but never written by
+      // the loops below: zero them once, in both buffers
       if constexpr (RL < NR) {
-        for (int idx = stid; idx < 4 * (NR - RL) * 8; idx += SMX_THREADS) {
-          const int ab = idx / ((NR - RL) * 8), rem = idx % ((NR - RL) * 8), r = RL + rem / 8, ch = rem % 8;
-          *reinterpret_cast<uint4*>(smem + SM::OFF_P + ab * SM::ATOM + sw128_off(r, ch)) = make_uint4(0u, 0u, 0u, 0u);
+        for (int idx = stid; idx < 2 * (NR - RL) / 8 * DEC_TILE; idx += SMX_THREADS) {
+          const int b = idx / ((NR - RL) / 8 * DEC_TILE), rem = idx % ((NR - RL) / 8 * DEC_TILE);
+          *reinterpret_cast<uint4*>(smem + SM::OFF_P + SM::p_off(b, RL + rem / DEC_TILE * 8, rem % DEC_TILE)) =
+              make_uint4(0u, 0u, 0u, 0u);
         }
       }
     }
@@ -711,8 +723,6 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
       int e_run = -1000;    // running power-of-two range of the value scales: every one < 2^e_run
       float pv_mul = 0.f;   // 2^-e_run
       float v_limit = 0.f;  // 2^e_run
-      // P^T store position of this thread's key: atom kl / 64, chunk (kl % 64) / 8 (swizzled by row), column
-      const int patom = (kl >> 6) * SM::ATOM + (kl & 7) * 2, pchunk = (kl & 63) >> 3;
       for (int i = 0; i < ntl; ++i) {
         const int b = i & 1;
         const int ki = i % KPS;
@@ -823,14 +833,31 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
         if (rescale && i >= 1) failed |= !mbar_wait_bounded(&bars[D_PV_DONE + (b ^ 1)], ((i - 1) >> 1) & 1);
         tc_fence_after();
         const float vsp = kv.z * pv_mul;
-        uint8_t* pb = smem + SM::OFF_P + 2 * b * SM::ATOM + patom;
+        // P^T of this thread's key: the rows of an 8-row group are 16 contiguous bytes (MN-major), so two rows
+        // convert in one instruction and eight go out in one 16-byte store
+        uint8_t* pb = smem + SM::OFF_P + SM::p_off(b, R0, kl);
+        if constexpr (RH % 8 == 0 && R0 % 8 == 0) {
 #pragma unroll
-        for (int r = 0; r < RH; ++r) {
-          const int R = R0 + r;
-          const float pe = fast_exp2(s[r]);
-          l[r] += pe;
-          *reinterpret_cast<__half*>(pb + (R >> 3) * 1024 + (R & 7) * 128 + ((pchunk ^ (R & 7)) << 4)) =
-              __float2half_rn(pe * vsp);
+          for (int g = 0; g < RH / 8; ++g) {
+            uint32_t w[4];
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const int r = 8 * g + 2 * h;
+              const float p0 = fast_exp2(s[r]), p1 = fast_exp2(s[r + 1]);
+              l[r] += p0;
+              l[r + 1] += p1;
+              const __half2 v = __floats2half2_rn(p0 * vsp, p1 * vsp);
+              w[h] = *reinterpret_cast<const uint32_t*>(&v);
+            }
+            *reinterpret_cast<uint4*>(pb + g * P_NGROUP) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < RH; ++r) {
+            const float pe = fast_exp2(s[r]);
+            l[r] += pe;
+            *reinterpret_cast<__half*>(smem + SM::OFF_P + SM::p_off(b, R0 + r, kl)) = __float2half_rn(pe * vsp);
+          }
         }
         if (rescale && i >= 1) {  // before PV(i), which waits for this tile's P
 #pragma unroll 1

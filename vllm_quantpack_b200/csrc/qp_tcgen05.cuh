@@ -255,6 +255,14 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr, uint32_t lbo,
   return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
          (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
+// Canonical UMMA shared-memory descriptor without swizzle (sm_100 version 1, layout type 0): core matrices of 8 rows
+// x 16 bytes stored as 128 contiguous bytes. K-major: LBO = byte stride between core matrices along K, SBO = along
+// M/N. MN-major (a core matrix holds 8 M/N elements of each of 8 K indices): SBO = byte stride between core matrices
+// along M/N, LBO = along K.
+__device__ __forceinline__ uint64_t interleave_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
 // instruction descriptor: fp32 accumulate, fp16 A and B, A K-major, B K- or MN-major, M x N
 __host__ __device__ constexpr uint32_t f16_idesc(int m, int n, bool b_mn_major) {
   return (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | ((b_mn_major ? 1u : 0u) << 16) |
