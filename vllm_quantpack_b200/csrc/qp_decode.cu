@@ -21,8 +21,11 @@
 //               16-token groups, into a ring of raw stages (a stage holds the tile, or at head 512 half of it);
 //   warp 1      MMA issuer (convergent; elect.sync picks the lane): HS/16 QK MMAs per tile into a double-buffered S,
 //               then the previous tile's PV MMAs, each group finished with tcgen05.commit onto mbarriers;
-//   warps 2-5   key operand: thread = key = TMEM lane; lop3 + one fp16 add (or fma) per channel pair gives the exact
-//               fp16 (u - zp) of two channels; k8v4 codes become 1152 + c by one prmt, minus 1152. The operand is
+//   warps 2-5   key operand: thread = key = TMEM lane; one AND per channel pair makes the int4 codes fp16
+//               subnormals (u x 2^-24, 16 u x 2^-24 for high nibbles, whose query channels K0q divides by 16); k8v4
+//               codes become c + 128 the same way (one XOR per word, one prmt per pair). The zero point (int4) or the
+//               bias 128 (k8v4) comes off in the MMA: one more MMA of K 16 per tile, A = -zp x 2^-14 from shared
+//               memory, B = the query row's sum split into three fp16 terms. The operand is
 //               written in 256-channel chunks (128 TMEM columns) into a ring of two chunk slots (one at head 512
 //               with 32 rows, where TMEM has no room for two), so the conversion of one chunk overlaps the MMAs of
 //               the other. The key / value scales go to shared memory for the softmax, the value zero points as
@@ -158,8 +161,10 @@ struct DecSmem {
   static constexpr int KPS = HS == 256 ? RS : 3;                   // tiles of key / value scales in flight
   static constexpr int RAW = SK * CELL;
   static constexpr int ATOM = NR * 128;  // one 64-element column of 128B-swizzle atoms over the NR rows
-  static constexpr int OFF_Q = 0;                          // Q: HS / 64 atoms, K-major
-  static constexpr int OFF_P = OFF_Q + HS / 64 * ATOM;     // P^T: 2 buffers x 2 ATOM (128 keys), MN-major (p_off)
+  // Q: HS / 64 atoms, K-major; then one more atom whose first 16 k hold the zero-point correction terms (K0q)
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_QZ = OFF_Q + HS / 64 * ATOM;
+  static constexpr int OFF_P = OFF_QZ + ATOM;              // P^T: 2 buffers x 2 ATOM (128 keys), MN-major (p_off)
   static constexpr int OFF_RAW = OFF_P + 4 * ATOM;         // RS raw stages
   // P^T (the B operand of the PV MMAs) is MN-major without swizzle: core matrices of 8 keys x 8 rows, 128 bytes
   // (key k at 16 k, row r at 2 r), the 16 key groups of a tile P_KGROUP apart, the row groups P_NGROUP apart; byte
@@ -174,7 +179,13 @@ struct DecSmem {
   // [8] value-scale maxima, [NR] O factors, [NR] float2 (row-sum factor, exp-argument shift)
   static constexpr int OFF_RED = OFF_LIM + NR * 4;
   static constexpr int OFF_SB = (OFF_RED + (8 + NR + 2 * NR) * 4 + 15) / 16 * 16;  // [NR][128] f32 scores
-  static constexpr int OFF_BAR = OFF_SB + NR * 128 * 4;
+  // the A operand of the zero-point correction MMA: 128 keys x 16 k fp16, K-major without swizzle (the 8-key groups
+  // AZ_MGROUP apart, the two 8-k halves AZ_KHALF apart), one buffer per key-operand slot (int4: the key's zero point
+  // changes every tile) or one constant buffer (k8v4)
+  static constexpr int AZ_MGROUP = 128, AZ_KHALF = 2048, AZ_BYTES = 4096;
+  static constexpr int AZB = FMT == FMT_INT4 ? 2 : 1;
+  static constexpr int OFF_AZ = (OFF_SB + NR * 128 * 4 + 127) / 128 * 128;
+  static constexpr int OFF_BAR = OFF_AZ + AZB * AZ_BYTES;
   static constexpr int NBAR = 40;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_TMEM + 16;
@@ -210,6 +221,14 @@ __device__ __forceinline__ uint32_t nib_hi(uint32_t x, uint32_t hi_bias) {
   return hfma2_u32(lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u /* 1/16 */, hi_bias);
 }
 
+// Key operand codes as fp16 subnormals (bits = value x 2^24), one AND per pair of channels: int4 low nibbles give
+// u x 2^-24, high nibbles 16 u x 2^-24 (K0q divides the query's high-nibble channels by 16, exactly); k8v4 codes c
+// biased to c + 128 by one XOR, two bytes per prmt. The MMA then sums exact products u q 2^-24 (tcgen05 kind::f16
+// takes subnormal inputs), and the zero point (int4: per key; k8v4: the bias 128) comes off through one more MMA of
+// K 16 per tile: A = -zp x 2^-14 in three k, B = the query row's sum of its effective channels x 2^-10 split into
+// three fp16 terms (K0q), so that A B = -zp 2^-24 sum(q).
+constexpr uint32_t KEY_SUB_LO = 0x000F000Fu, KEY_SUB_HI = 0x00F000F0u;
+
 template <int NR>
 __device__ __forceinline__ void tmem_ld_rows(uint32_t taddr, float (&v)[NR]) {
   tmem_ld_cols<NR>(taddr, v);
@@ -232,8 +251,9 @@ __host__ __device__ __forceinline__ int qk_k_of_channel(int c) {
 
 // ---------------------------------------------------------------------------------------------------- K0q
 // One warp per (query token, query head): the row as K1 reads it (q_rec_bytes(HS)): HS fp16 in the k order of the
-// QK operand, scaled by a power of two (|q| < 2^14); then the fp32 row scale A (softmax_scale / head x log2 e x
-// 2^-exponent) and three zero words. Written once per call; every split of the row's KV head reads it.
+// QK operand, scaled by a power of two (|q| < 2^14; int4: the high-nibble channels by a further 2^-4); then the
+// fp32 row scale A (softmax_scale / head x log2 e x 2^(24 - exponent)), the three fp16 terms of the zero-point
+// correction (the row's sum x 2^-10) and zeros. Written once per call; every split of the row's KV head reads it.
 template <int FMT, int DT, int HS>
 __global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_t q_st, int64_t q_sh, int64_t T,
                                                            int nq, int nkv, const uint32_t* sign_bits, int q_rotated,
@@ -266,12 +286,31 @@ __global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_
     frexpf(am, &ex);  // am < 2^ex
     ex = 14 - ex;     // am * 2^ex in [2^13, 2^14)
   }
+  // int4: the high-nibble (odd) channels meet operand codes 16 u x 2^-24, so they carry q / 16 (a power of two:
+  // exact); ysum: the row's sum of the channel values the MMA effectively multiplies by u x 2^-24
+  float ysum = 0.f;
 #pragma unroll
-  for (int i = 0; i < E; ++i) qrow[qk_k_of_channel<FMT>(lane * E + i)] = __float2half_rn(ldexpf(x[i], ex));
+  for (int i = 0; i < E; ++i) {
+    const int c = lane * E + i;
+    const bool hi = FMT == FMT_INT4 && (c & 1);
+    const __half h = __float2half_rn(ldexpf(x[i], hi ? ex - 4 : ex));
+    qrow[qk_k_of_channel<FMT>(c)] = h;
+    ysum += hi ? 16.f * __half2float(h) : __half2float(h);
+  }
+  ysum = warp_sum(ysum);
   if (lane == 0) {
     float* rc = reinterpret_cast<float*>(rec + 2 * HS);
-    rc[0] = ldexpf(qk_scale, -ex);
-    rc[1] = rc[2] = rc[3] = 0.f;
+    rc[0] = ldexpf(qk_scale, 24 - ex);  // the MMA's scores carry 2^-24
+    // ysum x 2^-10 (|.| < 2^12) as three fp16 terms, each the rounding of what the terms before it left
+    const float y = ldexpf(ysum, -10);
+    const __half h1 = __float2half_rn(y);
+    const float r1 = y - __half2float(h1);
+    const __half h2 = __float2half_rn(r1);
+    const __half h3 = __float2half_rn(r1 - __half2float(h2));
+    uint32_t* rz = reinterpret_cast<uint32_t*>(rc + 1);
+    rz[0] = static_cast<uint32_t>(__half_as_ushort(h1)) | (static_cast<uint32_t>(__half_as_ushort(h2)) << 16);
+    rz[1] = __half_as_ushort(h3);
+    rz[2] = 0u;
   }
 }
 
@@ -414,6 +453,8 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
     // never carries out of it): one integer add per MMA.
     const uint64_t q_desc = sw128_desc(smem_u32(smem + SM::OFF_Q), 16, 1024);
     const uint64_t p_desc = interleave_desc(smem_u32(smem + SM::OFF_P), P_KGROUP, P_NGROUP);
+    const uint64_t az_desc = interleave_desc(smem_u32(smem + SM::OFF_AZ), SM::AZ_KHALF, SM::AZ_MGROUP);
+    const uint64_t qz_desc = sw128_desc(smem_u32(smem + SM::OFF_QZ), 16, 1024);
     auto wait_all = [&](uint64_t* bar, uint32_t parity) {
       const bool ok = mbar_wait_spin(bar, parity);
       failed |= __any_sync(0xffffffffu, !ok);
@@ -470,6 +511,8 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
             umma_f16_ts(sd, ak + 8 * s,
                         q_desc + static_cast<uint64_t>(((4 * ch + (s >> 2)) * SM::ATOM + (s & 3) * 32) >> 4), ID,
                         (ch | s) ? 1u : 0u);
+          if (ch == 0)  // the zero-point correction: S^T += A_z (smem, this slot's buffer) x Q_z^T
+            umma_f16(sd, az_desc + static_cast<uint64_t>(((sl % SM::AZB) * SM::AZ_BYTES) >> 4), qz_desc, ID, 1u);
           umma_commit(&bars[D_AK_FREE + sl]);
           if (ch == NCH - 1) umma_commit(&bars[D_S_FULL + b]);
         }
@@ -487,6 +530,15 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
     float4* kp = reinterpret_cast<float4*>(smem + SM::OFF_KP);
     uint32_t* zb = reinterpret_cast<uint32_t*>(smem + SM::OFF_ZB);
+    // this key's row of the correction MMA's A: k 8-15 zero in every buffer; k8v4: k 0-2 the constant -128 x 2^-14
+    uint8_t* const az = smem + SM::OFF_AZ + (kl >> 3) * SM::AZ_MGROUP + (kl & 7) * 16;
+#pragma unroll
+    for (int b = 0; b < SM::AZB; ++b) {
+      *reinterpret_cast<uint4*>(az + b * SM::AZ_BYTES + SM::AZ_KHALF) = make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (FMT != FMT_INT4)
+        *reinterpret_cast<uint4*>(az + b * SM::AZ_BYTES) = make_uint4(0xA000A000u, 0x0000A000u, 0u, 0u);
+    }
+    fence_async_smem();  // read by the MMAs (async proxy) after the first key-operand barrier
     for (int i = 0; i < ntl; ++i) {
       const int u = i * SPT + part, stage = u % RS, ki = i % KPS;
       bool ok = mbar_wait_spin(&bars[D_RAW_FULL + stage], (u / RS) & 1);
@@ -515,9 +567,9 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
         const uint32_t other = __shfl_xor_sync(0xffffffffu, (lane & 1) ? lo16 : hi16, 1);
         zb[ki * 128 + kl] = (lane & 1) ? (other | (hi16 << 16)) : (lo16 | (other << 16));
       }
-      // the key's zero point as the fp16 pair biases of nib_lo / nib_hi (int4; unused for k8v4)
-      const uint32_t kz16 = kw & 0xFu;
-      const uint32_t klo = (0x6400u | kz16) * 0x00010001u, khi = (0xD400u | (kz16 << 4)) * 0x00010001u;
+      // int4: -zp x 2^-14 as fp16 (exact: zp < 16), the key's k 0-2 of the correction MMA's A
+      uint32_t zneg = 0u;
+      if constexpr (FMT == FMT_INT4) zneg = __half_as_ushort(__float2half_rn(-ldexpf(kz, -14)));
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {  // 256 channels (128 TMEM columns) per chunk
         const int k = i * NCH + ch, sl = k % AKS;
@@ -526,6 +578,11 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
           break;
         }
         tc_fence_after();
+        if constexpr (FMT == FMT_INT4) {  // its buffer is free with the slot: the correction MMA goes with chunk 0
+          if (ch == 0)
+            *reinterpret_cast<uint4*>(az + (sl % SM::AZB) * SM::AZ_BYTES) =
+                make_uint4(zneg | (zneg << 16), zneg, 0u, 0u);
+        }
         const uint32_t dst = tmem + (sl ? TM::AK1 : TM::AK0) + lane_off;
         const uint8_t* kc = cell + ch * (CL::KB / NCH);
 #pragma unroll 1
@@ -539,10 +596,10 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
               for (int e = 0; e < 2; ++e) {
                 const uint32_t w = e ? w2.y : w2.x, w8 = w >> 8;
                 const int j = 8 * k4 + 4 * e;
-                a[j + 0] = nib_lo(w, klo);   // channels 8 w' + {0, 4}: u - zp, exact
-                a[j + 1] = nib_hi(w, khi);   // {1, 5}
-                a[j + 2] = nib_lo(w8, klo);  // {2, 6}
-                a[j + 3] = nib_hi(w8, khi);  // {3, 7}
+                a[j + 0] = w & KEY_SUB_LO;   // channels 8 w' + {0, 4}: u x 2^-24
+                a[j + 1] = w & KEY_SUB_HI;   // {1, 5}: 16 u x 2^-24
+                a[j + 2] = w8 & KEY_SUB_LO;  // {2, 6}
+                a[j + 3] = w8 & KEY_SUB_HI;  // {3, 7}
               }
             }
           } else {
@@ -553,15 +610,18 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
               for (int e = 0; e < 2; ++e) {
                 const uint32_t x = (e ? w2.y : w2.x) ^ 0x80808080u;
                 const int j = 4 * k8 + 2 * e;
-                // {1152 + c0, 1152 + c1} - 1152: the int8 codes, exact
-                a[j] = hsub2_u32(prmt(x, 0x64646464u, 0x4140u), 0x64806480u);
-                a[j + 1] = hsub2_u32(prmt(x, 0x64646464u, 0x4342u), 0x64806480u);
+                // {c0 + 128, c1 + 128} x 2^-24
+                a[j] = prmt(x, 0u, 0x4140u);
+                a[j + 1] = prmt(x, 0u, 0x4342u);
               }
             }
           }
           tmem_st32u(dst + 32 * c, a);
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        if constexpr (FMT == FMT_INT4) {
+          if (ch == 0) fence_async_smem();
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[D_AK_FULL + sl]);
@@ -691,6 +751,15 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (r < rows) v = *reinterpret_cast<const uint4*>(qsrc + r * QREC + 16 * ch);
         *reinterpret_cast<uint4*>(smem + SM::OFF_Q + (ch >> 3) * SM::ATOM + sw128_off(r, ch & 7)) = v;
+      }
+      for (int idx = stid; idx < NR * 2; idx += SMX_THREADS) {  // k 0-15 of the correction atom: terms, zeros
+        const int r = idx >> 1, ch = idx & 1;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (r < rows && ch == 0) {
+          const uint32_t* rz = reinterpret_cast<const uint32_t*>(qsrc + r * QREC + 2 * HS + 4);
+          v = make_uint4(rz[0], rz[1], 0u, 0u);
+        }
+        *reinterpret_cast<uint4*>(smem + SM::OFF_QZ + sw128_off(r, ch)) = v;
       }
       for (int r = stid; r < NR; r += SMX_THREADS) {
         float2 c = make_float2(0.f, INFINITY);
