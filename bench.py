@@ -169,6 +169,7 @@ def build_request(torch, ops, w, device, seqs, seed=0):
 
 
 FLUSH_BYTES = 256 << 20   # each half of the flush buffer is twice the 126 MB L2
+LEAD_CYCLES = 100_000     # ~50 us of device spin before each start event: the host enqueues the whole step behind it
 
 
 def l2_flush(flush):
@@ -194,11 +195,14 @@ def sustain(torch, fn, seconds=1.0):
     return n
 
 
-def timed_steps(torch, fn, steps, warmup, flush, align=None):
+def timed_steps(torch, fn, steps, warmup, flush, align=None, lead=True):
     """Run `warmup` untimed steps, then `steps` steps each timed by CUDA events (L2 flushed before each). With several
     ranks, `align` (a one-element all-reduce on the stream) runs after the flush and before the start event, so that
     every rank starts its timed step when the slowest rank has finished its flush: a step with a collective inside
-    otherwise also times the other rank's flush and host-launch skew."""
+    otherwise also times the other rank's flush and host-launch skew. A short device spin (LEAD_CYCLES) then runs
+    before the start event, so that the host has enqueued the step's launches by the time the device reaches it and
+    the events time the device work, not the host's launch latency; lead=False (the end-to-end loops) leaves it out,
+    so that those times keep whatever launch latency the host adds."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -207,6 +211,8 @@ def timed_steps(torch, fn, steps, warmup, flush, align=None):
         l2_flush(flush)
         if align is not None:
             align()
+        if lead:
+            torch.cuda._sleep(LEAD_CYCLES)
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
@@ -394,7 +400,7 @@ def measure_prefill(args, torch, dist, ops, lib, w, device, rank, world, flush, 
         sustain(torch, step, 1.0)
         t = timed_steps(torch, step, args.steps, args.warmup, flush, align)
     t_k = timed_steps(torch, kernel_only, args.steps, args.warmup, flush, align)
-    t_e = timed_steps(torch, e2e_step, args.steps, args.warmup, flush, align)
+    t_e = timed_steps(torch, e2e_step, args.steps, args.warmup, flush, align, lead=False)
     ms, ms_k, ms_e = max_over_ranks(torch, dist, world, device,
                                     [statistics.mean(t), statistics.mean(t_k), statistics.mean(t_e)])
     refl = reference_fa2_prefill(torch, ops, R, w, flush, args) if with_reference and world == 1 else None
@@ -408,7 +414,8 @@ def measure_prefill(args, torch, dist, ops, lib, w, device, rank, world, flush, 
            "config": {"workload": "c3", **w, "nq": NQ, "nkv": NKV, "head_size": HS, "block_size": BS,
                       "parallelism": f"context split by sequence range over {world} GPUs, {exchange_name(runner)}"
                       if world > 1 else "1 GPU",
-                      "l2": "flushed before every step; cache larger than L2"},
+                      "l2": "flushed before every step; cache larger than L2",
+                      "timing": "CUDA events; a ~50 us device spin before each start event hides host launch latency (not in e2e)"},
            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                         "frac": achieved / peak, "traffic": TRAFFIC.get("c3") if world == 1 else None,
                         "traffic_unit": "bytes per launch (ncu dram__bytes_read + write)",
@@ -520,7 +527,7 @@ def run_b200(args, w, rank, world, local_rank):
         sustain(torch, step, 1.0)
         t_step = timed_steps(torch, step, args.steps, args.warmup, flush, align)
     t_kernel = timed_steps(torch, kernel_only, args.steps, args.warmup, flush, align)
-    t_e2e = timed_steps(torch, e2e_step, args.steps, args.warmup, flush, align)
+    t_e2e = timed_steps(torch, e2e_step, args.steps, args.warmup, flush, align, lead=False)
     torch.cuda.synchronize()
     ms, ms_k, ms_e = max_over_ranks(torch, dist, world, device,
                                     [statistics.mean(t_step), statistics.mean(t_kernel), statistics.mean(t_e2e)])
@@ -560,7 +567,8 @@ def run_b200(args, w, rank, world, local_rank):
         "config": {"workload": args.workload, **w, "nq": NQ, "nkv": NKV, "head_size": HS, "block_size": BS,
                    "num_splits": nsplit, "parallelism": f"one request split by sequence range over {world} GPUs "
                    f"({part['ctx']} tokens each), {exchange_name(runner)}" if world > 1 else "1 GPU",
-                   "l2": "flushed before every step (256 MB write, then 256 MB read); cache larger than L2"},
+                   "l2": "flushed before every step (256 MB write, then 256 MB read); cache larger than L2",
+                   "timing": "CUDA events; a ~50 us device spin before each start event hides host launch latency (not in e2e)"},
         "hbm_gbs": bytes_rank / (ms * 1e-3) / 1e9,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": TRAFFIC.get(args.workload) if world == 1 else None,
