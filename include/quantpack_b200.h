@@ -96,6 +96,10 @@ int64_t qp_decode_workspace_bytes(int64_t num_q_tokens, int num_q_heads, int hea
  * tokens_after_keys: tokens of every sequence that follow its seqused_k cached keys here (a sequence-parallel rank
  * holding an earlier range of the sequence): query token i then sees key k iff k <= seqused_k - qlen + i +
  * tokens_after_keys; 0 for an ordinary call, >= qlen - 1 lifts the causal mask.
+ * sliding_window: vLLM's SLIDING_WINDOW (1 + window_size[0]; 0 = none): query token i whose last visible key is p
+ * sees the keys [p - sliding_window + 1, p] only, as the stock kernel masks them (vllm/v1/attention/ops/
+ * triton_attention_helpers.py:196-218 and triton_unified_attention.py:533-536, vLLM 0.22); the splits then cover
+ * only the tiles of the window, so num_splits should come from min(context, window + max_seqlen_q + 127).
  * out_mode 0: out in dtype, model domain. out_mode 1: out fp32 in the RHT domain and lse_out (tokens, num_q_heads)
  * the base-2 log-sum-exp of the scaled scores (the partial a sequence-parallel rank exchanges). out_mode 2: the
  * split partials only, left in the workspace as part_o (tokens, num_q_heads, num_splits, head_size) fp32 followed by
@@ -111,8 +115,8 @@ int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stride_token, i
                     int64_t block_stride, int64_t head_stride, int64_t slot_stride, int64_t k_off, int64_t ks_off,
                     int64_t v_off, int64_t vs_off, int num_q_heads, int num_kv_heads, int head_size,
                     float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated, int tokens_after_keys,
-                    int out_mode, float* lse_out, int num_splits, void* workspace, int64_t workspace_bytes,
-                    void* stream);
+                    int sliding_window, int out_mode, float* lse_out, int num_splits, void* workspace,
+                    int64_t workspace_bytes, void* stream);
 
 /* Bytes of workspace qp_prefill needs for a chunk of qlen queries over a context of n tokens (prepared query tiles
  * and per-piece partials). */
@@ -144,9 +148,11 @@ int64_t qp_prefill_varlen_workspace_bytes(int64_t num_q_tokens, int num_chunks, 
 /* Short prefill chunks of several sequences in one launch: chunk i's query tokens q[cu_seqlens_q[i] ..
  * cu_seqlens_q[i + 1]) are the last positions of its context of seqused_k[i] cached tokens (causal among themselves),
  * read through block_table[i]; cu_seqlens_q / seqused_k are device int32 arrays (num_chunks + 1 / num_chunks) that
- * the call never reads back to the host. max_seqlen_k bounds seqused_k (it sizes the split count). The chunks run on
- * the split-KV decode kernel as sub-sequences of 32 / (query heads per KV head) tokens. out / out_mode / lse_out /
- * q_rotated as in qp_paged_decode (out_mode 0 or 1); head_size 256 or 512; HND cells, block_size % 16 == 0.
+ * the call never reads back to the host. max_seqlen_k bounds the keys any query token sees (seqused_k, or with a
+ * sliding window min(seqused_k, sliding_window + 158)); it sizes the split count and the workspace. The chunks run
+ * on the split-KV decode kernel as sub-sequences of 32 / (query heads per KV head) tokens. out / out_mode / lse_out /
+ * q_rotated / sliding_window as in qp_paged_decode (out_mode 0 or 1); head_size 256 or 512; HND cells,
+ * block_size % 16 == 0.
  * Replaces the Triton 2D sub-batch that the plugin runs for every chunk that is not long (int4_kv.py:113-119,
  * 313-323). */
 int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head, void* out,
@@ -155,8 +161,8 @@ int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_stride_token,
                       const int32_t* block_table, int64_t block_table_stride, const void* cache, int block_size,
                       int64_t block_stride, int64_t head_stride, int64_t slot_stride, int64_t k_off, int64_t ks_off,
                       int64_t v_off, int64_t vs_off, int num_q_heads, int num_kv_heads, int head_size,
-                      float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated, int out_mode, float* lse_out,
-                      void* workspace, int64_t workspace_bytes, void* stream);
+                      float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated, int sliding_window,
+                      int out_mode, float* lse_out, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Bytes of the library's static decode scratch used by qp_paged_decode_static. */
 #define QP_STATIC_DECODE_SCRATCH_BYTES (32ll << 20)
@@ -169,7 +175,8 @@ int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_stride_token,
  * the array and it keeps the last call's contents (nothing in it needs to start at zero); calls that overlap on the
  * GPU race on it, so serialize them. The array holds the split partials and the prepared query rows. Only out_mode 0
  * and 1 are served (QP_ERR_INVALID for 2: the partials would stay where no caller can reach them), and the keys are
- * taken as the sequence's last ones (tokens_after_keys 0): a single-GPU decode, not a rank of a sequence split.
+ * taken as the sequence's last ones (tokens_after_keys 0) with no sliding window: a single-GPU decode, not a rank of
+ * a sequence split.
  * Allocates nothing. No counterpart in the reference. */
 int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head,
                            void* out, int64_t out_stride_token, int64_t out_stride_head, int64_t num_q_tokens,

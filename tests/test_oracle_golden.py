@@ -135,3 +135,46 @@ def test_merge_of_partials_equals_whole_attention():
     merged, mlse = qo.merge_partials(np.stack([o1, o2]), np.stack([l1, l2]))
     assert np.allclose(merged, whole, atol=1e-12)
     assert np.allclose(mlse, lse, atol=1e-12)
+
+
+@pytest.mark.parametrize("window", [1, 3, 64, 129, 500])
+def test_sliding_window_keeps_the_last_window_keys_of_each_query(window):
+    """vLLM's SLIDING_WINDOW (1 + window_size[0]): the query at position p sees keys p - window + 1 .. p, restated
+    here as the attention over exactly those keys, per query token."""
+    rng = np.random.default_rng(3)
+    n, qlen, nq, nkv, hs = 300, 4, 4, 2, 32
+    K = rng.standard_normal((n, nkv, hs))
+    V = rng.standard_normal((n, nkv, hs))
+    q = rng.standard_normal((qlen, nq, hs))
+    got, lse = qo.attention_rht_domain(q, K, V, n, hs ** -0.5, hs, window)
+    for i in range(qlen):
+        p = n - qlen + i
+        lo = max(0, p - window + 1)
+        want, wl = qo.attention_rht_domain(q[i:i + 1], K[lo:p + 1], V[lo:p + 1], p + 1 - lo, hs ** -0.5, hs)
+        np.testing.assert_allclose(got[i], want[0], rtol=1e-12, atol=1e-12)
+        np.testing.assert_allclose(lse[i], wl[0], rtol=1e-12)
+    whole, _ = qo.attention_rht_domain(q, K, V, n, hs ** -0.5, hs)
+    if window >= n:
+        np.testing.assert_allclose(got, whole, rtol=1e-12, atol=1e-12)
+    else:
+        assert not np.allclose(got, whole)
+
+
+@pytest.mark.parametrize("window", [5, 100, 1000])
+def test_streamed_oracle_skips_only_chunks_outside_every_window(window):
+    """attention_from_cache reads the keys in chunks and skips the chunks before the first query's window: the same
+    result as the attention over the whole dequantised sequence."""
+    hs, nkv, nq, bs, n, qlen = 32, 2, 4, 16, 400, 3
+    nblocks = n // bs + 2
+    layout = qo.CacheLayout("int4", nblocks, nkv, bs, hs)
+    cache = np.zeros(nblocks * nkv * bs * layout.cell, dtype=np.uint8)
+    kb, vb = qo.synthetic_kv(n, nkv, hs, seed=1)
+    table = np.random.default_rng(2).permutation(nblocks)[: n // bs].astype(np.int32)
+    pos = np.arange(n)
+    qo.store("int4", kb, vb, table[pos // bs].astype(np.int64) * bs + pos % bs, cache, layout, qo.rht_signs(hs))
+    q = np.random.default_rng(4).standard_normal((qlen, nq, hs))
+    got, gl = qo.attention_from_cache(q, cache, layout, table, n, hs ** -0.5, chunk=64, sliding_window=window)
+    K, V = qo.read_sequence(cache, layout, table, n)
+    want, wl = qo.attention_rht_domain(q, K, V, n, hs ** -0.5, hs, window)
+    np.testing.assert_allclose(got, want, rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(gl, wl, rtol=1e-10)

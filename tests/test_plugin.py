@@ -226,6 +226,7 @@ class Recorder:
 
     def __init__(self, monkeypatch):
         self.calls = []
+        self.windows = []   # the sliding_window of every decode / varlen launch
         monkeypatch.setattr(ops, "paged_decode", self.decode)
         monkeypatch.setattr(ops, "prefill", self.prefill)
         monkeypatch.setattr(ops, "prefill_varlen", self.varlen)
@@ -233,6 +234,7 @@ class Recorder:
     def decode(self, q, kc, vc, out, *, cu_seqlens_q, seqused_k, block_table, max_seqlen_q, num_splits, **kw):
         self.calls.append(("decode", q.shape[0], cu_seqlens_q.tolist(), seqused_k.tolist(), max_seqlen_q,
                            num_splits))
+        self.windows.append(kw.get("sliding_window", 0))
         for b in range(len(seqused_k)):
             out[cu_seqlens_q[b]:cu_seqlens_q[b + 1]] = float(block_table[b, 0])
         return out
@@ -244,6 +246,7 @@ class Recorder:
 
     def varlen(self, q, kc, vc, out, *, cu_seqlens_q, seqused_k, max_seqlen_k, block_table, **kw):
         self.calls.append(("varlen", q.shape[0], cu_seqlens_q.tolist(), seqused_k.tolist(), max_seqlen_k))
+        self.windows.append(kw.get("sliding_window", 0))
         for b in range(len(seqused_k)):
             out[cu_seqlens_q[b]:cu_seqlens_q[b + 1]] = float(block_table[b, 0])
         return out
@@ -304,12 +307,37 @@ def test_unsupported_features_go_to_the_stock_path(monkeypatch):
     rec = Recorder(monkeypatch)
     stock, stock_calls = _stock_recorder()
     fn = int4_kv.make_unified_attention(stock)
-    q, kc, out, args = _step([4], [5000], window=(4096, 0))
-    fn(q, kc, kc, out, **args)
-    assert not rec.calls and len(stock_calls) == 1
     q, kc, out, args = _step([4], [5000])
     fn(q, kc, kc, out, **dict(args, softcap=30.0))
+    assert not rec.calls and len(stock_calls) == 1
+    fn(q, kc, kc, out, **dict(args, sinks=torch.zeros(NQ)))
     assert not rec.calls and len(stock_calls) == 2
+
+
+def test_sliding_window_layers_run_on_the_split_kv_kernel(monkeypatch):
+    """window_size (w, 0) is vLLM's SLIDING_WINDOW = w + 1: decodes take it to the split-KV kernel, and every prefill
+    chunk (the long one too: the tcgen05 prefill kernel has no window) goes to the one varlen launch."""
+    rec = Recorder(monkeypatch)
+    stock, stock_calls = _stock_recorder()
+    fn = int4_kv.make_unified_attention(stock)
+    q, kc, out, args = _step([4, 1], [5000, 700], window=(1023, 0))
+    fn(q, kc, kc, out, **args)
+    assert rec.calls == [("decode", q.shape[0], [0, 4, 5], [5000, 700], 4, None)] and rec.windows == [1024]
+    rec.calls.clear()
+    rec.windows.clear()
+    q, kc, out, args = _step([256, 2, 40], [40000, 20000, 300], window=(511, 0))
+    fn(q, kc, kc, out, **args)
+    assert ("decode", 2, [0, 2], [20000], 2, None) in rec.calls
+    assert ("varlen", 296, [0, 256, 296], [40000, 300], 40000) in rec.calls
+    assert len(rec.calls) == 2 and rec.windows == [512, 512] and not stock_calls
+    assert (out[:256] == 1).all() and (out[256:258] == 2).all() and (out[258:298] == 3).all()
+    # no window: (-1, -1); the same step then sends the long chunk to the prefill kernel
+    rec.calls.clear()
+    q, kc, out, args = _step([256, 2, 40], [40000, 20000, 300])
+    fn(q, kc, kc, out, **args)
+    assert ("prefill", 256, 40000) in rec.calls and len(rec.calls) == 3
+    assert int4_kv.sliding_window_of((-1, -1)) == 0 and int4_kv.sliding_window_of(None) == 0
+    assert int4_kv.sliding_window_of((0, 0)) == 1
 
 
 def test_head_512_is_served_and_other_head_sizes_go_stock(monkeypatch):
@@ -488,10 +516,10 @@ def test_k8v4_call_outside_the_kernels_raises(monkeypatch):
     Recorder(monkeypatch)
     stock, stock_calls = _stock_recorder()
     fn = int4_kv.make_unified_attention(stock)
-    q, _, out, args = _step([4], [5000], window=(4096, 0))
+    q, _, out, args = _step([4], [5000])
     kc8 = torch.zeros((4, 16, NKV, HS), dtype=torch.int8)
     with pytest.raises(NotImplementedError, match="k8v4"):
-        fn(q, kc8, kc8, out, **args)
+        fn(q, kc8, kc8, out, **dict(args, sinks=torch.zeros(NQ)))
     with pytest.raises(NotImplementedError, match="k8v4"):
         fn(q, kc8, kc8, out, **dict(args, softcap=30.0))
     fn2 = int4_kv.make_unified_attention(stock, prefill_on=False)

@@ -76,10 +76,20 @@ def decode_splits_override():
     return int(parts[2])
 
 
-def _plain(q, window_size, softcap, sinks, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
-    """True when the call uses no feature outside the B200 kernels (int4_kv.py:304-305)."""
-    return (window_size is None or window_size[0] < 0) and not softcap and sinks is None and alibi_slopes is None \
-        and qq_bias is None and output_scale is None and mm_prefix_range is None and q.shape[2] in HEAD_SIZES
+def _plain(q, softcap, sinks, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
+    """True when the call uses no feature outside the B200 kernels (the reference's list, int4_kv.py:304-305, less
+    the sliding window, which the split-KV kernel applies)."""
+    return not softcap and sinks is None and alibi_slopes is None and qq_bias is None and output_scale is None \
+        and mm_prefix_range is None and q.shape[2] in HEAD_SIZES
+
+
+def sliding_window_of(window_size):
+    """vLLM's SLIDING_WINDOW from the window_size argument (1 + left window, 0 for none): a query token at position p
+    sees keys p - SLIDING_WINDOW + 1 .. p (vllm/v1/attention/ops/triton_unified_attention.py:855, 1008, vLLM 0.22;
+    the right window is not applied there either)."""
+    if window_size is None or window_size[0] < 0:
+        return 0
+    return 1 + int(window_size[0])
 
 
 def _forward_step():
@@ -98,26 +108,27 @@ class StepPlan:
     without a wait. The reference reads both lists per step (int4_kv.py:260-278) and rebuilds its sub-batch indices
     per layer; here the second and later layers of a step touch no host memory at all."""
 
-    def __init__(self, cu_seqlens_q, seqused_k, group, prefill_on, head_size=256):
+    def __init__(self, cu_seqlens_q, seqused_k, group, prefill_on, head_size=256, long_chunks=True):
         nseq = seqused_k.shape[0]
         both = torch.cat([cu_seqlens_q.to(torch.int64), seqused_k.to(torch.int64)]).tolist()
         self.cu, self.used = both[:nseq + 1], both[nseq + 1:]
-        self.dec, self.pre, self.short, self.stock = split_step(self.cu, self.used, group, prefill_on, head_size)
+        self.dec, self.pre, self.short, self.stock = split_step(self.cu, self.used, group, prefill_on, head_size,
+                                                                long_chunks)
         dev = cu_seqlens_q.device
         self.dec_batch = _SubBatch(self.dec, self.cu, self.used, dev) if self.dec else None
         self.short_batch = _SubBatch(self.short, self.cu, self.used, dev) if self.short else None
         self.stock_batch = _SubBatch(self.stock, self.cu, self.used, dev) if self.stock else None
 
     @staticmethod
-    def of(cu_seqlens_q, seqused_k, group, prefill_on, head_size=256):
+    def of(cu_seqlens_q, seqused_k, group, prefill_on, head_size=256, long_chunks=True):
         """The step's plan, kept on vLLM's forward context (keyed by the length tensors themselves: another KV-cache
         group of the same step gets other tensors)."""
         step = _forward_step()
         plans = getattr(step, "_quantpack_b200_plans", None) if step is not None else None
-        key = (id(cu_seqlens_q), id(seqused_k), group, prefill_on, head_size)
+        key = (id(cu_seqlens_q), id(seqused_k), group, prefill_on, head_size, long_chunks)
         if plans is not None and key in plans and plans[key][0] is cu_seqlens_q and plans[key][1] is seqused_k:
             return plans[key][2]
-        plan = StepPlan(cu_seqlens_q, seqused_k, group, prefill_on, head_size)
+        plan = StepPlan(cu_seqlens_q, seqused_k, group, prefill_on, head_size, long_chunks)
         if step is not None:
             try:
                 if plans is None:
@@ -152,13 +163,14 @@ class _SubBatch:
         out[self.rows] = sub_out
 
 
-def split_step(cu, used, group, prefill_on=True, head_size=256):
+def split_step(cu, used, group, prefill_on=True, head_size=256, long_chunks=True):
     """Requests of one step by path: (decode, long, short, stock) index lists. Decode: 1..MAX_Q_SPLIT_KV query tokens
     whose rows fit one decode CTA. The other requests with queries are prefill chunks: long ones (at least MIN_QUERY
     tokens over at least MIN_CONTEXT cached tokens, or enough query rows to fill the machine on their own; head 256)
     each go to the tcgen05 prefill kernel, the rest together to one varlen launch of the split-KV kernel, as the
     reference sends its long chunks to FlashAttention and the rest to one Triton sub-batch (int4_kv.py:313-323).
-    With prefill routing off every chunk goes to the stock path. Requests without queries are left out."""
+    long_chunks=False (a sliding-window layer: the prefill kernel has no window) sends every chunk to the varlen
+    launch. With prefill routing off every chunk goes to the stock path. Requests without queries are left out."""
     from .int4_prefill import MIN_CONTEXT, MIN_QUERY
     dec, long, short, stock = [], [], [], []
     for i in range(len(used)):
@@ -169,7 +181,8 @@ def split_step(cu, used, group, prefill_on=True, head_size=256):
             dec.append(i)
         elif not prefill_on:
             stock.append(i)
-        elif head_size == 256 and ql >= MIN_QUERY and (used[i] >= MIN_CONTEXT or ql * group >= LONG_ROWS):
+        elif long_chunks and head_size == 256 and ql >= MIN_QUERY and (used[i] >= MIN_CONTEXT or
+                                                                       ql * group >= LONG_ROWS):
             long.append(i)
         else:
             short.append(i)
@@ -179,7 +192,8 @@ def split_step(cu, used, group, prefill_on=True, head_size=256):
 def make_unified_attention(stock_unified, prefill_on=True):
     """The replacement of `unified_attention_int4` (signature of int4_kv.py:294-301), falling back to
     `stock_unified` for int4 calls the B200 kernels do not cover. A k8v4 cache has no stock kernel to fall back to
-    (the stock int4 kernel would read its int8 keys as nibbles), so such a call raises instead."""
+    (the stock int4 kernel would read its int8 keys as nibbles), so such a call raises instead. A sliding-window
+    layer runs on the split-KV kernel: decodes as usual, every prefill chunk in the varlen launch."""
     from . import k8v4_kv, ops
 
     def unified_attention_int4(q, k_cache, v_cache, out, *, cu_seqlens_q, max_seqlen_q, seqused_k, max_seqlen_k,
@@ -190,26 +204,27 @@ def make_unified_attention(stock_unified, prefill_on=True):
                     block_table=block_table, softcap=softcap, sinks=sinks, alibi_slopes=alibi_slopes,
                     use_alibi_sqrt=use_alibi_sqrt, qq_bias=qq_bias, output_scale=output_scale,
                     mm_prefix_range=mm_prefix_range, k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache, **kw)
-        if not _plain(q, window_size, softcap, sinks, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
+        if not _plain(q, softcap, sinks, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
             if k8v4_kv.is_k8v4(k_cache):
                 raise NotImplementedError(
-                    f"{k8v4_kv.NAME}: sliding window, softcap, sinks, ALiBi, qq_bias, FP8 output, mm_prefix ranges and "
-                    f"head sizes other than {HEAD_SIZES} are not served by the B200 kernels, and vLLM's stock int4 "
-                    f"kernel cannot read a k8v4 cache")
+                    f"{k8v4_kv.NAME}: softcap, sinks, ALiBi, qq_bias, FP8 output, mm_prefix ranges and head sizes "
+                    f"other than {HEAD_SIZES} are not served by the B200 kernels, and vLLM's stock int4 kernel cannot "
+                    f"read a k8v4 cache")
             return stock_unified(q, k_cache, v_cache, out, **args)
         group = q.shape[1] // k_cache.shape[2]
         splits = decode_splits_override()
+        window = sliding_window_of(window_size)
 
         def decode(qs, outs, a):
             ops.paged_decode(qs, k_cache, v_cache, outs, cu_seqlens_q=a["cu_seqlens_q"],
                              max_seqlen_q=a["max_seqlen_q"], seqused_k=a["seqused_k"], max_seqlen_k=a["max_seqlen_k"],
                              softmax_scale=softmax_scale, block_table=a["block_table"], k_scale_cache=k_scale_cache,
-                             v_scale_cache=v_scale_cache, num_splits=splits)
+                             v_scale_cache=v_scale_cache, num_splits=splits, sliding_window=window)
 
         if max_seqlen_q <= MAX_Q_SPLIT_KV and max_seqlen_q * group <= MAX_DECODE_ROWS:
             # a decode step: no host read of the lengths (CUDA-graph capturable)
             return decode(q, out, args)
-        plan = StepPlan.of(cu_seqlens_q, seqused_k, group, prefill_on, q.shape[2])
+        plan = StepPlan.of(cu_seqlens_q, seqused_k, group, prefill_on, q.shape[2], long_chunks=window == 0)
         if plan.dec_batch is not None:
             plan.dec_batch.run(decode, q, out, args)
         if plan.short_batch is not None:
@@ -217,7 +232,7 @@ def make_unified_attention(stock_unified, prefill_on=True):
                 lambda qs, outs, a: ops.prefill_varlen(
                     qs, k_cache, v_cache, outs, cu_seqlens_q=a["cu_seqlens_q"], seqused_k=a["seqused_k"],
                     max_seqlen_k=a["max_seqlen_k"], block_table=a["block_table"], softmax_scale=softmax_scale,
-                    k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache), q, out, args)
+                    k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache, sliding_window=window), q, out, args)
         if plan.stock_batch is not None:
             if k8v4_kv.is_k8v4(k_cache):
                 raise NotImplementedError(f"{k8v4_kv.NAME}: prefill chunks need the B200 prefill kernel "

@@ -147,13 +147,25 @@ def sm_count(device):
     return torch.cuda.get_device_properties(device).multi_processor_count
 
 
+VARLEN_MAX_Q = 32   # query tokens of a varlen sub-sequence at most (32 query rows per KV head)
+
+
+def window_keys(max_seqlen_k, sliding_window, max_q):
+    """Keys the split count is sized for: the context, or with a sliding window the span of the tiles a request's
+    windows cover (its first token's window start to its last token, plus a partial tile)."""
+    max_seqlen_k = int(max_seqlen_k)
+    if sliding_window and sliding_window > 0:
+        return min(max_seqlen_k, int(sliding_window) + int(max_q) - 1 + 127)
+    return max_seqlen_k
+
+
 def decode_num_splits(num_seqs, num_kv_heads, max_seqlen_k, sms):
     return _lib.load().qp_decode_num_splits(num_seqs, num_kv_heads, max_seqlen_k, sms)
 
 
 def paged_decode(q, key_cache, value_cache, out, *, cu_seqlens_q, max_seqlen_q, seqused_k, max_seqlen_k,
                  softmax_scale, block_table, k_scale_cache, v_scale_cache, num_splits=None, q_rotated=False,
-                 out_fp32_lse=None, ws=None, partials_only=False, tokens_after_keys=0):
+                 out_fp32_lse=None, ws=None, partials_only=False, tokens_after_keys=0, sliding_window=0):
     """Split-KV decode of up to 32 query rows per KV head (4 MTP tokens x 6 heads) over the paged cache.
 
     q / out (tokens, query heads, hs). When `out_fp32_lse` is a tensor (tokens, query heads) fp32, `out` must be fp32
@@ -161,14 +173,16 @@ def paged_decode(q, key_cache, value_cache, out, *, cu_seqlens_q, max_seqlen_q, 
     rank exchanges); otherwise `out` gets the model-domain output in q's dtype. partials_only=True launches the split
     kernel alone and leaves its partials in the workspace (returned). tokens_after_keys: sequence tokens that follow
     the cached keys given here (a sequence-parallel rank holding an earlier range): query token i of a sequence sees
-    key k iff k <= seqused_k - qlen + i + tokens_after_keys."""
+    key k iff k <= seqused_k - qlen + i + tokens_after_keys. sliding_window: vLLM's SLIDING_WINDOW (1 +
+    window_size[0], 0 = none): that token then sees only the keys k > its last key - sliding_window."""
     hs = q.shape[-1]
     nq = q.shape[1]
     lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
     nkv = lay.nkv
     num_seqs = cu_seqlens_q.shape[0] - 1
     if num_splits is None:
-        num_splits = decode_num_splits(num_seqs, nkv, int(max_seqlen_k), sm_count(q.device))
+        num_splits = decode_num_splits(num_seqs, nkv, window_keys(max_seqlen_k, sliding_window, max_seqlen_q),
+                                       sm_count(q.device))
     wbytes = _lib.load().qp_decode_workspace_bytes(q.shape[0], nq, hs, int(num_splits))
     if ws is None:
         ws = workspace(q.device, wbytes)
@@ -195,8 +209,8 @@ def paged_decode(q, key_cache, value_cache, out, *, cu_seqlens_q, max_seqlen_q, 
     _lib.call("qp_paged_decode", lay.fmt, dt, q.data_ptr(), q.stride(0), q.stride(1), out.data_ptr(), out.stride(0),
               out.stride(1), q.shape[0], num_seqs, cu_seqlens_q.data_ptr(), seqused_k.data_ptr(), int(max_seqlen_q),
               block_table.data_ptr(), block_table.stride(0), *lay.args(), nq, nkv, hs, float(softmax_scale),
-              rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)), int(tokens_after_keys), mode,
-              lse_ptr, int(num_splits),
+              rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)), int(tokens_after_keys),
+              int(sliding_window), mode, lse_ptr, int(num_splits),
               ws.data_ptr(), ws.numel() * ws.element_size(), _stream(q.device))
     return ws if partials_only else out
 
@@ -275,13 +289,14 @@ def prefill(q, key_cache, value_cache, out, *, block_row, n, softmax_scale, k_sc
 
 
 def prefill_varlen(q, key_cache, value_cache, out, *, cu_seqlens_q, seqused_k, max_seqlen_k, block_table,
-                   softmax_scale, k_scale_cache, v_scale_cache, q_rotated=False, out_fp32_lse=None, ws=None):
+                   softmax_scale, k_scale_cache, v_scale_cache, q_rotated=False, out_fp32_lse=None, ws=None,
+                   sliding_window=0):
     """Several short prefill chunks in ONE launch (the reference's Triton sub-batch of the chunks that are not long,
     vllm_quantpack/attention/int4_kv.py:313-323): request i's query tokens q[cu_seqlens_q[i]:cu_seqlens_q[i + 1]] are
     the last positions of its context of seqused_k[i] cached tokens, causal among themselves, read through
     block_table[i]. Split on the device into sub-sequences of 32 / group tokens for the split-KV kernel, so nothing
     is read back to the host; max_seqlen_k (a host int, an upper bound of seqused_k) sizes the split count.
-    `out` as in prefill."""
+    `out` as in prefill; sliding_window as in paged_decode."""
     hs, nq, T = q.shape[-1], q.shape[1], q.shape[0]
     lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
     for name, t in (("cu_seqlens_q", cu_seqlens_q), ("seqused_k", seqused_k), ("block_table", block_table)):
@@ -292,7 +307,8 @@ def prefill_varlen(q, key_cache, value_cache, out, *, cu_seqlens_q, seqused_k, m
     dt = _dtype_code(q, "prefill_varlen")
     chunks = seqused_k.shape[0]
     lib = _lib.load()
-    wbytes = lib.qp_prefill_varlen_workspace_bytes(T, chunks, nq, lay.nkv, hs, int(max_seqlen_k))
+    max_k = window_keys(max_seqlen_k, sliding_window, VARLEN_MAX_Q)
+    wbytes = lib.qp_prefill_varlen_workspace_bytes(T, chunks, nq, lay.nkv, hs, max_k)
     if ws is None:
         ws = workspace(q.device, wbytes)
     if out_fp32_lse is not None:
@@ -305,7 +321,7 @@ def prefill_varlen(q, key_cache, value_cache, out, *, cu_seqlens_q, seqused_k, m
         mode, lse_ptr = 0, None
     _lib.call("qp_prefill_varlen", lay.fmt, dt, q.data_ptr(), q.stride(0), q.stride(1), out.data_ptr(),
               out.stride(0), out.stride(1), T, chunks, cu_seqlens_q.data_ptr(), seqused_k.data_ptr(),
-              int(max_seqlen_k), block_table.data_ptr(), block_table.stride(0), *lay.args(), nq, lay.nkv, hs,
-              float(softmax_scale), rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)), mode,
-              lse_ptr, ws.data_ptr(), ws.numel() * ws.element_size(), _stream(q.device))
+              max_k, block_table.data_ptr(), block_table.stride(0), *lay.args(), nq, lay.nkv, hs,
+              float(softmax_scale), rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)),
+              int(sliding_window), mode, lse_ptr, ws.data_ptr(), ws.numel() * ws.element_size(), _stream(q.device))
     return out

@@ -44,6 +44,7 @@
 // Every wait is bounded (a timeout records an error word and the roles leave; the softmax warps leave together).
 #include <math.h>
 
+#include <algorithm>
 #include <atomic>
 #include <type_traits>
 
@@ -113,6 +114,9 @@ struct DecodeParams {
   // sees, block-table row}, causal inside it (built on the device by varlen_table_kernel; entries past the real ones
   // hold 0 query tokens). cu_seqlens_q / seqused_k are not read.
   const int4* subseq;
+  // window > 0: vLLM's SLIDING_WINDOW (1 + window_size[0]): a query token whose last visible key is p sees the keys
+  // [p - window + 1, p] only (vllm/v1/attention/ops/triton_attention_helpers.py:196-218, vLLM 0.22)
+  int window;
   int num_splits;
   float* part_o;    // [tokens][nq][splits][HS]
   float* part_lse;  // [tokens][nq][splits], log2 units
@@ -176,8 +180,9 @@ struct DecSmem {
   static constexpr int OFF_ZB = OFF_KP + KPS * 128 * 16;   // [KPS][128] u32: paired value zero-point operand biases
   static constexpr int OFF_RP = OFF_ZB + KPS * 128 * 4;    // [2][NR] float2: row scale, row maximum
   static constexpr int OFF_LIM = OFF_RP + 2 * NR * 8;      // [NR] int: last key the row sees
+  static constexpr int OFF_WLO = OFF_LIM + NR * 4;         // [NR] int: first key the row sees (sliding window), or -1
   // [8] value-scale maxima, [NR] O factors, [NR] float2 (row-sum factor, exp-argument shift)
-  static constexpr int OFF_RED = OFF_LIM + NR * 4;
+  static constexpr int OFF_RED = OFF_WLO + NR * 4;
   static constexpr int OFF_SB = (OFF_RED + (8 + NR + 2 * NR) * 4 + 15) / 16 * 16;  // [NR][128] f32 scores
   // the A operand of the zero-point correction MMA: 128 keys x 16 k fp16, K-major without swizzle (the 8-key groups
   // AZ_MGROUP apart, the two 8-k halves AZ_KHALF apart), one buffer per key-operand slot (int4: the key's zero point
@@ -315,7 +320,8 @@ __global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_
 }
 
 // ---------------------------------------------------------------------------------------------------- K1
-template <int FMT, int DT, int HS, int NR, int RL>
+// WIN: the launch applies a sliding window (p.window > 0); the instantiations without one carry none of its code
+template <int FMT, int DT, int HS, int NR, int RL, bool WIN>
 __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const DecodeParams p) {
   using SM = DecSmem<FMT, HS, NR>;
   using CL = Cell<FMT, HS>;
@@ -361,9 +367,13 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
   }
   const int rows = qlen * p.group;
   if (qlen <= 0) return;
+  // with a sliding window the splits share the tiles from the one holding the first token's first key: the later
+  // tokens' windows start at most qlen - 1 <= 31 keys further on, so inside the first two tiles of that range
+  const int win_lo = WIN ? max(0, vis_base - p.window + 1) : 0;
+  const int tile_lo = win_lo / DEC_TILE;
   const int n_tiles = (n + DEC_TILE - 1) / DEC_TILE;
-  const int tps = (n_tiles + p.num_splits - 1) / p.num_splits;
-  const int tile0 = split * tps;
+  const int tps = max(0, (n_tiles - tile_lo + p.num_splits - 1) / p.num_splits);
+  const int tile0 = tile_lo + split * tps;
   const int ntl = max(0, min(tile0 + tps, n_tiles) - tile0);
   if (ntl == 0) {  // empty segment: lse = -inf
     for (int r = tid; r < rows; r += THREADS) {
@@ -735,12 +745,16 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
     float2* rp = reinterpret_cast<float2*>(smem + SM::OFF_RP);  // [2][NR]: row scale, row maximum
     int* lim = reinterpret_cast<int*>(smem + SM::OFF_LIM);
+    int* wlo = reinterpret_cast<int*>(smem + SM::OFF_WLO);
     float* red_vs = reinterpret_cast<float*>(smem + SM::OFF_RED);  // [softmax warps]
     float* frow = red_vs + 8;                                                // [NR]
     float2* adj = reinterpret_cast<float2*>(frow + NR);                      // [NR]
     float* sb = reinterpret_cast<float*>(smem + SM::OFF_SB);                 // [NR][128]
     const float4* kp = reinterpret_cast<const float4*>(smem + SM::OFF_KP);
     const int causal_from = min(n, vis_base + 1);
+    // sliding window: the last token's first key; a tile starting at or before it holds keys below some row's window
+    // (masked path), and a row whose window starts after the split's first tile opens there
+    const int win_hi = WIN ? vis_base + qlen - p.window : -1;
     // query rows (prepared by K0q: programmatic dependent launch, wait for it only now) -> Q^T operand, K-major
     // 128B-swizzled; row constants
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -767,6 +781,7 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
         rp[r] = c;
         rp[NR + r] = c;
         lim[r] = r < rows ? min(n - 1, vis_base + r / p.group) : -1;
+        wlo[r] = (WIN && r < rows) ? vis_base + r / p.group - p.window + 1 : -1;
         frow[r] = 1.f;
       }
       // P^T rows RL .. NR - 1 (whole 8-row groups: RL is a multiple of 8) are read by the MMAs but never written by
@@ -816,22 +831,41 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
         const int tok = (tile0 + i) * DEC_TILE + kl;
         // exp arguments: score (log2 units) minus the row maximum; emax: the largest one
         float emax = -INFINITY;
-        auto logits = [&](auto masked) {
+        bool opening = false;  // a row not opened yet (sliding window) has a key in this tile
+        auto logits = [&](auto masked, auto windowed) {
 #pragma unroll
           for (int r = 0; r < RH; ++r) {
             if (r % 4 == 0 && r > 0) asm volatile("" ::: "memory");  // 4 rows' constants in flight at a time
             const float2 c = rp[mb * NR + R0 + r];  // row scale, row maximum
-            float e = fmaf(s[r] * kv.x, c.x, -c.y);
-            if constexpr (decltype(masked)::value) {
-              if (tok > lim[R0 + r]) e = -INFINITY;  // past the row's last key or the context
+            if constexpr (decltype(windowed)::value) {
+              // a tile holding keys below some row's window start. A row with no key of this split so far (-inf:
+              // sliding window only) takes its scores as they are and sends the tile down the slow path, which opens
+              // it; such a row meets no other tile before it opens (its first key is at most win_hi)
+              const bool fresh = c.y == -INFINITY;
+              float e = fmaf(s[r] * kv.x, c.x, fresh ? 0.f : -c.y);
+              if (tok > lim[R0 + r] || tok < wlo[R0 + r]) e = -INFINITY;  // outside the row's keys or the context
+              opening |= fresh && e != -INFINITY;
+              s[r] = e;
+            } else {
+              float e = fmaf(s[r] * kv.x, c.x, -c.y);
+              if constexpr (decltype(masked)::value) {
+                if (tok > lim[R0 + r]) e = -INFINITY;  // past the row's last key or the context
+              }
+              s[r] = e;
             }
-            s[r] = e;
-            emax = fmaxf(emax, e);
+            emax = fmaxf(emax, s[r]);
           }
         };
-        if ((tile0 + i) * DEC_TILE + DEC_TILE > causal_from) logits(std::true_type{});
-        else logits(std::false_type{});
-        const bool grow = emax > RESCALE_SLACK || kv.z >= v_limit;
+        const int tile_start = (tile0 + i) * DEC_TILE;
+        if constexpr (WIN) {
+          if (tile_start <= win_hi) logits(std::true_type{}, std::true_type{});
+          else if (tile_start + DEC_TILE > causal_from) logits(std::true_type{}, std::false_type{});
+          else logits(std::false_type{}, std::false_type{});
+        } else {
+          if (tile_start + DEC_TILE > causal_from) logits(std::true_type{}, std::false_type{});
+          else logits(std::false_type{}, std::false_type{});
+        }
+        const bool grow = emax > RESCALE_SLACK || kv.z >= v_limit || opening;
         bool rescale = false;
         // every softmax thread takes the same barriers: a wait that ran out is folded into the vote
         if (named_bar_or(BAR_SMX, SMX_THREADS, grow || failed)) {
@@ -864,7 +898,7 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
             const int r = stid;
             float2 c = rp[mb * NR + r];
             float2 ad = make_float2(1.f, 0.f);
-            if (c.y != INFINITY) {  // an open row of the sequence
+            if (c.y != INFINITY) {  // an open row of the sequence, or one not opened yet (-inf)
               float mx = -INFINITY;
               const float4* row = reinterpret_cast<const float4*>(sb + r * 128);
 #pragma unroll 8
@@ -872,14 +906,29 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
                 const float4 v = row[(k + r) & 31];  // rotated start: threads read different banks
                 mx = fmaxf(mx, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
               }
-              const float mt = mx + c.y;  // the tile's largest score
-              float mn = c.y;
-              if (first) mn = mt == -INFINITY ? INFINITY : mt;  // no key in this split: the row is closed
-              else if (mt > c.y + RESCALE_SLACK) mn = mt;
-              if (mn != c.y) {
-                ad.x = first ? 0.f : fast_exp2(c.y - mn);
-                ad.y = c.y - mn;  // -inf for a row that closes
-                c.y = mn;
+              if constexpr (WIN) {
+                const bool fresh = first || c.y == -INFINITY;  // no key of this split seen yet
+                const float cy = c.y == -INFINITY ? 0.f : c.y;  // what the exp arguments were taken against
+                const float mt = mx + cy;                        // the tile's largest score
+                float mn = c.y;
+                // a row without a key so far stays unopened (-inf): its window may start further on
+                if (fresh) mn = mt != -INFINITY ? mt : -INFINITY;
+                else if (mt > c.y + RESCALE_SLACK) mn = mt;
+                if (mn != c.y) {
+                  ad.x = fresh ? 0.f : fast_exp2(c.y - mn);
+                  ad.y = mn == -INFINITY ? -INFINITY : cy - mn;  // -inf: no key yet, P = 0
+                  c.y = mn;
+                }
+              } else {
+                const float mt = mx + c.y;  // the tile's largest score
+                float mn = c.y;
+                if (first) mn = mt == -INFINITY ? INFINITY : mt;  // no key in this split: the row is closed
+                else if (mt > c.y + RESCALE_SLACK) mn = mt;
+                if (mn != c.y) {
+                  ad.x = first ? 0.f : fast_exp2(c.y - mn);
+                  ad.y = c.y - mn;  // -inf for a row that closes
+                  c.y = mn;
+                }
               }
               f = ad.x * o_range;
             }
@@ -1151,7 +1200,7 @@ static int merge_dispatch(const MergeParams& mp, int dtype, int head_size, int64
   }
 }
 
-template <int FMT, int DT, int HS, int RL>
+template <int FMT, int DT, int HS, int RL, bool WIN>
 static int launch_decode_t(const DecodeParams& dp, int grid_z, cudaStream_t st) {
   constexpr int NR = RL <= 16 ? 16 : 32;  // the MMAs' N: a multiple of 16 at M 128
   using SM = DecSmem<FMT, HS, NR>;
@@ -1159,7 +1208,7 @@ static int launch_decode_t(const DecodeParams& dp, int grid_z, cudaStream_t st) 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel<FMT, DT, HS, NR, RL>,
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<FMT, DT, HS, NR, RL, WIN>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES);
     if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode smem attribute: %s", cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
@@ -1176,7 +1225,7 @@ static int launch_decode_t(const DecodeParams& dp, int grid_z, cudaStream_t st) 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<FMT, DT, HS, NR, RL>, dp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<FMT, DT, HS, NR, RL, WIN>, dp);
   if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
   return QP_OK;
 }
@@ -1191,10 +1240,16 @@ static int launch_decode_hs(const DecodeParams& dp, int rows, int grid_z, cudaSt
       const_cast<uint8_t*>(dp.qrec));
   const int rc = check_launch("decode q prep");
   if (rc) return rc;
-  if (rows <= 8) return launch_decode_t<FMT, DT, HS, 8>(dp, grid_z, st);
-  if (rows <= 16) return launch_decode_t<FMT, DT, HS, 16>(dp, grid_z, st);
-  if (rows <= 24) return launch_decode_t<FMT, DT, HS, 24>(dp, grid_z, st);
-  return launch_decode_t<FMT, DT, HS, 32>(dp, grid_z, st);
+  if (dp.window > 0) {
+    if (rows <= 8) return launch_decode_t<FMT, DT, HS, 8, true>(dp, grid_z, st);
+    if (rows <= 16) return launch_decode_t<FMT, DT, HS, 16, true>(dp, grid_z, st);
+    if (rows <= 24) return launch_decode_t<FMT, DT, HS, 24, true>(dp, grid_z, st);
+    return launch_decode_t<FMT, DT, HS, 32, true>(dp, grid_z, st);
+  }
+  if (rows <= 8) return launch_decode_t<FMT, DT, HS, 8, false>(dp, grid_z, st);
+  if (rows <= 16) return launch_decode_t<FMT, DT, HS, 16, false>(dp, grid_z, st);
+  if (rows <= 24) return launch_decode_t<FMT, DT, HS, 24, false>(dp, grid_z, st);
+  return launch_decode_t<FMT, DT, HS, 32, false>(dp, grid_z, st);
 }
 
 template <int FMT>
@@ -1309,8 +1364,8 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
                                int block_size, int64_t block_stride, int64_t head_stride, int64_t slot_stride,
                                int64_t k_off, int64_t ks_off, int64_t v_off, int64_t vs_off, int num_q_heads,
                                int num_kv_heads, int head_size, float softmax_scale, const uint32_t* rht_sign_bits,
-                               int q_rotated, int tokens_after_keys, int out_mode, float* lse_out, int num_splits,
-                               void* workspace, int64_t workspace_bytes, void* stream) {
+                               int q_rotated, int tokens_after_keys, int sliding_window, int out_mode, float* lse_out,
+                               int num_splits, void* workspace, int64_t workspace_bytes, void* stream) {
   int rc = decode_check_cache("decode", fmt, dtype, head_size, cache, block_size, block_stride, head_stride,
                               slot_stride, k_off, ks_off, v_off, vs_off);
   if (rc) return rc;
@@ -1325,6 +1380,7 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
                      group, DEC_MAX_ROWS);
   if (out_mode < 0 || out_mode > 2) return set_error(QP_ERR_INVALID, "decode: out_mode %d", out_mode);
   if (tokens_after_keys < 0) return set_error(QP_ERR_INVALID, "decode: tokens_after_keys %d", tokens_after_keys);
+  if (sliding_window < 0) return set_error(QP_ERR_INVALID, "decode: sliding_window %d", sliding_window);
   if (num_splits <= 0) return set_error(QP_ERR_INVALID, "decode: num_splits %d", num_splits);
   if (num_splits > 1024) return set_error(QP_ERR_UNSUPPORTED, "decode: num_splits %d > 1024", num_splits);
   if (!q || !out || !cu_seqlens_q || !seqused_k || !block_table || !cache || !rht_sign_bits || !workspace)
@@ -1353,7 +1409,11 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
   dp.sign_bits = rht_sign_bits;
   dp.q_rotated = q_rotated;
   dp.num_tokens = num_q_tokens;
-  dp.tokens_after = tokens_after_keys < max_seqlen_q ? tokens_after_keys : max_seqlen_q;  // >= qlen - 1: no mask
+  // a window wider than any context here (2^30 keys) masks nothing
+  const int window = sliding_window >= (1 << 30) ? 0 : sliding_window;
+  // tokens after the keys change the causal mask up to qlen - 1 of them, a window's mask up to qlen + window - 1
+  dp.tokens_after = static_cast<int>(std::min<int64_t>(tokens_after_keys, static_cast<int64_t>(max_seqlen_q) + window));
+  dp.window = window;
   dp.num_splits = num_splits;
   decode_bind_workspace(dp, workspace, head_size);
 
@@ -1498,8 +1558,8 @@ extern "C" int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_st
                                  const void* cache, int block_size, int64_t block_stride, int64_t head_stride,
                                  int64_t slot_stride, int64_t k_off, int64_t ks_off, int64_t v_off, int64_t vs_off,
                                  int num_q_heads, int num_kv_heads, int head_size, float softmax_scale,
-                                 const uint32_t* rht_sign_bits, int q_rotated, int out_mode, float* lse_out,
-                                 void* workspace, int64_t workspace_bytes, void* stream) {
+                                 const uint32_t* rht_sign_bits, int q_rotated, int sliding_window, int out_mode,
+                                 float* lse_out, void* workspace, int64_t workspace_bytes, void* stream) {
   int rc = decode_check_cache("prefill varlen", fmt, dtype, head_size, cache, block_size, block_stride, head_stride,
                               slot_stride, k_off, ks_off, v_off, vs_off);
   if (rc) return rc;
@@ -1509,6 +1569,7 @@ extern "C" int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_st
                      (long long)num_q_tokens, num_q_heads, num_kv_heads);
   if (num_chunks == 0 || num_q_tokens == 0) return QP_OK;
   if (out_mode != 0 && out_mode != 1) return set_error(QP_ERR_INVALID, "prefill varlen: out_mode %d", out_mode);
+  if (sliding_window < 0) return set_error(QP_ERR_INVALID, "prefill varlen: sliding_window %d", sliding_window);
   const int group = num_q_heads / num_kv_heads;
   const int cq = chunk_q_of(group);
   if (!cq) return set_error(QP_ERR_UNSUPPORTED, "prefill varlen: %d query heads per KV head > %d", group, DEC_MAX_ROWS);
@@ -1548,6 +1609,7 @@ extern "C" int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_st
   dp.q_rotated = q_rotated;
   dp.num_tokens = num_q_tokens;
   dp.subseq = table;
+  dp.window = sliding_window >= (1 << 30) ? 0 : sliding_window;
   dp.num_splits = splits;
   decode_bind_workspace(dp, workspace, head_size);
   rc = launch_decode(fmt, dtype, head_size, dp, cq * group, upper, st);
@@ -1823,5 +1885,5 @@ extern "C" int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t
                          num_q_tokens, num_seqs, cu_seqlens_q, seqused_k, max_seqlen_q, block_table,
                          block_table_stride, cache, block_size, block_stride, head_stride, slot_stride, k_off, ks_off,
                          v_off, vs_off, num_q_heads, num_kv_heads, head_size, softmax_scale, rht_sign_bits, q_rotated,
-                         0, out_mode, lse_out, num_splits, scratch, kStaticDecodeScratchBytes, stream);
+                         0, 0, out_mode, lse_out, num_splits, scratch, kStaticDecodeScratchBytes, stream);
 }
