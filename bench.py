@@ -53,7 +53,7 @@ WORKLOADS = {
 CELL = {"int4": HS + 8, "k8v4": HS * 3 // 2 + 8}
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of that workload (profiles/):
 # decode_kernel at c2a, prefill_kernel at c3 (the workloads whose dominant kernel was captured).
-TRAFFIC = {"c2a": 277.01e6 + 6.71e6, "c3": 1700.8e6 + 120.2e6}
+TRAFFIC = {"c2a": 277.01e6 + 7.30e6, "c3": 1700.8e6 + 120.2e6}
 
 
 def algorithmic_bytes(w, seqs=None):
