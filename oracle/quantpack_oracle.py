@@ -254,13 +254,15 @@ def read_sequence(cache, layout, block_row, n):
 # ---------------------------------------------------------------------------------------------------- attention
 
 
-def attention_rht_domain(q_rot, K, V, n, softmax_scale, head_size, sliding_window=0):
+def attention_rht_domain(q_rot, K, V, n, softmax_scale, head_size, sliding_window=0, softcap=0.0):
     """fp64 attention of q_rot (qlen, nq, hs), the last qlen positions of a context of n tokens, over the cached
     K, V (n, nkv, hs) in the RHT domain, scale softmax_scale / head. Returns (out (qlen, nq, hs), lse (qlen, nq)) with
     lse the natural-log log-sum-exp of the scaled scores. `tests/test_int4_kv.py:127-132`. sliding_window > 0 (vLLM's
     SLIDING_WINDOW = 1 + window_size[0]): the query at position p sees only keys k with p - k < sliding_window, the
     stock kernel's mask (vllm/v1/attention/ops/triton_unified_attention.py:533-536 and triton_attention_helpers.py:
-    203-218, vLLM 0.22, whose int4 kernel the reference patches)."""
+    203-218, vLLM 0.22, whose int4 kernel the reference patches). softcap > 0: every scaled score S becomes
+    softcap * tanh(S / softcap) before the mask and the softmax (apply_softcap, triton_attention_helpers.py:28-36,
+    applied at triton_unified_attention.py:513-514)."""
     q_rot = np.asarray(q_rot, dtype=np.float64)
     qlen, nq, hs = q_rot.shape
     nkv = K.shape[1]
@@ -271,6 +273,8 @@ def attention_rht_domain(q_rot, K, V, n, softmax_scale, head_size, sliding_windo
     lse = np.full((qlen, nq), -np.inf)
     for h in range(nq):
         s = q_rot[:, h] @ K[:, h // g].T * (softmax_scale / head_size)
+        if softcap > 0:
+            s = softcap * np.tanh(s / softcap)
         s = np.where(keys[None, :] > pos[:, None], -np.inf, s)
         if sliding_window > 0:
             s = np.where(pos[:, None] - keys[None, :] >= sliding_window, -np.inf, s)
@@ -285,13 +289,13 @@ def attention_rht_domain(q_rot, K, V, n, softmax_scale, head_size, sliding_windo
     return out, lse
 
 
-def attention(q, K, V, n, softmax_scale, signs, dtype="bf16", sliding_window=0):
+def attention(q, K, V, n, softmax_scale, signs, dtype="bf16", sliding_window=0, softcap=0.0):
     """Attention output in the model domain, fp64: RHT(q) -> attention -> inverse RHT / head.
     `tests/test_int4_kv.py:126-133` (q rotated in fp32, output rotated back in fp32 then divided by head)."""
     qf = to_f32(q, dtype)
     hs = qf.shape[-1]
     q_rot = single_rht(qf, signs).astype(np.float64)
-    o, _ = attention_rht_domain(q_rot, K, V, n, softmax_scale, hs, sliding_window)
+    o, _ = attention_rht_domain(q_rot, K, V, n, softmax_scale, hs, sliding_window, softcap)
     return single_rht(o.astype(F32), signs, inverse=True).astype(np.float64) / hs
 
 
@@ -397,7 +401,8 @@ def read_range(cache, layout, block_row, start, end):
     return K, dequant_int4(vraw, vw)
 
 
-def attention_from_cache(q_rot, cache, layout, block_row, n, softmax_scale, chunk=16384, sliding_window=0):
+def attention_from_cache(q_rot, cache, layout, block_row, n, softmax_scale, chunk=16384, sliding_window=0,
+                         softcap=0.0):
     """attention_rht_domain over the cached context of one sequence, streamed in chunks of keys and folded by
     log-sum-exp (memory bounded for long contexts). Returns (out, natural-log lse)."""
     hs = layout.head_size
@@ -408,7 +413,7 @@ def attention_from_cache(q_rot, cache, layout, block_row, n, softmax_scale, chun
     for start in range(first, max(n, 1), chunk):
         end = min(n, start + chunk)
         K, V = read_range(cache, layout, block_row, start, end)
-        o, l = attention_rht_domain(q_rot, K, V, n - start, softmax_scale, hs, sliding_window)
+        o, l = attention_rht_domain(q_rot, K, V, n - start, softmax_scale, hs, sliding_window, softcap)
         outs.append(o)
         lses.append(l)
     return merge_partials(np.stack(outs), np.stack(lses))

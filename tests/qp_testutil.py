@@ -111,7 +111,8 @@ def make_queries(qlens, seed=5, nq=NQ, hs=HS, dtype="bf16"):
     return qo.from_f32(q, dtype)
 
 
-def decode(cache, q_bits, qlens, lens, table, dtype="bf16", num_splits=None, device="cuda", sliding_window=0):
+def decode(cache, q_bits, qlens, lens, table, dtype="bf16", num_splits=None, device="cuda", sliding_window=0,
+           softcap=0.0):
     """Run the B200 split-KV decode; returns the output as float32 numpy (tokens, nq, hs)."""
     kc, vc, ks, vs = cache.views
     q = to_torch(q_bits, device, dtype)
@@ -120,12 +121,13 @@ def decode(cache, q_bits, qlens, lens, table, dtype="bf16", num_splits=None, dev
     ops.paged_decode(q, kc, vc, out, cu_seqlens_q=cu, max_seqlen_q=max(qlens),
                      seqused_k=torch.tensor(lens, dtype=torch.int32, device=device), max_seqlen_k=max(lens),
                      softmax_scale=cache.hs ** -0.5, block_table=torch.from_numpy(table).to(device),
-                     k_scale_cache=ks, v_scale_cache=vs, num_splits=num_splits, sliding_window=sliding_window)
+                     k_scale_cache=ks, v_scale_cache=vs, num_splits=num_splits, sliding_window=sliding_window,
+                     softcap=softcap)
     torch.cuda.synchronize()
     return out.float().cpu().numpy()
 
 
-def reference(cache_bytes, layout, q_bits, qlens, lens, table, dtype="bf16", sliding_window=0):
+def reference(cache_bytes, layout, q_bits, qlens, lens, table, dtype="bf16", sliding_window=0, softcap=0.0):
     """fp64 oracle output (tokens, nq, hs) in the model domain, per sequence, from the cache bytes."""
     hs = layout.head_size
     sg = signs(hs)
@@ -135,7 +137,7 @@ def reference(cache_bytes, layout, q_bits, qlens, lens, table, dtype="bf16", sli
         qf = qo.to_f32(q_bits[at:at + ql], dtype)
         q_rot = qo.single_rht(qf, sg).astype(np.float64)
         o, _ = qo.attention_from_cache(q_rot, cache_bytes, layout, table[i], n, hs ** -0.5,
-                                       sliding_window=sliding_window)
+                                       sliding_window=sliding_window, softcap=softcap)
         outs.append(qo.single_rht(o.astype(np.float32), sg, inverse=True).astype(np.float64) / hs)
         at += ql
     return np.concatenate(outs)

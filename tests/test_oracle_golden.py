@@ -178,3 +178,22 @@ def test_streamed_oracle_skips_only_chunks_outside_every_window(window):
     want, wl = qo.attention_rht_domain(q, K, V, n, hs ** -0.5, hs, window)
     np.testing.assert_allclose(got, want, rtol=1e-10, atol=1e-12)
     np.testing.assert_allclose(gl, wl, rtol=1e-10)
+
+
+@pytest.mark.parametrize("softcap", [3.0, 50.0])
+def test_softcap_is_tanh_of_the_scaled_score(softcap):
+    """vLLM's apply_softcap: softcap * tanh(S / softcap) on the scaled score, before the softmax; restated here as an
+    explicit softmax over the capped scores."""
+    rng = np.random.default_rng(8)
+    n, qlen, nq, nkv, hs = 200, 2, 2, 1, 16
+    K = rng.standard_normal((n, nkv, hs)) * 3
+    V = rng.standard_normal((n, nkv, hs))
+    q = rng.standard_normal((qlen, nq, hs)) * 3
+    got, _ = qo.attention_rht_domain(q, K, V, n, hs ** -0.5, hs, 0, softcap)
+    for i in range(qlen):
+        p = n - qlen + i
+        for h in range(nq):
+            s = K[:p + 1, 0] @ q[i, h] * (hs ** -0.5 / hs)
+            s = softcap * np.tanh(s / softcap)
+            w = np.exp(s - s.max())
+            np.testing.assert_allclose(got[i, h], w @ V[:p + 1, 0] / w.sum(), rtol=1e-12, atol=1e-12)

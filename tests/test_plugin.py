@@ -308,7 +308,7 @@ def test_unsupported_features_go_to_the_stock_path(monkeypatch):
     stock, stock_calls = _stock_recorder()
     fn = int4_kv.make_unified_attention(stock)
     q, kc, out, args = _step([4], [5000])
-    fn(q, kc, kc, out, **dict(args, softcap=30.0))
+    fn(q, kc, kc, out, **dict(args, alibi_slopes=torch.zeros(NQ)))
     assert not rec.calls and len(stock_calls) == 1
     fn(q, kc, kc, out, **dict(args, sinks=torch.zeros(NQ)))
     assert not rec.calls and len(stock_calls) == 2
@@ -338,6 +338,20 @@ def test_sliding_window_layers_run_on_the_split_kv_kernel(monkeypatch):
     assert ("prefill", 256, 40000) in rec.calls and len(rec.calls) == 3
     assert int4_kv.sliding_window_of((-1, -1)) == 0 and int4_kv.sliding_window_of(None) == 0
     assert int4_kv.sliding_window_of((0, 0)) == 1
+
+
+def test_softcap_layers_run_on_the_split_kv_kernel(monkeypatch):
+    """A logit softcap (Gemma-2-style layers) is applied by the split-KV kernel: decodes carry it, and every chunk of
+    the step (the long one too: the prefill kernel has no softcap) goes to the varlen launch."""
+    rec = Recorder(monkeypatch)
+    stock, stock_calls = _stock_recorder()
+    fn = int4_kv.make_unified_attention(stock)
+    seen = []
+    monkeypatch.setattr(ops, "paged_decode", lambda *a, **kw: seen.append(("decode", kw["softcap"])))
+    monkeypatch.setattr(ops, "prefill_varlen", lambda *a, **kw: seen.append(("varlen", kw["softcap"])))
+    q, kc, out, args = _step([256, 2, 40], [40000, 20000, 300], window=(4095, 0))
+    fn(q, kc, kc, out, **dict(args, softcap=50.0))
+    assert sorted(seen) == [("decode", 50.0), ("varlen", 50.0)] and not rec.calls and not stock_calls
 
 
 def test_head_512_is_served_and_other_head_sizes_go_stock(monkeypatch):
@@ -521,7 +535,7 @@ def test_k8v4_call_outside_the_kernels_raises(monkeypatch):
     with pytest.raises(NotImplementedError, match="k8v4"):
         fn(q, kc8, kc8, out, **dict(args, sinks=torch.zeros(NQ)))
     with pytest.raises(NotImplementedError, match="k8v4"):
-        fn(q, kc8, kc8, out, **dict(args, softcap=30.0))
+        fn(q, kc8, kc8, out, **dict(args, alibi_slopes=torch.zeros(NQ)))
     fn2 = int4_kv.make_unified_attention(stock, prefill_on=False)
     q, _, out, args = _step([256], [40000])
     with pytest.raises(NotImplementedError, match="k8v4"):

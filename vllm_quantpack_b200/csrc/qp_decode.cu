@@ -117,6 +117,9 @@ struct DecodeParams {
   // window > 0: vLLM's SLIDING_WINDOW (1 + window_size[0]): a query token whose last visible key is p sees the keys
   // [p - window + 1, p] only (vllm/v1/attention/ops/triton_attention_helpers.py:196-218, vLLM 0.22)
   int window;
+  // softcap > 0: every score S (natural units) becomes softcap x tanh(S / softcap) before the softmax, vLLM's
+  // apply_softcap (vllm/v1/attention/ops/triton_attention_helpers.py:28-36, triton_unified_attention.py:513-514)
+  float softcap;
   int num_splits;
   float* part_o;    // [tokens][nq][splits][HS]
   float* part_lse;  // [tokens][nq][splits], log2 units
@@ -245,6 +248,15 @@ __device__ __forceinline__ void tmem_st_rows(uint32_t taddr, const float (&v)[NR
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// capl x tanh(t / capl) for a score t in log2 units (capl = softcap x log2 e, cap_k = 2 log2 e / capl), from
+// tanh(y) = 1 - 2 / (e^{2y} + 1) taken on |y| and given t's sign: absolute error ~1e-7 x capl, which is what a softmax
+// argument needs (no cancellation matters once it is multiplied back by capl); e^{2|y|} = 2^{|t| cap_k}, its exponent
+// held below 64 so the quotient stays finite.
+__device__ __forceinline__ float softcap_log2(float t, float capl, float cap_k) {
+  const float a = fast_exp2(fminf(fabsf(t) * cap_k, 64.f));
+  return copysignf(capl * (1.f - __fdividef(2.f, a + 1.f)), t);
+}
+
 // k index (0..HS-1) of the QK operand that carries channel c. int4: column j = 4 w + m of a key's TMEM lane holds
 // the pair lop3'd from word w (shifted right 8 for m >= 2; low nibbles for even m, high for odd), i.e. channels
 // 8 w + m (low half) and 8 w + m + 4 (high half); k8v4: the natural order (prmt takes bytes 0, 1 then 2, 3).
@@ -320,8 +332,9 @@ __global__ void __launch_bounds__(256) decode_qprep_kernel(const void* q, int64_
 }
 
 // ---------------------------------------------------------------------------------------------------- K1
-// WIN: the launch applies a sliding window (p.window > 0); the instantiations without one carry none of its code
-template <int FMT, int DT, int HS, int NR, int RL, bool WIN>
+// FEAT: the launch applies a sliding window (p.window > 0) and / or a logit softcap (p.softcap > 0); the
+// instantiations without FEAT carry none of their code
+template <int FMT, int DT, int HS, int NR, int RL, bool FEAT>
 __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const DecodeParams p) {
   using SM = DecSmem<FMT, HS, NR>;
   using CL = Cell<FMT, HS>;
@@ -369,7 +382,7 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
   if (qlen <= 0) return;
   // with a sliding window the splits share the tiles from the one holding the first token's first key: the later
   // tokens' windows start at most qlen - 1 <= 31 keys further on, so inside the first two tiles of that range
-  const int win_lo = WIN ? max(0, vis_base - p.window + 1) : 0;
+  const int win_lo = (FEAT && p.window > 0) ? max(0, vis_base - p.window + 1) : 0;
   const int tile_lo = win_lo / DEC_TILE;
   const int n_tiles = (n + DEC_TILE - 1) / DEC_TILE;
   const int tps = max(0, (n_tiles - tile_lo + p.num_splits - 1) / p.num_splits);
@@ -754,7 +767,10 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
     const int causal_from = min(n, vis_base + 1);
     // sliding window: the last token's first key; a tile starting at or before it holds keys below some row's window
     // (masked path), and a row whose window starts after the split's first tile opens there
-    const int win_hi = WIN ? vis_base + qlen - p.window : -1;
+    const int win_hi = (FEAT && p.window > 0) ? vis_base + qlen - p.window : -1;
+    // softcap in log2 units (the scores here are log2 e x the natural ones) and the factor of its exponential
+    const float capl = FEAT ? p.softcap * LOG2E : 0.f;
+    const float cap_k = capl > 0.f ? 2.f * LOG2E / capl : 0.f;
     // query rows (prepared by K0q: programmatic dependent launch, wait for it only now) -> Q^T operand, K-major
     // 128B-swizzled; row constants
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -781,7 +797,7 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
         rp[r] = c;
         rp[NR + r] = c;
         lim[r] = r < rows ? min(n - 1, vis_base + r / p.group) : -1;
-        wlo[r] = (WIN && r < rows) ? vis_base + r / p.group - p.window + 1 : -1;
+        wlo[r] = (FEAT && p.window > 0 && r < rows) ? vis_base + r / p.group - p.window + 1 : -1;
         frow[r] = 1.f;
       }
       // P^T rows RL .. NR - 1 (whole 8-row groups: RL is a multiple of 8) are read by the MMAs but never written by
@@ -837,13 +853,18 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
           for (int r = 0; r < RH; ++r) {
             if (r % 4 == 0 && r > 0) asm volatile("" ::: "memory");  // 4 rows' constants in flight at a time
             const float2 c = rp[mb * NR + R0 + r];  // row scale, row maximum
-            if constexpr (decltype(windowed)::value) {
-              // a tile holding keys below some row's window start. A row with no key of this split so far (-inf:
-              // sliding window only) takes its scores as they are and sends the tile down the slow path, which opens
-              // it; such a row meets no other tile before it opens (its first key is at most win_hi)
+            if constexpr (FEAT) {
+              // A row with no key of this split so far (-inf: FEAT only) takes its scores as they are and sends the
+              // tile down the slow path, which opens it; with a window, such a row meets no tile but masked ones
+              // before it opens (its first key is at most win_hi), without one it never gets a key (causality).
               const bool fresh = c.y == -INFINITY;
-              float e = fmaf(s[r] * kv.x, c.x, fresh ? 0.f : -c.y);
-              if (tok > lim[R0 + r] || tok < wlo[R0 + r]) e = -INFINITY;  // outside the row's keys or the context
+              float t = s[r] * kv.x * c.x;  // the score, log2 units
+              if (capl > 0.f) t = softcap_log2(t, capl, cap_k);
+              float e = t - (fresh ? 0.f : c.y);
+              if constexpr (decltype(masked)::value) {
+                // outside the row's keys (its window, when the tile reaches below one) or past the context
+                if (tok > lim[R0 + r] || (decltype(windowed)::value && tok < wlo[R0 + r])) e = -INFINITY;
+              }
               opening |= fresh && e != -INFINITY;
               s[r] = e;
             } else {
@@ -857,7 +878,7 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
           }
         };
         const int tile_start = (tile0 + i) * DEC_TILE;
-        if constexpr (WIN) {
+        if constexpr (FEAT) {
           if (tile_start <= win_hi) logits(std::true_type{}, std::true_type{});
           else if (tile_start + DEC_TILE > causal_from) logits(std::true_type{}, std::false_type{});
           else logits(std::false_type{}, std::false_type{});
@@ -906,17 +927,18 @@ __global__ void __maxnreg__((DecWarps<HS, RL>::REGS)) decode_kernel(const Decode
                 const float4 v = row[(k + r) & 31];  // rotated start: threads read different banks
                 mx = fmaxf(mx, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
               }
-              if constexpr (WIN) {
+              if constexpr (FEAT) {
                 const bool fresh = first || c.y == -INFINITY;  // no key of this split seen yet
                 const float cy = c.y == -INFINITY ? 0.f : c.y;  // what the exp arguments were taken against
                 const float mt = mx + cy;                        // the tile's largest score
                 float mn = c.y;
-                // a row without a key so far stays unopened (-inf): its window may start further on
-                if (fresh) mn = mt != -INFINITY ? mt : -INFINITY;
+                // a row without a key so far stays unopened (-inf) when a window may start its keys further on,
+                // and is closed otherwise (its keys are a prefix of the context)
+                if (fresh) mn = mt != -INFINITY ? mt : (p.window > 0 ? -INFINITY : INFINITY);
                 else if (mt > c.y + RESCALE_SLACK) mn = mt;
                 if (mn != c.y) {
                   ad.x = fresh ? 0.f : fast_exp2(c.y - mn);
-                  ad.y = mn == -INFINITY ? -INFINITY : cy - mn;  // -inf: no key yet, P = 0
+                  ad.y = (mn == -INFINITY || mn == INFINITY) ? -INFINITY : cy - mn;  // -inf: no key, P = 0
                   c.y = mn;
                 }
               } else {
@@ -1200,7 +1222,7 @@ static int merge_dispatch(const MergeParams& mp, int dtype, int head_size, int64
   }
 }
 
-template <int FMT, int DT, int HS, int RL, bool WIN>
+template <int FMT, int DT, int HS, int RL, bool FEAT>
 static int launch_decode_t(const DecodeParams& dp, int grid_z, cudaStream_t st) {
   constexpr int NR = RL <= 16 ? 16 : 32;  // the MMAs' N: a multiple of 16 at M 128
   using SM = DecSmem<FMT, HS, NR>;
@@ -1208,7 +1230,7 @@ static int launch_decode_t(const DecodeParams& dp, int grid_z, cudaStream_t st) 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel<FMT, DT, HS, NR, RL, WIN>,
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<FMT, DT, HS, NR, RL, FEAT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES);
     if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode smem attribute: %s", cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
@@ -1225,7 +1247,7 @@ static int launch_decode_t(const DecodeParams& dp, int grid_z, cudaStream_t st) 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<FMT, DT, HS, NR, RL, WIN>, dp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<FMT, DT, HS, NR, RL, FEAT>, dp);
   if (e != cudaSuccess) return set_error(QP_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
   return QP_OK;
 }
@@ -1240,7 +1262,7 @@ static int launch_decode_hs(const DecodeParams& dp, int rows, int grid_z, cudaSt
       const_cast<uint8_t*>(dp.qrec));
   const int rc = check_launch("decode q prep");
   if (rc) return rc;
-  if (dp.window > 0) {
+  if (dp.window > 0 || dp.softcap > 0.f) {
     if (rows <= 8) return launch_decode_t<FMT, DT, HS, 8, true>(dp, grid_z, st);
     if (rows <= 16) return launch_decode_t<FMT, DT, HS, 16, true>(dp, grid_z, st);
     if (rows <= 24) return launch_decode_t<FMT, DT, HS, 24, true>(dp, grid_z, st);
@@ -1364,8 +1386,9 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
                                int block_size, int64_t block_stride, int64_t head_stride, int64_t slot_stride,
                                int64_t k_off, int64_t ks_off, int64_t v_off, int64_t vs_off, int num_q_heads,
                                int num_kv_heads, int head_size, float softmax_scale, const uint32_t* rht_sign_bits,
-                               int q_rotated, int tokens_after_keys, int sliding_window, int out_mode, float* lse_out,
-                               int num_splits, void* workspace, int64_t workspace_bytes, void* stream) {
+                               int q_rotated, int tokens_after_keys, int sliding_window, float softcap, int out_mode,
+                               float* lse_out, int num_splits, void* workspace, int64_t workspace_bytes,
+                               void* stream) {
   int rc = decode_check_cache("decode", fmt, dtype, head_size, cache, block_size, block_stride, head_stride,
                               slot_stride, k_off, ks_off, v_off, vs_off);
   if (rc) return rc;
@@ -1381,6 +1404,7 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
   if (out_mode < 0 || out_mode > 2) return set_error(QP_ERR_INVALID, "decode: out_mode %d", out_mode);
   if (tokens_after_keys < 0) return set_error(QP_ERR_INVALID, "decode: tokens_after_keys %d", tokens_after_keys);
   if (sliding_window < 0) return set_error(QP_ERR_INVALID, "decode: sliding_window %d", sliding_window);
+  if (!(softcap >= 0.f) || isinf(softcap)) return set_error(QP_ERR_INVALID, "decode: softcap %g", softcap);
   if (num_splits <= 0) return set_error(QP_ERR_INVALID, "decode: num_splits %d", num_splits);
   if (num_splits > 1024) return set_error(QP_ERR_UNSUPPORTED, "decode: num_splits %d > 1024", num_splits);
   if (!q || !out || !cu_seqlens_q || !seqused_k || !block_table || !cache || !rht_sign_bits || !workspace)
@@ -1414,6 +1438,7 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
   // tokens after the keys change the causal mask up to qlen - 1 of them, a window's mask up to qlen + window - 1
   dp.tokens_after = static_cast<int>(std::min<int64_t>(tokens_after_keys, static_cast<int64_t>(max_seqlen_q) + window));
   dp.window = window;
+  dp.softcap = softcap;
   dp.num_splits = num_splits;
   decode_bind_workspace(dp, workspace, head_size);
 
@@ -1558,8 +1583,9 @@ extern "C" int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_st
                                  const void* cache, int block_size, int64_t block_stride, int64_t head_stride,
                                  int64_t slot_stride, int64_t k_off, int64_t ks_off, int64_t v_off, int64_t vs_off,
                                  int num_q_heads, int num_kv_heads, int head_size, float softmax_scale,
-                                 const uint32_t* rht_sign_bits, int q_rotated, int sliding_window, int out_mode,
-                                 float* lse_out, void* workspace, int64_t workspace_bytes, void* stream) {
+                                 const uint32_t* rht_sign_bits, int q_rotated, int sliding_window, float softcap,
+                                 int out_mode, float* lse_out, void* workspace, int64_t workspace_bytes,
+                                 void* stream) {
   int rc = decode_check_cache("prefill varlen", fmt, dtype, head_size, cache, block_size, block_stride, head_stride,
                               slot_stride, k_off, ks_off, v_off, vs_off);
   if (rc) return rc;
@@ -1570,6 +1596,7 @@ extern "C" int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_st
   if (num_chunks == 0 || num_q_tokens == 0) return QP_OK;
   if (out_mode != 0 && out_mode != 1) return set_error(QP_ERR_INVALID, "prefill varlen: out_mode %d", out_mode);
   if (sliding_window < 0) return set_error(QP_ERR_INVALID, "prefill varlen: sliding_window %d", sliding_window);
+  if (!(softcap >= 0.f) || isinf(softcap)) return set_error(QP_ERR_INVALID, "prefill varlen: softcap %g", softcap);
   const int group = num_q_heads / num_kv_heads;
   const int cq = chunk_q_of(group);
   if (!cq) return set_error(QP_ERR_UNSUPPORTED, "prefill varlen: %d query heads per KV head > %d", group, DEC_MAX_ROWS);
@@ -1610,6 +1637,7 @@ extern "C" int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_st
   dp.num_tokens = num_q_tokens;
   dp.subseq = table;
   dp.window = sliding_window >= (1 << 30) ? 0 : sliding_window;
+  dp.softcap = softcap;
   dp.num_splits = splits;
   decode_bind_workspace(dp, workspace, head_size);
   rc = launch_decode(fmt, dtype, head_size, dp, cq * group, upper, st);
@@ -1885,5 +1913,5 @@ extern "C" int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t
                          num_q_tokens, num_seqs, cu_seqlens_q, seqused_k, max_seqlen_q, block_table,
                          block_table_stride, cache, block_size, block_stride, head_stride, slot_stride, k_off, ks_off,
                          v_off, vs_off, num_q_heads, num_kv_heads, head_size, softmax_scale, rht_sign_bits, q_rotated,
-                         0, 0, out_mode, lse_out, num_splits, scratch, kStaticDecodeScratchBytes, stream);
+                         0, 0, 0.f, out_mode, lse_out, num_splits, scratch, kStaticDecodeScratchBytes, stream);
 }
