@@ -103,6 +103,9 @@ int64_t qp_decode_workspace_bytes(int64_t num_q_tokens, int num_q_heads, int hea
  * softcap: vLLM's logit softcap (0 = none): every score S = softmax_scale / head_size x q.k becomes
  * softcap x tanh(S / softcap) before the softmax (vllm/v1/attention/ops/triton_attention_helpers.py:28-36,
  * triton_unified_attention.py:513-514, vLLM 0.22).
+ * sinks: null, or num_q_heads fp32 sink logits (natural units, out_mode 0 only): exp(sink) joins every row's softmax
+ * denominator once, as vLLM's attention sinks (triton_attention_helpers.py:108-138: the row maximum starts at the
+ * sink with sum 1, in one segment only).
  * out_mode 0: out in dtype, model domain. out_mode 1: out fp32 in the RHT domain and lse_out (tokens, num_q_heads)
  * the base-2 log-sum-exp of the scaled scores (the partial a sequence-parallel rank exchanges). out_mode 2: the
  * split partials only, left in the workspace as part_o (tokens, num_q_heads, num_splits, head_size) fp32 followed by
@@ -118,8 +121,8 @@ int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stride_token, i
                     int64_t block_stride, int64_t head_stride, int64_t slot_stride, int64_t k_off, int64_t ks_off,
                     int64_t v_off, int64_t vs_off, int num_q_heads, int num_kv_heads, int head_size,
                     float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated, int tokens_after_keys,
-                    int sliding_window, float softcap, int out_mode, float* lse_out, int num_splits,
-                    void* workspace, int64_t workspace_bytes, void* stream);
+                    int sliding_window, float softcap, const float* sinks, int out_mode, float* lse_out,
+                    int num_splits, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Bytes of workspace qp_prefill needs for a chunk of qlen queries over a context of n tokens (prepared query tiles
  * and per-piece partials). */
@@ -154,7 +157,7 @@ int64_t qp_prefill_varlen_workspace_bytes(int64_t num_q_tokens, int num_chunks, 
  * the call never reads back to the host. max_seqlen_k bounds the keys any query token sees (seqused_k, or with a
  * sliding window min(seqused_k, sliding_window + 158)); it sizes the split count and the workspace. The chunks run
  * on the split-KV decode kernel as sub-sequences of 32 / (query heads per KV head) tokens. out / out_mode / lse_out /
- * q_rotated / sliding_window / softcap as in qp_paged_decode (out_mode 0 or 1); head_size 256 or 512; HND cells,
+ * q_rotated / sliding_window / softcap / sinks as in qp_paged_decode (out_mode 0 or 1); head_size 256 or 512; HND cells,
  * block_size % 16 == 0.
  * Replaces the Triton 2D sub-batch that the plugin runs for every chunk that is not long (int4_kv.py:113-119,
  * 313-323). */
@@ -165,8 +168,8 @@ int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_stride_token,
                       int64_t block_stride, int64_t head_stride, int64_t slot_stride, int64_t k_off, int64_t ks_off,
                       int64_t v_off, int64_t vs_off, int num_q_heads, int num_kv_heads, int head_size,
                       float softmax_scale, const uint32_t* rht_sign_bits, int q_rotated, int sliding_window,
-                      float softcap, int out_mode, float* lse_out, void* workspace, int64_t workspace_bytes,
-                      void* stream);
+                      float softcap, const float* sinks, int out_mode, float* lse_out, void* workspace,
+                      int64_t workspace_bytes, void* stream);
 
 /* Bytes of the library's static decode scratch used by qp_paged_decode_static. */
 #define QP_STATIC_DECODE_SCRATCH_BYTES (32ll << 20)
@@ -179,8 +182,8 @@ int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_stride_token,
  * the array and it keeps the last call's contents (nothing in it needs to start at zero); calls that overlap on the
  * GPU race on it, so serialize them. The array holds the split partials and the prepared query rows. Only out_mode 0
  * and 1 are served (QP_ERR_INVALID for 2: the partials would stay where no caller can reach them), and the keys are
- * taken as the sequence's last ones (tokens_after_keys 0) with no sliding window or softcap: a single-GPU decode,
- * not a rank of a sequence split.
+ * taken as the sequence's last ones (tokens_after_keys 0) with no sliding window, softcap or sinks: a single-GPU
+ * decode, not a rank of a sequence split.
  * Allocates nothing. No counterpart in the reference. */
 int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t q_stride_token, int64_t q_stride_head,
                            void* out, int64_t out_stride_token, int64_t out_stride_head, int64_t num_q_tokens,

@@ -254,7 +254,7 @@ def read_sequence(cache, layout, block_row, n):
 # ---------------------------------------------------------------------------------------------------- attention
 
 
-def attention_rht_domain(q_rot, K, V, n, softmax_scale, head_size, sliding_window=0, softcap=0.0):
+def attention_rht_domain(q_rot, K, V, n, softmax_scale, head_size, sliding_window=0, softcap=0.0, sinks=None):
     """fp64 attention of q_rot (qlen, nq, hs), the last qlen positions of a context of n tokens, over the cached
     K, V (n, nkv, hs) in the RHT domain, scale softmax_scale / head. Returns (out (qlen, nq, hs), lse (qlen, nq)) with
     lse the natural-log log-sum-exp of the scaled scores. `tests/test_int4_kv.py:127-132`. sliding_window > 0 (vLLM's
@@ -262,7 +262,7 @@ def attention_rht_domain(q_rot, K, V, n, softmax_scale, head_size, sliding_windo
     stock kernel's mask (vllm/v1/attention/ops/triton_unified_attention.py:533-536 and triton_attention_helpers.py:
     203-218, vLLM 0.22, whose int4 kernel the reference patches). softcap > 0: every scaled score S becomes
     softcap * tanh(S / softcap) before the mask and the softmax (apply_softcap, triton_attention_helpers.py:28-36,
-    applied at triton_unified_attention.py:513-514)."""
+    applied at triton_unified_attention.py:513-514). sinks (nq,): see apply_sinks."""
     q_rot = np.asarray(q_rot, dtype=np.float64)
     qlen, nq, hs = q_rot.shape
     nkv = K.shape[1]
@@ -286,16 +286,29 @@ def attention_rht_domain(q_rot, K, V, n, softmax_scale, head_size, sliding_windo
         safe = np.where(l > 0, l, 1.0)
         out[:, h] = np.where(ok[:, None], (p @ V[:, h // g]) / safe[:, None], 0.0)
         lse[:, h] = np.where(ok, m[:, 0] + np.log(safe), -np.inf)
-    return out, lse
+    return apply_sinks(out, lse, sinks)
 
 
-def attention(q, K, V, n, softmax_scale, signs, dtype="bf16", sliding_window=0, softcap=0.0):
+def apply_sinks(out, lse, sinks):
+    """Attention sinks: per query head a logit (natural units) whose exp joins the softmax denominator of every row
+    once and adds nothing to the numerator (vLLM: the row maximum starts at the sink with sum 1,
+    vllm/v1/attention/ops/triton_attention_helpers.py:108-138, triton_unified_attention.py:356-359). Takes the
+    attention over the keys, out (..., nq, hs) with natural-log lse (..., nq); returns both with the sink folded."""
+    if sinks is None:
+        return out, lse
+    s = np.asarray(sinks, dtype=np.float64)
+    tot = np.logaddexp(lse, s)
+    w = np.where(np.isfinite(lse), np.exp(lse - tot), 0.0)
+    return out * w[..., None], tot
+
+
+def attention(q, K, V, n, softmax_scale, signs, dtype="bf16", sliding_window=0, softcap=0.0, sinks=None):
     """Attention output in the model domain, fp64: RHT(q) -> attention -> inverse RHT / head.
     `tests/test_int4_kv.py:126-133` (q rotated in fp32, output rotated back in fp32 then divided by head)."""
     qf = to_f32(q, dtype)
     hs = qf.shape[-1]
     q_rot = single_rht(qf, signs).astype(np.float64)
-    o, _ = attention_rht_domain(q_rot, K, V, n, softmax_scale, hs, sliding_window, softcap)
+    o, _ = attention_rht_domain(q_rot, K, V, n, softmax_scale, hs, sliding_window, softcap, sinks)
     return single_rht(o.astype(F32), signs, inverse=True).astype(np.float64) / hs
 
 
@@ -402,7 +415,7 @@ def read_range(cache, layout, block_row, start, end):
 
 
 def attention_from_cache(q_rot, cache, layout, block_row, n, softmax_scale, chunk=16384, sliding_window=0,
-                         softcap=0.0):
+                         softcap=0.0, sinks=None):
     """attention_rht_domain over the cached context of one sequence, streamed in chunks of keys and folded by
     log-sum-exp (memory bounded for long contexts). Returns (out, natural-log lse)."""
     hs = layout.head_size
@@ -416,4 +429,5 @@ def attention_from_cache(q_rot, cache, layout, block_row, n, softmax_scale, chun
         o, l = attention_rht_domain(q_rot, K, V, n - start, softmax_scale, hs, sliding_window, softcap)
         outs.append(o)
         lses.append(l)
-    return merge_partials(np.stack(outs), np.stack(lses))
+    o, l = merge_partials(np.stack(outs), np.stack(lses))
+    return apply_sinks(o, l, sinks)  # once, after the chunks are folded

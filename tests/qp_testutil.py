@@ -112,7 +112,7 @@ def make_queries(qlens, seed=5, nq=NQ, hs=HS, dtype="bf16"):
 
 
 def decode(cache, q_bits, qlens, lens, table, dtype="bf16", num_splits=None, device="cuda", sliding_window=0,
-           softcap=0.0):
+           softcap=0.0, sinks=None):
     """Run the B200 split-KV decode; returns the output as float32 numpy (tokens, nq, hs)."""
     kc, vc, ks, vs = cache.views
     q = to_torch(q_bits, device, dtype)
@@ -122,12 +122,13 @@ def decode(cache, q_bits, qlens, lens, table, dtype="bf16", num_splits=None, dev
                      seqused_k=torch.tensor(lens, dtype=torch.int32, device=device), max_seqlen_k=max(lens),
                      softmax_scale=cache.hs ** -0.5, block_table=torch.from_numpy(table).to(device),
                      k_scale_cache=ks, v_scale_cache=vs, num_splits=num_splits, sliding_window=sliding_window,
-                     softcap=softcap)
+                     softcap=softcap, sinks=None if sinks is None else torch.tensor(sinks, device=device))
     torch.cuda.synchronize()
     return out.float().cpu().numpy()
 
 
-def reference(cache_bytes, layout, q_bits, qlens, lens, table, dtype="bf16", sliding_window=0, softcap=0.0):
+def reference(cache_bytes, layout, q_bits, qlens, lens, table, dtype="bf16", sliding_window=0, softcap=0.0,
+              sinks=None):
     """fp64 oracle output (tokens, nq, hs) in the model domain, per sequence, from the cache bytes."""
     hs = layout.head_size
     sg = signs(hs)
@@ -137,7 +138,7 @@ def reference(cache_bytes, layout, q_bits, qlens, lens, table, dtype="bf16", sli
         qf = qo.to_f32(q_bits[at:at + ql], dtype)
         q_rot = qo.single_rht(qf, sg).astype(np.float64)
         o, _ = qo.attention_from_cache(q_rot, cache_bytes, layout, table[i], n, hs ** -0.5,
-                                       sliding_window=sliding_window, softcap=softcap)
+                                       sliding_window=sliding_window, softcap=softcap, sinks=sinks)
         outs.append(qo.single_rht(o.astype(np.float32), sg, inverse=True).astype(np.float64) / hs)
         at += ql
     return np.concatenate(outs)

@@ -53,6 +53,6 @@ def test_host_side_calls_without_a_gpu(lib):
     assert lib.qp_decode_workspace_bytes(4, 24, 256, 74) >= 4 * 24 * 74 * 257 * 4
     # argument checks fail before any device work
     rc = lib.qp_paged_decode(0, 0, None, 0, 0, None, 0, 0, 4, 1, None, None, 9, None, 0, None, 16, 0, 0, 264, 0,
-                             128, 132, 260, 24, 4, 256, ctypes.c_float(0.0625), None, 0, 0, 0, ctypes.c_float(0.0), 0,
-                             None, 1, None, 0, None)
+                             128, 132, 260, 24, 4, 256, ctypes.c_float(0.0625), None, 0, 0, 0, ctypes.c_float(0.0),
+                             None, 0, None, 1, None, 0, None)
     assert rc == 2 and b"rows" in lib.qp_last_error()

@@ -1,5 +1,5 @@
-"""Sliding-window and softcap attention on the split-KV kernel (K1), against the fp64 oracle computed from the same
-cache bytes.
+"""Sliding-window, softcap and sink layers on the split-KV kernel (K1) and its merge (K2), against the fp64 oracle
+computed from the same cache bytes.
 
 vLLM passes window_size = (w, 0) and its int4 kernel (the one the reference patches) masks with SLIDING_WINDOW =
 1 + w: the query at position p sees keys p - SLIDING_WINDOW + 1 .. p (vllm/v1/attention/ops/
@@ -11,8 +11,10 @@ key, windows wider than the context, ragged MTP batches, keys whose magnitudes s
 head 512, the varlen launch of short chunks, a sequence split over two ranges (the window reaching into the earlier
 rank's range) and a mixed step through the installed `unified_attention_int4`. The logit softcap (vLLM's
 apply_softcap, softcap * tanh(S / softcap): triton_attention_helpers.py:28-36) with caps that bend most scores (3)
-and Gemma 2's (50), alone and with a window, in decode, the varlen launch and the router. Bound: relative error
-< 5e-3."""
+and Gemma 2's (50), alone and with a window, in decode, the varlen launch and the router. Attention sinks (vLLM:
+the row maximum starts at the sink with sum 1 in one segment, triton_attention_helpers.py:108-138), folded once by
+the merge whatever the split count, in decode, varlen and a router step with every feature at once. Bound: relative
+error < 5e-3."""
 import numpy as np
 import pytest
 import torch
@@ -44,11 +46,12 @@ def errors(got, ref, qlens):
     return [qo.relerr(got[a:b], ref[a:b]) for a, b in zip(starts[:-1], starts[1:])]
 
 
-def decode_case(device, fmt, qlens, lens, window, num_splits=None, softcap=0.0, **kw):
+def decode_case(device, fmt, qlens, lens, window, num_splits=None, softcap=0.0, sinks=None, **kw):
     cache, table, qb = build(device, fmt, qlens, lens, **kw)
-    got = U.decode(cache, qb, qlens, lens, table, num_splits=num_splits, sliding_window=window, softcap=softcap)
+    got = U.decode(cache, qb, qlens, lens, table, num_splits=num_splits, sliding_window=window, softcap=softcap,
+                   sinks=sinks)
     ref = U.reference(cache.host_bytes(), cache.layout, qb, qlens, lens, table, sliding_window=window,
-                      softcap=softcap)
+                      softcap=softcap, sinks=sinks)
     assert np.isfinite(got).all()
     return errors(got, ref, qlens)
 
@@ -111,9 +114,36 @@ def test_softcap_with_window(device, fmt):
     assert errs[0] < TOL, errs
 
 
+def sink_logits(seed=11, nq=U.NQ):
+    """Per-head sinks from well below the rows' scores to well above them (the sink then takes most of the mass)."""
+    return np.random.default_rng(seed).uniform(-3.0, 6.0, nq).astype(np.float32)
+
+
 @pytest.mark.parametrize("fmt", ["int4", "k8v4"])
-@pytest.mark.parametrize("window,softcap", [(64, 0.0), (700, 0.0), (0, 4.0), (700, 4.0)])
-def test_varlen_chunks(device, fmt, window, softcap):
+@pytest.mark.parametrize("num_splits", [None, 1, 7])
+def test_sinks_decode(device, fmt, num_splits):
+    """The sink joins each row's denominator once, however many splits the merge folds."""
+    errs = decode_case(device, fmt, [4, 1], [16384, 700], 0, num_splits=num_splits, sinks=sink_logits(), seed=10)
+    assert max(errs) < TOL, errs
+
+
+def test_sinks_need_the_model_domain_output(device):
+    cache, table, qb = build(device, "int4", [1], [100])
+    kc, vc, ks, vs = cache.views
+    q = U.to_torch(qb, device)
+    with pytest.raises(ValueError, match="sinks"):
+        ops.paged_decode(q, kc, vc, torch.empty(q.shape, dtype=torch.float32, device=device),
+                         cu_seqlens_q=torch.tensor([0, 1], dtype=torch.int32, device=device), max_seqlen_q=1,
+                         seqused_k=torch.tensor([100], dtype=torch.int32, device=device), max_seqlen_k=100,
+                         softmax_scale=U.HS ** -0.5, block_table=torch.from_numpy(table).to(device), k_scale_cache=ks,
+                         v_scale_cache=vs, out_fp32_lse=torch.empty(q.shape[:2], dtype=torch.float32, device=device),
+                         sinks=torch.zeros(U.NQ, device=device))
+
+
+@pytest.mark.parametrize("fmt", ["int4", "k8v4"])
+@pytest.mark.parametrize("window,softcap,sinks", [(64, 0.0, False), (700, 0.0, False), (0, 4.0, False),
+                                                  (700, 4.0, False), (0, 0.0, True), (700, 4.0, True)])
+def test_varlen_chunks(device, fmt, window, softcap, sinks):
     """Short chunks in one varlen launch (the long ones too, for a windowed or softcapped layer), first chunks
     included."""
     qlens = [100] * 6 + [37, 250]
@@ -123,15 +153,16 @@ def test_varlen_chunks(device, fmt, window, softcap):
     q = U.to_torch(qb, device)
     out = torch.full_like(q, float("nan"))
     cu = torch.tensor(np.concatenate([[0], np.cumsum(qlens)]), dtype=torch.int32, device=device)
+    sk = sink_logits() if sinks else None
     ops.prefill_varlen(q, kc, vc, out, cu_seqlens_q=cu, seqused_k=torch.tensor(lens, dtype=torch.int32, device=device),
                        max_seqlen_k=max(lens), block_table=torch.from_numpy(table).to(device),
                        softmax_scale=U.HS ** -0.5, k_scale_cache=ks, v_scale_cache=vs, sliding_window=window,
-                       softcap=softcap)
+                       softcap=softcap, sinks=None if sk is None else torch.from_numpy(sk).to(device))
     torch.cuda.synchronize()
     got = out.float().cpu().numpy()
     assert np.isfinite(got).all(), "a row was not written"
     ref = U.reference(cache.host_bytes(), cache.layout, qb, qlens, lens, table, sliding_window=window,
-                      softcap=softcap)
+                      softcap=softcap, sinks=sk)
     errs = errors(got, ref, qlens)
     assert max(errs) < TOL, errs
     assert _lib.device_error() == 0
@@ -166,17 +197,20 @@ def test_sequence_split_over_two_ranges(device, window):
 
 
 @pytest.mark.parametrize("fmt", ["int4", "k8v4"])
-@pytest.mark.parametrize("softcap", [0.0, 5.0], ids=["window", "window-softcap"])
-def test_mixed_step_through_the_router(device, stock, fmt, softcap):  # noqa: F811
-    """A sliding-window (and softcap) layer's step: MTP decodes, a chunk long enough for the prefill kernel (it goes
-    to the varlen launch instead: the prefill kernel has neither) and a short chunk; every sampled row against
-    fp64."""
+@pytest.mark.parametrize("softcap,sinks", [(0.0, False), (5.0, False), (5.0, True)],
+                         ids=["window", "window-softcap", "window-softcap-sinks"])
+def test_mixed_step_through_the_router(device, stock, fmt, softcap, sinks):  # noqa: F811
+    """A sliding-window (softcap, sink) layer's step: MTP decodes, a chunk long enough for the prefill kernel (it
+    goes to the varlen launch instead: the prefill kernel has none of them) and a short chunk; every sampled row
+    against fp64."""
     qlens = [192, 4, 2, 40]
     lens = [12000, 9000, 30000, 300]
     window = 1024
     cache, table, qb, q, kc, vc, args = mixed_step(device, fmt, qlens, lens)
     out = torch.full_like(q, float("nan"))
-    stock.unified_attention_int4(q, kc, vc, out, **dict(args, window_size=(window - 1, 0), softcap=softcap))
+    sk = sink_logits() if sinks else None
+    stock.unified_attention_int4(q, kc, vc, out, **dict(args, window_size=(window - 1, 0), softcap=softcap,
+                                                        sinks=None if sk is None else torch.from_numpy(sk).to(device)))
     torch.cuda.synchronize()
     got = out.float().cpu().numpy()
     assert np.isfinite(got).all(), "a row of the step was not written"
@@ -189,7 +223,7 @@ def test_mixed_step_through_the_router(device, stock, fmt, softcap):  # noqa: F8
         j = r - starts[i]
         q_rot = qo.single_rht(qo.to_f32(qb[r:r + 1], "bf16"), sg).astype(np.float64)
         o, _ = qo.attention_from_cache(q_rot, data, cache.layout, table[i], lens[i] - qlens[i] + j + 1, hs ** -0.5,
-                                       sliding_window=window, softcap=softcap)
+                                       sliding_window=window, softcap=softcap, sinks=sk)
         want.append(qo.single_rht(o.astype(np.float32), sg, inverse=True).astype(np.float64) / hs)
     err = qo.relerr(got[sample], np.concatenate(want))
     assert err < TOL, f"{fmt}: relative error {err:.3e}"

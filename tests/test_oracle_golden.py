@@ -197,3 +197,27 @@ def test_softcap_is_tanh_of_the_scaled_score(softcap):
             s = softcap * np.tanh(s / softcap)
             w = np.exp(s - s.max())
             np.testing.assert_allclose(got[i, h], w @ V[:p + 1, 0] / w.sum(), rtol=1e-12, atol=1e-12)
+
+
+def test_sinks_join_the_denominator_once():
+    """A sink is a virtual key with logit sink_h and value 0 in every row's softmax (vLLM's attention sinks); folded
+    after the keys, also when the keys come in chunks (attention_from_cache folds the chunks first)."""
+    rng = np.random.default_rng(9)
+    n, qlen, nq, nkv, hs = 150, 3, 4, 2, 16
+    K = rng.standard_normal((n, nkv, hs)) * 2
+    V = rng.standard_normal((n, nkv, hs))
+    q = rng.standard_normal((qlen, nq, hs)) * 2
+    sinks = np.array([-3.0, 0.0, 2.5, 40.0])
+    got, lse = qo.attention_rht_domain(q, K, V, n, hs ** -0.5, hs, sinks=sinks)
+    for i in range(qlen):
+        p = n - qlen + i
+        for h in range(nq):
+            s = np.append(K[:p + 1, h // 2] @ q[i, h] * (hs ** -0.5 / hs), sinks[h])
+            w = np.exp(s - s.max())
+            vals = np.vstack([V[:p + 1, h // 2], np.zeros(hs)])
+            np.testing.assert_allclose(got[i, h], w @ vals / w.sum(), rtol=1e-10, atol=1e-14)
+            np.testing.assert_allclose(lse[i, h], s.max() + np.log(w.sum()), rtol=1e-12)
+    plain, plain_lse = qo.attention_rht_domain(q, K, V, n, hs ** -0.5, hs)
+    halves = [qo.attention_rht_domain(q, K[a:b], V[a:b], n - a, hs ** -0.5, hs) for a, b in ((0, 70), (70, n))]
+    o, l = qo.merge_partials(np.stack([h[0] for h in halves]), np.stack([h[1] for h in halves]))
+    np.testing.assert_allclose(qo.apply_sinks(o, l, sinks)[0], got, rtol=1e-10, atol=1e-14)

@@ -310,7 +310,7 @@ def test_unsupported_features_go_to_the_stock_path(monkeypatch):
     q, kc, out, args = _step([4], [5000])
     fn(q, kc, kc, out, **dict(args, alibi_slopes=torch.zeros(NQ)))
     assert not rec.calls and len(stock_calls) == 1
-    fn(q, kc, kc, out, **dict(args, sinks=torch.zeros(NQ)))
+    fn(q, kc, kc, out, **dict(args, qq_bias=torch.zeros(4, 4)))
     assert not rec.calls and len(stock_calls) == 2
 
 
@@ -347,11 +347,18 @@ def test_softcap_layers_run_on_the_split_kv_kernel(monkeypatch):
     stock, stock_calls = _stock_recorder()
     fn = int4_kv.make_unified_attention(stock)
     seen = []
-    monkeypatch.setattr(ops, "paged_decode", lambda *a, **kw: seen.append(("decode", kw["softcap"])))
-    monkeypatch.setattr(ops, "prefill_varlen", lambda *a, **kw: seen.append(("varlen", kw["softcap"])))
+    monkeypatch.setattr(ops, "paged_decode", lambda *a, **kw: seen.append(("decode", kw["softcap"], kw["sinks"])))
+    monkeypatch.setattr(ops, "prefill_varlen", lambda *a, **kw: seen.append(("varlen", kw["softcap"], kw["sinks"])))
     q, kc, out, args = _step([256, 2, 40], [40000, 20000, 300], window=(4095, 0))
     fn(q, kc, kc, out, **dict(args, softcap=50.0))
-    assert sorted(seen) == [("decode", 50.0), ("varlen", 50.0)] and not rec.calls and not stock_calls
+    assert sorted(seen) == [("decode", 50.0, None), ("varlen", 50.0, None)] and not rec.calls and not stock_calls
+    # sinks (gpt-oss-style layers): the merge folds them in; the long chunk goes to the varlen launch as well
+    seen.clear()
+    sinks = torch.zeros(NQ)
+    q, kc, out, args = _step([256, 2], [40000, 20000])
+    fn(q, kc, kc, out, **dict(args, sinks=sinks))
+    assert [(c[0], c[2] is sinks) for c in sorted(seen, key=lambda c: c[0])] == [("decode", True), ("varlen", True)]
+    assert not stock_calls
 
 
 def test_head_512_is_served_and_other_head_sizes_go_stock(monkeypatch):
@@ -533,7 +540,7 @@ def test_k8v4_call_outside_the_kernels_raises(monkeypatch):
     q, _, out, args = _step([4], [5000])
     kc8 = torch.zeros((4, 16, NKV, HS), dtype=torch.int8)
     with pytest.raises(NotImplementedError, match="k8v4"):
-        fn(q, kc8, kc8, out, **dict(args, sinks=torch.zeros(NQ)))
+        fn(q, kc8, kc8, out, **dict(args, qq_bias=torch.zeros(4, 4)))
     with pytest.raises(NotImplementedError, match="k8v4"):
         fn(q, kc8, kc8, out, **dict(args, alibi_slopes=torch.zeros(NQ)))
     fn2 = int4_kv.make_unified_attention(stock, prefill_on=False)

@@ -27,7 +27,7 @@ SIGNATURES = {
     "qp_decode_num_splits": (_I, [_I, _I, _I, _I]),
     "qp_decode_workspace_bytes": (_L, [_L, _I, _I, _I]),
     "qp_paged_decode": (_I, [_I, _I, _P, _L, _L, _P, _L, _L, _L, _I, _P, _P, _I, _P, _L, _P, _I, _L, _L, _L, _L, _L,
-                             _L, _L, _I, _I, _I, _F, _P, _I, _I, _I, _F, _I, _P, _I, _P, _L, _P]),
+                             _L, _L, _I, _I, _I, _F, _P, _I, _I, _I, _F, _P, _I, _P, _I, _P, _L, _P]),
     "qp_paged_decode_static": (_I, [_I, _I, _P, _L, _L, _P, _L, _L, _L, _I, _P, _P, _I, _P, _L, _P, _I, _L, _L, _L, _L,
                                     _L, _L, _L, _I, _I, _I, _F, _P, _I, _I, _P, _I, _P]),
     "qp_prefill_workspace_bytes": (_L, [_I, _I, _I, _I, _I, _I]),
@@ -35,7 +35,7 @@ SIGNATURES = {
                         _P, _I, _I, _I, _P, _P, _L, _P]),
     "qp_prefill_varlen_workspace_bytes": (_L, [_L, _I, _I, _I, _I, _I]),
     "qp_prefill_varlen": (_I, [_I, _I, _P, _L, _L, _P, _L, _L, _L, _I, _P, _P, _I, _P, _L, _P, _I, _L, _L, _L, _L, _L,
-                               _L, _L, _I, _I, _I, _F, _P, _I, _I, _F, _I, _P, _P, _L, _P]),
+                               _L, _L, _I, _I, _I, _F, _P, _I, _I, _F, _P, _I, _P, _P, _L, _P]),
     "qp_peer_exchange_bytes": (_L, [_I, _L, _I, _I]),
     "qp_peer_partial_offset": (_L, [_I, _L, _I, _I, _I]),
     "qp_fold_peer_partials": (_I, [_I, _I, _L, _I, _I, _I, _P, ctypes.c_uint32, _I, _P, _L, _L, _P, _P, _P]),

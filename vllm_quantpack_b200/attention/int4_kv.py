@@ -76,11 +76,11 @@ def decode_splits_override():
     return int(parts[2])
 
 
-def _plain(q, sinks, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
+def _plain(q, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
     """True when the call uses no feature outside the B200 kernels (the reference's list, int4_kv.py:304-305, less
-    the sliding window and the softcap, which the split-KV kernel applies)."""
-    return sinks is None and alibi_slopes is None and qq_bias is None and output_scale is None \
-        and mm_prefix_range is None and q.shape[2] in HEAD_SIZES
+    the sliding window, the softcap and the sinks, which the split-KV kernel and its merge apply)."""
+    return alibi_slopes is None and qq_bias is None and output_scale is None and mm_prefix_range is None \
+        and q.shape[2] in HEAD_SIZES
 
 
 def sliding_window_of(window_size):
@@ -169,8 +169,8 @@ def split_step(cu, used, group, prefill_on=True, head_size=256, long_chunks=True
     tokens over at least MIN_CONTEXT cached tokens, or enough query rows to fill the machine on their own; head 256)
     each go to the tcgen05 prefill kernel, the rest together to one varlen launch of the split-KV kernel, as the
     reference sends its long chunks to FlashAttention and the rest to one Triton sub-batch (int4_kv.py:313-323).
-    long_chunks=False (a sliding-window or softcap layer: the prefill kernel has neither) sends every chunk to the
-    varlen launch. With prefill routing off every chunk goes to the stock path. Requests without queries are left out."""
+    long_chunks=False (a sliding-window, softcap or sink layer: the prefill kernel has none of them) sends every
+    chunk to the varlen launch. With prefill routing off every chunk goes to the stock path. Requests without queries are left out."""
     from .int4_prefill import MIN_CONTEXT, MIN_QUERY
     dec, long, short, stock = [], [], [], []
     for i in range(len(used)):
@@ -192,8 +192,8 @@ def split_step(cu, used, group, prefill_on=True, head_size=256, long_chunks=True
 def make_unified_attention(stock_unified, prefill_on=True):
     """The replacement of `unified_attention_int4` (signature of int4_kv.py:294-301), falling back to
     `stock_unified` for int4 calls the B200 kernels do not cover. A k8v4 cache has no stock kernel to fall back to
-    (the stock int4 kernel would read its int8 keys as nibbles), so such a call raises instead. A sliding-window or
-    softcap layer runs on the split-KV kernel: decodes as usual, every prefill chunk in the varlen launch."""
+    (the stock int4 kernel would read its int8 keys as nibbles), so such a call raises instead. A sliding-window,
+    softcap or sink layer runs on the split-KV kernel: decodes as usual, every prefill chunk in the varlen launch."""
     from . import k8v4_kv, ops
 
     def unified_attention_int4(q, k_cache, v_cache, out, *, cu_seqlens_q, max_seqlen_q, seqused_k, max_seqlen_k,
@@ -204,10 +204,10 @@ def make_unified_attention(stock_unified, prefill_on=True):
                     block_table=block_table, softcap=softcap, sinks=sinks, alibi_slopes=alibi_slopes,
                     use_alibi_sqrt=use_alibi_sqrt, qq_bias=qq_bias, output_scale=output_scale,
                     mm_prefix_range=mm_prefix_range, k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache, **kw)
-        if not _plain(q, sinks, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
+        if not _plain(q, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
             if k8v4_kv.is_k8v4(k_cache):
                 raise NotImplementedError(
-                    f"{k8v4_kv.NAME}: sinks, ALiBi, qq_bias, FP8 output, mm_prefix ranges and head sizes other than "
+                    f"{k8v4_kv.NAME}: ALiBi, qq_bias, FP8 output, mm_prefix ranges and head sizes other than "
                     f"{HEAD_SIZES} are not served by the B200 kernels, and vLLM's stock int4 kernel cannot read a "
                     f"k8v4 cache")
             return stock_unified(q, k_cache, v_cache, out, **args)
@@ -220,13 +220,14 @@ def make_unified_attention(stock_unified, prefill_on=True):
             ops.paged_decode(qs, k_cache, v_cache, outs, cu_seqlens_q=a["cu_seqlens_q"],
                              max_seqlen_q=a["max_seqlen_q"], seqused_k=a["seqused_k"], max_seqlen_k=a["max_seqlen_k"],
                              softmax_scale=softmax_scale, block_table=a["block_table"], k_scale_cache=k_scale_cache,
-                             v_scale_cache=v_scale_cache, num_splits=splits, sliding_window=window, softcap=cap)
+                             v_scale_cache=v_scale_cache, num_splits=splits, sliding_window=window, softcap=cap,
+                             sinks=sinks)
 
         if max_seqlen_q <= MAX_Q_SPLIT_KV and max_seqlen_q * group <= MAX_DECODE_ROWS:
             # a decode step: no host read of the lengths (CUDA-graph capturable)
             return decode(q, out, args)
         plan = StepPlan.of(cu_seqlens_q, seqused_k, group, prefill_on, q.shape[2],
-                           long_chunks=window == 0 and cap == 0.0)
+                           long_chunks=window == 0 and cap == 0.0 and sinks is None)
         if plan.dec_batch is not None:
             plan.dec_batch.run(decode, q, out, args)
         if plan.short_batch is not None:
@@ -234,8 +235,8 @@ def make_unified_attention(stock_unified, prefill_on=True):
                 lambda qs, outs, a: ops.prefill_varlen(
                     qs, k_cache, v_cache, outs, cu_seqlens_q=a["cu_seqlens_q"], seqused_k=a["seqused_k"],
                     max_seqlen_k=a["max_seqlen_k"], block_table=a["block_table"], softmax_scale=softmax_scale,
-                    k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache, sliding_window=window, softcap=cap),
-                q, out, args)
+                    k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache, sliding_window=window, softcap=cap,
+                    sinks=sinks), q, out, args)
         if plan.stock_batch is not None:
             if k8v4_kv.is_k8v4(k_cache):
                 raise NotImplementedError(f"{k8v4_kv.NAME}: prefill chunks need the B200 prefill kernel "

@@ -22,6 +22,22 @@ def _stream(device):
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def _sinks_ptr(sinks, nq, mode):
+    """Device pointer of fp32 sink logits (one per query head), or None. Sinks count once in a row's softmax, so
+    only the model-domain output (mode 0) can take them, never a partial."""
+    if sinks is None:
+        return None
+    if mode != 0:
+        raise ValueError("sinks apply to the model-domain output only, not to partials")
+    if sinks.dim() != 1 or sinks.shape[0] != nq:
+        raise ValueError(f"sinks must have one logit per query head ({nq}), got {tuple(sinks.shape)}")
+    if sinks.dtype != torch.float32 or not sinks.is_contiguous():
+        # a temporary on the current stream: torch's caching allocator hands its memory to a later allocation only
+        # in stream order, after the merge kernel that reads it
+        sinks = sinks.float().contiguous()
+    return sinks.data_ptr()
+
+
 def _dtype_code(t, what):
     code = _DTYPES.get(t.dtype)
     if code is None:
@@ -166,7 +182,7 @@ def decode_num_splits(num_seqs, num_kv_heads, max_seqlen_k, sms):
 def paged_decode(q, key_cache, value_cache, out, *, cu_seqlens_q, max_seqlen_q, seqused_k, max_seqlen_k,
                  softmax_scale, block_table, k_scale_cache, v_scale_cache, num_splits=None, q_rotated=False,
                  out_fp32_lse=None, ws=None, partials_only=False, tokens_after_keys=0, sliding_window=0,
-                 softcap=0.0):
+                 softcap=0.0, sinks=None):
     """Split-KV decode of up to 32 query rows per KV head (4 MTP tokens x 6 heads) over the paged cache.
 
     q / out (tokens, query heads, hs). When `out_fp32_lse` is a tensor (tokens, query heads) fp32, `out` must be fp32
@@ -176,7 +192,8 @@ def paged_decode(q, key_cache, value_cache, out, *, cu_seqlens_q, max_seqlen_q, 
     the cached keys given here (a sequence-parallel rank holding an earlier range): query token i of a sequence sees
     key k iff k <= seqused_k - qlen + i + tokens_after_keys. sliding_window: vLLM's SLIDING_WINDOW (1 +
     window_size[0], 0 = none): that token then sees only the keys k > its last key - sliding_window. softcap > 0:
-    vLLM's logit softcap, every score S becomes softcap * tanh(S / softcap)."""
+    vLLM's logit softcap, every score S becomes softcap * tanh(S / softcap). sinks: None or (query heads,) sink
+    logits whose exp joins every row's softmax denominator (vLLM's attention sinks; model-domain output only)."""
     hs = q.shape[-1]
     nq = q.shape[1]
     lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
@@ -212,7 +229,7 @@ def paged_decode(q, key_cache, value_cache, out, *, cu_seqlens_q, max_seqlen_q, 
               out.stride(1), q.shape[0], num_seqs, cu_seqlens_q.data_ptr(), seqused_k.data_ptr(), int(max_seqlen_q),
               block_table.data_ptr(), block_table.stride(0), *lay.args(), nq, nkv, hs, float(softmax_scale),
               rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)), int(tokens_after_keys),
-              int(sliding_window), float(softcap or 0.0), mode, lse_ptr, int(num_splits),
+              int(sliding_window), float(softcap or 0.0), _sinks_ptr(sinks, nq, mode), mode, lse_ptr, int(num_splits),
               ws.data_ptr(), ws.numel() * ws.element_size(), _stream(q.device))
     return ws if partials_only else out
 
@@ -292,13 +309,13 @@ def prefill(q, key_cache, value_cache, out, *, block_row, n, softmax_scale, k_sc
 
 def prefill_varlen(q, key_cache, value_cache, out, *, cu_seqlens_q, seqused_k, max_seqlen_k, block_table,
                    softmax_scale, k_scale_cache, v_scale_cache, q_rotated=False, out_fp32_lse=None, ws=None,
-                   sliding_window=0, softcap=0.0):
+                   sliding_window=0, softcap=0.0, sinks=None):
     """Several short prefill chunks in ONE launch (the reference's Triton sub-batch of the chunks that are not long,
     vllm_quantpack/attention/int4_kv.py:313-323): request i's query tokens q[cu_seqlens_q[i]:cu_seqlens_q[i + 1]] are
     the last positions of its context of seqused_k[i] cached tokens, causal among themselves, read through
     block_table[i]. Split on the device into sub-sequences of 32 / group tokens for the split-KV kernel, so nothing
     is read back to the host; max_seqlen_k (a host int, an upper bound of seqused_k) sizes the split count.
-    `out` as in prefill; sliding_window and softcap as in paged_decode."""
+    `out` as in prefill; sliding_window, softcap and sinks as in paged_decode."""
     hs, nq, T = q.shape[-1], q.shape[1], q.shape[0]
     lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
     for name, t in (("cu_seqlens_q", cu_seqlens_q), ("seqused_k", seqused_k), ("block_table", block_table)):
@@ -325,6 +342,6 @@ def prefill_varlen(q, key_cache, value_cache, out, *, cu_seqlens_q, seqused_k, m
               out.stride(0), out.stride(1), T, chunks, cu_seqlens_q.data_ptr(), seqused_k.data_ptr(),
               max_k, block_table.data_ptr(), block_table.stride(0), *lay.args(), nq, lay.nkv, hs,
               float(softmax_scale), rht.device_sign_bits(hs, q.device).data_ptr(), int(bool(q_rotated)),
-              int(sliding_window), float(softcap or 0.0), mode, lse_ptr, ws.data_ptr(), ws.numel() * ws.element_size(),
-              _stream(q.device))
+              int(sliding_window), float(softcap or 0.0), _sinks_ptr(sinks, nq, mode), mode, lse_ptr, ws.data_ptr(),
+              ws.numel() * ws.element_size(), _stream(q.device))
     return out

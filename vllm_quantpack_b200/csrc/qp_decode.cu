@@ -1092,6 +1092,10 @@ struct MergeParams {
   int64_t lo_t, lo_h;
   const uint32_t* sign_bits;
   float out_scale;  // multiplies the output (mode 0: 1 / head)
+  // mode 0, may be null: per query head, a sink logit (natural units) whose exp joins every row's softmax
+  // denominator once, vLLM's attention sinks (vllm/v1/attention/ops/triton_attention_helpers.py:108-138: the row
+  // maximum starts at the sink with sum 1 in one segment only; triton_unified_attention.py:356-359)
+  const float* sinks;
 };
 
 constexpr int MERGE_THREADS = 512;
@@ -1116,6 +1120,8 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(const MergeParams 
   float M = red[0];
 #pragma unroll
   for (int i = 1; i < NW; ++i) M = fmaxf(M, red[i]);
+  const float sink = p.sinks != nullptr ? p.sinks[qh] * LOG2E : -INFINITY;  // base 2, like the partials' lse
+  M = fmaxf(M, sink);
   float tot = 0.f;
   for (int s = tid; s < p.num_splits; s += MERGE_THREADS) {
     const float l = lse[s * p.pl_s];
@@ -1128,7 +1134,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(const MergeParams 
   if ((tid & 31) == 0) red[tid >> 5] = tot;
   __syncthreads();
   if (tid == 0) {
-    float s = 0.f;
+    float s = sink == -INFINITY ? 0.f : exp2f(sink - M);  // the sink: in the denominator only
 #pragma unroll
     for (int i = 0; i < NW; ++i) s += red[i];
     tot_sm = s;
@@ -1347,7 +1353,8 @@ static int decode_check_cache(const char* who, int fmt, int dtype, int head_size
 }
 
 static MergeParams decode_merge_params(const DecodeParams& dp, int head_size, int out_mode, void* out,
-                                       int64_t out_stride_token, int64_t out_stride_head, float* lse_out) {
+                                       int64_t out_stride_token, int64_t out_stride_head, float* lse_out,
+                                       const float* sinks = nullptr) {
   MergeParams mp{};
   mp.part_o = dp.part_o;
   mp.part_lse = dp.part_lse;
@@ -1368,6 +1375,7 @@ static MergeParams decode_merge_params(const DecodeParams& dp, int head_size, in
   mp.lo_h = 1;
   mp.sign_bits = dp.sign_bits;
   mp.out_scale = 1.f / static_cast<float>(head_size);
+  mp.sinks = sinks;
   return mp;
 }
 
@@ -1386,9 +1394,9 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
                                int block_size, int64_t block_stride, int64_t head_stride, int64_t slot_stride,
                                int64_t k_off, int64_t ks_off, int64_t v_off, int64_t vs_off, int num_q_heads,
                                int num_kv_heads, int head_size, float softmax_scale, const uint32_t* rht_sign_bits,
-                               int q_rotated, int tokens_after_keys, int sliding_window, float softcap, int out_mode,
-                               float* lse_out, int num_splits, void* workspace, int64_t workspace_bytes,
-                               void* stream) {
+                               int q_rotated, int tokens_after_keys, int sliding_window, float softcap,
+                               const float* sinks, int out_mode, float* lse_out, int num_splits, void* workspace,
+                               int64_t workspace_bytes, void* stream) {
   int rc = decode_check_cache("decode", fmt, dtype, head_size, cache, block_size, block_stride, head_stride,
                               slot_stride, k_off, ks_off, v_off, vs_off);
   if (rc) return rc;
@@ -1405,6 +1413,8 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
   if (tokens_after_keys < 0) return set_error(QP_ERR_INVALID, "decode: tokens_after_keys %d", tokens_after_keys);
   if (sliding_window < 0) return set_error(QP_ERR_INVALID, "decode: sliding_window %d", sliding_window);
   if (!(softcap >= 0.f) || isinf(softcap)) return set_error(QP_ERR_INVALID, "decode: softcap %g", softcap);
+  if (sinks && out_mode != 0)
+    return set_error(QP_ERR_INVALID, "decode: sinks need out_mode 0 (a partial must not carry them: they count once)");
   if (num_splits <= 0) return set_error(QP_ERR_INVALID, "decode: num_splits %d", num_splits);
   if (num_splits > 1024) return set_error(QP_ERR_UNSUPPORTED, "decode: num_splits %d > 1024", num_splits);
   if (!q || !out || !cu_seqlens_q || !seqused_k || !block_table || !cache || !rht_sign_bits || !workspace)
@@ -1446,7 +1456,8 @@ extern "C" int qp_paged_decode(int fmt, int dtype, const void* q, int64_t q_stri
   rc = launch_decode(fmt, dtype, head_size, dp, max_seqlen_q * group, num_seqs, st);
   if (rc) return rc;
   if (out_mode == 2) return QP_OK;  // split partials stay in the workspace
-  return merge_dispatch(decode_merge_params(dp, head_size, out_mode, out, out_stride_token, out_stride_head, lse_out),
+  return merge_dispatch(decode_merge_params(dp, head_size, out_mode, out, out_stride_token, out_stride_head, lse_out,
+                                          sinks),
                         dtype, head_size, num_q_tokens, st, true);
 }
 
@@ -1584,8 +1595,8 @@ extern "C" int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_st
                                  int64_t slot_stride, int64_t k_off, int64_t ks_off, int64_t v_off, int64_t vs_off,
                                  int num_q_heads, int num_kv_heads, int head_size, float softmax_scale,
                                  const uint32_t* rht_sign_bits, int q_rotated, int sliding_window, float softcap,
-                                 int out_mode, float* lse_out, void* workspace, int64_t workspace_bytes,
-                                 void* stream) {
+                                 const float* sinks, int out_mode, float* lse_out, void* workspace,
+                                 int64_t workspace_bytes, void* stream) {
   int rc = decode_check_cache("prefill varlen", fmt, dtype, head_size, cache, block_size, block_stride, head_stride,
                               slot_stride, k_off, ks_off, v_off, vs_off);
   if (rc) return rc;
@@ -1597,6 +1608,8 @@ extern "C" int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_st
   if (out_mode != 0 && out_mode != 1) return set_error(QP_ERR_INVALID, "prefill varlen: out_mode %d", out_mode);
   if (sliding_window < 0) return set_error(QP_ERR_INVALID, "prefill varlen: sliding_window %d", sliding_window);
   if (!(softcap >= 0.f) || isinf(softcap)) return set_error(QP_ERR_INVALID, "prefill varlen: softcap %g", softcap);
+  if (sinks && out_mode != 0)
+    return set_error(QP_ERR_INVALID, "prefill varlen: sinks need out_mode 0 (a partial must not carry them)");
   const int group = num_q_heads / num_kv_heads;
   const int cq = chunk_q_of(group);
   if (!cq) return set_error(QP_ERR_UNSUPPORTED, "prefill varlen: %d query heads per KV head > %d", group, DEC_MAX_ROWS);
@@ -1642,7 +1655,8 @@ extern "C" int qp_prefill_varlen(int fmt, int dtype, const void* q, int64_t q_st
   decode_bind_workspace(dp, workspace, head_size);
   rc = launch_decode(fmt, dtype, head_size, dp, cq * group, upper, st);
   if (rc) return rc;
-  return merge_dispatch(decode_merge_params(dp, head_size, out_mode, out, out_stride_token, out_stride_head, lse_out),
+  return merge_dispatch(decode_merge_params(dp, head_size, out_mode, out, out_stride_token, out_stride_head, lse_out,
+                                          sinks),
                         dtype, head_size, num_q_tokens, st, true);
 }
 
@@ -1913,5 +1927,6 @@ extern "C" int qp_paged_decode_static(int fmt, int dtype, const void* q, int64_t
                          num_q_tokens, num_seqs, cu_seqlens_q, seqused_k, max_seqlen_q, block_table,
                          block_table_stride, cache, block_size, block_stride, head_stride, slot_stride, k_off, ks_off,
                          v_off, vs_off, num_q_heads, num_kv_heads, head_size, softmax_scale, rht_sign_bits, q_rotated,
-                         0, 0, 0.f, out_mode, lse_out, num_splits, scratch, kStaticDecodeScratchBytes, stream);
+                         0, 0, 0.f, nullptr, out_mode, lse_out, num_splits, scratch, kStaticDecodeScratchBytes,
+                         stream);
 }
