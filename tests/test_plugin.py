@@ -573,3 +573,33 @@ def test_step_plan_is_made_once_per_step(monkeypatch):
     assert len(made) == 2
     fn(q, kc, kc, out, **dict(args, seqused_k=args["seqused_k"].clone()))   # other tensors, same step: new plan
     assert len(made) == 3
+
+
+def test_window_sizes_the_split_count_by_the_window():
+    """With a sliding window the splits cover only the tiles of the window (plus a partial tile), not the context."""
+    assert ops.window_keys(262144, 0, 4) == 262144
+    assert ops.window_keys(262144, 1024, 4) == 1024 + 3 + 127
+    assert ops.window_keys(500, 1024, 4) == 500
+    assert ops.window_keys(262144, 1, 1) == 128
+
+
+def test_step_split_without_long_chunks():
+    """long_chunks=False (window, softcap or sink layers): a chunk that would be long goes with the short ones."""
+    cu = [0, 256, 258, 298]
+    used = [40000, 20000, 300]
+    dec, long, short, stock = int4_kv.split_step(cu, used, group=6)
+    assert (dec, long, short, stock) == ([1], [0], [2], [])
+    dec, long, short, stock = int4_kv.split_step(cu, used, group=6, long_chunks=False)
+    assert (dec, long, short, stock) == ([1], [], [0, 2], [])
+
+
+def test_sinks_argument_checks():
+    """Sinks: one logit per query head, model-domain output only; other dtypes are converted to fp32."""
+    assert ops._sinks_ptr(None, NQ, 0) is None
+    s32 = torch.zeros(NQ)
+    assert ops._sinks_ptr(s32, NQ, 0) == s32.data_ptr()
+    assert ops._sinks_ptr(torch.zeros(NQ, dtype=torch.bfloat16), NQ, 0) != 0
+    with pytest.raises(ValueError, match="query head"):
+        ops._sinks_ptr(torch.zeros(NQ + 1), NQ, 0)
+    with pytest.raises(ValueError, match="model-domain"):
+        ops._sinks_ptr(s32, NQ, 1)
