@@ -1,8 +1,10 @@
 // K1: split-KV paged decode over an int4_per_token_head / k8v4_per_token_head cache, up to 32 query rows
 //     (qlen x query heads per KV head) per KV head, head size 256 or 512, on the 5th-generation tensor cores
 //     (tcgen05 + TMEM); K0q: the query preparation it reads; K2: log-sum-exp merge of the segments with the inverse
-//     RHT fused in. At head 512 the same kernel also serves chunk prefill, as decodes of a few query tokens each
-//     over the chunk's causal prefixes (qp_prefill).
+//     RHT and the attention sinks fused in. At head 512 the same kernel also serves chunk prefill, as decodes of a
+//     few query tokens each over the chunk's causal prefixes (qp_prefill), and at both head sizes the short chunks of
+//     a step in one launch (qp_prefill_varlen). A second instantiation (FEAT) applies vLLM's sliding window and logit
+//     softcap.
 //
 // Reference behaviour (what this computes, not how): the split-KV 3D path of vLLM's int4 kernel as the plugin
 // configures it (vllm_quantpack/attention/int4_kv.py:98-122: every query token of a step in one program, segments
@@ -16,11 +18,13 @@
 // bandwidth the A operand then saturates). So the keys are the M dimension and both cache operands live in TMEM:
 //   S^T (128 keys x N rows)          = K_op (TMEM, 128 keys x HS channels)          x Q^T (shared memory, N x HS)
 //   O^T (HS/128 x 128 channels x N)  = V^T_op (TMEM, HS/128 x 128 channels x keys)  x P^T (shared memory, N x keys)
-// One CTA of 14 warps per SM (it holds all 512 TMEM columns) per (split, KV head, sequence):
+// One CTA of 15 warps (19 at head 256 with up to 24 rows) per SM (it holds all 512 TMEM columns) per (split, KV
+// head, sequence):
 //   warp 0      producer: 1-D bulk copies (TMA engine, no tensor map, no multicast) of the tile's raw cells, whole
 //               16-token groups, into a ring of raw stages (a stage holds the tile, or at head 512 half of it);
-//   warp 1      MMA issuer (convergent; elect.sync picks the lane): HS/16 QK MMAs per tile into a double-buffered S,
-//               then the previous tile's PV MMAs, each group finished with tcgen05.commit onto mbarriers;
+//   warps 1, 14 MMA issuers (convergent; elect.sync picks the lane), on different SM sub-partitions: warp 1 the
+//               HS/16 QK MMAs of a tile into a double-buffered S, warp 14 the PV MMAs, each group finished with
+//               tcgen05.commit onto mbarriers;
 //   warps 2-5   key operand: thread = key = TMEM lane; one AND per channel pair makes the int4 codes fp16
 //               subnormals (u x 2^-24, 16 u x 2^-24 for high nibbles, whose query channels K0q divides by 16); k8v4
 //               codes become c + 128 the same way (one XOR per word, one prmt per pair). The zero point (int4) or the
@@ -30,7 +34,8 @@
 //               with 32 rows, where TMEM has no room for two), so the conversion of one chunk overlaps the MMAs of
 //               the other. The key / value scales go to shared memory for the softmax, the value zero points as
 //               paired fp16 operand biases;
-//   warps 6-9   value operand: V^T written with tcgen05.st.16x256b, whose thread layout (lanes i/4 and 8 + i/4,
+//   warps 6-9   value operand (and 15-18, a second set converting every other slot, at head 256 with <= 24 rows):
+//               V^T written with tcgen05.st.16x256b, whose thread layout (lanes i/4 and 8 + i/4,
 //               column pair 2(i%4)) puts one channel of four consecutive keys in each thread: one 32-bit word of
 //               each of four keys, interleaved by prmt, becomes the exact fp16 (u - zp) of every (channel, key).
 //               The zero point sits in the operand, so the running O accumulator only holds the signal; two value
