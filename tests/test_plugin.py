@@ -603,3 +603,25 @@ def test_sinks_argument_checks():
         ops._sinks_ptr(torch.zeros(NQ + 1), NQ, 0)
     with pytest.raises(ValueError, match="model-domain"):
         ops._sinks_ptr(s32, NQ, 1)
+
+
+def test_cache_layout_is_derived_once_per_set_of_views():
+    """CacheLayout.of keeps a layout by every input of its derivation: the same views give the same object, a view
+    with other strides or offsets is derived (and checked) anew, and an invalid set raises every time."""
+    kv4 = torch.zeros((5, NKV, 16, 2 * (HS // 2 + 4)), dtype=torch.uint8)
+    base = torch.tensor([], dtype=torch.float32).set_(kv4.untyped_storage())
+    st = [s // 4 for s in kv4.stride()]
+    phs = HS // 2 + 4
+    ks = torch.as_strided(base, (5, 16, NKV), (st[0], st[2], st[1]), HS // 2 // 4)
+    vs = torch.as_strided(base, (5, 16, NKV), (st[0], st[2], st[1]), (phs + HS // 2) // 4)
+    kc, vc = kv4.transpose(1, 2).split(phs, dim=-1)
+    a = ops.CacheLayout.of(kc, vc, ks, vs, HS)
+    assert ops.CacheLayout.of(kc, vc, ks, vs, HS) is a
+    kc2, vc2 = kv4.transpose(1, 2).split(phs, dim=-1)      # new view objects over the same bytes
+    assert ops.CacheLayout.of(kc2, vc2, ks, vs, HS) is a
+    for _ in range(2):
+        with pytest.raises(ValueError):
+            ops.CacheLayout.of(kc, vc, vs, ks, HS)           # scale views swapped
+    sub = kc[:4], vc[:4], ks[:4], vs[:4]                     # fewer blocks: another layout
+    b = ops.CacheLayout.of(*sub, HS)
+    assert b is not a and b.nblocks == 4 and b.args() == a.args()

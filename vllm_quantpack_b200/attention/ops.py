@@ -46,7 +46,8 @@ def _dtype_code(t, what):
 
 
 class CacheLayout:
-    """Byte layout of a paged int4 / k8v4 cache, derived from the four views vLLM passes.
+    """Byte layout of a paged int4 / k8v4 cache, derived from the four views vLLM passes (`of` keeps the layouts it
+    derived, keyed by everything they are derived from, so a call on the same cache pays for the checks once).
 
     int4 views (tests/test_int4_kv.py:95-103): key / value (blocks, block size, KV heads, hs/2 + 4) uint8 over cells
     [K | K scale | V | V scale]; k8v4 views (vllm_quantpack/attention/k8v4_kv.py:41-65): key (..., hs) int8, value
@@ -82,6 +83,24 @@ class CacheLayout:
         if self.ks_off != kb or self.v_off != kb + 4 or self.vs_off != kb + 4 + head_size // 2:
             raise ValueError(f"cell fields at K 0, K scale {self.ks_off}, V {self.v_off}, V scale {self.vs_off}: "
                              f"expected 0, {kb}, {kb + 4}, {kb + 4 + head_size // 2}")
+
+    _known = {}
+
+    @classmethod
+    def of(cls, k_cache, v_cache, k_scale_cache, v_scale_cache, head_size):
+        """The layout of these views: a derived one when every input to the derivation (addresses, dtypes, shapes,
+        strides, head size) matches, else a new one (checked; only valid layouts are kept)."""
+        key = (k_cache.data_ptr(), v_cache.data_ptr(), k_scale_cache.data_ptr(), v_scale_cache.data_ptr(),
+               k_cache.dtype, v_cache.dtype, k_scale_cache.dtype, v_scale_cache.dtype, k_cache.shape, v_cache.shape,
+               k_scale_cache.shape, v_scale_cache.shape, k_cache.stride(), v_cache.stride(), k_scale_cache.stride(),
+               v_scale_cache.stride(), head_size)
+        lay = cls._known.get(key)
+        if lay is None:
+            lay = cls(k_cache, v_cache, k_scale_cache, v_scale_cache, head_size)
+            if len(cls._known) >= 256:
+                cls._known.clear()
+            cls._known[key] = lay
+        return lay
 
     def args(self):
         return (self.base, self.block_size, self.block_stride, self.head_stride, self.slot_stride, self.k_off,
@@ -121,7 +140,7 @@ def reshape_and_cache_int4(key, value, key_cache, value_cache, slot_mapping, *, 
         raise ValueError(f"key head size {hs} != value head size {value.shape[-1]}")
     if key.stride(-1) != 1 or value.stride(-1) != 1:
         raise ValueError("key / value rows must be contiguous")
-    lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
+    lay = CacheLayout.of(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
     if slot_mapping.dtype != torch.int64:
         slot_mapping = slot_mapping.to(torch.int64)
     slot_mapping = slot_mapping.contiguous()
@@ -148,6 +167,9 @@ def workspace(device, nbytes):
     buffer that is outgrown stays allocated too: a CUDA graph captured earlier may still hold its address. Growing
     it inside a CUDA-graph capture allocates from the graph's pool: reserve the largest size before capturing."""
     key = str(torch.device(device))
+    ws = _workspaces.get(key)
+    if ws is not None and ws.numel() >= nbytes:  # the common case: no growth, no lock
+        return ws
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
@@ -159,8 +181,15 @@ def workspace(device, nbytes):
     return ws
 
 
+_sm_counts = {}
+
+
 def sm_count(device):
-    return torch.cuda.get_device_properties(device).multi_processor_count
+    key = str(torch.device(device))
+    n = _sm_counts.get(key)
+    if n is None:
+        n = _sm_counts[key] = torch.cuda.get_device_properties(device).multi_processor_count
+    return n
 
 
 VARLEN_MAX_Q = 32   # query tokens of a varlen sub-sequence at most (32 query rows per KV head)
@@ -175,8 +204,21 @@ def window_keys(max_seqlen_k, sliding_window, max_q):
     return max_seqlen_k
 
 
+_sizes = {}   # host-side size arithmetic of the library, by its arguments
+
+
+def _memo(fn_name, *args):
+    key = (fn_name,) + args
+    v = _sizes.get(key)
+    if v is None:
+        if len(_sizes) >= 4096:
+            _sizes.clear()
+        v = _sizes[key] = getattr(_lib.load(), fn_name)(*args)
+    return v
+
+
 def decode_num_splits(num_seqs, num_kv_heads, max_seqlen_k, sms):
-    return _lib.load().qp_decode_num_splits(num_seqs, num_kv_heads, max_seqlen_k, sms)
+    return _memo("qp_decode_num_splits", int(num_seqs), int(num_kv_heads), int(max_seqlen_k), int(sms))
 
 
 def paged_decode(q, key_cache, value_cache, out, *, cu_seqlens_q, max_seqlen_q, seqused_k, max_seqlen_k,
@@ -196,13 +238,13 @@ def paged_decode(q, key_cache, value_cache, out, *, cu_seqlens_q, max_seqlen_q, 
     logits whose exp joins every row's softmax denominator (vLLM's attention sinks; model-domain output only)."""
     hs = q.shape[-1]
     nq = q.shape[1]
-    lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
+    lay = CacheLayout.of(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
     nkv = lay.nkv
     num_seqs = cu_seqlens_q.shape[0] - 1
     if num_splits is None:
         num_splits = decode_num_splits(num_seqs, nkv, window_keys(max_seqlen_k, sliding_window, max_seqlen_q),
                                        sm_count(q.device))
-    wbytes = _lib.load().qp_decode_workspace_bytes(q.shape[0], nq, hs, int(num_splits))
+    wbytes = _memo("qp_decode_workspace_bytes", int(q.shape[0]), int(nq), int(hs), int(num_splits))
     if ws is None:
         ws = workspace(q.device, wbytes)
     for name, t in (("cu_seqlens_q", cu_seqlens_q), ("seqused_k", seqused_k), ("block_table", block_table)):
@@ -283,7 +325,7 @@ def prefill(q, key_cache, value_cache, out, *, block_row, n, softmax_scale, k_sc
     base-2 lse (vllm_quantpack/attention/int4_prefill.py:203-232 returns the RHT-domain output for rotated queries).
     tokens_after_keys as in paged_decode (n >= qlen - tokens_after_keys)."""
     hs, nq, qlen = q.shape[-1], q.shape[1], q.shape[0]
-    lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
+    lay = CacheLayout.of(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
     if block_row.dtype != torch.int32 or block_row.stride(-1) != 1:
         raise TypeError("block_row must be a contiguous int32 row")
     if q.stride(-1) != 1 or out.stride(-1) != 1:
@@ -317,7 +359,7 @@ def prefill_varlen(q, key_cache, value_cache, out, *, cu_seqlens_q, seqused_k, m
     is read back to the host; max_seqlen_k (a host int, an upper bound of seqused_k) sizes the split count.
     `out` as in prefill; sliding_window, softcap and sinks as in paged_decode."""
     hs, nq, T = q.shape[-1], q.shape[1], q.shape[0]
-    lay = CacheLayout(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
+    lay = CacheLayout.of(key_cache, value_cache, k_scale_cache, v_scale_cache, hs)
     for name, t in (("cu_seqlens_q", cu_seqlens_q), ("seqused_k", seqused_k), ("block_table", block_table)):
         if t.dtype != torch.int32 or t.stride(-1) != 1:
             raise TypeError(f"{name} must be int32 with contiguous rows")
