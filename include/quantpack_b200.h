@@ -1,9 +1,11 @@
 /* quantpack_b200: B200-native (sm_100a) quantized KV-cache attention, C ABI.
  *
  * Replaces the hot path of the vLLM plugin jramirez-uab/vllm-quantpack 0.1.8: the int4_per_token_head and
- * k8v4_per_token_head cache write, split-KV paged decode with up to 4 MTP query tokens, long-chunk prefill and the
- * log-sum-exp merge of attention partials. The reference's hot path is Python calling Triton kernels; each entry
- * point below names the reference function it stands in for (paths inside the reference project).
+ * k8v4_per_token_head cache write, split-KV paged decode with up to 4 MTP query tokens (with vLLM's sliding window,
+ * logit softcap and attention sinks where a layer has them), long-chunk prefill, the short chunks of a step in one
+ * launch and the log-sum-exp merge of attention partials. The reference's hot path is Python calling Triton
+ * kernels; each entry point below names the reference function it stands in for (paths inside the reference
+ * project).
  *
  * Conventions for every function:
  * - all pointers are device pointers unless stated; `stream` is a cudaStream_t (NULL = legacy default stream);
