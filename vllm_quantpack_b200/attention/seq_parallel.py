@@ -15,6 +15,8 @@ rank holding the newest tokens (after = 0) masks anything inside a decode step.
 There is no TMA multicast and no library kernel reading peer memory: the peer reads are plain loads in this build's
 own fold kernel, or the exchange is an NCCL all-gather into this GPU's own buffer.
 """
+import warnings
+
 import torch
 import torch.distributed as dist
 
@@ -70,7 +72,9 @@ class PeerExchange:
         self.shape = (num_tokens, num_heads, head_size)
         nbytes = lib.qp_peer_exchange_bytes(self.world, num_tokens, num_heads, head_size)
         try:
-            symm_mem.enable_symm_mem_for_group(group.group_name)  # required before rendezvous by older torch
+            with warnings.catch_warnings():  # required before rendezvous by older torch, deprecated by newer
+                warnings.simplefilter("ignore", FutureWarning)
+                symm_mem.enable_symm_mem_for_group(group.group_name)
         except Exception:
             pass
         self.buf = symm_mem.empty(nbytes // 4, dtype=torch.float32, device=device)
