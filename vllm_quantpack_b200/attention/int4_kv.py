@@ -195,24 +195,29 @@ def make_unified_attention(stock_unified, prefill_on=True):
     (the stock int4 kernel would read its int8 keys as nibbles), so such a call raises instead. A sliding-window,
     softcap or sink layer runs on the split-KV kernel: decodes as usual, every prefill chunk in the varlen launch."""
     from . import k8v4_kv, ops
+    # VLLM_QUANTPACK_INT4_DECODE is read once, when the replacement is made (the plugin reads its knobs at patch
+    # time, int4_kv.py:190-226), not in every layer's call
+    splits = decode_splits_override()
 
     def unified_attention_int4(q, k_cache, v_cache, out, *, cu_seqlens_q, max_seqlen_q, seqused_k, max_seqlen_k,
                                softmax_scale, window_size, block_table, softcap, sinks, alibi_slopes, use_alibi_sqrt,
                                qq_bias, output_scale, mm_prefix_range, k_scale_cache, v_scale_cache, **kw):
-        args = dict(cu_seqlens_q=cu_seqlens_q, max_seqlen_q=max_seqlen_q, seqused_k=seqused_k,
-                    max_seqlen_k=max_seqlen_k, softmax_scale=softmax_scale, window_size=window_size,
-                    block_table=block_table, softcap=softcap, sinks=sinks, alibi_slopes=alibi_slopes,
-                    use_alibi_sqrt=use_alibi_sqrt, qq_bias=qq_bias, output_scale=output_scale,
-                    mm_prefix_range=mm_prefix_range, k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache, **kw)
+        def stock_args():
+            return dict(cu_seqlens_q=cu_seqlens_q, max_seqlen_q=max_seqlen_q, seqused_k=seqused_k,
+                        max_seqlen_k=max_seqlen_k, softmax_scale=softmax_scale, window_size=window_size,
+                        block_table=block_table, softcap=softcap, sinks=sinks, alibi_slopes=alibi_slopes,
+                        use_alibi_sqrt=use_alibi_sqrt, qq_bias=qq_bias, output_scale=output_scale,
+                        mm_prefix_range=mm_prefix_range, k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache,
+                        **kw)
+
         if not _plain(q, alibi_slopes, qq_bias, output_scale, mm_prefix_range):
             if k8v4_kv.is_k8v4(k_cache):
                 raise NotImplementedError(
                     f"{k8v4_kv.NAME}: ALiBi, qq_bias, FP8 output, mm_prefix ranges and head sizes other than "
                     f"{HEAD_SIZES} are not served by the B200 kernels, and vLLM's stock int4 kernel cannot read a "
                     f"k8v4 cache")
-            return stock_unified(q, k_cache, v_cache, out, **args)
+            return stock_unified(q, k_cache, v_cache, out, **stock_args())
         group = q.shape[1] // k_cache.shape[2]
-        splits = decode_splits_override()
         window = sliding_window_of(window_size)
         cap = float(softcap) if softcap and softcap > 0 else 0.0
 
@@ -225,7 +230,12 @@ def make_unified_attention(stock_unified, prefill_on=True):
 
         if max_seqlen_q <= MAX_Q_SPLIT_KV and max_seqlen_q * group <= MAX_DECODE_ROWS:
             # a decode step: no host read of the lengths (CUDA-graph capturable)
-            return decode(q, out, args)
+            ops.paged_decode(q, k_cache, v_cache, out, cu_seqlens_q=cu_seqlens_q, max_seqlen_q=max_seqlen_q,
+                             seqused_k=seqused_k, max_seqlen_k=max_seqlen_k, softmax_scale=softmax_scale,
+                             block_table=block_table, k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache,
+                             num_splits=splits, sliding_window=window, softcap=cap, sinks=sinks)
+            return None
+        args = stock_args()
         plan = StepPlan.of(cu_seqlens_q, seqused_k, group, prefill_on, q.shape[2],
                            long_chunks=window == 0 and cap == 0.0 and sinks is None)
         if plan.dec_batch is not None:
