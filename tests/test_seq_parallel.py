@@ -34,15 +34,16 @@ def _case(n_total, qlen, nq=6, nkv=2, hs=64, seed=0):
     return q, K, V
 
 
-def _worker(rank, world, port, n_total, qlen, result_dir):
+def _worker(rank, world, port, n_total, qlen, result_dir, window=0):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         q, K, V = _case(n_total, qlen)
         hs = q.shape[-1]
         lo, hi, after = sp.sequence_range(n_total, rank, world)
-        # this rank's partial: its keys only, query token i at local position (hi - lo) + after - qlen + i
-        o, lse = qo.attention_rht_domain(q, K[lo:hi], V[lo:hi], (hi - lo) + after, hs ** -0.5, hs)
+        # this rank's partial: its keys only, query token i at local position (hi - lo) + after - qlen + i (with a
+        # sliding window, a rank may hold none of a token's keys: lse -inf, folded with weight 0)
+        o, lse = qo.attention_rht_domain(q, K[lo:hi], V[lo:hi], (hi - lo) + after, hs ** -0.5, hs, window)
         x = sp.PartialExchange(dist.group.WORLD, qlen, q.shape[1], hs, "cpu")
         x.o.copy_(torch.from_numpy(o))
         x.lse.copy_(torch.from_numpy(lse * LOG2E))  # the kernels exchange base-2 lse
@@ -65,12 +66,15 @@ def test_sequence_range_partition():
         sp.sequence_range(10, 2, 2)
 
 
-@pytest.mark.parametrize("world,n_total,qlen", [(2, 900, 4), (2, 640, 64), (3, 1000, 3)])
-def test_exchange_and_fold_match_whole_sequence(tmp_path, world, n_total, qlen):
-    mp.spawn(_worker, args=(world, _free_port(), n_total, qlen, str(tmp_path)), nprocs=world, join=True)
+@pytest.mark.parametrize("world,n_total,qlen,window", [(2, 900, 4, 0), (2, 640, 64, 0), (3, 1000, 3, 0),
+                                                       (2, 900, 4, 300), (3, 1000, 3, 500), (2, 640, 64, 400)])
+def test_exchange_and_fold_match_whole_sequence(tmp_path, world, n_total, qlen, window):
+    """With a sliding window the earlier ranks see fewer keys, or none (900 / 300: rank 0 holds no key of any
+    token's window)."""
+    mp.spawn(_worker, args=(world, _free_port(), n_total, qlen, str(tmp_path), window), nprocs=world, join=True)
     q, K, V = _case(n_total, qlen)
     hs = q.shape[-1]
-    ref, ref_lse = qo.attention_rht_domain(q, K, V, n_total, hs ** -0.5, hs)
+    ref, ref_lse = qo.attention_rht_domain(q, K, V, n_total, hs ** -0.5, hs, window)
     for r in range(world):
         got = np.load(tmp_path / f"r{r}.npy")
         o, lse = got[: ref.size].reshape(ref.shape), got[ref.size:].reshape(ref_lse.shape)
